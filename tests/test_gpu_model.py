@@ -1,0 +1,161 @@
+"""Model-level parity of the CUDA token loop (through the C ABI) with the
+CPU oracle, on the benchmark configurations' shapes.
+
+The bar (north star): greedy token sequences identical to the reference's;
+logits within 1e-3 relative / 1e-2 absolute, i.e. |a - b| <= 1e-2 + 1e-3 |b|.
+"""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():  # pragma: no cover
+    pytest.skip("needs a GPU", allow_module_level=True)
+
+from tinyminigo_b200 import synth  # noqa: E402
+from tinyminigo_b200.model import GenParams, Model, ModelConfig, generate, generate_batch  # noqa: E402
+
+GOLD = Path(__file__).resolve().parent / "golden"
+
+
+def close(a, b):
+    return np.all(np.abs(a - b) <= 1e-2 + 1e-3 * np.abs(b))
+
+
+def margin(logits):
+    s = np.sort(logits)
+    return float(s[-1] - s[-2])
+
+
+def cfg_obj(cfg, eos=()):
+    return ModelConfig(cfg["hidden_size"], cfg["num_hidden_layers"], cfg["num_attention_heads"],
+                       cfg["num_key_value_heads"], cfg["head_dim"], cfg["intermediate_size"],
+                       cfg["rms_norm_eps"], cfg["rope_theta"], cfg["vocab_size"], list(eos), 0)
+
+
+@pytest.fixture(scope="module")
+def c1():
+    d = json.loads((GOLD / "hf_c1.json").read_text())
+    cfg = synth.CONFIGS["c1"]
+    t = synth.make_weights(cfg, d["weight_seed"])
+    return d, cfg, t
+
+
+@pytest.fixture(scope="module")
+def c2():
+    cfg = synth.CONFIGS["c2"]
+    t = synth.make_weights(cfg, 2024, device="cuda")
+    return cfg, t
+
+
+def test_c1_generate_matches_oracle_and_hf(orc, c1):
+    d, cfg, t = c1
+    om = orc.OracleModel(cfg, t)
+    ref_toks, ref_first, _, _ = om.generate(d["prompt"], 40)
+    assert ref_toks.tolist() == d["greedy"]
+    m = Model.from_tensors(cfg_obj(cfg), t)
+    out = generate(m, d["prompt"], GenParams(max_tokens=40))
+    assert out.tokens == d["greedy"]
+    assert close(out.logits_first_step, ref_first)
+    assert np.max(np.abs(out.logits_first_step - ref_first)) < 1e-4
+
+
+def test_c1_load_from_file_and_stepwise_logits(orc, c1, tmp_path):
+    d, cfg, t = c1
+    path = synth.write_model(tmp_path, cfg, t)
+    m = Model.load(path)
+    assert m.config.vocab_size == 32000 and m.config.head_dim == 16
+    om = orc.OracleModel(cfg, t)
+    cache = m.new_cache(128)
+    a = m.prefill(d["prompt"][:9], cache)
+    b = om.forward_seq(d["prompt"][:9])
+    assert close(a, b)
+    for tok in d["prompt"][9:] + d["greedy"][:6]:
+        a = m.forward_token(tok, cache)
+        b = om.forward_token(tok)
+        assert close(a, b) and np.max(np.abs(a - b)) < 1e-4
+    assert cache.len(0) == om.kv_len(0) == 16 + 6
+    for layer in range(cfg["num_hidden_layers"]):
+        kr, vr = om.kv_read(layer)
+        assert np.allclose(cache.keys_flat(layer), kr, atol=1e-5, rtol=1e-5)
+        assert np.allclose(cache.values_flat(layer), vr, atol=1e-5, rtol=1e-5)
+    cache.reset()
+    assert cache.len(0) == 0
+
+
+def test_c1_eos_stops_like_reference(orc, c1):
+    d, cfg, t = c1
+    eos = d["greedy"][5]
+    om = orc.OracleModel(cfg, t)
+    ref, _, _, _ = om.generate(d["prompt"], 40, eos=[eos])
+    m = Model.from_tensors(cfg_obj(cfg, [eos]), t)
+    seen = []
+    out = generate(m, d["prompt"], GenParams(max_tokens=40), on_token=seen.append)
+    assert out.tokens == ref.tolist() == d["greedy"][:6]
+    assert seen == out.tokens
+    assert m._gen_cache.len(0) == om.kv_len(0) == 16 + 5
+
+
+def test_c1_sampled_matches_oracle(orc, c1):
+    d, cfg, t = c1
+    om = orc.OracleModel(cfg, t)
+    m = Model.from_tensors(cfg_obj(cfg), t)
+    p = GenParams(max_tokens=30, temperature=0.8, top_k=40, top_p=0.95, repetition_penalty=1.1,
+                  seed=7)
+    u = orc.stdrng_uniforms(7, 30)
+    ref, _, _, _ = om.generate(d["prompt"], 30, 0.8, 40, 0.95, 1.1, 7, uniforms=u)
+    out = generate(m, d["prompt"], p)  # uniforms from the library's StdRng restatement
+    assert out.tokens == ref.tolist()
+
+
+def test_c1_greedy_with_penalty(orc, c1):
+    d, cfg, t = c1
+    om = orc.OracleModel(cfg, t)
+    m = Model.from_tensors(cfg_obj(cfg), t)
+    ref, _, _, _ = om.generate(d["prompt"], 20, 0.0, 0, 1.0, 1.3)
+    out = generate(m, d["prompt"], GenParams(max_tokens=20, repetition_penalty=1.3))
+    assert out.tokens == ref.tolist()
+
+
+def test_c2_greedy_identical(orc, c2):
+    cfg, t = c2
+    prompt = synth.random_prompt(cfg["vocab_size"], 64, 11)
+    om = orc.OracleModel(cfg, t)
+    steps = 24
+    ref, ref_first, _, _ = om.generate(prompt, steps)
+    m = Model.from_tensors(cfg_obj(cfg), t)
+    out = generate(m, prompt, GenParams(max_tokens=steps))
+    assert close(out.logits_first_step, ref_first), np.max(np.abs(out.logits_first_step - ref_first))
+    if out.tokens != ref.tolist():
+        i = next(j for j, (a, b) in enumerate(zip(out.tokens, ref.tolist())) if a != b)
+        pytest.fail(f"greedy diverged at step {i}: gpu {out.tokens[i]} vs ref {ref[i]}")
+    m.close()
+
+
+def test_c2_batched_streams_match_single(orc, c2):
+    cfg, t = c2
+    m = Model.from_tensors(cfg_obj(cfg), t)
+    prompts = np.stack([synth.random_prompt(cfg["vocab_size"], 16, s) for s in range(4)])
+    outs = generate_batch(m, prompts, [GenParams(max_tokens=8)] * 4)
+    for s in range(4):
+        single = generate(m, prompts[s], GenParams(max_tokens=8))
+        assert outs[s] == single.tokens
+    m.close()
+
+
+def test_capacity_and_bad_tokens_are_errors(c1):
+    d, cfg, t = c1
+    m = Model.from_tensors(cfg_obj(cfg), t)
+    cache = m.new_cache(4)
+    with pytest.raises(Exception, match="capacity"):
+        m.prefill(list(range(5)), cache)
+    with pytest.raises(Exception, match="out of range"):
+        m.forward_token(10**6, cache)
+    with pytest.raises(ValueError):
+        m.prefill([], cache)
+    with pytest.raises(Exception, match="top_k"):
+        generate(m, d["prompt"], GenParams(max_tokens=3, temperature=0.7, top_k=0))

@@ -1,0 +1,1498 @@
+// The token-loop engine behind the C ABI (include/tmg_cuda.h): Model
+// (weights + scratch on one GPU), KvCache, forward_token, forward_seq and
+// generate of src/model.rs, driving the kernels of this directory.
+//
+// Decode is one CUDA graph per step: 5 kernels per layer (qkv GEMV with the
+// input RMSNorm fused in, attention with RoPE + KV append fused in, o GEMV +
+// residual, gate/up GEMV with the post-attention RMSNorm and SwiGLU fused in,
+// down GEMV + residual) and the LM head (final RMSNorm fused in; in greedy
+// mode the argmax and generate's bookkeeping too), launched with
+// programmatic dependent launch so each kernel's weight stream starts while
+// the previous kernel drains.  generate runs its whole loop on the device;
+// the host only launches graph replays and reads tokens back in chunks.
+#include <dlfcn.h>
+#include <math.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/tmg_cuda.h"
+#include "common.cuh"
+#include "kernels.cuh"
+#include "loader.h"
+#include "tp.h"
+
+using namespace tmg;
+
+namespace {
+
+struct Layer {
+  uint16_t* wqkv = nullptr;  // [(nq + 2 nkv) d, h]: q rows, then k, then v
+  uint16_t* wo = nullptr;    // [h, nq d]
+  uint16_t* wg = nullptr;    // [I, h]
+  uint16_t* wu = nullptr;    // [I, h]
+  uint16_t* wd = nullptr;    // [h, I]
+  float* in_norm = nullptr;
+  float* post_norm = nullptr;
+  unsigned have = 0;  // bit per tensor
+};
+
+constexpr unsigned kHaveQ = 1, kHaveK = 2, kHaveV = 4, kHaveO = 8, kHaveG = 16, kHaveU = 32,
+                   kHaveD = 64, kHaveIn = 128, kHavePost = 256, kHaveAll = 511;
+
+}  // namespace
+
+struct tmg_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int num_sms = 148;
+  bool has_model = false;
+  bool finalized = false;
+  tmg_config cfg{};
+  // tensor parallel
+  int rank = 0, world = 1;
+  TpComm* tp = nullptr;
+  // dims (local shard)
+  int h = 0, d = 0, L = 0, nq = 0, nkv = 0, I = 0, V = 0;
+  int nq_g = 0, nkv_g = 0, I_g = 0;  // global
+  int64_t V_l = 0, v_off = 0;         // vocab shard of the LM head
+  int qkv_rows = 0;
+  // weights
+  std::vector<Layer> layers;
+  uint16_t* embed = nullptr;  // [V, h], replicated
+  uint16_t* lm_head = nullptr;  // [V_l, h]
+  float* final_norm = nullptr;
+  bool lm_tied = true;
+  int64_t weight_bytes = 0;
+  std::vector<void*> allocs;
+  // decode scratch (kMaxStreams rows)
+  float *x = nullptr, *xn = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr,
+        *logits = nullptr, *partial = nullptr;
+  unsigned long long *am_part = nullptr, *sm_part = nullptr;
+  unsigned int* tickets = nullptr;  // [0]: head, [1..16]: sampler
+  int32_t* d_err = nullptr;
+  float* logits_full = nullptr;  // [M, V] gathered logits under TP
+  // prefill scratch
+  int64_t pf_cap = 0;
+  float *X = nullptr, *Xn = nullptr, *QKV = nullptr, *ATT = nullptr, *G = nullptr, *U = nullptr;
+  uint32_t* d_tok = nullptr;
+  // op-level scratch
+  void* op_buf = nullptr;
+  size_t op_cap = 0;
+  // pinned staging
+  void* pinned = nullptr;
+  size_t pinned_cap = 0;
+  std::string err;
+};
+
+struct tmg_kv {
+  tmg_ctx* ctx = nullptr;
+  int M = 1;
+  int64_t cap = 0;
+  int kvd = 0;
+  std::vector<float*> k, v;  // per layer [M, cap, kvd]
+  float *rope_cos = nullptr, *rope_sin = nullptr;
+  int32_t* d_state = nullptr;  // token | pos | done | n_gen, kMaxStreams each
+  StreamState st{};
+  uint32_t* d_gen = nullptr;
+  int64_t gen_alloc = 0;
+  float* d_uni = nullptr;
+  int64_t uni_alloc = 0;
+  float* part = nullptr;
+  unsigned int* att_ticket = nullptr;
+  int nsplit = 1;
+  std::vector<int64_t> lens;
+  cudaGraphExec_t g_plain = nullptr;
+  cudaGraphExec_t g_dec = nullptr;  // forward + argmax with gen_cap = dec_cap
+  int64_t dec_cap = 0;
+  int32_t* h_state = nullptr;  // pinned staging of the state block
+  cudaEvent_t state_ev = nullptr;  // the last upload from h_state
+  std::vector<void*> allocs;
+};
+
+namespace {
+
+constexpr int64_t kPrefillChunk = 4096;
+
+int fail(tmg_ctx* c, int code, const std::string& m) {
+  if (c) c->err = m;
+  return code;
+}
+int cuda_fail(tmg_ctx* c, cudaError_t e, const char* where) {
+  return fail(c, TMG_ERR_CUDA, std::string(where) + ": " + cudaGetErrorString(e));
+}
+#define CK(expr, where)                               \
+  do {                                                \
+    cudaError_t _e = (expr);                          \
+    if (_e != cudaSuccess) return cuda_fail(c, _e, where); \
+  } while (0)
+
+template <typename T>
+cudaError_t dalloc(std::vector<void*>& list, T** p, size_t count) {
+  void* q = nullptr;
+  cudaError_t e = cudaMalloc(&q, std::max<size_t>(count, 1) * sizeof(T));
+  if (e != cudaSuccess) return e;
+  list.push_back(q);
+  *p = static_cast<T*>(q);
+  return cudaSuccess;
+}
+
+void free_all(std::vector<void*>& list) {
+  for (void* p : list) cudaFree(p);
+  list.clear();
+}
+
+cudaError_t ensure_pinned(tmg_ctx* c, size_t bytes) {
+  if (c->pinned_cap >= bytes) return cudaSuccess;
+  if (c->pinned) cudaFreeHost(c->pinned);
+  c->pinned = nullptr;
+  c->pinned_cap = 0;
+  size_t want = std::max<size_t>(bytes, 1 << 20);
+  TMG_CUDA_TRY(cudaHostAlloc(&c->pinned, want, cudaHostAllocDefault));
+  c->pinned_cap = want;
+  return cudaSuccess;
+}
+
+cudaError_t ensure_op(tmg_ctx* c, size_t bytes) {
+  if (c->op_cap >= bytes) return cudaSuccess;
+  if (c->op_buf) cudaFree(c->op_buf);
+  c->op_buf = nullptr;
+  c->op_cap = 0;
+  TMG_CUDA_TRY(cudaMalloc(&c->op_buf, bytes));
+  TMG_CUDA_TRY(cudaMemset(c->op_buf, 0, bytes));
+  c->op_cap = bytes;
+  return cudaSuccess;
+}
+
+// ---------------------------------------------------------------------------
+// Weight placement (with the tensor-parallel shard of this rank).
+// ---------------------------------------------------------------------------
+int check_shape(tmg_ctx* c, const std::string& name, int64_t numel, int64_t want) {
+  if (numel != want)
+    return fail(c, TMG_ERR_INVALID,
+                "tensor " + name + ": " + std::to_string(numel) + " elements, expected " +
+                    std::to_string(want));
+  return TMG_OK;
+}
+
+// Copy rows [r0, r0 + nr) x cols [c0, c0 + nc) of a host [R, C] bf16 matrix
+// into a device [nr, nc] matrix at dst.
+int upload_block(tmg_ctx* c, uint16_t* dst, const uint16_t* src, int64_t C, int64_t r0,
+                 int64_t nr, int64_t c0, int64_t nc) {
+  CK(cudaMemcpy2DAsync(dst, size_t(nc) * 2, src + r0 * C + c0, size_t(C) * 2, size_t(nc) * 2,
+                       size_t(nr), cudaMemcpyHostToDevice, c->stream),
+     "upload");
+  return TMG_OK;
+}
+
+int upload_vec(tmg_ctx* c, float* dst, int32_t dtype, const void* host, int64_t n) {
+  std::vector<float> tmp(n);
+  if (dtype == 0) std::memcpy(tmp.data(), host, n * 4);
+  else if (dtype == 1)
+    for (int64_t i = 0; i < n; ++i) {
+      uint32_t u = uint32_t(static_cast<const uint16_t*>(host)[i]) << 16;
+      std::memcpy(&tmp[i], &u, 4);
+    }
+  else
+    for (int64_t i = 0; i < n; ++i) tmp[i] = f16_to_f32(static_cast<const uint16_t*>(host)[i]);
+  CK(cudaMemcpyAsync(dst, tmp.data(), n * 4, cudaMemcpyHostToDevice, c->stream), "upload");
+  CK(cudaStreamSynchronize(c->stream), "upload");
+  return TMG_OK;
+}
+
+int set_tensor(tmg_ctx* c, const std::string& name, int32_t dtype, const void* host,
+               int64_t numel) {
+  if (!c->has_model) return fail(c, TMG_ERR_INVALID, "context has no model config");
+  if (c->finalized) return fail(c, TMG_ERR_INVALID, "weights already finalized");
+  const int64_t h = c->h, d = c->d;
+  const bool is_vec = name == "model.norm.weight" || name.find("layernorm.weight") != std::string::npos;
+  if (!is_vec && dtype != 1)
+    return fail(c, TMG_ERR_INVALID, "tensor " + name + ": the device path needs BF16 matrices");
+  int rc;
+  if (name == "model.embed_tokens.weight") {
+    if ((rc = check_shape(c, name, numel, int64_t(c->V) * h))) return rc;
+    CK(cudaMemcpyAsync(c->embed, host, size_t(numel) * 2, cudaMemcpyHostToDevice, c->stream),
+       "upload");
+    return TMG_OK;
+  }
+  if (name == "model.norm.weight") {
+    if ((rc = check_shape(c, name, numel, h))) return rc;
+    return upload_vec(c, c->final_norm, dtype, host, numel);
+  }
+  if (name == "lm_head.weight") {
+    if ((rc = check_shape(c, name, numel, int64_t(c->V) * h))) return rc;
+    if (c->lm_tied) {
+      CK(dalloc(c->allocs, &c->lm_head, size_t(c->V_l) * h), "alloc");
+      c->weight_bytes += c->V_l * h * 2;
+      c->lm_tied = false;
+    }
+    return upload_block(c, c->lm_head, static_cast<const uint16_t*>(host), h, c->v_off, c->V_l,
+                        0, h);
+  }
+  const std::string pre = "model.layers.";
+  if (name.compare(0, pre.size(), pre) != 0)
+    return fail(c, TMG_ERR_INVALID, "unknown tensor " + name);
+  size_t dot = name.find('.', pre.size());
+  if (dot == std::string::npos) return fail(c, TMG_ERR_INVALID, "unknown tensor " + name);
+  const int li = std::atoi(name.substr(pre.size(), dot - pre.size()).c_str());
+  if (li < 0 || li >= c->L) return fail(c, TMG_ERR_INVALID, "layer out of range: " + name);
+  const std::string suf = name.substr(dot + 1);
+  Layer& Lw = c->layers[li];
+  const uint16_t* src = static_cast<const uint16_t*>(host);
+  const int64_t qg = int64_t(c->nq_g) * d, kg = int64_t(c->nkv_g) * d;
+  const int64_t ql = int64_t(c->nq) * d, kl = int64_t(c->nkv) * d;
+  if (suf == "self_attn.q_proj.weight") {
+    if ((rc = check_shape(c, name, numel, qg * h))) return rc;
+    Lw.have |= kHaveQ;
+    return upload_block(c, Lw.wqkv, src, h, c->rank * ql, ql, 0, h);
+  }
+  if (suf == "self_attn.k_proj.weight") {
+    if ((rc = check_shape(c, name, numel, kg * h))) return rc;
+    Lw.have |= kHaveK;
+    return upload_block(c, Lw.wqkv + ql * h, src, h, c->rank * kl, kl, 0, h);
+  }
+  if (suf == "self_attn.v_proj.weight") {
+    if ((rc = check_shape(c, name, numel, kg * h))) return rc;
+    Lw.have |= kHaveV;
+    return upload_block(c, Lw.wqkv + (ql + kl) * h, src, h, c->rank * kl, kl, 0, h);
+  }
+  if (suf == "self_attn.o_proj.weight") {
+    if ((rc = check_shape(c, name, numel, h * qg))) return rc;
+    Lw.have |= kHaveO;
+    return upload_block(c, Lw.wo, src, qg, 0, h, c->rank * ql, ql);
+  }
+  if (suf == "mlp.gate_proj.weight" || suf == "mlp.up_proj.weight") {
+    if ((rc = check_shape(c, name, numel, int64_t(c->I_g) * h))) return rc;
+    const bool gate = suf[4] == 'g';
+    Lw.have |= gate ? kHaveG : kHaveU;
+    return upload_block(c, gate ? Lw.wg : Lw.wu, src, h, int64_t(c->rank) * c->I, c->I, 0, h);
+  }
+  if (suf == "mlp.down_proj.weight") {
+    if ((rc = check_shape(c, name, numel, h * int64_t(c->I_g)))) return rc;
+    Lw.have |= kHaveD;
+    return upload_block(c, Lw.wd, src, c->I_g, 0, h, int64_t(c->rank) * c->I, c->I);
+  }
+  if (suf == "input_layernorm.weight" || suf == "post_attention_layernorm.weight") {
+    if ((rc = check_shape(c, name, numel, h))) return rc;
+    const bool in = suf[0] == 'i';
+    Lw.have |= in ? kHaveIn : kHavePost;
+    return upload_vec(c, in ? Lw.in_norm : Lw.post_norm, dtype, host, numel);
+  }
+  return fail(c, TMG_ERR_INVALID, "unknown tensor " + name);
+}
+
+int alloc_model(tmg_ctx* c) {
+  const tmg_config& f = c->cfg;
+  if (f.hidden_size <= 0 || f.num_hidden_layers <= 0 || f.num_attention_heads <= 0 ||
+      f.num_key_value_heads <= 0 || f.head_dim <= 0 || f.intermediate_size <= 0 ||
+      f.vocab_size <= 0 || f.head_dim % 2 != 0 ||
+      f.num_attention_heads % f.num_key_value_heads != 0)
+    return fail(c, TMG_ERR_INVALID, "invalid model config");
+  if (f.num_key_value_heads % c->world != 0 || f.intermediate_size % c->world != 0 ||
+      f.num_attention_heads % c->world != 0)
+    return fail(c, TMG_ERR_INVALID, "heads / intermediate size do not divide by the TP world");
+  c->h = f.hidden_size;
+  c->d = f.head_dim;
+  c->L = f.num_hidden_layers;
+  c->nq_g = f.num_attention_heads;
+  c->nkv_g = f.num_key_value_heads;
+  c->I_g = f.intermediate_size;
+  c->V = f.vocab_size;
+  c->nq = c->nq_g / c->world;
+  c->nkv = c->nkv_g / c->world;
+  c->I = c->I_g / c->world;
+  c->V_l = (int64_t(c->V) + c->world - 1) / c->world;
+  c->v_off = int64_t(c->rank) * c->V_l;
+  c->V_l = std::min<int64_t>(c->V_l, int64_t(c->V) - c->v_off);
+  c->qkv_rows = (c->nq + 2 * c->nkv) * c->d;
+  const int64_t h = c->h;
+  c->layers.assign(c->L, Layer());
+  for (auto& Lw : c->layers) {
+    CK(dalloc(c->allocs, &Lw.wqkv, size_t(c->qkv_rows) * h), "alloc weights");
+    CK(dalloc(c->allocs, &Lw.wo, size_t(h) * c->nq * c->d), "alloc weights");
+    CK(dalloc(c->allocs, &Lw.wg, size_t(c->I) * h), "alloc weights");
+    CK(dalloc(c->allocs, &Lw.wu, size_t(c->I) * h), "alloc weights");
+    CK(dalloc(c->allocs, &Lw.wd, size_t(h) * c->I), "alloc weights");
+    CK(dalloc(c->allocs, &Lw.in_norm, size_t(h)), "alloc weights");
+    CK(dalloc(c->allocs, &Lw.post_norm, size_t(h)), "alloc weights");
+    c->weight_bytes += 2 * (int64_t(c->qkv_rows) * h + h * c->nq * c->d + 3 * int64_t(c->I) * h);
+  }
+  CK(dalloc(c->allocs, &c->embed, size_t(c->V) * h), "alloc weights");
+  CK(dalloc(c->allocs, &c->final_norm, size_t(h)), "alloc weights");
+  c->weight_bytes += int64_t(c->V) * h * 2;
+  c->lm_tied = true;
+  c->lm_head = c->embed + c->v_off * h;
+  // decode scratch
+  const int M = kMaxStreams;
+  CK(dalloc(c->allocs, &c->x, size_t(M) * h), "alloc scratch");
+  CK(dalloc(c->allocs, &c->xn, size_t(M) * h), "alloc scratch");
+  CK(dalloc(c->allocs, &c->partial, size_t(M) * h), "alloc scratch");
+  CK(dalloc(c->allocs, &c->qkv, size_t(M) * c->qkv_rows), "alloc scratch");
+  CK(dalloc(c->allocs, &c->attn, size_t(M) * c->nq * c->d), "alloc scratch");
+  CK(dalloc(c->allocs, &c->act, size_t(M) * c->I), "alloc scratch");
+  CK(dalloc(c->allocs, &c->logits, size_t(M) * c->V_l), "alloc scratch");
+  if (c->world > 1) CK(dalloc(c->allocs, &c->logits_full, size_t(M) * c->V), "alloc scratch");
+  CK(dalloc(c->allocs, &c->am_part, size_t(M) * c->num_sms * 8), "alloc scratch");
+  CK(dalloc(c->allocs, &c->sm_part, size_t(M) * 64 * kMaxTopK), "alloc scratch");
+  CK(dalloc(c->allocs, &c->tickets, 64), "alloc scratch");
+  CK(cudaMemset(c->tickets, 0, 64 * sizeof(unsigned int)), "memset");
+  CK(dalloc(c->allocs, &c->d_err, 4), "alloc scratch");
+  CK(cudaMemset(c->d_err, 0, 16), "memset");
+  c->has_model = true;
+  return TMG_OK;
+}
+
+int finalize(tmg_ctx* c) {
+  if (!c->has_model) return fail(c, TMG_ERR_INVALID, "context has no model config");
+  if (c->finalized) return TMG_OK;
+  for (int l = 0; l < c->L; ++l)
+    if (c->layers[l].have != kHaveAll)
+      return fail(c, TMG_ERR_INVALID,
+                  "missing tensor in layer " + std::to_string(l) + " (have mask " +
+                      std::to_string(c->layers[l].have) + ")");
+  CK(cudaStreamSynchronize(c->stream), "finalize");
+  c->finalized = true;
+  return TMG_OK;
+}
+
+int ensure_prefill(tmg_ctx* c, int64_t T) {
+  const int64_t Tc = std::min<int64_t>(T, kPrefillChunk);
+  if (c->pf_cap >= Tc) return TMG_OK;
+  for (void* p : {(void*)c->X, (void*)c->Xn, (void*)c->QKV, (void*)c->ATT, (void*)c->G,
+                  (void*)c->U, (void*)c->d_tok})
+    if (p) cudaFree(p);
+  c->pf_cap = 0;
+  std::vector<void*> tmp;
+  CK(dalloc(tmp, &c->X, size_t(Tc) * c->h), "alloc prefill");
+  CK(dalloc(tmp, &c->Xn, size_t(Tc) * c->h), "alloc prefill");
+  CK(dalloc(tmp, &c->QKV, size_t(Tc) * c->qkv_rows), "alloc prefill");
+  CK(dalloc(tmp, &c->ATT, size_t(Tc) * c->nq * c->d), "alloc prefill");
+  CK(dalloc(tmp, &c->G, size_t(Tc) * c->I), "alloc prefill");
+  CK(dalloc(tmp, &c->U, size_t(Tc) * c->I), "alloc prefill");
+  CK(dalloc(tmp, &c->d_tok, size_t(Tc)), "alloc prefill");
+  c->pf_cap = Tc;
+  return TMG_OK;
+}
+
+// y (+)= x . W^T for T rows (the prefill GEMM).
+cudaError_t gemm(tmg_ctx* c, const float* x, const uint16_t* w, int64_t T, int64_t N, int64_t K,
+                 float* y, int64_t ldy, bool acc) {
+  return launch_gemm_simt(x, w, T, N, K, y, ldy, acc, c->stream);
+}
+
+// GEMV with an optional fused prologue; falls back to separate embedding /
+// norm kernels when the fused kernel does not take the shape.
+cudaError_t gemv(tmg_ctx* c, GemvArgs a, GemvPro pro, GemvEpi epi, bool pdl) {
+  if (!gemv_fused_ok(a, epi) && pro != PRO_NONE) {
+    if (pro == PRO_EMBED_NORM) {
+      TMG_CUDA_TRY(launch_embed(a.embed, a.tokens, a.M, a.K, a.x_out, c->stream));
+      a.x = a.x_out;
+    }
+    TMG_CUDA_TRY(launch_rmsnorm(a.x, a.norm_w, a.eps, a.K, a.M, a.norm_mode, c->xn, c->stream));
+    a.x = c->xn;
+    pro = PRO_NONE;
+  }
+  return launch_gemv(a, pro, epi, c->stream, pdl, c->num_sms);
+}
+
+// Sum the partial [M, n] over the TP ranks and add it into dst.
+cudaError_t tp_reduce_add(tmg_ctx* c, float* partial, float* dst, int64_t n) {
+  TMG_CUDA_TRY(tp_allreduce_sum(c->tp, partial, n, c->stream));
+  return launch_add(partial, dst, n, c->stream);
+}
+
+// Per-kernel CUDA events of the profiling pass (tmg_profile_decode).
+struct Prof {
+  cudaStream_t s;
+  std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> marks;
+  cudaEvent_t open = nullptr;
+  void begin() {
+    cudaEventCreate(&open);
+    cudaEventRecord(open, s);
+  }
+  void end(int cls) {
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    cudaEventRecord(e, s);
+    marks.push_back({cls, {open, e}});
+    open = nullptr;
+  }
+  ~Prof() {
+    for (auto& m : marks) {
+      cudaEventDestroy(m.second.first);
+      cudaEventDestroy(m.second.second);
+    }
+  }
+};
+
+// One forward_token for the M streams of kv (model.rs:392-491).
+cudaError_t enqueue_forward(tmg_ctx* c, tmg_kv* kv, const StreamState& st, bool argmax,
+                            Prof* prof = nullptr) {
+  const int M = kv->M;
+  const bool pdl = prof == nullptr;
+  auto B = [&]() {
+    if (prof) prof->begin();
+  };
+  auto E = [&](int cls) {
+    if (prof) prof->end(cls);
+  };
+  const float eps = c->cfg.rms_norm_eps;
+  const bool tp = c->world > 1;
+  for (int l = 0; l < c->L; ++l) {
+    const Layer& Lw = c->layers[l];
+    GemvArgs A;
+    A.w = Lw.wqkv;
+    A.N = c->qkv_rows;
+    A.K = c->h;
+    A.M = M;
+    A.y = c->qkv;
+    A.ldy = c->qkv_rows;
+    A.norm_w = Lw.in_norm;
+    A.eps = eps;
+    A.norm_mode = 0;
+    if (l == 0) {
+      A.embed = c->embed;
+      A.tokens = st.token;
+      A.x_out = c->x;
+      B();
+      TMG_CUDA_TRY(gemv(c, A, PRO_EMBED_NORM, EPI_STORE, pdl));
+      E(0);
+    } else {
+      A.x = c->x;
+      B();
+      TMG_CUDA_TRY(gemv(c, A, PRO_NORM, EPI_STORE, pdl));
+      E(0);
+    }
+    AttnDecodeArgs T;
+    T.qkv = c->qkv;
+    T.qkv_ld = c->qkv_rows;
+    T.kc = kv->k[l];
+    T.vc = kv->v[l];
+    T.cap = kv->cap;
+    T.rope_cos = kv->rope_cos;
+    T.rope_sin = kv->rope_sin;
+    T.out = c->attn;
+    T.part = kv->part;
+    T.ticket = kv->att_ticket;
+    T.st = st;
+    T.nq = c->nq;
+    T.nkv = c->nkv;
+    T.d = c->d;
+    T.nsplit = kv->nsplit;
+    T.M = M;
+    T.scale = 1.0f / sqrtf(float(c->d));
+    B();
+    TMG_CUDA_TRY(launch_attn_decode(T, c->stream, pdl));
+    E(1);
+    GemvArgs O;
+    O.w = Lw.wo;
+    O.N = c->h;
+    O.K = c->nq * c->d;
+    O.M = M;
+    O.x = c->attn;
+    O.y = tp ? c->partial : c->x;
+    O.ldy = c->h;
+    B();
+    TMG_CUDA_TRY(gemv(c, O, PRO_NONE, tp ? EPI_STORE : EPI_ADD, pdl));
+    E(2);
+    if (tp) TMG_CUDA_TRY(tp_reduce_add(c, c->partial, c->x, int64_t(M) * c->h));
+    GemvArgs GU;
+    GU.w = Lw.wg;
+    GU.w2 = Lw.wu;
+    GU.N = c->I;
+    GU.K = c->h;
+    GU.M = M;
+    GU.x = c->x;
+    GU.norm_w = Lw.post_norm;
+    GU.eps = eps;
+    GU.y = c->act;
+    GU.ldy = c->I;
+    B();
+    TMG_CUDA_TRY(gemv(c, GU, PRO_NORM, EPI_SWIGLU, pdl));
+    E(3);
+    GemvArgs D;
+    D.w = Lw.wd;
+    D.N = c->h;
+    D.K = c->I;
+    D.M = M;
+    D.x = c->act;
+    D.y = tp ? c->partial : c->x;
+    D.ldy = c->h;
+    B();
+    TMG_CUDA_TRY(gemv(c, D, PRO_NONE, tp ? EPI_STORE : EPI_ADD, pdl));
+    E(4);
+    if (tp) TMG_CUDA_TRY(tp_reduce_add(c, c->partial, c->x, int64_t(M) * c->h));
+  }
+  GemvArgs H;
+  H.w = c->lm_head;
+  H.N = c->V_l;
+  H.K = c->h;
+  H.M = M;
+  H.x = c->x;
+  H.norm_w = c->final_norm;
+  H.eps = eps;
+  H.norm_mode = 0;
+  H.y = c->logits;
+  H.ldy = c->V_l;
+  H.am_part = c->am_part;
+  H.ticket = &c->tickets[0];
+  H.st = st;
+  if (!tp) {
+    B();
+    cudaError_t e = gemv(c, H, PRO_NORM, argmax ? EPI_HEAD_ARGMAX : EPI_HEAD, pdl);
+    E(5);
+    return e;
+  }
+  // TP: vocab-split head; gather the logits, then the same end of step
+  TMG_CUDA_TRY(gemv(c, H, PRO_NORM, EPI_STORE, pdl));
+  TMG_CUDA_TRY(tp_allgather_rows(c->tp, c->logits, c->V_l, c->logits_full, c->V, M, c->stream));
+  return launch_step_end(st, M, argmax ? c->logits_full : nullptr, c->V, c->stream);
+}
+
+// forward_seq for one stream (model.rs:503-590): chunks of kPrefillChunk
+// tokens through all layers; the last row's logits land in row `stream` of
+// the decode logits buffer.
+int forward_seq(tmg_ctx* c, tmg_kv* kv, int stream, const uint32_t* tokens, int64_t T,
+                bool host_tokens) {
+  int rc;
+  if ((rc = ensure_prefill(c, T))) return rc;
+  const int64_t p0 = kv->lens[stream];
+  const int64_t kvd = kv->kvd;
+  const float eps = c->cfg.rms_norm_eps;
+  const float scale = 1.0f / sqrtf(float(c->d));
+  const bool tp = c->world > 1;
+  if (host_tokens) CK(ensure_pinned(c, size_t(T) * 4), "pinned");
+  for (int64_t t0 = 0; t0 < T; t0 += c->pf_cap) {
+    const int64_t Tc = std::min<int64_t>(c->pf_cap, T - t0);
+    const int64_t pos0 = p0 + t0;
+    const uint32_t* dtok;
+    if (host_tokens) {
+      CK(cudaStreamSynchronize(c->stream), "prefill");
+      std::memcpy(c->pinned, tokens + t0, size_t(Tc) * 4);
+      CK(cudaMemcpyAsync(c->d_tok, c->pinned, size_t(Tc) * 4, cudaMemcpyHostToDevice, c->stream),
+         "prefill tokens");
+      dtok = c->d_tok;
+    } else {
+      dtok = tokens + t0;
+    }
+    CK(launch_embed(c->embed, dtok, Tc, c->h, c->X, c->stream), "embed");
+    for (int l = 0; l < c->L; ++l) {
+      const Layer& Lw = c->layers[l];
+      float* kc = kv->k[l] + size_t(stream) * kv->cap * kvd;
+      float* vc = kv->v[l] + size_t(stream) * kv->cap * kvd;
+      CK(launch_rmsnorm(c->X, Lw.in_norm, eps, c->h, Tc, 1, c->Xn, c->stream), "rmsnorm");
+      CK(gemm(c, c->Xn, Lw.wqkv, Tc, c->qkv_rows, c->h, c->QKV, c->qkv_rows, false), "gemm qkv");
+      CK(launch_rope_append(c->QKV, c->qkv_rows, Tc, c->nq, c->nkv, c->d, kv->rope_cos,
+                            kv->rope_sin, pos0, kc, vc, c->stream),
+         "rope");
+      CK(launch_attn_prefill(c->QKV, c->qkv_rows, kc, vc, Tc, pos0, c->nq, c->nkv, c->d, scale,
+                             c->ATT, int64_t(c->nq) * c->d, c->stream),
+         "attention");
+      if (tp) {
+        CK(gemm(c, c->ATT, Lw.wo, Tc, c->h, int64_t(c->nq) * c->d, c->Xn, c->h, false), "gemm o");
+        CK(tp_reduce_add(c, c->Xn, c->X, Tc * c->h), "allreduce");
+      } else {
+        CK(gemm(c, c->ATT, Lw.wo, Tc, c->h, int64_t(c->nq) * c->d, c->X, c->h, true), "gemm o");
+      }
+      CK(launch_rmsnorm(c->X, Lw.post_norm, eps, c->h, Tc, 1, c->Xn, c->stream), "rmsnorm");
+      CK(gemm(c, c->Xn, Lw.wg, Tc, c->I, c->h, c->G, c->I, false), "gemm gate");
+      CK(gemm(c, c->Xn, Lw.wu, Tc, c->I, c->h, c->U, c->I, false), "gemm up");
+      CK(launch_swiglu(c->G, c->U, Tc * c->I, c->G, c->stream), "swiglu");
+      if (tp) {
+        CK(gemm(c, c->G, Lw.wd, Tc, c->h, c->I, c->Xn, c->h, false), "gemm down");
+        CK(tp_reduce_add(c, c->Xn, c->X, Tc * c->h), "allreduce");
+      } else {
+        CK(gemm(c, c->G, Lw.wd, Tc, c->h, c->I, c->X, c->h, true), "gemm down");
+      }
+    }
+    if (t0 + Tc == T) {
+      GemvArgs H;
+      H.w = c->lm_head;
+      H.N = c->V_l;
+      H.K = c->h;
+      H.M = 1;
+      H.x = c->X + size_t(Tc - 1) * c->h;
+      H.norm_w = c->final_norm;
+      H.eps = eps;
+      H.norm_mode = 1;  // forward_seq's final norm is rms_norm_batch (model.rs:587)
+      H.y = c->logits + size_t(stream) * c->V_l;
+      H.ldy = c->V_l;
+      CK(gemv(c, H, PRO_NORM, EPI_STORE, false), "lm_head");
+      if (tp)
+        CK(tp_allgather_rows(c->tp, c->logits + size_t(stream) * c->V_l, c->V_l,
+                             c->logits_full + size_t(stream) * c->V, c->V, 1, c->stream),
+           "allgather");
+    }
+  }
+  CK(launch_set_pos(kv->st, stream, int32_t(p0 + T), c->stream), "set pos");
+  kv->lens[stream] = p0 + T;
+  return TMG_OK;
+}
+
+const float* logits_row(tmg_ctx* c, int m) {
+  return c->world > 1 ? c->logits_full + size_t(m) * c->V : c->logits + size_t(m) * c->V_l;
+}
+
+std::vector<float> rope_table(int d, float theta, int64_t n_pos, bool sin_part) {
+  // Rope::new / ensure, src/tensor.rs:1005-1023: f32 powf, recip, f32
+  // angle, glibc sinf / cosf -- the same values the reference computes.
+  const int half = d / 2;
+  std::vector<float> inv(half);
+  for (int i = 0; i < half; ++i) {
+    const float e = (2.0f * float(i)) / float(d);
+    inv[i] = 1.0f / powf(theta, e);
+  }
+  std::vector<float> t(size_t(n_pos) * half);
+  for (int64_t p = 0; p < n_pos; ++p)
+    for (int i = 0; i < half; ++i) {
+      const float ang = float(p) * inv[i];
+      t[size_t(p) * half + i] = sin_part ? sinf(ang) : cosf(ang);
+    }
+  return t;
+}
+
+int reset_state(tmg_ctx* c, tmg_kv* kv) {
+  CK(cudaMemsetAsync(kv->d_state, 0, sizeof(int32_t) * 4 * kMaxStreams, c->stream), "reset");
+  for (auto& v : kv->lens) v = 0;
+  return TMG_OK;
+}
+
+int check_sampling(tmg_ctx* c, const tmg_gen_params* p) {
+  if (!p || p->max_tokens < 0) return fail(c, TMG_ERR_INVALID, "bad generation params");
+  if (p->temperature > 0.f && (p->top_k < 1 || p->top_k > kMaxTopK || p->top_k >= c->V))
+    return fail(c, TMG_ERR_INVALID,
+                "device sampling needs 1 <= top_k <= 64 (top_k = 0 / full-vocabulary "
+                "sampling is not implemented on the device)");
+  return TMG_OK;
+}
+
+// The generate loop for all streams of kv (model.rs:614-663).
+int run_generate(tmg_ctx* c, tmg_kv* kv, const uint32_t* prompts, int64_t T,
+                 const tmg_gen_params* params, const float* uniforms, uint32_t* tokens_out,
+                 int64_t* n_out, float* first_logits, double* prefill_secs, tmg_token_cb cb,
+                 void* user) {
+  int rc;
+  if (!c->finalized) return fail(c, TMG_ERR_INVALID, "weights not finalized");
+  if ((rc = check_sampling(c, params))) return rc;
+  const int M = kv->M;
+  const int64_t maxt = params->max_tokens;
+  for (int m = 1; m < M; ++m)
+    if (params[m].max_tokens != maxt || params[m].temperature != params[0].temperature ||
+        params[m].top_k != params[0].top_k || params[m].top_p != params[0].top_p ||
+        params[m].repetition_penalty != params[0].repetition_penalty)
+      return fail(c, TMG_ERR_INVALID, "batched streams must share sampling settings");
+  if (T <= 0) return fail(c, TMG_ERR_INVALID, "empty prompt");
+  if (T + maxt > kv->cap) return fail(c, TMG_ERR_CAPACITY, "prompt + max_tokens exceeds KV capacity");
+  for (int64_t i = 0; i < int64_t(M) * T; ++i)
+    if (prompts[i] >= uint32_t(c->V)) return fail(c, TMG_ERR_INVALID, "token id out of range");
+  if ((rc = reset_state(c, kv))) return rc;
+  auto t0 = std::chrono::steady_clock::now();
+  for (int m = 0; m < M; ++m)
+    if ((rc = forward_seq(c, kv, m, prompts + size_t(m) * T, T, true))) return rc;
+  CK(cudaStreamSynchronize(c->stream), "prefill");
+  auto t1 = std::chrono::steady_clock::now();
+  if (prefill_secs) *prefill_secs = std::chrono::duration<double>(t1 - t0).count();
+  if (first_logits)
+    for (int m = 0; m < M; ++m)
+      CK(cudaMemcpy(first_logits + size_t(m) * c->V, logits_row(c, m), size_t(c->V) * 4,
+                    cudaMemcpyDeviceToHost),
+         "first logits");
+  for (int m = 0; m < M; ++m) n_out[m] = 0;
+  if (maxt == 0) return TMG_OK;
+
+  // device state for the loop
+  if (kv->gen_alloc < int64_t(M) * maxt) {
+    if (kv->d_gen) cudaFree(kv->d_gen);
+    kv->d_gen = nullptr;
+    kv->gen_alloc = 0;
+    CK(cudaMalloc(&kv->d_gen, size_t(M) * maxt * 4), "alloc");
+    kv->gen_alloc = int64_t(M) * maxt;
+  }
+  const bool sampled = params->temperature > 0.f;
+  const bool greedy_fused = !sampled && params->repetition_penalty == 1.0f;
+  if (sampled) {
+    if (kv->uni_alloc < int64_t(M) * maxt) {
+      if (kv->d_uni) cudaFree(kv->d_uni);
+      kv->d_uni = nullptr;
+      kv->uni_alloc = 0;
+      CK(cudaMalloc(&kv->d_uni, size_t(M) * maxt * 4), "alloc");
+      kv->uni_alloc = int64_t(M) * maxt;
+    }
+    std::vector<float> u(size_t(M) * maxt);
+    if (uniforms) std::memcpy(u.data(), uniforms, u.size() * 4);
+    else
+      for (int m = 0; m < M; ++m) stdrng_uniforms(params[m].seed, maxt, u.data() + size_t(m) * maxt);
+    CK(cudaMemcpyAsync(kv->d_uni, u.data(), u.size() * 4, cudaMemcpyHostToDevice, c->stream),
+       "uniforms");
+    CK(cudaStreamSynchronize(c->stream), "uniforms");
+  }
+  StreamState st = kv->st;
+  st.gen = kv->d_gen;
+  st.gen_cap = int32_t(maxt);
+  st.n_eos = c->cfg.n_eos;
+  for (int e = 0; e < c->cfg.n_eos && e < kMaxEos; ++e) st.eos[e] = c->cfg.eos_token_ids[e];
+
+  SampleArgs S;
+  S.logits = const_cast<float*>(logits_row(c, 0));
+  S.V = c->V;
+  S.M = M;
+  S.temperature = params->temperature;
+  S.top_k = int(params->top_k);
+  S.top_p = params->top_p;
+  S.penalty = params->repetition_penalty;
+  S.uniforms = kv->d_uni;
+  S.uni_ld = maxt;
+  S.part = c->sm_part;
+  S.ticket = &c->tickets[1];
+  S.err = c->d_err;
+  S.st = st;
+  S.record = true;
+
+  // first token from the prefill logits
+  if (greedy_fused) {
+    CK(launch_sample(S, c->stream, false, c->num_sms), "argmax");
+  } else {
+    CK(launch_sample(S, c->stream, false, c->num_sms), "sample");
+  }
+  // the per-step graph: forward (+ argmax) [+ sampler]
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "capture");
+  cudaError_t ce = enqueue_forward(c, kv, st, greedy_fused);
+  if (ce == cudaSuccess && !greedy_fused) ce = launch_sample(S, c->stream, true, c->num_sms);
+  cudaError_t ee = cudaStreamEndCapture(c->stream, &graph);
+  if (ce != cudaSuccess) {
+    if (graph) cudaGraphDestroy(graph);
+    return cuda_fail(c, ce, "capture step");
+  }
+  CK(ee, "capture");
+  ce = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  CK(ce, "instantiate");
+
+  // launch max_tokens steps in chunks; read back tokens a chunk behind
+  const int64_t chunk = 8;
+  std::vector<int32_t> h_state(4 * kMaxStreams);
+  std::vector<uint32_t> h_gen(size_t(M) * maxt);
+  int64_t launched = 0;
+  std::vector<int64_t> reported(M, 0);
+  bool stop = false;
+  cudaEvent_t ev[2];
+  CK(cudaEventCreateWithFlags(&ev[0], cudaEventDisableTiming), "event");
+  CK(cudaEventCreateWithFlags(&ev[1], cudaEventDisableTiming), "event");
+  int32_t* pinned_state = nullptr;
+  CK(ensure_pinned(c, sizeof(int32_t) * 4 * kMaxStreams * 2 + size_t(M) * maxt * 4 * 2), "pinned");
+  pinned_state = static_cast<int32_t*>(c->pinned);
+  uint32_t* pinned_gen = reinterpret_cast<uint32_t*>(pinned_state + 8 * kMaxStreams);
+  int pending = -1;
+  auto drain = [&](int slot) -> int {
+    CK(cudaEventSynchronize(ev[slot]), "sync");
+    int32_t* s = pinned_state + slot * 4 * kMaxStreams;
+    uint32_t* g = pinned_gen + size_t(slot) * M * maxt;
+    bool all_done = true;
+    for (int m = 0; m < M; ++m) {
+      const int32_t ng = s[3 * kMaxStreams + m];
+      if (cb && m == 0)
+        for (int64_t i = reported[0]; i < ng && !stop; ++i)
+          if (cb(g[i], user) != 0) stop = true;
+      reported[m] = ng;
+      if (!s[2 * kMaxStreams + m]) all_done = false;
+    }
+    if (all_done) stop = true;
+    return TMG_OK;
+  };
+  while (launched < maxt && !stop) {
+    const int64_t n = std::min<int64_t>(chunk, maxt - launched);
+    for (int64_t i = 0; i < n; ++i) CK(cudaGraphLaunch(exec, c->stream), "graph launch");
+    launched += n;
+    const int slot = int((launched / chunk) & 1);
+    CK(cudaMemcpyAsync(pinned_state + slot * 4 * kMaxStreams, kv->d_state,
+                       sizeof(int32_t) * 4 * kMaxStreams, cudaMemcpyDeviceToHost, c->stream),
+       "state");
+    CK(cudaMemcpyAsync(pinned_gen + size_t(slot) * M * maxt, kv->d_gen, size_t(M) * maxt * 4,
+                       cudaMemcpyDeviceToHost, c->stream),
+       "tokens");
+    CK(cudaEventRecord(ev[slot], c->stream), "event");
+    if (pending >= 0 && (rc = drain(pending))) return rc;
+    pending = slot;
+  }
+  if (pending >= 0 && (rc = drain(pending))) return rc;
+  CK(cudaStreamSynchronize(c->stream), "generate");
+  cudaEventDestroy(ev[0]);
+  cudaEventDestroy(ev[1]);
+  cudaGraphExecDestroy(exec);
+  int32_t err_word = 0;
+  CK(cudaMemcpy(&err_word, c->d_err, 4, cudaMemcpyDeviceToHost), "err");
+  CK(cudaMemcpy(h_state.data(), kv->d_state, h_state.size() * 4, cudaMemcpyDeviceToHost), "state");
+  CK(cudaMemcpy(h_gen.data(), kv->d_gen, h_gen.size() * 4, cudaMemcpyDeviceToHost), "tokens");
+  if (err_word) {
+    CK(cudaMemset(c->d_err, 0, 4), "err");
+    return fail(c, TMG_ERR_NAN, "NaN logits reached the sampler");
+  }
+  for (int m = 0; m < M; ++m) {
+    const int32_t ng = h_state[3 * kMaxStreams + m];
+    n_out[m] = ng;
+    std::memcpy(tokens_out + size_t(m) * maxt, h_gen.data() + size_t(m) * maxt, size_t(ng) * 4);
+    kv->lens[m] = h_state[kMaxStreams + m];
+    if (cb && m == 0)
+      for (int64_t i = reported[0]; i < ng && !stop; ++i)
+        if (cb(h_gen[i], user) != 0) stop = true;
+  }
+  return TMG_OK;
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+const char* tmg_version(void) { return "tinyminigo_b200 0.1 (sm_100a)"; }
+
+float tmg_f16_to_f32(uint16_t h) { return f16_to_f32(h); }
+
+int tmg_config_parse(const char* json_text, tmg_config* out, char* err, int errlen) {
+  std::string e;
+  Json j;
+  if (!json_text || !out) return TMG_ERR_INVALID;
+  if (!json_parse(json_text, std::strlen(json_text), j, e) || !config_from_json(j, out, e)) {
+    if (err && errlen > 0) std::snprintf(err, size_t(errlen), "%s", e.c_str());
+    return TMG_ERR_IO;
+  }
+  return TMG_OK;
+}
+
+int tmg_config_load(const char* path, tmg_config* out, char* err, int errlen) {
+  std::string text, e;
+  if (!path || !out) return TMG_ERR_INVALID;
+  if (!read_file(path, text, e)) {
+    if (err && errlen > 0) std::snprintf(err, size_t(errlen), "%s", e.c_str());
+    return TMG_ERR_IO;
+  }
+  int rc = tmg_config_parse(text.c_str(), out, err, errlen);
+  return rc;
+}
+
+int tmg_safetensors_count(const char* path, int64_t* n, char* err, int errlen) {
+  MappedFile f;
+  std::string e;
+  std::vector<StTensor> ts;
+  if (!path || !n) return TMG_ERR_INVALID;
+  if (!f.open(path, e) || !safetensors_parse(f.data(), f.size, ts, e)) {
+    if (err && errlen > 0) std::snprintf(err, size_t(errlen), "%s", e.c_str());
+    return TMG_ERR_IO;
+  }
+  *n = int64_t(ts.size());
+  return TMG_OK;
+}
+
+int tmg_safetensors_info(const char* path, int64_t i, char* name, int namelen, int32_t* dtype,
+                         int32_t* rank, int64_t shape[4], int64_t* offset, int64_t* nbytes,
+                         char* err, int errlen) {
+  MappedFile f;
+  std::string e;
+  std::vector<StTensor> ts;
+  if (!path) return TMG_ERR_INVALID;
+  if (!f.open(path, e) || !safetensors_parse(f.data(), f.size, ts, e)) {
+    if (err && errlen > 0) std::snprintf(err, size_t(errlen), "%s", e.c_str());
+    return TMG_ERR_IO;
+  }
+  if (i < 0 || i >= int64_t(ts.size())) return TMG_ERR_INVALID;
+  const StTensor& t = ts[size_t(i)];
+  if (name && namelen > 0) std::snprintf(name, size_t(namelen), "%s", t.name.c_str());
+  if (dtype) *dtype = t.dtype;
+  if (rank) *rank = int32_t(t.shape.size());
+  if (shape)
+    for (int k = 0; k < 4; ++k) shape[k] = k < int(t.shape.size()) ? t.shape[k] : 0;
+  if (offset) *offset = t.offset;
+  if (nbytes) *nbytes = t.nbytes;
+  return TMG_OK;
+}
+
+int tmg_rng_uniforms(uint64_t seed, int64_t n, float* out) {
+  if (n < 0 || (n > 0 && !out)) return TMG_ERR_INVALID;
+  stdrng_uniforms(seed, n, out);
+  return TMG_OK;
+}
+
+int tmg_create(int device, const tmg_config* cfg, tmg_ctx** out) {
+  if (!out) return TMG_ERR_INVALID;
+  *out = nullptr;
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n <= device || device < 0) return TMG_ERR_CUDA;
+  tmg_ctx* c = new tmg_ctx();
+  c->device = device;
+  if (cudaSetDevice(device) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
+      gemv_prepare() != cudaSuccess || attn_prepare() != cudaSuccess) {
+    delete c;
+    return TMG_ERR_CUDA;
+  }
+  if (cfg) {
+    c->cfg = *cfg;
+    c->has_model = true;  // allocation happens at the first weight (after a TP init)
+    c->h = 0;
+  }
+  *out = c;
+  return TMG_OK;
+}
+
+int tmg_destroy(tmg_ctx* c) {
+  if (!c) return TMG_ERR_INVALID;
+  cudaSetDevice(c->device);
+  cudaStreamSynchronize(c->stream);
+  free_all(c->allocs);
+  for (void* p : {(void*)c->X, (void*)c->Xn, (void*)c->QKV, (void*)c->ATT, (void*)c->G,
+                  (void*)c->U, (void*)c->d_tok, c->op_buf})
+    if (p) cudaFree(p);
+  if (c->pinned) cudaFreeHost(c->pinned);
+  if (c->tp) tp_destroy(c->tp);
+  cudaStreamDestroy(c->stream);
+  delete c;
+  return TMG_OK;
+}
+
+const char* tmg_last_error(const tmg_ctx* c) { return c ? c->err.c_str() : "null context"; }
+
+static int ensure_alloc(tmg_ctx* c) {
+  if (!c->has_model) return fail(c, TMG_ERR_INVALID, "context has no model config");
+  if (c->h == 0) return alloc_model(c);
+  return TMG_OK;
+}
+
+int tmg_set_tensor(tmg_ctx* c, const char* name, int32_t dtype, const void* host, int64_t numel) {
+  if (!c || !name || !host || numel <= 0) return fail(c, TMG_ERR_INVALID, "bad argument");
+  cudaSetDevice(c->device);
+  int rc = ensure_alloc(c);
+  if (rc) return rc;
+  return set_tensor(c, name, dtype, host, numel);
+}
+
+int tmg_load_safetensors(tmg_ctx* c, const char* path) {
+  if (!c || !path) return fail(c, TMG_ERR_INVALID, "bad argument");
+  cudaSetDevice(c->device);
+  int rc = ensure_alloc(c);
+  if (rc) return rc;
+  MappedFile f;
+  std::string e;
+  std::vector<StTensor> ts;
+  if (!f.open(path, e) || !safetensors_parse(f.data(), f.size, ts, e))
+    return fail(c, TMG_ERR_IO, e);
+  for (const StTensor& t : ts) {
+    int64_t numel = t.nbytes / (t.dtype == 0 ? 4 : 2);
+    rc = set_tensor(c, t.name, t.dtype, f.data() + t.offset, numel);
+    if (rc) return rc;
+  }
+  CK(cudaStreamSynchronize(c->stream), "load");
+  return finalize(c);
+}
+
+int tmg_finalize(tmg_ctx* c) {
+  if (!c) return TMG_ERR_INVALID;
+  cudaSetDevice(c->device);
+  return finalize(c);
+}
+
+int64_t tmg_weight_bytes(const tmg_ctx* c) { return c ? c->weight_bytes : 0; }
+
+int tmg_kv_create(tmg_ctx* c, int32_t n_streams, int64_t capacity, tmg_kv** out) {
+  if (!c || !out || n_streams < 1 || n_streams > kMaxStreams || capacity < 1)
+    return fail(c, TMG_ERR_INVALID, "bad KV cache shape (1..16 streams)");
+  if (!c->finalized) return fail(c, TMG_ERR_INVALID, "weights not finalized");
+  cudaSetDevice(c->device);
+  tmg_kv* kv = new tmg_kv();
+  kv->ctx = c;
+  kv->M = n_streams;
+  kv->cap = capacity;
+  kv->kvd = c->nkv * c->d;
+  kv->lens.assign(n_streams, 0);
+  auto bail = [&](cudaError_t e) {
+    free_all(kv->allocs);
+    delete kv;
+    return cuda_fail(c, e, "KV cache allocation");
+  };
+  cudaError_t e;
+  for (int l = 0; l < c->L; ++l) {
+    float *kp, *vp;
+    if ((e = dalloc(kv->allocs, &kp, size_t(n_streams) * capacity * kv->kvd)) != cudaSuccess) return bail(e);
+    if ((e = dalloc(kv->allocs, &vp, size_t(n_streams) * capacity * kv->kvd)) != cudaSuccess) return bail(e);
+    kv->k.push_back(kp);
+    kv->v.push_back(vp);
+  }
+  const int half = c->d / 2;
+  if ((e = dalloc(kv->allocs, &kv->rope_cos, size_t(capacity) * half)) != cudaSuccess) return bail(e);
+  if ((e = dalloc(kv->allocs, &kv->rope_sin, size_t(capacity) * half)) != cudaSuccess) return bail(e);
+  std::vector<float> tc = rope_table(c->d, c->cfg.rope_theta, capacity, false);
+  std::vector<float> ts = rope_table(c->d, c->cfg.rope_theta, capacity, true);
+  if ((e = cudaMemcpy(kv->rope_cos, tc.data(), tc.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess) return bail(e);
+  if ((e = cudaMemcpy(kv->rope_sin, ts.data(), ts.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess) return bail(e);
+  if ((e = dalloc(kv->allocs, &kv->d_state, 4 * kMaxStreams)) != cudaSuccess) return bail(e);
+  if ((e = cudaMemset(kv->d_state, 0, 16 * kMaxStreams)) != cudaSuccess) return bail(e);
+  kv->st.token = reinterpret_cast<uint32_t*>(kv->d_state);
+  kv->st.pos = kv->d_state + kMaxStreams;
+  kv->st.done = kv->d_state + 2 * kMaxStreams;
+  kv->st.n_gen = kv->d_state + 3 * kMaxStreams;
+  kv->st.gen = nullptr;
+  kv->st.gen_cap = 0;
+  kv->st.n_eos = 0;
+  kv->nsplit = attn_decode_nsplit(c->nkv, n_streams, capacity, c->num_sms);
+  const int G = c->nq / c->nkv;
+  if ((e = dalloc(kv->allocs, &kv->part, size_t(n_streams) * c->nkv * kv->nsplit * G * (c->d + 2))) != cudaSuccess) return bail(e);
+  if ((e = dalloc(kv->allocs, &kv->att_ticket, size_t(n_streams) * c->nkv)) != cudaSuccess) return bail(e);
+  if ((e = cudaMemset(kv->att_ticket, 0, size_t(n_streams) * c->nkv * 4)) != cudaSuccess) return bail(e);
+  *out = kv;
+  return TMG_OK;
+}
+
+int tmg_kv_destroy(tmg_kv* kv) {
+  if (!kv) return TMG_ERR_INVALID;
+  cudaSetDevice(kv->ctx->device);
+  cudaStreamSynchronize(kv->ctx->stream);
+  if (kv->g_plain) cudaGraphExecDestroy(kv->g_plain);
+  if (kv->g_dec) cudaGraphExecDestroy(kv->g_dec);
+  if (kv->state_ev) cudaEventDestroy(kv->state_ev);
+  if (kv->h_state) cudaFreeHost(kv->h_state);
+  if (kv->d_gen) cudaFree(kv->d_gen);
+  if (kv->d_uni) cudaFree(kv->d_uni);
+  free_all(kv->allocs);
+  delete kv;
+  return TMG_OK;
+}
+
+int tmg_kv_len(const tmg_kv* kv, int32_t layer, int32_t stream, int64_t* out) {
+  if (!kv || !out || stream < 0 || stream >= kv->M || layer < 0 || layer >= kv->ctx->L)
+    return TMG_ERR_INVALID;
+  *out = kv->lens[stream];
+  return TMG_OK;
+}
+
+int tmg_kv_reset(tmg_kv* kv) {
+  if (!kv) return TMG_ERR_INVALID;
+  tmg_ctx* c = kv->ctx;
+  cudaSetDevice(c->device);
+  int rc = reset_state(c, kv);
+  if (rc) return rc;
+  CK(cudaStreamSynchronize(c->stream), "reset");
+  return TMG_OK;
+}
+
+int tmg_kv_truncate(tmg_kv* kv, int32_t stream, int64_t len) {
+  if (!kv || stream < 0 || stream >= kv->M || len < 0 || len > kv->lens[stream])
+    return fail(kv ? kv->ctx : nullptr, TMG_ERR_INVALID, "bad truncate length");
+  kv->lens[stream] = len;  // the device position is uploaded by the next forward
+  return TMG_OK;
+}
+
+int tmg_kv_read(tmg_kv* kv, int32_t layer, int32_t stream, float* keys, float* values) {
+  if (!kv || stream < 0 || stream >= kv->M || layer < 0 || layer >= kv->ctx->L)
+    return TMG_ERR_INVALID;
+  tmg_ctx* c = kv->ctx;
+  cudaSetDevice(c->device);
+  CK(cudaStreamSynchronize(c->stream), "kv read");
+  const size_t n = size_t(kv->lens[stream]) * kv->kvd;
+  const size_t off = size_t(stream) * kv->cap * kv->kvd;
+  if (keys) CK(cudaMemcpy(keys, kv->k[layer] + off, n * 4, cudaMemcpyDeviceToHost), "kv read");
+  if (values) CK(cudaMemcpy(values, kv->v[layer] + off, n * 4, cudaMemcpyDeviceToHost), "kv read");
+  return TMG_OK;
+}
+
+int tmg_forward_token(tmg_ctx* c, tmg_kv* kv, const uint32_t* tokens, float* logits) {
+  if (!c || !kv || !tokens || kv->ctx != c) return fail(c, TMG_ERR_INVALID, "bad argument");
+  if (!c->finalized) return fail(c, TMG_ERR_INVALID, "weights not finalized");
+  cudaSetDevice(c->device);
+  for (int m = 0; m < kv->M; ++m) {
+    if (tokens[m] >= uint32_t(c->V)) return fail(c, TMG_ERR_INVALID, "token id out of range");
+    if (kv->lens[m] + 1 > kv->cap) return fail(c, TMG_ERR_CAPACITY, "KV cache full");
+  }
+  // state: the tokens; not done; no recording; pos from the host mirror
+  std::vector<int32_t> s(4 * kMaxStreams, 0);
+  for (int m = 0; m < kv->M; ++m) {
+    s[m] = int32_t(tokens[m]);
+    s[kMaxStreams + m] = int32_t(kv->lens[m]);
+  }
+  CK(ensure_pinned(c, s.size() * 4), "pinned");
+  CK(cudaStreamSynchronize(c->stream), "forward");
+  std::memcpy(c->pinned, s.data(), s.size() * 4);
+  CK(cudaMemcpyAsync(kv->d_state, c->pinned, s.size() * 4, cudaMemcpyHostToDevice, c->stream),
+     "tokens");
+  if (!kv->g_plain) {
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "capture");
+    cudaError_t ce = enqueue_forward(c, kv, kv->st, false);
+    cudaError_t ee = cudaStreamEndCapture(c->stream, &g);
+    if (ce != cudaSuccess) {
+      if (g) cudaGraphDestroy(g);
+      return cuda_fail(c, ce, "capture forward");
+    }
+    CK(ee, "capture");
+    ce = cudaGraphInstantiate(&kv->g_plain, g, 0);
+    cudaGraphDestroy(g);
+    CK(ce, "instantiate");
+  }
+  CK(cudaGraphLaunch(kv->g_plain, c->stream), "forward");
+  if (logits)
+    for (int m = 0; m < kv->M; ++m)
+      CK(cudaMemcpyAsync(logits + size_t(m) * c->V, logits_row(c, m), size_t(c->V) * 4,
+                         cudaMemcpyDeviceToHost, c->stream),
+         "logits");
+  CK(cudaStreamSynchronize(c->stream), "forward");
+  for (int m = 0; m < kv->M; ++m) kv->lens[m] += 1;
+  return TMG_OK;
+}
+
+int tmg_forward_seq(tmg_ctx* c, tmg_kv* kv, int32_t stream, const uint32_t* tokens, int64_t T,
+                    float* logits) {
+  if (!c || !kv || kv->ctx != c || stream < 0 || stream >= kv->M)
+    return fail(c, TMG_ERR_INVALID, "bad argument");
+  if (T <= 0 || !tokens) return fail(c, TMG_ERR_INVALID, "empty prompt");
+  if (!c->finalized) return fail(c, TMG_ERR_INVALID, "weights not finalized");
+  if (kv->lens[stream] + T > kv->cap) return fail(c, TMG_ERR_CAPACITY, "KV cache full");
+  for (int64_t i = 0; i < T; ++i)
+    if (tokens[i] >= uint32_t(c->V)) return fail(c, TMG_ERR_INVALID, "token id out of range");
+  cudaSetDevice(c->device);
+  int rc = forward_seq(c, kv, stream, tokens, T, true);
+  if (rc) return rc;
+  if (logits)
+    CK(cudaMemcpyAsync(logits, logits_row(c, stream), size_t(c->V) * 4, cudaMemcpyDeviceToHost,
+                       c->stream),
+       "logits");
+  CK(cudaStreamSynchronize(c->stream), "forward_seq");
+  return TMG_OK;
+}
+
+int tmg_generate(tmg_ctx* c, tmg_kv* kv, const uint32_t* prompt, int64_t T,
+                 const tmg_gen_params* params, const float* uniforms, uint32_t* tokens_out,
+                 int64_t* n_out, float* first_logits, double* prefill_secs, tmg_token_cb cb,
+                 void* user) {
+  if (!c || !kv || kv->ctx != c || !prompt || !params || !n_out ||
+      (params->max_tokens > 0 && !tokens_out))
+    return fail(c, TMG_ERR_INVALID, "bad argument");
+  if (kv->M != 1) return fail(c, TMG_ERR_INVALID, "tmg_generate needs a 1-stream cache");
+  cudaSetDevice(c->device);
+  return run_generate(c, kv, prompt, T, params, uniforms, tokens_out, n_out, first_logits,
+                      prefill_secs, cb, user);
+}
+
+int tmg_generate_batch(tmg_ctx* c, tmg_kv* kv, const uint32_t* prompts, int64_t T,
+                       const tmg_gen_params* params, const float* uniforms, uint32_t* tokens_out,
+                       int64_t* n_out) {
+  if (!c || !kv || kv->ctx != c || !prompts || !params || !n_out)
+    return fail(c, TMG_ERR_INVALID, "bad argument");
+  cudaSetDevice(c->device);
+  return run_generate(c, kv, prompts, T, params, uniforms, tokens_out, n_out, nullptr, nullptr,
+                      nullptr, nullptr);
+}
+
+// Upload (token, pos = host length, done = 0, n_gen = 0) for every stream
+// through a pinned staging block that is reused only after its previous
+// copy has executed.
+static int upload_state(tmg_ctx* c, tmg_kv* kv, const uint32_t* tokens) {
+  if (!kv->h_state) {
+    CK(cudaHostAlloc(reinterpret_cast<void**>(&kv->h_state), 16 * kMaxStreams,
+                     cudaHostAllocDefault),
+       "pinned");
+    CK(cudaEventCreateWithFlags(&kv->state_ev, cudaEventDisableTiming), "event");
+  } else {
+    CK(cudaEventSynchronize(kv->state_ev), "state");
+  }
+  std::memset(kv->h_state, 0, 16 * kMaxStreams);
+  for (int m = 0; m < kv->M; ++m) {
+    kv->h_state[m] = int32_t(tokens[m]);
+    kv->h_state[kMaxStreams + m] = int32_t(kv->lens[m]);
+  }
+  CK(cudaMemcpyAsync(kv->d_state, kv->h_state, 16 * kMaxStreams, cudaMemcpyHostToDevice,
+                     c->stream),
+     "state");
+  CK(cudaEventRecord(kv->state_ev, c->stream), "state");
+  return TMG_OK;
+}
+
+static int prepare_decode(tmg_ctx* c, tmg_kv* kv, const uint32_t* tokens, int64_t n_steps,
+                          StreamState* st) {
+  if (!c->finalized) return fail(c, TMG_ERR_INVALID, "weights not finalized");
+  if (n_steps < 1 || n_steps > (int64_t(1) << 30)) return fail(c, TMG_ERR_INVALID, "bad n_steps");
+  for (int m = 0; m < kv->M; ++m) {
+    if (tokens[m] >= uint32_t(c->V)) return fail(c, TMG_ERR_INVALID, "token id out of range");
+    if (kv->lens[m] + n_steps > kv->cap) return fail(c, TMG_ERR_CAPACITY, "KV cache full");
+  }
+  if (kv->gen_alloc < int64_t(kv->M) * n_steps) {
+    CK(cudaStreamSynchronize(c->stream), "decode");
+    if (kv->d_gen) cudaFree(kv->d_gen);
+    kv->d_gen = nullptr;
+    kv->gen_alloc = 0;
+    CK(cudaMalloc(&kv->d_gen, size_t(kv->M) * n_steps * 4), "alloc");
+    kv->gen_alloc = int64_t(kv->M) * n_steps;
+    if (kv->g_dec) cudaGraphExecDestroy(kv->g_dec);
+    kv->g_dec = nullptr;
+  }
+  int rc = upload_state(c, kv, tokens);
+  if (rc) return rc;
+  *st = kv->st;
+  st->gen = kv->d_gen;
+  st->gen_cap = int32_t(n_steps);
+  st->n_eos = 0;
+  return TMG_OK;
+}
+
+int tmg_decode(tmg_ctx* c, tmg_kv* kv, const uint32_t* tokens, int64_t n_steps, uint32_t* out) {
+  if (!c || !kv || kv->ctx != c || !tokens) return fail(c, TMG_ERR_INVALID, "bad argument");
+  cudaSetDevice(c->device);
+  StreamState st;
+  int rc = prepare_decode(c, kv, tokens, n_steps, &st);
+  if (rc) return rc;
+  if (!kv->g_dec || kv->dec_cap != n_steps) {
+    if (kv->g_dec) cudaGraphExecDestroy(kv->g_dec);
+    kv->g_dec = nullptr;
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "capture");
+    cudaError_t ce = enqueue_forward(c, kv, st, true);
+    cudaError_t ee = cudaStreamEndCapture(c->stream, &g);
+    if (ce != cudaSuccess) {
+      if (g) cudaGraphDestroy(g);
+      return cuda_fail(c, ce, "capture decode");
+    }
+    CK(ee, "capture");
+    ce = cudaGraphInstantiate(&kv->g_dec, g, 0);
+    cudaGraphDestroy(g);
+    CK(ce, "instantiate");
+    kv->dec_cap = n_steps;
+  }
+  for (int64_t i = 0; i < n_steps; ++i) CK(cudaGraphLaunch(kv->g_dec, c->stream), "decode");
+  for (int m = 0; m < kv->M; ++m) kv->lens[m] += n_steps;
+  if (out) {
+    CK(cudaMemcpyAsync(out, kv->d_gen, size_t(kv->M) * n_steps * 4, cudaMemcpyDeviceToHost,
+                       c->stream),
+       "tokens");
+    CK(cudaStreamSynchronize(c->stream), "decode");
+  }
+  return TMG_OK;
+}
+
+int tmg_sync(tmg_ctx* c) {
+  if (!c) return TMG_ERR_INVALID;
+  cudaSetDevice(c->device);
+  CK(cudaStreamSynchronize(c->stream), "sync");
+  return TMG_OK;
+}
+
+void* tmg_stream(tmg_ctx* c) { return c ? static_cast<void*>(c->stream) : nullptr; }
+
+int tmg_profile_decode(tmg_ctx* c, tmg_kv* kv, const uint32_t* tokens, int64_t n_steps,
+                       double* ms, int64_t* launches) {
+  if (!c || !kv || kv->ctx != c || !tokens || !ms || !launches)
+    return fail(c, TMG_ERR_INVALID, "bad argument");
+  cudaSetDevice(c->device);
+  StreamState st;
+  int rc = prepare_decode(c, kv, tokens, n_steps, &st);
+  if (rc) return rc;
+  Prof prof;
+  prof.s = c->stream;
+  for (int64_t i = 0; i < n_steps; ++i) {
+    cudaError_t e = enqueue_forward(c, kv, st, true, &prof);
+    if (e != cudaSuccess) return cuda_fail(c, e, "profile");
+  }
+  CK(cudaStreamSynchronize(c->stream), "profile");
+  for (int k = 0; k < 6; ++k) {
+    ms[k] = 0.0;
+    launches[k] = 0;
+  }
+  for (auto& m : prof.marks) {
+    float t = 0.f;
+    CK(cudaEventElapsedTime(&t, m.second.first, m.second.second), "elapsed");
+    ms[m.first] += t;
+    launches[m.first] += 1;
+  }
+  for (int m = 0; m < kv->M; ++m) kv->lens[m] += n_steps;
+  return TMG_OK;
+}
+
+int tmg_tp_unique_id(uint8_t id[128]) { return tp_unique_id(id) == 0 ? TMG_OK : TMG_ERR_NCCL; }
+
+int tmg_tp_init(tmg_ctx* c, const uint8_t id[128], int32_t rank, int32_t world) {
+  if (!c || !id || world < 1 || rank < 0 || rank >= world) return fail(c, TMG_ERR_INVALID, "bad argument");
+  if (c->h != 0) return fail(c, TMG_ERR_INVALID, "tmg_tp_init must precede the weight upload");
+  cudaSetDevice(c->device);
+  std::string e;
+  c->tp = tp_create(id, rank, world, e);
+  if (!c->tp) return fail(c, TMG_ERR_NCCL, e);
+  c->rank = rank;
+  c->world = world;
+  return TMG_OK;
+}
+
+// --- op level ---------------------------------------------------------------
+int tmg_op_gemv_bf16(tmg_ctx* c, const float* x, const uint16_t* w, int64_t N, int64_t K,
+                     int32_t M, float* y) {
+  if (!c || !x || !w || !y || N <= 0 || K <= 0 || M < 1 || M > kMaxStreams)
+    return fail(c, TMG_ERR_INVALID, "bad argument");
+  cudaSetDevice(c->device);
+  GemvArgs a;
+  a.w = w;
+  a.x = x;
+  a.y = y;
+  a.ldy = N;
+  a.N = N;
+  a.K = int(K);
+  a.M = M;
+  CK(launch_gemv(a, PRO_NONE, EPI_STORE, c->stream, false, c->num_sms), "gemv");
+  CK(cudaStreamSynchronize(c->stream), "gemv");
+  return TMG_OK;
+}
+
+int tmg_op_gemm_bf16(tmg_ctx* c, const float* x, const uint16_t* w, int64_t N, int64_t K,
+                     int64_t T, float* y) {
+  if (!c || !x || !w || !y || N <= 0 || K <= 0 || T <= 0)
+    return fail(c, TMG_ERR_INVALID, "bad argument");
+  cudaSetDevice(c->device);
+  CK(gemm(c, x, w, T, N, K, y, N, false), "gemm");
+  CK(cudaStreamSynchronize(c->stream), "gemm");
+  return TMG_OK;
+}
+
+int tmg_op_rmsnorm(tmg_ctx* c, const float* x, const float* w, float eps, int64_t n, int64_t rows,
+                   int32_t mode, float* out) {
+  if (!c || !x || !w || !out || n <= 0 || rows <= 0 || (mode != 0 && mode != 1))
+    return fail(c, TMG_ERR_INVALID, "bad argument");
+  cudaSetDevice(c->device);
+  CK(launch_rmsnorm(x, w, eps, n, rows, mode, out, c->stream), "rmsnorm");
+  CK(cudaStreamSynchronize(c->stream), "rmsnorm");
+  return TMG_OK;
+}
+
+int tmg_op_rope(tmg_ctx* c, float* x, int64_t rows, int32_t n_heads, int32_t head_dim,
+                int64_t pos0, float theta) {
+  if (!c || !x || rows <= 0 || n_heads <= 0 || head_dim <= 0 || head_dim % 2 || pos0 < 0)
+    return fail(c, TMG_ERR_INVALID, "bad argument");
+  cudaSetDevice(c->device);
+  const int64_t np = pos0 + rows;
+  std::vector<float> tc = rope_table(head_dim, theta, np, false);
+  std::vector<float> ts = rope_table(head_dim, theta, np, true);
+  const size_t bytes = tc.size() * 4;
+  CK(ensure_op(c, 2 * bytes + 64), "op scratch");
+  float* dc = static_cast<float*>(c->op_buf);
+  float* ds = dc + tc.size();
+  CK(cudaMemcpy(dc, tc.data(), bytes, cudaMemcpyHostToDevice), "rope table");
+  CK(cudaMemcpy(ds, ts.data(), bytes, cudaMemcpyHostToDevice), "rope table");
+  CK(launch_rope_rows(x, int64_t(n_heads) * head_dim, rows, n_heads, head_dim, dc, ds, pos0,
+                      c->stream),
+     "rope");
+  CK(cudaStreamSynchronize(c->stream), "rope");
+  return TMG_OK;
+}
+
+int tmg_op_swiglu(tmg_ctx* c, const float* gate, const float* up, int64_t n, float* out) {
+  if (!c || !gate || !up || !out || n <= 0) return fail(c, TMG_ERR_INVALID, "bad argument");
+  cudaSetDevice(c->device);
+  CK(launch_swiglu(gate, up, n, out, c->stream), "swiglu");
+  CK(cudaStreamSynchronize(c->stream), "swiglu");
+  return TMG_OK;
+}
+
+int tmg_op_attn_decode(tmg_ctx* c, const float* q, const float* keys, const float* values,
+                       int64_t n_ctx, int32_t n_q, int32_t n_kv, int32_t head_dim, float* out) {
+  if (!c || !q || !keys || !values || !out || n_ctx <= 0 || n_q <= 0 || n_kv <= 0 ||
+      n_q % n_kv || head_dim <= 0 || head_dim % 8)
+    return fail(c, TMG_ERR_INVALID, "bad argument");
+  cudaSetDevice(c->device);
+  const int G = n_q / n_kv;
+  const int nsplit = attn_decode_nsplit(n_kv, 1, n_ctx, c->num_sms);
+  const size_t part_f = size_t(n_kv) * nsplit * G * (head_dim + 2);
+  CK(ensure_op(c, part_f * 4 + 4096), "op scratch");
+  AttnDecodeArgs a;
+  a.qkv = q;
+  a.qkv_ld = 0;
+  a.kc = const_cast<float*>(keys);
+  a.vc = const_cast<float*>(values);
+  a.cap = n_ctx;
+  a.out = out;
+  a.part = static_cast<float*>(c->op_buf);
+  a.ticket = reinterpret_cast<unsigned int*>(static_cast<char*>(c->op_buf) + part_f * 4);
+  int32_t* posv = reinterpret_cast<int32_t*>(static_cast<char*>(c->op_buf) + part_f * 4 + 2048);
+  const int32_t pv = int32_t(n_ctx - 1);
+  CK(cudaMemsetAsync(a.ticket, 0, 1024, c->stream), "memset");
+  CK(cudaMemcpyAsync(posv, &pv, 4, cudaMemcpyHostToDevice, c->stream), "pos");
+  a.pos_override = posv;
+  a.nq = n_q;
+  a.nkv = n_kv;
+  a.d = head_dim;
+  a.nsplit = nsplit;
+  a.M = 1;
+  a.scale = 1.0f / sqrtf(float(head_dim));
+  CK(launch_attn_decode(a, c->stream, false), "attention");
+  CK(cudaStreamSynchronize(c->stream), "attention");
+  return TMG_OK;
+}
+
+int tmg_op_attn_prefill(tmg_ctx* c, const float* q, const float* keys, const float* values,
+                        int64_t T, int64_t start_pos, int32_t n_q, int32_t n_kv, int32_t head_dim,
+                        float* out) {
+  if (!c || !q || !keys || !values || !out || T <= 0 || start_pos < 0 || n_q <= 0 ||
+      n_kv <= 0 || n_q % n_kv)
+    return fail(c, TMG_ERR_INVALID, "bad argument");
+  cudaSetDevice(c->device);
+  CK(launch_attn_prefill(q, int64_t(n_q) * head_dim, keys, values, T, start_pos, n_q, n_kv,
+                         head_dim, 1.0f / sqrtf(float(head_dim)), out, int64_t(n_q) * head_dim,
+                         c->stream),
+     "attention");
+  CK(cudaStreamSynchronize(c->stream), "attention");
+  return TMG_OK;
+}
+
+int tmg_op_argmax(tmg_ctx* c, const float* logits, int64_t V, int32_t rows, uint32_t* out) {
+  if (!c || !logits || !out || V <= 0 || rows <= 0) return fail(c, TMG_ERR_INVALID, "bad argument");
+  cudaSetDevice(c->device);
+  CK(launch_argmax_rows(logits, V, rows, out, c->stream), "argmax");
+  CK(cudaStreamSynchronize(c->stream), "argmax");
+  return TMG_OK;
+}
+
+int tmg_op_sample(tmg_ctx* c, float* logits, int64_t V, int32_t rows, const uint32_t* generated,
+                  int64_t n_gen, float temperature, int64_t top_k, float top_p, float penalty,
+                  const float* uniforms, uint32_t* next, uint32_t* cand_ids, float* cand_probs,
+                  int32_t* cutoff) {
+  if (!c || !logits || !next || V <= 0 || rows < 1 || rows > kMaxStreams || n_gen < 0 ||
+      (n_gen > 0 && !generated))
+    return fail(c, TMG_ERR_INVALID, "bad argument");
+  if (temperature > 0.f && (top_k < 1 || top_k > kMaxTopK || top_k >= V))
+    return fail(c, TMG_ERR_INVALID, "device sampling needs 1 <= top_k <= 64");
+  if (temperature > 0.f && !uniforms) return fail(c, TMG_ERR_INVALID, "uniforms required");
+  cudaSetDevice(c->device);
+  const int ns = sample_slices(V, rows, c->num_sms);
+  const size_t part_b = size_t(rows) * ns * kMaxTopK * 8;
+  CK(ensure_op(c, part_b + 4096), "op scratch");
+  SampleArgs a;
+  a.logits = logits;
+  a.V = V;
+  a.M = rows;
+  a.generated = generated;
+  a.gen_ld = n_gen;
+  a.n_gen_fixed = n_gen;
+  a.temperature = temperature;
+  a.top_k = int(top_k);
+  a.top_p = top_p;
+  a.penalty = penalty;
+  a.uniforms = uniforms;
+  a.uni_ld = 1;
+  a.next = next;
+  a.cand_ids = cand_ids;
+  a.cand_probs = cand_probs;
+  a.cutoff = cutoff;
+  a.part = static_cast<unsigned long long*>(c->op_buf);
+  a.ticket = reinterpret_cast<unsigned int*>(static_cast<char*>(c->op_buf) + part_b);
+  a.err = reinterpret_cast<int32_t*>(static_cast<char*>(c->op_buf) + part_b + 1024);
+  CK(cudaMemsetAsync(a.ticket, 0, 2048, c->stream), "memset");
+  CK(launch_sample(a, c->stream, false, c->num_sms), "sample");
+  int32_t errw = 0;
+  CK(cudaMemcpyAsync(&errw, a.err, 4, cudaMemcpyDeviceToHost, c->stream), "err");
+  CK(cudaStreamSynchronize(c->stream), "sample");
+  if (errw) return fail(c, TMG_ERR_NAN, "NaN logits reached the sampler");
+  return TMG_OK;
+}
+
+}  // extern "C"

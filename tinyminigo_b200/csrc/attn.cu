@@ -1,0 +1,404 @@
+// Attention for the token loop.
+//
+// Decode (src/model.rs:420-459): RoPE of q and k at pos (Rope::rotate,
+// src/tensor.rs:1026-1037, from the host-built cos/sin table), the KV append
+// (KvCache::push, model.rs:288-293), and GQA attention of each query head
+// over the stream's cached rows, kv_head = head / (n_q / n_kv).  The context
+// is split over CTAs (split-KV); each CTA keeps an online softmax per head
+// of its GQA group and reads every K/V row of its range once for all G heads
+// of the group; the last CTA of a (stream, kv head) combines the partials.
+// HBM-bound for long contexts: algorithmic bytes = 2 * n_ctx * kv_dim * 4
+// per layer and stream.
+//
+// Prefill (attention_batch, src/tensor.rs:1099-1139): causal attention of T
+// query rows over the cache, one thread (or two, for head_dim 128) per
+// query row, K/V tiles staged in shared memory, online softmax in f32.
+#include <math.h>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace tmg {
+
+namespace {
+
+constexpr int kAttnThreads = 128;
+constexpr int kTile = 32;  // positions per shared-memory tile
+
+// Rotate pair (a, b) by (c, s): (a c - b s, a s + b c), rounded like the
+// reference (two products, then one add/sub; no FMA contraction).
+__device__ __forceinline__ void rot(float a, float b, float c, float s, float* o0, float* o1) {
+  float ac = __fmul_rn(a, c), bs = __fmul_rn(b, s), as = __fmul_rn(a, s), bc = __fmul_rn(b, c);
+  *o0 = __fsub_rn(ac, bs);
+  *o1 = __fadd_rn(as, bc);
+}
+
+// Grid (n_kv, nsplit, M); 128 threads.  Dynamic smem: q [G][d], K tile
+// [kTile][d+4], V tile [kTile][d], p [G][kTile].
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDecodeArgs a) {
+  extern __shared__ float sm[];
+  __shared__ float m_s[16], l_s[16], alpha_s[16];
+  __shared__ bool last_s;
+  const int kvh = blockIdx.x, split = blockIdx.y, m = blockIdx.z;
+  const int d = a.d, half = d / 2, G = a.nq / a.nkv, kvd = a.nkv * d;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float* qs = sm;                      // [G][d]
+  float* ks_ = qs + G * d;             // [kTile][d+4]
+  float* vs = ks_ + kTile * (d + 4);   // [kTile][d]
+  float* ps = vs + kTile * d;          // [G][kTile]
+
+  pdl_trigger();
+  pdl_wait();
+
+  const bool fixed = a.pos_override != nullptr;
+  const int pos = fixed ? a.pos_override[m] : a.st.pos[m];
+  const bool done = fixed ? true : (a.st.done[m] != 0);
+  const bool append = !done && pos < a.cap;
+  const int n_ctx = fixed ? pos + 1 : (append ? pos + 1 : pos);
+  const float* qkv = a.qkv + size_t(m) * a.qkv_ld;
+  float* kc = a.kc + size_t(m) * a.cap * kvd;
+  float* vc = a.vc + size_t(m) * a.cap * kvd;
+
+  // q heads of this group, rotated at pos (model.rs:422-426)
+  const int rp = pos < a.cap ? pos : 0;
+  for (int i = tid; i < G * half; i += blockDim.x) {
+    const int g = i / half, j = i % half;
+    const float* qh = qkv + (kvh * G + g) * d;
+    if (fixed) {
+      qs[g * d + j] = qh[j];
+      qs[g * d + j + half] = qh[j + half];
+    } else {
+      float o0, o1;
+      rot(qh[j], qh[j + half], a.rope_cos[size_t(rp) * half + j], a.rope_sin[size_t(rp) * half + j],
+          &o0, &o1);
+      qs[g * d + j] = o0;
+      qs[g * d + j + half] = o1;
+    }
+  }
+  // context range of this split
+  int chunk = (n_ctx + a.nsplit - 1) / a.nsplit;
+  const int c0 = split * chunk;
+  const int c1 = min(n_ctx, c0 + chunk);
+  // the CTA whose range holds pos appends the rotated k and raw v
+  if (append && pos >= c0 && pos < c1) {
+    const float* kh = qkv + a.nq * d + kvh * d;
+    const float* vh = qkv + (a.nq + a.nkv) * d + kvh * d;
+    float* kdst = kc + size_t(pos) * kvd + kvh * d;
+    float* vdst = vc + size_t(pos) * kvd + kvh * d;
+    for (int j = tid; j < half; j += blockDim.x) {
+      float o0, o1;
+      rot(kh[j], kh[j + half], a.rope_cos[size_t(pos) * half + j],
+          a.rope_sin[size_t(pos) * half + j], &o0, &o1);
+      kdst[j] = o0;
+      kdst[j + half] = o1;
+    }
+    for (int j = tid; j < d; j += blockDim.x) vdst[j] = vh[j];
+  }
+  if (tid < G) {
+    m_s[tid] = -INFINITY;
+    l_s[tid] = 0.f;
+  }
+  // outputs owned by this thread: indices tid, tid+128, ... of [G][d]
+  constexpr int kMaxOwn = 8;  // G * d <= 1024
+  float o_acc[kMaxOwn];
+#pragma unroll
+  for (int r = 0; r < kMaxOwn; ++r) o_acc[r] = 0.f;
+  __syncthreads();
+
+  const int d4 = d / 4;
+  for (int t0 = c0; t0 < c1; t0 += kTile) {
+    const int nt = min(kTile, c1 - t0);
+    // stage K (padded rows) and V tiles
+    for (int i = tid; i < nt * d4; i += blockDim.x) {
+      const int t = i / d4, j4 = i % d4;
+      const float4 kv4 = *reinterpret_cast<const float4*>(kc + size_t(t0 + t) * kvd + kvh * d + j4 * 4);
+      const float4 vv4 = *reinterpret_cast<const float4*>(vc + size_t(t0 + t) * kvd + kvh * d + j4 * 4);
+      *reinterpret_cast<float4*>(ks_ + t * (d + 4) + j4 * 4) = kv4;
+      *reinterpret_cast<float4*>(vs + t * d + j4 * 4) = vv4;
+    }
+    __syncthreads();
+    // scores: warp w handles heads w, w+4, ...; lane = position
+    for (int g = warp; g < G; g += kAttnThreads / 32) {
+      float s = -INFINITY;
+      if (lane < nt) {
+        const float* kr = ks_ + lane * (d + 4);
+        const float* qr = qs + g * d;
+        float acc = 0.f;
+        for (int j = 0; j < d; j += 4) {
+          const float4 k4 = *reinterpret_cast<const float4*>(kr + j);
+          const float4 q4 = *reinterpret_cast<const float4*>(qr + j);
+          acc = fmaf(q4.x, k4.x, acc);
+          acc = fmaf(q4.y, k4.y, acc);
+          acc = fmaf(q4.z, k4.z, acc);
+          acc = fmaf(q4.w, k4.w, acc);
+        }
+        s = acc * a.scale;
+      }
+      const float mt = warp_max(s);
+      const float m_old = m_s[g];
+      const float m_new = fmaxf(m_old, mt);
+      const float p = lane < nt ? expf(s - m_new) : 0.f;
+      const float lsum = warp_sum(p);
+      ps[g * kTile + lane] = p;
+      if (lane == 0) {
+        const float alpha = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
+        alpha_s[g] = alpha;
+        l_s[g] = l_s[g] * alpha + lsum;
+        m_s[g] = m_new;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < kMaxOwn; ++r) {
+      const int idx = tid + r * kAttnThreads;
+      if (idx < G * d) {
+        const int g = idx / d, j = idx % d;
+        float acc = o_acc[r] * alpha_s[g];
+        for (int t = 0; t < nt; ++t) acc = fmaf(ps[g * kTile + t], vs[t * d + j], acc);
+        o_acc[r] = acc;
+      }
+    }
+    __syncthreads();
+  }
+
+  // partial (m, l, o[d]) per head
+  float* part = a.part + ((size_t(m) * a.nkv + kvh) * a.nsplit + split) * G * (d + 2);
+#pragma unroll
+  for (int r = 0; r < kMaxOwn; ++r) {
+    const int idx = tid + r * kAttnThreads;
+    if (idx < G * d) part[(idx / d) * (d + 2) + 2 + (idx % d)] = o_acc[r];
+  }
+  if (tid < G) {
+    part[tid * (d + 2)] = m_s[tid];
+    part[tid * (d + 2) + 1] = l_s[tid];
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    const unsigned int t = atomicAdd(&a.ticket[m * a.nkv + kvh], 1u);
+    last_s = (t == gridDim.y - 1);
+  }
+  __syncthreads();
+  if (!last_s) return;
+  __threadfence();
+  const float* pb = a.part + (size_t(m) * a.nkv + kvh) * a.nsplit * G * (d + 2);
+  for (int idx = tid; idx < G * d; idx += blockDim.x) {
+    const int g = idx / d, j = idx % d;
+    float mx = -INFINITY;
+    for (int s = 0; s < a.nsplit; ++s) mx = fmaxf(mx, __ldcg(pb + (s * G + g) * (d + 2)));
+    float L = 0.f, acc = 0.f;
+    for (int s = 0; s < a.nsplit; ++s) {
+      const float* ps_ = pb + (s * G + g) * (d + 2);
+      const float ms = __ldcg(ps_);
+      if (ms == -INFINITY) continue;
+      const float w = expf(ms - mx);
+      L = fmaf(__ldcg(ps_ + 1), w, L);
+      acc = fmaf(__ldcg(ps_ + 2 + j), w, acc);
+    }
+    a.out[size_t(m) * a.nq * d + (kvh * G + g) * d + j] = L > 0.f ? acc / L : 0.f;
+  }
+  if (tid == 0) a.ticket[m * a.nkv + kvh] = 0u;
+}
+
+// ---------------------------------------------------------------------------
+// Prefill causal attention.  Template on head_dim; DPT dims per thread,
+// TPR = D / DPT threads per query row.  Grid (n_q, ceil(T / rows_per_cta)).
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(
+    const float* __restrict__ q, int64_t q_ld, const float* __restrict__ kc,
+    const float* __restrict__ vc, int64_t T, int64_t pos0, int nq, int nkv, float scale,
+    float* __restrict__ out, int64_t out_ld) {
+  constexpr int DPT = D < 64 ? D : 64;
+  constexpr int TPR = D / DPT;
+  constexpr int ROWS = kAttnThreads / TPR;
+  __shared__ float ks[kTile][D];
+  __shared__ float vs[kTile][D];
+  const int h = blockIdx.x;
+  const int kvh = h / (nq / nkv);
+  const int kvd = nkv * D;
+  const int tid = threadIdx.x;
+  const int rloc = tid / TPR, part = tid % TPR;
+  const int64_t row = int64_t(blockIdx.y) * ROWS + rloc;
+  const bool valid = row < T;
+  const int64_t my_pos = pos0 + (valid ? row : 0);
+  const int64_t last_row = (T - 1 < int64_t(blockIdx.y) * ROWS + ROWS - 1 ? T - 1 : int64_t(blockIdx.y) * ROWS + ROWS - 1);
+  const int64_t n_keys = pos0 + last_row + 1;
+
+  float qr[DPT], o[DPT];
+#pragma unroll
+  for (int j = 0; j < DPT; ++j) {
+    qr[j] = valid ? q[row * q_ld + h * D + part * DPT + j] : 0.f;
+    o[j] = 0.f;
+  }
+  float m_run = -INFINITY, l_run = 0.f;
+
+  for (int64_t t0 = 0; t0 < n_keys; t0 += kTile) {
+    const int nt = int(n_keys - t0 < kTile ? n_keys - t0 : kTile);
+    __syncthreads();
+    for (int i = tid; i < nt * (D / 4); i += kAttnThreads) {
+      const int t = i / (D / 4), j4 = i % (D / 4);
+      *reinterpret_cast<float4*>(&ks[t][j4 * 4]) =
+          *reinterpret_cast<const float4*>(kc + (t0 + t) * kvd + kvh * D + j4 * 4);
+      *reinterpret_cast<float4*>(&vs[t][j4 * 4]) =
+          *reinterpret_cast<const float4*>(vc + (t0 + t) * kvd + kvh * D + j4 * 4);
+    }
+    __syncthreads();
+    float s[kTile];
+    float mt = -INFINITY;
+#pragma unroll
+    for (int t = 0; t < kTile; ++t) {
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < DPT; ++j) acc = fmaf(qr[j], ks[t][part * DPT + j], acc);
+#pragma unroll
+      for (int o2 = 1; o2 < TPR; o2 <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o2);
+      const bool ok = t < nt && (t0 + t) <= my_pos;
+      s[t] = ok ? acc * scale : -INFINITY;
+      mt = fmaxf(mt, s[t]);
+    }
+    const float m_new = fmaxf(m_run, mt);
+    if (m_new == -INFINITY) continue;  // nothing visible in this tile yet
+    const float alpha = m_run == -INFINITY ? 0.f : expf(m_run - m_new);
+    float lsum = 0.f;
+#pragma unroll
+    for (int t = 0; t < kTile; ++t) {
+      s[t] = s[t] == -INFINITY ? 0.f : expf(s[t] - m_new);
+      lsum += s[t];
+    }
+    l_run = l_run * alpha + lsum;
+    m_run = m_new;
+#pragma unroll
+    for (int j = 0; j < DPT; ++j) {
+      float acc = o[j] * alpha;
+#pragma unroll
+      for (int t = 0; t < kTile; ++t) acc = fmaf(s[t], vs[t][part * DPT + j], acc);
+      o[j] = acc;
+    }
+  }
+  if (valid) {
+    const float inv = 1.0f / l_run;
+#pragma unroll
+    for (int j = 0; j < DPT; ++j) out[row * out_ld + h * D + part * DPT + j] = o[j] * inv;
+  }
+}
+
+// RoPE of q and k for T prefill rows + KV append (model.rs:533-553).
+// Grid (T); threads over (heads x half).
+__global__ void rope_append_kernel(float* qkv, int64_t ld, int nq, int nkv, int d,
+                                   const float* __restrict__ cs, const float* __restrict__ sn,
+                                   int64_t pos0, float* kc, float* vc) {
+  const int64_t t = blockIdx.x;
+  const int64_t pos = pos0 + t;
+  const int half = d / 2, kvd = nkv * d;
+  float* row = qkv + t * ld;
+  for (int i = threadIdx.x; i < (nq + nkv) * half; i += blockDim.x) {
+    const int hh = i / half, j = i % half;
+    float* v = row + hh * d;
+    float o0, o1;
+    rot(v[j], v[j + half], cs[pos * half + j], sn[pos * half + j], &o0, &o1);
+    if (hh < nq) {
+      v[j] = o0;
+      v[j + half] = o1;
+    } else {
+      float* kdst = kc + pos * kvd + (hh - nq) * d;
+      kdst[j] = o0;
+      kdst[j + half] = o1;
+    }
+  }
+  const float* vsrc = row + (nq + nkv) * d;
+  for (int j = threadIdx.x; j < kvd; j += blockDim.x) vc[pos * kvd + j] = vsrc[j];
+}
+
+__global__ void rope_rows_kernel(float* x, int64_t ld, int n_heads, int d,
+                                 const float* __restrict__ cs, const float* __restrict__ sn,
+                                 int64_t pos0) {
+  const int64_t t = blockIdx.x, pos = pos0 + t;
+  const int half = d / 2;
+  float* row = x + t * ld;
+  for (int i = threadIdx.x; i < n_heads * half; i += blockDim.x) {
+    const int hh = i / half, j = i % half;
+    float* v = row + hh * d;
+    float o0, o1;
+    rot(v[j], v[j + half], cs[pos * half + j], sn[pos * half + j], &o0, &o1);
+    v[j] = o0;
+    v[j + half] = o1;
+  }
+}
+
+}  // namespace
+
+int attn_decode_nsplit(int nkv, int M, int64_t cap, int num_sms) {
+  const int64_t want = (int64_t(num_sms) * 8 + int64_t(nkv) * M - 1) / (int64_t(nkv) * M);
+  const int64_t maxs = (cap + kTile - 1) / kTile;
+  int64_t n = std::min<int64_t>(want, maxs);
+  return int(std::max<int64_t>(1, std::min<int64_t>(n, 1024)));
+}
+
+constexpr int kMaxAttnSmem = 96 * 1024;
+
+cudaError_t attn_prepare() {
+  return cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              kMaxAttnSmem);
+}
+
+cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) {
+  const int G = a.nq / a.nkv;
+  if (G * a.nkv != a.nq || a.d % 8 != 0 || G * a.d > 8 * kAttnThreads || G > 16)
+    return cudaErrorInvalidValue;
+  const size_t smem = sizeof(float) * (G * a.d + kTile * (a.d + 4) + kTile * a.d + G * kTile);
+  if (smem > size_t(kMaxAttnSmem)) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.nkv, a.nsplit, a.M);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, attn_decode_kernel, a);
+}
+
+cudaError_t launch_attn_prefill(const float* q, int64_t q_ld, const float* kc, const float* vc,
+                                int64_t T, int64_t pos0, int nq, int nkv, int d, float scale,
+                                float* out, int64_t out_ld, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  switch (d) {
+#define TMG_ATTN_CASE(D)                                                                   \
+  case D: {                                                                                \
+    constexpr int ROWS = kAttnThreads / (D / (D < 64 ? D : 64));                           \
+    dim3 grid(nq, unsigned((T + ROWS - 1) / ROWS));                                        \
+    attn_prefill_kernel<D><<<grid, kAttnThreads, 0, s>>>(q, q_ld, kc, vc, T, pos0, nq, nkv, \
+                                                         scale, out, out_ld);              \
+    return cudaGetLastError();                                                             \
+  }
+    TMG_ATTN_CASE(16)
+    TMG_ATTN_CASE(32)
+    TMG_ATTN_CASE(64)
+    TMG_ATTN_CASE(128)
+#undef TMG_ATTN_CASE
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_rope_append(float* qkv, int64_t qkv_ld, int64_t T, int nq, int nkv, int d,
+                               const float* rope_cos, const float* rope_sin, int64_t pos0,
+                               float* kc, float* vc, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  rope_append_kernel<<<unsigned(T), 256, 0, s>>>(qkv, qkv_ld, nq, nkv, d, rope_cos, rope_sin, pos0,
+                                                 kc, vc);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rope_rows(float* x, int64_t ld, int64_t rows, int n_heads, int d,
+                             const float* rope_cos, const float* rope_sin, int64_t pos0,
+                             cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  rope_rows_kernel<<<unsigned(rows), 256, 0, s>>>(x, ld, n_heads, d, rope_cos, rope_sin, pos0);
+  return cudaGetLastError();
+}
+
+}  // namespace tmg
