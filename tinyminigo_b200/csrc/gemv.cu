@@ -420,10 +420,10 @@ cudaError_t set_m1_attr() {
 
 template <int PRO>
 cudaError_t set_m1_attrs() {
-  TMG_CUDA_TRY(set_m1_attr<PRO, EPI_STORE>());
-  TMG_CUDA_TRY(set_m1_attr<PRO, EPI_ADD>());
-  TMG_CUDA_TRY(set_m1_attr<PRO, EPI_SWIGLU>());
-  TMG_CUDA_TRY(set_m1_attr<PRO, EPI_HEAD>());
+  TMG_CUDA_TRY((set_m1_attr<PRO, EPI_STORE>()));
+  TMG_CUDA_TRY((set_m1_attr<PRO, EPI_ADD>()));
+  TMG_CUDA_TRY((set_m1_attr<PRO, EPI_SWIGLU>()));
+  TMG_CUDA_TRY((set_m1_attr<PRO, EPI_HEAD>()));
   return set_m1_attr<PRO, EPI_HEAD_ARGMAX>();
 }
 
