@@ -195,7 +195,7 @@ def test_sample_selection_bit_exact(ctx, orc, V, T, k, p, pen):
     rows = 3
     logits = (rng.normal(0, 1.5, (rows, V))).astype(np.float32)
     # ties across a slice boundary and inside the top-k
-    logits[0, 5] = logits[0, 4100] = logits[0, 90000 % V] = 9.0
+    logits[0, 5] = logits[0, 4100 % V] = logits[0, 90000 % V] = 9.0
     gen = rng.integers(0, V, (rows, 25)).astype(np.uint32)
     gen[:, 3] = gen[:, 0]  # repeated ids are penalised once
     gen[0, 1] = 5

@@ -25,8 +25,8 @@ LIB = PKG / "lib" / "libtmg_cuda.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O3", "--expt-relaxed-constexpr",
               "-I", str(CSRC), "-I", str(INC)]
-SOURCES = ["api.cu", "gemv.cu", "attn.cu", "prefill.cu", "sample.cu", "tp.cu", "loader.cpp",
-           "rng.cpp"]
+SOURCES = ["api.cu", "gemv.cu", "attn.cu", "prefill.cu", "sample.cu", "tp.cu", "gemm_sm100.cu",
+           "loader.cpp", "rng.cpp"]
 
 
 def nvcc() -> str:

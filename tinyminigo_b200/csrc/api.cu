@@ -82,6 +82,9 @@ struct tmg_ctx {
   // op-level scratch
   void* op_buf = nullptr;
   size_t op_cap = 0;
+  // hi/lo BF16 split of the prefill GEMM's activations
+  uint16_t *sp_hi = nullptr, *sp_lo = nullptr;
+  size_t sp_cap = 0;
   // pinned staging
   void* pinned = nullptr;
   size_t pinned_cap = 0;
@@ -156,13 +159,47 @@ cudaError_t ensure_pinned(tmg_ctx* c, size_t bytes) {
   return cudaSuccess;
 }
 
+// Every copy and fill is ordered on the context's (non-blocking) stream:
+// legacy-stream cudaMemcpy / cudaMemset do not order against it, and a
+// pageable host-to-device cudaMemcpy may return before its DMA lands.
+cudaError_t copy_sync(tmg_ctx* c, void* dst, const void* src, size_t n, cudaMemcpyKind k) {
+  TMG_CUDA_TRY(cudaMemcpyAsync(dst, src, n, k, c->stream));
+  return cudaStreamSynchronize(c->stream);
+}
+
+cudaError_t zero_sync(tmg_ctx* c, void* p, size_t n) {
+  TMG_CUDA_TRY(cudaMemsetAsync(p, 0, n, c->stream));
+  return cudaStreamSynchronize(c->stream);
+}
+
+// The device error word: 1 = NaN logits reached the sampler, 2 = a bounded
+// device-side wait gave up.
+int err_status(tmg_ctx* c, int32_t w) {
+  if (w == 1) return fail(c, TMG_ERR_NAN, "NaN logits reached the sampler");
+  return fail(c, TMG_ERR_TIMEOUT, "a bounded device-side wait gave up (pipeline stalled)");
+}
+
+// Wait for the stream, then read and clear the device error word.
+int sync_check(tmg_ctx* c, const char* where) {
+  int32_t w = 0;
+  cudaError_t e = copy_sync(c, &w, c->d_err, 4, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(c, e, where);
+  if (w) {
+    e = zero_sync(c, c->d_err, 4);
+    if (e != cudaSuccess) return cuda_fail(c, e, where);
+    return err_status(c, w);
+  }
+  return TMG_OK;
+}
+
 cudaError_t ensure_op(tmg_ctx* c, size_t bytes) {
   if (c->op_cap >= bytes) return cudaSuccess;
+  TMG_CUDA_TRY(cudaStreamSynchronize(c->stream));
   if (c->op_buf) cudaFree(c->op_buf);
   c->op_buf = nullptr;
   c->op_cap = 0;
   TMG_CUDA_TRY(cudaMalloc(&c->op_buf, bytes));
-  TMG_CUDA_TRY(cudaMemset(c->op_buf, 0, bytes));
+  TMG_CUDA_TRY(zero_sync(c, c->op_buf, bytes));
   c->op_cap = bytes;
   return cudaSuccess;
 }
@@ -338,9 +375,7 @@ int alloc_model(tmg_ctx* c) {
   CK(dalloc(c->allocs, &c->am_part, size_t(M) * c->num_sms * 8), "alloc scratch");
   CK(dalloc(c->allocs, &c->sm_part, size_t(M) * 64 * kMaxTopK), "alloc scratch");
   CK(dalloc(c->allocs, &c->tickets, 64), "alloc scratch");
-  CK(cudaMemset(c->tickets, 0, 64 * sizeof(unsigned int)), "memset");
-  CK(dalloc(c->allocs, &c->d_err, 4), "alloc scratch");
-  CK(cudaMemset(c->d_err, 0, 16), "memset");
+  CK(zero_sync(c, c->tickets, 64 * sizeof(unsigned int)), "memset");
   c->has_model = true;
   return TMG_OK;
 }
@@ -377,15 +412,35 @@ int ensure_prefill(tmg_ctx* c, int64_t T) {
   return TMG_OK;
 }
 
-// y (+)= x . W^T for T rows (the prefill GEMM).
+cudaError_t ensure_split(tmg_ctx* c, size_t n) {
+  if (c->sp_cap >= n) return cudaSuccess;
+  TMG_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  if (c->sp_hi) cudaFree(c->sp_hi);
+  if (c->sp_lo) cudaFree(c->sp_lo);
+  c->sp_hi = c->sp_lo = nullptr;
+  c->sp_cap = 0;
+  TMG_CUDA_TRY(cudaMalloc(&c->sp_hi, n * 2));
+  TMG_CUDA_TRY(cudaMalloc(&c->sp_lo, n * 2));
+  c->sp_cap = n;
+  return cudaSuccess;
+}
+
+// y (+)= x . W^T for T rows (the prefill GEMM): tcgen05 tensor cores on the
+// hi/lo BF16 split of x; the SIMT kernel only for rows of K % 8 != 0.
 cudaError_t gemm(tmg_ctx* c, const float* x, const uint16_t* w, int64_t T, int64_t N, int64_t K,
                  float* y, int64_t ldy, bool acc) {
+  if (gemm_tc_supported(K, w)) {
+    TMG_CUDA_TRY(ensure_split(c, size_t(T) * K));
+    TMG_CUDA_TRY(launch_split(x, T * K, c->sp_hi, c->sp_lo, c->stream));
+    return launch_gemm_tc(c->sp_hi, c->sp_lo, w, T, N, K, y, ldy, acc, c->d_err, c->stream);
+  }
   return launch_gemm_simt(x, w, T, N, K, y, ldy, acc, c->stream);
 }
 
 // GEMV with an optional fused prologue; falls back to separate embedding /
 // norm kernels when the fused kernel does not take the shape.
 cudaError_t gemv(tmg_ctx* c, GemvArgs a, GemvPro pro, GemvEpi epi, bool pdl) {
+  a.err = c->d_err;
   if (!gemv_fused_ok(a, epi) && pro != PRO_NONE) {
     if (pro == PRO_EMBED_NORM) {
       TMG_CUDA_TRY(launch_embed(a.embed, a.tokens, a.M, a.K, a.x_out, c->stream));
@@ -697,8 +752,8 @@ int run_generate(tmg_ctx* c, tmg_kv* kv, const uint32_t* prompts, int64_t T,
   if (prefill_secs) *prefill_secs = std::chrono::duration<double>(t1 - t0).count();
   if (first_logits)
     for (int m = 0; m < M; ++m)
-      CK(cudaMemcpy(first_logits + size_t(m) * c->V, logits_row(c, m), size_t(c->V) * 4,
-                    cudaMemcpyDeviceToHost),
+      CK(copy_sync(c, first_logits + size_t(m) * c->V, logits_row(c, m), size_t(c->V) * 4,
+                   cudaMemcpyDeviceToHost),
          "first logits");
   for (int m = 0; m < M; ++m) n_out[m] = 0;
   if (maxt == 0) return TMG_OK;
@@ -825,12 +880,13 @@ int run_generate(tmg_ctx* c, tmg_kv* kv, const uint32_t* prompts, int64_t T,
   cudaEventDestroy(ev[1]);
   cudaGraphExecDestroy(exec);
   int32_t err_word = 0;
-  CK(cudaMemcpy(&err_word, c->d_err, 4, cudaMemcpyDeviceToHost), "err");
-  CK(cudaMemcpy(h_state.data(), kv->d_state, h_state.size() * 4, cudaMemcpyDeviceToHost), "state");
-  CK(cudaMemcpy(h_gen.data(), kv->d_gen, h_gen.size() * 4, cudaMemcpyDeviceToHost), "tokens");
+  CK(copy_sync(c, &err_word, c->d_err, 4, cudaMemcpyDeviceToHost), "err");
+  CK(copy_sync(c, h_state.data(), kv->d_state, h_state.size() * 4, cudaMemcpyDeviceToHost),
+     "state");
+  CK(copy_sync(c, h_gen.data(), kv->d_gen, h_gen.size() * 4, cudaMemcpyDeviceToHost), "tokens");
   if (err_word) {
-    CK(cudaMemset(c->d_err, 0, 4), "err");
-    return fail(c, TMG_ERR_NAN, "NaN logits reached the sampler");
+    CK(zero_sync(c, c->d_err, 4), "err");
+    return err_status(c, err_word);
   }
   for (int m = 0; m < M; ++m) {
     const int32_t ng = h_state[3 * kMaxStreams + m];
@@ -930,7 +986,11 @@ int tmg_create(int device, const tmg_config* cfg, tmg_ctx** out) {
   if (cudaSetDevice(device) != cudaSuccess ||
       cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
-      gemv_prepare() != cudaSuccess || attn_prepare() != cudaSuccess) {
+      gemv_prepare() != cudaSuccess || attn_prepare() != cudaSuccess ||
+      gemm_tc_prepare() != cudaSuccess || dalloc(c->allocs, &c->d_err, 4) != cudaSuccess ||
+      zero_sync(c, c->d_err, 16) != cudaSuccess) {
+    free_all(c->allocs);
+    if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
     return TMG_ERR_CUDA;
   }
@@ -949,7 +1009,7 @@ int tmg_destroy(tmg_ctx* c) {
   cudaStreamSynchronize(c->stream);
   free_all(c->allocs);
   for (void* p : {(void*)c->X, (void*)c->Xn, (void*)c->QKV, (void*)c->ATT, (void*)c->G,
-                  (void*)c->U, (void*)c->d_tok, c->op_buf})
+                  (void*)c->U, (void*)c->d_tok, c->op_buf, (void*)c->sp_hi, (void*)c->sp_lo})
     if (p) cudaFree(p);
   if (c->pinned) cudaFreeHost(c->pinned);
   if (c->tp) tp_destroy(c->tp);
@@ -1030,10 +1090,10 @@ int tmg_kv_create(tmg_ctx* c, int32_t n_streams, int64_t capacity, tmg_kv** out)
   if ((e = dalloc(kv->allocs, &kv->rope_sin, size_t(capacity) * half)) != cudaSuccess) return bail(e);
   std::vector<float> tc = rope_table(c->d, c->cfg.rope_theta, capacity, false);
   std::vector<float> ts = rope_table(c->d, c->cfg.rope_theta, capacity, true);
-  if ((e = cudaMemcpy(kv->rope_cos, tc.data(), tc.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess) return bail(e);
-  if ((e = cudaMemcpy(kv->rope_sin, ts.data(), ts.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess) return bail(e);
+  if ((e = copy_sync(c, kv->rope_cos, tc.data(), tc.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess) return bail(e);
+  if ((e = copy_sync(c, kv->rope_sin, ts.data(), ts.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess) return bail(e);
   if ((e = dalloc(kv->allocs, &kv->d_state, 4 * kMaxStreams)) != cudaSuccess) return bail(e);
-  if ((e = cudaMemset(kv->d_state, 0, 16 * kMaxStreams)) != cudaSuccess) return bail(e);
+  if ((e = zero_sync(c, kv->d_state, 16 * kMaxStreams)) != cudaSuccess) return bail(e);
   kv->st.token = reinterpret_cast<uint32_t*>(kv->d_state);
   kv->st.pos = kv->d_state + kMaxStreams;
   kv->st.done = kv->d_state + 2 * kMaxStreams;
@@ -1045,7 +1105,7 @@ int tmg_kv_create(tmg_ctx* c, int32_t n_streams, int64_t capacity, tmg_kv** out)
   const int G = c->nq / c->nkv;
   if ((e = dalloc(kv->allocs, &kv->part, size_t(n_streams) * c->nkv * kv->nsplit * G * (c->d + 2))) != cudaSuccess) return bail(e);
   if ((e = dalloc(kv->allocs, &kv->att_ticket, size_t(n_streams) * c->nkv)) != cudaSuccess) return bail(e);
-  if ((e = cudaMemset(kv->att_ticket, 0, size_t(n_streams) * c->nkv * 4)) != cudaSuccess) return bail(e);
+  if ((e = zero_sync(c, kv->att_ticket, size_t(n_streams) * c->nkv * 4)) != cudaSuccess) return bail(e);
   *out = kv;
   return TMG_OK;
 }
@@ -1097,8 +1157,9 @@ int tmg_kv_read(tmg_kv* kv, int32_t layer, int32_t stream, float* keys, float* v
   CK(cudaStreamSynchronize(c->stream), "kv read");
   const size_t n = size_t(kv->lens[stream]) * kv->kvd;
   const size_t off = size_t(stream) * kv->cap * kv->kvd;
-  if (keys) CK(cudaMemcpy(keys, kv->k[layer] + off, n * 4, cudaMemcpyDeviceToHost), "kv read");
-  if (values) CK(cudaMemcpy(values, kv->v[layer] + off, n * 4, cudaMemcpyDeviceToHost), "kv read");
+  if (keys) CK(copy_sync(c, keys, kv->k[layer] + off, n * 4, cudaMemcpyDeviceToHost), "kv read");
+  if (values)
+    CK(copy_sync(c, values, kv->v[layer] + off, n * 4, cudaMemcpyDeviceToHost), "kv read");
   return TMG_OK;
 }
 
@@ -1141,9 +1202,8 @@ int tmg_forward_token(tmg_ctx* c, tmg_kv* kv, const uint32_t* tokens, float* log
       CK(cudaMemcpyAsync(logits + size_t(m) * c->V, logits_row(c, m), size_t(c->V) * 4,
                          cudaMemcpyDeviceToHost, c->stream),
          "logits");
-  CK(cudaStreamSynchronize(c->stream), "forward");
   for (int m = 0; m < kv->M; ++m) kv->lens[m] += 1;
-  return TMG_OK;
+  return sync_check(c, "forward");
 }
 
 int tmg_forward_seq(tmg_ctx* c, tmg_kv* kv, int32_t stream, const uint32_t* tokens, int64_t T,
@@ -1162,8 +1222,7 @@ int tmg_forward_seq(tmg_ctx* c, tmg_kv* kv, int32_t stream, const uint32_t* toke
     CK(cudaMemcpyAsync(logits, logits_row(c, stream), size_t(c->V) * 4, cudaMemcpyDeviceToHost,
                        c->stream),
        "logits");
-  CK(cudaStreamSynchronize(c->stream), "forward_seq");
-  return TMG_OK;
+  return sync_check(c, "forward_seq");
 }
 
 int tmg_generate(tmg_ctx* c, tmg_kv* kv, const uint32_t* prompt, int64_t T,
@@ -1269,7 +1328,7 @@ int tmg_decode(tmg_ctx* c, tmg_kv* kv, const uint32_t* tokens, int64_t n_steps, 
     CK(cudaMemcpyAsync(out, kv->d_gen, size_t(kv->M) * n_steps * 4, cudaMemcpyDeviceToHost,
                        c->stream),
        "tokens");
-    CK(cudaStreamSynchronize(c->stream), "decode");
+    return sync_check(c, "decode");
   }
   return TMG_OK;
 }
@@ -1277,8 +1336,11 @@ int tmg_decode(tmg_ctx* c, tmg_kv* kv, const uint32_t* tokens, int64_t n_steps, 
 int tmg_sync(tmg_ctx* c) {
   if (!c) return TMG_ERR_INVALID;
   cudaSetDevice(c->device);
-  CK(cudaStreamSynchronize(c->stream), "sync");
-  return TMG_OK;
+  if (!c->d_err) {
+    CK(cudaStreamSynchronize(c->stream), "sync");
+    return TMG_OK;
+  }
+  return sync_check(c, "sync");
 }
 
 void* tmg_stream(tmg_ctx* c) { return c ? static_cast<void*>(c->stream) : nullptr; }
@@ -1377,8 +1439,8 @@ int tmg_op_rope(tmg_ctx* c, float* x, int64_t rows, int32_t n_heads, int32_t hea
   CK(ensure_op(c, 2 * bytes + 64), "op scratch");
   float* dc = static_cast<float*>(c->op_buf);
   float* ds = dc + tc.size();
-  CK(cudaMemcpy(dc, tc.data(), bytes, cudaMemcpyHostToDevice), "rope table");
-  CK(cudaMemcpy(ds, ts.data(), bytes, cudaMemcpyHostToDevice), "rope table");
+  CK(copy_sync(c, dc, tc.data(), bytes, cudaMemcpyHostToDevice), "rope table");
+  CK(copy_sync(c, ds, ts.data(), bytes, cudaMemcpyHostToDevice), "rope table");
   CK(launch_rope_rows(x, int64_t(n_heads) * head_dim, rows, n_heads, head_dim, dc, ds, pos0,
                       c->stream),
      "rope");

@@ -23,7 +23,8 @@ namespace tmg {
 namespace {
 
 constexpr int kAttnThreads = 128;
-constexpr int kTile = 32;  // positions per shared-memory tile
+constexpr int kTile = 32;      // positions per shared-memory tile
+constexpr int kMinChunk = 64;  // fewest positions a decode split takes
 
 // Rotate pair (a, b) by (c, s): (a c - b s, a s + b c), rounded like the
 // reference (two products, then one add/sub; no FMA contraction).
@@ -75,8 +76,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
       qs[g * d + j + half] = o1;
     }
   }
-  // context range of this split
+  // context range of this split: at least kMinChunk positions per split, so
+  // short contexts use few CTAs (the rest only take their ticket)
   int chunk = (n_ctx + a.nsplit - 1) / a.nsplit;
+  chunk = max(kMinChunk, (chunk + kTile - 1) / kTile * kTile);
+  const int n_used = (n_ctx + chunk - 1) / chunk;
   const int c0 = split * chunk;
   const int c1 = min(n_ctx, c0 + chunk);
   // the CTA whose range holds pos appends the rotated k and raw v
@@ -161,16 +165,33 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
     __syncthreads();
   }
 
-  // partial (m, l, o[d]) per head
-  float* part = a.part + ((size_t(m) * a.nkv + kvh) * a.nsplit + split) * G * (d + 2);
+  float* out = a.out + size_t(m) * a.nq * d + kvh * G * d;
+  if (n_used == 1) {
+    // the whole context in one CTA: finish here, no partials
+    if (split == 0) {
 #pragma unroll
-  for (int r = 0; r < kMaxOwn; ++r) {
-    const int idx = tid + r * kAttnThreads;
-    if (idx < G * d) part[(idx / d) * (d + 2) + 2 + (idx % d)] = o_acc[r];
+      for (int r = 0; r < kMaxOwn; ++r) {
+        const int idx = tid + r * kAttnThreads;
+        if (idx < G * d) {
+          const float L = l_s[idx / d];
+          out[idx] = L > 0.f ? o_acc[r] / L : 0.f;
+        }
+      }
+    }
+    return;  // one-split launches need no ticket
   }
-  if (tid < G) {
-    part[tid * (d + 2)] = m_s[tid];
-    part[tid * (d + 2) + 1] = l_s[tid];
+  // partial (m, l, o[d]) per head
+  if (split < n_used) {
+    float* part = a.part + ((size_t(m) * a.nkv + kvh) * a.nsplit + split) * G * (d + 2);
+#pragma unroll
+    for (int r = 0; r < kMaxOwn; ++r) {
+      const int idx = tid + r * kAttnThreads;
+      if (idx < G * d) part[(idx / d) * (d + 2) + 2 + (idx % d)] = o_acc[r];
+    }
+    if (tid < G) {
+      part[tid * (d + 2)] = m_s[tid];
+      part[tid * (d + 2) + 1] = l_s[tid];
+    }
   }
   __syncthreads();
   if (tid == 0) {
@@ -181,21 +202,42 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
   __syncthreads();
   if (!last_s) return;
   __threadfence();
+  // combine: the per-split weights w = exp(m_s - max) once per (split, head)
+  // in shared memory, then every output sums its column over the splits
   const float* pb = a.part + (size_t(m) * a.nkv + kvh) * a.nsplit * G * (d + 2);
+  float* wts = sm;  // [G][n_used] (the tiles are no longer needed)
+  for (int g = warp; g < G; g += kAttnThreads / 32) {
+    float mx = -INFINITY;
+    for (int s = lane; s < n_used; s += 32) mx = fmaxf(mx, __ldcg(pb + (s * G + g) * (d + 2)));
+    mx = warp_max(mx);
+    float L = 0.f;
+    for (int s = lane; s < n_used; s += 32) {
+      const float ms = __ldcg(pb + (s * G + g) * (d + 2));
+      const float w = ms == -INFINITY ? 0.f : expf(ms - mx);
+      wts[g * n_used + s] = w;
+      L = fmaf(__ldcg(pb + (s * G + g) * (d + 2) + 1), w, L);
+    }
+    L = warp_sum(L);
+    if (lane == 0) l_s[g] = L;
+  }
+  __syncthreads();
   for (int idx = tid; idx < G * d; idx += blockDim.x) {
     const int g = idx / d, j = idx % d;
-    float mx = -INFINITY;
-    for (int s = 0; s < a.nsplit; ++s) mx = fmaxf(mx, __ldcg(pb + (s * G + g) * (d + 2)));
-    float L = 0.f, acc = 0.f;
-    for (int s = 0; s < a.nsplit; ++s) {
-      const float* ps_ = pb + (s * G + g) * (d + 2);
-      const float ms = __ldcg(ps_);
-      if (ms == -INFINITY) continue;
-      const float w = expf(ms - mx);
-      L = fmaf(__ldcg(ps_ + 1), w, L);
-      acc = fmaf(__ldcg(ps_ + 2 + j), w, acc);
+    float acc = 0.f;
+    int s = 0;
+    for (; s + 4 <= n_used; s += 4) {
+      const float o0 = __ldcg(pb + ((s + 0) * G + g) * (d + 2) + 2 + j);
+      const float o1 = __ldcg(pb + ((s + 1) * G + g) * (d + 2) + 2 + j);
+      const float o2 = __ldcg(pb + ((s + 2) * G + g) * (d + 2) + 2 + j);
+      const float o3 = __ldcg(pb + ((s + 3) * G + g) * (d + 2) + 2 + j);
+      acc = fmaf(o0, wts[g * n_used + s], acc);
+      acc = fmaf(o1, wts[g * n_used + s + 1], acc);
+      acc = fmaf(o2, wts[g * n_used + s + 2], acc);
+      acc = fmaf(o3, wts[g * n_used + s + 3], acc);
     }
-    a.out[size_t(m) * a.nq * d + (kvh * G + g) * d + j] = L > 0.f ? acc / L : 0.f;
+    for (; s < n_used; ++s) acc = fmaf(__ldcg(pb + (s * G + g) * (d + 2) + 2 + j), wts[g * n_used + s], acc);
+    const float L = l_s[g];
+    out[idx] = L > 0.f ? acc / L : 0.f;
   }
   if (tid == 0) a.ticket[m * a.nkv + kvh] = 0u;
 }
@@ -346,7 +388,9 @@ cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s, bool pdl
   const int G = a.nq / a.nkv;
   if (G * a.nkv != a.nq || a.d % 8 != 0 || G * a.d > 8 * kAttnThreads || G > 16)
     return cudaErrorInvalidValue;
-  const size_t smem = sizeof(float) * (G * a.d + kTile * (a.d + 4) + kTile * a.d + G * kTile);
+  // tiles, or the combine's per-split weights when those are larger
+  const size_t tiles = size_t(G) * a.d + kTile * (a.d + 4) + kTile * a.d + G * kTile;
+  const size_t smem = sizeof(float) * std::max<size_t>(tiles, size_t(G) * a.nsplit);
   if (smem > size_t(kMaxAttnSmem)) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.nkv, a.nsplit, a.M);

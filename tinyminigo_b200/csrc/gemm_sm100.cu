@@ -1,0 +1,291 @@
+// Prefill GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// matmul_batch_w_into (src/tensor.rs:573-792): Y[T, N] = X[T, K] . W[N, K]^T
+// with X f32 activations and W BF16 weights.  The reference accumulates in
+// f32; a plain BF16 MMA on the activations would keep only 8 mantissa bits,
+// so X is split into two BF16 operands, X = Xhi + Xlo (Xhi = bf16(X), Xlo =
+// bf16(X - Xhi), ~16 bits together), and every K step issues two MMAs into
+// the same f32 TMEM accumulator: Xhi.W and Xlo.W.  W is exact in BF16.
+//
+// One CTA computes a 128 x BN tile (BN = 256):
+//   warp 0      TMA producer: per 64-wide K block, Xhi / Xlo [128 x 64] and
+//               W [BN x 64] tiles (128-byte swizzle) into a 3-stage ring;
+//   warp 1      allocates BN TMEM columns, issues tcgen05.mma (one elected
+//               lane; M=128, N=BN, K=16 per instruction) and commits each
+//               stage back to the producer, then the tile to the epilogue;
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 16 columns at a time, then
+//               store (or add into) Y in f32.
+// Every mbarrier wait is bounded; a wait that gives up sets the error word
+// and the CTA skips the rest of its work (the host reports TMG_ERR_TIMEOUT).
+// Single-GPU code: no multicast, no peer memory.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace tmg {
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 3;
+constexpr int A_BYTES = BM * BK * 2;  // 16 KB
+constexpr int B_BYTES = BN * BK * 2;  // 32 KB
+constexpr int STAGE_BYTES = 2 * A_BYTES + B_BYTES;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr int kThreadsG = 192;
+constexpr uint32_t kTmemCols = BN;
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// UMMA shared-memory descriptor of a K-major tile written by TMA with the
+// 128-byte swizzle: rows of 128 B, 8-row groups 1024 B apart (SBO), the
+// second 16-byte K chunk 16 B away (LBO = 1), version 1, layout SWIZZLE_128B.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= uint64_t((saddr >> 4) & 0x3fff);
+  d |= uint64_t(1) << 16;                 // LBO (16 B units)
+  d |= uint64_t(1024 >> 4) << 32;         // SBO
+  d |= uint64_t(1) << 46;                 // version
+  d |= uint64_t(2) << 61;                 // SWIZZLE_128B
+  return d;
+}
+
+// kind::f16 instruction descriptor: BF16 x BF16 -> F32, both K-major.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) |
+                            (uint32_t(BM >> 4) << 24);
+
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+      ::"r"(tmem_d), "l"(da), "l"(db), "r"(kIdesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15},"
+      " [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__global__ void __launch_bounds__(kThreadsG, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_lo,
+                   const __grid_constant__ CUtensorMap map_w, float* __restrict__ y, int64_t ldy,
+                   int T, int N, int K, int accumulate, int32_t* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accum = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  __shared__ int failed;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  const int nk = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    failed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // TMA producer
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % STAGES;
+      const uint32_t ph = (kb / STAGES) & 1;
+      if (!mbar_wait(&empty[s], ph ^ 1)) {
+        atomicExch(err, 2);
+        failed = 1;
+        break;
+      }
+      uint8_t* st = smem + s * STAGE_BYTES;
+      mbar_expect_tx(&full[s], STAGE_BYTES);
+      tma_load_2d(st, &map_hi, &full[s], kb * BK, m0);
+      tma_load_2d(st + A_BYTES, &map_lo, &full[s], kb * BK, m0);
+      tma_load_2d(st + 2 * A_BYTES, &map_w, &full[s], kb * BK, n0);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer
+    bool ok = true;
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % STAGES;
+      const uint32_t ph = (kb / STAGES) & 1;
+      if (!mbar_wait(&full[s], ph)) {
+        atomicExch(err, 2);
+        failed = 1;
+        ok = false;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t a_hi = smem_u32(smem + s * STAGE_BYTES);
+      const uint32_t a_lo = a_hi + A_BYTES;
+      const uint32_t b = a_hi + 2 * A_BYTES;
+#pragma unroll
+      for (int k = 0; k < BK / 16; ++k) {
+        const uint64_t db = umma_desc(b + k * 32);
+        umma(tmem, umma_desc(a_hi + k * 32), db, (kb | k) != 0);
+        umma(tmem, umma_desc(a_lo + k * 32), db, 1);
+      }
+      umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+    }
+    if (ok) umma_commit(accum);
+  } else if (warp >= 2) {
+    // epilogue: warp w reads TMEM lanes 32 * (w % 4) ...
+    const int q = warp & 3;
+    const bool ok = mbar_wait(accum, 0);
+    if (!ok) {
+      atomicExch(err, 2);
+    } else {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int row = m0 + q * 32 + lane;
+      for (int c = 0; c < BN; c += 16) {
+        float v[16];
+        tmem_ld16(tmem + (uint32_t(q * 32) << 16) + uint32_t(c), v);
+        if (row < T) {
+          float* yr = y + int64_t(row) * ldy + n0 + c;
+          if (n0 + c + 16 <= N && (reinterpret_cast<uintptr_t>(yr) & 15) == 0) {
+#pragma unroll
+            for (int i = 0; i < 16; i += 4) {
+              float4* p = reinterpret_cast<float4*>(yr + i);
+              float4 o = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+              if (accumulate) {
+                const float4 old = *p;
+                o.x += old.x;
+                o.y += old.y;
+                o.z += old.z;
+                o.w += old.w;
+              }
+              *p = o;
+            }
+          } else {
+            for (int i = 0; i < 16; ++i)
+              if (n0 + c + i < N) yr[i] = accumulate ? yr[i] + v[i] : v[i];
+          }
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols));
+  }
+}
+
+__global__ void split_kernel(const float* __restrict__ x, int64_t n, __nv_bfloat16* __restrict__ hi,
+                             __nv_bfloat16* __restrict__ lo) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const float v = x[i];
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    hi[i] = h;
+    lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2D bf16 [rows, K] row-major map with a (64 x box_rows) box, 128B swizzle.
+bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t K, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(K) * 2};
+  cuuint32_t box[2] = {cuuint32_t(BK), cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool gemm_tc_supported(int64_t K, const void* w) {
+  return K % 8 == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0 && encode_fn() != nullptr;
+}
+
+cudaError_t gemm_tc_prepare() {
+  return cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              SMEM_BYTES);
+}
+
+cudaError_t launch_split(const float* x, int64_t n, uint16_t* hi, uint16_t* lo, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  const int64_t blocks = std::min<int64_t>((n + 255) / 256, 148 * 16);
+  split_kernel<<<unsigned(blocks), 256, 0, s>>>(x, n, reinterpret_cast<__nv_bfloat16*>(hi),
+                                                reinterpret_cast<__nv_bfloat16*>(lo));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_tc(const uint16_t* x_hi, const uint16_t* x_lo, const uint16_t* w,
+                           int64_t T, int64_t N, int64_t K, float* y, int64_t ldy,
+                           bool accumulate, int32_t* err, cudaStream_t s) {
+  if (T <= 0 || N <= 0) return cudaSuccess;
+  if (K % 8 != 0 || T > (int64_t(1) << 30) || N > (int64_t(1) << 30) || K > (int64_t(1) << 30))
+    return cudaErrorInvalidValue;
+  CUtensorMap mh, ml, mw;
+  if (!make_map(&mh, x_hi, T, K, BM) || !make_map(&ml, x_lo, T, K, BM) ||
+      !make_map(&mw, w, N, K, BN))
+    return cudaErrorInvalidValue;
+  dim3 grid(unsigned((N + BN - 1) / BN), unsigned((T + BM - 1) / BM));
+  gemm_tc_kernel<<<grid, kThreadsG, SMEM_BYTES, s>>>(mh, ml, mw, y, ldy, int(T), int(N), int(K),
+                                                     accumulate ? 1 : 0, err);
+  return cudaGetLastError();
+}
+
+}  // namespace tmg

@@ -4,18 +4,20 @@
 //
 // y[n] = sum_k x[k] * W[n, k] with W BF16 [N, K] row-major, f32 math.  The
 // reference runs 8-lane AVX2 FMA chains per row; here every weight byte is
-// streamed once from HBM with 16-byte L1-bypassing loads, widened to f32 in
-// registers (exact), and reduced with warp shuffles.  This kernel family is
-// HBM-bound: algorithmic bytes = 2 * N * K per launch (+ 4 * K of x).
+// streamed once from HBM, widened to f32 in registers (exact), and reduced
+// with warp shuffles.  HBM-bound: algorithmic bytes = 2 * N * K per launch
+// (+ 4 * K of x).
 //
 // Two kernels:
-//  * gemv_m1: one activation row (the batch-1 token loop).  K % 256 == 0.
-//    A CTA of 8 warps stages x (normalised when fused with RMSNorm) in
-//    shared memory in a permuted layout that makes every warp's float4
-//    reads conflict-free; each warp owns a fixed K segment (split-K inside
-//    the CTA when N is small) and two output rows per task, so a lane keeps
-//    2 x chunks x 16 B of weights in flight.  The first task's weights are
-//    requested before griddepcontrol.wait, overlapping the previous kernel.
+//  * gemv_tma (one activation row: the batch-1 token loop; K % 256 == 0).
+//    One persistent CTA per SM: a producer warp streams groups of whole
+//    weight rows (contiguous, <= 32 KB) with cp.async.bulk into a 3-stage
+//    shared-memory ring guarded by mbarriers, starting before
+//    griddepcontrol.wait so the stream overlaps the previous kernel; eight
+//    consumer warps keep their K segment of x (normalised when RMSNorm is
+//    fused) in registers and reduce each row with warp shuffles, split-K
+//    across warps when K > 2048.  The 96 KB ring leaves room for the next
+//    kernel's CTA on the same SM.
 //  * gemv_gen: up to 16 activation rows, any K (the multi-stream step and
 //    odd shapes).  One row per warp task, x read through L1.
 //
@@ -32,6 +34,10 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / kWarp;
+constexpr int kConsumerWarps = 8;
+constexpr int kTmaThreads = (kConsumerWarps + 1) * kWarp;
+constexpr int kStages = 3;
+constexpr int kStageMax = 32 * 1024;  // bytes of one ring stage
 
 __device__ __forceinline__ float dot8(const float4& xa, const float4& xb, const uint4& w,
                                       float acc) {
@@ -92,150 +98,192 @@ __device__ void head_finish(const GemvArgs& a, int M, unsigned long long* red_s,
   if (threadIdx.x == 0) *a.ticket = 0u;
 }
 
+__device__ __forceinline__ void consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * kWarp) : "memory");
+}
+
 // ---------------------------------------------------------------------------
-// gemv_m1
+// gemv_tma
+//
+// Row groups: `rpc` = 8 / ksplit row slots per group; warp w owns K segment
+// ks = w % ksplit (chunks x 256 elements) of row slot w / ksplit.  With
+// SwiGLU the first rpc/2 slots are gate rows and the rest the up rows of
+// the same outputs.  Group g is one contiguous block of rows per matrix,
+// loaded by one (two for SwiGLU) bulk copies.
 // ---------------------------------------------------------------------------
 template <int PRO, int EPI>
-__global__ void __launch_bounds__(kThreads, 2)
-    gemv_m1_kernel(const GemvArgs a, const int chunks, const int ksplit) {
-  extern __shared__ float4 xs4[];  // K floats, permuted
-  __shared__ float red[kWarps];
-  __shared__ float part[kWarps][2];
-  __shared__ unsigned long long best_s[kWarps];
+__global__ void __launch_bounds__(kTmaThreads, 1)
+    gemv_tma_kernel(const GemvArgs a, const int chunks, const int ksplit) {
+  extern __shared__ __align__(128) uint8_t dsm[];  // ring | x (K floats)
+  __shared__ __align__(8) uint64_t full[kStages];
+  __shared__ __align__(8) uint64_t empty[kStages];
+  __shared__ float part[2][kConsumerWarps];
+  __shared__ float ssq[kConsumerWarps];
+  __shared__ unsigned long long best_s[kConsumerWarps + 1];
+  __shared__ volatile int abort_s[2];  // set by a wait that gave up, per iteration parity
   __shared__ bool last_s;
 
+  constexpr bool SW = EPI == EPI_SWIGLU;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int K = a.K;
-  const int ks = warp % ksplit, slot = warp / ksplit, rpc = kWarps / ksplit;
-  constexpr int RPT = (EPI == EPI_SWIGLU) ? 1 : 2;
-  const int64_t ngroups = (a.N + int64_t(rpc) * RPT - 1) / (int64_t(rpc) * RPT);
-  const int kbase = ks * chunks * 256;
+  const int rpc = kConsumerWarps / ksplit;
+  const int rpg = SW ? rpc / 2 : rpc;  // output rows per group
+  const int64_t ngroups = (a.N + rpg - 1) / rpg;
+  const size_t row_bytes = size_t(K) * 2;
+  const uint32_t stage_bytes = uint32_t(rpc * row_bytes);
+  uint8_t* ring = dsm;
+  float* xs = reinterpret_cast<float*>(dsm + kStages * stage_bytes);
 
-  pdl_trigger();
-
-  uint4 w0[8], w1[8];
-  auto issue = [&](int64_t g) {
-    const int64_t r0 = (EPI == EPI_SWIGLU) ? g * rpc + slot : (g * rpc + slot) * 2;
-    const bool v0 = r0 < a.N;
-    const bool v1 = (EPI == EPI_SWIGLU) ? v0 : (r0 + 1 < a.N);
-    const uint16_t* p0 = a.w + r0 * K + kbase + lane * 8;
-    const uint16_t* p1 = (EPI == EPI_SWIGLU) ? a.w2 + r0 * K + kbase + lane * 8 : p0 + K;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      if (c < chunks) {
-        w0[c] = v0 ? ld_stream(p0 + c * 256) : make_uint4(0, 0, 0, 0);
-        w1[c] = v1 ? ld_stream(p1 + c * 256) : make_uint4(0, 0, 0, 0);
-      }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
     }
-  };
-
-  int64_t g = blockIdx.x;
-  if (g < ngroups) issue(g);  // independent of earlier kernels
-  pdl_wait();
-
-  // ---- prologue: x (or rmsnorm(x)) into shared memory ---------------------
-  const int k8_step = kThreads * 8;
-  float inv = 1.0f;
-  const uint16_t* erow = nullptr;
-  if (PRO == PRO_EMBED_NORM) erow = a.embed + size_t(a.tokens[0]) * K;
-  auto load8 = [&](int k8, float* v) {
-    if (PRO == PRO_EMBED_NORM) {
-      uint4 u = *reinterpret_cast<const uint4*>(erow + k8);
-      v[0] = bf16lo(u.x); v[1] = bf16hi(u.x); v[2] = bf16lo(u.y); v[3] = bf16hi(u.y);
-      v[4] = bf16lo(u.z); v[5] = bf16hi(u.z); v[6] = bf16lo(u.w); v[7] = bf16hi(u.w);
-    } else {
-      float4 p = *reinterpret_cast<const float4*>(a.x + k8);
-      float4 q = *reinterpret_cast<const float4*>(a.x + k8 + 4);
-      v[0] = p.x; v[1] = p.y; v[2] = p.z; v[3] = p.w;
-      v[4] = q.x; v[5] = q.y; v[6] = q.z; v[7] = q.w;
-    }
-  };
-  if (PRO != PRO_NONE) {
-    float ss = 0.f;
-    for (int k8 = threadIdx.x * 8; k8 < K; k8 += k8_step) {
-      float v[8];
-      load8(k8, v);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
-    }
-    ss = block_sum<kThreads>(ss, red);
-    inv = 1.0f / sqrtf(ss / float(K) + a.eps);
-  }
-  for (int k8 = threadIdx.x * 8; k8 < K; k8 += k8_step) {
-    float v[8];
-    load8(k8, v);
-    if (PRO == PRO_EMBED_NORM && blockIdx.x == 0) {
-      *reinterpret_cast<float4*>(a.x_out + k8) = make_float4(v[0], v[1], v[2], v[3]);
-      *reinterpret_cast<float4*>(a.x_out + k8 + 4) = make_float4(v[4], v[5], v[6], v[7]);
-    }
-    if (PRO != PRO_NONE) {
-      float4 wa = *reinterpret_cast<const float4*>(a.norm_w + k8);
-      float4 wb = *reinterpret_cast<const float4*>(a.norm_w + k8 + 4);
-      v[0] = norm_scale(v[0], inv, wa.x, a.norm_mode); v[1] = norm_scale(v[1], inv, wa.y, a.norm_mode);
-      v[2] = norm_scale(v[2], inv, wa.z, a.norm_mode); v[3] = norm_scale(v[3], inv, wa.w, a.norm_mode);
-      v[4] = norm_scale(v[4], inv, wb.x, a.norm_mode); v[5] = norm_scale(v[5], inv, wb.y, a.norm_mode);
-      v[6] = norm_scale(v[6], inv, wb.z, a.norm_mode); v[7] = norm_scale(v[7], inv, wb.w, a.norm_mode);
-    }
-    const int i4 = ((k8 >> 8) * 2) * 32 + ((k8 & 255) >> 3);
-    xs4[i4] = make_float4(v[0], v[1], v[2], v[3]);
-    xs4[i4 + 32] = make_float4(v[4], v[5], v[6], v[7]);
+    abort_s[0] = abort_s[1] = 0;
+    mbar_fence_init();
   }
   __syncthreads();
+  pdl_trigger();
 
-  // ---- main loop over row groups -----------------------------------------
   unsigned long long best = 0ull;
-  const int cg0 = kbase >> 8;
-  for (; g < ngroups; g += gridDim.x) {
-    if (g != blockIdx.x) issue(g);
-    float acc0 = 0.f, acc1 = 0.f;
+  if (warp == kConsumerWarps) {
+    // ---- producer: weights only, so no wait on the previous kernel ----
+    if (lane == 0) {
+      int it = 0;
+      for (int64_t g = blockIdx.x; g < ngroups; g += gridDim.x, ++it) {
+        const int s = it % kStages;
+        const uint32_t ph = (it / kStages) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1)) {
+          abort_s[0] = abort_s[1] = 1;  // consumers stop waiting for stages
+          if (a.err) atomicExch(a.err, 2);
+          break;
+        }
+        uint8_t* dst = ring + s * stage_bytes;
+        const int64_t r0 = g * rpg;
+        const int64_t nr = min(int64_t(rpg), a.N - r0);
+        const uint32_t bytes = uint32_t(nr * row_bytes);
+        mbar_expect_tx(&full[s], SW ? 2 * bytes : bytes);
+        bulk_g2s(dst, a.w + r0 * K, bytes, &full[s]);
+        if (SW) bulk_g2s(dst + rpg * row_bytes, a.w2 + r0 * K, bytes, &full[s]);
+      }
+    }
+  } else {
+    // ---- consumers ----
+    pdl_wait();
+    const int ks = warp % ksplit, slot = warp / ksplit;
+    const int kbase = ks * chunks * 256;
+    // stage x (embedding row or activations) in shared memory
+    const uint16_t* erow = PRO == PRO_EMBED_NORM ? a.embed + size_t(a.tokens[0]) * K : nullptr;
+    float ss = 0.f;
+    for (int k8 = threadIdx.x * 8; k8 < K; k8 += kConsumerWarps * kWarp * 8) {
+      float4 p, q;
+      if (PRO == PRO_EMBED_NORM) {
+        const uint4 u = *reinterpret_cast<const uint4*>(erow + k8);
+        p = make_float4(bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y));
+        q = make_float4(bf16lo(u.z), bf16hi(u.z), bf16lo(u.w), bf16hi(u.w));
+        if (blockIdx.x == 0) {
+          *reinterpret_cast<float4*>(a.x_out + k8) = p;
+          *reinterpret_cast<float4*>(a.x_out + k8 + 4) = q;
+        }
+      } else {
+        p = *reinterpret_cast<const float4*>(a.x + k8);
+        q = *reinterpret_cast<const float4*>(a.x + k8 + 4);
+      }
+      *reinterpret_cast<float4*>(xs + k8) = p;
+      *reinterpret_cast<float4*>(xs + k8 + 4) = q;
+      if (PRO != PRO_NONE) {
+        ss = fmaf(p.x, p.x, ss); ss = fmaf(p.y, p.y, ss); ss = fmaf(p.z, p.z, ss); ss = fmaf(p.w, p.w, ss);
+        ss = fmaf(q.x, q.x, ss); ss = fmaf(q.y, q.y, ss); ss = fmaf(q.z, q.z, ss); ss = fmaf(q.w, q.w, ss);
+      }
+    }
+    if (PRO != PRO_NONE) {
+      ss = warp_sum(ss);
+      if (lane == 0) ssq[warp] = ss;
+    }
+    consumer_sync();
+    float inv = 1.0f;
+    if (PRO != PRO_NONE) {
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) tot += ssq[w];
+      inv = 1.0f / sqrtf(tot / float(K) + a.eps);
+    }
+    // this warp's K segment, in registers
+    float4 xa[8], xb[8];
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       if (c < chunks) {
-        const float4 xa = xs4[((cg0 + c) * 2) * 32 + lane];
-        const float4 xb = xs4[((cg0 + c) * 2 + 1) * 32 + lane];
-        acc0 = dot8(xa, xb, w0[c], acc0);
-        acc1 = dot8(xa, xb, w1[c], acc1);
+        const int k = kbase + c * 256 + lane * 8;
+        float4 p = *reinterpret_cast<const float4*>(xs + k);
+        float4 q = *reinterpret_cast<const float4*>(xs + k + 4);
+        if (PRO != PRO_NONE) {
+          const float4 wa = __ldg(reinterpret_cast<const float4*>(a.norm_w + k));
+          const float4 wb = __ldg(reinterpret_cast<const float4*>(a.norm_w + k + 4));
+          const int md = a.norm_mode;
+          p = make_float4(norm_scale(p.x, inv, wa.x, md), norm_scale(p.y, inv, wa.y, md),
+                          norm_scale(p.z, inv, wa.z, md), norm_scale(p.w, inv, wa.w, md));
+          q = make_float4(norm_scale(q.x, inv, wb.x, md), norm_scale(q.y, inv, wb.y, md),
+                          norm_scale(q.z, inv, wb.z, md), norm_scale(q.w, inv, wb.w, md));
+        }
+        xa[c] = p;
+        xb[c] = q;
       }
     }
-    acc0 = warp_sum(acc0);
-    acc1 = warp_sum(acc1);
-    if (ksplit > 1) {
-      if (lane == 0) {
-        part[warp][0] = acc0;
-        part[warp][1] = acc1;
-      }
-      __syncthreads();
-      if (ks == 0 && lane == 0)
-        for (int j = 1; j < ksplit; ++j) {
-          acc0 += part[warp + j][0];
-          acc1 += part[warp + j][1];
-        }
-    }
-    if (ks == 0 && lane == 0) {
-      if (EPI == EPI_SWIGLU) {
-        const int64_t r = g * rpc + slot;
-        if (r < a.N) {
-          const float sg = acc0 / (1.0f + expf(-acc0));
-          a.y[r] = sg * acc1;
-        }
-      } else {
-        const int64_t r0 = (g * rpc + slot) * 2;
+    const bool need_sync = ksplit > 1 || SW;
+    int it = 0;
+    for (int64_t g = blockIdx.x; g < ngroups; g += gridDim.x, ++it) {
+      const int s = it % kStages;
+      const uint32_t ph = (it / kStages) & 1;
+      const int64_t r0 = g * rpg;
+      const int rslot = SW ? slot % rpg : slot;
+      const bool valid = r0 + rslot < a.N;
+      float acc = 0.f;
+      const bool ok = !(abort_s[0] | abort_s[1]) && mbar_wait(&full[s], ph);
+      if (ok) {
+        if (valid) {
+          const uint16_t* wr = reinterpret_cast<const uint16_t*>(ring + s * stage_bytes +
+                                                                 slot * row_bytes) +
+                               kbase + lane * 8;
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const int64_t r = r0 + i;
-          const float v = i == 0 ? acc0 : acc1;
-          if (r < a.N) {
-            if (EPI == EPI_ADD) a.y[r] += v;
-            else a.y[r] = v;
-            if (EPI == EPI_HEAD_ARGMAX) {
-              unsigned long long kk = argmax_key(v, uint32_t(r));
-              best = kk > best ? kk : best;
-            }
+          for (int c = 0; c < 8; ++c)
+            if (c < chunks) acc = dot8(xa[c], xb[c], *reinterpret_cast<const uint4*>(wr + c * 256), acc);
+        }
+      } else if (lane == 0) {
+        abort_s[it & 1] = 1;
+        if (a.err) atomicExch(a.err, 2);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      acc = warp_sum(acc);
+      bool stop = !ok;
+      if (need_sync) {
+        // every consumer warp passes this barrier each iteration, so the
+        // stop decision (this iteration's flag) is the same for all of them
+        if (lane == 0) part[it & 1][warp] = acc;
+        consumer_sync();
+        stop = abort_s[it & 1] != 0;
+      }
+      if (!stop && lane == 0 && ks == 0 && valid && (!SW || slot < rpg)) {
+        if (ksplit > 1)
+          for (int j = 1; j < ksplit; ++j) acc += part[it & 1][warp + j];
+        const int64_t r = r0 + rslot;
+        if (SW) {
+          float up = 0.f;
+          for (int j = 0; j < ksplit; ++j) up += part[it & 1][(slot + rpg) * ksplit + j];
+          const float sg = acc / (1.0f + expf(-acc));
+          a.y[r] = sg * up;
+        } else if (EPI == EPI_ADD) {
+          a.y[r] += acc;
+        } else {
+          a.y[r] = acc;
+          if (EPI == EPI_HEAD_ARGMAX) {
+            const unsigned long long kk = argmax_key(acc, uint32_t(r));
+            best = kk > best ? kk : best;
           }
         }
       }
+      if (stop) break;
     }
-    if (ksplit > 1) __syncthreads();
   }
 
   if (EPI == EPI_HEAD_ARGMAX) {
@@ -244,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncthreads();
     if (threadIdx.x == 0) {
       unsigned long long b = best_s[0];
-      for (int w = 1; w < kWarps; ++w) b = best_s[w] > b ? best_s[w] : b;
+      for (int w = 1; w <= kConsumerWarps; ++w) b = best_s[w] > b ? best_s[w] : b;
       a.am_part[blockIdx.x] = b;
     }
   }
@@ -344,6 +392,7 @@ __global__ void __launch_bounds__(kThreads) gemv_gen_kernel(const GemvArgs a) {
     head_finish<EPI == EPI_HEAD_ARGMAX>(a, M, red_s, &last_s);
 }
 
+
 template <typename Kern>
 cudaError_t launch_k(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
                      const GemvArgs& a, int c, int ks) {
@@ -375,34 +424,36 @@ cudaError_t launch_k2(Kern kern, dim3 grid, dim3 block, cudaStream_t s, bool pdl
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
-bool use_m1(const GemvArgs& a) {
+bool use_tma(const GemvArgs& a) {
   return a.M == 1 && a.K % 256 == 0 && a.K <= 256 * 8 * 8 &&
          (reinterpret_cast<uintptr_t>(a.w) & 15) == 0 &&
          (a.w2 == nullptr || (reinterpret_cast<uintptr_t>(a.w2) & 15) == 0) &&
          (a.x == nullptr || (reinterpret_cast<uintptr_t>(a.x) & 15) == 0);
 }
 
-// Split-K factor inside a CTA: the smallest that gives every warp of a
-// 2-CTA-per-SM grid a task, with at most 8 chunks of 256 per warp.
+// Split-K factor: segments of at most 8 x 256 elements per warp, a stage of
+// at most 32 KB, and (when possible) at least 4 row groups per SM.
 void pick_split(const GemvArgs& a, GemvEpi epi, int num_sms, int* chunks, int* ksplit) {
   const int tc = a.K / 256;
-  const int64_t tasks1 = (epi == EPI_SWIGLU) ? a.N : (a.N + 1) / 2;
-  const int64_t want = int64_t(num_sms) * 2 * kWarps;
   int best = -1;
   for (int ks : {1, 2, 4, 8}) {
     if (tc % ks != 0 || tc / ks > 8) continue;
+    const int rpc = kConsumerWarps / ks;
+    if (epi == EPI_SWIGLU && rpc < 2) continue;
+    if (size_t(rpc) * a.K * 2 > size_t(kStageMax)) continue;
     best = ks;
-    if (tasks1 * ks >= want) break;
+    const int rpg = epi == EPI_SWIGLU ? rpc / 2 : rpc;
+    if ((a.N + rpg - 1) / rpg >= int64_t(num_sms) * 4) break;
   }
   *ksplit = best;
   *chunks = best > 0 ? tc / best : 0;
 }
 
-int m1_grid(const GemvArgs& a, GemvEpi epi, int ksplit, int num_sms) {
-  const int rpc = kWarps / ksplit;
-  const int64_t per = int64_t(rpc) * ((epi == EPI_SWIGLU) ? 1 : 2);
-  const int64_t ngroups = (a.N + per - 1) / per;
-  return int(std::min<int64_t>(ngroups, int64_t(num_sms) * 2));
+int tma_grid(const GemvArgs& a, GemvEpi epi, int ksplit, int num_sms) {
+  const int rpc = kConsumerWarps / ksplit;
+  const int rpg = epi == EPI_SWIGLU ? rpc / 2 : rpc;
+  const int64_t ngroups = (a.N + rpg - 1) / rpg;
+  return int(std::min<int64_t>(ngroups, int64_t(num_sms)));
 }
 
 int gen_grid(const GemvArgs& a, int num_sms) {
@@ -410,41 +461,44 @@ int gen_grid(const GemvArgs& a, int num_sms) {
   return int(std::min<int64_t>(need, int64_t(num_sms) * 4));
 }
 
-constexpr int kMaxM1Smem = 256 * 8 * 8 * sizeof(float);  // K <= 16384
+size_t tma_smem(const GemvArgs& a, int ksplit) {
+  return size_t(kStages) * (kConsumerWarps / ksplit) * a.K * 2 + size_t(a.K) * 4;
+}
+
+constexpr int kMaxTmaSmem = kStages * kStageMax + 256 * 8 * 8 * 4;  // ring + x (K <= 16384)
 
 template <int PRO, int EPI>
-cudaError_t set_m1_attr() {
-  return cudaFuncSetAttribute(gemv_m1_kernel<PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              kMaxM1Smem);
+cudaError_t set_tma_attr() {
+  return cudaFuncSetAttribute(gemv_tma_kernel<PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              kMaxTmaSmem);
 }
 
 template <int PRO>
-cudaError_t set_m1_attrs() {
-  TMG_CUDA_TRY((set_m1_attr<PRO, EPI_STORE>()));
-  TMG_CUDA_TRY((set_m1_attr<PRO, EPI_ADD>()));
-  TMG_CUDA_TRY((set_m1_attr<PRO, EPI_SWIGLU>()));
-  TMG_CUDA_TRY((set_m1_attr<PRO, EPI_HEAD>()));
-  return set_m1_attr<PRO, EPI_HEAD_ARGMAX>();
+cudaError_t set_tma_attrs() {
+  TMG_CUDA_TRY((set_tma_attr<PRO, EPI_STORE>()));
+  TMG_CUDA_TRY((set_tma_attr<PRO, EPI_ADD>()));
+  TMG_CUDA_TRY((set_tma_attr<PRO, EPI_SWIGLU>()));
+  TMG_CUDA_TRY((set_tma_attr<PRO, EPI_HEAD>()));
+  return set_tma_attr<PRO, EPI_HEAD_ARGMAX>();
 }
 
 template <int PRO, int EPI>
-cudaError_t launch_m1(const GemvArgs& a, cudaStream_t s, bool pdl, int num_sms, int chunks,
-                      int ksplit) {
-  auto kern = gemv_m1_kernel<PRO, EPI>;
-  const size_t smem = size_t(a.K) * sizeof(float);
-  const int grid = m1_grid(a, GemvEpi(EPI), ksplit, num_sms);
-  return launch_k(kern, dim3(grid), dim3(kThreads), smem, s, pdl, a, chunks, ksplit);
+cudaError_t launch_tma(const GemvArgs& a, cudaStream_t s, bool pdl, int num_sms, int chunks,
+                       int ksplit) {
+  const int grid = tma_grid(a, GemvEpi(EPI), ksplit, num_sms);
+  return launch_k(gemv_tma_kernel<PRO, EPI>, dim3(grid), dim3(kTmaThreads), tma_smem(a, ksplit),
+                  s, pdl, a, chunks, ksplit);
 }
 
 template <int PRO>
-cudaError_t launch_m1_epi(const GemvArgs& a, GemvEpi epi, cudaStream_t s, bool pdl, int num_sms,
-                          int chunks, int ksplit) {
+cudaError_t launch_tma_epi(const GemvArgs& a, GemvEpi epi, cudaStream_t s, bool pdl, int num_sms,
+                           int chunks, int ksplit) {
   switch (epi) {
-    case EPI_STORE: return launch_m1<PRO, EPI_STORE>(a, s, pdl, num_sms, chunks, ksplit);
-    case EPI_ADD: return launch_m1<PRO, EPI_ADD>(a, s, pdl, num_sms, chunks, ksplit);
-    case EPI_SWIGLU: return launch_m1<PRO, EPI_SWIGLU>(a, s, pdl, num_sms, chunks, ksplit);
-    case EPI_HEAD: return launch_m1<PRO, EPI_HEAD>(a, s, pdl, num_sms, chunks, ksplit);
-    case EPI_HEAD_ARGMAX: return launch_m1<PRO, EPI_HEAD_ARGMAX>(a, s, pdl, num_sms, chunks, ksplit);
+    case EPI_STORE: return launch_tma<PRO, EPI_STORE>(a, s, pdl, num_sms, chunks, ksplit);
+    case EPI_ADD: return launch_tma<PRO, EPI_ADD>(a, s, pdl, num_sms, chunks, ksplit);
+    case EPI_SWIGLU: return launch_tma<PRO, EPI_SWIGLU>(a, s, pdl, num_sms, chunks, ksplit);
+    case EPI_HEAD: return launch_tma<PRO, EPI_HEAD>(a, s, pdl, num_sms, chunks, ksplit);
+    case EPI_HEAD_ARGMAX: return launch_tma<PRO, EPI_HEAD_ARGMAX>(a, s, pdl, num_sms, chunks, ksplit);
   }
   return cudaErrorInvalidValue;
 }
@@ -466,23 +520,23 @@ cudaError_t launch_gen(const GemvArgs& a, GemvEpi epi, cudaStream_t s, bool pdl,
 }  // namespace
 
 cudaError_t gemv_prepare() {
-  TMG_CUDA_TRY(set_m1_attrs<PRO_NONE>());
-  TMG_CUDA_TRY(set_m1_attrs<PRO_NORM>());
-  return set_m1_attrs<PRO_EMBED_NORM>();
+  TMG_CUDA_TRY(set_tma_attrs<PRO_NONE>());
+  TMG_CUDA_TRY(set_tma_attrs<PRO_NORM>());
+  return set_tma_attrs<PRO_EMBED_NORM>();
 }
 
 bool gemv_fused_ok(const GemvArgs& a, GemvEpi epi) {
-  if (!use_m1(a)) return false;
+  if (!use_tma(a)) return false;
   int chunks, ks;
   pick_split(a, epi, 148, &chunks, &ks);
   return ks > 0;
 }
 
 int gemv_grid(const GemvArgs& a, GemvEpi epi, int num_sms) {
-  if (use_m1(a)) {
+  if (use_tma(a)) {
     int chunks, ks;
     pick_split(a, epi, num_sms, &chunks, &ks);
-    if (ks > 0) return m1_grid(a, epi, ks, num_sms);
+    if (ks > 0) return tma_grid(a, epi, ks, num_sms);
   }
   return gen_grid(a, num_sms);
 }
@@ -490,15 +544,15 @@ int gemv_grid(const GemvArgs& a, GemvEpi epi, int num_sms) {
 cudaError_t launch_gemv(const GemvArgs& a, GemvPro pro, GemvEpi epi, cudaStream_t s, bool pdl,
                         int num_sms) {
   if (a.N <= 0 || a.K <= 0 || a.M < 1 || a.M > kMaxStreams) return cudaErrorInvalidValue;
-  if (use_m1(a)) {
+  if (use_tma(a)) {
     int chunks, ks;
     pick_split(a, epi, num_sms, &chunks, &ks);
     if (ks > 0) {
       switch (pro) {
-        case PRO_NONE: return launch_m1_epi<PRO_NONE>(a, epi, s, pdl, num_sms, chunks, ks);
-        case PRO_NORM: return launch_m1_epi<PRO_NORM>(a, epi, s, pdl, num_sms, chunks, ks);
+        case PRO_NONE: return launch_tma_epi<PRO_NONE>(a, epi, s, pdl, num_sms, chunks, ks);
+        case PRO_NORM: return launch_tma_epi<PRO_NORM>(a, epi, s, pdl, num_sms, chunks, ks);
         case PRO_EMBED_NORM:
-          return launch_m1_epi<PRO_EMBED_NORM>(a, epi, s, pdl, num_sms, chunks, ks);
+          return launch_tma_epi<PRO_EMBED_NORM>(a, epi, s, pdl, num_sms, chunks, ks);
       }
     }
   }

@@ -76,6 +76,7 @@ struct GemvArgs {
   unsigned long long* am_part = nullptr;  // [grid, M]
   unsigned int* ticket = nullptr;
   StreamState st{};
+  int32_t* err = nullptr;  // device error word (2 = a bounded wait gave up)
 };
 
 cudaError_t launch_gemv(const GemvArgs& a, GemvPro pro, GemvEpi epi, cudaStream_t s, bool pdl,
@@ -141,6 +142,15 @@ cudaError_t launch_swiglu(const float* gate, const float* up, int64_t n, float* 
 // y[T, N] (+)= x[T, K] . W^T  (SIMT f32 path, any shape).
 cudaError_t launch_gemm_simt(const float* x, const uint16_t* w, int64_t T, int64_t N, int64_t K,
                              float* y, int64_t ldy, bool accumulate, cudaStream_t s);
+// Tensor-core prefill GEMM (tcgen05): y[T, N] (+)= (x_hi + x_lo)[T, K] . W^T
+// with x split into two BF16 operands by launch_split.  err: device error
+// word (2 when a bounded wait gave up).
+bool gemm_tc_supported(int64_t K, const void* w);
+cudaError_t gemm_tc_prepare();
+cudaError_t launch_split(const float* x, int64_t n, uint16_t* hi, uint16_t* lo, cudaStream_t s);
+cudaError_t launch_gemm_tc(const uint16_t* x_hi, const uint16_t* x_lo, const uint16_t* w,
+                           int64_t T, int64_t N, int64_t K, float* y, int64_t ldy,
+                           bool accumulate, int32_t* err, cudaStream_t s);
 // argmax per row (op level and the first greedy step).
 cudaError_t launch_argmax_rows(const float* logits, int64_t V, int rows, uint32_t* out,
                                cudaStream_t s);
