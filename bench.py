@@ -159,10 +159,12 @@ def cpu_decode_sample(cfg, tensors, prompt, n_tokens):
             "cores": oracle.num_threads(), "decode_s": t_dec, "prefill_s": t_pre}
 
 
-def make_c2(device: str):
+def make_c2(device: str, layers: int = 0):
     from tinyminigo_b200 import synth
 
     cfg = synth.CONFIGS["c2"]
+    if layers:
+        cfg = synth.with_layers(cfg, layers)
     t0 = time.time()
     w = synth.make_weights(cfg, 2024, device=device)
     log(f"c2 weights generated on {device} in {time.time() - t0:.1f}s")
@@ -230,7 +232,7 @@ def run_ours(args, rank, world, local_rank):
     from tinyminigo_b200 import synth
     from tinyminigo_b200.model import GenParams, Model, ModelConfig, generate
 
-    cfg, w = make_c2("cuda")
+    cfg, w = make_c2("cuda", args.ncu_layers if args.ncu_steps else 0)
     mc = ModelConfig(cfg["hidden_size"], cfg["num_hidden_layers"], cfg["num_attention_heads"],
                      cfg["num_key_value_heads"], cfg["head_dim"], cfg["intermediate_size"],
                      cfg["rms_norm_eps"], cfg["rope_theta"], cfg["vocab_size"], [], 0)
@@ -242,6 +244,13 @@ def run_ours(args, rank, world, local_rank):
 
     # --- device-resident decode loop (value) ---
     cache = model.new_cache(PROMPT + GEN + 8)
+    if args.ncu_steps:
+        # profiling mode: one prefill and a short greedy decode, nothing else
+        logits = model.forward_seq(prompt, cache)
+        model.decode([int(np.argmax(logits))], cache, args.ncu_steps)
+        cache.close()
+        model.close()
+        return
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     pe0, pe1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
@@ -377,6 +386,10 @@ def main():
     ap.add_argument("--workload", choices=["c2"], default="c2")
     ap.add_argument("--cpu-tokens", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ncu-steps", type=int, default=0,
+                    help="profiling mode: prefill + this many decode steps, no timing, no output")
+    ap.add_argument("--ncu-layers", type=int, default=0,
+                    help="profiling mode only: build the c2 shape with this many layers")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -278,12 +278,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(
   for (int64_t t0 = 0; t0 < n_keys; t0 += kTile) {
     const int nt = int(n_keys - t0 < kTile ? n_keys - t0 : kTile);
     __syncthreads();
-    for (int i = tid; i < nt * (D / 4); i += kAttnThreads) {
+    for (int i = tid; i < kTile * (D / 4); i += kAttnThreads) {
       const int t = i / (D / 4), j4 = i % (D / 4);
-      *reinterpret_cast<float4*>(&ks[t][j4 * 4]) =
-          *reinterpret_cast<const float4*>(kc + (t0 + t) * kvd + kvh * D + j4 * 4);
-      *reinterpret_cast<float4*>(&vs[t][j4 * 4]) =
-          *reinterpret_cast<const float4*>(vc + (t0 + t) * kvd + kvh * D + j4 * 4);
+      float4 kv4 = make_float4(0.f, 0.f, 0.f, 0.f), vv4 = kv4;  // rows past nt: zeros, not
+      if (t < nt) {                                              // stale smem (0 * NaN)
+        kv4 = *reinterpret_cast<const float4*>(kc + (t0 + t) * kvd + kvh * D + j4 * 4);
+        vv4 = *reinterpret_cast<const float4*>(vc + (t0 + t) * kvd + kvh * D + j4 * 4);
+      }
+      *reinterpret_cast<float4*>(&ks[t][j4 * 4]) = kv4;
+      *reinterpret_cast<float4*>(&vs[t][j4 * 4]) = vv4;
     }
     __syncthreads();
     float s[kTile];

@@ -16,6 +16,7 @@ library; logits come back to the host only when asked for.
 from __future__ import annotations
 
 import ctypes
+import weakref
 from dataclasses import dataclass, field
 from pathlib import Path
 
@@ -148,6 +149,7 @@ class Model:
         check(lib().tmg_create(device, ctypes.byref(cc), ctypes.byref(h)), None, "tmg_create")
         self._h = h
         self._gen_cache = None
+        self._caches = []
         if tp is not None:
             uid, rank, world = tp
             buf = (ctypes.c_uint8 * 128).from_buffer_copy(bytes(uid))
@@ -183,9 +185,16 @@ class Model:
         return m
 
     def close(self):
+        """Free the device state; caches made from this model are closed
+        first (a cache cannot outlive its model's context)."""
         if getattr(self, "_gen_cache", None) is not None:
             self._gen_cache.close()
             self._gen_cache = None
+        for ref in getattr(self, "_caches", []):
+            c = ref()
+            if c is not None:
+                c.close()
+        self._caches = []
         if getattr(self, "_h", None):
             lib().tmg_destroy(self._h)
             self._h = None
@@ -278,6 +287,9 @@ class KvCache:
         check(lib().tmg_kv_create(model._h, n_streams, capacity, ctypes.byref(h)), model._h,
               "kv_create")
         self._h = h
+        if not hasattr(model, "_caches"):
+            model._caches = []
+        model._caches.append(weakref.ref(self))
 
     def close(self):
         if getattr(self, "_h", None):
