@@ -36,12 +36,14 @@ __device__ __forceinline__ void rot(float a, float b, float c, float s, float* o
 
 // Grid (n_kv, nsplit, M); 128 threads.  Dynamic smem: q [G][d], K tile
 // [kTile][d+4], V tile [kTile][d], p [G][kTile].
+template <int D>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDecodeArgs a) {
   extern __shared__ float sm[];
   __shared__ float m_s[16], l_s[16], alpha_s[16];
   __shared__ bool last_s;
   const int kvh = blockIdx.x, split = blockIdx.y, m = blockIdx.z;
-  const int d = a.d, half = d / 2, G = a.nq / a.nkv, kvd = a.nkv * d;
+  constexpr int d = D;
+  const int half = d / 2, G = a.nq / a.nkv, kvd = a.nkv * d;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float* qs = sm;                      // [G][d]
   float* ks_ = qs + G * d;             // [kTile][d+4]
@@ -127,16 +129,17 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
       if (lane < nt) {
         const float* kr = ks_ + lane * (d + 4);
         const float* qr = qs + g * d;
-        float acc = 0.f;
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
         for (int j = 0; j < d; j += 4) {
           const float4 k4 = *reinterpret_cast<const float4*>(kr + j);
           const float4 q4 = *reinterpret_cast<const float4*>(qr + j);
-          acc = fmaf(q4.x, k4.x, acc);
-          acc = fmaf(q4.y, k4.y, acc);
-          acc = fmaf(q4.z, k4.z, acc);
-          acc = fmaf(q4.w, k4.w, acc);
+          a0 = fmaf(q4.x, k4.x, a0);
+          a1 = fmaf(q4.y, k4.y, a1);
+          a2 = fmaf(q4.z, k4.z, a2);
+          a3 = fmaf(q4.w, k4.w, a3);
         }
-        s = acc * a.scale;
+        s = ((a0 + a1) + (a2 + a3)) * a.scale;
       }
       const float mt = warp_max(s);
       const float m_old = m_s[g];
@@ -157,9 +160,18 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
       const int idx = tid + r * kAttnThreads;
       if (idx < G * d) {
         const int g = idx / d, j = idx % d;
-        float acc = o_acc[r] * alpha_s[g];
-        for (int t = 0; t < nt; ++t) acc = fmaf(ps[g * kTile + t], vs[t * d + j], acc);
-        o_acc[r] = acc;
+        // P.V over the tile's nt rows (rows past nt are stale), in four
+        // independent chains over t
+        float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
+        int t = 0;
+        for (; t + 4 <= nt; t += 4) {
+          b0 = fmaf(ps[g * kTile + t], vs[t * d + j], b0);
+          b1 = fmaf(ps[g * kTile + t + 1], vs[(t + 1) * d + j], b1);
+          b2 = fmaf(ps[g * kTile + t + 2], vs[(t + 2) * d + j], b2);
+          b3 = fmaf(ps[g * kTile + t + 3], vs[(t + 3) * d + j], b3);
+        }
+        for (; t < nt; ++t) b0 = fmaf(ps[g * kTile + t], vs[t * d + j], b0);
+        o_acc[r] = fmaf(o_acc[r], alpha_s[g], (b0 + b1) + (b2 + b3));
       }
     }
     __syncthreads();
@@ -382,15 +394,30 @@ int attn_decode_nsplit(int nkv, int M, int64_t cap, int num_sms) {
 
 constexpr int kMaxAttnSmem = 96 * 1024;
 
-cudaError_t attn_prepare() {
-  return cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+template <int D>
+cudaError_t attn_attr() {
+  return cudaFuncSetAttribute(attn_decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               kMaxAttnSmem);
+}
+
+cudaError_t attn_prepare() {
+  TMG_CUDA_TRY(attn_attr<16>());
+  TMG_CUDA_TRY(attn_attr<32>());
+  TMG_CUDA_TRY(attn_attr<64>());
+  return attn_attr<128>();
 }
 
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) {
   const int G = a.nq / a.nkv;
-  if (G * a.nkv != a.nq || a.d % 8 != 0 || G * a.d > 8 * kAttnThreads || G > 16)
-    return cudaErrorInvalidValue;
+  if (G * a.nkv != a.nq || G * a.d > 8 * kAttnThreads || G > 16) return cudaErrorInvalidValue;
+  void (*kern)(const AttnDecodeArgs) = nullptr;
+  switch (a.d) {
+    case 16: kern = attn_decode_kernel<16>; break;
+    case 32: kern = attn_decode_kernel<32>; break;
+    case 64: kern = attn_decode_kernel<64>; break;
+    case 128: kern = attn_decode_kernel<128>; break;
+    default: return cudaErrorInvalidValue;
+  }
   // tiles, or the combine's per-split weights when those are larger
   const size_t tiles = size_t(G) * a.d + kTile * (a.d + 4) + kTile * a.d + G * kTile;
   const size_t smem = sizeof(float) * std::max<size_t>(tiles, size_t(G) * a.nsplit);
@@ -405,7 +432,7 @@ cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s, bool pdl
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, attn_decode_kernel, a);
+  return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 cudaError_t launch_attn_prefill(const float* q, int64_t q_ld, const float* kc, const float* vc,

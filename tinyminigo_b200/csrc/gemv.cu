@@ -52,6 +52,24 @@ __device__ __forceinline__ float dot8(const float4& xa, const float4& xb, const 
   return acc;
 }
 
+// Eight independent accumulators (one per element of a 16-byte chunk): the
+// FMA chains stay 'chunks' long instead of 8 * chunks, so a warp issues
+// back to back instead of waiting on its own previous FMA.
+__device__ __forceinline__ void fma8(const float4& xa, const float4& xb, const uint4& w,
+                                     float (&s)[8]) {
+  s[0] = fmaf(xa.x, bf16lo(w.x), s[0]);
+  s[1] = fmaf(xa.y, bf16hi(w.x), s[1]);
+  s[2] = fmaf(xa.z, bf16lo(w.y), s[2]);
+  s[3] = fmaf(xa.w, bf16hi(w.y), s[3]);
+  s[4] = fmaf(xb.x, bf16lo(w.z), s[4]);
+  s[5] = fmaf(xb.y, bf16hi(w.z), s[5]);
+  s[6] = fmaf(xb.z, bf16lo(w.w), s[6]);
+  s[7] = fmaf(xb.w, bf16hi(w.w), s[7]);
+}
+__device__ __forceinline__ float sum8(const float (&s)[8]) {
+  return ((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7]));
+}
+
 // RMSNorm scaling of one element, in either of the reference's orders.
 __device__ __forceinline__ float norm_scale(float v, float inv, float w, int mode) {
   if (mode == 0) {
@@ -244,9 +262,15 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           const uint16_t* wr = reinterpret_cast<const uint16_t*>(ring + s * stage_bytes +
                                                                  slot * row_bytes) +
                                kbase + lane * 8;
+          uint4 wv[8];
 #pragma unroll
           for (int c = 0; c < 8; ++c)
-            if (c < chunks) acc = dot8(xa[c], xb[c], *reinterpret_cast<const uint4*>(wr + c * 256), acc);
+            if (c < chunks) wv[c] = *reinterpret_cast<const uint4*>(wr + c * 256);
+          float sacc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            if (c < chunks) fma8(xa[c], xb[c], wv[c], sacc);
+          acc = sum8(sacc);
         }
       } else if (lane == 0) {
         abort_s[it & 1] = 1;
