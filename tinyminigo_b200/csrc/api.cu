@@ -987,7 +987,8 @@ int tmg_create(int device, const tmg_config* cfg, tmg_ctx** out) {
       cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
       gemv_prepare() != cudaSuccess || attn_prepare() != cudaSuccess ||
-      gemm_tc_prepare() != cudaSuccess || dalloc(c->allocs, &c->d_err, 4) != cudaSuccess ||
+      gemm_tc_prepare() != cudaSuccess || prefill_prepare() != cudaSuccess ||
+      sample_prepare() != cudaSuccess || dalloc(c->allocs, &c->d_err, 4) != cudaSuccess ||
       zero_sync(c, c->d_err, 16) != cudaSuccess) {
     free_all(c->allocs);
     if (c->stream) cudaStreamDestroy(c->stream);

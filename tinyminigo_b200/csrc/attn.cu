@@ -396,11 +396,13 @@ constexpr int kMaxAttnSmem = 96 * 1024;
 
 template <int D>
 cudaError_t attn_attr() {
-  return cudaFuncSetAttribute(attn_decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              kMaxAttnSmem);
+  TMG_CUDA_TRY(set_carveout(attn_prefill_kernel<D>));
+  return set_carveout(attn_decode_kernel<D>, kMaxAttnSmem);
 }
 
 cudaError_t attn_prepare() {
+  TMG_CUDA_TRY(set_carveout(rope_append_kernel));
+  TMG_CUDA_TRY(set_carveout(rope_rows_kernel));
   TMG_CUDA_TRY(attn_attr<16>());
   TMG_CUDA_TRY(attn_attr<32>());
   TMG_CUDA_TRY(attn_attr<64>());

@@ -158,3 +158,20 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
     cudaError_t _e = (expr);                     \
     if (_e != cudaSuccess) return _e;            \
   } while (0)
+
+namespace tmg {
+// Every kernel of the library asks for the largest shared-memory carveout,
+// so consecutive kernels never make an SM switch its L1 / shared split
+// (which drains the SM and keeps the next kernel's CTAs from co-residing
+// with the previous kernel's under programmatic dependent launch).
+template <typename K>
+inline cudaError_t set_carveout(K kern, int max_dynamic_smem = -1) {
+  cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kern),
+                                       cudaFuncAttributePreferredSharedMemoryCarveout,
+                                       int(cudaSharedmemCarveoutMaxShared));
+  if (e == cudaSuccess && max_dynamic_smem >= 0)
+    e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kern),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, max_dynamic_smem);
+  return e;
+}
+}  // namespace tmg

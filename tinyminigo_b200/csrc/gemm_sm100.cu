@@ -260,8 +260,8 @@ bool gemm_tc_supported(int64_t K, const void* w) {
 }
 
 cudaError_t gemm_tc_prepare() {
-  return cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              SMEM_BYTES);
+  TMG_CUDA_TRY(set_carveout(split_kernel));
+  return set_carveout(gemm_tc_kernel, SMEM_BYTES);
 }
 
 cudaError_t launch_split(const float* x, int64_t n, uint16_t* hi, uint16_t* lo, cudaStream_t s) {

@@ -493,8 +493,9 @@ constexpr int kMaxTmaSmem = kStages * kStageMax + 256 * 8 * 8 * 4;  // ring + x 
 
 template <int PRO, int EPI>
 cudaError_t set_tma_attr() {
-  return cudaFuncSetAttribute(gemv_tma_kernel<PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              kMaxTmaSmem);
+  TMG_CUDA_TRY((set_carveout(gemv_gen_kernel<EPI, true>)));
+  TMG_CUDA_TRY((set_carveout(gemv_gen_kernel<EPI, false>)));
+  return set_carveout(gemv_tma_kernel<PRO, EPI>, kMaxTmaSmem);
 }
 
 template <int PRO>

@@ -87,6 +87,8 @@ bool gemv_fused_ok(const GemvArgs& a, GemvEpi epi);
 // (dynamic shared memory limits).
 cudaError_t gemv_prepare();
 cudaError_t attn_prepare();
+cudaError_t prefill_prepare();
+cudaError_t sample_prepare();
 // Scratch the launcher needs for EPI_HEAD*: number of CTAs it will use.
 int gemv_grid(const GemvArgs& a, GemvEpi epi, int num_sms);
 

@@ -150,6 +150,17 @@ __global__ void step_end_kernel(StreamState st, const float* __restrict__ logits
 
 }  // namespace
 
+cudaError_t prefill_prepare() {
+  TMG_CUDA_TRY(set_carveout(embed_kernel));
+  TMG_CUDA_TRY(set_carveout(rmsnorm_kernel<256>));
+  TMG_CUDA_TRY(set_carveout(swiglu_kernel));
+  TMG_CUDA_TRY(set_carveout(gemm_simt_kernel));
+  TMG_CUDA_TRY(set_carveout(argmax_rows_kernel));
+  TMG_CUDA_TRY(set_carveout(set_pos_kernel));
+  TMG_CUDA_TRY(set_carveout(add_kernel));
+  return set_carveout(step_end_kernel);
+}
+
 cudaError_t launch_embed(const uint16_t* embed, const uint32_t* tokens, int64_t T, int h, float* x,
                          cudaStream_t s) {
   if (T <= 0) return cudaSuccess;

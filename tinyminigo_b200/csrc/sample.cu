@@ -203,6 +203,8 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(const SampleArgs a) {
 
 }  // namespace
 
+cudaError_t sample_prepare() { return set_carveout(sample_kernel); }
+
 int sample_slices(int64_t V, int M, int num_sms) {
   (void)M;
   (void)num_sms;
