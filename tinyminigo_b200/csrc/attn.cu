@@ -23,8 +23,9 @@ namespace tmg {
 namespace {
 
 constexpr int kAttnThreads = 128;
-constexpr int kTile = 32;      // positions per shared-memory tile
+constexpr int kTile = 64;      // positions per shared-memory tile
 constexpr int kMinChunk = 64;  // fewest positions a decode split takes
+constexpr int kPTile = 32;     // key positions per prefill tile
 
 // Rotate pair (a, b) by (c, s): (a c - b s, a s + b c), rounded like the
 // reference (two products, then one add/sub; no FMA contraction).
@@ -62,7 +63,19 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
   float* kc = a.kc + size_t(m) * a.cap * kvd;
   float* vc = a.vc + size_t(m) * a.cap * kvd;
 
-  // q heads of this group, rotated at pos (model.rs:422-426)
+  // context range of this split: at least kMinChunk positions per split, so
+  // short contexts use few CTAs (the rest only take their ticket)
+  int chunk = (n_ctx + a.nsplit - 1) / a.nsplit;
+  chunk = max(kMinChunk, (chunk + kTile - 1) / kTile * kTile);
+  const int n_used = (n_ctx + chunk - 1) / chunk;
+  const int c0 = split * chunk;
+  const int c1 = min(n_ctx, c0 + chunk);
+  if (n_used == 1 && split > 0) return;  // one-split launches need no ticket
+  const bool own_pos = append && pos >= c0 && pos < c1;
+  const int d4 = d / 4;
+
+  // q heads of this group rotated at pos (model.rs:422-426), and the first
+  // K/V tile, requested together
   const int rp = pos < a.cap ? pos : 0;
   for (int i = tid; i < G * half; i += blockDim.x) {
     const int g = i / half, j = i % half;
@@ -78,27 +91,42 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
       qs[g * d + j + half] = o1;
     }
   }
-  // context range of this split: at least kMinChunk positions per split, so
-  // short contexts use few CTAs (the rest only take their ticket)
-  int chunk = (n_ctx + a.nsplit - 1) / a.nsplit;
-  chunk = max(kMinChunk, (chunk + kTile - 1) / kTile * kTile);
-  const int n_used = (n_ctx + chunk - 1) / chunk;
-  const int c0 = split * chunk;
-  const int c1 = min(n_ctx, c0 + chunk);
+  auto load_tile = [&](int t0, int nt) {
+    for (int i = tid; i < nt * d4; i += blockDim.x) {
+      const int t = i / d4, j4 = i % d4;
+      if (own_pos && t0 + t == pos) continue;  // written below from registers
+      const float4 kv4 = *reinterpret_cast<const float4*>(kc + size_t(t0 + t) * kvd + kvh * d + j4 * 4);
+      const float4 vv4 = *reinterpret_cast<const float4*>(vc + size_t(t0 + t) * kvd + kvh * d + j4 * 4);
+      *reinterpret_cast<float4*>(ks_ + t * (d + 4) + j4 * 4) = kv4;
+      *reinterpret_cast<float4*>(vs + t * d + j4 * 4) = vv4;
+    }
+  };
+  if (c0 < c1) load_tile(c0, min(kTile, c1 - c0));
   // the CTA whose range holds pos appends the rotated k and raw v
-  if (append && pos >= c0 && pos < c1) {
+  // (KvCache::push, model.rs:432) and puts them in its tile directly
+  if (own_pos) {
     const float* kh = qkv + a.nq * d + kvh * d;
     const float* vh = qkv + (a.nq + a.nkv) * d + kvh * d;
     float* kdst = kc + size_t(pos) * kvd + kvh * d;
     float* vdst = vc + size_t(pos) * kvd + kvh * d;
+    const bool in_first = pos < c0 + kTile;
+    const int tr = pos - c0;
     for (int j = tid; j < half; j += blockDim.x) {
       float o0, o1;
       rot(kh[j], kh[j + half], a.rope_cos[size_t(pos) * half + j],
           a.rope_sin[size_t(pos) * half + j], &o0, &o1);
       kdst[j] = o0;
       kdst[j + half] = o1;
+      if (in_first) {
+        ks_[tr * (d + 4) + j] = o0;
+        ks_[tr * (d + 4) + j + half] = o1;
+      }
     }
-    for (int j = tid; j < d; j += blockDim.x) vdst[j] = vh[j];
+    for (int j = tid; j < d; j += blockDim.x) {
+      const float v = vh[j];
+      vdst[j] = v;
+      if (in_first) vs[tr * d + j] = v;
+    }
   }
   if (tid < G) {
     m_s[tid] = -INFINITY;
@@ -111,42 +139,44 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
   for (int r = 0; r < kMaxOwn; ++r) o_acc[r] = 0.f;
   __syncthreads();
 
-  const int d4 = d / 4;
   for (int t0 = c0; t0 < c1; t0 += kTile) {
     const int nt = min(kTile, c1 - t0);
-    // stage K (padded rows) and V tiles
-    for (int i = tid; i < nt * d4; i += blockDim.x) {
-      const int t = i / d4, j4 = i % d4;
-      const float4 kv4 = *reinterpret_cast<const float4*>(kc + size_t(t0 + t) * kvd + kvh * d + j4 * 4);
-      const float4 vv4 = *reinterpret_cast<const float4*>(vc + size_t(t0 + t) * kvd + kvh * d + j4 * 4);
-      *reinterpret_cast<float4*>(ks_ + t * (d + 4) + j4 * 4) = kv4;
-      *reinterpret_cast<float4*>(vs + t * d + j4 * 4) = vv4;
+    if (t0 != c0) {  // later tiles (long contexts)
+      load_tile(t0, nt);
+      __syncthreads();
     }
-    __syncthreads();
-    // scores: warp w handles heads w, w+4, ...; lane = position
+    // scores: warp w handles heads w, w+4, ...; lane holds positions lane
+    // and lane + 32
     for (int g = warp; g < G; g += kAttnThreads / 32) {
-      float s = -INFINITY;
-      if (lane < nt) {
-        const float* kr = ks_ + lane * (d + 4);
-        const float* qr = qs + g * d;
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      const float* qr = qs + g * d;
+      float sc[2];
 #pragma unroll
-        for (int j = 0; j < d; j += 4) {
-          const float4 k4 = *reinterpret_cast<const float4*>(kr + j);
-          const float4 q4 = *reinterpret_cast<const float4*>(qr + j);
-          a0 = fmaf(q4.x, k4.x, a0);
-          a1 = fmaf(q4.y, k4.y, a1);
-          a2 = fmaf(q4.z, k4.z, a2);
-          a3 = fmaf(q4.w, k4.w, a3);
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int t = lane + 32 * h2;
+        sc[h2] = -INFINITY;
+        if (t < nt) {
+          const float* kr = ks_ + t * (d + 4);
+          float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+          for (int j = 0; j < d; j += 4) {
+            const float4 k4 = *reinterpret_cast<const float4*>(kr + j);
+            const float4 q4 = *reinterpret_cast<const float4*>(qr + j);
+            a0 = fmaf(q4.x, k4.x, a0);
+            a1 = fmaf(q4.y, k4.y, a1);
+            a2 = fmaf(q4.z, k4.z, a2);
+            a3 = fmaf(q4.w, k4.w, a3);
+          }
+          sc[h2] = ((a0 + a1) + (a2 + a3)) * a.scale;
         }
-        s = ((a0 + a1) + (a2 + a3)) * a.scale;
       }
-      const float mt = warp_max(s);
+      const float mt = warp_max(fmaxf(sc[0], sc[1]));
       const float m_old = m_s[g];
       const float m_new = fmaxf(m_old, mt);
-      const float p = lane < nt ? expf(s - m_new) : 0.f;
-      const float lsum = warp_sum(p);
-      ps[g * kTile + lane] = p;
+      const float p0 = lane < nt ? expf(sc[0] - m_new) : 0.f;
+      const float p1 = lane + 32 < nt ? expf(sc[1] - m_new) : 0.f;
+      const float lsum = warp_sum(p0 + p1);
+      ps[g * kTile + lane] = p0;
+      ps[g * kTile + lane + 32] = p1;
       if (lane == 0) {
         const float alpha = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
         alpha_s[g] = alpha;
@@ -160,8 +190,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
       const int idx = tid + r * kAttnThreads;
       if (idx < G * d) {
         const int g = idx / d, j = idx % d;
-        // P.V over the tile's nt rows (rows past nt are stale), in four
-        // independent chains over t
+        // P.V over the tile's nt rows, in four independent chains over t
         float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
         int t = 0;
         for (; t + 4 <= nt; t += 4) {
@@ -176,7 +205,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
     }
     __syncthreads();
   }
-
   float* out = a.out + size_t(m) * a.nq * d + kvh * G * d;
   if (n_used == 1) {
     // the whole context in one CTA: finish here, no partials
@@ -266,8 +294,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(
   constexpr int DPT = D < 64 ? D : 64;
   constexpr int TPR = D / DPT;
   constexpr int ROWS = kAttnThreads / TPR;
-  __shared__ float ks[kTile][D];
-  __shared__ float vs[kTile][D];
+  __shared__ float ks[kPTile][D];
+  __shared__ float vs[kPTile][D];
   const int h = blockIdx.x;
   const int kvh = h / (nq / nkv);
   const int kvd = nkv * D;
@@ -287,10 +315,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(
   }
   float m_run = -INFINITY, l_run = 0.f;
 
-  for (int64_t t0 = 0; t0 < n_keys; t0 += kTile) {
-    const int nt = int(n_keys - t0 < kTile ? n_keys - t0 : kTile);
+  for (int64_t t0 = 0; t0 < n_keys; t0 += kPTile) {
+    const int nt = int(n_keys - t0 < kPTile ? n_keys - t0 : kPTile);
     __syncthreads();
-    for (int i = tid; i < kTile * (D / 4); i += kAttnThreads) {
+    for (int i = tid; i < kPTile * (D / 4); i += kAttnThreads) {
       const int t = i / (D / 4), j4 = i % (D / 4);
       float4 kv4 = make_float4(0.f, 0.f, 0.f, 0.f), vv4 = kv4;  // rows past nt: zeros, not
       if (t < nt) {                                              // stale smem (0 * NaN)
@@ -301,10 +329,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(
       *reinterpret_cast<float4*>(&vs[t][j4 * 4]) = vv4;
     }
     __syncthreads();
-    float s[kTile];
+    float s[kPTile];
     float mt = -INFINITY;
 #pragma unroll
-    for (int t = 0; t < kTile; ++t) {
+    for (int t = 0; t < kPTile; ++t) {
       float acc = 0.f;
 #pragma unroll
       for (int j = 0; j < DPT; ++j) acc = fmaf(qr[j], ks[t][part * DPT + j], acc);
@@ -319,7 +347,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(
     const float alpha = m_run == -INFINITY ? 0.f : expf(m_run - m_new);
     float lsum = 0.f;
 #pragma unroll
-    for (int t = 0; t < kTile; ++t) {
+    for (int t = 0; t < kPTile; ++t) {
       s[t] = s[t] == -INFINITY ? 0.f : expf(s[t] - m_new);
       lsum += s[t];
     }
@@ -329,7 +357,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(
     for (int j = 0; j < DPT; ++j) {
       float acc = o[j] * alpha;
 #pragma unroll
-      for (int t = 0; t < kTile; ++t) acc = fmaf(s[t], vs[t][part * DPT + j], acc);
+      for (int t = 0; t < kPTile; ++t) acc = fmaf(s[t], vs[t][part * DPT + j], acc);
       o[j] = acc;
     }
   }

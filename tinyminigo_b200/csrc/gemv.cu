@@ -36,7 +36,8 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / kWarp;
 constexpr int kConsumerWarps = 8;
 constexpr int kTmaThreads = (kConsumerWarps + 1) * kWarp;
-constexpr int kStages = 3;
+constexpr int kRingBytes = 96 * 1024;  // bytes in flight per SM (HBM latency x bandwidth share)
+constexpr int kMaxStages = 12;
 constexpr int kStageMax = 32 * 1024;  // bytes of one ring stage
 
 __device__ __forceinline__ float dot8(const float4& xa, const float4& xb, const uint4& w,
@@ -129,12 +130,15 @@ __device__ __forceinline__ void consumer_sync() {
 // the same outputs.  Group g is one contiguous block of rows per matrix,
 // loaded by one (two for SwiGLU) bulk copies.
 // ---------------------------------------------------------------------------
+// Two CTAs fit on one SM (registers and shared memory), so under
+// programmatic dependent launch the next GEMV's producer starts streaming
+// while this one drains.
 template <int PRO, int EPI>
-__global__ void __launch_bounds__(kTmaThreads, 1)
+__global__ void __launch_bounds__(kTmaThreads, 2)
     gemv_tma_kernel(const GemvArgs a, const int chunks, const int ksplit) {
-  extern __shared__ __align__(128) uint8_t dsm[];  // ring | x (K floats)
-  __shared__ __align__(8) uint64_t full[kStages];
-  __shared__ __align__(8) uint64_t empty[kStages];
+  extern __shared__ __align__(128) uint8_t dsm[];  // ring | x (K floats, with a norm)
+  __shared__ __align__(8) uint64_t full[kMaxStages];
+  __shared__ __align__(8) uint64_t empty[kMaxStages];
   __shared__ float part[2][kConsumerWarps];
   __shared__ float ssq[kConsumerWarps];
   __shared__ unsigned long long best_s[kConsumerWarps + 1];
@@ -149,11 +153,12 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   const int64_t ngroups = (a.N + rpg - 1) / rpg;
   const size_t row_bytes = size_t(K) * 2;
   const uint32_t stage_bytes = uint32_t(rpc * row_bytes);
+  const int nst = min(kMaxStages, int(kRingBytes / stage_bytes));
   uint8_t* ring = dsm;
-  float* xs = reinterpret_cast<float*>(dsm + kStages * stage_bytes);
+  float* xs = reinterpret_cast<float*>(dsm + nst * stage_bytes);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < nst; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumerWarps);
     }
@@ -169,8 +174,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     if (lane == 0) {
       int it = 0;
       for (int64_t g = blockIdx.x; g < ngroups; g += gridDim.x, ++it) {
-        const int s = it % kStages;
-        const uint32_t ph = (it / kStages) & 1;
+        const int s = it % nst;
+        const uint32_t ph = (it / nst) & 1;
         if (!mbar_wait(&empty[s], ph ^ 1)) {
           abort_s[0] = abort_s[1] = 1;  // consumers stop waiting for stages
           if (a.err) atomicExch(a.err, 2);
@@ -190,10 +195,11 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     pdl_wait();
     const int ks = warp % ksplit, slot = warp / ksplit;
     const int kbase = ks * chunks * 256;
-    // stage x (embedding row or activations) in shared memory
+    // with a norm: stage x (embedding row or activations) in shared memory,
+    // since the sum of squares spans all of K
     const uint16_t* erow = PRO == PRO_EMBED_NORM ? a.embed + size_t(a.tokens[0]) * K : nullptr;
     float ss = 0.f;
-    for (int k8 = threadIdx.x * 8; k8 < K; k8 += kConsumerWarps * kWarp * 8) {
+    for (int k8 = threadIdx.x * 8; PRO != PRO_NONE && k8 < K; k8 += kConsumerWarps * kWarp * 8) {
       float4 p, q;
       if (PRO == PRO_EMBED_NORM) {
         const uint4 u = *reinterpret_cast<const uint4*>(erow + k8);
@@ -214,26 +220,26 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         ss = fmaf(q.x, q.x, ss); ss = fmaf(q.y, q.y, ss); ss = fmaf(q.z, q.z, ss); ss = fmaf(q.w, q.w, ss);
       }
     }
+    float inv = 1.0f;
     if (PRO != PRO_NONE) {
       ss = warp_sum(ss);
       if (lane == 0) ssq[warp] = ss;
-    }
-    consumer_sync();
-    float inv = 1.0f;
-    if (PRO != PRO_NONE) {
+      consumer_sync();
       float tot = 0.f;
 #pragma unroll
       for (int w = 0; w < kConsumerWarps; ++w) tot += ssq[w];
       inv = 1.0f / sqrtf(tot / float(K) + a.eps);
     }
-    // this warp's K segment, in registers
+    // this warp's K segment, in registers (without a norm, straight from
+    // global memory: the rows of x are produced by the previous kernel)
+    const float* xsrc = PRO == PRO_NONE ? a.x : xs;
     float4 xa[8], xb[8];
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       if (c < chunks) {
         const int k = kbase + c * 256 + lane * 8;
-        float4 p = *reinterpret_cast<const float4*>(xs + k);
-        float4 q = *reinterpret_cast<const float4*>(xs + k + 4);
+        float4 p = *reinterpret_cast<const float4*>(xsrc + k);
+        float4 q = *reinterpret_cast<const float4*>(xsrc + k + 4);
         if (PRO != PRO_NONE) {
           const float4 wa = __ldg(reinterpret_cast<const float4*>(a.norm_w + k));
           const float4 wb = __ldg(reinterpret_cast<const float4*>(a.norm_w + k + 4));
@@ -250,8 +256,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     const bool need_sync = ksplit > 1 || SW;
     int it = 0;
     for (int64_t g = blockIdx.x; g < ngroups; g += gridDim.x, ++it) {
-      const int s = it % kStages;
-      const uint32_t ph = (it / kStages) & 1;
+      const int s = it % nst;
+      const uint32_t ph = (it / nst) & 1;
       const int64_t r0 = g * rpg;
       const int rslot = SW ? slot % rpg : slot;
       const bool valid = r0 + rslot < a.N;
@@ -262,14 +268,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           const uint16_t* wr = reinterpret_cast<const uint16_t*>(ring + s * stage_bytes +
                                                                  slot * row_bytes) +
                                kbase + lane * 8;
-          uint4 wv[8];
-#pragma unroll
-          for (int c = 0; c < 8; ++c)
-            if (c < chunks) wv[c] = *reinterpret_cast<const uint4*>(wr + c * 256);
           float sacc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
           for (int c = 0; c < 8; ++c)
-            if (c < chunks) fma8(xa[c], xb[c], wv[c], sacc);
+            if (c < chunks) fma8(xa[c], xb[c], *reinterpret_cast<const uint4*>(wr + c * 256), sacc);
           acc = sum8(sacc);
         }
       } else if (lane == 0) {
@@ -485,11 +487,14 @@ int gen_grid(const GemvArgs& a, int num_sms) {
   return int(std::min<int64_t>(need, int64_t(num_sms) * 4));
 }
 
-size_t tma_smem(const GemvArgs& a, int ksplit) {
-  return size_t(kStages) * (kConsumerWarps / ksplit) * a.K * 2 + size_t(a.K) * 4;
+// ring (as many whole stages as fit kRingBytes) + x staging when normed
+size_t tma_smem(const GemvArgs& a, int ksplit, GemvPro pro) {
+  const size_t stage = size_t(kConsumerWarps / ksplit) * a.K * 2;
+  const size_t nst = std::min<size_t>(kMaxStages, kRingBytes / stage);
+  return nst * stage + (pro != PRO_NONE ? size_t(a.K) * 4 : 0);
 }
 
-constexpr int kMaxTmaSmem = kStages * kStageMax + 256 * 8 * 8 * 4;  // ring + x (K <= 16384)
+constexpr int kMaxTmaSmem = kRingBytes + 256 * 8 * 8 * 4;  // ring + x (K <= 16384)
 
 template <int PRO, int EPI>
 cudaError_t set_tma_attr() {
@@ -511,7 +516,8 @@ template <int PRO, int EPI>
 cudaError_t launch_tma(const GemvArgs& a, cudaStream_t s, bool pdl, int num_sms, int chunks,
                        int ksplit) {
   const int grid = tma_grid(a, GemvEpi(EPI), ksplit, num_sms);
-  return launch_k(gemv_tma_kernel<PRO, EPI>, dim3(grid), dim3(kTmaThreads), tma_smem(a, ksplit),
+  return launch_k(gemv_tma_kernel<PRO, EPI>, dim3(grid), dim3(kTmaThreads),
+                  tma_smem(a, ksplit, GemvPro(PRO)),
                   s, pdl, a, chunks, ksplit);
 }
 
