@@ -298,6 +298,22 @@ def run_ours(args, rank, world, local_rank):
     cache_trunc(cache, PROMPT)
     dec_toks = model.decode([t0_tok], cache, GEN)[0]
 
+    if args.trace:
+        # device timeline of one captured step (globaltimer stamps), in us
+        # from the step's first kernel start
+        cache_trunc(cache, PROMPT)
+        tl = model.trace_decode([t0_tok], cache)
+        base = min(r[1] for r in tl)
+        with open(args.trace, "w") as f:
+            f.write("kernel            start   wait0   wait1     end     dur  gap_from_prev_end\n")
+            prev_end = base
+            for r in tl:
+                s, w0, w1, e = [(v - base) / 1e3 for v in r[1:]]
+                f.write(f"{r[0]:14s} {s:7.2f} {w0:7.2f} {w1:7.2f} {e:7.2f} {e - w0:7.2f} "
+                        f"{w0 - (prev_end - base) / 1e3:7.2f}\n")
+                prev_end = r[4]
+            f.write(f"step total {(max(r[4] for r in tl) - base) / 1e3:.2f} us\n")
+
     # --- per-kernel profile pass (dominant kernel's roofline) ---
     cache_trunc(cache, PROMPT)
     prof = model.profile_decode([t0_tok], cache, 16)
@@ -388,6 +404,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-steps", type=int, default=0,
                     help="profiling mode: prefill + this many decode steps, no timing, no output")
+    ap.add_argument("--trace", default="",
+                    help="write the device timeline of one decode step to this file")
     ap.add_argument("--ncu-layers", type=int, default=0,
                     help="profiling mode only: build the c2 shape with this many layers")
     args = ap.parse_args()

@@ -200,6 +200,14 @@ void* tmg_stream(tmg_ctx* ctx);
  * 4 down GEMV, 5 LM head. */
 int tmg_profile_decode(tmg_ctx* ctx, tmg_kv* kv, const uint32_t* tokens, int64_t n_steps,
                        double* ms, int64_t* launches);
+/* Profiling aid: the device timeline of one captured greedy step (the real
+ * graph, with its launch overlap), from %globaltimer stamps.  For each
+ * kernel i of the step (n_slots of them, at most max_slots): out[4i..4i+3] =
+ * first CTA start, first CTA past griddepcontrol.wait, last CTA past it, last
+ * CTA end (ns); kinds[i] = 0 qkv GEMV, 1 attention, 2 o GEMV, 3 gate/up
+ * GEMV, 4 down GEMV, 5 LM head.  Appends two positions per stream. */
+int tmg_trace_decode(tmg_ctx* ctx, tmg_kv* kv, const uint32_t* tokens, uint64_t* out,
+                     int32_t* kinds, int32_t max_slots, int32_t* n_slots);
 
 /* ---------------------------------------------------------------------------
  * Tensor parallel (8B-class config, 2/4/8 GPUs of one node).  Call before

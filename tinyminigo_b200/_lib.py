@@ -97,6 +97,7 @@ SIGNATURES = {
     "tmg_sync": (_I, [_P]),
     "tmg_stream": (_P, [_P]),
     "tmg_profile_decode": (_I, [_P, _P, _P, _I64, _P, _P]),
+    "tmg_trace_decode": (_I, [_P, _P, _P, _P, _P, _I32, ctypes.POINTER(_I32)]),
     "tmg_tp_unique_id": (_I, [_P]),
     "tmg_tp_init": (_I, [_P, _P, _I32, _I32]),
     "tmg_op_gemv_bf16": (_I, [_P, _P, _P, _I64, _I64, _I32, _P]),

@@ -484,8 +484,27 @@ struct Prof {
 };
 
 // One forward_token for the M streams of kv (model.rs:392-491).
+// Trace slots of one captured forward (tmg_trace_decode): kernel i of the
+// forward writes its timeline into slot i; kinds[i] = its class.
+struct TraceCtx {
+  unsigned long long* buf = nullptr;
+  int next = 0;
+  std::vector<int> kinds;
+  Trace take(int kind) {
+    Trace t;
+    if (buf) {
+      t.buf = buf;
+      t.slot = next++;
+      kinds.push_back(kind);
+    }
+    return t;
+  }
+};
+
 cudaError_t enqueue_forward(tmg_ctx* c, tmg_kv* kv, const StreamState& st, bool argmax,
-                            Prof* prof = nullptr) {
+                            Prof* prof = nullptr, TraceCtx* trc = nullptr) {
+  TraceCtx none;
+  TraceCtx& tc = trc ? *trc : none;
   const int M = kv->M;
   const bool pdl = prof == nullptr;
   auto B = [&]() {
@@ -508,6 +527,7 @@ cudaError_t enqueue_forward(tmg_ctx* c, tmg_kv* kv, const StreamState& st, bool 
     A.norm_w = Lw.in_norm;
     A.eps = eps;
     A.norm_mode = 0;
+    A.trace = tc.take(0);
     if (l == 0) {
       A.embed = c->embed;
       A.tokens = st.token;
@@ -539,6 +559,7 @@ cudaError_t enqueue_forward(tmg_ctx* c, tmg_kv* kv, const StreamState& st, bool 
     T.nsplit = kv->nsplit;
     T.M = M;
     T.scale = 1.0f / sqrtf(float(c->d));
+    T.trace = tc.take(1);
     B();
     TMG_CUDA_TRY(launch_attn_decode(T, c->stream, pdl));
     E(1);
@@ -550,6 +571,7 @@ cudaError_t enqueue_forward(tmg_ctx* c, tmg_kv* kv, const StreamState& st, bool 
     O.x = c->attn;
     O.y = tp ? c->partial : c->x;
     O.ldy = c->h;
+    O.trace = tc.take(2);
     B();
     TMG_CUDA_TRY(gemv(c, O, PRO_NONE, tp ? EPI_STORE : EPI_ADD, pdl));
     E(2);
@@ -565,6 +587,7 @@ cudaError_t enqueue_forward(tmg_ctx* c, tmg_kv* kv, const StreamState& st, bool 
     GU.eps = eps;
     GU.y = c->act;
     GU.ldy = c->I;
+    GU.trace = tc.take(3);
     B();
     TMG_CUDA_TRY(gemv(c, GU, PRO_NORM, EPI_SWIGLU, pdl));
     E(3);
@@ -576,6 +599,7 @@ cudaError_t enqueue_forward(tmg_ctx* c, tmg_kv* kv, const StreamState& st, bool 
     D.x = c->act;
     D.y = tp ? c->partial : c->x;
     D.ldy = c->h;
+    D.trace = tc.take(4);
     B();
     TMG_CUDA_TRY(gemv(c, D, PRO_NONE, tp ? EPI_STORE : EPI_ADD, pdl));
     E(4);
@@ -595,6 +619,7 @@ cudaError_t enqueue_forward(tmg_ctx* c, tmg_kv* kv, const StreamState& st, bool 
   H.am_part = c->am_part;
   H.ticket = &c->tickets[0];
   H.st = st;
+  H.trace = tc.take(5);
   if (!tp) {
     B();
     cudaError_t e = gemv(c, H, PRO_NORM, argmax ? EPI_HEAD_ARGMAX : EPI_HEAD, pdl);
@@ -1373,6 +1398,52 @@ int tmg_profile_decode(tmg_ctx* c, tmg_kv* kv, const uint32_t* tokens, int64_t n
   }
   for (int m = 0; m < kv->M; ++m) kv->lens[m] += n_steps;
   return TMG_OK;
+}
+
+int tmg_trace_decode(tmg_ctx* c, tmg_kv* kv, const uint32_t* tokens, uint64_t* out,
+                     int32_t* kinds, int32_t max_slots, int32_t* n_slots) {
+  if (!c || !kv || kv->ctx != c || !tokens || !out || !kinds || !n_slots)
+    return fail(c, TMG_ERR_INVALID, "bad argument");
+  cudaSetDevice(c->device);
+  StreamState st;
+  int rc = prepare_decode(c, kv, tokens, 2, &st);
+  if (rc) return rc;
+  const int cap = 4096;
+  unsigned long long* buf = nullptr;
+  CK(cudaMalloc(&buf, size_t(cap) * 4 * 8), "trace");
+  std::vector<unsigned long long> init(size_t(cap) * 4);
+  for (int i = 0; i < cap; ++i) {
+    init[size_t(i) * 4 + 0] = init[size_t(i) * 4 + 1] = ~0ull;
+    init[size_t(i) * 4 + 2] = init[size_t(i) * 4 + 3] = 0ull;
+  }
+  TraceCtx tc;
+  tc.buf = buf;
+  cudaGraph_t g = nullptr;
+  cudaGraphExec_t ex = nullptr;
+  cudaError_t e = cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal);
+  if (e == cudaSuccess) {
+    cudaError_t ce = enqueue_forward(c, kv, st, true, nullptr, &tc);
+    e = cudaStreamEndCapture(c->stream, &g);
+    if (ce != cudaSuccess) e = ce;
+  }
+  if (e == cudaSuccess) e = cudaGraphInstantiate(&ex, g, 0);
+  // one untraced-warm replay, then the traced one
+  for (int rep = 0; rep < 2 && e == cudaSuccess; ++rep) {
+    e = cudaMemcpyAsync(buf, init.data(), init.size() * 8, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = cudaGraphLaunch(ex, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+  }
+  const int n = std::min<int>(tc.next, std::min<int>(cap, max_slots));
+  if (e == cudaSuccess)
+    e = cudaMemcpy(out, buf, size_t(n) * 4 * 8, cudaMemcpyDeviceToHost);
+  if (ex) cudaGraphExecDestroy(ex);
+  if (g) cudaGraphDestroy(g);
+  cudaFree(buf);
+  if (e != cudaSuccess) return cuda_fail(c, e, "trace");
+  for (int i = 0; i < n; ++i) kinds[i] = tc.kinds[i];
+  *n_slots = n;
+  for (int m = 0; m < kv->M; ++m) kv->lens[m] += 2;
+  return sync_check(c, "trace");
 }
 
 int tmg_tp_unique_id(uint8_t id[128]) { return tp_unique_id(id) == 0 ? TMG_OK : TMG_ERR_NCCL; }

@@ -51,8 +51,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
   float* vs = ks_ + kTile * (d + 4);   // [kTile][d]
   float* ps = vs + kTile * d;          // [G][kTile]
 
+  if (tid == 0) trace_mark(a.trace, 0);
   pdl_trigger();
   pdl_wait();
+  if (tid == 0) {
+    trace_mark(a.trace, 1);
+    trace_mark(a.trace, 2);
+  }
 
   const bool fixed = a.pos_override != nullptr;
   const int pos = fixed ? a.pos_override[m] : a.st.pos[m];
@@ -70,7 +75,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
   const int n_used = (n_ctx + chunk - 1) / chunk;
   const int c0 = split * chunk;
   const int c1 = min(n_ctx, c0 + chunk);
-  if (n_used == 1 && split > 0) return;  // one-split launches need no ticket
+  if (n_used == 1 && split > 0) {  // one-split launches need no ticket
+    if (tid == 0) trace_mark(a.trace, 3);
+    return;
+  }
   const bool own_pos = append && pos >= c0 && pos < c1;
   const int d4 = d / 4;
 
@@ -218,6 +226,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
         }
       }
     }
+    if (tid == 0) trace_mark(a.trace, 3);
     return;  // one-split launches need no ticket
   }
   // partial (m, l, o[d]) per head
@@ -240,7 +249,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
     last_s = (t == gridDim.y - 1);
   }
   __syncthreads();
-  if (!last_s) return;
+  if (!last_s) {
+    if (tid == 0) trace_mark(a.trace, 3);
+    return;
+  }
   __threadfence();
   // combine: the per-split weights w = exp(m_s - max) once per (split, head)
   // in shared memory, then every output sums its column over the splits
@@ -279,7 +291,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
     const float L = l_s[g];
     out[idx] = L > 0.f ? acc / L : 0.f;
   }
-  if (tid == 0) a.ticket[m * a.nkv + kvh] = 0u;
+  if (tid == 0) {
+    a.ticket[m * a.nkv + kvh] = 0u;
+    trace_mark(a.trace, 3);
+  }
 }
 
 // ---------------------------------------------------------------------------

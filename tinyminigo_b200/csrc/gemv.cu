@@ -164,6 +164,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
     }
     abort_s[0] = abort_s[1] = 0;
     mbar_fence_init();
+    trace_mark(a.trace, 0);
   }
   __syncthreads();
   pdl_trigger();
@@ -193,6 +194,10 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
   } else {
     // ---- consumers ----
     pdl_wait();
+    if (threadIdx.x == 0) {
+      trace_mark(a.trace, 1);
+      trace_mark(a.trace, 2);
+    }
     const int ks = warp % ksplit, slot = warp / ksplit;
     const int kbase = ks * chunks * 256;
     // with a norm: stage x (embedding row or activations) in shared memory,
@@ -324,6 +329,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
   }
   if (EPI == EPI_HEAD || EPI == EPI_HEAD_ARGMAX)
     head_finish<EPI == EPI_HEAD_ARGMAX>(a, 1, best_s, &last_s);
+  if (threadIdx.x == 0) trace_mark(a.trace, 3);
 }
 
 // ---------------------------------------------------------------------------

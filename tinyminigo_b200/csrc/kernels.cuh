@@ -23,6 +23,22 @@ struct StreamState {
   uint32_t eos[kMaxEos];
 };
 
+// Optional device timeline of one forward (tmg_trace_decode): per launch
+// slot, [0] first CTA start, [1] first CTA past griddepcontrol.wait,
+// [2] last CTA past the wait, [3] last CTA end (globaltimer ns).
+struct Trace {
+  unsigned long long* buf = nullptr;
+  int slot = 0;
+};
+__device__ __forceinline__ void trace_mark(const Trace& t, int what) {
+  if (t.buf == nullptr) return;
+  unsigned long long now;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(now));
+  unsigned long long* p = t.buf + t.slot * 4 + what;
+  if (what == 0 || what == 1) atomicMin(p, now);
+  else atomicMax(p, now);
+}
+
 // Record a chosen token for stream m (the body of generate's loop after
 // sampling, src/model.rs:648-653): push it, stop on EOS.  After max_tokens
 // tokens the next call only marks the stream done (the reference's final,
@@ -77,6 +93,7 @@ struct GemvArgs {
   unsigned int* ticket = nullptr;
   StreamState st{};
   int32_t* err = nullptr;  // device error word (2 = a bounded wait gave up)
+  Trace trace{};
 };
 
 cudaError_t launch_gemv(const GemvArgs& a, GemvPro pro, GemvEpi epi, cudaStream_t s, bool pdl,
@@ -111,6 +128,7 @@ struct AttnDecodeArgs {
   const int32_t* pos_override = nullptr;  // op-level: fixed n_ctx - 1 (no append)
   int nq = 0, nkv = 0, d = 0, nsplit = 1, M = 1;
   float scale = 1.f;
+  Trace trace{};
 };
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);
 int attn_decode_nsplit(int nkv, int M, int64_t cap, int num_sms);

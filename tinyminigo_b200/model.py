@@ -274,6 +274,19 @@ class Model:
         names = ["qkv_gemv", "attn_decode", "o_gemv", "gateup_gemv", "down_gemv", "lm_head"]
         return {k: (float(ms[i]), int(n[i])) for i, k in enumerate(names)}
 
+    def trace_decode(self, tokens, cache: "KvCache") -> list:
+        """Device timeline of one captured greedy step: per kernel (kind,
+        first start, first past wait, last past wait, last end) in ns."""
+        t = np.ascontiguousarray(np.atleast_1d(np.asarray(tokens, np.uint32)))
+        cap = 1024
+        out = np.zeros((cap, 4), np.uint64)
+        kinds = np.zeros(cap, np.int32)
+        n = ctypes.c_int32(0)
+        check(lib().tmg_trace_decode(self._h, cache._h, _ptr(t), _ptr(out), _ptr(kinds), cap,
+                                     ctypes.byref(n)), self._h, "trace_decode")
+        names = ["qkv_gemv", "attn_decode", "o_gemv", "gateup_gemv", "down_gemv", "lm_head"]
+        return [(names[kinds[i]], *[int(v) for v in out[i]]) for i in range(n.value)]
+
 
 class KvCache:
     """KvCache (src/model.rs:250-332) on the device: per layer and stream an
