@@ -24,6 +24,7 @@
 #include "kernels.cuh"
 #include "loader.h"
 #include "tp.h"
+#include "fused.cuh"
 
 using namespace tmg;
 
@@ -75,6 +76,8 @@ struct tmg_ctx {
   unsigned int* tickets = nullptr;  // [0]: head, [1..16]: sampler
   int32_t* d_err = nullptr;
   float* logits_full = nullptr;  // [M, V] gathered logits under TP
+  unsigned int* bar = nullptr;   // grid barrier of the fused decode kernel
+  bool fused_ok = false;         // the fused batch-1 decode kernel takes this shape
   // prefill scratch
   int64_t pf_cap = 0;
   float *X = nullptr, *Xn = nullptr, *QKV = nullptr, *ATT = nullptr, *G = nullptr, *U = nullptr;
@@ -112,6 +115,7 @@ struct tmg_kv {
   cudaGraphExec_t g_dec = nullptr;  // forward + argmax with gen_cap = dec_cap
   int64_t dec_cap = 0;
   int32_t* h_state = nullptr;  // pinned staging of the state block
+  FusedLayer* d_layers = nullptr;  // per-layer pointers for the fused kernel (stream 0)
   cudaEvent_t state_ev = nullptr;  // the last upload from h_state
   std::vector<void*> allocs;
 };
@@ -186,6 +190,8 @@ int sync_check(tmg_ctx* c, const char* where) {
   if (e != cudaSuccess) return cuda_fail(c, e, where);
   if (w) {
     e = zero_sync(c, c->d_err, 4);
+    // a fused launch that gave up may have left its grid barrier mid-way
+    if (e == cudaSuccess && c->bar) e = zero_sync(c, c->bar, 16);
     if (e != cudaSuccess) return cuda_fail(c, e, where);
     return err_status(c, w);
   }
@@ -376,6 +382,9 @@ int alloc_model(tmg_ctx* c) {
   CK(dalloc(c->allocs, &c->sm_part, size_t(M) * 64 * kMaxTopK), "alloc scratch");
   CK(dalloc(c->allocs, &c->tickets, 64), "alloc scratch");
   CK(zero_sync(c, c->tickets, 64 * sizeof(unsigned int)), "memset");
+  CK(dalloc(c->allocs, &c->bar, 4), "alloc scratch");
+  CK(zero_sync(c, c->bar, 16), "memset");
+  c->fused_ok = c->world == 1 && fused_supported(c->h, c->nq * c->d, c->I, c->d, c->nq / c->nkv);
   c->has_model = true;
   return TMG_OK;
 }
@@ -749,6 +758,43 @@ int check_sampling(tmg_ctx* c, const tmg_gen_params* p) {
   return TMG_OK;
 }
 
+// n_steps greedy steps (forward + argmax + generate's bookkeeping) of the
+// single stream of kv in one persistent launch (decode_fused.cu).
+cudaError_t launch_fused(tmg_ctx* c, tmg_kv* kv, const StreamState& st, int64_t n_steps) {
+  FusedArgs f;
+  f.layers = kv->d_layers;
+  f.L = c->L;
+  f.h = c->h;
+  f.nq = c->nq;
+  f.nkv = c->nkv;
+  f.d = c->d;
+  f.I = c->I;
+  f.V = int(c->V_l);
+  f.eps = c->cfg.rms_norm_eps;
+  f.scale = 1.0f / sqrtf(float(c->d));
+  f.embed = c->embed;
+  f.lm_head = c->lm_head;
+  f.final_norm = c->final_norm;
+  f.rope_cos = kv->rope_cos;
+  f.rope_sin = kv->rope_sin;
+  f.cap = kv->cap;
+  f.x = c->x;
+  f.qkv = c->qkv;
+  f.part = kv->part;
+  f.act = c->act;
+  f.logits = c->logits;
+  f.am_part = c->am_part;
+  f.bar = c->bar;
+  f.nsplit = kv->nsplit;
+  f.xs_floats = std::max(c->h, c->nq * c->d);
+  f.st = st;
+  f.n_steps = int(n_steps);
+  f.err = c->d_err;
+  return launch_decode_fused(f, c->num_sms, c->stream);
+}
+
+bool use_fused(tmg_ctx* c, tmg_kv* kv) { return c->fused_ok && kv->M == 1 && kv->d_layers; }
+
 // The generate loop for all streams of kv (model.rs:614-663).
 int run_generate(tmg_ctx* c, tmg_kv* kv, const uint32_t* prompts, int64_t T,
                  const tmg_gen_params* params, const float* uniforms, uint32_t* tokens_out,
@@ -837,24 +883,28 @@ int run_generate(tmg_ctx* c, tmg_kv* kv, const uint32_t* prompts, int64_t T,
   } else {
     CK(launch_sample(S, c->stream, false, c->num_sms), "sample");
   }
-  // the per-step graph: forward (+ argmax) [+ sampler]
-  cudaGraph_t graph = nullptr;
+  // the per-step work: the fused persistent kernel (greedy, one stream), or
+  // a graph of forward (+ argmax) [+ sampler]
+  const bool fused = greedy_fused && use_fused(c, kv);
   cudaGraphExec_t exec = nullptr;
-  CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "capture");
-  cudaError_t ce = enqueue_forward(c, kv, st, greedy_fused);
-  if (ce == cudaSuccess && !greedy_fused) ce = launch_sample(S, c->stream, true, c->num_sms);
-  cudaError_t ee = cudaStreamEndCapture(c->stream, &graph);
-  if (ce != cudaSuccess) {
-    if (graph) cudaGraphDestroy(graph);
-    return cuda_fail(c, ce, "capture step");
+  if (!fused) {
+    cudaGraph_t graph = nullptr;
+    CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "capture");
+    cudaError_t ce = enqueue_forward(c, kv, st, greedy_fused);
+    if (ce == cudaSuccess && !greedy_fused) ce = launch_sample(S, c->stream, true, c->num_sms);
+    cudaError_t ee = cudaStreamEndCapture(c->stream, &graph);
+    if (ce != cudaSuccess) {
+      if (graph) cudaGraphDestroy(graph);
+      return cuda_fail(c, ce, "capture step");
+    }
+    CK(ee, "capture");
+    ce = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    CK(ce, "instantiate");
   }
-  CK(ee, "capture");
-  ce = cudaGraphInstantiate(&exec, graph, 0);
-  cudaGraphDestroy(graph);
-  CK(ce, "instantiate");
 
   // launch max_tokens steps in chunks; read back tokens a chunk behind
-  const int64_t chunk = 8;
+  const int64_t chunk = fused ? 32 : 8;
   std::vector<int32_t> h_state(4 * kMaxStreams);
   std::vector<uint32_t> h_gen(size_t(M) * maxt);
   int64_t launched = 0;
@@ -884,11 +934,15 @@ int run_generate(tmg_ctx* c, tmg_kv* kv, const uint32_t* prompts, int64_t T,
     if (all_done) stop = true;
     return TMG_OK;
   };
+  int n_chunks = 0;
   while (launched < maxt && !stop) {
     const int64_t n = std::min<int64_t>(chunk, maxt - launched);
-    for (int64_t i = 0; i < n; ++i) CK(cudaGraphLaunch(exec, c->stream), "graph launch");
+    if (fused)
+      CK(launch_fused(c, kv, st, n), "fused decode");
+    else
+      for (int64_t i = 0; i < n; ++i) CK(cudaGraphLaunch(exec, c->stream), "graph launch");
     launched += n;
-    const int slot = int((launched / chunk) & 1);
+    const int slot = (n_chunks++) & 1;
     CK(cudaMemcpyAsync(pinned_state + slot * 4 * kMaxStreams, kv->d_state,
                        sizeof(int32_t) * 4 * kMaxStreams, cudaMemcpyDeviceToHost, c->stream),
        "state");
@@ -903,7 +957,7 @@ int run_generate(tmg_ctx* c, tmg_kv* kv, const uint32_t* prompts, int64_t T,
   CK(cudaStreamSynchronize(c->stream), "generate");
   cudaEventDestroy(ev[0]);
   cudaEventDestroy(ev[1]);
-  cudaGraphExecDestroy(exec);
+  if (exec) cudaGraphExecDestroy(exec);
   int32_t err_word = 0;
   CK(copy_sync(c, &err_word, c->d_err, 4, cudaMemcpyDeviceToHost), "err");
   CK(copy_sync(c, h_state.data(), kv->d_state, h_state.size() * 4, cudaMemcpyDeviceToHost),
@@ -1013,6 +1067,7 @@ int tmg_create(int device, const tmg_config* cfg, tmg_ctx** out) {
       cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
       gemv_prepare() != cudaSuccess || attn_prepare() != cudaSuccess ||
       gemm_tc_prepare() != cudaSuccess || prefill_prepare() != cudaSuccess ||
+      fused_prepare() != cudaSuccess ||
       sample_prepare() != cudaSuccess || dalloc(c->allocs, &c->d_err, 4) != cudaSuccess ||
       zero_sync(c, c->d_err, 16) != cudaSuccess) {
     free_all(c->allocs);
@@ -1128,6 +1183,18 @@ int tmg_kv_create(tmg_ctx* c, int32_t n_streams, int64_t capacity, tmg_kv** out)
   kv->st.gen_cap = 0;
   kv->st.n_eos = 0;
   kv->nsplit = attn_decode_nsplit(c->nkv, n_streams, capacity, c->num_sms);
+  if (c->fused_ok && n_streams == 1) {
+    std::vector<FusedLayer> fl(c->L);
+    for (int l = 0; l < c->L; ++l) {
+      const Layer& Lw = c->layers[l];
+      fl[l] = FusedLayer{Lw.wqkv, Lw.wo, Lw.wg, Lw.wu, Lw.wd, Lw.in_norm, Lw.post_norm, kv->k[l],
+                         kv->v[l]};
+    }
+    if ((e = dalloc(kv->allocs, &kv->d_layers, size_t(c->L))) != cudaSuccess) return bail(e);
+    if ((e = copy_sync(c, kv->d_layers, fl.data(), fl.size() * sizeof(FusedLayer),
+                       cudaMemcpyHostToDevice)) != cudaSuccess)
+      return bail(e);
+  }
   const int G = c->nq / c->nkv;
   if ((e = dalloc(kv->allocs, &kv->part, size_t(n_streams) * c->nkv * kv->nsplit * G * (c->d + 2))) != cudaSuccess) return bail(e);
   if ((e = dalloc(kv->allocs, &kv->att_ticket, size_t(n_streams) * c->nkv)) != cudaSuccess) return bail(e);
@@ -1331,7 +1398,7 @@ int tmg_decode(tmg_ctx* c, tmg_kv* kv, const uint32_t* tokens, int64_t n_steps, 
   StreamState st;
   int rc = prepare_decode(c, kv, tokens, n_steps, &st);
   if (rc) return rc;
-  if (!kv->g_dec || kv->dec_cap != n_steps) {
+  if (!use_fused(c, kv) && (!kv->g_dec || kv->dec_cap != n_steps)) {
     if (kv->g_dec) cudaGraphExecDestroy(kv->g_dec);
     kv->g_dec = nullptr;
     cudaGraph_t g = nullptr;
@@ -1348,7 +1415,11 @@ int tmg_decode(tmg_ctx* c, tmg_kv* kv, const uint32_t* tokens, int64_t n_steps, 
     CK(ce, "instantiate");
     kv->dec_cap = n_steps;
   }
-  for (int64_t i = 0; i < n_steps; ++i) CK(cudaGraphLaunch(kv->g_dec, c->stream), "decode");
+  if (use_fused(c, kv)) {
+    CK(launch_fused(c, kv, st, n_steps), "fused decode");
+  } else {
+    for (int64_t i = 0; i < n_steps; ++i) CK(cudaGraphLaunch(kv->g_dec, c->stream), "decode");
+  }
   for (int m = 0; m < kv->M; ++m) kv->lens[m] += n_steps;
   if (out) {
     CK(cudaMemcpyAsync(out, kv->d_gen, size_t(kv->M) * n_steps * 4, cudaMemcpyDeviceToHost,
