@@ -104,6 +104,8 @@ const char* tmg_version(void);
  * context for the tmg_op_* calls). */
 int tmg_create(int device, const tmg_config* cfg, tmg_ctx** out);
 int tmg_destroy(tmg_ctx* ctx);
+/* The message of the last failure on ctx; with ctx NULL, why the last
+ * tmg_create on the calling thread failed. */
 const char* tmg_last_error(const tmg_ctx* ctx);
 
 /* Upload every tensor of a safetensors file (load_model_safetensors,
@@ -208,6 +210,18 @@ int tmg_profile_decode(tmg_ctx* ctx, tmg_kv* kv, const uint32_t* tokens, int64_t
  * GEMV, 4 down GEMV, 5 LM head.  Appends two positions per stream. */
 int tmg_trace_decode(tmg_ctx* ctx, tmg_kv* kv, const uint32_t* tokens, uint64_t* out,
                      int32_t* kinds, int32_t max_slots, int32_t* n_slots);
+/* Profiling aid for the fused single-stream decode kernel: one greedy step
+ * with %globaltimer stamps.  out receives n_ctas * (5 L + 1) records of 12
+ * per CTA and phase (per layer: qkv, attention, o, gate/up, down; then the
+ * LM head): the times (ns) its work ended, it passed the grid barrier, its
+ * weight stream issued the phase's first and last copies, its input was
+ * ready, its GEMV loop ended and its first stage was ready; its group count
+ * (attention: tile loaded, partial written, merge done, merged or not);
+ * then SM cycles: consumer warp 0 waiting for stages, consumer warp 0
+ * computing, the producer waiting for free stages, the producer issuing.
+ * max_u64 is the room in out; *n_ctas is set.  Appends one position. */
+int tmg_trace_fused(tmg_ctx* ctx, tmg_kv* kv, uint32_t token, uint64_t* out, int64_t max_u64,
+                    int32_t* n_ctas);
 
 /* ---------------------------------------------------------------------------
  * Tensor parallel (8B-class config, 2/4/8 GPUs of one node).  Call before

@@ -98,6 +98,7 @@ SIGNATURES = {
     "tmg_stream": (_P, [_P]),
     "tmg_profile_decode": (_I, [_P, _P, _P, _I64, _P, _P]),
     "tmg_trace_decode": (_I, [_P, _P, _P, _P, _P, _I32, ctypes.POINTER(_I32)]),
+    "tmg_trace_fused": (_I, [_P, _P, ctypes.c_uint32, _P, ctypes.c_int64, ctypes.POINTER(_I32)]),
     "tmg_tp_unique_id": (_I, [_P]),
     "tmg_tp_init": (_I, [_P, _P, _I32, _I32]),
     "tmg_op_gemv_bf16": (_I, [_P, _P, _P, _I64, _I64, _I32, _P]),
@@ -133,7 +134,7 @@ def lib() -> ctypes.CDLL:
 def check(rc: int, ctx=None, what: str = "") -> None:
     if rc != TMG_OK:
         msg = ""
-        if ctx is not None:
-            m = lib().tmg_last_error(ctx)
-            msg = m.decode() if m else ""
+        # a null context reads why the last tmg_create on this thread failed
+        m = lib().tmg_last_error(ctx)
+        msg = m.decode() if m else ""
         raise TmgError(rc, f"{what}: {msg}" if what else msg)

@@ -15,6 +15,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -77,6 +78,8 @@ struct tmg_ctx {
   int32_t* d_err = nullptr;
   float* logits_full = nullptr;  // [M, V] gathered logits under TP
   unsigned int* bar = nullptr;   // grid barrier of the fused decode kernel
+  int fused_pf = 0;              // its L2 prefetch distance (stages; TMG_FUSED_PF)
+  int fused_stages = 0;          // its ring depth cap (0: all that fit; TMG_FUSED_STAGES)
   bool fused_ok = false;         // the fused batch-1 decode kernel takes this shape
   // prefill scratch
   int64_t pf_cap = 0;
@@ -123,6 +126,9 @@ struct tmg_kv {
 namespace {
 
 constexpr int64_t kPrefillChunk = 4096;
+
+// Why the last tmg_create on this thread failed (there is no context to hold it).
+thread_local std::string g_create_err;
 
 int fail(tmg_ctx* c, int code, const std::string& m) {
   if (c) c->err = m;
@@ -191,7 +197,7 @@ int sync_check(tmg_ctx* c, const char* where) {
   if (w) {
     e = zero_sync(c, c->d_err, 4);
     // a fused launch that gave up may have left its grid barrier mid-way
-    if (e == cudaSuccess && c->bar) e = zero_sync(c, c->bar, 16);
+    if (e == cudaSuccess && c->bar) e = zero_sync(c, c->bar, fused_bar_words() * sizeof(unsigned int));
     if (e != cudaSuccess) return cuda_fail(c, e, where);
     return err_status(c, w);
   }
@@ -382,9 +388,11 @@ int alloc_model(tmg_ctx* c) {
   CK(dalloc(c->allocs, &c->sm_part, size_t(M) * 64 * kMaxTopK), "alloc scratch");
   CK(dalloc(c->allocs, &c->tickets, 64), "alloc scratch");
   CK(zero_sync(c, c->tickets, 64 * sizeof(unsigned int)), "memset");
-  CK(dalloc(c->allocs, &c->bar, 4), "alloc scratch");
-  CK(zero_sync(c, c->bar, 16), "memset");
-  c->fused_ok = c->world == 1 && fused_supported(c->h, c->nq * c->d, c->I, c->d, c->nq / c->nkv);
+  CK(dalloc(c->allocs, &c->bar, fused_bar_words()), "alloc scratch");
+  CK(zero_sync(c, c->bar, fused_bar_words() * sizeof(unsigned int)), "memset");
+  c->fused_ok = c->world == 1 && fused_supported(c->h, c->nq, c->nkv, c->d, c->I, c->V_l, c->num_sms);
+  if (const char* pf = getenv("TMG_FUSED_PF")) c->fused_pf = atoi(pf);
+  if (const char* ns = getenv("TMG_FUSED_STAGES")) c->fused_stages = atoi(ns);
   c->has_model = true;
   return TMG_OK;
 }
@@ -760,7 +768,8 @@ int check_sampling(tmg_ctx* c, const tmg_gen_params* p) {
 
 // n_steps greedy steps (forward + argmax + generate's bookkeeping) of the
 // single stream of kv in one persistent launch (decode_fused.cu).
-cudaError_t launch_fused(tmg_ctx* c, tmg_kv* kv, const StreamState& st, int64_t n_steps) {
+cudaError_t launch_fused(tmg_ctx* c, tmg_kv* kv, const StreamState& st, int64_t n_steps,
+                         unsigned long long* trace = nullptr) {
   FusedArgs f;
   f.layers = kv->d_layers;
   f.L = c->L;
@@ -781,15 +790,18 @@ cudaError_t launch_fused(tmg_ctx* c, tmg_kv* kv, const StreamState& st, int64_t 
   f.x = c->x;
   f.qkv = c->qkv;
   f.part = kv->part;
+  f.att = c->attn;
   f.act = c->act;
   f.logits = c->logits;
   f.am_part = c->am_part;
   f.bar = c->bar;
   f.nsplit = kv->nsplit;
-  f.xs_floats = std::max(c->h, c->nq * c->d);
+  f.pf_ahead = c->fused_pf;
+  f.max_stages = c->fused_stages;
   f.st = st;
   f.n_steps = int(n_steps);
   f.err = c->d_err;
+  f.trace = trace;
   return launch_decode_fused(f, c->num_sms, c->stream);
 }
 
@@ -1059,17 +1071,28 @@ int tmg_create(int device, const tmg_config* cfg, tmg_ctx** out) {
   *out = nullptr;
   int n = 0;
   cudaError_t e = cudaGetDeviceCount(&n);
-  if (e != cudaSuccess || n <= device || device < 0) return TMG_ERR_CUDA;
+  if (e != cudaSuccess || n <= device || device < 0) {
+    g_create_err = e != cudaSuccess ? std::string("tmg_create: ") + cudaGetErrorString(e)
+                                    : std::string("tmg_create: no such device");
+    return TMG_ERR_CUDA;
+  }
   tmg_ctx* c = new tmg_ctx();
   c->device = device;
-  if (cudaSetDevice(device) != cudaSuccess ||
-      cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
-      cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
-      gemv_prepare() != cudaSuccess || attn_prepare() != cudaSuccess ||
-      gemm_tc_prepare() != cudaSuccess || prefill_prepare() != cudaSuccess ||
-      fused_prepare() != cudaSuccess ||
-      sample_prepare() != cudaSuccess || dalloc(c->allocs, &c->d_err, 4) != cudaSuccess ||
-      zero_sync(c, c->d_err, 16) != cudaSuccess) {
+  const char* step = nullptr;
+  cudaError_t ce = cudaSuccess;
+  auto run = [&](const char* name, cudaError_t r) {
+    if (!step && r != cudaSuccess) { step = name; ce = r; }
+    return !step;
+  };
+  run("cudaSetDevice", cudaSetDevice(device)) &&
+      run("stream", cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking)) &&
+      run("sm count", cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device)) &&
+      run("gemv_prepare", gemv_prepare()) && run("attn_prepare", attn_prepare()) &&
+      run("gemm_tc_prepare", gemm_tc_prepare()) && run("prefill_prepare", prefill_prepare()) &&
+      run("fused_prepare", fused_prepare()) && run("sample_prepare", sample_prepare()) &&
+      run("error word", dalloc(c->allocs, &c->d_err, 4)) && run("error word", zero_sync(c, c->d_err, 16));
+  if (step) {
+    g_create_err = std::string("tmg_create: ") + step + ": " + cudaGetErrorString(ce);
     free_all(c->allocs);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
@@ -1099,7 +1122,7 @@ int tmg_destroy(tmg_ctx* c) {
   return TMG_OK;
 }
 
-const char* tmg_last_error(const tmg_ctx* c) { return c ? c->err.c_str() : "null context"; }
+const char* tmg_last_error(const tmg_ctx* c) { return c ? c->err.c_str() : g_create_err.c_str(); }
 
 static int ensure_alloc(tmg_ctx* c) {
   if (!c->has_model) return fail(c, TMG_ERR_INVALID, "context has no model config");
@@ -1514,6 +1537,29 @@ int tmg_trace_decode(tmg_ctx* c, tmg_kv* kv, const uint32_t* tokens, uint64_t* o
   for (int i = 0; i < n; ++i) kinds[i] = tc.kinds[i];
   *n_slots = n;
   for (int m = 0; m < kv->M; ++m) kv->lens[m] += 2;
+  return sync_check(c, "trace");
+}
+
+int tmg_trace_fused(tmg_ctx* c, tmg_kv* kv, uint32_t token, uint64_t* out, int64_t max_u64,
+                    int32_t* n_ctas) {
+  if (!c || !kv || kv->ctx != c || !out || !n_ctas) return fail(c, TMG_ERR_INVALID, "bad argument");
+  if (!use_fused(c, kv)) return fail(c, TMG_ERR_INVALID, "the fused decode kernel does not apply");
+  const size_t n = size_t(c->num_sms) * (size_t(c->L) * 5 + 1) * 12;
+  if (max_u64 < int64_t(n)) return fail(c, TMG_ERR_INVALID, "trace buffer too small");
+  cudaSetDevice(c->device);
+  StreamState st;
+  int rc = prepare_decode(c, kv, &token, 1, &st);
+  if (rc) return rc;
+  unsigned long long* buf = nullptr;
+  CK(cudaMalloc(&buf, n * 8), "trace");
+  cudaError_t e = cudaMemsetAsync(buf, 0, n * 8, c->stream);
+  if (e == cudaSuccess) e = launch_fused(c, kv, st, 1, buf);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+  if (e == cudaSuccess) e = cudaMemcpy(out, buf, n * 8, cudaMemcpyDeviceToHost);
+  cudaFree(buf);
+  if (e != cudaSuccess) return cuda_fail(c, e, "trace");
+  *n_ctas = c->num_sms;
+  kv->lens[0] += 1;
   return sync_check(c, "trace");
 }
 

@@ -7,22 +7,33 @@
 //    CTA needs for all n_steps tokens -- q/k/v, o, gate/up, down of each
 //    layer, then the LM head -- through a ring of 32 KB shared-memory stages
 //    with cp.async.bulk (TMA) and mbarriers.  Weights never depend on
-//    activations, so this stream runs ahead of the math, across phase and
-//    token boundaries, limited only by free ring stages: HBM stays busy
-//    while the consumers sit at a grid barrier.
+//    activations, so the stream runs ahead of the math across phase and
+//    token boundaries.  Further ahead still, it prefetches the rows of later
+//    stages into L2 (cp.async.bulk.prefetch), so HBM keeps streaming while
+//    the consumers sit in attention or at a grid barrier, and the ring
+//    refills from L2 afterwards.
 //  * eight consumer warps run the phases of each layer, each followed by a
 //    grid barrier (bounded spin; a barrier that gives up sets the error word
 //    and every CTA leaves):
-//      QKV   rmsnorm(x) . Wqkv^T           -> qkv          (rows split over CTAs)
-//      ATTN  RoPE, KV append at pos, split-KV attention   -> partials
-//      O     combine partials, . Wo^T      -> x += ...
-//      GU    rmsnorm(x) . Wgate^T, Wup^T   -> act = silu(g) * u
-//      DOWN  act . Wdown^T                 -> x += ...
+//      QKV   rmsnorm(x) . Wqkv^T; RoPE on q and k, k/v appended at pos
+//      ATTN  split-KV attention per (kv head, split); the last split of a
+//            head to finish merges the partials into the attention output
+//      O     att . Wo^T              -> x += ...
+//      GU    rmsnorm(x) . Wgate^T, Wup^T -> act = silu(g) * u
+//      DOWN  act . Wdown^T           -> x += ...
 //    then HEAD: rmsnorm(x) . Wlm^T -> logits + per-CTA argmax; after one more
 //    barrier every CTA reduces the argmax (the same token everywhere), CTA 0
 //    records it, and the next token starts.
+// Inside a GEMV phase each warp works alone: it waits for a stage, dots its
+// row (or K segment of a row) against the input it holds in registers and
+// parks the sum in shared memory; one epilogue at the end of the phase
+// combines the K segments and applies the phase's output step.  Residual
+// rows are updated with one red.add each (each row has a single writer per
+// phase, so the result is x + y exactly, as with a plain add).
 // Row groups of a phase are dealt to CTAs round-robin with a rotating offset
 // so every CTA streams the same number of bytes per token within one group.
+// QKV groups pair rows j and j + d/2 of one q or k head (RoPE partners), so
+// the rotation and the KV append happen in the QKV epilogue.
 // All arithmetic is f32 with BF16 weights widened exactly, as in the
 // separate kernels; cross-CTA activations are read through L2 (ld.cg).
 #include <math.h>
@@ -39,8 +50,12 @@ constexpr int kCThreads = kCWarps * kWarp;         // 256
 constexpr int kFThreads = kCThreads + kWarp;       // + producer warp
 constexpr int kStage = 32 * 1024;                  // ring stage bytes
 constexpr int kMaxStagesF = 6;
-constexpr int kTileF = 64;                         // attention positions per tile
-constexpr int kMaxDefer = 512;                     // deferred residual rows per phase
+constexpr int kTileF = 32;                         // attention positions per tile
+constexpr int kMaxRes = 1024;                      // per-warp results of one phase
+constexpr int kMaxLocal = kMaxRes / kCWarps;       // groups of one CTA in a phase
+constexpr int kTicketBase = 64;                    // bar[64 + kv head]: attention tickets
+constexpr int kBarWords = 128;                     // words of the barrier block
+constexpr int kTraceWords = 12;                    // trace record per CTA and phase
 
 enum Phase : int { PH_QKV = 0, PH_O = 1, PH_GU = 2, PH_DOWN = 3, PH_HEAD = 4 };
 
@@ -66,6 +81,30 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_all;" ::: "memory");
 }
+// Stage n floats (n % 4 == 0, 16-byte aligned) into shared memory with
+// cp.async; the reader waits (cp.async.wait_all, then a CTA barrier).
+__device__ __forceinline__ void stage_vec(float* dst, const float* src, int n) {
+  for (int i = threadIdx.x * 4; i < n; i += kCThreads * 4) cp_async16(dst + i, src + i);
+}
+
+// L2 policy for weight rows: once copied to shared memory they are dead.
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ void bulk_g2s_ef(void* dst, const void* src, uint32_t bytes,
+                                            uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+// Bring [src, src + bytes) into L2 (no completion to wait for).
+__device__ __forceinline__ void l2_prefetch(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 
 __device__ __forceinline__ void fma8(const float4& xa, const float4& xb, const uint4& w,
                                      float (&s)[8]) {
@@ -82,31 +121,43 @@ __device__ __forceinline__ float sum8(const float (&s)[8]) {
   return ((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7]));
 }
 
+// RoPE of one pair (rotate-half form), without FMA contraction.
 __device__ __forceinline__ void rot(float a, float b, float c, float s, float* o0, float* o1) {
   float ac = __fmul_rn(a, c), bs = __fmul_rn(b, s), as = __fmul_rn(a, s), bc = __fmul_rn(b, c);
   *o0 = __fsub_rn(ac, bs);
   *o1 = __fadd_rn(as, bc);
 }
 
-// The geometry of one GEMV phase: rows of K elements in groups of `rpc` row
-// slots (for SwiGLU, rpg gate rows + rpg up rows), one 32 KB stage each.
+// ---------------------------------------------------------------------------
+// Phase geometry.  A group is one stage of rpc = 8 / ks rows of K elements
+// (at most 32 KB); warp w takes row slot w / ks and K segment w % ks.
+// ---------------------------------------------------------------------------
 struct PhaseGeo {
   const uint16_t* w;
-  const uint16_t* w2;
-  int64_t N;       // output rows
+  const uint16_t* w2;      // up rows (GU)
+  int64_t N;               // output rows
   int K;
-  int ks;          // K split over warps
-  int chunks;      // 256-element chunks per warp segment
-  int rpc;         // row slots per group (8 / ks)
-  int rpg;         // output rows per group
+  int ks;                  // K split over warps
+  int chunks;              // 256-element chunks per warp segment
+  int rpc;                 // row slots per group (8 / ks)
+  int rpg;                 // output rows per group (GU: rpc / 2 gate + as many up)
   int64_t ngroups;
-  uint32_t bytes;  // stage bytes of a full group
+  int64_t pair_groups;     // QKV: leading groups holding RoPE partner rows
+  int D;                   // head dim
 };
+
+__device__ __forceinline__ int ksplit(int K) {
+  int ks = 1;
+  while (K / ks > 2048) ks *= 2;
+  return ks;
+}
 
 __device__ __forceinline__ PhaseGeo geo(const FusedArgs& a, int ph, int l) {
   PhaseGeo g;
   const FusedLayer& L = a.layers[l];
   g.w2 = nullptr;
+  g.pair_groups = 0;
+  g.D = a.d;
   switch (ph) {
     case PH_QKV: g.w = L.wqkv; g.N = (a.nq + 2 * a.nkv) * a.d; g.K = a.h; break;
     case PH_O: g.w = L.wo; g.N = a.h; g.K = a.nq * a.d; break;
@@ -114,14 +165,69 @@ __device__ __forceinline__ PhaseGeo geo(const FusedArgs& a, int ph, int l) {
     case PH_DOWN: g.w = L.wd; g.N = a.h; g.K = a.I; break;
     default: g.w = a.lm_head; g.N = a.V; g.K = a.h; break;
   }
-  g.ks = 1;
-  while (g.K / g.ks > 2048) g.ks *= 2;
+  g.ks = ksplit(g.K);
   g.chunks = g.K / g.ks / 256;
   g.rpc = kCWarps / g.ks;
   g.rpg = ph == PH_GU ? g.rpc / 2 : g.rpc;
   g.ngroups = (g.N + g.rpg - 1) / g.rpg;
-  g.bytes = uint32_t(g.rpc) * g.K * 2;
+  if (ph == PH_QKV) g.pair_groups = int64_t(a.nq + a.nkv) * a.d / g.rpc;
   return g;
+}
+
+// Output row held by `slot` of group grp (GU: the gate/up row index).
+__device__ __forceinline__ int64_t slot_row(const PhaseGeo& g, int64_t grp, int slot) {
+  if (g.pair_groups > 0) {
+    if (grp < g.pair_groups) {
+      const int hp = g.rpc / 2, half = g.D / 2;
+      const int64_t gph = half / hp;  // groups per head
+      const int64_t ra = (grp / gph) * g.D + (grp % gph) * hp;
+      return slot < hp ? ra + slot : ra + half + (slot - hp);
+    }
+    return grp * g.rpc + slot;  // v rows follow the q and k rows
+  }
+  return grp * g.rpg + (slot % g.rpg);
+}
+
+// The (at most two) contiguous row ranges a group copies into its stage.
+struct Ranges {
+  const uint16_t* src[2];
+  uint32_t bytes[2];
+  uint32_t doff[2];
+  int n;
+};
+__device__ __forceinline__ Ranges group_ranges(const PhaseGeo& g, int64_t grp) {
+  Ranges r;
+  const uint32_t rowb = uint32_t(g.K) * 2;
+  if (g.pair_groups > 0) {
+    const int64_t ra = slot_row(g, grp, 0);
+    if (grp < g.pair_groups) {
+      const int hp = g.rpc / 2;
+      r.n = 2;
+      r.src[0] = g.w + ra * g.K;
+      r.src[1] = g.w + (ra + g.D / 2) * g.K;
+      r.bytes[0] = r.bytes[1] = uint32_t(hp) * rowb;
+      r.doff[0] = 0;
+      r.doff[1] = uint32_t(hp) * rowb;
+    } else {
+      r.n = 1;
+      r.src[0] = g.w + ra * g.K;
+      r.bytes[0] = uint32_t(g.rpc) * rowb;
+      r.doff[0] = 0;
+    }
+    return r;
+  }
+  const int64_t r0 = grp * g.rpg;
+  const int64_t nr = min(int64_t(g.rpg), g.N - r0);
+  r.n = g.w2 ? 2 : 1;
+  r.src[0] = g.w + r0 * g.K;
+  r.bytes[0] = uint32_t(nr) * rowb;
+  r.doff[0] = 0;
+  if (g.w2) {
+    r.src[1] = g.w2 + r0 * g.K;
+    r.bytes[1] = r.bytes[0];
+    r.doff[1] = uint32_t(g.rpg) * rowb;
+  }
+  return r;
 }
 
 // First group of this CTA in a phase whose groups start at rotation `off`.
@@ -130,53 +236,55 @@ __device__ __forceinline__ int64_t first_group(int off) {
   return int64_t(((int(blockIdx.x) - off) % n + n) % n);
 }
 
+// Upper bound on the kernel's static shared memory, checked at prepare time.
+constexpr size_t kStaticReserve = 8 * 1024;
+
 struct Shared {
   uint64_t full[kMaxStagesF];
   uint64_t empty[kMaxStagesF];
-  float part[2][kCWarps];
+  float res[kMaxRes];  // per-warp sums of this phase: [local group][warp]
   float ssq[kCWarps];
   unsigned long long best[kCWarps];
-  float defer_v[kMaxDefer];
-  float defer_old[kMaxDefer];
+  float m_s[8], l_s[8], alpha_s[8];
+  int flag;
   int gen_ok;
-  volatile int abort;      // consumers -> producer: stop issuing
+  volatile int abort;      // stop issuing / waiting (error or early end)
   volatile int issued;     // producer: stages issued so far
   volatile int prod_done;  // producer: no more stages will be issued
-  float m_s[8], l_s[8], alpha_s[8];
 };
 
 // ---------------------------------------------------------------------------
-// Grid barrier among the consumer warps of all CTAs.  Generation counting,
-// reusable across launches; every wait is bounded in time.
+// Grid barrier among the consumer warps of all CTAs: one monotonic arrival
+// counter (zeroed before the launch); the k-th barrier waits until it reaches
+// k * gridDim.x.  Every wait is bounded in time; a CTA that has aborted does
+// not arrive and raises bar[2], which releases the others.
 // ---------------------------------------------------------------------------
-__device__ bool grid_sync(const FusedArgs& a, unsigned int& gen, Shared& S) {
+__device__ bool grid_sync(const FusedArgs& a, unsigned int& target, Shared& S,
+                          unsigned long long* tr) {
   csync();
   if (threadIdx.x == 0) {
-    int ok = 1;
-    __threadfence();
-    const unsigned int g = gen;
-    if (atomicAdd(&a.bar[0], 1u) == gridDim.x - 1) {
-      atomicExch(&a.bar[0], 0u);
-      __threadfence();
-      atomicExch(&a.bar[1], g + 1);
-    } else {
+    if (tr) tr[0] = global_ns();
+    int ok = S.abort ? 0 : 1;
+    target += gridDim.x;
+    if (ok) {
+      asm volatile("fence.acq_rel.gpu;" ::: "memory");
+      asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
       const unsigned long long t0 = global_ns();
       unsigned int spins = 0;
-      while (ld_acquire(&a.bar[1]) == g) {
+      while (int(ld_acquire(a.bar) - target) < 0) {
         if ((++spins & 255) == 0) {
-          if (ld_acquire(&a.bar[2]) != 0 || global_ns() - t0 > kWaitNs) {
+          if (ld_acquire(a.bar + 2) != 0 || global_ns() - t0 > kWaitNs) {
             ok = 0;
             break;
           }
         }
       }
     }
-    gen = g + 1;
-    __threadfence();
     if (!ok) {
-      atomicExch(&a.bar[2], 1u);
+      atomicExch(a.bar + 2, 1u);
       if (a.err) atomicExch(a.err, 2);
     }
+    if (tr) tr[1] = global_ns();
     S.gen_ok = ok;
   }
   csync();
@@ -186,34 +294,108 @@ __device__ bool grid_sync(const FusedArgs& a, unsigned int& gen, Shared& S) {
 // ---------------------------------------------------------------------------
 // Producer: the weight stream of all steps, in consumption order.
 // ---------------------------------------------------------------------------
-__device__ void producer(const FusedArgs& a, Shared& S, uint8_t* ring, int nst) {
-  int it = 0;
-  int off = 0;
-  for (int step = 0; step < a.n_steps; ++step) {
-    for (int l = 0; l <= a.L; ++l) {
-      for (int ph = (l == a.L ? PH_HEAD : PH_QKV); ph <= (l == a.L ? PH_HEAD : PH_DOWN); ++ph) {
-        const PhaseGeo g = geo(a, ph, l < a.L ? l : 0);
-        for (int64_t grp = first_group(off); grp < g.ngroups; grp += gridDim.x, ++it) {
-          const int s = it % nst;
-          const uint32_t par = (it / nst) & 1;
-          if (S.abort) return;
-          if (!mbar_wait(&S.empty[s], par ^ 1)) {
-            S.abort = 1;
-            if (a.err) atomicExch(a.err, 2);
-            return;
-          }
-          uint8_t* dst = ring + size_t(s) * kStage;
-          const int64_t r0 = grp * g.rpg;
-          const int64_t nr = min(int64_t(g.rpg), g.N - r0);
-          const uint32_t bytes = uint32_t(nr) * g.K * 2;
-          mbar_expect_tx(&S.full[s], ph == PH_GU ? 2 * bytes : bytes);
-          bulk_g2s(dst, g.w + r0 * g.K, bytes, &S.full[s]);
-          if (ph == PH_GU) bulk_g2s(dst + size_t(g.rpg) * g.K * 2, g.w2 + r0 * g.K, bytes, &S.full[s]);
-          S.issued = it + 1;
-        }
-        off = int((off + g.ngroups) % gridDim.x);
+struct Cursor {
+  int step, l, ph, off;
+  int64_t grp;
+  PhaseGeo g;
+  bool valid;
+};
+
+__device__ __forceinline__ void cur_settle(const FusedArgs& a, Cursor& c) {
+  while (c.valid && c.grp >= c.g.ngroups) {
+    c.off = int((c.off + c.g.ngroups) % gridDim.x);
+    if (c.ph == PH_HEAD) {
+      if (++c.step >= a.n_steps) {
+        c.valid = false;
+        break;
       }
+      c.l = 0;
+      c.ph = PH_QKV;
+    } else if (c.ph == PH_DOWN) {
+      ++c.l;
+      c.ph = c.l == a.L ? PH_HEAD : PH_QKV;
+    } else {
+      ++c.ph;
     }
+    c.g = geo(a, c.ph, c.l < a.L ? c.l : 0);
+    c.grp = first_group(c.off);
+  }
+}
+__device__ __forceinline__ void cur_begin(const FusedArgs& a, Cursor& c) {
+  c.step = 0;
+  c.l = 0;
+  c.ph = PH_QKV;
+  c.off = 0;
+  c.g = geo(a, PH_QKV, 0);
+  c.grp = first_group(0);
+  c.valid = a.n_steps > 0;
+  cur_settle(a, c);
+}
+__device__ __forceinline__ void cur_next(const FusedArgs& a, Cursor& c) {
+  c.grp += gridDim.x;
+  cur_settle(a, c);
+}
+
+__device__ void producer(const FusedArgs& a, Shared& S, uint8_t* ring, int nst) {
+  const uint64_t pol = evict_first_policy();
+  const int nph = a.L * 5 + 1;
+  Cursor ic, pc;
+  cur_begin(a, ic);
+  pc = ic;
+  int it = 0, pf = 0;
+  unsigned long long* tr_cur = nullptr;  // diagnostics of the phase being issued
+  unsigned long long t_last = 0, c_wait = 0, c_issue = 0;
+  while (ic.valid) {
+    // L2 prefetch of stages it + nst .. it + nst + pf_ahead - 1
+    while (pc.valid && pf < it + nst + a.pf_ahead) {
+      if (pf >= it + nst) {
+        const Ranges r = group_ranges(pc.g, pc.grp);
+        l2_prefetch(r.src[0], r.bytes[0]);
+        if (r.n > 1) l2_prefetch(r.src[1], r.bytes[1]);
+      }
+      cur_next(a, pc);
+      ++pf;
+    }
+    const int s = it % nst;
+    const uint32_t par = (it / nst) & 1;
+    if (S.abort) return;
+    const long long c0 = clock64();
+    if (!mbar_wait(&S.empty[s], par ^ 1)) {
+      S.abort = 1;
+      if (a.err) atomicExch(a.err, 2);
+      return;
+    }
+    const long long c1 = clock64();
+    const Ranges r = group_ranges(ic.g, ic.grp);
+    mbar_expect_tx(&S.full[s], r.bytes[0] + (r.n > 1 ? r.bytes[1] : 0u));
+    uint8_t* dst = ring + size_t(s) * kStage;
+    bulk_g2s_ef(dst + r.doff[0], r.src[0], r.bytes[0], &S.full[s], pol);
+    if (r.n > 1) bulk_g2s_ef(dst + r.doff[1], r.src[1], r.bytes[1], &S.full[s], pol);
+    S.issued = it + 1;
+    if (a.trace && ic.step == 0) {
+      const int p = ic.l == a.L ? a.L * 5 : ic.l * 5 + (ic.ph == PH_QKV ? 0 : ic.ph + 1);
+      unsigned long long* tr = a.trace + (size_t(blockIdx.x) * nph + p) * kTraceWords;
+      if (tr != tr_cur) {
+        if (tr_cur) {
+          tr_cur[3] = t_last;
+          tr_cur[10] = c_wait;
+          tr_cur[11] = c_issue;
+        }
+        tr_cur = tr;
+        tr[2] = global_ns();
+        c_wait = c_issue = 0;
+      }
+      t_last = global_ns();
+      c_wait += c1 - c0;
+      c_issue += clock64() - c1;
+    }
+    cur_next(a, ic);
+    ++it;
+  }
+  if (tr_cur) {
+    tr_cur[3] = t_last;
+    tr_cur[10] = c_wait;
+    tr_cur[11] = c_issue;
   }
 }
 
@@ -224,204 +406,340 @@ struct XSeg {
   float4 a[8], b[8];
 };
 
-// Load this warp's K segment of the phase input into registers: from the
-// staged (normalised) x in shared memory or straight from global memory.
-__device__ __forceinline__ void load_seg(XSeg& x, const float* src, bool via_l2, int kbase,
-                                         int chunks, int lane) {
+// This warp's K segment of the phase input, from f32 activations (via L2)
+// or from a BF16 row (the embedding, widened exactly).
+__device__ __forceinline__ void load_seg_l2(XSeg& x, const float* src, int kbase, int chunks,
+                                            int lane) {
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
     if (c < chunks) {
       const int k = kbase + c * 256 + lane * 8;
-      if (via_l2) {
-        x.a[c] = ldcg4(src + k);
-        x.b[c] = ldcg4(src + k + 4);
-      } else {
-        x.a[c] = *reinterpret_cast<const float4*>(src + k);
-        x.b[c] = *reinterpret_cast<const float4*>(src + k + 4);
-      }
+      x.a[c] = ldcg4(src + k);
+      x.b[c] = ldcg4(src + k + 4);
+    }
+  }
+}
+__device__ __forceinline__ void load_seg_bf16(XSeg& x, const uint16_t* src, int kbase, int chunks,
+                                              int lane) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    if (c < chunks) {
+      const uint4 u = *reinterpret_cast<const uint4*>(src + kbase + c * 256 + lane * 8);
+      x.a[c] = make_float4(bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y));
+      x.b[c] = make_float4(bf16lo(u.z), bf16hi(u.z), bf16lo(u.w), bf16hi(u.w));
     }
   }
 }
 
-// rmsnorm of v[0..n) (already in shared memory `xs`) in place:
-// v * inv * w (rms_norm_into's order).
-__device__ __forceinline__ void norm_in_smem(float* xs, const float* w, int n, float eps, Shared& S) {
-  float ss = 0.f;
-  for (int k = threadIdx.x; k < n; k += kCThreads) ss = fmaf(xs[k], xs[k], ss);
-  ss = warp_sum(ss);
-  if ((threadIdx.x & 31) == 0) S.ssq[threadIdx.x >> 5] = ss;
-  csync();
-  float tot = 0.f;
+// rmsnorm of the n-vector whose K segments the warps hold (warps slot*ks ..
+// slot*ks + ks - 1 cover all of it): x <- (x * inv) * w, rms_norm_into's
+// order, w staged in shared memory.  With ks > 1 the segment sums meet in
+// shared memory.
+__device__ __forceinline__ void norm_seg(XSeg& x, const float* w, int kbase, int chunks, int ks,
+                                         int n, float eps, Shared& S) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-  for (int i = 0; i < kCWarps; ++i) tot += S.ssq[i];
-  const float inv = 1.0f / sqrtf(tot / float(n) + eps);
-  for (int k = threadIdx.x; k < n; k += kCThreads) {
-    const float t = xs[k] * inv;
-    xs[k] = t * __ldg(w + k);
+  for (int c = 0; c < 8; ++c) {
+    if (c < chunks) {
+      s0 = fmaf(x.a[c].x, x.a[c].x, s0);
+      s1 = fmaf(x.a[c].y, x.a[c].y, s1);
+      s0 = fmaf(x.a[c].z, x.a[c].z, s0);
+      s1 = fmaf(x.a[c].w, x.a[c].w, s1);
+      s0 = fmaf(x.b[c].x, x.b[c].x, s0);
+      s1 = fmaf(x.b[c].y, x.b[c].y, s1);
+      s0 = fmaf(x.b[c].z, x.b[c].z, s0);
+      s1 = fmaf(x.b[c].w, x.b[c].w, s1);
+    }
   }
-  csync();
+  float tot = warp_sum(s0 + s1);
+  if (ks > 1) {
+    if (lane == 0) S.ssq[warp] = tot;
+    csync();
+    tot = 0.f;
+    for (int j = 0; j < ks; ++j) tot += S.ssq[(warp / ks) * ks + j];
+  }
+  const float inv = 1.0f / sqrtf(tot / float(n) + eps);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    if (c < chunks) {
+      const int k = kbase + c * 256 + lane * 8;
+      const float4 wa = *reinterpret_cast<const float4*>(w + k);
+      const float4 wb = *reinterpret_cast<const float4*>(w + k + 4);
+      x.a[c] = make_float4((x.a[c].x * inv) * wa.x, (x.a[c].y * inv) * wa.y,
+                           (x.a[c].z * inv) * wa.z, (x.a[c].w * inv) * wa.w);
+      x.b[c] = make_float4((x.b[c].x * inv) * wb.x, (x.b[c].y * inv) * wb.y,
+                           (x.b[c].z * inv) * wb.z, (x.b[c].w * inv) * wb.w);
+    }
+  }
 }
 
-// One GEMV phase over this CTA's groups.  EPI: 0 store y, 1 deferred
-// residual add into y, 2 SwiGLU into y, 3 LM head (store + argmax).
-template <int EPI>
-__device__ __forceinline__ bool gemv_phase(const PhaseGeo& g, const XSeg& x, float* y, int off, int& it, int nst,
-                           uint8_t* ring, Shared& S, unsigned long long& best, int& n_def) {
+// One GEMV phase over this CTA's groups: each warp dots its slot/segment of
+// every stage.  imm (LM head with ks == 1): logits and the argmax candidate
+// directly; otherwise the sums go to S.res for the phase's epilogue.
+// Returns the number of local groups.
+// Position in the stage ring: stage count, slot, phase parity.
+struct RingPos {
+  int it, s;
+  uint32_t par;
+  __device__ __forceinline__ void next(int nst) {
+    ++it;
+    if (++s == nst) {
+      s = 0;
+      par ^= 1u;
+    }
+  }
+};
+
+__device__ __forceinline__ int gemv_phase(const PhaseGeo& g, int chunks, const XSeg& x, int off,
+                                          RingPos& rp, int nst, const uint8_t* ring, Shared& S,
+                                          bool imm, float* logits, unsigned long long& best,
+                                          unsigned long long* tw) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ks = warp % g.ks, slot = warp / g.ks;
-  const int kbase = ks * g.chunks * 256;
-  const bool need_sync = g.ks > 1 || EPI == 2;
-  int k_local = 0;
-  for (int64_t grp = first_group(off); grp < g.ngroups; grp += gridDim.x, ++it, ++k_local) {
-    const int s = it % nst;
-    const uint32_t par = (it / nst) & 1;
-    const int64_t r0 = grp * g.rpg;
-    const int rslot = EPI == 2 ? slot % g.rpg : slot;
-    const bool valid = r0 + rslot < g.N;
+  const int slot = warp / g.ks;
+  const int kbase = (warp % g.ks) * chunks * 256;
+  // this lane's first weight element in stage 0
+  const uint16_t* wbase = reinterpret_cast<const uint16_t*>(ring + size_t(slot) * g.K * 2) + kbase + lane * 8;
+  int kl = 0;
+  long long c_wait = 0, c_math = 0;
+  for (int64_t grp = first_group(off); grp < g.ngroups; grp += gridDim.x, rp.next(nst), ++kl) {
+    const int s = rp.s;
     float acc = 0.f;
-    const bool ok = !S.abort && mbar_wait(&S.full[s], par);
-    if (ok && valid) {
-      const uint16_t* wr = reinterpret_cast<const uint16_t*>(ring + size_t(s) * kStage +
-                                                             size_t(slot) * g.K * 2) +
-                           kbase + lane * 8;
+    const long long c0 = tw ? clock64() : 0;
+    const bool ok = !S.abort && mbar_wait(&S.full[s], rp.par);
+    const long long c1 = tw ? clock64() : 0;
+    if (tw && kl == 0 && threadIdx.x == 0) tw[6] = global_ns();
+    if (ok) {
+      const uint16_t* wr = wbase + s * (kStage / 2);
       float sacc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 8; ++c)
-        if (c < g.chunks) fma8(x.a[c], x.b[c], *reinterpret_cast<const uint4*>(wr + c * 256), sacc);
+        if (c < chunks) fma8(x.a[c], x.b[c], *reinterpret_cast<const uint4*>(wr + c * 256), sacc);
       acc = sum8(sacc);
+    } else if (lane == 0) {
+      S.abort = 1;
     }
-    if (!ok && lane == 0) S.abort = 1;
     __syncwarp();
     if (lane == 0) mbar_arrive(&S.empty[s]);
     acc = warp_sum(acc);
-    if (need_sync) {
-      if (lane == 0) S.part[it & 1][warp] = acc;
-      csync();
+    if (tw) {
+      c_wait += c1 - c0;
+      c_math += clock64() - c1;
     }
-    if (lane == 0 && ks == 0 && valid && (EPI != 2 || slot < g.rpg)) {
-      for (int j = 1; j < g.ks; ++j) acc += S.part[it & 1][warp + j];
-      const int64_t r = r0 + rslot;
-      if (EPI == 2) {
-        float up = 0.f;
-        for (int j = 0; j < g.ks; ++j) up += S.part[it & 1][(slot + g.rpg) * g.ks + j];
-        const float sg = acc / (1.0f + expf(-acc));
-        y[r] = sg * up;
-      } else if (EPI == 1) {
-        S.defer_v[k_local * g.rpg + rslot] = acc;
-      } else {
-        y[r] = acc;
-        if (EPI == 3) {
+    if (lane == 0) {
+      if (imm) {
+        const int64_t r = grp * g.rpg + slot;
+        if (r < g.N) {
+          logits[r] = acc;
           const unsigned long long kk = argmax_key(acc, uint32_t(r));
           best = kk > best ? kk : best;
         }
+      } else if (kl < kMaxLocal) {
+        S.res[kl * kCWarps + warp] = acc;
       }
     }
   }
-  if (EPI == 1) n_def = k_local * g.rpg;
-  return !S.abort;
+  if (tw && threadIdx.x == 0) {
+    tw[8] = c_wait;
+    tw[9] = c_math;
+  }
+  return kl;
 }
 
-// Prefetch the residual rows this CTA will update in a deferred-add phase.
-__device__ __forceinline__ void prefetch_residual(const PhaseGeo& g, const float* x, int off, Shared& S) {
+// Sum of slot `slot` of local group kl over its K segments, in order.
+__device__ __forceinline__ float res_val(const Shared& S, int kl, int slot, int ks) {
+  float v = S.res[kl * kCWarps + slot * ks];
+  for (int j = 1; j < ks; ++j) v += S.res[kl * kCWarps + slot * ks + j];
+  return v;
+}
+
+// QKV epilogue: RoPE on the q/k partner rows at position pos (rope_s: the
+// cos then sin row of pos); q to qkv, k and v appended to the cache at pos
+// (when there is room).
+__device__ __forceinline__ void epi_qkv(const FusedArgs& a, const FusedLayer& L, const PhaseGeo& g,
+                                        int off, int nloc, int pos, bool append,
+                                        const float* rope_s, Shared& S) {
+  const int D = g.D, half = D / 2, hp = g.rpc / 2, kvd = a.nkv * D;
   const int64_t f = first_group(off);
-  const int64_t my_groups = f < g.ngroups ? (g.ngroups - 1 - f) / gridDim.x + 1 : 0;
-  const int n = int(my_groups) * g.rpg;
-  for (int k = threadIdx.x; k < n && k < kMaxDefer; k += kCThreads) {
-    const int64_t r = (f + int64_t(k / g.rpg) * gridDim.x) * g.rpg + k % g.rpg;
-    S.defer_old[k] = r < g.N ? ldcg(x + r) : 0.f;
+  for (int i = threadIdx.x; i < nloc * g.rpc; i += kCThreads) {
+    const int kl = i / g.rpc, slot = i % g.rpc;
+    const int64_t grp = f + int64_t(kl) * gridDim.x;
+    if (grp < g.pair_groups) {
+      if (slot >= hp) continue;  // done with its partner
+      const int64_t ra = slot_row(g, grp, slot);
+      const int64_t head = ra / D;
+      const int j = int(ra % D);
+      float o0, o1;
+      rot(res_val(S, kl, slot, g.ks), res_val(S, kl, slot + hp, g.ks), rope_s[j], rope_s[half + j],
+          &o0, &o1);
+      if (head < a.nq) {
+        a.qkv[ra] = o0;
+        a.qkv[ra + half] = o1;
+      } else if (append) {
+        float* kr = L.kc + size_t(pos) * kvd + (head - a.nq) * D;
+        kr[j] = o0;
+        kr[j + half] = o1;
+      }
+    } else if (append) {
+      const int64_t r = slot_row(g, grp, slot) - int64_t(a.nq + a.nkv) * D;
+      L.vc[size_t(pos) * kvd + r] = res_val(S, kl, slot, g.ks);
+    }
   }
 }
 
-__device__ __forceinline__ void apply_residual(const PhaseGeo& g, float* x, int off, int n_def, Shared& S) {
-  csync();
+// O / DOWN epilogue: x[r] += y[r] (a single add per row).
+__device__ __forceinline__ void epi_residual(float* x, const PhaseGeo& g, int off, int nloc,
+                                             const Shared& S) {
   const int64_t f = first_group(off);
-  for (int k = threadIdx.x; k < n_def && k < kMaxDefer; k += kCThreads) {
-    const int64_t r = (f + int64_t(k / g.rpg) * gridDim.x) * g.rpg + k % g.rpg;
-    if (r < g.N) x[r] = S.defer_old[k] + S.defer_v[k];
+  for (int i = threadIdx.x; i < nloc * g.rpc; i += kCThreads) {
+    const int kl = i / g.rpc, slot = i % g.rpc;
+    const int64_t r = (f + int64_t(kl) * gridDim.x) * g.rpg + slot;
+    if (r < g.N) atomicAdd(x + r, res_val(S, kl, slot, g.ks));
   }
 }
 
-// Attention partials of one (kv head, split) item: RoPE, KV append by the
-// owner of pos, online softmax over the split's positions.
+// GU epilogue: act = silu(gate) * up.
+__device__ __forceinline__ void epi_swiglu(float* act, const PhaseGeo& g, int off, int nloc,
+                                           const Shared& S) {
+  const int64_t f = first_group(off);
+  for (int i = threadIdx.x; i < nloc * g.rpg; i += kCThreads) {
+    const int kl = i / g.rpg, q = i % g.rpg;
+    const int64_t r = (f + int64_t(kl) * gridDim.x) * g.rpg + q;
+    if (r < g.N) {
+      const float gv = res_val(S, kl, q, g.ks), uv = res_val(S, kl, q + g.rpg, g.ks);
+      act[r] = gv / (1.0f + expf(-gv)) * uv;
+    }
+  }
+}
+
+// LM head epilogue (ks > 1): logits and this thread's argmax candidate.
+__device__ __forceinline__ void epi_head(float* logits, const PhaseGeo& g, int off, int nloc,
+                                         const Shared& S, unsigned long long& best) {
+  const int64_t f = first_group(off);
+  for (int i = threadIdx.x; i < nloc * g.rpc; i += kCThreads) {
+    const int kl = i / g.rpc, slot = i % g.rpc;
+    const int64_t r = (f + int64_t(kl) * gridDim.x) * g.rpg + slot;
+    if (r < g.N) {
+      const float v = res_val(S, kl, slot, g.ks);
+      logits[r] = v;
+      const unsigned long long kk = argmax_key(v, uint32_t(r));
+      best = kk > best ? kk : best;
+    }
+  }
+}
+
+// What the attention items of one layer read and write (passed by value to
+// the out-of-line item function, so the kernel arguments stay in the
+// parameter bank).
+struct AttnArgs {
+  const float* qkv;
+  const float* kc;
+  const float* vc;
+  float* part;
+  float* att;
+  unsigned int* tickets;
+  int nq, nkv, nsplit;
+  float scale;
+};
+
+// Merge the n_used split partials of kv head kvh into the attention output.
 template <int D>
-__device__ __forceinline__ void attn_item(const FusedArgs& a, const FusedLayer& L, int kvh, int split, int chunk,
-                          int n_ctx, int pos, bool append, float* sm, Shared& S) {
+__device__ __forceinline__ void combine_head(const AttnArgs& a, int kvh, int n_used, float* sm) {
+  const int G = a.nq / a.nkv, tid = threadIdx.x;
+  const float* pb = a.part + size_t(kvh) * a.nsplit * G * (D + 2);
+  float* mv = sm;                  // [G][n_used]
+  float* lv = mv + G * n_used;     // [G][n_used]
+  float* wv = lv + G * n_used;     // [G][n_used]
+  float* Ls = wv + G * n_used;     // [G]
+  for (int i = tid; i < G * n_used; i += kCThreads) {
+    const int s = i / G, g = i % G;
+    const float* p = pb + (size_t(s) * G + g) * (D + 2);
+    mv[g * n_used + s] = ldcg(p);
+    lv[g * n_used + s] = ldcg(p + 1);
+  }
+  csync();
+  if (tid < G) {
+    float mx = -INFINITY;
+    for (int s = 0; s < n_used; ++s) mx = fmaxf(mx, mv[tid * n_used + s]);
+    float L = 0.f;
+    for (int s = 0; s < n_used; ++s) {
+      const float ms = mv[tid * n_used + s];
+      const float w = ms == -INFINITY ? 0.f : expf(ms - mx);
+      wv[tid * n_used + s] = w;
+      L = fmaf(lv[tid * n_used + s], w, L);
+    }
+    Ls[tid] = L;
+  }
+  csync();
+  for (int idx = tid; idx < G * D; idx += kCThreads) {
+    const int g = idx / D, j = idx % D;
+    float acc = 0.f;
+    for (int s = 0; s < n_used; ++s)
+      acc = fmaf(ldcg(pb + (size_t(s) * G + g) * (D + 2) + 2 + j), wv[g * n_used + s], acc);
+    const float L = Ls[g];
+    a.att[size_t(kvh) * G * D + idx] = L > 0.f ? acc / L : 0.f;
+  }
+}
+
+// Attention of one (kv head, split) item over positions [split*chunk,
+// min(n_ctx, (split+1)*chunk)) with online softmax; q (already rotated) from
+// qkv, keys/values from the cache.  A single split writes the output; else
+// the partial (m, l, o) goes to `part` and the last split to finish merges.
+template <int D>
+__device__ __noinline__ void attn_item(const AttnArgs a, int kvh,
+                                          int split, int chunk, int n_ctx, int n_used, float* sm,
+                                          Shared& S, unsigned long long* tp) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int G = a.nq / a.nkv, half = D / 2, kvd = a.nkv * D;
+  const int G = a.nq / a.nkv, kvd = a.nkv * D;
   float* qs = sm;                       // [G][D]
   float* ks_ = qs + G * D;              // [kTileF][D+4]
   float* vs = ks_ + kTileF * (D + 4);   // [kTileF][D]
   float* ps = vs + kTileF * D;          // [G][kTileF]
   const int c0 = split * chunk, c1 = min(n_ctx, c0 + chunk);
-  const bool own = append && pos >= c0 && pos < c1;
-  const int64_t rp = pos < a.cap ? pos : a.cap - 1;  // the host keeps pos < cap
-  for (int i = tid; i < G * half; i += kCThreads) {
-    const int g = i / half, j = i % half;
-    const float* qh = a.qkv + (kvh * G + g) * D;
-    float o0, o1;
-    rot(ldcg(qh + j), ldcg(qh + j + half), a.rope_cos[rp * half + j], a.rope_sin[rp * half + j],
-        &o0, &o1);
-    qs[g * D + j] = o0;
-    qs[g * D + j + half] = o1;
-  }
-  if (own) {
-    const float* kh = a.qkv + a.nq * D + kvh * D;
-    const float* vh = a.qkv + (a.nq + a.nkv) * D + kvh * D;
-    for (int j = tid; j < half; j += kCThreads) {
-      float o0, o1;
-      rot(ldcg(kh + j), ldcg(kh + j + half), a.rope_cos[size_t(pos) * half + j],
-          a.rope_sin[size_t(pos) * half + j], &o0, &o1);
-      L.kc[size_t(pos) * kvd + kvh * D + j] = o0;
-      L.kc[size_t(pos) * kvd + kvh * D + j + half] = o1;
-    }
-    for (int j = tid; j < D; j += kCThreads) L.vc[size_t(pos) * kvd + kvh * D + j] = ldcg(vh + j);
-  }
   if (tid < G) {
     S.m_s[tid] = -INFINITY;
     S.l_s[tid] = 0.f;
   }
-  float o_acc[4] = {0.f, 0.f, 0.f, 0.f};  // G * D <= 1024 outputs, tid + 256 r
-  csync();  // the append is visible to this CTA's tile loads
+  float o_acc[4] = {0.f, 0.f, 0.f, 0.f};  // G * D <= 1024 outputs: tid + 256 r
   for (int t0 = c0; t0 < c1; t0 += kTileF) {
     const int nt = min(kTileF, c1 - t0);
     for (int i = tid; i < nt * (D / 4); i += kCThreads) {
       const int t = i / (D / 4), j4 = i % (D / 4);
-      cp_async16(ks_ + t * (D + 4) + j4 * 4, L.kc + size_t(t0 + t) * kvd + kvh * D + j4 * 4);
-      cp_async16(vs + t * D + j4 * 4, L.vc + size_t(t0 + t) * kvd + kvh * D + j4 * 4);
+      cp_async16(ks_ + t * (D + 4) + j4 * 4, a.kc + size_t(t0 + t) * kvd + kvh * D + j4 * 4);
+      cp_async16(vs + t * D + j4 * 4, a.vc + size_t(t0 + t) * kvd + kvh * D + j4 * 4);
+    }
+    if (t0 == c0) {
+      const float* qh = a.qkv + size_t(kvh) * G * D;
+      for (int i = tid; i < G * D / 4; i += kCThreads)
+        reinterpret_cast<float4*>(qs)[i] = ldcg4(qh + i * 4);
     }
     cp_async_wait_all();
     csync();
+    if (tp && tid == 0 && t0 == c0) tp[4] = global_ns();
     if (warp < G) {
       const int g = warp;
       const float* qr = qs + g * D;
-      float sc[2];
+      float sc = -INFINITY;
+      if (lane < nt) {
+        const float* kr = ks_ + lane * (D + 4);
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        const int t = lane + 32 * h2;
-        sc[h2] = -INFINITY;
-        if (t < nt) {
-          const float* kr = ks_ + t * (D + 4);
-          float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll
-          for (int j = 0; j < D; j += 4) {
-            const float4 k4 = *reinterpret_cast<const float4*>(kr + j);
-            const float4 q4 = *reinterpret_cast<const float4*>(qr + j);
-            a0 = fmaf(q4.x, k4.x, a0);
-            a1 = fmaf(q4.y, k4.y, a1);
-            a2 = fmaf(q4.z, k4.z, a2);
-            a3 = fmaf(q4.w, k4.w, a3);
-          }
-          sc[h2] = ((a0 + a1) + (a2 + a3)) * a.scale;
+        for (int j = 0; j < D; j += 4) {
+          const float4 k4 = *reinterpret_cast<const float4*>(kr + j);
+          const float4 q4 = *reinterpret_cast<const float4*>(qr + j);
+          a0 = fmaf(q4.x, k4.x, a0);
+          a1 = fmaf(q4.y, k4.y, a1);
+          a2 = fmaf(q4.z, k4.z, a2);
+          a3 = fmaf(q4.w, k4.w, a3);
         }
+        sc = ((a0 + a1) + (a2 + a3)) * a.scale;
       }
-      const float mt = warp_max(fmaxf(sc[0], sc[1]));
+      const float mt = warp_max(sc);
       const float m_old = S.m_s[g];
       const float m_new = fmaxf(m_old, mt);
-      const float p0 = lane < nt ? expf(sc[0] - m_new) : 0.f;
-      const float p1 = lane + 32 < nt ? expf(sc[1] - m_new) : 0.f;
-      const float lsum = warp_sum(p0 + p1);
-      ps[g * kTileF + lane] = p0;
-      ps[g * kTileF + lane + 32] = p1;
+      const float p = lane < nt ? expf(sc - m_new) : 0.f;
+      const float lsum = warp_sum(p);
+      ps[g * kTileF + lane] = p;
       if (lane == 0) {
         const float alpha = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
         S.alpha_s[g] = alpha;
@@ -449,6 +767,18 @@ __device__ __forceinline__ void attn_item(const FusedArgs& a, const FusedLayer& 
     }
     csync();
   }
+  if (n_used == 1) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int idx = tid + r * kCThreads;
+      if (idx < G * D) {
+        const float l = S.l_s[idx / D];
+        a.att[size_t(kvh) * G * D + idx] = l > 0.f ? o_acc[r] / l : 0.f;
+      }
+    }
+    csync();
+    return;
+  }
   float* part = a.part + (size_t(kvh) * a.nsplit + split) * G * (D + 2);
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
@@ -459,48 +789,34 @@ __device__ __forceinline__ void attn_item(const FusedArgs& a, const FusedLayer& 
     part[tid * (D + 2)] = S.m_s[tid];
     part[tid * (D + 2) + 1] = S.l_s[tid];
   }
+  __threadfence();
   csync();
-}
-
-// attention output (q_dim floats) into shared memory from the partials.
-template <int D>
-__device__ __forceinline__ void combine(const FusedArgs& a, int n_used, float* out, float* wts, Shared& S) {
-  const int G = a.nq / a.nkv, tid = threadIdx.x;
-  const int nh = a.nkv * G;  // query heads
-  // per (kv head, g): the weights exp(m_s - max) of the used splits
-  for (int hq = tid; hq < nh; hq += kCThreads) {
-    const int kvh = hq / G, g = hq % G;
-    const float* pb = a.part + size_t(kvh) * a.nsplit * G * (D + 2) + g * (D + 2);
-    float mx = -INFINITY;
-    for (int s = 0; s < n_used; ++s) mx = fmaxf(mx, ldcg(pb + size_t(s) * G * (D + 2)));
-    float L = 0.f;
-    for (int s = 0; s < n_used; ++s) {
-      const float ms = ldcg(pb + size_t(s) * G * (D + 2));
-      const float w = ms == -INFINITY ? 0.f : expf(ms - mx);
-      wts[hq * n_used + s] = w;
-      L = fmaf(ldcg(pb + size_t(s) * G * (D + 2) + 1), w, L);
-    }
-    wts[nh * n_used + hq] = L;
+  if (tp && tid == 0) tp[5] = global_ns();
+  if (tid == 0)
+    S.flag = atomicAdd(a.tickets + kvh, 1u) == unsigned(n_used - 1) ? 1 : 0;
+  csync();
+  if (S.flag) {
+    __threadfence();
+    combine_head<D>(a, kvh, n_used, sm);
+    if (tid == 0) atomicExch(a.tickets + kvh, 0u);
   }
   csync();
-  for (int idx = tid; idx < nh * D; idx += kCThreads) {
-    const int hq = idx / D, j = idx % D, kvh = hq / G, g = hq % G;
-    const float* pb = a.part + size_t(kvh) * a.nsplit * G * (D + 2) + g * (D + 2) + 2 + j;
-    float acc = 0.f;
-    for (int s = 0; s < n_used; ++s) acc = fmaf(ldcg(pb + size_t(s) * G * (D + 2)), wts[hq * n_used + s], acc);
-    const float L = wts[nh * n_used + hq];
-    out[idx] = L > 0.f ? acc / L : 0.f;
+  if (tp && tid == 0) {
+    tp[6] = global_ns();
+    tp[7] = S.flag;
   }
-  csync();
 }
 
-template <int D>
+// D: head dim.  CH: 256-element chunks of every warp segment when all
+// phases agree (8 for 2048-wide segments), 0 = read from the phase.
+template <int D, int CH>
 __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedArgs a, int nst) {
   extern __shared__ __align__(1024) uint8_t dsm[];
   __shared__ Shared S;
   uint8_t* ring = dsm;
-  float* xs = reinterpret_cast<float*>(dsm + size_t(nst) * kStage);  // max(h, q_dim, I) floats
-  float* asm_ = xs + a.xs_floats;  // attention tiles / combine weights
+  float* asm_ = reinterpret_cast<float*>(dsm + size_t(nst) * kStage);  // attention / merge
+  float* nw_s = asm_ + a.attn_floats;  // [h] the next rmsnorm weight vector
+  float* rope_s = nw_s + a.h;          // [D] cos, sin of the step's position
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -525,115 +841,111 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
   }
 
   // ---------------- consumers ----------------
-  unsigned int gen = 0;
-  if (threadIdx.x == 0) gen = ld_acquire(&a.bar[1]);
+  unsigned int target = 0;  // arrivals the last grid barrier waited for
   const StreamState& st = a.st;
   int pos = st.pos[0];
   int done = st.done[0];
   int n_gen = st.n_gen[0];
   uint32_t tok = st.token[0];
-  const int G = a.nq / a.nkv;
-  int it = 0, off = 0;
+  RingPos rp{0, 0, 0u};
+  int off = 0;
   bool ok = true;
-  XSeg x;  // this warp's K segment of the current phase's input
+  const int nph = a.L * 5 + 1;
   for (int step = 0; step < a.n_steps && ok && !done; ++step) {
+    unsigned long long* trs =
+        a.trace && step == 0 ? a.trace + size_t(blockIdx.x) * nph * kTraceWords : nullptr;
+    auto tslot = [&](int i) { return trs ? trs + i * kTraceWords : nullptr; };
+    // the first rmsnorm's weights and the RoPE row of this position
+    stage_vec(nw_s, a.layers[0].in_norm, a.h);
+    {
+      const int64_t rrow = pos < a.cap ? pos : a.cap - 1;  // the host keeps pos < cap
+      stage_vec(rope_s, a.rope_cos + rrow * (D / 2), D / 2);
+      stage_vec(rope_s + D / 2, a.rope_sin + rrow * (D / 2), D / 2);
+    }
     const bool append = pos < a.cap;
     const int n_ctx = append ? pos + 1 : pos;
     int chunk = (n_ctx + a.nsplit - 1) / a.nsplit;
     chunk = max(kTileF, (chunk + kTileF - 1) / kTileF * kTileF);
     const int n_used = (n_ctx + chunk - 1) / chunk;
-    for (int l = 0; l < a.L && ok; ++l) {
-      const FusedLayer& Lw = a.layers[l];
-      // ---- QKV: x (the embedding row at layer 0) -> rmsnorm -> Wqkv ----
-      {
-        const PhaseGeo g = geo(a, PH_QKV, l);
-        if (l == 0) {
-          const uint16_t* erow = a.embed + size_t(tok) * a.h;
-          for (int k = threadIdx.x; k < a.h; k += kCThreads) {
-            const float v = bf16f(erow[k]);
-            xs[k] = v;
-            if (blockIdx.x == 0) a.x[k] = v;
-          }
-        } else {
-          for (int k = threadIdx.x; k < a.h; k += kCThreads) xs[k] = ldcg(a.x + k);
-        }
+    // phases of the step: per layer QKV, ATTN, O, GU, DOWN; then HEAD
+    for (int p = 0; p < nph && ok; ++p) {
+      const int l = p / 5;
+      const int kind = p == a.L * 5 ? 5 : p % 5;
+      if (kind == 1) {
+        // ---- ATTN: (kv head, split) items; the last split of a head merges ----
+        AttnArgs aa;
+        aa.qkv = a.qkv;
+        aa.kc = a.layers[l].kc;
+        aa.vc = a.layers[l].vc;
+        aa.part = a.part;
+        aa.att = a.att;
+        aa.tickets = a.bar + kTicketBase;
+        aa.nq = a.nq;
+        aa.nkv = a.nkv;
+        aa.nsplit = a.nsplit;
+        aa.scale = a.scale;
+        for (int item = blockIdx.x; item < a.nkv * n_used; item += gridDim.x)
+          attn_item<D>(aa, item / n_used, item % n_used, chunk, n_ctx, n_used, asm_, S,
+                       item == int(blockIdx.x) ? tslot(p) : nullptr);
+        ok = grid_sync(a, target, S, tslot(p));
+        continue;
+      }
+      const int ph = kind == 0 ? PH_QKV : kind == 2 ? PH_O : kind == 3 ? PH_GU
+                   : kind == 4 ? PH_DOWN : PH_HEAD;
+      const int lw = ph == PH_HEAD ? 0 : l;
+      const PhaseGeo g = geo(a, ph, lw);
+      const int chunks = CH > 0 ? CH : g.chunks;
+      const int kbase = (warp % g.ks) * chunks * 256;
+      // the rmsnorm weights two phases ahead go to nw_s now (its last reader
+      // finished before the barrier just passed)
+      if (ph == PH_O) stage_vec(nw_s, a.layers[l].post_norm, a.h);
+      if (ph == PH_DOWN) stage_vec(nw_s, l + 1 < a.L ? a.layers[l + 1].in_norm : a.final_norm, a.h);
+      // the phase input, in registers: QKV rmsnorm(x) (the embedding row at
+      // layer 0), O att, GU rmsnorm(x), DOWN act, HEAD rmsnorm(x)
+      XSeg x;
+      if (ph == PH_QKV && l == 0) {
+        const uint16_t* erow = a.embed + size_t(tok) * a.h;
+        load_seg_bf16(x, erow, kbase, chunks, lane);
+        if (blockIdx.x == 0)
+          for (int k = threadIdx.x; k < a.h; k += kCThreads) a.x[k] = bf16f(erow[k]);
+      } else {
+        load_seg_l2(x, ph == PH_O ? a.att : ph == PH_DOWN ? a.act : a.x, kbase, chunks, lane);
+      }
+      if (ph == PH_QKV || ph == PH_GU || ph == PH_HEAD) {
+        cp_async_wait_all();
         csync();
-        norm_in_smem(xs, Lw.in_norm, a.h, a.eps, S);
-        load_seg(x, xs, false, (warp % g.ks) * g.chunks * 256, g.chunks, lane);
-        unsigned long long b = 0;
-        int nd = 0;
-        ok = gemv_phase<0>(g, x, a.qkv, off, it, nst, ring, S, b, nd);
-        off = int((off + g.ngroups) % gridDim.x);
-        ok = ok && grid_sync(a, gen, S);
+        norm_seg(x, nw_s, kbase, chunks, g.ks, a.h, a.eps, S);
       }
-      if (!ok) break;
-      // ---- ATTN: partials per (kv head, split) item ----
-      for (int item = blockIdx.x; item < a.nkv * n_used; item += gridDim.x)
-        attn_item<D>(a, Lw, item / n_used, item % n_used, chunk, n_ctx, pos, append, asm_, S);
-      ok = grid_sync(a, gen, S);
-      if (!ok) break;
-      // ---- O: combine -> Wo -> x += ----
-      {
-        const PhaseGeo g = geo(a, PH_O, l);
-        prefetch_residual(g, a.x, off, S);
-        combine<D>(a, n_used, xs, asm_, S);
-        load_seg(x, xs, false, (warp % g.ks) * g.chunks * 256, g.chunks, lane);
-        unsigned long long b = 0;
-        int nd = 0;
-        ok = gemv_phase<1>(g, x, a.x, off, it, nst, ring, S, b, nd);
-        apply_residual(g, a.x, off, nd, S);
-        off = int((off + g.ngroups) % gridDim.x);
-        ok = ok && grid_sync(a, gen, S);
-      }
-      if (!ok) break;
-      // ---- GU: rmsnorm(x) -> Wgate, Wup -> act ----
-      {
-        const PhaseGeo g = geo(a, PH_GU, l);
-        for (int k = threadIdx.x; k < a.h; k += kCThreads) xs[k] = ldcg(a.x + k);
-        csync();
-        norm_in_smem(xs, Lw.post_norm, a.h, a.eps, S);
-        load_seg(x, xs, false, (warp % g.ks) * g.chunks * 256, g.chunks, lane);
-        unsigned long long b = 0;
-        int nd = 0;
-        ok = gemv_phase<2>(g, x, a.act, off, it, nst, ring, S, b, nd);
-        off = int((off + g.ngroups) % gridDim.x);
-        ok = ok && grid_sync(a, gen, S);
-      }
-      if (!ok) break;
-      // ---- DOWN: act -> Wdown -> x += ----
-      {
-        const PhaseGeo g = geo(a, PH_DOWN, l);
-        prefetch_residual(g, a.x, off, S);
-        load_seg(x, a.act, true, (warp % g.ks) * g.chunks * 256, g.chunks, lane);
-        unsigned long long b = 0;
-        int nd = 0;
-        ok = gemv_phase<1>(g, x, a.x, off, it, nst, ring, S, b, nd);
-        apply_residual(g, a.x, off, nd, S);
-        off = int((off + g.ngroups) % gridDim.x);
-        ok = ok && grid_sync(a, gen, S);
-      }
-    }
-    if (!ok) break;
-    // ---- HEAD: final rmsnorm -> LM head -> logits, argmax ----
-    {
-      const PhaseGeo g = geo(a, PH_HEAD, 0);
-      for (int k = threadIdx.x; k < a.h; k += kCThreads) xs[k] = ldcg(a.x + k);
-      csync();
-      norm_in_smem(xs, a.final_norm, a.h, a.eps, S);
-      load_seg(x, xs, false, (warp % g.ks) * g.chunks * 256, g.chunks, lane);
+      unsigned long long* tp = tslot(p);
+      if (tp && threadIdx.x == 0) tp[4] = global_ns();
+      const bool imm = ph == PH_HEAD && g.ks == 1;
       unsigned long long best = 0;
-      int nd = 0;
-      ok = gemv_phase<3>(g, x, a.logits, off, it, nst, ring, S, best, nd);
-      off = int((off + g.ngroups) % gridDim.x);
-      best = warp_max_u64(best);
-      if (lane == 0) S.best[warp] = best;
-      csync();
-      if (threadIdx.x == 0) {
-        unsigned long long bb = 0;
-        for (int w = 0; w < kCWarps; ++w) bb = S.best[w] > bb ? S.best[w] : bb;
-        a.am_part[blockIdx.x] = bb;
+      const int nloc = gemv_phase(g, chunks, x, off, rp, nst, ring, S, imm, a.logits, best, tp);
+      if (tp && threadIdx.x == 0) {
+        tp[5] = global_ns();
+        tp[7] = nloc;
       }
-      ok = ok && grid_sync(a, gen, S);
+      if (!imm) {
+        csync();
+        switch (ph) {
+          case PH_QKV: epi_qkv(a, a.layers[lw], g, off, nloc, pos, append, rope_s, S); break;
+          case PH_GU: epi_swiglu(a.act, g, off, nloc, S); break;
+          case PH_HEAD: epi_head(a.logits, g, off, nloc, S, best); break;
+          default: epi_residual(a.x, g, off, nloc, S); break;
+        }
+      }
+      off = int((off + g.ngroups) % gridDim.x);
+      if (ph == PH_HEAD) {
+        best = warp_max_u64(best);
+        if (lane == 0) S.best[warp] = best;
+        csync();
+        if (threadIdx.x == 0) {
+          unsigned long long bb = 0;
+          for (int w = 0; w < kCWarps; ++w) bb = S.best[w] > bb ? S.best[w] : bb;
+          a.am_part[blockIdx.x] = bb;
+        }
+      }
+      ok = grid_sync(a, target, S, tslot(p));
     }
     if (!ok) break;
     // every CTA reduces the argmax partials: the same token everywhere
@@ -669,82 +981,120 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
       }
     }
   }
-  // The stream stops here.  When generation ended early (EOS) the producer
-  // has issued stages ahead: tell it to stop, then consume (wait for and
-  // release) every stage it issued, so no copy is in flight when the CTA
-  // exits.  In the normal case it has issued exactly what was consumed.
+  // The stream stops here.  When generation ended early (EOS) or a wait gave
+  // up, the producer may have issued stages nobody consumed: tell it to
+  // stop, keep releasing what it issued until it has stopped, then wait for
+  // the copies of the last nst issued stages (the only ones that can still
+  // be in flight), so no copy lands after the CTA exits.
   if (threadIdx.x == 0) S.abort = 1;
   {
     const unsigned long long t0 = global_ns();
     for (;;) {
       const int pdone = S.prod_done;
       const int issued = S.issued;
-      if (it < issued) {
-        const int s = it % nst;
-        mbar_wait(&S.full[s], (it / nst) & 1);
+      if (rp.it < issued) {
+        mbar_wait(&S.full[rp.s], rp.par);
         __syncwarp();
-        if (lane == 0) mbar_arrive(&S.empty[s]);
-        ++it;
+        if (lane == 0) mbar_arrive(&S.empty[rp.s]);
+        rp.next(nst);
       } else if (pdone || global_ns() - t0 > kWaitNs) {
         break;
       }
     }
   }
-  (void)G;
+  csync();
+  if (threadIdx.x == 0) {
+    const int issued = S.issued;
+    for (int j = max(0, issued - nst); j < issued; ++j) mbar_wait(&S.full[j % nst], (j / nst) & 1);
+  }
 }
 
-}  // namespace
+template <int D, int CH>
+cudaError_t prepare_one() {
+  cudaFuncAttributes fa{};
+  TMG_CUDA_TRY(cudaFuncGetAttributes(&fa, decode_fused_kernel<D, CH>));
+  if (fa.sharedSizeBytes > kStaticReserve) return cudaErrorInvalidConfiguration;
+  int dev = 0, optin = 0;
+  TMG_CUDA_TRY(cudaGetDevice(&dev));
+  TMG_CUDA_TRY(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+  return set_carveout(decode_fused_kernel<D, CH>, optin - int(fa.sharedSizeBytes));
+}
 
-namespace {
+int ksplit_host(int K) {
+  int ks = 1;
+  while (K / ks > 2048) ks *= 2;
+  return ks;
+}
+
 // K is split over 1, 2, 4 or 8 warps so that a warp's segment is a whole
 // number of 256-element chunks, at most 2048 elements.
 bool seg_ok(int K) {
-  int ks = 1;
-  while (K / ks > 2048) ks *= 2;
+  const int ks = ksplit_host(K);
   return ks <= 8 && K % (ks * 256) == 0;
 }
-}  // namespace
 
-bool fused_supported(int h, int q_dim, int I, int d, int G) {
-  return seg_ok(h) && seg_ok(q_dim) && seg_ok(I) && (d == 64 || d == 128) && G >= 1 && G <= 8 &&
-         G * d <= 4 * kCThreads;
+// Groups one CTA takes in a phase of ngroups groups (deferred phases hold
+// one result per warp and group in shared memory).
+bool local_ok(int64_t ngroups, int num_sms) {
+  return (ngroups + num_sms - 1) / num_sms <= kMaxLocal;
 }
 
-// Dynamic shared memory: the ring (as many 32 KB stages as fit, <= 6), x
-// staging (max(h, q_dim) floats), and the attention tiles or the combine's
-// weights (n_q * (nsplit + 1) floats), whichever is larger.
-size_t fused_smem(int h, int q_dim, int nq, int d, int G, int nsplit, int* nst_out) {
-  const size_t xs = size_t(std::max(h, q_dim)) * 4;
+}  // namespace
+
+bool fused_supported(int h, int nq, int nkv, int d, int I, int64_t V, int num_sms) {
+  if (nkv <= 0 || nq % nkv != 0 || nkv > kBarWords - kTicketBase) return false;
+  const int G = nq / nkv, q_dim = nq * d;
+  if (!(seg_ok(h) && seg_ok(q_dim) && seg_ok(I) && (d == 64 || d == 128) && G >= 1 && G <= 8 &&
+        G * d <= 4 * kCThreads))
+    return false;
+  // QKV groups hold rpc/2 rows from each RoPE half of a head
+  const int rpc_h = kCWarps / ksplit_host(h);
+  if (rpc_h < 2 || d % rpc_h != 0 || (d / 2) % (rpc_h / 2) != 0) return false;
+  const int rpc_q = kCWarps / ksplit_host(q_dim), rpc_i = kCWarps / ksplit_host(I);
+  return local_ok(int64_t(nq + 2 * nkv) * d / rpc_h, num_sms) &&
+         local_ok((h + rpc_q - 1) / rpc_q, num_sms) &&
+         local_ok((I + rpc_h / 2 - 1) / (rpc_h / 2), num_sms) &&
+         local_ok((h + rpc_i - 1) / rpc_i, num_sms) &&
+         (ksplit_host(h) == 1 || local_ok((V + rpc_h - 1) / rpc_h, num_sms));
+}
+
+int fused_bar_words() { return kBarWords; }
+
+// Dynamic shared memory: the ring (as many 32 KB stages as fit, at most
+// max_stages or 6), the attention tiles or the merge's arrays (whichever is
+// larger; *attn_floats), one rmsnorm weight vector (h) and a RoPE row (d).
+size_t fused_smem(int h, int d, int G, int nsplit, int max_stages, int* nst_out, int* attn_floats) {
   const size_t att = std::max<size_t>(
       size_t(G) * d + size_t(kTileF) * (d + 4) + size_t(kTileF) * d + size_t(G) * kTileF,
-      size_t(nq) * (nsplit + 1)) * 4;
-  const size_t budget = 227 * 1024 - sizeof(Shared) - 1024;
-  int nst = budget > xs + att ? int((budget - xs - att) / kStage) : 0;
-  nst = std::min(nst, kMaxStagesF);
+      size_t(G) * (3 * size_t(nsplit) + 1));
+  *attn_floats = int((att + 3) / 4 * 4);  // keep what follows 16-byte aligned
+  const size_t rest = (size_t(*attn_floats) + h + d) * 4;
+  // the kernel's static shared memory and the 1 KB alignment slack of the
+  // dynamic segment come out of the 227 KB
+  const size_t budget = 227 * 1024 - kStaticReserve - 1024;
+  int nst = budget > rest ? int((budget - rest) / kStage) : 0;
+  nst = std::min(nst, max_stages > 0 ? std::min(max_stages, kMaxStagesF) : kMaxStagesF);
   *nst_out = nst;
-  return size_t(nst) * kStage + xs + att;
+  return size_t(nst) * kStage + rest;
 }
 
 cudaError_t fused_prepare() {
-  const int max_smem = 227 * 1024 - int(sizeof(Shared));
-  TMG_CUDA_TRY(set_carveout(decode_fused_kernel<64>, max_smem));
-  return set_carveout(decode_fused_kernel<128>, max_smem);
+  TMG_CUDA_TRY((prepare_one<64, 0>()));
+  TMG_CUDA_TRY((prepare_one<64, 8>()));
+  TMG_CUDA_TRY((prepare_one<128, 0>()));
+  return prepare_one<128, 8>();
 }
 
-cudaError_t launch_decode_fused(const FusedArgs& a, int num_sms, cudaStream_t s) {
+cudaError_t launch_decode_fused(const FusedArgs& args, int num_sms, cudaStream_t s) {
+  FusedArgs a = args;
   int nst = 0;
   const int G = a.nq / a.nkv;
-  const size_t smem = fused_smem(a.h, a.nq * a.d, a.nq, a.d, G, a.nsplit, &nst);
-  if (nst < 2 || a.xs_floats < std::max(a.h, a.nq * a.d)) return cudaErrorInvalidValue;
-  // rows of the residual one CTA updates in the o and down phases must fit
-  // the deferred-update arrays
-  for (int K : {a.nq * a.d, a.I}) {
-    int ks = 1;
-    while (K / ks > 2048) ks *= 2;
-    const int64_t rpg = kCWarps / ks;
-    const int64_t groups = (a.h + rpg - 1) / rpg;
-    if ((groups + num_sms - 1) / num_sms * rpg > kMaxDefer) return cudaErrorInvalidValue;
-  }
+  const size_t smem = fused_smem(a.h, a.d, G, a.nsplit, a.max_stages, &nst, &a.attn_floats);
+  if (nst < 2 || !a.att || a.pf_ahead < 0) return cudaErrorInvalidValue;
+  const bool ch8 = a.h / ksplit_host(a.h) == 2048 && (a.nq * a.d) / ksplit_host(a.nq * a.d) == 2048 &&
+                   a.I / ksplit_host(a.I) == 2048;
+  // the grid barrier counts from zero in every launch
+  TMG_CUDA_TRY(cudaMemsetAsync(a.bar, 0, 4 * sizeof(unsigned int), s));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(num_sms);
   cfg.blockDim = dim3(kFThreads);
@@ -755,8 +1105,12 @@ cudaError_t launch_decode_fused(const FusedArgs& a, int num_sms, cudaStream_t s)
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (a.d == 64) return cudaLaunchKernelEx(&cfg, decode_fused_kernel<64>, a, nst);
-  if (a.d == 128) return cudaLaunchKernelEx(&cfg, decode_fused_kernel<128>, a, nst);
+  if (a.d == 64)
+    return ch8 ? cudaLaunchKernelEx(&cfg, decode_fused_kernel<64, 8>, a, nst)
+               : cudaLaunchKernelEx(&cfg, decode_fused_kernel<64, 0>, a, nst);
+  if (a.d == 128)
+    return ch8 ? cudaLaunchKernelEx(&cfg, decode_fused_kernel<128, 8>, a, nst)
+               : cudaLaunchKernelEx(&cfg, decode_fused_kernel<128, 0>, a, nst);
   return cudaErrorInvalidValue;
 }
 

@@ -34,19 +34,31 @@ struct FusedArgs {
   float* x = nullptr;       // [h] residual
   float* qkv = nullptr;     // [(nq + 2 nkv) d]
   float* part = nullptr;    // [nkv, nsplit, G, d + 2] attention partials
+  float* att = nullptr;     // [nq d] attention output
   float* act = nullptr;     // [I]
   float* logits = nullptr;  // [V]
   unsigned long long* am_part = nullptr;  // [grid]
-  unsigned int* bar = nullptr;            // [0] arrivals, [1] generation, [2] abort
+  // fused_bar_words() words: [0] barrier arrivals, [2] abort, [64 + kv head]
+  // attention tickets (zero between launches)
+  unsigned int* bar = nullptr;
   int nsplit = 1;
-  int xs_floats = 0;  // max(h, nq d)
+  int pf_ahead = 0;    // stages of L2 prefetch beyond the ring
+  int max_stages = 0;  // cap on the ring's stages (0: as many as fit)
+  int attn_floats = 0; // set by the launcher: attention region of shared memory
   StreamState st{};
   int n_steps = 0;
   int32_t* err = nullptr;
+  // diagnostics: [grid][L * 5 + 1][12] records of the first step per CTA
+  // and phase (globaltimer ns: work done, barrier passed, producer's first
+  // and last issue, input ready, GEMV done, first stage ready; the group
+  // count; SM cycles of stage waits and math of consumer warp 0, of free-
+  // stage waits and issue work of the producer), or null
+  unsigned long long* trace = nullptr;
 };
 
-bool fused_supported(int h, int q_dim, int I, int d, int G);
-size_t fused_smem(int h, int q_dim, int nq, int d, int G, int nsplit, int* nst_out);
+bool fused_supported(int h, int nq, int nkv, int d, int I, int64_t V, int num_sms);
+int fused_bar_words();
+size_t fused_smem(int h, int d, int G, int nsplit, int max_stages, int* nst_out, int* attn_floats);
 cudaError_t fused_prepare();
 // Cooperative launch: one CTA per SM (num_sms CTAs).
 cudaError_t launch_decode_fused(const FusedArgs& a, int num_sms, cudaStream_t s);

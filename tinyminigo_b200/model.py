@@ -287,6 +287,16 @@ class Model:
         names = ["qkv_gemv", "attn_decode", "o_gemv", "gateup_gemv", "down_gemv", "lm_head"]
         return [(names[kinds[i]], *[int(v) for v in out[i]]) for i in range(n.value)]
 
+    def trace_fused(self, token: int, cache: "KvCache", n_ctas_max: int = 1024) -> np.ndarray:
+        """One greedy step of the fused decode kernel with timestamps:
+        [n_ctas, 5 L + 1, 12] per CTA and phase (see tmg_trace_fused)."""
+        nph = self.config.num_hidden_layers * 5 + 1
+        out = np.zeros(n_ctas_max * nph * 12, np.uint64)
+        n = ctypes.c_int32(0)
+        check(lib().tmg_trace_fused(self._h, cache._h, int(token), _ptr(out), out.size,
+                                    ctypes.byref(n)), self._h, "trace_fused")
+        return out[: n.value * nph * 12].reshape(n.value, nph, 12)
+
 
 class KvCache:
     """KvCache (src/model.rs:250-332) on the device: per layer and stream an
