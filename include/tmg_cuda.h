@@ -258,6 +258,18 @@ int tmg_op_swiglu(tmg_ctx* ctx, const float* gate, const float* up, int64_t n, f
  * n_ctx cached rows of [n_kv * head_dim] (keys already rotated). */
 int tmg_op_attn_decode(tmg_ctx* ctx, const float* q, const float* keys, const float* values,
                        int64_t n_ctx, int32_t n_q, int32_t n_kv, int32_t head_dim, float* out);
+/* The same decode attention as tmg_op_attn_decode (same split count, same
+ * results), for callers that may not allocate device memory at call time.
+ * No counterpart in the reference.  It allocates nothing: partials,
+ * tickets and the position word live in a 4 MiB static per-device scratch
+ * (requests needing more return TMG_ERR_CAPACITY before enqueuing
+ * anything).  It only enqueues on the context's stream (results are ready
+ * after tmg_sync).  The first call on a device sets the scratch up and
+ * should precede any stream capture.  Calls that overlap on one device race
+ * on the shared scratch: order them. */
+int tmg_op_attn_decode_noalloc(tmg_ctx* ctx, const float* q, const float* keys,
+                               const float* values, int64_t n_ctx, int32_t n_q, int32_t n_kv,
+                               int32_t head_dim, float* out);
 /* attention_batch, src/tensor.rs:1099-1139: T causal query rows at
  * start_pos.. over [start_pos + T, n_kv * head_dim] cached rows. */
 int tmg_op_attn_prefill(tmg_ctx* ctx, const float* q, const float* keys, const float* values,

@@ -107,6 +107,7 @@ SIGNATURES = {
     "tmg_op_rope": (_I, [_P, _P, _I64, _I32, _I32, _I64, _F]),
     "tmg_op_swiglu": (_I, [_P, _P, _P, _I64, _P]),
     "tmg_op_attn_decode": (_I, [_P, _P, _P, _P, _I64, _I32, _I32, _I32, _P]),
+    "tmg_op_attn_decode_noalloc": (_I, [_P, _P, _P, _P, _I64, _I32, _I32, _I32, _P]),
     "tmg_op_attn_prefill": (_I, [_P, _P, _P, _P, _I64, _I64, _I32, _I32, _I32, _P]),
     "tmg_op_argmax": (_I, [_P, _P, _I64, _I32, _P]),
     "tmg_op_sample": (_I, [_P, _P, _I64, _I32, _P, _I64, _F, _I64, _F, _F, _P, _P, _P, _P, _P]),

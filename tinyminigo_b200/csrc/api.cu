@@ -1680,6 +1680,22 @@ int tmg_op_attn_decode(tmg_ctx* c, const float* q, const float* keys, const floa
   return TMG_OK;
 }
 
+int tmg_op_attn_decode_noalloc(tmg_ctx* c, const float* q, const float* keys, const float* values,
+                               int64_t n_ctx, int32_t n_q, int32_t n_kv, int32_t head_dim,
+                               float* out) {
+  if (!c || !q || !keys || !values || !out || n_ctx <= 0 || n_q <= 0 || n_kv <= 0 ||
+      n_q % n_kv || head_dim <= 0 || head_dim % 8)
+    return fail(c, TMG_ERR_INVALID, "bad argument");
+  cudaSetDevice(c->device);
+  std::string why;
+  const int r = attn_decode_noalloc(c->device, c->num_sms, c->stream, q, keys, values, n_ctx, n_q,
+                                    n_kv, head_dim, out, &why);
+  if (r == 2) return fail(c, TMG_ERR_CAPACITY, "tmg_op_attn_decode_noalloc: " + why);
+  if (r == 1) return fail(c, TMG_ERR_INVALID, "tmg_op_attn_decode_noalloc: " + why);
+  if (r != 0) return fail(c, TMG_ERR_CUDA, "tmg_op_attn_decode_noalloc: " + why);
+  return TMG_OK;
+}
+
 int tmg_op_attn_prefill(tmg_ctx* c, const float* q, const float* keys, const float* values,
                         int64_t T, int64_t start_pos, int32_t n_q, int32_t n_kv, int32_t head_dim,
                         float* out) {

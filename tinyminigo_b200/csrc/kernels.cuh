@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <string>
+
 namespace tmg {
 
 constexpr int kMaxStreams = 16;  // streams batched in one decode step
@@ -132,6 +134,12 @@ struct AttnDecodeArgs {
 };
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);
 int attn_decode_nsplit(int nkv, int M, int64_t cap, int num_sms);
+// Decode attention on the static per-device scratch (attn_noalloc.cu):
+// enqueues on s, allocates nothing.  0 = enqueued; 1 bad device, 2 too
+// large for the scratch, 3 CUDA error; *why says which.
+int attn_decode_noalloc(int device, int num_sms, cudaStream_t s, const float* q, const float* keys,
+                        const float* values, int64_t n_ctx, int n_q, int n_kv, int head_dim,
+                        float* out, std::string* why);
 
 // ---------------------------------------------------------------------------
 // Prefill pieces.
