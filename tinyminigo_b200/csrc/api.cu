@@ -78,6 +78,7 @@ struct tmg_ctx {
   int32_t* d_err = nullptr;
   float* logits_full = nullptr;  // [M, V] gathered logits under TP
   unsigned int* bar = nullptr;   // grid barrier of the fused decode kernel
+  unsigned long long* ll = nullptr;  // its tagged exchange words (x, att, act, qkv)
   int fused_pf = 0;              // its L2 prefetch distance (stages; TMG_FUSED_PF)
   int fused_stages = 0;          // its ring depth cap (0: all that fit; TMG_FUSED_STAGES)
   bool fused_ok = false;         // the fused batch-1 decode kernel takes this shape
@@ -119,6 +120,7 @@ struct tmg_kv {
   int64_t dec_cap = 0;
   int32_t* h_state = nullptr;  // pinned staging of the state block
   FusedLayer* d_layers = nullptr;  // per-layer pointers for the fused kernel (stream 0)
+  unsigned long long* part_ll = nullptr;  // its tagged attention partials
   cudaEvent_t state_ev = nullptr;  // the last upload from h_state
   std::vector<void*> allocs;
 };
@@ -388,6 +390,7 @@ int alloc_model(tmg_ctx* c) {
   CK(dalloc(c->allocs, &c->sm_part, size_t(M) * 64 * kMaxTopK), "alloc scratch");
   CK(dalloc(c->allocs, &c->tickets, 64), "alloc scratch");
   CK(zero_sync(c, c->tickets, 64 * sizeof(unsigned int)), "memset");
+  CK(dalloc(c->allocs, &c->ll, fused_ll_words(h, c->nq * c->d, c->I, c->qkv_rows)), "alloc scratch");
   CK(dalloc(c->allocs, &c->bar, fused_bar_words()), "alloc scratch");
   CK(zero_sync(c, c->bar, fused_bar_words() * sizeof(unsigned int)), "memset");
   c->fused_ok = c->world == 1 && fused_supported(c->h, c->nq, c->nkv, c->d, c->I, c->V_l, c->num_sms);
@@ -787,11 +790,14 @@ cudaError_t launch_fused(tmg_ctx* c, tmg_kv* kv, const StreamState& st, int64_t 
   f.rope_cos = kv->rope_cos;
   f.rope_sin = kv->rope_sin;
   f.cap = kv->cap;
-  f.x = c->x;
-  f.qkv = c->qkv;
-  f.part = kv->part;
-  f.att = c->attn;
-  f.act = c->act;
+  const int q_dim = c->nq * c->d;
+  f.ll_base = c->ll;
+  f.ll_bytes = fused_ll_words(c->h, q_dim, c->I, c->qkv_rows) * sizeof(unsigned long long);
+  f.x_ll = c->ll;
+  f.att_ll = f.x_ll + c->h;
+  f.act_ll = f.att_ll + q_dim;
+  f.qkv_ll = f.act_ll + c->I;
+  f.part_ll = kv->part_ll;
   f.logits = c->logits;
   f.am_part = c->am_part;
   f.bar = c->bar;
@@ -805,7 +811,7 @@ cudaError_t launch_fused(tmg_ctx* c, tmg_kv* kv, const StreamState& st, int64_t 
   return launch_decode_fused(f, c->num_sms, c->stream);
 }
 
-bool use_fused(tmg_ctx* c, tmg_kv* kv) { return c->fused_ok && kv->M == 1 && kv->d_layers; }
+bool use_fused(tmg_ctx* c, tmg_kv* kv) { return c->fused_ok && kv->M == 1 && kv->d_layers && kv->part_ll; }
 
 // The generate loop for all streams of kv (model.rs:614-663).
 int run_generate(tmg_ctx* c, tmg_kv* kv, const uint32_t* prompts, int64_t T,
@@ -1217,6 +1223,8 @@ int tmg_kv_create(tmg_ctx* c, int32_t n_streams, int64_t capacity, tmg_kv** out)
     if ((e = copy_sync(c, kv->d_layers, fl.data(), fl.size() * sizeof(FusedLayer),
                        cudaMemcpyHostToDevice)) != cudaSuccess)
       return bail(e);
+    const size_t pw = size_t(c->nkv) * kv->nsplit * (c->nq / c->nkv) * (c->d + 2);
+    if ((e = dalloc(kv->allocs, &kv->part_ll, pw)) != cudaSuccess) return bail(e);
   }
   const int G = c->nq / c->nkv;
   if ((e = dalloc(kv->allocs, &kv->part, size_t(n_streams) * c->nkv * kv->nsplit * G * (c->d + 2))) != cudaSuccess) return bail(e);

@@ -47,13 +47,21 @@ namespace {
 
 constexpr int kCWarps = 8;                         // consumer warps
 constexpr int kCThreads = kCWarps * kWarp;         // 256
-constexpr int kFThreads = kCThreads + kWarp;       // + producer warp
+constexpr int kFThreads = kCThreads + 4 * kWarp;   // + the producer's warpgroup
+// Registers per thread: the launch gives every thread kLaunchRegs (65536 /
+// 384, rounded down to the allocation unit); the producer's warpgroup (one
+// working warp, three idle) then gives registers back and the two consumer
+// warpgroups take them: 128 * 56 + 256 * 224 = 64512 = 384 * 168.
+constexpr int kLaunchRegs = 168;
+constexpr int kProducerRegs = 56;
+constexpr int kConsumerRegs = 224;
+static_assert(4 * kWarp * kProducerRegs + 2 * 4 * kWarp * kConsumerRegs <= kFThreads * kLaunchRegs,
+              "register split exceeds the launch's registers");
 constexpr int kStage = 32 * 1024;                  // ring stage bytes
 constexpr int kMaxStagesF = 6;
 constexpr int kTileF = 32;                         // attention positions per tile
 constexpr int kMaxRes = 1024;                      // per-warp results of one phase
 constexpr int kMaxLocal = kMaxRes / kCWarps;       // groups of one CTA in a phase
-constexpr int kTicketBase = 64;                    // bar[64 + kv head]: attention tickets
 constexpr int kBarWords = 128;                     // words of the barrier block
 constexpr int kTraceWords = 12;                    // trace record per CTA and phase
 
@@ -61,11 +69,6 @@ enum Phase : int { PH_QKV = 0, PH_O = 1, PH_GU = 2, PH_DOWN = 3, PH_HEAD = 4 };
 
 __device__ __forceinline__ void csync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kCThreads) : "memory");
-}
-
-__device__ __forceinline__ float ldcg(const float* p) { return __ldcg(p); }
-__device__ __forceinline__ float4 ldcg4(const float* p) {
-  return __ldcg(reinterpret_cast<const float4*>(p));
 }
 
 __device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
@@ -246,7 +249,7 @@ struct Shared {
   float ssq[kCWarps];
   unsigned long long best[kCWarps];
   float m_s[8], l_s[8], alpha_s[8];
-  int flag;
+  int fail[2];  // a poll gave up (indexed by the parity of the poll count)
   int gen_ok;
   volatile int abort;      // stop issuing / waiting (error or early end)
   volatile int issued;     // producer: stages issued so far
@@ -400,33 +403,157 @@ __device__ void producer(const FusedArgs& a, Shared& S, uint8_t* ring, int nst) 
 }
 
 // ---------------------------------------------------------------------------
+// Flag-in-data exchange between CTAs.  Every activation that crosses CTAs
+// inside a step (x after O and after DOWN, the rotated q/k/v of the
+// position, the attention partials and output, act) travels as 8-byte
+// words {value, tag} written with one relaxed 64-bit store; a reader polls
+// the words it needs until each carries the tag of the phase that writes
+// it.  A 64-bit access is single-copy atomic, so a matching tag comes with
+// its value, and neither a fence nor a barrier sits between producer and
+// consumer.  Tags number the phases of a launch from 1 (the host zeroes the
+// buffers before each launch).  A buffer is written again only after a
+// chain of phases that needs every CTA to have finished reading it (every
+// CTA owns groups in every GEMV phase), so a reader never misses its tag.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void ll_store(unsigned long long* p, float v, uint32_t tag) {
+  const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ ulonglong2 ll_load2(const unsigned long long* p) {
+  ulonglong2 r;
+  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];"
+               : "=l"(r.x), "=l"(r.y)
+               : "l"(p)
+               : "memory");
+  return r;
+}
+
+constexpr int kGatherPairs = 16;                            // word pairs per thread
+constexpr unsigned a_backoff_ns = 100;                      // pause between polls
+constexpr int kMaxGather = kGatherPairs * 2 * kCThreads;   // 8192 words
+
+// All consumer threads: wait until src[0..n) (n even, <= kMaxGather) carry
+// `tag`, then copy the values to dst in shared memory.  Returns false, in
+// every thread alike, when a wait gave up or the kernel is aborting; `gc`
+// counts the polls (the failure flag alternates slots so that a slow reader
+// of one poll never sees the next poll's flag).
+__device__ __noinline__ bool ll_gather(float* dst, const unsigned long long* src, int n, uint32_t tag,
+                          const unsigned int* abort_word, Shared& S, uint32_t& gc) {
+  ulonglong2 v[kGatherPairs];
+  uint32_t need = 0;  // bit k: pair k still to come
+#pragma unroll
+  for (int k = 0; k < kGatherPairs; ++k) {
+    const int i = (threadIdx.x + k * kCThreads) * 2;
+    if (i < n) {
+      v[k] = ll_load2(src + i);
+      need |= 1u << k;
+    }
+  }
+  const unsigned long long t0 = global_ns();
+  unsigned int spins = 0;
+  bool ok = true;
+  for (;;) {
+#pragma unroll
+    for (int k = 0; k < kGatherPairs; ++k) {
+      if ((need >> k) & 1u) {
+        if (uint32_t(v[k].x >> 32) == tag && uint32_t(v[k].y >> 32) == tag) {
+          const int i = (threadIdx.x + k * kCThreads) * 2;
+          dst[i] = __uint_as_float(uint32_t(v[k].x));
+          dst[i + 1] = __uint_as_float(uint32_t(v[k].y));
+          need &= ~(1u << k);
+        }
+      }
+    }
+    if (!need) break;
+    if ((++spins & 15) == 0 && (ld_acquire(abort_word) != 0 || global_ns() - t0 > kWaitNs)) {
+      ok = false;
+      break;
+    }
+    // back off a little: 148 CTAs re-reading the same lines load L2
+    __nanosleep(a_backoff_ns);
+#pragma unroll
+    for (int k = 0; k < kGatherPairs; ++k)
+      if ((need >> k) & 1u) v[k] = ll_load2(src + (threadIdx.x + k * kCThreads) * 2);
+  }
+  const int slot = gc & 1;
+  ++gc;
+  if (!ok || (threadIdx.x == 0 && S.abort)) S.fail[slot] = 1;
+  csync();
+  return S.fail[slot] == 0;
+}
+
+// Up to three short ranges (each at most 2 kCThreads words, even) gathered
+// in one poll, as ll_gather.
+struct LLRange {
+  float* dst;
+  const unsigned long long* src;
+  int n;
+};
+__device__ __noinline__ bool ll_gather3(const LLRange* r, int nr, uint32_t tag,
+                                        const unsigned int* abort_word, Shared& S, uint32_t& gc) {
+  ulonglong2 v[3];
+  uint32_t need = 0;
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    if (k < nr && threadIdx.x * 2 < r[k].n) {
+      v[k] = ll_load2(r[k].src + threadIdx.x * 2);
+      need |= 1u << k;
+    }
+  }
+  const unsigned long long t0 = global_ns();
+  unsigned int spins = 0;
+  bool ok = true;
+  for (;;) {
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      if (((need >> k) & 1u) && uint32_t(v[k].x >> 32) == tag && uint32_t(v[k].y >> 32) == tag) {
+        r[k].dst[threadIdx.x * 2] = __uint_as_float(uint32_t(v[k].x));
+        r[k].dst[threadIdx.x * 2 + 1] = __uint_as_float(uint32_t(v[k].y));
+        need &= ~(1u << k);
+      }
+    }
+    if (!need) break;
+    if ((++spins & 15) == 0 && (ld_acquire(abort_word) != 0 || global_ns() - t0 > kWaitNs)) {
+      ok = false;
+      break;
+    }
+    __nanosleep(a_backoff_ns);
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+      if ((need >> k) & 1u) v[k] = ll_load2(r[k].src + threadIdx.x * 2);
+  }
+  const int slot = gc & 1;
+  ++gc;
+  if (!ok || (threadIdx.x == 0 && S.abort)) S.fail[slot] = 1;
+  csync();
+  return S.fail[slot] == 0;
+}
+
+// Give up: raise the kernel-wide abort word and the error word.
+__device__ __forceinline__ void raise_abort(const FusedArgs& a) {
+  if (threadIdx.x == 0) {
+    atomicExch(a.bar + 2, 1u);
+    if (a.err) atomicExch(a.err, 2);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Consumers
 // ---------------------------------------------------------------------------
 struct XSeg {
   float4 a[8], b[8];
 };
 
-// This warp's K segment of the phase input, from f32 activations (via L2)
-// or from a BF16 row (the embedding, widened exactly).
-__device__ __forceinline__ void load_seg_l2(XSeg& x, const float* src, int kbase, int chunks,
-                                            int lane) {
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    if (c < chunks) {
-      const int k = kbase + c * 256 + lane * 8;
-      x.a[c] = ldcg4(src + k);
-      x.b[c] = ldcg4(src + k + 4);
-    }
-  }
-}
-__device__ __forceinline__ void load_seg_bf16(XSeg& x, const uint16_t* src, int kbase, int chunks,
+// This warp's K segment of the phase input from shared memory, or from a
+// BF16 row in global memory (the embedding, widened exactly).
+__device__ __forceinline__ void load_seg_smem(XSeg& x, const float* src, int kbase, int chunks,
                                               int lane) {
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
     if (c < chunks) {
-      const uint4 u = *reinterpret_cast<const uint4*>(src + kbase + c * 256 + lane * 8);
-      x.a[c] = make_float4(bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y));
-      x.b[c] = make_float4(bf16lo(u.z), bf16hi(u.z), bf16lo(u.w), bf16hi(u.w));
+      const int k = kbase + c * 256 + lane * 8;
+      x.a[c] = *reinterpret_cast<const float4*>(src + k);
+      x.b[c] = *reinterpret_cast<const float4*>(src + k + 4);
     }
   }
 }
@@ -474,10 +601,6 @@ __device__ __forceinline__ void norm_seg(XSeg& x, const float* w, int kbase, int
   }
 }
 
-// One GEMV phase over this CTA's groups: each warp dots its slot/segment of
-// every stage.  imm (LM head with ks == 1): logits and the argmax candidate
-// directly; otherwise the sums go to S.res for the phase's epilogue.
-// Returns the number of local groups.
 // Position in the stage ring: stage count, slot, phase parity.
 struct RingPos {
   int it, s;
@@ -491,23 +614,33 @@ struct RingPos {
   }
 };
 
-__device__ __forceinline__ int gemv_phase(const PhaseGeo& g, int chunks, const XSeg& x, int off,
-                                          RingPos& rp, int nst, const uint8_t* ring, Shared& S,
-                                          bool imm, float* logits, unsigned long long& best,
-                                          unsigned long long* tw) {
+// One GEMV phase over this CTA's groups: the
+// warp's K segment of the input from shared memory (src), rmsnorm'd with nw
+// when given; then each warp dots its slot/segment of every stage.  imm (LM
+// head with ks == 1): logits and the argmax candidate directly; otherwise
+// the sums go to S.res for the phase's epilogue.  Returns the number of
+// local groups; tw (diagnostics) receives the first stage's arrival time.
+__device__ __forceinline__ int gemv_block(int64_t ngroups, int K, int ks, int rpg, int64_t N,
+                                       int chunks, const float* src, const float* nw, float eps,
+                                       int n_norm, int off, RingPos& rp_io, int nst,
+                                       const uint8_t* ring, Shared& S, bool imm, float* logits,
+                                       unsigned long long& best_io, unsigned long long* tw) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int slot = warp / g.ks;
-  const int kbase = (warp % g.ks) * chunks * 256;
+  const int slot = warp / ks;
+  const int kbase = (warp % ks) * chunks * 256;
+  XSeg x;
+  load_seg_smem(x, src, kbase, chunks, lane);
+  if (nw) norm_seg(x, nw, kbase, chunks, ks, n_norm, eps, S);
+  RingPos rp = rp_io;
+  unsigned long long best = best_io;
   // this lane's first weight element in stage 0
-  const uint16_t* wbase = reinterpret_cast<const uint16_t*>(ring + size_t(slot) * g.K * 2) + kbase + lane * 8;
+  const uint16_t* wbase =
+      reinterpret_cast<const uint16_t*>(ring + size_t(slot) * K * 2) + kbase + lane * 8;
   int kl = 0;
-  long long c_wait = 0, c_math = 0;
-  for (int64_t grp = first_group(off); grp < g.ngroups; grp += gridDim.x, rp.next(nst), ++kl) {
+  for (int64_t grp = first_group(off); grp < ngroups; grp += gridDim.x, rp.next(nst), ++kl) {
     const int s = rp.s;
     float acc = 0.f;
-    const long long c0 = tw ? clock64() : 0;
     const bool ok = !S.abort && mbar_wait(&S.full[s], rp.par);
-    const long long c1 = tw ? clock64() : 0;
     if (tw && kl == 0 && threadIdx.x == 0) tw[6] = global_ns();
     if (ok) {
       const uint16_t* wr = wbase + s * (kStage / 2);
@@ -522,14 +655,10 @@ __device__ __forceinline__ int gemv_phase(const PhaseGeo& g, int chunks, const X
     __syncwarp();
     if (lane == 0) mbar_arrive(&S.empty[s]);
     acc = warp_sum(acc);
-    if (tw) {
-      c_wait += c1 - c0;
-      c_math += clock64() - c1;
-    }
     if (lane == 0) {
       if (imm) {
-        const int64_t r = grp * g.rpg + slot;
-        if (r < g.N) {
+        const int64_t r = grp * rpg + slot;
+        if (r < N) {
           logits[r] = acc;
           const unsigned long long kk = argmax_key(acc, uint32_t(r));
           best = kk > best ? kk : best;
@@ -539,10 +668,8 @@ __device__ __forceinline__ int gemv_phase(const PhaseGeo& g, int chunks, const X
       }
     }
   }
-  if (tw && threadIdx.x == 0) {
-    tw[8] = c_wait;
-    tw[9] = c_math;
-  }
+  rp_io = rp;
+  best_io = best;
   return kl;
 }
 
@@ -554,13 +681,15 @@ __device__ __forceinline__ float res_val(const Shared& S, int kl, int slot, int 
 }
 
 // QKV epilogue: RoPE on the q/k partner rows at position pos (rope_s: the
-// cos then sin row of pos); q to qkv, k and v appended to the cache at pos
-// (when there is room).
+// cos then sin row of pos).  q, k and v of the position go out as tagged
+// words; k and v are also appended to the cache at pos (when there is room),
+// where later steps read them.
 __device__ __forceinline__ void epi_qkv(const FusedArgs& a, const FusedLayer& L, const PhaseGeo& g,
                                         int off, int nloc, int pos, bool append,
-                                        const float* rope_s, Shared& S) {
+                                        const float* rope_s, uint32_t tag, Shared& S) {
   const int D = g.D, half = D / 2, hp = g.rpc / 2, kvd = a.nkv * D;
   const int64_t f = first_group(off);
+  const int64_t vbase = int64_t(a.nq + a.nkv) * D;
   for (int i = threadIdx.x; i < nloc * g.rpc; i += kCThreads) {
     const int kl = i / g.rpc, slot = i % g.rpc;
     const int64_t grp = f + int64_t(kl) * gridDim.x;
@@ -572,42 +701,45 @@ __device__ __forceinline__ void epi_qkv(const FusedArgs& a, const FusedLayer& L,
       float o0, o1;
       rot(res_val(S, kl, slot, g.ks), res_val(S, kl, slot + hp, g.ks), rope_s[j], rope_s[half + j],
           &o0, &o1);
-      if (head < a.nq) {
-        a.qkv[ra] = o0;
-        a.qkv[ra + half] = o1;
-      } else if (append) {
+      ll_store(a.qkv_ll + ra, o0, tag);
+      ll_store(a.qkv_ll + ra + half, o1, tag);
+      if (head >= a.nq && append) {
         float* kr = L.kc + size_t(pos) * kvd + (head - a.nq) * D;
         kr[j] = o0;
         kr[j + half] = o1;
       }
-    } else if (append) {
-      const int64_t r = slot_row(g, grp, slot) - int64_t(a.nq + a.nkv) * D;
-      L.vc[size_t(pos) * kvd + r] = res_val(S, kl, slot, g.ks);
+    } else {
+      const int64_t r = slot_row(g, grp, slot);
+      const float v = res_val(S, kl, slot, g.ks);
+      ll_store(a.qkv_ll + r, v, tag);
+      if (append) L.vc[size_t(pos) * kvd + (r - vbase)] = v;
     }
   }
 }
 
-// O / DOWN epilogue: x[r] += y[r] (a single add per row).
-__device__ __forceinline__ void epi_residual(float* x, const PhaseGeo& g, int off, int nloc,
+// O / DOWN epilogue: x[r] = x_s[r] + y[r] out as tagged words (x_s: x as
+// this CTA last gathered it).
+__device__ __forceinline__ void epi_residual(unsigned long long* x_ll, const float* x_s,
+                                             const PhaseGeo& g, int off, int nloc, uint32_t tag,
                                              const Shared& S) {
   const int64_t f = first_group(off);
   for (int i = threadIdx.x; i < nloc * g.rpc; i += kCThreads) {
     const int kl = i / g.rpc, slot = i % g.rpc;
     const int64_t r = (f + int64_t(kl) * gridDim.x) * g.rpg + slot;
-    if (r < g.N) atomicAdd(x + r, res_val(S, kl, slot, g.ks));
+    if (r < g.N) ll_store(x_ll + r, x_s[r] + res_val(S, kl, slot, g.ks), tag);
   }
 }
 
-// GU epilogue: act = silu(gate) * up.
-__device__ __forceinline__ void epi_swiglu(float* act, const PhaseGeo& g, int off, int nloc,
-                                           const Shared& S) {
+// GU epilogue: act = silu(gate) * up, out as tagged words.
+__device__ __forceinline__ void epi_swiglu(unsigned long long* act_ll, const PhaseGeo& g, int off,
+                                           int nloc, uint32_t tag, const Shared& S) {
   const int64_t f = first_group(off);
   for (int i = threadIdx.x; i < nloc * g.rpg; i += kCThreads) {
     const int kl = i / g.rpg, q = i % g.rpg;
     const int64_t r = (f + int64_t(kl) * gridDim.x) * g.rpg + q;
     if (r < g.N) {
       const float gv = res_val(S, kl, q, g.ks), uv = res_val(S, kl, q + g.rpg, g.ks);
-      act[r] = gv / (1.0f + expf(-gv)) * uv;
+      ll_store(act_ll + r, gv / (1.0f + expf(-gv)) * uv, tag);
     }
   }
 }
@@ -629,66 +761,29 @@ __device__ __forceinline__ void epi_head(float* logits, const PhaseGeo& g, int o
 }
 
 // What the attention items of one layer read and write (passed by value to
-// the out-of-line item function, so the kernel arguments stay in the
+// the out-of-line item functions, so the kernel arguments stay in the
 // parameter bank).
 struct AttnArgs {
-  const float* qkv;
-  const float* kc;
+  const unsigned long long* qkv_ll;  // q | k | v of the position, tagged
+  const float* kc;                   // cache rows < pos
   const float* vc;
-  float* part;
-  float* att;
-  unsigned int* tickets;
+  unsigned long long* part_ll;       // [n_kv, nsplit, G, D + 2] tagged partials
+  unsigned long long* att_ll;        // [n_q * D] tagged output
+  const unsigned int* abort_word;
   int nq, nkv, nsplit;
   float scale;
 };
 
-// Merge the n_used split partials of kv head kvh into the attention output.
-template <int D>
-__device__ __forceinline__ void combine_head(const AttnArgs& a, int kvh, int n_used, float* sm) {
-  const int G = a.nq / a.nkv, tid = threadIdx.x;
-  const float* pb = a.part + size_t(kvh) * a.nsplit * G * (D + 2);
-  float* mv = sm;                  // [G][n_used]
-  float* lv = mv + G * n_used;     // [G][n_used]
-  float* wv = lv + G * n_used;     // [G][n_used]
-  float* Ls = wv + G * n_used;     // [G]
-  for (int i = tid; i < G * n_used; i += kCThreads) {
-    const int s = i / G, g = i % G;
-    const float* p = pb + (size_t(s) * G + g) * (D + 2);
-    mv[g * n_used + s] = ldcg(p);
-    lv[g * n_used + s] = ldcg(p + 1);
-  }
-  csync();
-  if (tid < G) {
-    float mx = -INFINITY;
-    for (int s = 0; s < n_used; ++s) mx = fmaxf(mx, mv[tid * n_used + s]);
-    float L = 0.f;
-    for (int s = 0; s < n_used; ++s) {
-      const float ms = mv[tid * n_used + s];
-      const float w = ms == -INFINITY ? 0.f : expf(ms - mx);
-      wv[tid * n_used + s] = w;
-      L = fmaf(lv[tid * n_used + s], w, L);
-    }
-    Ls[tid] = L;
-  }
-  csync();
-  for (int idx = tid; idx < G * D; idx += kCThreads) {
-    const int g = idx / D, j = idx % D;
-    float acc = 0.f;
-    for (int s = 0; s < n_used; ++s)
-      acc = fmaf(ldcg(pb + (size_t(s) * G + g) * (D + 2) + 2 + j), wv[g * n_used + s], acc);
-    const float L = Ls[g];
-    a.att[size_t(kvh) * G * D + idx] = L > 0.f ? acc / L : 0.f;
-  }
-}
-
 // Attention of one (kv head, split) item over positions [split*chunk,
-// min(n_ctx, (split+1)*chunk)) with online softmax; q (already rotated) from
-// qkv, keys/values from the cache.  A single split writes the output; else
-// the partial (m, l, o) goes to `part` and the last split to finish merges.
+// min(n_ctx, (split+1)*chunk)) with online softmax.  q and, when the
+// position is in range, its k and v come as tagged words from the QKV
+// epilogues; earlier positions from the cache.  A single split writes the
+// output; otherwise the partial (m, l, o) goes out for the merge.
 template <int D>
-__device__ __noinline__ void attn_item(const AttnArgs a, int kvh,
-                                          int split, int chunk, int n_ctx, int n_used, float* sm,
-                                          Shared& S, unsigned long long* tp) {
+__device__ __noinline__ bool attn_item(const AttnArgs a, int kvh, int split, int chunk, int n_ctx,
+                                       int pos, bool append, int n_used, uint32_t tag_qkv,
+                                       uint32_t tag_att, float* sm, Shared& S, uint32_t& gc,
+                                       unsigned long long* tp) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = a.nq / a.nkv, kvd = a.nkv * D;
   float* qs = sm;                       // [G][D]
@@ -696,6 +791,7 @@ __device__ __noinline__ void attn_item(const AttnArgs a, int kvh,
   float* vs = ks_ + kTileF * (D + 4);   // [kTileF][D]
   float* ps = vs + kTileF * D;          // [G][kTileF]
   const int c0 = split * chunk, c1 = min(n_ctx, c0 + chunk);
+  const int cache_end = append ? pos : n_ctx;  // rows below come from the cache
   if (tid < G) {
     S.m_s[tid] = -INFINITY;
     S.l_s[tid] = 0.f;
@@ -703,19 +799,29 @@ __device__ __noinline__ void attn_item(const AttnArgs a, int kvh,
   float o_acc[4] = {0.f, 0.f, 0.f, 0.f};  // G * D <= 1024 outputs: tid + 256 r
   for (int t0 = c0; t0 < c1; t0 += kTileF) {
     const int nt = min(kTileF, c1 - t0);
-    for (int i = tid; i < nt * (D / 4); i += kCThreads) {
+    const int nc = max(0, min(nt, cache_end - t0));
+    for (int i = tid; i < nc * (D / 4); i += kCThreads) {
       const int t = i / (D / 4), j4 = i % (D / 4);
       cp_async16(ks_ + t * (D + 4) + j4 * 4, a.kc + size_t(t0 + t) * kvd + kvh * D + j4 * 4);
       cp_async16(vs + t * D + j4 * 4, a.vc + size_t(t0 + t) * kvd + kvh * D + j4 * 4);
     }
-    if (t0 == c0) {
-      const float* qh = a.qkv + size_t(kvh) * G * D;
-      for (int i = tid; i < G * D / 4; i += kCThreads)
-        reinterpret_cast<float4*>(qs)[i] = ldcg4(qh + i * 4);
+    if (t0 == c0 || nc < nt) {
+      // q (first tile) and the position's own k and v (its last row) in one poll
+      LLRange r[3];
+      int nr = 0;
+      if (t0 == c0) r[nr++] = LLRange{qs, a.qkv_ll + size_t(kvh) * G * D, G * D};
+      if (nc < nt) {
+        r[nr++] = LLRange{ks_ + nc * (D + 4), a.qkv_ll + size_t(a.nq) * D + kvh * D, D};
+        r[nr++] = LLRange{vs + nc * D, a.qkv_ll + size_t(a.nq + a.nkv) * D + kvh * D, D};
+      }
+      if (!ll_gather3(r, nr, tag_qkv, a.abort_word, S, gc)) {
+        cp_async_wait_all();
+        return false;
+      }
+      if (t0 == c0 && tp && tid == 0) tp[1] = global_ns();
     }
     cp_async_wait_all();
     csync();
-    if (tp && tid == 0 && t0 == c0) tp[4] = global_ns();
     if (warp < G) {
       const int g = warp;
       const float* qr = qs + g * D;
@@ -773,38 +879,58 @@ __device__ __noinline__ void attn_item(const AttnArgs a, int kvh,
       const int idx = tid + r * kCThreads;
       if (idx < G * D) {
         const float l = S.l_s[idx / D];
-        a.att[size_t(kvh) * G * D + idx] = l > 0.f ? o_acc[r] / l : 0.f;
+        ll_store(a.att_ll + size_t(kvh) * G * D + idx, l > 0.f ? o_acc[r] / l : 0.f, tag_att);
       }
     }
-    csync();
-    return;
-  }
-  float* part = a.part + (size_t(kvh) * a.nsplit + split) * G * (D + 2);
+  } else {
+    unsigned long long* part = a.part_ll + (size_t(kvh) * a.nsplit + split) * G * (D + 2);
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    const int idx = tid + r * kCThreads;
-    if (idx < G * D) part[(idx / D) * (D + 2) + 2 + (idx % D)] = o_acc[r];
+    for (int r = 0; r < 4; ++r) {
+      const int idx = tid + r * kCThreads;
+      if (idx < G * D) ll_store(part + (idx / D) * (D + 2) + 2 + (idx % D), o_acc[r], tag_att);
+    }
+    if (tid < G) {
+      ll_store(part + tid * (D + 2), S.m_s[tid], tag_att);
+      ll_store(part + tid * (D + 2) + 1, S.l_s[tid], tag_att);
+    }
   }
+  csync();
+  return true;
+}
+
+// Merge the n_used split partials of kv head kvh into its attention output.
+template <int D>
+__device__ __noinline__ bool merge_head(const AttnArgs a, int kvh, int n_used, uint32_t tag_att,
+                                        float* sm, Shared& S, uint32_t& gc) {
+  const int G = a.nq / a.nkv, tid = threadIdx.x, rec = G * (D + 2);
+  float* P = sm;                   // [n_used][G][D + 2]
+  float* wv = P + n_used * rec;    // [G][n_used]
+  float* Ls = wv + G * n_used;     // [G]
+  if (!ll_gather(P, a.part_ll + size_t(kvh) * a.nsplit * rec, n_used * rec, tag_att, a.abort_word,
+                 S, gc))
+    return false;
   if (tid < G) {
-    part[tid * (D + 2)] = S.m_s[tid];
-    part[tid * (D + 2) + 1] = S.l_s[tid];
-  }
-  __threadfence();
-  csync();
-  if (tp && tid == 0) tp[5] = global_ns();
-  if (tid == 0)
-    S.flag = atomicAdd(a.tickets + kvh, 1u) == unsigned(n_used - 1) ? 1 : 0;
-  csync();
-  if (S.flag) {
-    __threadfence();
-    combine_head<D>(a, kvh, n_used, sm);
-    if (tid == 0) atomicExch(a.tickets + kvh, 0u);
+    float mx = -INFINITY;
+    for (int s = 0; s < n_used; ++s) mx = fmaxf(mx, P[s * rec + tid * (D + 2)]);
+    float L = 0.f;
+    for (int s = 0; s < n_used; ++s) {
+      const float ms = P[s * rec + tid * (D + 2)];
+      const float w = ms == -INFINITY ? 0.f : expf(ms - mx);
+      wv[tid * n_used + s] = w;
+      L = fmaf(P[s * rec + tid * (D + 2) + 1], w, L);
+    }
+    Ls[tid] = L;
   }
   csync();
-  if (tp && tid == 0) {
-    tp[6] = global_ns();
-    tp[7] = S.flag;
+  for (int idx = tid; idx < G * D; idx += kCThreads) {
+    const int g = idx / D, j = idx % D;
+    float acc = 0.f;
+    for (int s = 0; s < n_used; ++s) acc = fmaf(P[s * rec + g * (D + 2) + 2 + j], wv[g * n_used + s], acc);
+    const float L = Ls[g];
+    ll_store(a.att_ll + size_t(kvh) * G * D + idx, L > 0.f ? acc / L : 0.f, tag_att);
   }
+  csync();
+  return true;
 }
 
 // D: head dim.  CH: 256-element chunks of every warp segment when all
@@ -814,9 +940,11 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
   extern __shared__ __align__(1024) uint8_t dsm[];
   __shared__ Shared S;
   uint8_t* ring = dsm;
-  float* asm_ = reinterpret_cast<float*>(dsm + size_t(nst) * kStage);  // attention / merge
-  float* nw_s = asm_ + a.attn_floats;  // [h] the next rmsnorm weight vector
-  float* rope_s = nw_s + a.h;          // [D] cos, sin of the step's position
+  // attention tiles / merge, then the gathered att (O) or act (DOWN)
+  float* asm_ = reinterpret_cast<float*>(dsm + size_t(nst) * kStage);
+  float* x_s = asm_ + a.attn_floats;  // [h] x as last gathered (the residual)
+  float* nw_s = x_s + a.h;            // [h] the next rmsnorm weight vector
+  float* rope_s = nw_s + a.h;         // [D] cos, sin of the step's position
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -827,21 +955,26 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
     S.abort = 0;
     S.issued = 0;
     S.prod_done = 0;
+    S.fail[0] = S.fail[1] = 0;
     mbar_fence_init();
   }
   __syncthreads();
 
-  if (warp == kCWarps) {
-    if (lane == 0) {
+  if (warp >= kCWarps) {
+    // warpgroup 2: the producer warp and three idle warps hand registers back
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
+    if (warp == kCWarps && lane == 0) {
       producer(a, S, ring, nst);
       __threadfence_block();
       S.prod_done = 1;
     }
     return;
   }
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsumerRegs));
 
   // ---------------- consumers ----------------
   unsigned int target = 0;  // arrivals the last grid barrier waited for
+  uint32_t gc = 0;          // polls so far
   const StreamState& st = a.st;
   int pos = st.pos[0];
   int done = st.done[0];
@@ -855,6 +988,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
     unsigned long long* trs =
         a.trace && step == 0 ? a.trace + size_t(blockIdx.x) * nph * kTraceWords : nullptr;
     auto tslot = [&](int i) { return trs ? trs + i * kTraceWords : nullptr; };
+    const uint32_t tag0 = uint32_t(step) * uint32_t(nph);  // phase p writes tag0 + p + 1
     // the first rmsnorm's weights and the RoPE row of this position
     stage_vec(nw_s, a.layers[0].in_norm, a.h);
     {
@@ -864,30 +998,38 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
     }
     const bool append = pos < a.cap;
     const int n_ctx = append ? pos + 1 : pos;
-    int chunk = (n_ctx + a.nsplit - 1) / a.nsplit;
+    int chunk = (n_ctx + a.max_splits - 1) / a.max_splits;
     chunk = max(kTileF, (chunk + kTileF - 1) / kTileF * kTileF);
     const int n_used = (n_ctx + chunk - 1) / chunk;
     // phases of the step: per layer QKV, ATTN, O, GU, DOWN; then HEAD
     for (int p = 0; p < nph && ok; ++p) {
       const int l = p / 5;
       const int kind = p == a.L * 5 ? 5 : p % 5;
+      const uint32_t tag = tag0 + uint32_t(p) + 1u;
+      unsigned long long* tp = tslot(p);
+      if (tp && threadIdx.x == 0) tp[0] = global_ns();
       if (kind == 1) {
-        // ---- ATTN: (kv head, split) items; the last split of a head merges ----
+        // ---- ATTN: partials of this CTA's items, then the merges it owns ----
         AttnArgs aa;
-        aa.qkv = a.qkv;
+        aa.qkv_ll = a.qkv_ll;
         aa.kc = a.layers[l].kc;
         aa.vc = a.layers[l].vc;
-        aa.part = a.part;
-        aa.att = a.att;
-        aa.tickets = a.bar + kTicketBase;
+        aa.part_ll = a.part_ll;
+        aa.att_ll = a.att_ll;
+        aa.abort_word = a.bar + 2;
         aa.nq = a.nq;
         aa.nkv = a.nkv;
         aa.nsplit = a.nsplit;
         aa.scale = a.scale;
-        for (int item = blockIdx.x; item < a.nkv * n_used; item += gridDim.x)
-          attn_item<D>(aa, item / n_used, item % n_used, chunk, n_ctx, n_used, asm_, S,
-                       item == int(blockIdx.x) ? tslot(p) : nullptr);
-        ok = grid_sync(a, target, S, tslot(p));
+        for (int item = blockIdx.x; item < a.nkv * n_used && ok; item += gridDim.x)
+          ok = attn_item<D>(aa, item / n_used, item % n_used, chunk, n_ctx, pos, append, n_used,
+                            tag - 1u, tag, asm_, S, gc, item == int(blockIdx.x) ? tp : nullptr);
+        if (tp && threadIdx.x == 0) tp[5] = global_ns();
+        if (n_used > 1)
+          for (int item = blockIdx.x; item < a.nkv * n_used && ok; item += gridDim.x)
+            if (item % n_used == 0) ok = merge_head<D>(aa, item / n_used, n_used, tag, asm_, S, gc);
+        if (tp && threadIdx.x == 0) tp[6] = global_ns();
+        if (!ok) raise_abort(a);
         continue;
       }
       const int ph = kind == 0 ? PH_QKV : kind == 2 ? PH_O : kind == 3 ? PH_GU
@@ -895,32 +1037,47 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
       const int lw = ph == PH_HEAD ? 0 : l;
       const PhaseGeo g = geo(a, ph, lw);
       const int chunks = CH > 0 ? CH : g.chunks;
-      const int kbase = (warp % g.ks) * chunks * 256;
-      // the rmsnorm weights two phases ahead go to nw_s now (its last reader
-      // finished before the barrier just passed)
+      // the rmsnorm weights two phases ahead go to nw_s now (its last reader,
+      // the previous rmsnorm, is behind a CTA barrier)
       if (ph == PH_O) stage_vec(nw_s, a.layers[l].post_norm, a.h);
       if (ph == PH_DOWN) stage_vec(nw_s, l + 1 < a.L ? a.layers[l + 1].in_norm : a.final_norm, a.h);
-      // the phase input, in registers: QKV rmsnorm(x) (the embedding row at
-      // layer 0), O att, GU rmsnorm(x), DOWN act, HEAD rmsnorm(x)
-      XSeg x;
+      // the phase input: x (the embedding row at layer 0) for QKV, GU and
+      // HEAD, att for O, act for DOWN -- gathered into shared memory
+      const float* src = x_s;
       if (ph == PH_QKV && l == 0) {
         const uint16_t* erow = a.embed + size_t(tok) * a.h;
-        load_seg_bf16(x, erow, kbase, chunks, lane);
-        if (blockIdx.x == 0)
-          for (int k = threadIdx.x; k < a.h; k += kCThreads) a.x[k] = bf16f(erow[k]);
+        for (int k = threadIdx.x * 8; k < a.h; k += kCThreads * 8) {
+          const uint4 u = *reinterpret_cast<const uint4*>(erow + k);
+          *reinterpret_cast<float4*>(x_s + k) = make_float4(bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y));
+          *reinterpret_cast<float4*>(x_s + k + 4) = make_float4(bf16lo(u.z), bf16hi(u.z), bf16lo(u.w), bf16hi(u.w));
+        }
+        csync();
+      } else if (ph == PH_O) {
+        ok = ll_gather(asm_, a.att_ll, a.nq * a.d, tag - 1u, a.bar + 2, S, gc);
+        src = asm_;
+      } else if (ph == PH_DOWN) {
+        ok = ll_gather(asm_, a.act_ll, a.I, tag - 1u, a.bar + 2, S, gc);
+        src = asm_;
       } else {
-        load_seg_l2(x, ph == PH_O ? a.att : ph == PH_DOWN ? a.act : a.x, kbase, chunks, lane);
+        // x after the phase just before: the previous layer's DOWN (QKV,
+        // HEAD) or this layer's O (GU)
+        ok = ll_gather(x_s, a.x_ll, a.h, tag - 1u, a.bar + 2, S, gc);
       }
-      if (ph == PH_QKV || ph == PH_GU || ph == PH_HEAD) {
+      if (!ok) {
+        raise_abort(a);
+        break;
+      }
+      if (tp && threadIdx.x == 0) tp[1] = global_ns();
+      const bool normed = ph == PH_QKV || ph == PH_GU || ph == PH_HEAD;
+      if (normed) {
         cp_async_wait_all();
         csync();
-        norm_seg(x, nw_s, kbase, chunks, g.ks, a.h, a.eps, S);
       }
-      unsigned long long* tp = tslot(p);
-      if (tp && threadIdx.x == 0) tp[4] = global_ns();
       const bool imm = ph == PH_HEAD && g.ks == 1;
       unsigned long long best = 0;
-      const int nloc = gemv_phase(g, chunks, x, off, rp, nst, ring, S, imm, a.logits, best, tp);
+      const int nloc = gemv_block(g.ngroups, g.K, g.ks, g.rpg, g.N, chunks, src,
+                                  normed ? nw_s : nullptr, a.eps, a.h, off, rp, nst, ring, S, imm,
+                                  a.logits, best, tp);
       if (tp && threadIdx.x == 0) {
         tp[5] = global_ns();
         tp[7] = nloc;
@@ -928,12 +1085,15 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
       if (!imm) {
         csync();
         switch (ph) {
-          case PH_QKV: epi_qkv(a, a.layers[lw], g, off, nloc, pos, append, rope_s, S); break;
-          case PH_GU: epi_swiglu(a.act, g, off, nloc, S); break;
+          case PH_QKV:
+            epi_qkv(a, a.layers[lw], g, off, nloc, pos, append, rope_s, tag, S);
+            break;
+          case PH_GU: epi_swiglu(a.act_ll, g, off, nloc, tag, S); break;
           case PH_HEAD: epi_head(a.logits, g, off, nloc, S, best); break;
-          default: epi_residual(a.x, g, off, nloc, S); break;
+          default: epi_residual(a.x_ll, x_s, g, off, nloc, tag, S); break;
         }
       }
+      csync();  // x_s, asm_ and S.res are free for the next phase
       off = int((off + g.ngroups) % gridDim.x);
       if (ph == PH_HEAD) {
         best = warp_max_u64(best);
@@ -944,8 +1104,10 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
           for (int w = 0; w < kCWarps; ++w) bb = S.best[w] > bb ? S.best[w] : bb;
           a.am_part[blockIdx.x] = bb;
         }
+        // the one grid barrier of a step: the argmax partials, and the cache
+        // rows appended this step, are visible everywhere after it
+        ok = grid_sync(a, target, S, nullptr);
       }
-      ok = grid_sync(a, target, S, tslot(p));
     }
     if (!ok) break;
     // every CTA reduces the argmax partials: the same token everywhere
@@ -1009,11 +1171,17 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
   }
 }
 
+// Whether every instance was compiled with the register count the
+// warpgroup split assumes (set by fused_prepare; otherwise the fused path is
+// not used, since a consumer's setmaxnreg.inc could then wait forever).
+bool g_regs_ok = true;
+
 template <int D, int CH>
 cudaError_t prepare_one() {
   cudaFuncAttributes fa{};
   TMG_CUDA_TRY(cudaFuncGetAttributes(&fa, decode_fused_kernel<D, CH>));
   if (fa.sharedSizeBytes > kStaticReserve) return cudaErrorInvalidConfiguration;
+  if (fa.numRegs != kLaunchRegs) g_regs_ok = false;
   int dev = 0, optin = 0;
   TMG_CUDA_TRY(cudaGetDevice(&dev));
   TMG_CUDA_TRY(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
@@ -1042,33 +1210,48 @@ bool local_ok(int64_t ngroups, int num_sms) {
 }  // namespace
 
 bool fused_supported(int h, int nq, int nkv, int d, int I, int64_t V, int num_sms) {
-  if (nkv <= 0 || nq % nkv != 0 || nkv > kBarWords - kTicketBase) return false;
+  if (!g_regs_ok || nkv <= 0 || nq % nkv != 0) return false;
   const int G = nq / nkv, q_dim = nq * d;
   if (!(seg_ok(h) && seg_ok(q_dim) && seg_ok(I) && (d == 64 || d == 128) && G >= 1 && G <= 8 &&
         G * d <= 4 * kCThreads))
+    return false;
+  // every tagged exchange fits one gather (a kv head's queries: one word
+  // pair per thread)
+  if (h > kMaxGather || q_dim > kMaxGather || I > kMaxGather || G * (d + 2) > kMaxGather ||
+      G * d > 2 * kCThreads)
     return false;
   // QKV groups hold rpc/2 rows from each RoPE half of a head
   const int rpc_h = kCWarps / ksplit_host(h);
   if (rpc_h < 2 || d % rpc_h != 0 || (d / 2) % (rpc_h / 2) != 0) return false;
   const int rpc_q = kCWarps / ksplit_host(q_dim), rpc_i = kCWarps / ksplit_host(I);
-  return local_ok(int64_t(nq + 2 * nkv) * d / rpc_h, num_sms) &&
-         local_ok((h + rpc_q - 1) / rpc_q, num_sms) &&
-         local_ok((I + rpc_h / 2 - 1) / (rpc_h / 2), num_sms) &&
-         local_ok((h + rpc_i - 1) / rpc_i, num_sms) &&
-         (ksplit_host(h) == 1 || local_ok((V + rpc_h - 1) / rpc_h, num_sms));
+  const int64_t groups[5] = {int64_t(nq + 2 * nkv) * d / rpc_h, (h + rpc_q - 1) / rpc_q,
+                             (I + rpc_h / 2 - 1) / (rpc_h / 2), (h + rpc_i - 1) / rpc_i,
+                             (V + rpc_h - 1) / rpc_h};
+  // every CTA owns groups in every phase (what makes reusing the tagged
+  // buffers safe), and the deferred phases fit the per-warp result table
+  for (int i = 0; i < 5; ++i)
+    if (groups[i] < num_sms) return false;
+  return local_ok(groups[0], num_sms) && local_ok(groups[1], num_sms) &&
+         local_ok(groups[2], num_sms) && local_ok(groups[3], num_sms) &&
+         (ksplit_host(h) == 1 || local_ok(groups[4], num_sms));
 }
 
 int fused_bar_words() { return kBarWords; }
 
 // Dynamic shared memory: the ring (as many 32 KB stages as fit, at most
-// max_stages or 6), the attention tiles or the merge's arrays (whichever is
-// larger; *attn_floats), one rmsnorm weight vector (h) and a RoPE row (d).
-size_t fused_smem(int h, int d, int G, int nsplit, int max_stages, int* nst_out, int* attn_floats) {
-  const size_t att = std::max<size_t>(
-      size_t(G) * d + size_t(kTileF) * (d + 4) + size_t(kTileF) * d + size_t(G) * kTileF,
-      size_t(G) * (3 * size_t(nsplit) + 1));
+// max_stages or 6); a region for the attention tiles, the merge's gathered
+// partials, the gathered att or act (the largest; *attn_floats); x as last
+// gathered (h); one rmsnorm weight vector (h); a RoPE row (d).  *max_splits:
+// the most attention splits one merge can gather.
+size_t fused_smem(int h, int q_dim, int I, int d, int G, int nsplit, int max_stages, int* nst_out,
+                  int* attn_floats, int* max_splits) {
+  *max_splits = std::max(1, std::min(nsplit, kMaxGather / (G * (d + 2))));
+  const size_t tiles =
+      size_t(G) * d + size_t(kTileF) * (d + 4) + size_t(kTileF) * d + size_t(G) * kTileF;
+  const size_t merge = size_t(*max_splits) * G * (d + 2) + size_t(G) * *max_splits + G;
+  const size_t att = std::max(std::max(tiles, merge), std::max(size_t(q_dim), size_t(I)));
   *attn_floats = int((att + 3) / 4 * 4);  // keep what follows 16-byte aligned
-  const size_t rest = (size_t(*attn_floats) + h + d) * 4;
+  const size_t rest = (size_t(*attn_floats) + 2 * size_t(h) + d) * 4;
   // the kernel's static shared memory and the 1 KB alignment slack of the
   // dynamic segment come out of the 227 KB
   const size_t budget = 227 * 1024 - kStaticReserve - 1024;
@@ -1089,12 +1272,18 @@ cudaError_t launch_decode_fused(const FusedArgs& args, int num_sms, cudaStream_t
   FusedArgs a = args;
   int nst = 0;
   const int G = a.nq / a.nkv;
-  const size_t smem = fused_smem(a.h, a.d, G, a.nsplit, a.max_stages, &nst, &a.attn_floats);
-  if (nst < 2 || !a.att || a.pf_ahead < 0) return cudaErrorInvalidValue;
+  const size_t smem = fused_smem(a.h, a.nq * a.d, a.I, a.d, G, a.nsplit, a.max_stages, &nst,
+                                 &a.attn_floats, &a.max_splits);
+  if (nst < 2 || !a.x_ll || !a.att_ll || !a.act_ll || !a.qkv_ll || !a.part_ll || a.pf_ahead < 0)
+    return cudaErrorInvalidValue;
   const bool ch8 = a.h / ksplit_host(a.h) == 2048 && (a.nq * a.d) / ksplit_host(a.nq * a.d) == 2048 &&
                    a.I / ksplit_host(a.I) == 2048;
-  // the grid barrier counts from zero in every launch
+  // the grid barrier counts from zero in every launch, and the tagged
+  // exchange buffers hold no tag of this launch
   TMG_CUDA_TRY(cudaMemsetAsync(a.bar, 0, 4 * sizeof(unsigned int), s));
+  TMG_CUDA_TRY(cudaMemsetAsync(a.ll_base, 0, a.ll_bytes, s));
+  TMG_CUDA_TRY(cudaMemsetAsync(a.part_ll, 0,
+                               size_t(a.nkv) * a.nsplit * G * (a.d + 2) * sizeof(unsigned long long), s));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(num_sms);
   cfg.blockDim = dim3(kFThreads);

@@ -31,20 +31,25 @@ struct FusedArgs {
   const float* rope_cos = nullptr;
   const float* rope_sin = nullptr;
   int64_t cap = 0;
-  float* x = nullptr;       // [h] residual
-  float* qkv = nullptr;     // [(nq + 2 nkv) d]
-  float* part = nullptr;    // [nkv, nsplit, G, d + 2] attention partials
-  float* att = nullptr;     // [nq d] attention output
-  float* act = nullptr;     // [I]
+  // tagged exchange words {value, tag} (see decode_fused.cu), zeroed by the
+  // launcher: x [h], att [nq d], act [I], qkv [(nq + 2 nkv) d] in one block
+  // at ll_base (ll_bytes), the attention partials [nkv, nsplit, G, d + 2]
+  unsigned long long* ll_base = nullptr;
+  size_t ll_bytes = 0;
+  unsigned long long* x_ll = nullptr;
+  unsigned long long* att_ll = nullptr;
+  unsigned long long* act_ll = nullptr;
+  unsigned long long* qkv_ll = nullptr;
+  unsigned long long* part_ll = nullptr;
   float* logits = nullptr;  // [V]
   unsigned long long* am_part = nullptr;  // [grid]
-  // fused_bar_words() words: [0] barrier arrivals, [2] abort, [64 + kv head]
-  // attention tickets (zero between launches)
+  // fused_bar_words() words: [0] barrier arrivals, [2] abort
   unsigned int* bar = nullptr;
   int nsplit = 1;
   int pf_ahead = 0;    // stages of L2 prefetch beyond the ring
   int max_stages = 0;  // cap on the ring's stages (0: as many as fit)
   int attn_floats = 0; // set by the launcher: attention region of shared memory
+  int max_splits = 1;  // set by the launcher: attention splits per kv head
   StreamState st{};
   int n_steps = 0;
   int32_t* err = nullptr;
@@ -58,7 +63,12 @@ struct FusedArgs {
 
 bool fused_supported(int h, int nq, int nkv, int d, int I, int64_t V, int num_sms);
 int fused_bar_words();
-size_t fused_smem(int h, int d, int G, int nsplit, int max_stages, int* nst_out, int* attn_floats);
+size_t fused_smem(int h, int q_dim, int I, int d, int G, int nsplit, int max_stages, int* nst_out,
+                  int* attn_floats, int* max_splits);
+// Words of the tagged exchange block (x, att, act, qkv) of a model.
+inline size_t fused_ll_words(int h, int q_dim, int I, int qkv_rows) {
+  return size_t(h) + q_dim + I + qkv_rows;
+}
 cudaError_t fused_prepare();
 // Cooperative launch: one CTA per SM (num_sms CTAs).
 cudaError_t launch_decode_fused(const FusedArgs& a, int num_sms, cudaStream_t s);
