@@ -15,10 +15,16 @@ flush is needed); e2e = the same metric through the public API
 (tmg_generate with host prompt buffers, tokens read back every 8 steps),
 decode tok/s as the reference's main.rs defines it.
 
+The decode runs as ONE persistent kernel per step (decode_fused_kernel: all
+256 tokens, every layer, the LM head and the argmax), so the roofline entry
+describes that kernel: achieved = algorithmic bytes per launch (BF16
+weights of every layer and the LM head plus the KV rows read, per token,
+times 256 tokens) / the launch's device time.  traffic = DRAM bytes of an
+ncu capture of the same kernel on a smaller case, scaled per algorithmic
+byte (profiles/decode_fused_c2.json).
+
 With --gpus N > 1 every rank runs an independent replica of c2 (the 1B
-config fits one GPU; "replicas only", weak scaling).  --workload c4 runs the
-8B-class config tensor-parallel over the N ranks (NCCL allreduce per
-sublayer; strong scaling).
+config fits one GPU; "replicas only", weak scaling).
 
 --impl reference times the reference's CPU algorithm (the C++ restatement in
 oracle/, with the reference's thread policy) on the host cores, rank 0 only.
@@ -314,16 +320,17 @@ def run_ours(args, rank, world, local_rank):
                 prev_end = r[4]
             f.write(f"step total {(max(r[4] for r in tl) - base) / 1e3:.2f} us\n")
 
-    # --- per-kernel profile pass (dominant kernel's roofline) ---
-    cache_trunc(cache, PROMPT)
-    prof = model.profile_decode([t0_tok], cache, 16)
-    attn_bytes = 2 * kvd * 4 * (PROMPT + 8) * 1.0
-    bytes_per = {"qkv_gemv": layer_bytes["qkv_gemv"], "o_gemv": layer_bytes["o_gemv"],
-                 "gateup_gemv": layer_bytes["gateup_gemv"], "down_gemv": layer_bytes["down_gemv"],
-                 "lm_head": head_bytes, "attn_decode": attn_bytes}
-    dom = max(prof, key=lambda k: prof[k][0])
-    dom_ms = prof[dom][0] / max(prof[dom][1], 1)
-    achieved = bytes_per[dom] / (dom_ms / 1e3) / 1e9
+    # --- roofline of the dominant kernel: the fused decode kernel is the
+    # whole timed step (one launch per step) ---
+    launch_ms = elapsed_ms / args.steps
+    alg_bytes_launch = (weight_bytes_tok + kv_bytes_tok) * GEN
+    achieved = alg_bytes_launch / (launch_ms / 1e3) / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "decode_fused_c2.json"
+    if tf.exists():
+        ratio = json.loads(tf.read_text()).get("dram_bytes_per_algorithmic_byte")
+        if ratio:
+            traffic = int(ratio * alg_bytes_launch)
 
     # --- end to end through the public API (host buffers) ---
     e2e_vals, h2d, d2h = [], 0, 0
@@ -365,14 +372,15 @@ def run_ours(args, rank, world, local_rank):
             "decode_hbm_gbs": round(step_gbs, 1),
             "decode_hbm_frac": round(step_gbs / peak, 4),
             "prefill_tok_s": round(PROMPT / (prefill_ms / 1e3), 1),
-            "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1),
-                         "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": None, "peak_kind": peak_kind,
-                         "per_kernel_ms": {k: round(v[0] / max(v[1], 1), 5) for k, v in prof.items()}},
+            "roofline": {"bound": "hbm", "kernel": "decode_fused_kernel",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "algorithmic_bytes_per_launch": int(alg_bytes_launch),
+                         "launch_ms": round(launch_ms, 3), "peak_kind": peak_kind},
             "clocks": clocks,
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "gpu_launches": args.steps * GEN * (cfg["num_hidden_layers"] * 5 + 1),
+            "gpu_launches": args.steps,  # one decode_fused_kernel launch per step
             "greedy_consistent": bool(ok),
         }
         if cpu:

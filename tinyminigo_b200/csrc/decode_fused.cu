@@ -429,7 +429,7 @@ __device__ __forceinline__ ulonglong2 ll_load2(const unsigned long long* p) {
 }
 
 constexpr int kGatherPairs = 16;                            // word pairs per thread
-constexpr unsigned a_backoff_ns = 100;                      // pause between polls
+constexpr unsigned kBackoffNs = 0;                          // pause between polls
 constexpr int kMaxGather = kGatherPairs * 2 * kCThreads;   // 8192 words
 
 // All consumer threads: wait until src[0..n) (n even, <= kMaxGather) carry
@@ -469,8 +469,7 @@ __device__ __noinline__ bool ll_gather(float* dst, const unsigned long long* src
       ok = false;
       break;
     }
-    // back off a little: 148 CTAs re-reading the same lines load L2
-    __nanosleep(a_backoff_ns);
+    if (kBackoffNs) __nanosleep(kBackoffNs);
 #pragma unroll
     for (int k = 0; k < kGatherPairs; ++k)
       if ((need >> k) & 1u) v[k] = ll_load2(src + (threadIdx.x + k * kCThreads) * 2);
@@ -517,7 +516,7 @@ __device__ __noinline__ bool ll_gather3(const LLRange* r, int nr, uint32_t tag,
       ok = false;
       break;
     }
-    __nanosleep(a_backoff_ns);
+    if (kBackoffNs) __nanosleep(kBackoffNs);
 #pragma unroll
     for (int k = 0; k < 3; ++k)
       if ((need >> k) & 1u) v[k] = ll_load2(r[k].src + threadIdx.x * 2);
@@ -822,6 +821,7 @@ __device__ __noinline__ bool attn_item(const AttnArgs a, int kvh, int split, int
     }
     cp_async_wait_all();
     csync();
+    if (t0 == c0 && tp && tid == 0) tp[2] = global_ns();
     if (warp < G) {
       const int g = warp;
       const float* qr = qs + g * D;
@@ -872,6 +872,7 @@ __device__ __noinline__ bool attn_item(const AttnArgs a, int kvh, int split, int
       }
     }
     csync();
+    if (t0 == c0 && tp && tid == 0) tp[3] = global_ns();
   }
   if (n_used == 1) {
 #pragma unroll
