@@ -80,7 +80,7 @@ struct tmg_ctx {
   unsigned int* bar = nullptr;   // grid barrier of the fused decode kernel
   unsigned long long* ll = nullptr;  // its tagged exchange words (x, att, act, qkv)
   int fused_pf = 0;              // its L2 prefetch distance (stages; TMG_FUSED_PF)
-  int fused_stages = 0;          // its ring depth cap (0: all that fit; TMG_FUSED_STAGES)
+  int fused_stages = 4;          // its ring depth cap (0: all that fit; TMG_FUSED_STAGES)
   bool fused_ok = false;         // the fused batch-1 decode kernel takes this shape
   // prefill scratch
   int64_t pf_cap = 0;

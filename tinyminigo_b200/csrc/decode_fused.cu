@@ -90,6 +90,19 @@ __device__ __forceinline__ void stage_vec(float* dst, const float* src, int n) {
   for (int i = threadIdx.x * 4; i < n; i += kCThreads * 4) cp_async16(dst + i, src + i);
 }
 
+// GEMV inputs live in shared memory in a lane-major layout: within each
+// 256-element chunk, the 8 elements lane l multiplies with one 16-byte
+// weight load (l*8 .. l*8+7) sit as two float4 at l*4 and 128 + l*4, so a
+// warp's two float4 loads per chunk are contiguous (no bank conflicts).
+__device__ __forceinline__ int perm_idx(int k) {
+  const int e = k & 255;
+  return (k - e) + ((e >> 2) & 1) * 128 + (e >> 3) * 4 + (e & 3);
+}
+// stage_vec into the lane-major layout (n % 8 == 0).
+__device__ __forceinline__ void stage_vec_perm(float* dst, const float* src, int n) {
+  for (int i = threadIdx.x * 4; i < n; i += kCThreads * 4) cp_async16(dst + perm_idx(i), src + i);
+}
+
 // L2 policy for weight rows: once copied to shared memory they are dead.
 __device__ __forceinline__ uint64_t evict_first_policy() {
   uint64_t p;
@@ -433,12 +446,17 @@ constexpr unsigned kBackoffNs = 0;                          // pause between pol
 constexpr int kMaxGather = kGatherPairs * 2 * kCThreads;   // 8192 words
 
 // All consumer threads: wait until src[0..n) (n even, <= kMaxGather) carry
-// `tag`, then copy the values to dst in shared memory.  Returns false, in
+// `tag`, then copy the values to dst in shared memory (in the lane-major
+// layout when asked; n % 8 == 0 then).  Returns false, in
 // every thread alike, when a wait gave up or the kernel is aborting; `gc`
 // counts the polls (the failure flag alternates slots so that a slow reader
 // of one poll never sees the next poll's flag).
 __device__ __noinline__ bool ll_gather(float* dst, const unsigned long long* src, int n, uint32_t tag,
-                          const unsigned int* abort_word, Shared& S, uint32_t& gc) {
+                          const unsigned int* abort_word, Shared& S, uint32_t& gc,
+                          bool lane_major = false) {
+  const unsigned long long t0 = global_ns();
+  unsigned int spins = 0;
+  bool ok = true;
   ulonglong2 v[kGatherPairs];
   uint32_t need = 0;  // bit k: pair k still to come
 #pragma unroll
@@ -449,17 +467,14 @@ __device__ __noinline__ bool ll_gather(float* dst, const unsigned long long* src
       need |= 1u << k;
     }
   }
-  const unsigned long long t0 = global_ns();
-  unsigned int spins = 0;
-  bool ok = true;
   for (;;) {
 #pragma unroll
     for (int k = 0; k < kGatherPairs; ++k) {
       if ((need >> k) & 1u) {
         if (uint32_t(v[k].x >> 32) == tag && uint32_t(v[k].y >> 32) == tag) {
           const int i = (threadIdx.x + k * kCThreads) * 2;
-          dst[i] = __uint_as_float(uint32_t(v[k].x));
-          dst[i + 1] = __uint_as_float(uint32_t(v[k].y));
+          *reinterpret_cast<float2*>(dst + (lane_major ? perm_idx(i) : i)) =
+              make_float2(__uint_as_float(uint32_t(v[k].x)), __uint_as_float(uint32_t(v[k].y)));
           need &= ~(1u << k);
         }
       }
@@ -543,16 +558,16 @@ struct XSeg {
   float4 a[8], b[8];
 };
 
-// This warp's K segment of the phase input from shared memory, or from a
-// BF16 row in global memory (the embedding, widened exactly).
+// This warp's K segment of the phase input from shared memory (lane-major
+// layout, see perm_idx).
 __device__ __forceinline__ void load_seg_smem(XSeg& x, const float* src, int kbase, int chunks,
                                               int lane) {
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
     if (c < chunks) {
-      const int k = kbase + c * 256 + lane * 8;
-      x.a[c] = *reinterpret_cast<const float4*>(src + k);
-      x.b[c] = *reinterpret_cast<const float4*>(src + k + 4);
+      const float* p = src + kbase + c * 256 + lane * 4;  // lane-major layout
+      x.a[c] = *reinterpret_cast<const float4*>(p);
+      x.b[c] = *reinterpret_cast<const float4*>(p + 128);
     }
   }
 }
@@ -589,9 +604,9 @@ __device__ __forceinline__ void norm_seg(XSeg& x, const float* w, int kbase, int
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
     if (c < chunks) {
-      const int k = kbase + c * 256 + lane * 8;
-      const float4 wa = *reinterpret_cast<const float4*>(w + k);
-      const float4 wb = *reinterpret_cast<const float4*>(w + k + 4);
+      const float* p = w + kbase + c * 256 + lane * 4;  // lane-major, as x
+      const float4 wa = *reinterpret_cast<const float4*>(p);
+      const float4 wb = *reinterpret_cast<const float4*>(p + 128);
       x.a[c] = make_float4((x.a[c].x * inv) * wa.x, (x.a[c].y * inv) * wa.y,
                            (x.a[c].z * inv) * wa.z, (x.a[c].w * inv) * wa.w);
       x.b[c] = make_float4((x.b[c].x * inv) * wb.x, (x.b[c].y * inv) * wb.y,
@@ -717,7 +732,7 @@ __device__ __forceinline__ void epi_qkv(const FusedArgs& a, const FusedLayer& L,
 }
 
 // O / DOWN epilogue: x[r] = x_s[r] + y[r] out as tagged words (x_s: x as
-// this CTA last gathered it).
+// this CTA last gathered it, lane-major).
 __device__ __forceinline__ void epi_residual(unsigned long long* x_ll, const float* x_s,
                                              const PhaseGeo& g, int off, int nloc, uint32_t tag,
                                              const Shared& S) {
@@ -725,7 +740,7 @@ __device__ __forceinline__ void epi_residual(unsigned long long* x_ll, const flo
   for (int i = threadIdx.x; i < nloc * g.rpc; i += kCThreads) {
     const int kl = i / g.rpc, slot = i % g.rpc;
     const int64_t r = (f + int64_t(kl) * gridDim.x) * g.rpg + slot;
-    if (r < g.N) ll_store(x_ll + r, x_s[r] + res_val(S, kl, slot, g.ks), tag);
+    if (r < g.N) ll_store(x_ll + r, x_s[perm_idx(int(r))] + res_val(S, kl, slot, g.ks), tag);
   }
 }
 
@@ -943,8 +958,8 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
   uint8_t* ring = dsm;
   // attention tiles / merge, then the gathered att (O) or act (DOWN)
   float* asm_ = reinterpret_cast<float*>(dsm + size_t(nst) * kStage);
-  float* x_s = asm_ + a.attn_floats;  // [h] x as last gathered (the residual)
-  float* nw_s = x_s + a.h;            // [h] the next rmsnorm weight vector
+  float* x_s = asm_ + a.attn_floats;  // [h] x as last gathered (the residual), lane-major
+  float* nw_s = x_s + a.h;            // [h] the next rmsnorm weight vector, lane-major
   float* rope_s = nw_s + a.h;         // [D] cos, sin of the step's position
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -991,7 +1006,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
     auto tslot = [&](int i) { return trs ? trs + i * kTraceWords : nullptr; };
     const uint32_t tag0 = uint32_t(step) * uint32_t(nph);  // phase p writes tag0 + p + 1
     // the first rmsnorm's weights and the RoPE row of this position
-    stage_vec(nw_s, a.layers[0].in_norm, a.h);
+    stage_vec_perm(nw_s, a.layers[0].in_norm, a.h);
     {
       const int64_t rrow = pos < a.cap ? pos : a.cap - 1;  // the host keeps pos < cap
       stage_vec(rope_s, a.rope_cos + rrow * (D / 2), D / 2);
@@ -1040,8 +1055,9 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
       const int chunks = CH > 0 ? CH : g.chunks;
       // the rmsnorm weights two phases ahead go to nw_s now (its last reader,
       // the previous rmsnorm, is behind a CTA barrier)
-      if (ph == PH_O) stage_vec(nw_s, a.layers[l].post_norm, a.h);
-      if (ph == PH_DOWN) stage_vec(nw_s, l + 1 < a.L ? a.layers[l + 1].in_norm : a.final_norm, a.h);
+      if (ph == PH_O) stage_vec_perm(nw_s, a.layers[l].post_norm, a.h);
+      if (ph == PH_DOWN)
+        stage_vec_perm(nw_s, l + 1 < a.L ? a.layers[l + 1].in_norm : a.final_norm, a.h);
       // the phase input: x (the embedding row at layer 0) for QKV, GU and
       // HEAD, att for O, act for DOWN -- gathered into shared memory
       const float* src = x_s;
@@ -1049,20 +1065,21 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
         const uint16_t* erow = a.embed + size_t(tok) * a.h;
         for (int k = threadIdx.x * 8; k < a.h; k += kCThreads * 8) {
           const uint4 u = *reinterpret_cast<const uint4*>(erow + k);
-          *reinterpret_cast<float4*>(x_s + k) = make_float4(bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y));
-          *reinterpret_cast<float4*>(x_s + k + 4) = make_float4(bf16lo(u.z), bf16hi(u.z), bf16lo(u.w), bf16hi(u.w));
+          float* d = x_s + perm_idx(k);  // lane-major: the 8 values split 4 + 4
+          *reinterpret_cast<float4*>(d) = make_float4(bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y));
+          *reinterpret_cast<float4*>(d + 128) = make_float4(bf16lo(u.z), bf16hi(u.z), bf16lo(u.w), bf16hi(u.w));
         }
         csync();
       } else if (ph == PH_O) {
-        ok = ll_gather(asm_, a.att_ll, a.nq * a.d, tag - 1u, a.bar + 2, S, gc);
+        ok = ll_gather(asm_, a.att_ll, a.nq * a.d, tag - 1u, a.bar + 2, S, gc, true);
         src = asm_;
       } else if (ph == PH_DOWN) {
-        ok = ll_gather(asm_, a.act_ll, a.I, tag - 1u, a.bar + 2, S, gc);
+        ok = ll_gather(asm_, a.act_ll, a.I, tag - 1u, a.bar + 2, S, gc, true);
         src = asm_;
       } else {
         // x after the phase just before: the previous layer's DOWN (QKV,
         // HEAD) or this layer's O (GU)
-        ok = ll_gather(x_s, a.x_ll, a.h, tag - 1u, a.bar + 2, S, gc);
+        ok = ll_gather(x_s, a.x_ll, a.h, tag - 1u, a.bar + 2, S, gc, true);
       }
       if (!ok) {
         raise_abort(a);
