@@ -120,7 +120,10 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def dist_init(world: int, local_rank: int):
+def dist_init(world: int, local_rank: int, backend: str = "nccl"):
+    """The process group of a multi-GPU run (one process per GPU, replicas):
+    used only for the barriers around the timed region and the max over
+    ranks.  A short timeout so that ranks waiting on a dead peer fail."""
     if world <= 1:
         return None
     import datetime
@@ -128,17 +131,25 @@ def dist_init(world: int, local_rank: int):
     import torch
     import torch.distributed as dist
 
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                            device_id=torch.device("cuda", local_rank))
+    kw = {"device_id": torch.device("cuda", local_rank)} if backend == "nccl" else {}
+    dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120), **kw)
     return dist
 
 
+def replica_tok_s(world: int, tokens_per_rank: int, max_elapsed_ms: float) -> float:
+    """Whole-job decode throughput of `world` independent replicas: all the
+    tokens every rank produced over the slowest rank's time."""
+    return world * tokens_per_rank / (max_elapsed_ms / 1e3)
+
+
 def max_over_ranks(dist, v: float) -> float:
+    """The slowest rank's time: every rank gets the max of v over ranks."""
     if dist is None:
         return v
     import torch
 
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -288,8 +299,7 @@ def run_ours(args, rank, world, local_rank):
     if dist is not None:
         dist.barrier()
     elapsed_ms = max_over_ranks(dist, elapsed_ms)
-    toks = world * GEN * args.steps
-    value = toks / (elapsed_ms / 1e3)
+    value = replica_tok_s(world, GEN * args.steps, elapsed_ms)
     per_tok_ms = elapsed_ms / (args.steps * GEN)
     layer_bytes, head_bytes = c2_bytes(cfg)
     L = cfg["num_hidden_layers"]
