@@ -17,7 +17,7 @@
 //               store (or add into) Y in f32.
 // Every mbarrier wait is bounded; a wait that gives up sets the error word
 // and the CTA skips the rest of its work (the host reports TMG_ERR_TIMEOUT).
-// Single-GPU code: no multicast, no peer memory.
+// Single-GPU code: every CTA loads its own tiles; no peer memory.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
