@@ -131,6 +131,8 @@ def dist_init(world: int, local_rank: int, backend: str = "nccl"):
     import torch
     import torch.distributed as dist
 
+    # rank 0 prints exactly one JSON line on stdout: keep NCCL's banner off it
+    os.environ["NCCL_DEBUG"] = os.environ.get("TMG_BENCH_NCCL_DEBUG", "WARN")
     kw = {"device_id": torch.device("cuda", local_rank)} if backend == "nccl" else {}
     dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120), **kw)
     return dist
