@@ -168,9 +168,9 @@ __device__ __forceinline__ int ksplit(int K) {
   return ks;
 }
 
-__device__ __forceinline__ PhaseGeo geo(const FusedArgs& a, int ph, int l) {
+__device__ __forceinline__ PhaseGeo geo(const FusedArgs& a, const FusedLayer* layers, int ph, int l) {
   PhaseGeo g;
-  const FusedLayer& L = a.layers[l];
+  const FusedLayer& L = layers[l];
   g.w2 = nullptr;
   g.pair_groups = 0;
   g.D = a.d;
@@ -311,6 +311,7 @@ __device__ bool grid_sync(const FusedArgs& a, unsigned int& target, Shared& S,
 // Producer: the weight stream of all steps, in consumption order.
 // ---------------------------------------------------------------------------
 struct Cursor {
+  const FusedLayer* layers;  // the per-layer table in shared memory
   int step, l, ph, off;
   int64_t grp;
   PhaseGeo g;
@@ -333,16 +334,17 @@ __device__ __forceinline__ void cur_settle(const FusedArgs& a, Cursor& c) {
     } else {
       ++c.ph;
     }
-    c.g = geo(a, c.ph, c.l < a.L ? c.l : 0);
+    c.g = geo(a, c.layers, c.ph, c.l < a.L ? c.l : 0);
     c.grp = first_group(c.off);
   }
 }
-__device__ __forceinline__ void cur_begin(const FusedArgs& a, Cursor& c) {
+__device__ __forceinline__ void cur_begin(const FusedArgs& a, const FusedLayer* layers, Cursor& c) {
+  c.layers = layers;
   c.step = 0;
   c.l = 0;
   c.ph = PH_QKV;
   c.off = 0;
-  c.g = geo(a, PH_QKV, 0);
+  c.g = geo(a, c.layers, PH_QKV, 0);
   c.grp = first_group(0);
   c.valid = a.n_steps > 0;
   cur_settle(a, c);
@@ -352,11 +354,12 @@ __device__ __forceinline__ void cur_next(const FusedArgs& a, Cursor& c) {
   cur_settle(a, c);
 }
 
-__device__ void producer(const FusedArgs& a, Shared& S, uint8_t* ring, int nst) {
+__device__ void producer(const FusedArgs& a, const FusedLayer* layers, Shared& S, uint8_t* ring,
+                         int nst) {
   const uint64_t pol = evict_first_policy();
   const int nph = a.L * 5 + 1;
   Cursor ic, pc;
-  cur_begin(a, ic);
+  cur_begin(a, layers, ic);
   pc = ic;
   int it = 0, pf = 0;
   unsigned long long* tr_cur = nullptr;  // diagnostics of the phase being issued
@@ -447,16 +450,19 @@ constexpr int kMaxGather = kGatherPairs * 2 * kCThreads;   // 8192 words
 
 // All consumer threads: wait until src[0..n) (n even, <= kMaxGather) carry
 // `tag`, then copy the values to dst in shared memory (in the lane-major
-// layout when asked; n % 8 == 0 then).  Returns false, in
+// layout when asked; n % 8 == 0 then).  With wx (an rmsnorm input; wx holds
+// the norm weights in dst's layout, staged and waited for), also
+// wx <- wx * x in place and each warp's share of sum(x^2) into S.ssq.  Returns false, in
 // every thread alike, when a wait gave up or the kernel is aborting; `gc`
 // counts the polls (the failure flag alternates slots so that a slow reader
 // of one poll never sees the next poll's flag).
 __device__ __noinline__ bool ll_gather(float* dst, const unsigned long long* src, int n, uint32_t tag,
                           const unsigned int* abort_word, Shared& S, uint32_t& gc,
-                          bool lane_major = false) {
+                          bool lane_major = false, float* wx = nullptr) {
   const unsigned long long t0 = global_ns();
   unsigned int spins = 0;
   bool ok = true;
+  float ss = 0.f;
   ulonglong2 v[kGatherPairs];
   uint32_t need = 0;  // bit k: pair k still to come
 #pragma unroll
@@ -473,8 +479,18 @@ __device__ __noinline__ bool ll_gather(float* dst, const unsigned long long* src
       if ((need >> k) & 1u) {
         if (uint32_t(v[k].x >> 32) == tag && uint32_t(v[k].y >> 32) == tag) {
           const int i = (threadIdx.x + k * kCThreads) * 2;
-          *reinterpret_cast<float2*>(dst + (lane_major ? perm_idx(i) : i)) =
+          const int j = lane_major ? perm_idx(i) : i;
+          const float2 val =
               make_float2(__uint_as_float(uint32_t(v[k].x)), __uint_as_float(uint32_t(v[k].y)));
+          *reinterpret_cast<float2*>(dst + j) = val;
+          if (wx) {  // rmsnorm input: weights * x in place, and sum(x^2)
+            float2 w = *reinterpret_cast<const float2*>(wx + j);
+            w.x *= val.x;
+            w.y *= val.y;
+            *reinterpret_cast<float2*>(wx + j) = w;
+            ss = fmaf(val.x, val.x, ss);
+            ss = fmaf(val.y, val.y, ss);
+          }
           need &= ~(1u << k);
         }
       }
@@ -488,6 +504,10 @@ __device__ __noinline__ bool ll_gather(float* dst, const unsigned long long* src
 #pragma unroll
     for (int k = 0; k < kGatherPairs; ++k)
       if ((need >> k) & 1u) v[k] = ll_load2(src + (threadIdx.x + k * kCThreads) * 2);
+  }
+  if (wx) {
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) S.ssq[threadIdx.x >> 5] = ss;
   }
   const int slot = gc & 1;
   ++gc;
@@ -503,7 +523,7 @@ struct LLRange {
   const unsigned long long* src;
   int n;
 };
-__device__ __noinline__ bool ll_gather3(const LLRange* r, int nr, uint32_t tag,
+__device__ __forceinline__ bool ll_gather3(const LLRange* r, int nr, uint32_t tag,
                                         const unsigned int* abort_word, Shared& S, uint32_t& gc) {
   ulonglong2 v[3];
   uint32_t need = 0;
@@ -615,6 +635,14 @@ __device__ __forceinline__ void norm_seg(XSeg& x, const float* w, int kbase, int
   }
 }
 
+// 1/rms(x) from the warps' shares in S.ssq (after a CTA barrier).
+__device__ __forceinline__ float rms_scale(const Shared& S, int n, float eps) {
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < kCWarps; ++w) tot += S.ssq[w];
+  return 1.0f / sqrtf(tot / float(n) + eps);
+}
+
 // Position in the stage ring: stage count, slot, phase parity.
 struct RingPos {
   int it, s;
@@ -628,23 +656,31 @@ struct RingPos {
   }
 };
 
-// One GEMV phase over this CTA's groups: the
-// warp's K segment of the input from shared memory (src), rmsnorm'd with nw
-// when given; then each warp dots its slot/segment of every stage.  imm (LM
+// One GEMV phase over this CTA's groups: the warp's K segment of the input
+// from shared memory (src), rmsnorm'd with nw when given; then each warp
+// dots its slot/segment of every stage.  imm (LM
 // head with ks == 1): logits and the argmax candidate directly; otherwise
 // the sums go to S.res for the phase's epilogue.  Returns the number of
 // local groups; tw (diagnostics) receives the first stage's arrival time.
 __device__ __forceinline__ int gemv_block(int64_t ngroups, int K, int ks, int rpg, int64_t N,
-                                       int chunks, const float* src, const float* nw, float eps,
-                                       int n_norm, int off, RingPos& rp_io, int nst,
-                                       const uint8_t* ring, Shared& S, bool imm, float* logits,
-                                       unsigned long long& best_io, unsigned long long* tw) {
+                                       int chunks, const float* src, const float* nw,
+                                       float eps, int n_norm, int off,
+                                       RingPos& rp_io, int nst, const uint8_t* ring, Shared& S,
+                                       bool imm, float* logits, unsigned long long& best_io,
+                                       unsigned long long* tw) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int slot = warp / ks;
   const int kbase = (warp % ks) * chunks * 256;
+  const long long c0 = tw ? clock64() : 0;
   XSeg x;
   load_seg_smem(x, src, kbase, chunks, lane);
+  const long long c1 = tw ? clock64() : 0;
   if (nw) norm_seg(x, nw, kbase, chunks, ks, n_norm, eps, S);
+  const long long c2 = tw ? clock64() : 0;
+  if (tw && threadIdx.x == 0) {
+    tw[8] = c1 - c0;
+    tw[9] = c2 - c1;
+  }
   RingPos rp = rp_io;
   unsigned long long best = best_io;
   // this lane's first weight element in stage 0
@@ -655,7 +691,10 @@ __device__ __forceinline__ int gemv_block(int64_t ngroups, int K, int ks, int rp
     const int s = rp.s;
     float acc = 0.f;
     const bool ok = !S.abort && mbar_wait(&S.full[s], rp.par);
-    if (tw && kl == 0 && threadIdx.x == 0) tw[6] = global_ns();
+    if (tw && kl == 0 && threadIdx.x == 0) {
+      tw[6] = global_ns();
+      tw[4] = clock64() - c2;
+    }
     if (ok) {
       const uint16_t* wr = wbase + s * (kStage / 2);
       float sacc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -694,13 +733,13 @@ __device__ __forceinline__ float res_val(const Shared& S, int kl, int slot, int 
   return v;
 }
 
-// QKV epilogue: RoPE on the q/k partner rows at position pos (rope_s: the
-// cos then sin row of pos).  q, k and v of the position go out as tagged
+// QKV epilogue: the rmsnorm factor (scale), then RoPE on the q/k partner
+// rows at position pos (rope_s: the cos then sin row of pos).  q, k and v of the position go out as tagged
 // words; k and v are also appended to the cache at pos (when there is room),
 // where later steps read them.
 __device__ __forceinline__ void epi_qkv(const FusedArgs& a, const FusedLayer& L, const PhaseGeo& g,
                                         int off, int nloc, int pos, bool append,
-                                        const float* rope_s, uint32_t tag, Shared& S) {
+                                        const float* rope_s, float scale, uint32_t tag, Shared& S) {
   const int D = g.D, half = D / 2, hp = g.rpc / 2, kvd = a.nkv * D;
   const int64_t f = first_group(off);
   const int64_t vbase = int64_t(a.nq + a.nkv) * D;
@@ -713,8 +752,8 @@ __device__ __forceinline__ void epi_qkv(const FusedArgs& a, const FusedLayer& L,
       const int64_t head = ra / D;
       const int j = int(ra % D);
       float o0, o1;
-      rot(res_val(S, kl, slot, g.ks), res_val(S, kl, slot + hp, g.ks), rope_s[j], rope_s[half + j],
-          &o0, &o1);
+      rot(res_val(S, kl, slot, g.ks) * scale, res_val(S, kl, slot + hp, g.ks) * scale, rope_s[j],
+          rope_s[half + j], &o0, &o1);
       ll_store(a.qkv_ll + ra, o0, tag);
       ll_store(a.qkv_ll + ra + half, o1, tag);
       if (head >= a.nq && append) {
@@ -724,7 +763,7 @@ __device__ __forceinline__ void epi_qkv(const FusedArgs& a, const FusedLayer& L,
       }
     } else {
       const int64_t r = slot_row(g, grp, slot);
-      const float v = res_val(S, kl, slot, g.ks);
+      const float v = res_val(S, kl, slot, g.ks) * scale;
       ll_store(a.qkv_ll + r, v, tag);
       if (append) L.vc[size_t(pos) * kvd + (r - vbase)] = v;
     }
@@ -744,15 +783,16 @@ __device__ __forceinline__ void epi_residual(unsigned long long* x_ll, const flo
   }
 }
 
-// GU epilogue: act = silu(gate) * up, out as tagged words.
+// GU epilogue: the rmsnorm factor (scale), then act = silu(gate) * up, out
+// as tagged words.
 __device__ __forceinline__ void epi_swiglu(unsigned long long* act_ll, const PhaseGeo& g, int off,
-                                           int nloc, uint32_t tag, const Shared& S) {
+                                           int nloc, float scale, uint32_t tag, const Shared& S) {
   const int64_t f = first_group(off);
   for (int i = threadIdx.x; i < nloc * g.rpg; i += kCThreads) {
     const int kl = i / g.rpg, q = i % g.rpg;
     const int64_t r = (f + int64_t(kl) * gridDim.x) * g.rpg + q;
     if (r < g.N) {
-      const float gv = res_val(S, kl, q, g.ks), uv = res_val(S, kl, q + g.rpg, g.ks);
+      const float gv = res_val(S, kl, q, g.ks) * scale, uv = res_val(S, kl, q + g.rpg, g.ks) * scale;
       ll_store(act_ll + r, gv / (1.0f + expf(-gv)) * uv, tag);
     }
   }
@@ -774,9 +814,7 @@ __device__ __forceinline__ void epi_head(float* logits, const PhaseGeo& g, int o
   }
 }
 
-// What the attention items of one layer read and write (passed by value to
-// the out-of-line item functions, so the kernel arguments stay in the
-// parameter bank).
+// What the attention items of one layer read and write.
 struct AttnArgs {
   const unsigned long long* qkv_ll;  // q | k | v of the position, tagged
   const float* kc;                   // cache rows < pos
@@ -794,7 +832,7 @@ struct AttnArgs {
 // epilogues; earlier positions from the cache.  A single split writes the
 // output; otherwise the partial (m, l, o) goes out for the merge.
 template <int D>
-__device__ __noinline__ bool attn_item(const AttnArgs a, int kvh, int split, int chunk, int n_ctx,
+__device__ __forceinline__ bool attn_item(const AttnArgs a, int kvh, int split, int chunk, int n_ctx,
                                        int pos, bool append, int n_used, uint32_t tag_qkv,
                                        uint32_t tag_att, float* sm, Shared& S, uint32_t& gc,
                                        unsigned long long* tp) {
@@ -916,7 +954,7 @@ __device__ __noinline__ bool attn_item(const AttnArgs a, int kvh, int split, int
 
 // Merge the n_used split partials of kv head kvh into its attention output.
 template <int D>
-__device__ __noinline__ bool merge_head(const AttnArgs a, int kvh, int n_used, uint32_t tag_att,
+__device__ __forceinline__ bool merge_head(const AttnArgs a, int kvh, int n_used, uint32_t tag_att,
                                         float* sm, Shared& S, uint32_t& gc) {
   const int G = a.nq / a.nkv, tid = threadIdx.x, rec = G * (D + 2);
   float* P = sm;                   // [n_used][G][D + 2]
@@ -961,7 +999,15 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
   float* x_s = asm_ + a.attn_floats;  // [h] x as last gathered (the residual), lane-major
   float* nw_s = x_s + a.h;            // [h] the next rmsnorm weight vector, lane-major
   float* rope_s = nw_s + a.h;         // [D] cos, sin of the step's position
+  // [L] the per-layer pointer table, read every phase by every role
+  FusedLayer* layers_s = reinterpret_cast<FusedLayer*>(rope_s + D);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  {
+    const unsigned long long* src = reinterpret_cast<const unsigned long long*>(a.layers);
+    unsigned long long* dst = reinterpret_cast<unsigned long long*>(layers_s);
+    const int words = a.L * int(sizeof(FusedLayer) / 8);
+    for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < nst; ++s) {
@@ -980,7 +1026,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
     // warpgroup 2: the producer warp and three idle warps hand registers back
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
     if (warp == kCWarps && lane == 0) {
-      producer(a, S, ring, nst);
+      producer(a, layers_s, S, ring, nst);
       __threadfence_block();
       S.prod_done = 1;
     }
@@ -1006,7 +1052,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
     auto tslot = [&](int i) { return trs ? trs + i * kTraceWords : nullptr; };
     const uint32_t tag0 = uint32_t(step) * uint32_t(nph);  // phase p writes tag0 + p + 1
     // the first rmsnorm's weights and the RoPE row of this position
-    stage_vec_perm(nw_s, a.layers[0].in_norm, a.h);
+    stage_vec_perm(nw_s, layers_s[0].in_norm, a.h);
     {
       const int64_t rrow = pos < a.cap ? pos : a.cap - 1;  // the host keeps pos < cap
       stage_vec(rope_s, a.rope_cos + rrow * (D / 2), D / 2);
@@ -1028,8 +1074,8 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
         // ---- ATTN: partials of this CTA's items, then the merges it owns ----
         AttnArgs aa;
         aa.qkv_ll = a.qkv_ll;
-        aa.kc = a.layers[l].kc;
-        aa.vc = a.layers[l].vc;
+        aa.kc = layers_s[l].kc;
+        aa.vc = layers_s[l].vc;
         aa.part_ll = a.part_ll;
         aa.att_ll = a.att_ll;
         aa.abort_word = a.bar + 2;
@@ -1051,24 +1097,45 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
       const int ph = kind == 0 ? PH_QKV : kind == 2 ? PH_O : kind == 3 ? PH_GU
                    : kind == 4 ? PH_DOWN : PH_HEAD;
       const int lw = ph == PH_HEAD ? 0 : l;
-      const PhaseGeo g = geo(a, ph, lw);
+      const PhaseGeo g = geo(a, layers_s, ph, lw);
       const int chunks = CH > 0 ? CH : g.chunks;
       // the rmsnorm weights two phases ahead go to nw_s now (its last reader,
       // the previous rmsnorm, is behind a CTA barrier)
-      if (ph == PH_O) stage_vec_perm(nw_s, a.layers[l].post_norm, a.h);
+      if (ph == PH_O) stage_vec_perm(nw_s, layers_s[l].post_norm, a.h);
       if (ph == PH_DOWN)
-        stage_vec_perm(nw_s, l + 1 < a.L ? a.layers[l + 1].in_norm : a.final_norm, a.h);
-      // the phase input: x (the embedding row at layer 0) for QKV, GU and
-      // HEAD, att for O, act for DOWN -- gathered into shared memory
+        stage_vec_perm(nw_s, l + 1 < a.L ? layers_s[l + 1].in_norm : a.final_norm, a.h);
+      // the phase input in shared memory (lane-major): for QKV and GU the
+      // rmsnorm input x * w (in place over the staged weights nw_s, the raw x
+      // kept in x_s for the residual, each warp's share of sum(x^2) in
+      // S.ssq; the 1/rms factor goes on each row's dot product in the
+      // epilogue); x for HEAD (normalised per warp); att for O; act for DOWN
       const float* src = x_s;
       if (ph == PH_QKV && l == 0) {
+        cp_async_wait_all();  // nw_s (staged at the step's start)
+        csync();
+        src = nw_s;
         const uint16_t* erow = a.embed + size_t(tok) * a.h;
+        float ss = 0.f;
         for (int k = threadIdx.x * 8; k < a.h; k += kCThreads * 8) {
           const uint4 u = *reinterpret_cast<const uint4*>(erow + k);
-          float* d = x_s + perm_idx(k);  // lane-major: the 8 values split 4 + 4
-          *reinterpret_cast<float4*>(d) = make_float4(bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y));
-          *reinterpret_cast<float4*>(d + 128) = make_float4(bf16lo(u.z), bf16hi(u.z), bf16lo(u.w), bf16hi(u.w));
+          const int j = perm_idx(k);  // lane-major: the 8 values split 4 + 4
+          const float4 v0 = make_float4(bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y));
+          const float4 v1 = make_float4(bf16lo(u.z), bf16hi(u.z), bf16lo(u.w), bf16hi(u.w));
+          *reinterpret_cast<float4*>(x_s + j) = v0;
+          *reinterpret_cast<float4*>(x_s + j + 128) = v1;
+          float4 w0 = *reinterpret_cast<const float4*>(nw_s + j);
+          float4 w1 = *reinterpret_cast<const float4*>(nw_s + j + 128);
+          w0 = make_float4(w0.x * v0.x, w0.y * v0.y, w0.z * v0.z, w0.w * v0.w);
+          w1 = make_float4(w1.x * v1.x, w1.y * v1.y, w1.z * v1.z, w1.w * v1.w);
+          *reinterpret_cast<float4*>(nw_s + j) = w0;
+          *reinterpret_cast<float4*>(nw_s + j + 128) = w1;
+          ss = fmaf(v0.x, v0.x, ss); ss = fmaf(v0.y, v0.y, ss);
+          ss = fmaf(v0.z, v0.z, ss); ss = fmaf(v0.w, v0.w, ss);
+          ss = fmaf(v1.x, v1.x, ss); ss = fmaf(v1.y, v1.y, ss);
+          ss = fmaf(v1.z, v1.z, ss); ss = fmaf(v1.w, v1.w, ss);
         }
+        ss = warp_sum(ss);
+        if (lane == 0) S.ssq[warp] = ss;
         csync();
       } else if (ph == PH_O) {
         ok = ll_gather(asm_, a.att_ll, a.nq * a.d, tag - 1u, a.bar + 2, S, gc, true);
@@ -1080,22 +1147,36 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
         // x after the phase just before: the previous layer's DOWN (QKV,
         // HEAD) or this layer's O (GU)
         ok = ll_gather(x_s, a.x_ll, a.h, tag - 1u, a.bar + 2, S, gc, true);
+        cp_async_wait_all();  // nw_s (staged a phase or more ago)
+        if (ok && ph != PH_HEAD) {
+          // nw_s <- nw_s * x (same layout) and each warp's share of sum(x^2)
+          float ss = 0.f;
+          for (int j = threadIdx.x * 4; j < a.h; j += kCThreads * 4) {
+            const float4 v = *reinterpret_cast<const float4*>(x_s + j);
+            float4 w = *reinterpret_cast<const float4*>(nw_s + j);
+            w = make_float4(w.x * v.x, w.y * v.y, w.z * v.z, w.w * v.w);
+            *reinterpret_cast<float4*>(nw_s + j) = w;
+            ss = fmaf(v.x, v.x, ss);
+            ss = fmaf(v.y, v.y, ss);
+            ss = fmaf(v.z, v.z, ss);
+            ss = fmaf(v.w, v.w, ss);
+          }
+          ss = warp_sum(ss);
+          if (lane == 0) S.ssq[warp] = ss;
+          src = nw_s;
+        }
+        csync();
       }
       if (!ok) {
         raise_abort(a);
         break;
       }
       if (tp && threadIdx.x == 0) tp[1] = global_ns();
-      const bool normed = ph == PH_QKV || ph == PH_GU || ph == PH_HEAD;
-      if (normed) {
-        cp_async_wait_all();
-        csync();
-      }
       const bool imm = ph == PH_HEAD && g.ks == 1;
       unsigned long long best = 0;
       const int nloc = gemv_block(g.ngroups, g.K, g.ks, g.rpg, g.N, chunks, src,
-                                  normed ? nw_s : nullptr, a.eps, a.h, off, rp, nst, ring, S, imm,
-                                  a.logits, best, tp);
+                                  ph == PH_HEAD ? nw_s : nullptr, a.eps, a.h, off, rp, nst, ring,
+                                  S, imm, a.logits, best, tp);
       if (tp && threadIdx.x == 0) {
         tp[5] = global_ns();
         tp[7] = nloc;
@@ -1104,9 +1185,10 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
         csync();
         switch (ph) {
           case PH_QKV:
-            epi_qkv(a, a.layers[lw], g, off, nloc, pos, append, rope_s, tag, S);
+            epi_qkv(a, layers_s[lw], g, off, nloc, pos, append, rope_s, rms_scale(S, a.h, a.eps),
+                    tag, S);
             break;
-          case PH_GU: epi_swiglu(a.act_ll, g, off, nloc, tag, S); break;
+          case PH_GU: epi_swiglu(a.act_ll, g, off, nloc, rms_scale(S, a.h, a.eps), tag, S); break;
           case PH_HEAD: epi_head(a.logits, g, off, nloc, S, best); break;
           default: epi_residual(a.x_ll, x_s, g, off, nloc, tag, S); break;
         }
@@ -1259,17 +1341,18 @@ int fused_bar_words() { return kBarWords; }
 // Dynamic shared memory: the ring (as many 32 KB stages as fit, at most
 // max_stages or 6); a region for the attention tiles, the merge's gathered
 // partials, the gathered att or act (the largest; *attn_floats); x as last
-// gathered (h); one rmsnorm weight vector (h); a RoPE row (d).  *max_splits:
+// gathered (h); one rmsnorm weight vector (h); a RoPE row (d); the per-layer
+// pointer table (L FusedLayer).  *max_splits:
 // the most attention splits one merge can gather.
-size_t fused_smem(int h, int q_dim, int I, int d, int G, int nsplit, int max_stages, int* nst_out,
-                  int* attn_floats, int* max_splits) {
+size_t fused_smem(int h, int q_dim, int I, int d, int G, int nsplit, int L, int max_stages,
+                  int* nst_out, int* attn_floats, int* max_splits) {
   *max_splits = std::max(1, std::min(nsplit, kMaxGather / (G * (d + 2))));
   const size_t tiles =
       size_t(G) * d + size_t(kTileF) * (d + 4) + size_t(kTileF) * d + size_t(G) * kTileF;
   const size_t merge = size_t(*max_splits) * G * (d + 2) + size_t(G) * *max_splits + G;
   const size_t att = std::max(std::max(tiles, merge), std::max(size_t(q_dim), size_t(I)));
   *attn_floats = int((att + 3) / 4 * 4);  // keep what follows 16-byte aligned
-  const size_t rest = (size_t(*attn_floats) + 2 * size_t(h) + d) * 4;
+  const size_t rest = (size_t(*attn_floats) + 2 * size_t(h) + d) * 4 + size_t(L) * sizeof(FusedLayer);
   // the kernel's static shared memory and the 1 KB alignment slack of the
   // dynamic segment come out of the 227 KB
   const size_t budget = 227 * 1024 - kStaticReserve - 1024;
@@ -1290,7 +1373,7 @@ cudaError_t launch_decode_fused(const FusedArgs& args, int num_sms, cudaStream_t
   FusedArgs a = args;
   int nst = 0;
   const int G = a.nq / a.nkv;
-  const size_t smem = fused_smem(a.h, a.nq * a.d, a.I, a.d, G, a.nsplit, a.max_stages, &nst,
+  const size_t smem = fused_smem(a.h, a.nq * a.d, a.I, a.d, G, a.nsplit, a.L, a.max_stages, &nst,
                                  &a.attn_floats, &a.max_splits);
   if (nst < 2 || !a.x_ll || !a.att_ll || !a.act_ll || !a.qkv_ll || !a.part_ll || a.pf_ahead < 0)
     return cudaErrorInvalidValue;

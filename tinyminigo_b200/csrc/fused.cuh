@@ -63,8 +63,8 @@ struct FusedArgs {
 
 bool fused_supported(int h, int nq, int nkv, int d, int I, int64_t V, int num_sms);
 int fused_bar_words();
-size_t fused_smem(int h, int q_dim, int I, int d, int G, int nsplit, int max_stages, int* nst_out,
-                  int* attn_floats, int* max_splits);
+size_t fused_smem(int h, int q_dim, int I, int d, int G, int nsplit, int L, int max_stages,
+                  int* nst_out, int* attn_floats, int* max_splits);
 // Words of the tagged exchange block (x, att, act, qkv) of a model.
 inline size_t fused_ll_words(int h, int q_dim, int I, int qkv_rows) {
   return size_t(h) + q_dim + I + qkv_rows;
