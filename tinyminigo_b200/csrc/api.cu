@@ -121,6 +121,7 @@ struct tmg_kv {
   int32_t* h_state = nullptr;  // pinned staging of the state block
   FusedLayer* d_layers = nullptr;  // per-layer pointers for the fused kernel (stream 0)
   unsigned long long* part_ll = nullptr;  // its tagged attention partials
+  int nsplit_f = 1;                       // their split capacity per kv head
   cudaEvent_t state_ev = nullptr;  // the last upload from h_state
   std::vector<void*> allocs;
 };
@@ -801,7 +802,7 @@ cudaError_t launch_fused(tmg_ctx* c, tmg_kv* kv, const StreamState& st, int64_t 
   f.logits = c->logits;
   f.am_part = c->am_part;
   f.bar = c->bar;
-  f.nsplit = kv->nsplit;
+  f.nsplit = kv->nsplit_f;
   f.pf_ahead = c->fused_pf;
   f.max_stages = c->fused_stages;
   f.st = st;
@@ -1223,7 +1224,8 @@ int tmg_kv_create(tmg_ctx* c, int32_t n_streams, int64_t capacity, tmg_kv** out)
     if ((e = copy_sync(c, kv->d_layers, fl.data(), fl.size() * sizeof(FusedLayer),
                        cudaMemcpyHostToDevice)) != cudaSuccess)
       return bail(e);
-    const size_t pw = size_t(c->nkv) * kv->nsplit * (c->nq / c->nkv) * (c->d + 2);
+    kv->nsplit_f = fused_nsplit(c->nq / c->nkv, c->d, capacity);
+    const size_t pw = size_t(c->nkv) * kv->nsplit_f * (c->nq / c->nkv) * (c->d + 2);
     if ((e = dalloc(kv->allocs, &kv->part_ll, pw)) != cudaSuccess) return bail(e);
   }
   const int G = c->nq / c->nkv;

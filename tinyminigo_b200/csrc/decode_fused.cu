@@ -948,7 +948,9 @@ __device__ __forceinline__ bool attn_item(const AttnArgs a, int kvh, int split, 
       ll_store(part + tid * (D + 2) + 1, S.l_s[tid], tag_att);
     }
   }
+  if (tp && tid == 0) tp[8] = global_ns();
   csync();
+  if (tp && tid == 0) tp[9] = global_ns();
   return true;
 }
 
@@ -1337,6 +1339,15 @@ bool fused_supported(int h, int nq, int nkv, int d, int I, int64_t V, int num_sm
 }
 
 int fused_bar_words() { return kBarWords; }
+
+// Attention splits per kv head the fused kernel may use for a cache of
+// `capacity` positions: one kTileF-position tile per split, as many as one
+// merge can gather.
+int fused_nsplit(int G, int d, int64_t capacity) {
+  const int64_t tiles = (capacity + kTileF - 1) / kTileF;
+  const int64_t most = kMaxGather / (int64_t(G) * (d + 2));
+  return int(std::max<int64_t>(1, std::min(tiles, most)));
+}
 
 // Dynamic shared memory: the ring (as many 32 KB stages as fit, at most
 // max_stages or 6); a region for the attention tiles, the merge's gathered

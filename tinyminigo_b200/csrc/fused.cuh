@@ -63,6 +63,7 @@ struct FusedArgs {
 
 bool fused_supported(int h, int nq, int nkv, int d, int I, int64_t V, int num_sms);
 int fused_bar_words();
+int fused_nsplit(int G, int d, int64_t capacity);
 size_t fused_smem(int h, int q_dim, int I, int d, int G, int nsplit, int L, int max_stages,
                   int* nst_out, int* attn_floats, int* max_splits);
 // Words of the tagged exchange block (x, att, act, qkv) of a model.
