@@ -409,6 +409,226 @@ def run_ours(args, rank, world, local_rank):
     model.close()
 
 
+def model_config(cfg):
+    from tinyminigo_b200.model import ModelConfig
+
+    return ModelConfig(cfg["hidden_size"], cfg["num_hidden_layers"], cfg["num_attention_heads"],
+                       cfg["num_key_value_heads"], cfg["head_dim"], cfg["intermediate_size"],
+                       cfg["rms_norm_eps"], cfg["rope_theta"], cfg["vocab_size"], [], 0)
+
+
+def base_line(args, world, metric, value, unit, ms_per_step, workload, scaling, clocks, **extra):
+    d = {"metric": metric, "value": round(value, 2), "unit": unit, "n_gpus": world,
+         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
+         "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
+         "dtype": "f32 (bf16 weights)", "data": "synthetic (seeded N(0,0.02^2) bf16 weights, "
+         "random prompt)", "config": workload, "clocks": clocks}
+    d.update(extra)
+    return d
+
+
+def run_c3(args, rank, world, local_rank):
+    """C3: a 2048-token random prompt through the prefill path of the c2
+    shape (tcgen05 GEMMs, prefill attention); one step = one prefill from an
+    empty cache.  value = prompt tokens / s on the device; e2e = the same
+    through forward_seq with the prompt and the logits in host memory."""
+    import torch
+
+    if rank != 0:
+        return
+    torch.cuda.set_device(local_rank)
+    from tinyminigo_b200 import synth
+    from tinyminigo_b200.model import Model
+
+    T = 2048
+    cfg, w = make_c2("cuda")
+    model = Model.from_tensors(model_config(cfg), w, device=local_rank)
+    prompt = synth.random_prompt(cfg["vocab_size"], T, 13)
+    cache = model.new_cache(T + 8)
+    stream = torch.cuda.ExternalStream(model.stream_handle(), device=local_rank)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def step():
+        cache.truncate(0)
+        model.forward_seq(prompt, cache, want_logits=False)
+
+    for _ in range(args.warmup):
+        step()
+    model.sync()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        model.sync()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    # e2e: host prompt in, host logits out, every step
+    t_e = []
+    for _ in range(args.steps):
+        cache.truncate(0)
+        t0 = time.perf_counter()
+        model.forward_seq(prompt, cache)
+        t_e.append(time.perf_counter() - t0)
+    h, L = cfg["hidden_size"], cfg["num_hidden_layers"]
+    layer_params = sum(v // 2 for v in c2_bytes(cfg)[0].values())
+    nq, d = cfg["num_attention_heads"], cfg["head_dim"]
+    flops = (2 * T * layer_params * L + L * 4 * d * nq * T * (T + 1) // 2
+             + 2 * cfg["vocab_size"] * h)
+    tflops = flops / (ms / 1e3) / 1e12
+    pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = float(pk.get("bf16_tflops", 1590.0))
+    res = base_line(args, world, "prefill_tok_s", T / (ms / 1e3), "tok/s", ms,
+                    {"workload": "c3: c2 shape, 2048-token random prompt, prefill", "global_batch": 1,
+                     "seq_len": T, "parallelism": "single GPU"}, "weak", clk.summary(),
+                    roofline={"bound": "tensor", "kernel": "gemm_tc_kernel (whole prefill)",
+                              "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
+                              "frac": round(tflops / peak, 4), "traffic": None,
+                              "algorithmic_flops_per_step": int(flops),
+                              "note": "f32 activations as bf16 hi+lo: the tensor cores run 2x these "
+                                      "flops for the linear layers"},
+                    e2e={"value": round(T / statistics.median(t_e), 2), "unit": "tok/s",
+                         "h2d_bytes_per_step": T * 4, "d2h_bytes_per_step": cfg["vocab_size"] * 4})
+    print(json.dumps(res), flush=True)
+    cache.close()
+    model.close()
+
+
+def run_c4(args, rank, world, local_rank):
+    """C4: the 8B-class config sharded tensor-parallel over the ranks (one
+    process per GPU, NCCL allreduce per sublayer); 128-token prompt, then a
+    512-token greedy decode per step from the rewound cache.  value = decode
+    tok/s of the one sequence (strong scaling), max over ranks."""
+    import ctypes
+
+    import torch
+
+    torch.cuda.set_device(local_rank)
+    dist = dist_init(world, local_rank)
+    from tinyminigo_b200 import synth
+    from tinyminigo_b200._lib import check, lib
+    from tinyminigo_b200.model import Model
+
+    P4, G4 = 128, 512
+    cfg = synth.CONFIGS["c4"]
+    t0 = time.time()
+    w = synth.make_weights(cfg, 2025, device="cuda")
+    log(f"c4 weights generated in {time.time() - t0:.1f}s")
+    tp = None
+    if world > 1:
+        uid = (ctypes.c_uint8 * 128)()
+        if rank == 0:
+            check(lib().tmg_tp_unique_id(uid))
+        t = torch.tensor(list(bytes(uid)), dtype=torch.uint8, device="cuda")
+        dist.broadcast(t, 0)
+        tp = (bytes(t.cpu().tolist()), rank, world)
+    model = Model.from_tensors(model_config(cfg), w, device=local_rank, tp=tp)
+    del w
+    prompt = synth.random_prompt(cfg["vocab_size"], P4, 17)
+    cache = model.new_cache(P4 + G4 + 8)
+    logits = model.forward_seq(prompt, cache)
+    tok = int(np.argmax(logits))
+    stream = torch.cuda.ExternalStream(model.stream_handle(), device=local_rank)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def step():
+        cache.truncate(P4)
+        model.decode([tok], cache, G4, wait=False)
+
+    for _ in range(args.warmup):
+        step()
+    model.sync()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        model.sync()
+        torch.cuda.synchronize()
+    ms = max_over_ranks(dist, ev0.elapsed_time(ev1)) / args.steps
+    value = G4 / (ms / 1e3)
+    h, L, I, V = cfg["hidden_size"], cfg["num_hidden_layers"], cfg["intermediate_size"], cfg["vocab_size"]
+    qd, kd = cfg["num_attention_heads"] * cfg["head_dim"], cfg["num_key_value_heads"] * cfg["head_dim"]
+    wbytes = 2 * (L * ((qd + 2 * kd) * h + h * qd + 3 * I * h) + V * h)
+    kvb = L * 2 * kd * 4 * (P4 + G4 / 2)
+    per_gpu = (wbytes + kvb) / world
+    gbs = per_gpu / (ms / 1e3 / G4) / 1e9
+    peak, peak_kind = peaks()
+    if rank == 0:
+        res = base_line(args, world, "decode_tok_s", value, "tok/s", ms,
+                        {"workload": "c4: 8B-class, untied, 128-token prompt, greedy 512",
+                         "global_batch": 1, "seq_len": P4 + G4,
+                         "parallelism": f"tp{world}" if world > 1 else "single GPU"},
+                        "strong", clk.summary(),
+                        roofline={"bound": "hbm", "kernel": "decode step (per-GPU bytes)",
+                                  "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                                  "frac": round(gbs / peak, 4), "traffic": None,
+                                  "algorithmic_bytes_per_token_per_gpu": int(per_gpu),
+                                  "peak_kind": peak_kind},
+                        gpu_launches=None)
+        print(json.dumps(res), flush=True)
+    if dist is not None:
+        dist.barrier()
+    cache.close()
+    model.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def run_c5(args, rank, world, local_rank):
+    """C5: 16 streams, each with its own random 32768-token prompt prefilled,
+    then 256 sampled steps (T 0.8, top-k 40, top-p 0.95, penalty 1.1, seed
+    base + i) through generate_batch.  value = aggregate decode tok/s: the
+    generate_batch time minus the time of the same 16 prefills measured
+    alone right before (the API prefills inside generate)."""
+    import torch
+
+    if rank != 0:
+        return
+    torch.cuda.set_device(local_rank)
+    from tinyminigo_b200 import synth
+    from tinyminigo_b200.model import GenParams, Model, generate_batch
+
+    M, T5, G5 = 16, 32768, 256
+    cfg, w = make_c2("cuda")
+    model = Model.from_tensors(model_config(cfg), w, device=local_rank)
+    prompts = np.stack([synth.random_prompt(cfg["vocab_size"], T5, 100 + i) for i in range(M)])
+    cache = model.new_cache(T5 + G5 + 8, n_streams=M)
+    params = [GenParams(max_tokens=G5, temperature=0.8, top_k=40, top_p=0.95,
+                        repetition_penalty=1.1, seed=1000 + i) for i in range(M)]
+    with ClockSampler(local_rank) as clk:
+        t0 = time.perf_counter()
+        for i in range(M):
+            model.forward_seq(prompts[i], cache, stream=i, want_logits=False)
+        model.sync()
+        t_pre = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        outs = generate_batch(model, prompts, params, cache=cache)
+        t_all = time.perf_counter() - t0
+    dec = max(t_all - t_pre, 1e-9)
+    n_tok = sum(len(o) for o in outs)
+    kv_step = M * cfg["num_hidden_layers"] * 2 * cfg["num_key_value_heads"] * cfg["head_dim"] * 4 * (T5 + G5 / 2)
+    wbytes = sum(c2_bytes(cfg)[0].values()) * cfg["num_hidden_layers"] + c2_bytes(cfg)[1]
+    gbs = (wbytes + kv_step) * G5 / dec / 1e9
+    peak, peak_kind = peaks()
+    res = base_line(args, world, "decode_tok_s", n_tok / dec, "tok/s", dec * 1e3,
+                    {"workload": "c5: c2 shape, 16 streams x 32768-token prompts, 256 sampled "
+                                 "steps (T 0.8, k 40, p 0.95, penalty 1.1)", "global_batch": M,
+                     "seq_len": T5 + G5, "parallelism": "single GPU"}, "weak", clk.summary(),
+                    roofline={"bound": "hbm", "kernel": "decode steps (weights once + 16 KV)",
+                              "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                              "frac": round(gbs / peak, 4), "traffic": None,
+                              "peak_kind": peak_kind},
+                    prefill_s=round(t_pre, 2), generate_batch_s=round(t_all, 2),
+                    timing="host wall clock: generate_batch minus the same prefills alone")
+    print(json.dumps(res), flush=True)
+    cache.close()
+    model.close()
+
+
 def cache_trunc(cache, n):
     cache.truncate(n)
 
@@ -419,7 +639,10 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c2"], default="c2")
+    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5"], default="c2",
+                    help="c2 (default): the headline decode; c3: 2048-token prefill; "
+                         "c4: 8B tensor-parallel decode over the ranks; c5: 16 streams at 32K "
+                         "context, sampled")
     ap.add_argument("--cpu-tokens", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-steps", type=int, default=0,
@@ -438,7 +661,14 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank)
         return
-    run_ours(args, rank, world, local_rank)
+    if args.workload == "c3":
+        run_c3(args, rank, world, local_rank)
+    elif args.workload == "c4":
+        run_c4(args, rank, world, local_rank)
+    elif args.workload == "c5":
+        run_c5(args, rank, world, local_rank)
+    else:
+        run_ours(args, rank, world, local_rank)
 
 
 if __name__ == "__main__":
