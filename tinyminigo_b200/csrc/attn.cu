@@ -429,7 +429,10 @@ __global__ void rope_rows_kernel(float* x, int64_t ld, int n_heads, int d,
 }  // namespace
 
 int attn_decode_nsplit(int nkv, int M, int64_t cap, int num_sms) {
-  const int64_t want = (int64_t(num_sms) * 8 + int64_t(nkv) * M - 1) / (int64_t(nkv) * M);
+  // enough CTAs to fill the GPU, and for long contexts at most ~512
+  // positions (8 tiles, loaded one after another) per split
+  const int64_t fill = (int64_t(num_sms) * 8 + int64_t(nkv) * M - 1) / (int64_t(nkv) * M);
+  const int64_t want = std::max<int64_t>(fill, (cap + 511) / 512);
   const int64_t maxs = (cap + kTile - 1) / kTile;
   int64_t n = std::min<int64_t>(want, maxs);
   return int(std::max<int64_t>(1, std::min<int64_t>(n, 1024)));
