@@ -592,7 +592,7 @@ def run_c5(args, rank, world, local_rank):
     from tinyminigo_b200 import synth
     from tinyminigo_b200.model import GenParams, Model, generate_batch
 
-    M, T5, G5 = 16, 32768, 256
+    M, T5, G5 = 16, args.c5_ctx, args.c5_steps
     cfg, w = make_c2("cuda")
     model = Model.from_tensors(model_config(cfg), w, device=local_rank)
     prompts = np.stack([synth.random_prompt(cfg["vocab_size"], T5, 100 + i) for i in range(M)])
@@ -615,7 +615,7 @@ def run_c5(args, rank, world, local_rank):
     gbs = (wbytes + kv_step) * G5 / dec / 1e9
     peak, peak_kind = peaks()
     res = base_line(args, world, "decode_tok_s", n_tok / dec, "tok/s", dec * 1e3,
-                    {"workload": "c5: c2 shape, 16 streams x 32768-token prompts, 256 sampled "
+                    {"workload": f"c5: c2 shape, 16 streams x {T5}-token prompts, {G5} sampled "
                                  "steps (T 0.8, k 40, p 0.95, penalty 1.1)", "global_batch": M,
                      "seq_len": T5 + G5, "parallelism": "single GPU"}, "weak", clk.summary(),
                     roofline={"bound": "hbm", "kernel": "decode steps (weights once + 16 KV)",
@@ -644,6 +644,8 @@ def main():
                          "c4: 8B tensor-parallel decode over the ranks; c5: 16 streams at 32K "
                          "context, sampled")
     ap.add_argument("--cpu-tokens", type=int, default=8)
+    ap.add_argument("--c5-ctx", type=int, default=32768, help="c5: prompt length per stream")
+    ap.add_argument("--c5-steps", type=int, default=256, help="c5: sampled steps")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-steps", type=int, default=0,
                     help="profiling mode: prefill + this many decode steps, no timing, no output")

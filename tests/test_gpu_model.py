@@ -159,3 +159,22 @@ def test_capacity_and_bad_tokens_are_errors(c1):
         m.prefill([], cache)
     with pytest.raises(Exception, match="top_k"):
         generate(m, d["prompt"], GenParams(max_tokens=3, temperature=0.7, top_k=0))
+
+
+def test_batched_long_prompts_match_single_streams(c2):
+    # 16 streams with 2048-token prompts: the batched decode attention splits
+    # each context into multi-tile ranges, and the position being decoded
+    # can sit in any tile of the last range; every stream must match its
+    # own single-stream run (which decodes through a different kernel)
+    cfg, t = c2
+    cfg2 = synth.with_layers(cfg, 2)
+    t2 = {k: v for k, v in t.items() if not k.startswith("model.layers.")
+          or int(k.split(".")[2]) < 2}
+    m = Model.from_tensors(cfg_obj(cfg2), t2)
+    M, T, steps = 16, 2048, 12
+    prompts = np.stack([synth.random_prompt(cfg["vocab_size"], T, 50 + s) for s in range(M)])
+    outs = generate_batch(m, prompts, [GenParams(max_tokens=steps)] * M)
+    for s in range(M):
+        single = generate(m, prompts[s], GenParams(max_tokens=steps))
+        assert outs[s] == single.tokens, f"stream {s}"
+    m.close()

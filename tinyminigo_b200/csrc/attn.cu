@@ -35,21 +35,40 @@ __device__ __forceinline__ void rot(float a, float b, float c, float s, float* o
   *o1 = __fadd_rn(as, bc);
 }
 
-// Grid (n_kv, nsplit, M); 128 threads.  Dynamic smem: q [G][d], K tile
-// [kTile][d+4], V tile [kTile][d], p [G][kTile].
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// K/V tile buffers of the decode kernel: two (the next tile loads while the
+// current one is used) where they fit the shared-memory budget.
+template <int D>
+constexpr int attn_bufs() { return D <= 64 ? 2 : 1; }
+
+// Grid (n_kv, nsplit, M); 128 threads.  Dynamic smem: q [G][d], K tiles
+// [NB][kTile][d+4], V tiles [NB][kTile][d], p [G][kTile], and the decoded
+// position's rotated k and raw v [2][d].
 template <int D>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDecodeArgs a) {
   extern __shared__ float sm[];
   __shared__ float m_s[16], l_s[16], alpha_s[16];
   __shared__ bool last_s;
+  constexpr int NB = attn_bufs<D>();
   const int kvh = blockIdx.x, split = blockIdx.y, m = blockIdx.z;
   constexpr int d = D;
   const int half = d / 2, G = a.nq / a.nkv, kvd = a.nkv * d;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  float* qs = sm;                      // [G][d]
-  float* ks_ = qs + G * d;             // [kTile][d+4]
-  float* vs = ks_ + kTile * (d + 4);   // [kTile][d]
-  float* ps = vs + kTile * d;          // [G][kTile]
+  float* qs = sm;                           // [G][d]
+  float* ks_ = qs + G * d;                  // [NB][kTile][d+4]
+  float* vs = ks_ + NB * kTile * (d + 4);   // [NB][kTile][d]
+  float* ps = vs + NB * kTile * d;          // [G][kTile]
+  float* kp_s = ps + G * kTile;             // [d] k of the decoded position (rotated)
+  float* vp_s = kp_s + d;                   // [d] its v
 
   if (tid == 0) trace_mark(a.trace, 0);
   pdl_trigger();
@@ -99,89 +118,126 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
       qs[g * d + j + half] = o1;
     }
   }
-  auto load_tile = [&](int t0, int nt) {
-    for (int i = tid; i < nt * d4; i += blockDim.x) {
-      const int t = i / d4, j4 = i % d4;
-      if (own_pos && t0 + t == pos) continue;  // written below from registers
-      const float4 kv4 = *reinterpret_cast<const float4*>(kc + size_t(t0 + t) * kvd + kvh * d + j4 * 4);
-      const float4 vv4 = *reinterpret_cast<const float4*>(vc + size_t(t0 + t) * kvd + kvh * d + j4 * 4);
-      *reinterpret_cast<float4*>(ks_ + t * (d + 4) + j4 * 4) = kv4;
-      *reinterpret_cast<float4*>(vs + t * d + j4 * 4) = vv4;
-    }
-  };
-  if (c0 < c1) load_tile(c0, min(kTile, c1 - c0));
   // the CTA whose range holds pos appends the rotated k and raw v
-  // (KvCache::push, model.rs:432) and puts them in its tile directly
+  // (KvCache::push, model.rs:432) and keeps them for its tile
   if (own_pos) {
     const float* kh = qkv + a.nq * d + kvh * d;
     const float* vh = qkv + (a.nq + a.nkv) * d + kvh * d;
     float* kdst = kc + size_t(pos) * kvd + kvh * d;
     float* vdst = vc + size_t(pos) * kvd + kvh * d;
-    const bool in_first = pos < c0 + kTile;
-    const int tr = pos - c0;
     for (int j = tid; j < half; j += blockDim.x) {
       float o0, o1;
       rot(kh[j], kh[j + half], a.rope_cos[size_t(pos) * half + j],
           a.rope_sin[size_t(pos) * half + j], &o0, &o1);
       kdst[j] = o0;
       kdst[j + half] = o1;
-      if (in_first) {
-        ks_[tr * (d + 4) + j] = o0;
-        ks_[tr * (d + 4) + j + half] = o1;
-      }
+      kp_s[j] = o0;
+      kp_s[j + half] = o1;
     }
     for (int j = tid; j < d; j += blockDim.x) {
       const float v = vh[j];
       vdst[j] = v;
-      if (in_first) vs[tr * d + j] = v;
+      vp_s[j] = v;
     }
   }
+  __syncthreads();
+  // tile (t0, nt) into buffer b: cache rows by cp.async, the decoded
+  // position's row (when in range) from kp_s/vp_s; one commit group
+  auto load_tile = [&](int b, int t0, int nt) {
+    float* kb = ks_ + b * kTile * (d + 4);
+    float* vb = vs + b * kTile * d;
+    for (int i = tid; i < nt * d4; i += blockDim.x) {
+      const int t = i / d4, j4 = i % d4;
+      if (own_pos && t0 + t == pos) {
+        *reinterpret_cast<float4*>(kb + t * (d + 4) + j4 * 4) =
+            *reinterpret_cast<const float4*>(kp_s + j4 * 4);
+        *reinterpret_cast<float4*>(vb + t * d + j4 * 4) =
+            *reinterpret_cast<const float4*>(vp_s + j4 * 4);
+        continue;
+      }
+      cp_async16(kb + t * (d + 4) + j4 * 4, kc + size_t(t0 + t) * kvd + kvh * d + j4 * 4);
+      cp_async16(vb + t * d + j4 * 4, vc + size_t(t0 + t) * kvd + kvh * d + j4 * 4);
+    }
+    cp_async_commit();
+  };
+  if (c0 < c1) load_tile(0, c0, min(kTile, c1 - c0));
   if (tid < G) {
     m_s[tid] = -INFINITY;
     l_s[tid] = 0.f;
   }
-  // outputs owned by this thread: indices tid, tid+128, ... of [G][d]
-  constexpr int kMaxOwn = 8;  // G * d <= 1024
+  // Work split inside a tile, so that each K and V row is read from shared
+  // memory once per head slot rather than once per query head:
+  //  * scores: thread -> position tid % kTile and heads hs, hs + kHS, ...
+  //    (hs = tid / kTile): its K row once, q rows by broadcast;
+  //  * P.V: thread -> column tid % d and heads ps, ps + kPS, ... (ps =
+  //    tid / d): its V column once, p by broadcast.
+  constexpr int kHS = kAttnThreads / kTile;              // head slots, scores
+  constexpr int kPS = kAttnThreads / D >= 1 ? kAttnThreads / D : 1;  // head slots, P.V
+  constexpr int kMaxOwn = 16 / kPS > 0 ? 16 / kPS : 1;   // heads per thread in P.V (G <= 16)
+  constexpr int kMaxSc = 16 / kHS;                       // heads per thread in scores
+  const int pj = tid % d, pslot = tid / d;
   float o_acc[kMaxOwn];
 #pragma unroll
   for (int r = 0; r < kMaxOwn; ++r) o_acc[r] = 0.f;
   __syncthreads();
 
-  for (int t0 = c0; t0 < c1; t0 += kTile) {
+  for (int t0 = c0, it = 0; t0 < c1; t0 += kTile, ++it) {
     const int nt = min(kTile, c1 - t0);
-    if (t0 != c0) {  // later tiles (long contexts)
-      load_tile(t0, nt);
-      __syncthreads();
+    const int b = NB == 2 ? (it & 1) : 0;
+    if (NB == 2) {
+      // the next tile loads into the other buffer while this one is used
+      const bool more = t0 + kTile < c1;
+      if (more) load_tile(b ^ 1, t0 + kTile, min(kTile, c1 - t0 - kTile));
+      if (more) cp_async_wait<1>();
+      else cp_async_wait<0>();
+    } else {
+      if (t0 != c0) load_tile(0, t0, nt);
+      cp_async_wait<0>();
     }
-    // scores: warp w handles heads w, w+4, ...; lane holds positions lane
-    // and lane + 32
-    for (int g = warp; g < G; g += kAttnThreads / 32) {
-      const float* qr = qs + g * d;
-      float sc[2];
+    __syncthreads();
+    const float* kt = ks_ + b * kTile * (d + 4);
+    const float* vt = vs + b * kTile * d;
+    // raw scores s[g][t] = q_g . k_t * scale into ps
+    {
+      const int t = tid % kTile, hs = tid / kTile;
+      float acc[kMaxSc][4];
 #pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        const int t = lane + 32 * h2;
-        sc[h2] = -INFINITY;
-        if (t < nt) {
-          const float* kr = ks_ + t * (d + 4);
-          float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      for (int i = 0; i < kMaxSc; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+      if (t < nt) {
+        const float* kr = kt + t * (d + 4);
+#pragma unroll 4
+        for (int j = 0; j < d; j += 4) {
+          const float4 k4 = *reinterpret_cast<const float4*>(kr + j);
 #pragma unroll
-          for (int j = 0; j < d; j += 4) {
-            const float4 k4 = *reinterpret_cast<const float4*>(kr + j);
-            const float4 q4 = *reinterpret_cast<const float4*>(qr + j);
-            a0 = fmaf(q4.x, k4.x, a0);
-            a1 = fmaf(q4.y, k4.y, a1);
-            a2 = fmaf(q4.z, k4.z, a2);
-            a3 = fmaf(q4.w, k4.w, a3);
+          for (int i = 0; i < kMaxSc; ++i) {
+            const int g = hs + i * kHS;
+            if (g < G) {
+              const float4 q4 = *reinterpret_cast<const float4*>(qs + g * d + j);
+              acc[i][0] = fmaf(q4.x, k4.x, acc[i][0]);
+              acc[i][1] = fmaf(q4.y, k4.y, acc[i][1]);
+              acc[i][2] = fmaf(q4.z, k4.z, acc[i][2]);
+              acc[i][3] = fmaf(q4.w, k4.w, acc[i][3]);
+            }
           }
-          sc[h2] = ((a0 + a1) + (a2 + a3)) * a.scale;
         }
       }
-      const float mt = warp_max(fmaxf(sc[0], sc[1]));
+#pragma unroll
+      for (int i = 0; i < kMaxSc; ++i) {
+        const int g = hs + i * kHS;
+        if (g < G)
+          ps[g * kTile + t] =
+              t < nt ? ((acc[i][0] + acc[i][1]) + (acc[i][2] + acc[i][3])) * a.scale : -INFINITY;
+      }
+    }
+    __syncthreads();
+    // online softmax per head: a warp per head, lanes over the positions
+    for (int g = warp; g < G; g += kAttnThreads / 32) {
+      const float s0 = ps[g * kTile + lane], s1 = ps[g * kTile + lane + 32];
+      const float mt = warp_max(fmaxf(s0, s1));
       const float m_old = m_s[g];
       const float m_new = fmaxf(m_old, mt);
-      const float p0 = lane < nt ? expf(sc[0] - m_new) : 0.f;
-      const float p1 = lane + 32 < nt ? expf(sc[1] - m_new) : 0.f;
+      const float p0 = lane < nt ? expf(s0 - m_new) : 0.f;
+      const float p1 = lane + 32 < nt ? expf(s1 - m_new) : 0.f;
       const float lsum = warp_sum(p0 + p1);
       ps[g * kTile + lane] = p0;
       ps[g * kTile + lane + 32] = p1;
@@ -193,22 +249,23 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
       }
     }
     __syncthreads();
+    // P.V over the tile's nt rows, in four independent chains over t
+    if (pslot < kPS) {
 #pragma unroll
-    for (int r = 0; r < kMaxOwn; ++r) {
-      const int idx = tid + r * kAttnThreads;
-      if (idx < G * d) {
-        const int g = idx / d, j = idx % d;
-        // P.V over the tile's nt rows, in four independent chains over t
-        float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
-        int t = 0;
-        for (; t + 4 <= nt; t += 4) {
-          b0 = fmaf(ps[g * kTile + t], vs[t * d + j], b0);
-          b1 = fmaf(ps[g * kTile + t + 1], vs[(t + 1) * d + j], b1);
-          b2 = fmaf(ps[g * kTile + t + 2], vs[(t + 2) * d + j], b2);
-          b3 = fmaf(ps[g * kTile + t + 3], vs[(t + 3) * d + j], b3);
+      for (int r = 0; r < kMaxOwn; ++r) {
+        const int g = pslot + r * kPS;
+        if (g < G) {
+          float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
+          int t = 0;
+          for (; t + 4 <= nt; t += 4) {
+            b0 = fmaf(ps[g * kTile + t], vt[t * d + pj], b0);
+            b1 = fmaf(ps[g * kTile + t + 1], vt[(t + 1) * d + pj], b1);
+            b2 = fmaf(ps[g * kTile + t + 2], vt[(t + 2) * d + pj], b2);
+            b3 = fmaf(ps[g * kTile + t + 3], vt[(t + 3) * d + pj], b3);
+          }
+          for (; t < nt; ++t) b0 = fmaf(ps[g * kTile + t], vt[t * d + pj], b0);
+          o_acc[r] = fmaf(o_acc[r], alpha_s[g], (b0 + b1) + (b2 + b3));
         }
-        for (; t < nt; ++t) b0 = fmaf(ps[g * kTile + t], vs[t * d + j], b0);
-        o_acc[r] = fmaf(o_acc[r], alpha_s[g], (b0 + b1) + (b2 + b3));
       }
     }
     __syncthreads();
@@ -216,13 +273,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
   float* out = a.out + size_t(m) * a.nq * d + kvh * G * d;
   if (n_used == 1) {
     // the whole context in one CTA: finish here, no partials
-    if (split == 0) {
+    if (split == 0 && pslot < kPS) {
 #pragma unroll
       for (int r = 0; r < kMaxOwn; ++r) {
-        const int idx = tid + r * kAttnThreads;
-        if (idx < G * d) {
-          const float L = l_s[idx / d];
-          out[idx] = L > 0.f ? o_acc[r] / L : 0.f;
+        const int g = pslot + r * kPS;
+        if (g < G) {
+          const float L = l_s[g];
+          out[g * d + pj] = L > 0.f ? o_acc[r] / L : 0.f;
         }
       }
     }
@@ -232,10 +289,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
   // partial (m, l, o[d]) per head
   if (split < n_used) {
     float* part = a.part + ((size_t(m) * a.nkv + kvh) * a.nsplit + split) * G * (d + 2);
+    if (pslot < kPS) {
 #pragma unroll
-    for (int r = 0; r < kMaxOwn; ++r) {
-      const int idx = tid + r * kAttnThreads;
-      if (idx < G * d) part[(idx / d) * (d + 2) + 2 + (idx % d)] = o_acc[r];
+      for (int r = 0; r < kMaxOwn; ++r) {
+        const int g = pslot + r * kPS;
+        if (g < G) part[g * (d + 2) + 2 + pj] = o_acc[r];
+      }
     }
     if (tid < G) {
       part[tid * (d + 2)] = m_s[tid];
@@ -430,7 +489,7 @@ __global__ void rope_rows_kernel(float* x, int64_t ld, int n_heads, int d,
 
 int attn_decode_nsplit(int nkv, int M, int64_t cap, int num_sms) {
   // enough CTAs to fill the GPU, and for long contexts at most ~512
-  // positions (8 tiles, loaded one after another) per split
+  // positions (8 tiles) per split
   const int64_t fill = (int64_t(num_sms) * 8 + int64_t(nkv) * M - 1) / (int64_t(nkv) * M);
   const int64_t want = std::max<int64_t>(fill, (cap + 511) / 512);
   const int64_t maxs = (cap + kTile - 1) / kTile;
@@ -467,7 +526,9 @@ cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s, bool pdl
     default: return cudaErrorInvalidValue;
   }
   // tiles, or the combine's per-split weights when those are larger
-  const size_t tiles = size_t(G) * a.d + kTile * (a.d + 4) + kTile * a.d + G * kTile;
+  const int nb = a.d <= 64 ? 2 : 1;  // attn_bufs<D>()
+  const size_t tiles = size_t(G) * a.d + size_t(nb) * kTile * (a.d + 4) + size_t(nb) * kTile * a.d +
+                       G * kTile + 2 * size_t(a.d);
   const size_t smem = sizeof(float) * std::max<size_t>(tiles, size_t(G) * a.nsplit);
   if (smem > size_t(kMaxAttnSmem)) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
