@@ -79,7 +79,8 @@ struct tmg_ctx {
   float* logits_full = nullptr;  // [M, V] gathered logits under TP
   unsigned int* bar = nullptr;   // grid barrier of the fused decode kernel
   unsigned long long* ll = nullptr;  // its tagged exchange words (x, att, act, qkv)
-  int fused_pf = 0;              // its L2 prefetch distance (stages; TMG_FUSED_PF)
+  int fused_pf = 0;              // its stall-time L2 prefetch distance (stages; TMG_FUSED_PF)
+  int fused_pf_pace = 0;         // cycles between those prefetches (TMG_FUSED_PF_PACE)
   int fused_stages = 4;          // its ring depth cap (0: all that fit; TMG_FUSED_STAGES)
   bool fused_ok = false;         // the fused batch-1 decode kernel takes this shape
   // prefill scratch
@@ -396,6 +397,7 @@ int alloc_model(tmg_ctx* c) {
   CK(zero_sync(c, c->bar, fused_bar_words() * sizeof(unsigned int)), "memset");
   c->fused_ok = c->world == 1 && fused_supported(c->h, c->nq, c->nkv, c->d, c->I, c->V_l, c->num_sms);
   if (const char* pf = getenv("TMG_FUSED_PF")) c->fused_pf = atoi(pf);
+  if (const char* pp = getenv("TMG_FUSED_PF_PACE")) c->fused_pf_pace = atoi(pp);
   if (const char* ns = getenv("TMG_FUSED_STAGES")) c->fused_stages = atoi(ns);
   c->has_model = true;
   return TMG_OK;
@@ -804,6 +806,7 @@ cudaError_t launch_fused(tmg_ctx* c, tmg_kv* kv, const StreamState& st, int64_t 
   f.bar = c->bar;
   f.nsplit = kv->nsplit_f;
   f.pf_ahead = c->fused_pf;
+  f.pf_pace = c->fused_pf_pace;
   f.max_stages = c->fused_stages;
   f.st = st;
   f.n_steps = int(n_steps);

@@ -60,8 +60,8 @@ static_assert(4 * kWarp * kProducerRegs + 2 * 4 * kWarp * kConsumerRegs <= kFThr
 constexpr int kStage = 32 * 1024;                  // ring stage bytes
 constexpr int kMaxStagesF = 6;
 constexpr int kTileF = 32;                         // attention positions per tile
-constexpr int kMaxRes = 1024;                      // per-warp results of one phase
-constexpr int kMaxLocal = kMaxRes / kCWarps;       // groups of one CTA in a phase
+constexpr int kMaxRes = 2048;                      // per-warp results of one phase
+constexpr int kMaxLocal = kMaxRes / kCWarps;       // LM head groups of one CTA (deferred)
 constexpr int kBarWords = 128;                     // words of the barrier block
 constexpr int kTraceWords = 12;                    // trace record per CTA and phase
 
@@ -146,21 +146,27 @@ __device__ __forceinline__ void rot(float a, float b, float c, float s, float* o
 
 // ---------------------------------------------------------------------------
 // Phase geometry.  A group is one stage of rpc = 8 / ks rows of K elements
-// (at most 32 KB); warp w takes row slot w / ks and K segment w % ks.
+// (at most 32 KB).  Layer phases (QKV, O, GU, DOWN): warp w takes K segment
+// w of 8 (K / 8 elements) of every row.  LM head: warp w takes row slot
+// w / ks and K segment w % ks.
 // ---------------------------------------------------------------------------
 struct PhaseGeo {
   const uint16_t* w;
   const uint16_t* w2;      // up rows (GU)
-  int64_t N;               // output rows
+  int N;                   // output rows
   int K;
-  int ks;                  // K split over warps
-  int chunks;              // 256-element chunks per warp segment
+  int ks;                  // K split over warps (LM head)
+  int chunks;              // 256-element chunks per warp segment (LM head)
   int rpc;                 // row slots per group (8 / ks)
   int rpg;                 // output rows per group (GU: rpc / 2 gate + as many up)
-  int64_t ngroups;
-  int64_t pair_groups;     // QKV: leading groups holding RoPE partner rows
+  int lrpc, lrpg;          // their log2 (all of rpc, rpg, D are powers of two)
+  int ngroups;
+  int pair_groups;         // QKV: leading groups holding RoPE partner rows
   int D;                   // head dim
+  int lD;
 };
+
+__device__ __forceinline__ int ilog2(int p) { return __ffs(p) - 1; }  // p a power of two
 
 __device__ __forceinline__ int ksplit(int K) {
   int ks = 1;
@@ -174,34 +180,38 @@ __device__ __forceinline__ PhaseGeo geo(const FusedArgs& a, const FusedLayer* la
   g.w2 = nullptr;
   g.pair_groups = 0;
   g.D = a.d;
+  g.lD = ilog2(a.d);
   switch (ph) {
     case PH_QKV: g.w = L.wqkv; g.N = (a.nq + 2 * a.nkv) * a.d; g.K = a.h; break;
     case PH_O: g.w = L.wo; g.N = a.h; g.K = a.nq * a.d; break;
     case PH_GU: g.w = L.wg; g.w2 = L.wu; g.N = a.I; g.K = a.h; break;
     case PH_DOWN: g.w = L.wd; g.N = a.h; g.K = a.I; break;
-    default: g.w = a.lm_head; g.N = a.V; g.K = a.h; break;
+    default: g.w = a.lm_head; g.N = int(a.V); g.K = a.h; break;
   }
   g.ks = ksplit(g.K);
   g.chunks = g.K / g.ks / 256;
   g.rpc = kCWarps / g.ks;
   g.rpg = ph == PH_GU ? g.rpc / 2 : g.rpc;
-  g.ngroups = (g.N + g.rpg - 1) / g.rpg;
-  if (ph == PH_QKV) g.pair_groups = int64_t(a.nq + a.nkv) * a.d / g.rpc;
+  g.lrpc = ilog2(g.rpc);
+  g.lrpg = ilog2(g.rpg);
+  g.ngroups = (g.N + g.rpg - 1) >> g.lrpg;
+  if (ph == PH_QKV) g.pair_groups = ((a.nq + a.nkv) * a.d) >> g.lrpc;
   return g;
 }
 
 // Output row held by `slot` of group grp (GU: the gate/up row index).
-__device__ __forceinline__ int64_t slot_row(const PhaseGeo& g, int64_t grp, int slot) {
+__device__ __forceinline__ int slot_row(const PhaseGeo& g, int grp, int slot) {
   if (g.pair_groups > 0) {
     if (grp < g.pair_groups) {
-      const int hp = g.rpc / 2, half = g.D / 2;
-      const int64_t gph = half / hp;  // groups per head
-      const int64_t ra = (grp / gph) * g.D + (grp % gph) * hp;
+      // rpc / 2 rows from each RoPE half of a head; D / rpc groups per head
+      const int hp = g.rpc >> 1, half = g.D >> 1;
+      const int lgph = g.lD - g.lrpc;  // log2 of groups per head
+      const int ra = ((grp >> lgph) << g.lD) + ((grp & ((1 << lgph) - 1)) << (g.lrpc - 1));
       return slot < hp ? ra + slot : ra + half + (slot - hp);
     }
-    return grp * g.rpc + slot;  // v rows follow the q and k rows
+    return (grp << g.lrpc) + slot;  // v rows follow the q and k rows
   }
-  return grp * g.rpg + (slot % g.rpg);
+  return (grp << g.lrpg) + (slot & (g.rpg - 1));
 }
 
 // The (at most two) contiguous row ranges a group copies into its stage.
@@ -211,49 +221,50 @@ struct Ranges {
   uint32_t doff[2];
   int n;
 };
-__device__ __forceinline__ Ranges group_ranges(const PhaseGeo& g, int64_t grp) {
+__device__ __forceinline__ Ranges group_ranges(const PhaseGeo& g, int grp) {
   Ranges r;
   const uint32_t rowb = uint32_t(g.K) * 2;
   if (g.pair_groups > 0) {
-    const int64_t ra = slot_row(g, grp, 0);
+    const int ra = slot_row(g, grp, 0);
     if (grp < g.pair_groups) {
       const int hp = g.rpc / 2;
       r.n = 2;
-      r.src[0] = g.w + ra * g.K;
-      r.src[1] = g.w + (ra + g.D / 2) * g.K;
+      r.src[0] = g.w + size_t(ra) * g.K;
+      r.src[1] = g.w + size_t(ra + g.D / 2) * g.K;
       r.bytes[0] = r.bytes[1] = uint32_t(hp) * rowb;
       r.doff[0] = 0;
       r.doff[1] = uint32_t(hp) * rowb;
     } else {
       r.n = 1;
-      r.src[0] = g.w + ra * g.K;
+      r.src[0] = g.w + size_t(ra) * g.K;
       r.bytes[0] = uint32_t(g.rpc) * rowb;
       r.doff[0] = 0;
     }
     return r;
   }
-  const int64_t r0 = grp * g.rpg;
-  const int64_t nr = min(int64_t(g.rpg), g.N - r0);
+  const int r0 = grp << g.lrpg;
+  const int nr = min(g.rpg, g.N - r0);
   r.n = g.w2 ? 2 : 1;
-  r.src[0] = g.w + r0 * g.K;
+  r.src[0] = g.w + size_t(r0) * g.K;
   r.bytes[0] = uint32_t(nr) * rowb;
   r.doff[0] = 0;
   if (g.w2) {
-    r.src[1] = g.w2 + r0 * g.K;
+    r.src[1] = g.w2 + size_t(r0) * g.K;
     r.bytes[1] = r.bytes[0];
     r.doff[1] = uint32_t(g.rpg) * rowb;
   }
   return r;
 }
 
-// First group of this CTA in a phase whose groups start at rotation `off`.
-__device__ __forceinline__ int64_t first_group(int off) {
-  const int n = gridDim.x;
-  return int64_t(((int(blockIdx.x) - off) % n + n) % n);
+// First group of this CTA in a phase whose groups start at rotation `off`
+// (0 <= off < gridDim.x).
+__device__ __forceinline__ int first_group(int off) {
+  const int d = int(blockIdx.x) - off;
+  return d < 0 ? d + int(gridDim.x) : d;
 }
 
 // Upper bound on the kernel's static shared memory, checked at prepare time.
-constexpr size_t kStaticReserve = 8 * 1024;
+constexpr size_t kStaticReserve = 12 * 1024;
 
 struct Shared {
   uint64_t full[kMaxStagesF];
@@ -267,6 +278,7 @@ struct Shared {
   volatile int abort;      // stop issuing / waiting (error or early end)
   volatile int issued;     // producer: stages issued so far
   volatile int prod_done;  // producer: no more stages will be issued
+  volatile int streaming;  // consumers: inside a GEMV's stage loop
 };
 
 // ---------------------------------------------------------------------------
@@ -313,14 +325,14 @@ __device__ bool grid_sync(const FusedArgs& a, unsigned int& target, Shared& S,
 struct Cursor {
   const FusedLayer* layers;  // the per-layer table in shared memory
   int step, l, ph, off;
-  int64_t grp;
+  int grp;
   PhaseGeo g;
   bool valid;
 };
 
 __device__ __forceinline__ void cur_settle(const FusedArgs& a, Cursor& c) {
   while (c.valid && c.grp >= c.g.ngroups) {
-    c.off = int((c.off + c.g.ngroups) % gridDim.x);
+    c.off = (c.off + c.g.ngroups) % int(gridDim.x);
     if (c.ph == PH_HEAD) {
       if (++c.step >= a.n_steps) {
         c.valid = false;
@@ -360,26 +372,37 @@ __device__ void producer(const FusedArgs& a, const FusedLayer* layers, Shared& S
   const int nph = a.L * 5 + 1;
   Cursor ic, pc;
   cur_begin(a, layers, ic);
+  // pc: the first stage past the ring (stage it + nst), the next one the
+  // stall-time L2 prefetch may bring in; pf counts the stages it passed
   pc = ic;
   int it = 0, pf = 0;
+  for (int k = 0; k < nst && pc.valid; ++k, ++pf) cur_next(a, pc);
+  long long pf_next = 0;  // clock of the next prefetch allowed (pacing)
   unsigned long long* tr_cur = nullptr;  // diagnostics of the phase being issued
   unsigned long long t_last = 0, c_wait = 0, c_issue = 0;
   while (ic.valid) {
-    // L2 prefetch of stages it + nst .. it + nst + pf_ahead - 1
-    while (pc.valid && pf < it + nst + a.pf_ahead) {
-      if (pf >= it + nst) {
-        const Ranges r = group_ranges(pc.g, pc.grp);
-        l2_prefetch(r.src[0], r.bytes[0]);
-        if (r.n > 1) l2_prefetch(r.src[1], r.bytes[1]);
-      }
-      cur_next(a, pc);
-      ++pf;
-    }
     const int s = it % nst;
     const uint32_t par = (it / nst) & 1;
     if (S.abort) return;
     const long long c0 = clock64();
-    if (!mbar_wait(&S.empty[s], par ^ 1)) {
+    // While the slot is busy and the consumers are outside a GEMV (waiting
+    // on an exchange, in attention, in an epilogue), the weight stream
+    // would stall: bring the stages after the ring into L2 instead, at most
+    // pf_ahead past it, one every pf_pace cycles.
+    bool got = mbar_try(&S.empty[s], par ^ 1);
+    while (!got && a.pf_ahead > 0 && S.streaming == 0 && pc.valid && pf < it + nst + a.pf_ahead) {
+      const long long now = clock64();
+      if (now >= pf_next) {
+        const Ranges r = group_ranges(pc.g, pc.grp);
+        l2_prefetch(r.src[0], r.bytes[0]);
+        if (r.n > 1) l2_prefetch(r.src[1], r.bytes[1]);
+        cur_next(a, pc);
+        ++pf;
+        pf_next = now + a.pf_pace;
+      }
+      got = mbar_try(&S.empty[s], par ^ 1);
+    }
+    if (!got && !mbar_wait(&S.empty[s], par ^ 1)) {
       S.abort = 1;
       if (a.err) atomicExch(a.err, 2);
       return;
@@ -410,6 +433,10 @@ __device__ void producer(const FusedArgs& a, const FusedLayer* layers, Shared& S
     }
     cur_next(a, ic);
     ++it;
+    if (pf < it + nst) {  // the ring moved past pc
+      if (pc.valid) cur_next(a, pc);
+      ++pf;
+    }
   }
   if (tr_cur) {
     tr_cur[3] = t_last;
@@ -662,7 +689,7 @@ struct RingPos {
 // head with ks == 1): logits and the argmax candidate directly; otherwise
 // the sums go to S.res for the phase's epilogue.  Returns the number of
 // local groups; tw (diagnostics) receives the first stage's arrival time.
-__device__ __forceinline__ int gemv_block(int64_t ngroups, int K, int ks, int rpg, int64_t N,
+__device__ __forceinline__ int gemv_block(int ngroups, int K, int ks, int rpg, int N,
                                        int chunks, const float* src, const float* nw,
                                        float eps, int n_norm, int off,
                                        RingPos& rp_io, int nst, const uint8_t* ring, Shared& S,
@@ -683,11 +710,12 @@ __device__ __forceinline__ int gemv_block(int64_t ngroups, int K, int ks, int rp
   }
   RingPos rp = rp_io;
   unsigned long long best = best_io;
+  if (threadIdx.x == 0) S.streaming = 1;
   // this lane's first weight element in stage 0
   const uint16_t* wbase =
       reinterpret_cast<const uint16_t*>(ring + size_t(slot) * K * 2) + kbase + lane * 8;
   int kl = 0;
-  for (int64_t grp = first_group(off); grp < ngroups; grp += gridDim.x, rp.next(nst), ++kl) {
+  for (int grp = first_group(off); grp < ngroups; grp += gridDim.x, rp.next(nst), ++kl) {
     const int s = rp.s;
     float acc = 0.f;
     const bool ok = !S.abort && mbar_wait(&S.full[s], rp.par);
@@ -710,7 +738,7 @@ __device__ __forceinline__ int gemv_block(int64_t ngroups, int K, int ks, int rp
     acc = warp_sum(acc);
     if (lane == 0) {
       if (imm) {
-        const int64_t r = grp * rpg + slot;
+        const int r = grp * rpg + slot;
         if (r < N) {
           logits[r] = acc;
           const unsigned long long kk = argmax_key(acc, uint32_t(r));
@@ -721,6 +749,7 @@ __device__ __forceinline__ int gemv_block(int64_t ngroups, int K, int ks, int rp
       }
     }
   }
+  if (threadIdx.x == 0) S.streaming = 0;
   rp_io = rp;
   best_io = best;
   return kl;
@@ -733,6 +762,119 @@ __device__ __forceinline__ float res_val(const Shared& S, int kl, int slot, int 
   return v;
 }
 
+// Layer phases: row `slot` of local group kl, the sum of the 8 warps' K
+// segments in warp order.
+__device__ __forceinline__ float res_k(const Shared& S, int kl, int slot, int rpc) {
+  const float* r = S.res + (kl * rpc + slot) * kCWarps;
+  return ((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7]));
+}
+
+// One layer-phase GEMV over this CTA's groups (R = rpc rows per stage):
+// warp w holds x[w*K/8, (w+1)*K/8) (chunks 256-element chunks, lane-major
+// in shared memory) and dots it with that segment of all R rows of every
+// stage; a transposed butterfly (R values per lane -> one row per lane
+// group) reduces over the lanes, and each warp's R partial sums go to
+// S.res[(kl * R + row) * 8 + warp] for the epilogue.  Returns the number
+// of local groups.
+template <int R>
+__device__ __forceinline__ int gemv_kseg(int ngroups, int K, int chunks, const float* src,
+                                         int off, RingPos& rp_io, int nst, const uint8_t* ring,
+                                         Shared& S, unsigned long long* tw) {
+  constexpr int M = R == 8 ? 3 : R == 4 ? 2 : R == 2 ? 1 : 0;  // log2 R
+  constexpr int NC = 8 / R;                                      // most chunks a warp holds
+  constexpr int NA = 8 / R;                                      // accumulators per row
+  // one or two rows per stage (segments of 4 to 8 chunks): x is read from
+  // shared memory with each stage instead of held in registers
+  constexpr bool XS = R <= 2;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kbase = warp * chunks * 256;
+  const long long c0 = tw ? clock64() : 0;
+  float4 xa[XS ? 1 : NC], xb[XS ? 1 : NC];
+#pragma unroll
+  for (int c = 0; c < (XS ? 0 : NC); ++c) {
+    if (c < chunks) {
+      const float* p = src + kbase + c * 256 + lane * 4;  // lane-major layout
+      xa[c] = *reinterpret_cast<const float4*>(p);
+      xb[c] = *reinterpret_cast<const float4*>(p + 128);
+    }
+  }
+  if (tw && threadIdx.x == 0) {
+    tw[8] = clock64() - c0;
+    tw[9] = 0;
+  }
+  const long long c2 = tw ? clock64() : 0;
+  if (threadIdx.x == 0) S.streaming = 1;
+  RingPos rp = rp_io;
+  const uint16_t* wbase = reinterpret_cast<const uint16_t*>(ring) + kbase + lane * 8;
+  const int myrow = M > 0 ? (lane >> (5 - M)) & (R - 1) : 0;
+  const bool writer = (lane & ((32 >> M) - 1)) == 0;
+  int kl = 0;
+  for (int grp = first_group(off); grp < ngroups; grp += gridDim.x, rp.next(nst), ++kl) {
+    const int s = rp.s;
+    float acc[R][NA];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int i = 0; i < NA; ++i) acc[r][i] = 0.f;
+    const bool ok = !S.abort && mbar_wait(&S.full[s], rp.par);
+    if (tw && kl == 0 && threadIdx.x == 0) {
+      tw[6] = global_ns();
+      tw[4] = clock64() - c2;
+    }
+    if (ok) {
+      const uint16_t* wr = wbase + s * (kStage / 2);
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        if (c < chunks) {
+          const float* xp = src + kbase + c * 256 + lane * 4;
+          const float4 ua = XS ? *reinterpret_cast<const float4*>(xp) : xa[XS ? 0 : c];
+          const float4 ub = XS ? *reinterpret_cast<const float4*>(xp + 128) : xb[XS ? 0 : c];
+          const float xv[8] = {ua.x, ua.y, ua.z, ua.w, ub.x, ub.y, ub.z, ub.w};
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const uint4 w = *reinterpret_cast<const uint4*>(wr + size_t(r) * K + c * 256);
+            const float wv[8] = {bf16lo(w.x), bf16hi(w.x), bf16lo(w.y), bf16hi(w.y),
+                                 bf16lo(w.z), bf16hi(w.z), bf16lo(w.w), bf16hi(w.w)};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[r][e % NA] = fmaf(xv[e], wv[e], acc[r][e % NA]);
+          }
+        }
+      }
+    } else if (lane == 0) {
+      S.abort = 1;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&S.empty[s]);
+    float v[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      float t = acc[r][0];
+#pragma unroll
+      for (int i = 1; i < NA; ++i) t += acc[r][i];
+      v[r] = t;
+    }
+    // halve the rows held per lane M times (lane bit 16, 8, 4 picks the
+    // upper half), then sum over the lanes that share a row
+#pragma unroll
+    for (int st = 0; st < M; ++st) {
+      const int h = R >> (st + 1), bit = 16 >> st;
+      const bool up = (lane & bit) != 0;
+#pragma unroll
+      for (int i = 0; i < h; ++i) {
+        const float send = up ? v[i] : v[i + h];
+        const float keep = up ? v[i + h] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+      }
+    }
+#pragma unroll
+    for (int bit = 16 >> M; bit >= 1; bit >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], bit);
+    if (writer && (kl + 1) * R * kCWarps <= kMaxRes) S.res[(kl * R + myrow) * kCWarps + warp] = v[0];
+  }
+  if (threadIdx.x == 0) S.streaming = 0;
+  rp_io = rp;
+  return kl;
+}
+
 // QKV epilogue: the rmsnorm factor (scale), then RoPE on the q/k partner
 // rows at position pos (rope_s: the cos then sin row of pos).  q, k and v of the position go out as tagged
 // words; k and v are also appended to the cache at pos (when there is room),
@@ -741,18 +883,18 @@ __device__ __forceinline__ void epi_qkv(const FusedArgs& a, const FusedLayer& L,
                                         int off, int nloc, int pos, bool append,
                                         const float* rope_s, float scale, uint32_t tag, Shared& S) {
   const int D = g.D, half = D / 2, hp = g.rpc / 2, kvd = a.nkv * D;
-  const int64_t f = first_group(off);
-  const int64_t vbase = int64_t(a.nq + a.nkv) * D;
-  for (int i = threadIdx.x; i < nloc * g.rpc; i += kCThreads) {
-    const int kl = i / g.rpc, slot = i % g.rpc;
-    const int64_t grp = f + int64_t(kl) * gridDim.x;
+  const int f = first_group(off);
+  const int vbase = (a.nq + a.nkv) * D;
+  for (int i = threadIdx.x; i < (nloc << g.lrpc); i += kCThreads) {
+    const int kl = i >> g.lrpc, slot = i & (g.rpc - 1);
+    const int grp = f + kl * int(gridDim.x);
     if (grp < g.pair_groups) {
       if (slot >= hp) continue;  // done with its partner
-      const int64_t ra = slot_row(g, grp, slot);
-      const int64_t head = ra / D;
-      const int j = int(ra % D);
+      const int ra = slot_row(g, grp, slot);
+      const int head = ra >> g.lD;
+      const int j = ra & (D - 1);
       float o0, o1;
-      rot(res_val(S, kl, slot, g.ks) * scale, res_val(S, kl, slot + hp, g.ks) * scale, rope_s[j],
+      rot(res_k(S, kl, slot, g.rpc) * scale, res_k(S, kl, slot + hp, g.rpc) * scale, rope_s[j],
           rope_s[half + j], &o0, &o1);
       ll_store(a.qkv_ll + ra, o0, tag);
       ll_store(a.qkv_ll + ra + half, o1, tag);
@@ -762,8 +904,8 @@ __device__ __forceinline__ void epi_qkv(const FusedArgs& a, const FusedLayer& L,
         kr[j + half] = o1;
       }
     } else {
-      const int64_t r = slot_row(g, grp, slot);
-      const float v = res_val(S, kl, slot, g.ks) * scale;
+      const int r = slot_row(g, grp, slot);
+      const float v = res_k(S, kl, slot, g.rpc) * scale;
       ll_store(a.qkv_ll + r, v, tag);
       if (append) L.vc[size_t(pos) * kvd + (r - vbase)] = v;
     }
@@ -775,11 +917,11 @@ __device__ __forceinline__ void epi_qkv(const FusedArgs& a, const FusedLayer& L,
 __device__ __forceinline__ void epi_residual(unsigned long long* x_ll, const float* x_s,
                                              const PhaseGeo& g, int off, int nloc, uint32_t tag,
                                              const Shared& S) {
-  const int64_t f = first_group(off);
-  for (int i = threadIdx.x; i < nloc * g.rpc; i += kCThreads) {
-    const int kl = i / g.rpc, slot = i % g.rpc;
-    const int64_t r = (f + int64_t(kl) * gridDim.x) * g.rpg + slot;
-    if (r < g.N) ll_store(x_ll + r, x_s[perm_idx(int(r))] + res_val(S, kl, slot, g.ks), tag);
+  const int f = first_group(off);
+  for (int i = threadIdx.x; i < (nloc << g.lrpc); i += kCThreads) {
+    const int kl = i >> g.lrpc, slot = i & (g.rpc - 1);
+    const int r = ((f + kl * int(gridDim.x)) << g.lrpg) + slot;
+    if (r < g.N) ll_store(x_ll + r, x_s[perm_idx(r)] + res_k(S, kl, slot, g.rpc), tag);
   }
 }
 
@@ -787,12 +929,12 @@ __device__ __forceinline__ void epi_residual(unsigned long long* x_ll, const flo
 // as tagged words.
 __device__ __forceinline__ void epi_swiglu(unsigned long long* act_ll, const PhaseGeo& g, int off,
                                            int nloc, float scale, uint32_t tag, const Shared& S) {
-  const int64_t f = first_group(off);
-  for (int i = threadIdx.x; i < nloc * g.rpg; i += kCThreads) {
-    const int kl = i / g.rpg, q = i % g.rpg;
-    const int64_t r = (f + int64_t(kl) * gridDim.x) * g.rpg + q;
+  const int f = first_group(off);
+  for (int i = threadIdx.x; i < (nloc << g.lrpg); i += kCThreads) {
+    const int kl = i >> g.lrpg, q = i & (g.rpg - 1);
+    const int r = ((f + kl * int(gridDim.x)) << g.lrpg) + q;
     if (r < g.N) {
-      const float gv = res_val(S, kl, q, g.ks) * scale, uv = res_val(S, kl, q + g.rpg, g.ks) * scale;
+      const float gv = res_k(S, kl, q, g.rpc) * scale, uv = res_k(S, kl, q + g.rpg, g.rpc) * scale;
       ll_store(act_ll + r, gv / (1.0f + expf(-gv)) * uv, tag);
     }
   }
@@ -801,10 +943,10 @@ __device__ __forceinline__ void epi_swiglu(unsigned long long* act_ll, const Pha
 // LM head epilogue (ks > 1): logits and this thread's argmax candidate.
 __device__ __forceinline__ void epi_head(float* logits, const PhaseGeo& g, int off, int nloc,
                                          const Shared& S, unsigned long long& best) {
-  const int64_t f = first_group(off);
-  for (int i = threadIdx.x; i < nloc * g.rpc; i += kCThreads) {
-    const int kl = i / g.rpc, slot = i % g.rpc;
-    const int64_t r = (f + int64_t(kl) * gridDim.x) * g.rpg + slot;
+  const int f = first_group(off);
+  for (int i = threadIdx.x; i < (nloc << g.lrpc); i += kCThreads) {
+    const int kl = i >> g.lrpc, slot = i & (g.rpc - 1);
+    const int r = ((f + kl * int(gridDim.x)) << g.lrpg) + slot;
     if (r < g.N) {
       const float v = res_val(S, kl, slot, g.ks);
       logits[r] = v;
@@ -989,9 +1131,10 @@ __device__ __forceinline__ bool merge_head(const AttnArgs a, int kvh, int n_used
   return true;
 }
 
-// D: head dim.  CH: 256-element chunks of every warp segment when all
-// phases agree (8 for 2048-wide segments), 0 = read from the phase.
-template <int D, int CH>
+// D: head dim.  RA: rows per stage of the phases with K = h or n_q * d
+// (QKV, O, GU); RB: of DOWN (K = I).  The LM head's warp segments are 2048
+// elements (8 chunks).
+template <int D, int RA, int RB>
 __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedArgs a, int nst) {
   extern __shared__ __align__(1024) uint8_t dsm[];
   __shared__ Shared S;
@@ -1019,6 +1162,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
     S.abort = 0;
     S.issued = 0;
     S.prod_done = 0;
+    S.streaming = 0;
     S.fail[0] = S.fail[1] = 0;
     mbar_fence_init();
   }
@@ -1100,7 +1244,6 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
                    : kind == 4 ? PH_DOWN : PH_HEAD;
       const int lw = ph == PH_HEAD ? 0 : l;
       const PhaseGeo g = geo(a, layers_s, ph, lw);
-      const int chunks = CH > 0 ? CH : g.chunks;
       // the rmsnorm weights two phases ahead go to nw_s now (its last reader,
       // the previous rmsnorm, is behind a CTA barrier)
       if (ph == PH_O) stage_vec_perm(nw_s, layers_s[l].post_norm, a.h);
@@ -1176,9 +1319,15 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
       if (tp && threadIdx.x == 0) tp[1] = global_ns();
       const bool imm = ph == PH_HEAD && g.ks == 1;
       unsigned long long best = 0;
-      const int nloc = gemv_block(g.ngroups, g.K, g.ks, g.rpg, g.N, chunks, src,
-                                  ph == PH_HEAD ? nw_s : nullptr, a.eps, a.h, off, rp, nst, ring,
-                                  S, imm, a.logits, best, tp);
+      int nloc = 0;
+      if (ph == PH_HEAD) {
+        nloc = gemv_block(g.ngroups, g.K, g.ks, g.rpg, g.N, 8, src, nw_s, a.eps, a.h, off, rp,
+                          nst, ring, S, imm, a.logits, best, tp);
+      } else if (ph == PH_DOWN) {
+        nloc = gemv_kseg<RB>(g.ngroups, g.K, g.K / (kCWarps * 256), src, off, rp, nst, ring, S, tp);
+      } else {
+        nloc = gemv_kseg<RA>(g.ngroups, g.K, g.K / (kCWarps * 256), src, off, rp, nst, ring, S, tp);
+      }
       if (tp && threadIdx.x == 0) {
         tp[5] = global_ns();
         tp[7] = nloc;
@@ -1196,7 +1345,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
         }
       }
       csync();  // x_s, asm_ and S.res are free for the next phase
-      off = int((off + g.ngroups) % gridDim.x);
+      off = (off + g.ngroups) % int(gridDim.x);
       if (ph == PH_HEAD) {
         best = warp_max_u64(best);
         if (lane == 0) S.best[warp] = best;
@@ -1278,16 +1427,16 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
 // not used, since a consumer's setmaxnreg.inc could then wait forever).
 bool g_regs_ok = true;
 
-template <int D, int CH>
+template <int D, int RA, int RB>
 cudaError_t prepare_one() {
   cudaFuncAttributes fa{};
-  TMG_CUDA_TRY(cudaFuncGetAttributes(&fa, decode_fused_kernel<D, CH>));
+  TMG_CUDA_TRY(cudaFuncGetAttributes(&fa, decode_fused_kernel<D, RA, RB>));
   if (fa.sharedSizeBytes > kStaticReserve) return cudaErrorInvalidConfiguration;
   if (fa.numRegs != kLaunchRegs) g_regs_ok = false;
   int dev = 0, optin = 0;
   TMG_CUDA_TRY(cudaGetDevice(&dev));
   TMG_CUDA_TRY(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-  return set_carveout(decode_fused_kernel<D, CH>, optin - int(fa.sharedSizeBytes));
+  return set_carveout(decode_fused_kernel<D, RA, RB>, optin - int(fa.sharedSizeBytes));
 }
 
 int ksplit_host(int K) {
@@ -1308,12 +1457,28 @@ bool seg_ok(int K) {
 bool local_ok(int64_t ngroups, int num_sms) {
   return (ngroups + num_sms - 1) / num_sms <= kMaxLocal;
 }
+// The (QKV/O/GU, DOWN) rows-per-stage pairs with a kernel instance: 2048-
+// and 8192-wide (1B-class), 4096- and 14336-wide (8B-class) rows.
+bool rows_ok(int ra, int rb) { return (ra == 8 && rb == 2) || (ra == 4 && rb == 1); }
+
+// The same for a layer phase of rpc rows per group (8 partial sums per row).
+bool local_ok_k(int64_t ngroups, int num_sms, int rpc) {
+  return (ngroups + num_sms - 1) / num_sms * rpc * kCWarps <= kMaxRes;
+}
 
 }  // namespace
 
 bool fused_supported(int h, int nq, int nkv, int d, int I, int64_t V, int num_sms) {
   if (!g_regs_ok || nkv <= 0 || nq % nkv != 0) return false;
   const int G = nq / nkv, q_dim = nq * d;
+  // layer GEMVs split K over the 8 warps in whole 256-element chunks; the
+  // LM head's warp segments are 2048 wide; a kernel instance for the rows
+  // per stage
+  if (h % (kCWarps * 256) != 0 || q_dim % (kCWarps * 256) != 0 || I % (kCWarps * 256) != 0)
+    return false;
+  if (h / ksplit_host(h) != 2048 || ksplit_host(q_dim) != ksplit_host(h) ||
+      !rows_ok(kCWarps / ksplit_host(h), kCWarps / ksplit_host(I)))
+    return false;
   if (!(seg_ok(h) && seg_ok(q_dim) && seg_ok(I) && (d == 64 || d == 128) && G >= 1 && G <= 8 &&
         G * d <= 4 * kCThreads))
     return false;
@@ -1333,8 +1498,8 @@ bool fused_supported(int h, int nq, int nkv, int d, int I, int64_t V, int num_sm
   // buffers safe), and the deferred phases fit the per-warp result table
   for (int i = 0; i < 5; ++i)
     if (groups[i] < num_sms) return false;
-  return local_ok(groups[0], num_sms) && local_ok(groups[1], num_sms) &&
-         local_ok(groups[2], num_sms) && local_ok(groups[3], num_sms) &&
+  return local_ok_k(groups[0], num_sms, rpc_h) && local_ok_k(groups[1], num_sms, rpc_q) &&
+         local_ok_k(groups[2], num_sms, rpc_h) && local_ok_k(groups[3], num_sms, rpc_i) &&
          (ksplit_host(h) == 1 || local_ok(groups[4], num_sms));
 }
 
@@ -1374,10 +1539,10 @@ size_t fused_smem(int h, int q_dim, int I, int d, int G, int nsplit, int L, int 
 }
 
 cudaError_t fused_prepare() {
-  TMG_CUDA_TRY((prepare_one<64, 0>()));
-  TMG_CUDA_TRY((prepare_one<64, 8>()));
-  TMG_CUDA_TRY((prepare_one<128, 0>()));
-  return prepare_one<128, 8>();
+  TMG_CUDA_TRY((prepare_one<64, 8, 2>()));
+  TMG_CUDA_TRY((prepare_one<64, 4, 1>()));
+  TMG_CUDA_TRY((prepare_one<128, 8, 2>()));
+  return prepare_one<128, 4, 1>();
 }
 
 cudaError_t launch_decode_fused(const FusedArgs& args, int num_sms, cudaStream_t s) {
@@ -1386,10 +1551,10 @@ cudaError_t launch_decode_fused(const FusedArgs& args, int num_sms, cudaStream_t
   const int G = a.nq / a.nkv;
   const size_t smem = fused_smem(a.h, a.nq * a.d, a.I, a.d, G, a.nsplit, a.L, a.max_stages, &nst,
                                  &a.attn_floats, &a.max_splits);
-  if (nst < 2 || !a.x_ll || !a.att_ll || !a.act_ll || !a.qkv_ll || !a.part_ll || a.pf_ahead < 0)
+  if (nst < 2 || !a.x_ll || !a.att_ll || !a.act_ll || !a.qkv_ll || !a.part_ll || a.pf_ahead < 0 || a.pf_pace < 0)
     return cudaErrorInvalidValue;
-  const bool ch8 = a.h / ksplit_host(a.h) == 2048 && (a.nq * a.d) / ksplit_host(a.nq * a.d) == 2048 &&
-                   a.I / ksplit_host(a.I) == 2048;
+  const int ra = kCWarps / ksplit_host(a.h), rb = kCWarps / ksplit_host(a.I);
+  if (!rows_ok(ra, rb)) return cudaErrorInvalidValue;
   // the grid barrier counts from zero in every launch, and the tagged
   // exchange buffers hold no tag of this launch
   TMG_CUDA_TRY(cudaMemsetAsync(a.bar, 0, 4 * sizeof(unsigned int), s));
@@ -1406,12 +1571,13 @@ cudaError_t launch_decode_fused(const FusedArgs& args, int num_sms, cudaStream_t
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  const bool r82 = ra == 8;
   if (a.d == 64)
-    return ch8 ? cudaLaunchKernelEx(&cfg, decode_fused_kernel<64, 8>, a, nst)
-               : cudaLaunchKernelEx(&cfg, decode_fused_kernel<64, 0>, a, nst);
+    return r82 ? cudaLaunchKernelEx(&cfg, decode_fused_kernel<64, 8, 2>, a, nst)
+               : cudaLaunchKernelEx(&cfg, decode_fused_kernel<64, 4, 1>, a, nst);
   if (a.d == 128)
-    return ch8 ? cudaLaunchKernelEx(&cfg, decode_fused_kernel<128, 8>, a, nst)
-               : cudaLaunchKernelEx(&cfg, decode_fused_kernel<128, 0>, a, nst);
+    return r82 ? cudaLaunchKernelEx(&cfg, decode_fused_kernel<128, 8, 2>, a, nst)
+               : cudaLaunchKernelEx(&cfg, decode_fused_kernel<128, 4, 1>, a, nst);
   return cudaErrorInvalidValue;
 }
 

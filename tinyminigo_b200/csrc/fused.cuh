@@ -46,7 +46,8 @@ struct FusedArgs {
   // fused_bar_words() words: [0] barrier arrivals, [2] abort
   unsigned int* bar = nullptr;
   int nsplit = 1;
-  int pf_ahead = 0;    // stages of L2 prefetch beyond the ring
+  int pf_ahead = 0;    // stages of stall-time L2 prefetch beyond the ring
+  int pf_pace = 0;     // clock cycles between two such prefetches
   int max_stages = 0;  // cap on the ring's stages (0: as many as fit)
   int attn_floats = 0; // set by the launcher: attention region of shared memory
   int max_splits = 1;  // set by the launcher: attention splits per kv head
