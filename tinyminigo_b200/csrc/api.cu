@@ -81,6 +81,7 @@ struct tmg_ctx {
   unsigned long long* ll = nullptr;  // its tagged exchange words (x, att, act, qkv)
   int fused_pf = 0;              // its stall-time L2 prefetch distance (stages; TMG_FUSED_PF)
   int fused_pf_pace = 0;         // cycles between those prefetches (TMG_FUSED_PF_PACE)
+  int fused_rep = 4;             // copies of its x/att/act exchange words (TMG_FUSED_REP)
   int fused_stages = 4;          // its ring depth cap (0: all that fit; TMG_FUSED_STAGES)
   bool fused_ok = false;         // the fused batch-1 decode kernel takes this shape
   // prefill scratch
@@ -392,7 +393,9 @@ int alloc_model(tmg_ctx* c) {
   CK(dalloc(c->allocs, &c->sm_part, size_t(M) * 64 * kMaxTopK), "alloc scratch");
   CK(dalloc(c->allocs, &c->tickets, 64), "alloc scratch");
   CK(zero_sync(c, c->tickets, 64 * sizeof(unsigned int)), "memset");
-  CK(dalloc(c->allocs, &c->ll, fused_ll_words(h, c->nq * c->d, c->I, c->qkv_rows)), "alloc scratch");
+  if (const char* rp = getenv("TMG_FUSED_REP")) c->fused_rep = std::max(1, std::min(16, atoi(rp)));
+  CK(dalloc(c->allocs, &c->ll, fused_ll_words(h, c->nq * c->d, c->I, c->qkv_rows, c->fused_rep)),
+     "alloc scratch");
   CK(dalloc(c->allocs, &c->bar, fused_bar_words()), "alloc scratch");
   CK(zero_sync(c, c->bar, fused_bar_words() * sizeof(unsigned int)), "memset");
   c->fused_ok = c->world == 1 && fused_supported(c->h, c->nq, c->nkv, c->d, c->I, c->V_l, c->num_sms);
@@ -795,11 +798,13 @@ cudaError_t launch_fused(tmg_ctx* c, tmg_kv* kv, const StreamState& st, int64_t 
   f.cap = kv->cap;
   const int q_dim = c->nq * c->d;
   f.ll_base = c->ll;
-  f.ll_bytes = fused_ll_words(c->h, q_dim, c->I, c->qkv_rows) * sizeof(unsigned long long);
+  f.ll_bytes =
+      fused_ll_words(c->h, q_dim, c->I, c->qkv_rows, c->fused_rep) * sizeof(unsigned long long);
+  f.ll_rep = c->fused_rep;
   f.x_ll = c->ll;
-  f.att_ll = f.x_ll + c->h;
-  f.act_ll = f.att_ll + q_dim;
-  f.qkv_ll = f.act_ll + c->I;
+  f.att_ll = f.x_ll + size_t(c->fused_rep) * c->h;
+  f.act_ll = f.att_ll + size_t(c->fused_rep) * q_dim;
+  f.qkv_ll = f.act_ll + size_t(c->fused_rep) * c->I;
   f.part_ll = kv->part_ll;
   f.logits = c->logits;
   f.am_part = c->am_part;

@@ -462,6 +462,10 @@ __device__ __forceinline__ void ll_store(unsigned long long* p, float v, uint32_
   const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
   asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
+__device__ __forceinline__ void ll_store_rep(unsigned long long* base, int n, int rep, int r,
+                                             float v, uint32_t tag) {
+  for (int c = 0; c < rep; ++c) ll_store(base + size_t(c) * n + r, v, tag);
+}
 __device__ __forceinline__ ulonglong2 ll_load2(const unsigned long long* p) {
   ulonglong2 r;
   asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];"
@@ -470,6 +474,15 @@ __device__ __forceinline__ ulonglong2 ll_load2(const unsigned long long* p) {
                : "memory");
   return r;
 }
+
+// The copy of a replicated exchange vector (n words per copy) this CTA reads.
+__device__ __forceinline__ const unsigned long long* ll_mine(const unsigned long long* base, int n,
+                                                             int rep) {
+  return base + size_t(blockIdx.x % unsigned(rep)) * n;
+}
+// Store v at word r of every copy.
+__device__ __forceinline__ void ll_store_rep(unsigned long long* base, int n, int rep, int r,
+                                             float v, uint32_t tag);
 
 constexpr int kGatherPairs = 16;                            // word pairs per thread
 constexpr unsigned kBackoffNs = 0;                          // pause between polls
@@ -914,28 +927,29 @@ __device__ __forceinline__ void epi_qkv(const FusedArgs& a, const FusedLayer& L,
 
 // O / DOWN epilogue: x[r] = x_s[r] + y[r] out as tagged words (x_s: x as
 // this CTA last gathered it, lane-major).
-__device__ __forceinline__ void epi_residual(unsigned long long* x_ll, const float* x_s,
+__device__ __forceinline__ void epi_residual(unsigned long long* x_ll, int rep, const float* x_s,
                                              const PhaseGeo& g, int off, int nloc, uint32_t tag,
                                              const Shared& S) {
   const int f = first_group(off);
   for (int i = threadIdx.x; i < (nloc << g.lrpc); i += kCThreads) {
     const int kl = i >> g.lrpc, slot = i & (g.rpc - 1);
     const int r = ((f + kl * int(gridDim.x)) << g.lrpg) + slot;
-    if (r < g.N) ll_store(x_ll + r, x_s[perm_idx(r)] + res_k(S, kl, slot, g.rpc), tag);
+    if (r < g.N) ll_store_rep(x_ll, g.N, rep, r, x_s[perm_idx(r)] + res_k(S, kl, slot, g.rpc), tag);
   }
 }
 
 // GU epilogue: the rmsnorm factor (scale), then act = silu(gate) * up, out
 // as tagged words.
-__device__ __forceinline__ void epi_swiglu(unsigned long long* act_ll, const PhaseGeo& g, int off,
-                                           int nloc, float scale, uint32_t tag, const Shared& S) {
+__device__ __forceinline__ void epi_swiglu(unsigned long long* act_ll, int rep, const PhaseGeo& g,
+                                           int off, int nloc, float scale, uint32_t tag,
+                                           const Shared& S) {
   const int f = first_group(off);
   for (int i = threadIdx.x; i < (nloc << g.lrpg); i += kCThreads) {
     const int kl = i >> g.lrpg, q = i & (g.rpg - 1);
     const int r = ((f + kl * int(gridDim.x)) << g.lrpg) + q;
     if (r < g.N) {
       const float gv = res_k(S, kl, q, g.rpc) * scale, uv = res_k(S, kl, q + g.rpg, g.rpc) * scale;
-      ll_store(act_ll + r, gv / (1.0f + expf(-gv)) * uv, tag);
+      ll_store_rep(act_ll, g.N, rep, r, gv / (1.0f + expf(-gv)) * uv, tag);
     }
   }
 }
@@ -965,6 +979,7 @@ struct AttnArgs {
   unsigned long long* att_ll;        // [n_q * D] tagged output
   const unsigned int* abort_word;
   int nq, nkv, nsplit;
+  int rep;                           // copies of att_ll
   float scale;
 };
 
@@ -1075,7 +1090,8 @@ __device__ __forceinline__ bool attn_item(const AttnArgs a, int kvh, int split, 
       const int idx = tid + r * kCThreads;
       if (idx < G * D) {
         const float l = S.l_s[idx / D];
-        ll_store(a.att_ll + size_t(kvh) * G * D + idx, l > 0.f ? o_acc[r] / l : 0.f, tag_att);
+        ll_store_rep(a.att_ll, a.nq * D, a.rep, kvh * G * D + idx, l > 0.f ? o_acc[r] / l : 0.f,
+                     tag_att);
       }
     }
   } else {
@@ -1125,7 +1141,7 @@ __device__ __forceinline__ bool merge_head(const AttnArgs a, int kvh, int n_used
     float acc = 0.f;
     for (int s = 0; s < n_used; ++s) acc = fmaf(P[s * rec + g * (D + 2) + 2 + j], wv[g * n_used + s], acc);
     const float L = Ls[g];
-    ll_store(a.att_ll + size_t(kvh) * G * D + idx, L > 0.f ? acc / L : 0.f, tag_att);
+    ll_store_rep(a.att_ll, a.nq * D, a.rep, kvh * G * D + idx, L > 0.f ? acc / L : 0.f, tag_att);
   }
   csync();
   return true;
@@ -1224,6 +1240,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
         aa.vc = layers_s[l].vc;
         aa.part_ll = a.part_ll;
         aa.att_ll = a.att_ll;
+        aa.rep = a.ll_rep;
         aa.abort_word = a.bar + 2;
         aa.nq = a.nq;
         aa.nkv = a.nkv;
@@ -1283,15 +1300,17 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
         if (lane == 0) S.ssq[warp] = ss;
         csync();
       } else if (ph == PH_O) {
-        ok = ll_gather(asm_, a.att_ll, a.nq * a.d, tag - 1u, a.bar + 2, S, gc, true);
+        ok = ll_gather(asm_, ll_mine(a.att_ll, a.nq * a.d, a.ll_rep), a.nq * a.d, tag - 1u,
+                       a.bar + 2, S, gc, true);
         src = asm_;
       } else if (ph == PH_DOWN) {
-        ok = ll_gather(asm_, a.act_ll, a.I, tag - 1u, a.bar + 2, S, gc, true);
+        ok = ll_gather(asm_, ll_mine(a.act_ll, a.I, a.ll_rep), a.I, tag - 1u, a.bar + 2, S, gc,
+                       true);
         src = asm_;
       } else {
         // x after the phase just before: the previous layer's DOWN (QKV,
         // HEAD) or this layer's O (GU)
-        ok = ll_gather(x_s, a.x_ll, a.h, tag - 1u, a.bar + 2, S, gc, true);
+        ok = ll_gather(x_s, ll_mine(a.x_ll, a.h, a.ll_rep), a.h, tag - 1u, a.bar + 2, S, gc, true);
         cp_async_wait_all();  // nw_s (staged a phase or more ago)
         if (ok && ph != PH_HEAD) {
           // nw_s <- nw_s * x (same layout) and each warp's share of sum(x^2)
@@ -1319,6 +1338,9 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
       if (tp && threadIdx.x == 0) tp[1] = global_ns();
       const bool imm = ph == PH_HEAD && g.ks == 1;
       unsigned long long best = 0;
+      // the rmsnorm factor of QKV / GU (S.ssq is complete after the gather's
+      // barrier), ready before the epilogue needs it
+      const float rscale = (ph == PH_QKV || ph == PH_GU) ? rms_scale(S, a.h, a.eps) : 1.f;
       int nloc = 0;
       if (ph == PH_HEAD) {
         nloc = gemv_block(g.ngroups, g.K, g.ks, g.rpg, g.N, 8, src, nw_s, a.eps, a.h, off, rp,
@@ -1334,15 +1356,16 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
       }
       if (!imm) {
         csync();
+        const long long ce = tp ? clock64() : 0;
         switch (ph) {
           case PH_QKV:
-            epi_qkv(a, layers_s[lw], g, off, nloc, pos, append, rope_s, rms_scale(S, a.h, a.eps),
-                    tag, S);
+            epi_qkv(a, layers_s[lw], g, off, nloc, pos, append, rope_s, rscale, tag, S);
             break;
-          case PH_GU: epi_swiglu(a.act_ll, g, off, nloc, rms_scale(S, a.h, a.eps), tag, S); break;
+          case PH_GU: epi_swiglu(a.act_ll, a.ll_rep, g, off, nloc, rscale, tag, S); break;
           case PH_HEAD: epi_head(a.logits, g, off, nloc, S, best); break;
-          default: epi_residual(a.x_ll, x_s, g, off, nloc, tag, S); break;
+          default: epi_residual(a.x_ll, a.ll_rep, x_s, g, off, nloc, tag, S); break;
         }
+        if (tp && threadIdx.x == 0) tp[9] = clock64() - ce;
       }
       csync();  // x_s, asm_ and S.res are free for the next phase
       off = (off + g.ngroups) % int(gridDim.x);
@@ -1551,7 +1574,8 @@ cudaError_t launch_decode_fused(const FusedArgs& args, int num_sms, cudaStream_t
   const int G = a.nq / a.nkv;
   const size_t smem = fused_smem(a.h, a.nq * a.d, a.I, a.d, G, a.nsplit, a.L, a.max_stages, &nst,
                                  &a.attn_floats, &a.max_splits);
-  if (nst < 2 || !a.x_ll || !a.att_ll || !a.act_ll || !a.qkv_ll || !a.part_ll || a.pf_ahead < 0 || a.pf_pace < 0)
+  if (nst < 2 || !a.x_ll || !a.att_ll || !a.act_ll || !a.qkv_ll || !a.part_ll || a.pf_ahead < 0 || a.pf_pace < 0 ||
+      a.ll_rep < 1)
     return cudaErrorInvalidValue;
   const int ra = kCWarps / ksplit_host(a.h), rb = kCWarps / ksplit_host(a.I);
   if (!rows_ok(ra, rb)) return cudaErrorInvalidValue;

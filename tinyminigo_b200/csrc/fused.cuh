@@ -48,6 +48,7 @@ struct FusedArgs {
   int nsplit = 1;
   int pf_ahead = 0;    // stages of stall-time L2 prefetch beyond the ring
   int pf_pace = 0;     // clock cycles between two such prefetches
+  int ll_rep = 1;      // copies of x_ll, att_ll and act_ll (each n words apart)
   int max_stages = 0;  // cap on the ring's stages (0: as many as fit)
   int attn_floats = 0; // set by the launcher: attention region of shared memory
   int max_splits = 1;  // set by the launcher: attention splits per kv head
@@ -68,8 +69,10 @@ int fused_nsplit(int G, int d, int64_t capacity);
 size_t fused_smem(int h, int q_dim, int I, int d, int G, int nsplit, int L, int max_stages,
                   int* nst_out, int* attn_floats, int* max_splits);
 // Words of the tagged exchange block (x, att, act, qkv) of a model.
-inline size_t fused_ll_words(int h, int q_dim, int I, int qkv_rows) {
-  return size_t(h) + q_dim + I + qkv_rows;
+// Tagged exchange words: x, att and act in `rep` copies each (readers spread
+// over the copies), then the position's q/k/v.
+inline size_t fused_ll_words(int h, int q_dim, int I, int qkv_rows, int rep) {
+  return size_t(rep) * (size_t(h) + q_dim + I) + qkv_rows;
 }
 cudaError_t fused_prepare();
 // Cooperative launch: one CTA per SM (num_sms CTAs).
