@@ -23,7 +23,7 @@ namespace tmg {
 namespace {
 
 constexpr int kAttnThreads = 128;
-constexpr int kTile = 64;      // positions per shared-memory tile
+constexpr int kTile = 64;      // decode split lengths are multiples of this
 constexpr int kMinChunk = 64;  // fewest positions a decode split takes
 constexpr int kPTile = 32;     // key positions per prefill tile
 
@@ -47,27 +47,28 @@ __device__ __forceinline__ void cp_async_wait() {
 
 // K/V tile buffers of the decode kernel: two (the next tile loads while the
 // current one is used) where they fit the shared-memory budget.
-template <int D>
-constexpr int attn_bufs() { return D <= 64 ? 2 : 1; }
+constexpr int kTileD = 32;     // positions per shared-memory tile of the decode kernel
+constexpr int kAttnBufs = 2;   // its K/V tile buffers (the next tile loads during this one)
 
 // Grid (n_kv, nsplit, M); 128 threads.  Dynamic smem: q [G][d], K tiles
-// [NB][kTile][d+4], V tiles [NB][kTile][d], p [G][kTile], and the decoded
-// position's rotated k and raw v [2][d].
-template <int D>
+// [NB][kTileD][d+16], V tiles [NB][kTileD][d], p [kTileD][G rounded up to
+// 4], and the decoded position's rotated k and raw v [2][d].
+template <int D, int GM>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDecodeArgs a) {
   extern __shared__ float sm[];
   __shared__ float m_s[16], l_s[16], alpha_s[16];
   __shared__ bool last_s;
-  constexpr int NB = attn_bufs<D>();
+  constexpr int NB = kAttnBufs;
   const int kvh = blockIdx.x, split = blockIdx.y, m = blockIdx.z;
   constexpr int d = D;
   const int half = d / 2, G = a.nq / a.nkv, kvd = a.nkv * d;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int GP = (G + 3) & ~3;               // heads per p row, padded to float4
   float* qs = sm;                           // [G][d]
-  float* ks_ = qs + G * d;                  // [NB][kTile][d+4]
-  float* vs = ks_ + NB * kTile * (d + 4);   // [NB][kTile][d]
-  float* ps = vs + NB * kTile * d;          // [G][kTile]
-  float* kp_s = ps + G * kTile;             // [d] k of the decoded position (rotated)
+  float* ks_ = qs + G * d;                    // [NB][kTileD][d+16]
+  float* vs = ks_ + NB * kTileD * (d + 16);   // [NB][kTileD][d]
+  float* ps = vs + NB * kTileD * d;           // [kTileD][GP] scores, then p
+  float* kp_s = ps + kTileD * GP;             // [d] k of the decoded position (rotated)
   float* vp_s = kp_s + d;                   // [d] its v
 
   if (tid == 0) trace_mark(a.trace, 0);
@@ -144,103 +145,95 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
   // tile (t0, nt) into buffer b: cache rows by cp.async, the decoded
   // position's row (when in range) from kp_s/vp_s; one commit group
   auto load_tile = [&](int b, int t0, int nt) {
-    float* kb = ks_ + b * kTile * (d + 4);
-    float* vb = vs + b * kTile * d;
+    float* kb = ks_ + b * kTileD * (d + 16);
+    float* vb = vs + b * kTileD * d;
     for (int i = tid; i < nt * d4; i += blockDim.x) {
       const int t = i / d4, j4 = i % d4;
       if (own_pos && t0 + t == pos) {
-        *reinterpret_cast<float4*>(kb + t * (d + 4) + j4 * 4) =
+        *reinterpret_cast<float4*>(kb + t * (d + 16) + j4 * 4) =
             *reinterpret_cast<const float4*>(kp_s + j4 * 4);
         *reinterpret_cast<float4*>(vb + t * d + j4 * 4) =
             *reinterpret_cast<const float4*>(vp_s + j4 * 4);
         continue;
       }
-      cp_async16(kb + t * (d + 4) + j4 * 4, kc + size_t(t0 + t) * kvd + kvh * d + j4 * 4);
+      cp_async16(kb + t * (d + 16) + j4 * 4, kc + size_t(t0 + t) * kvd + kvh * d + j4 * 4);
       cp_async16(vb + t * d + j4 * 4, vc + size_t(t0 + t) * kvd + kvh * d + j4 * 4);
     }
     cp_async_commit();
   };
-  if (c0 < c1) load_tile(0, c0, min(kTile, c1 - c0));
+  if (c0 < c1) load_tile(0, c0, min(kTileD, c1 - c0));
   if (tid < G) {
     m_s[tid] = -INFINITY;
     l_s[tid] = 0.f;
   }
-  // Work split inside a tile, so that each K and V row is read from shared
-  // memory once per head slot rather than once per query head:
-  //  * scores: thread -> position tid % kTile and heads hs, hs + kHS, ...
-  //    (hs = tid / kTile): its K row once, q rows by broadcast;
-  //  * P.V: thread -> column tid % d and heads ps, ps + kPS, ... (ps =
-  //    tid / d): its V column once, p by broadcast.
-  constexpr int kHS = kAttnThreads / kTile;              // head slots, scores
-  constexpr int kPS = kAttnThreads / D >= 1 ? kAttnThreads / D : 1;  // head slots, P.V
-  constexpr int kMaxOwn = 16 / kPS > 0 ? 16 / kPS : 1;   // heads per thread in P.V (G <= 16)
-  constexpr int kMaxSc = 16 / kHS;                       // heads per thread in scores
-  const int pj = tid % d, pslot = tid / d;
-  float o_acc[kMaxOwn];
+  // Work split inside a tile (GM: heads per kv head, at most):
+  //  * scores: thread -> position tid / 4 and every fourth float4 of its K
+  //    row (tid & 3), all heads; the quarters meet by two shuffles.  K rows
+  //    are d + 16 floats apart, so the eight lanes of one 16-byte phase hit
+  //    distinct banks;
+  //  * P.V: thread -> column tid % d and part tid / d of the tile's
+  //    positions, all heads: its V value once per position, the heads' p
+  //    by broadcast float4 loads; the parts meet at the end.
+  constexpr int kParts = kAttnThreads / D >= 1 ? kAttnThreads / D : 1;
+  constexpr int kPer = kTileD / kParts;  // positions per part
+  const int pj = tid % d, ph = tid / d;
+  float o_acc[GM];
 #pragma unroll
-  for (int r = 0; r < kMaxOwn; ++r) o_acc[r] = 0.f;
+  for (int g = 0; g < GM; ++g) o_acc[g] = 0.f;
   __syncthreads();
 
-  for (int t0 = c0, it = 0; t0 < c1; t0 += kTile, ++it) {
-    const int nt = min(kTile, c1 - t0);
-    const int b = NB == 2 ? (it & 1) : 0;
-    if (NB == 2) {
-      // the next tile loads into the other buffer while this one is used
-      const bool more = t0 + kTile < c1;
-      if (more) load_tile(b ^ 1, t0 + kTile, min(kTile, c1 - t0 - kTile));
-      if (more) cp_async_wait<1>();
-      else cp_async_wait<0>();
-    } else {
-      if (t0 != c0) load_tile(0, t0, nt);
-      cp_async_wait<0>();
-    }
+  for (int t0 = c0, it = 0; t0 < c1; t0 += kTileD, ++it) {
+    const int nt = min(kTileD, c1 - t0);
+    const int b = it & 1;
+    // the next tile loads into the other buffer while this one is used
+    const bool more = t0 + kTileD < c1;
+    if (more) load_tile(b ^ 1, t0 + kTileD, min(kTileD, c1 - t0 - kTileD));
+    if (more) cp_async_wait<1>();
+    else cp_async_wait<0>();
     __syncthreads();
-    const float* kt = ks_ + b * kTile * (d + 4);
-    const float* vt = vs + b * kTile * d;
-    // raw scores s[g][t] = q_g . k_t * scale into ps
+    const float* kt = ks_ + b * kTileD * (d + 16);
+    const float* vt = vs + b * kTileD * d;
+    // raw scores s[t][g] = q_g . k_t * scale into ps
     {
-      const int t = tid % kTile, hs = tid / kTile;
-      float acc[kMaxSc][4];
+      const int t = tid >> 2, dq = tid & 3;
+      float acc[GM];
 #pragma unroll
-      for (int i = 0; i < kMaxSc; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+      for (int g = 0; g < GM; ++g) acc[g] = 0.f;
       if (t < nt) {
-        const float* kr = kt + t * (d + 4);
-#pragma unroll 4
-        for (int j = 0; j < d; j += 4) {
+        const float* kr = kt + t * (d + 16) + dq * 4;
+#pragma unroll
+        for (int j = 0; j < d; j += 16) {
           const float4 k4 = *reinterpret_cast<const float4*>(kr + j);
 #pragma unroll
-          for (int i = 0; i < kMaxSc; ++i) {
-            const int g = hs + i * kHS;
+          for (int g = 0; g < GM; ++g) {
             if (g < G) {
-              const float4 q4 = *reinterpret_cast<const float4*>(qs + g * d + j);
-              acc[i][0] = fmaf(q4.x, k4.x, acc[i][0]);
-              acc[i][1] = fmaf(q4.y, k4.y, acc[i][1]);
-              acc[i][2] = fmaf(q4.z, k4.z, acc[i][2]);
-              acc[i][3] = fmaf(q4.w, k4.w, acc[i][3]);
+              const float4 q4 = *reinterpret_cast<const float4*>(qs + g * d + dq * 4 + j);
+              acc[g] = fmaf(q4.x, k4.x, acc[g]);
+              acc[g] = fmaf(q4.y, k4.y, acc[g]);
+              acc[g] = fmaf(q4.z, k4.z, acc[g]);
+              acc[g] = fmaf(q4.w, k4.w, acc[g]);
             }
           }
         }
       }
 #pragma unroll
-      for (int i = 0; i < kMaxSc; ++i) {
-        const int g = hs + i * kHS;
-        if (g < G)
-          ps[g * kTile + t] =
-              t < nt ? ((acc[i][0] + acc[i][1]) + (acc[i][2] + acc[i][3])) * a.scale : -INFINITY;
+      for (int g = 0; g < GM; ++g) {
+        if (g < G) {
+          float full = acc[g] + __shfl_xor_sync(0xffffffffu, acc[g], 1);
+          full += __shfl_xor_sync(0xffffffffu, full, 2);
+          if ((g & 3) == dq) ps[t * GP + g] = t < nt ? full * a.scale : -INFINITY;
+        }
       }
     }
     __syncthreads();
-    // online softmax per head: a warp per head, lanes over the positions
+    // online softmax per head: a warp per head, a lane per position
     for (int g = warp; g < G; g += kAttnThreads / 32) {
-      const float s0 = ps[g * kTile + lane], s1 = ps[g * kTile + lane + 32];
-      const float mt = warp_max(fmaxf(s0, s1));
+      const float s0 = ps[lane * GP + g];
       const float m_old = m_s[g];
-      const float m_new = fmaxf(m_old, mt);
+      const float m_new = fmaxf(m_old, warp_max(s0));
       const float p0 = lane < nt ? expf(s0 - m_new) : 0.f;
-      const float p1 = lane + 32 < nt ? expf(s1 - m_new) : 0.f;
-      const float lsum = warp_sum(p0 + p1);
-      ps[g * kTile + lane] = p0;
-      ps[g * kTile + lane + 32] = p1;
+      const float lsum = warp_sum(p0);
+      ps[lane * GP + g] = p0;
       if (lane == 0) {
         const float alpha = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
         alpha_s[g] = alpha;
@@ -249,23 +242,44 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
       }
     }
     __syncthreads();
-    // P.V over the tile's nt rows, in four independent chains over t
-    if (pslot < kPS) {
+    // P.V over this thread's part of the tile's nt rows
+    if (ph < kParts) {
 #pragma unroll
-      for (int r = 0; r < kMaxOwn; ++r) {
-        const int g = pslot + r * kPS;
-        if (g < G) {
-          float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
-          int t = 0;
-          for (; t + 4 <= nt; t += 4) {
-            b0 = fmaf(ps[g * kTile + t], vt[t * d + pj], b0);
-            b1 = fmaf(ps[g * kTile + t + 1], vt[(t + 1) * d + pj], b1);
-            b2 = fmaf(ps[g * kTile + t + 2], vt[(t + 2) * d + pj], b2);
-            b3 = fmaf(ps[g * kTile + t + 3], vt[(t + 3) * d + pj], b3);
+      for (int g = 0; g < GM; ++g)
+        if (g < G) o_acc[g] *= alpha_s[g];
+      const int tb = ph * kPer;
+      const int te = min(nt, tb + kPer);
+#pragma unroll 4
+      for (int t = tb; t < te; ++t) {
+        const float v = vt[t * d + pj];
+#pragma unroll
+        for (int c = 0; c < GM / 4; ++c) {
+          if (4 * c < G) {
+            const float4 p4 = *reinterpret_cast<const float4*>(ps + t * GP + 4 * c);
+            o_acc[4 * c] = fmaf(p4.x, v, o_acc[4 * c]);
+            if (4 * c + 1 < G) o_acc[4 * c + 1] = fmaf(p4.y, v, o_acc[4 * c + 1]);
+            if (4 * c + 2 < G) o_acc[4 * c + 2] = fmaf(p4.z, v, o_acc[4 * c + 2]);
+            if (4 * c + 3 < G) o_acc[4 * c + 3] = fmaf(p4.w, v, o_acc[4 * c + 3]);
           }
-          for (; t < nt; ++t) b0 = fmaf(ps[g * kTile + t], vt[t * d + pj], b0);
-          o_acc[r] = fmaf(o_acc[r], alpha_s[g], (b0 + b1) + (b2 + b3));
         }
+      }
+    }
+    __syncthreads();
+  }
+  // the parts meet in part 0 (the tile buffers are free now)
+  if (kParts > 1) {
+    float* comb = ks_;  // [kParts - 1][G][d]
+    if (ph >= 1 && ph < kParts) {
+#pragma unroll
+      for (int g = 0; g < GM; ++g)
+        if (g < G) comb[((ph - 1) * G + g) * d + pj] = o_acc[g];
+    }
+    __syncthreads();
+    if (ph == 0) {
+      for (int q = 1; q < kParts; ++q) {
+#pragma unroll
+        for (int g = 0; g < GM; ++g)
+          if (g < G) o_acc[g] += comb[((q - 1) * G + g) * d + pj];
       }
     }
     __syncthreads();
@@ -273,13 +287,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
   float* out = a.out + size_t(m) * a.nq * d + kvh * G * d;
   if (n_used == 1) {
     // the whole context in one CTA: finish here, no partials
-    if (split == 0 && pslot < kPS) {
+    if (split == 0 && ph == 0) {
 #pragma unroll
-      for (int r = 0; r < kMaxOwn; ++r) {
-        const int g = pslot + r * kPS;
+      for (int g = 0; g < GM; ++g) {
         if (g < G) {
           const float L = l_s[g];
-          out[g * d + pj] = L > 0.f ? o_acc[r] / L : 0.f;
+          out[g * d + pj] = L > 0.f ? o_acc[g] / L : 0.f;
         }
       }
     }
@@ -289,12 +302,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
   // partial (m, l, o[d]) per head
   if (split < n_used) {
     float* part = a.part + ((size_t(m) * a.nkv + kvh) * a.nsplit + split) * G * (d + 2);
-    if (pslot < kPS) {
+    if (ph == 0) {
 #pragma unroll
-      for (int r = 0; r < kMaxOwn; ++r) {
-        const int g = pslot + r * kPS;
-        if (g < G) part[g * (d + 2) + 2 + pj] = o_acc[r];
-      }
+      for (int g = 0; g < GM; ++g)
+        if (g < G) part[g * (d + 2) + 2 + pj] = o_acc[g];
     }
     if (tid < G) {
       part[tid * (d + 2)] = m_s[tid];
@@ -502,7 +513,8 @@ constexpr int kMaxAttnSmem = 96 * 1024;
 template <int D>
 cudaError_t attn_attr() {
   TMG_CUDA_TRY(set_carveout(attn_prefill_kernel<D>));
-  return set_carveout(attn_decode_kernel<D>, kMaxAttnSmem);
+  TMG_CUDA_TRY((set_carveout(attn_decode_kernel<D, 4>, kMaxAttnSmem)));
+  return set_carveout(attn_decode_kernel<D, 16>, kMaxAttnSmem);
 }
 
 cudaError_t attn_prepare() {
@@ -518,17 +530,18 @@ cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s, bool pdl
   const int G = a.nq / a.nkv;
   if (G * a.nkv != a.nq || G * a.d > 8 * kAttnThreads || G > 16) return cudaErrorInvalidValue;
   void (*kern)(const AttnDecodeArgs) = nullptr;
+  const bool g4 = G <= 4;
   switch (a.d) {
-    case 16: kern = attn_decode_kernel<16>; break;
-    case 32: kern = attn_decode_kernel<32>; break;
-    case 64: kern = attn_decode_kernel<64>; break;
-    case 128: kern = attn_decode_kernel<128>; break;
+    case 16: kern = g4 ? attn_decode_kernel<16, 4> : attn_decode_kernel<16, 16>; break;
+    case 32: kern = g4 ? attn_decode_kernel<32, 4> : attn_decode_kernel<32, 16>; break;
+    case 64: kern = g4 ? attn_decode_kernel<64, 4> : attn_decode_kernel<64, 16>; break;
+    case 128: kern = g4 ? attn_decode_kernel<128, 4> : attn_decode_kernel<128, 16>; break;
     default: return cudaErrorInvalidValue;
   }
   // tiles, or the combine's per-split weights when those are larger
-  const int nb = a.d <= 64 ? 2 : 1;  // attn_bufs<D>()
-  const size_t tiles = size_t(G) * a.d + size_t(nb) * kTile * (a.d + 4) + size_t(nb) * kTile * a.d +
-                       G * kTile + 2 * size_t(a.d);
+  const size_t gp = (size_t(G) + 3) & ~size_t(3);
+  const size_t tiles = size_t(G) * a.d + size_t(kAttnBufs) * kTileD * (a.d + 16) +
+                       size_t(kAttnBufs) * kTileD * a.d + kTileD * gp + 2 * size_t(a.d);
   const size_t smem = sizeof(float) * std::max<size_t>(tiles, size_t(G) * a.nsplit);
   if (smem > size_t(kMaxAttnSmem)) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
