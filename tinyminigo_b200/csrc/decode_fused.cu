@@ -279,6 +279,7 @@ struct Shared {
   volatile int issued;     // producer: stages issued so far
   volatile int prod_done;  // producer: no more stages will be issued
   volatile int streaming;  // consumers: inside a GEMV's stage loop
+  volatile int in_attn;    // consumers: in an attention phase
 };
 
 // ---------------------------------------------------------------------------
@@ -385,23 +386,32 @@ __device__ void producer(const FusedArgs& a, const FusedLayer* layers, Shared& S
     const uint32_t par = (it / nst) & 1;
     if (S.abort) return;
     const long long c0 = clock64();
-    // While the slot is busy and the consumers are outside a GEMV (waiting
-    // on an exchange, in attention, in an epilogue), the weight stream
-    // would stall: bring the stages after the ring into L2 instead, at most
-    // pf_ahead past it, one every pf_pace cycles.
+    // While the slot is busy and the consumers are in the attention chain
+    // (ATTN entry to O's input; most CTAs only wait there), the weight
+    // stream would stall: bring the stages after the ring into L2 instead,
+    // at most pf_ahead past it, one every pf_pace cycles.
     bool got = mbar_try(&S.empty[s], par ^ 1);
-    while (!got && a.pf_ahead > 0 && S.streaming == 0 && pc.valid && pf < it + nst + a.pf_ahead) {
-      const long long now = clock64();
-      if (now >= pf_next) {
-        const Ranges r = group_ranges(pc.g, pc.grp);
-        l2_prefetch(r.src[0], r.bytes[0]);
-        if (r.n > 1) l2_prefetch(r.src[1], r.bytes[1]);
-        cur_next(a, pc);
-        ++pf;
-        pf_next = now + a.pf_pace;
+    if (!got && a.pf_ahead > 0) {
+      // poll the slot, prefetching while the condition holds (bounded in
+      // time like mbar_wait)
+      const unsigned long long tw0 = global_ns();
+      for (unsigned int i = 1; !got; ++i) {
+        if (S.in_attn != 0 && pc.valid && pf < it + nst + a.pf_ahead) {
+          const long long now = clock64();
+          if (now >= pf_next) {
+            const Ranges r = group_ranges(pc.g, pc.grp);
+            l2_prefetch(r.src[0], r.bytes[0]);
+            if (r.n > 1) l2_prefetch(r.src[1], r.bytes[1]);
+            cur_next(a, pc);
+            ++pf;
+            pf_next = now + a.pf_pace;
+          }
+        }
+        got = mbar_try(&S.empty[s], par ^ 1);
+        if (!got && (i & 255) == 0 && (S.abort || global_ns() - tw0 > kWaitNs)) break;
       }
-      got = mbar_try(&S.empty[s], par ^ 1);
     }
+    if (!got && S.abort) return;
     if (!got && !mbar_wait(&S.empty[s], par ^ 1)) {
       S.abort = 1;
       if (a.err) atomicExch(a.err, 2);
@@ -799,6 +809,7 @@ __device__ __forceinline__ int gemv_kseg(int ngroups, int K, int chunks, const f
   // one or two rows per stage (segments of 4 to 8 chunks): x is read from
   // shared memory with each stage instead of held in registers
   constexpr bool XS = R <= 2;
+  static_assert(R == 8 || R == 4 || R == 2 || R == 1, "rows per stage");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kbase = warp * chunks * 256;
   const long long c0 = tw ? clock64() : 0;
@@ -1179,6 +1190,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
     S.issued = 0;
     S.prod_done = 0;
     S.streaming = 0;
+    S.in_attn = 0;
     S.fail[0] = S.fail[1] = 0;
     mbar_fence_init();
   }
@@ -1234,6 +1246,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
       if (tp && threadIdx.x == 0) tp[0] = global_ns();
       if (kind == 1) {
         // ---- ATTN: partials of this CTA's items, then the merges it owns ----
+        if (threadIdx.x == 0) S.in_attn = 1;
         AttnArgs aa;
         aa.qkv_ll = a.qkv_ll;
         aa.kc = layers_s[l].kc;
@@ -1302,6 +1315,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
       } else if (ph == PH_O) {
         ok = ll_gather(asm_, ll_mine(a.att_ll, a.nq * a.d, a.ll_rep), a.nq * a.d, tag - 1u,
                        a.bar + 2, S, gc, true);
+        if (threadIdx.x == 0) S.in_attn = 0;  // the attention chain ends with att here
         src = asm_;
       } else if (ph == PH_DOWN) {
         ok = ll_gather(asm_, ll_mine(a.act_ll, a.I, a.ll_rep), a.I, tag - 1u, a.bar + 2, S, gc,
@@ -1480,9 +1494,10 @@ bool seg_ok(int K) {
 bool local_ok(int64_t ngroups, int num_sms) {
   return (ngroups + num_sms - 1) / num_sms <= kMaxLocal;
 }
-// The (QKV/O/GU, DOWN) rows-per-stage pairs with a kernel instance: 2048-
-// and 8192-wide (1B-class), 4096- and 14336-wide (8B-class) rows.
-bool rows_ok(int ra, int rb) { return (ra == 8 && rb == 2) || (ra == 4 && rb == 1); }
+// The (QKV/O/GU, DOWN) rows-per-stage pair with a kernel instance: 2048-
+// and 8192-wide rows (1B-class shapes; wider intermediate sizes also exceed
+// one exchange gather).
+bool rows_ok(int ra, int rb) { return ra == 8 && rb == 2; }
 
 // The same for a layer phase of rpc rows per group (8 partial sums per row).
 bool local_ok_k(int64_t ngroups, int num_sms, int rpc) {
@@ -1563,9 +1578,7 @@ size_t fused_smem(int h, int q_dim, int I, int d, int G, int nsplit, int L, int 
 
 cudaError_t fused_prepare() {
   TMG_CUDA_TRY((prepare_one<64, 8, 2>()));
-  TMG_CUDA_TRY((prepare_one<64, 4, 1>()));
-  TMG_CUDA_TRY((prepare_one<128, 8, 2>()));
-  return prepare_one<128, 4, 1>();
+  return prepare_one<128, 8, 2>();
 }
 
 cudaError_t launch_decode_fused(const FusedArgs& args, int num_sms, cudaStream_t s) {
@@ -1595,13 +1608,8 @@ cudaError_t launch_decode_fused(const FusedArgs& args, int num_sms, cudaStream_t
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const bool r82 = ra == 8;
-  if (a.d == 64)
-    return r82 ? cudaLaunchKernelEx(&cfg, decode_fused_kernel<64, 8, 2>, a, nst)
-               : cudaLaunchKernelEx(&cfg, decode_fused_kernel<64, 4, 1>, a, nst);
-  if (a.d == 128)
-    return r82 ? cudaLaunchKernelEx(&cfg, decode_fused_kernel<128, 8, 2>, a, nst)
-               : cudaLaunchKernelEx(&cfg, decode_fused_kernel<128, 4, 1>, a, nst);
+  if (a.d == 64) return cudaLaunchKernelEx(&cfg, decode_fused_kernel<64, 8, 2>, a, nst);
+  if (a.d == 128) return cudaLaunchKernelEx(&cfg, decode_fused_kernel<128, 8, 2>, a, nst);
   return cudaErrorInvalidValue;
 }
 
