@@ -162,3 +162,25 @@ def test_fused_trace_is_well_formed(c2l2):
     assert groups[5 * L] == (V + 7) // 8
     cache.close()
     m.close()
+
+
+def test_fused_head_dim_128_matches_oracle(orc):
+    # the head-dim-128 kernel instance: 16 query heads of 128 over 4 kv heads
+    # (n_q * d = hidden = 2048), 2 layers, a 40-token prompt and 48 greedy
+    # steps against the oracle
+    cfg = dict(synth.CONFIGS["c2"])
+    cfg.update(num_attention_heads=16, num_key_value_heads=4, head_dim=128,
+               vocab_size=32000, num_hidden_layers=2)
+    t = synth.make_weights(cfg, 11)
+    prompt = synth.random_prompt(cfg["vocab_size"], 40, 12)
+    steps = 48
+    ids, margins, second = oracle_greedy(orc.OracleModel(cfg, t), prompt, steps)
+    m = Model.from_tensors(cfg_obj(cfg), t)
+    out = generate(m, prompt, GenParams(max_tokens=steps))
+    assert_greedy_agrees(out.tokens, ids, margins, second)
+    c = m.new_cache(128)
+    tok0 = int(np.argmax(m.forward_seq(prompt, c)))
+    tr = m.trace_fused(tok0, c)  # the fused kernel ran for this shape
+    assert tr.shape[1] == 5 * 2 + 1
+    c.close()
+    m.close()

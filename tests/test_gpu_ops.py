@@ -120,7 +120,8 @@ def attn_bound(q, keys, vals):
 
 @pytest.mark.parametrize("n_ctx,nq,nkv,d", [(1, 4, 2, 16), (5, 4, 4, 64), (33, 32, 8, 64),
                                              (300, 32, 8, 64), (2000, 8, 2, 128),
-                                             (4097, 4, 1, 64)])
+                                             (4097, 4, 1, 64), (77, 12, 4, 32),
+                                             (600, 16, 2, 64), (130, 16, 1, 64)])
 def test_attn_decode(ctx, orc, n_ctx, nq, nkv, d):
     rng = np.random.default_rng(n_ctx + d)
     q = rng.normal(0, 1, nq * d).astype(np.float32)
