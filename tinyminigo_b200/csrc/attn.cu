@@ -49,6 +49,13 @@ __device__ __forceinline__ void cp_async_wait() {
 // current one is used) where they fit the shared-memory budget.
 constexpr int kTileD = 32;     // positions per shared-memory tile of the decode kernel
 constexpr int kAttnBufs = 2;   // its K/V tile buffers (the next tile loads during this one)
+// K tile row stride (floats) and the float4 swizzle of row t: rows of d >= 32
+// unpadded with float4 index j4 stored at j4 ^ 4 on odd rows, so that the
+// eight lanes of a 16-byte phase (two rows, four quarters) hit distinct banks
+template <int D>
+constexpr int attn_kstride() { return D >= 32 ? D : D + 16; }
+template <int D>
+__device__ __forceinline__ int attn_kswz(int t) { return D >= 32 ? (t & 1) << 2 : 0; }
 
 // Grid (n_kv, nsplit, M); 128 threads.  Dynamic smem: q [G][d], K tiles
 // [NB][kTileD][d+16], V tiles [NB][kTileD][d], p [kTileD][G rounded up to
@@ -56,7 +63,7 @@ constexpr int kAttnBufs = 2;   // its K/V tile buffers (the next tile loads duri
 template <int D, int GM>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDecodeArgs a) {
   extern __shared__ float sm[];
-  __shared__ float m_s[16], l_s[16], alpha_s[16];
+  __shared__ float m_s[16], l_s[16];
   __shared__ bool last_s;
   constexpr int NB = kAttnBufs;
   const int kvh = blockIdx.x, split = blockIdx.y, m = blockIdx.z;
@@ -66,8 +73,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
   const int GP = (G + 3) & ~3;               // heads per p row, padded to float4
   float* qs = sm;                           // [G][d]
   float* ks_ = qs + G * d;                    // [NB][kTileD][d+16]
-  float* vs = ks_ + NB * kTileD * (d + 16);   // [NB][kTileD][d]
-  float* ps = vs + NB * kTileD * d;           // [kTileD][GP] scores, then p
+  constexpr int KS = attn_kstride<D>();
+  float* vs = ks_ + NB * kTileD * KS;         // [NB][kTileD][d]
+  float* ps = vs + NB * kTileD * d;           // [kTileD][GP] p, a warp's rows each
   float* kp_s = ps + kTileD * GP;             // [d] k of the decoded position (rotated)
   float* vp_s = kp_s + d;                   // [d] its v
 
@@ -143,157 +151,211 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
   }
   __syncthreads();
   // tile (t0, nt) into buffer b: cache rows by cp.async, the decoded
-  // position's row (when in range) from kp_s/vp_s; one commit group
+  // position's row (when in range) from kp_s/vp_s (the caller commits)
   auto load_tile = [&](int b, int t0, int nt) {
-    float* kb = ks_ + b * kTileD * (d + 16);
+    float* kb = ks_ + b * kTileD * KS;
     float* vb = vs + b * kTileD * d;
     for (int i = tid; i < nt * d4; i += blockDim.x) {
       const int t = i / d4, j4 = i % d4;
+      const int pk = (j4 ^ attn_kswz<D>(t)) * 4;
       if (own_pos && t0 + t == pos) {
-        *reinterpret_cast<float4*>(kb + t * (d + 16) + j4 * 4) =
+        *reinterpret_cast<float4*>(kb + t * KS + pk) =
             *reinterpret_cast<const float4*>(kp_s + j4 * 4);
         *reinterpret_cast<float4*>(vb + t * d + j4 * 4) =
             *reinterpret_cast<const float4*>(vp_s + j4 * 4);
         continue;
       }
-      cp_async16(kb + t * (d + 16) + j4 * 4, kc + size_t(t0 + t) * kvd + kvh * d + j4 * 4);
+      cp_async16(kb + t * KS + pk, kc + size_t(t0 + t) * kvd + kvh * d + j4 * 4);
       cp_async16(vb + t * d + j4 * 4, vc + size_t(t0 + t) * kvd + kvh * d + j4 * 4);
     }
-    cp_async_commit();
   };
-  if (c0 < c1) load_tile(0, c0, min(kTileD, c1 - c0));
-  if (tid < G) {
-    m_s[tid] = -INFINITY;
-    l_s[tid] = 0.f;
-  }
-  // Work split inside a tile (GM: heads per kv head, at most):
-  //  * scores: thread -> position tid / 4 and every fourth float4 of its K
-  //    row (tid & 3), all heads; the quarters meet by two shuffles.  K rows
-  //    are d + 16 floats apart, so the eight lanes of one 16-byte phase hit
-  //    distinct banks;
-  //  * P.V: thread -> column tid % d and part tid / d of the tile's
-  //    positions, all heads: its V value once per position, the heads' p
-  //    by broadcast float4 loads; the parts meet at the end.
-  constexpr int kParts = kAttnThreads / D >= 1 ? kAttnThreads / D : 1;
-  constexpr int kPer = kTileD / kParts;  // positions per part
-  const int pj = tid % d, ph = tid / d;
-  float o_acc[GM];
+  // the first NB - 1 tiles, one commit group each (empty past the range)
 #pragma unroll
-  for (int g = 0; g < GM; ++g) o_acc[g] = 0.f;
-  __syncthreads();
+  for (int k = 0; k < NB - 1; ++k) {
+    const int tk = c0 + k * kTileD;
+    if (tk < c1) load_tile(k, tk, min(kTileD, c1 - tk));
+    cp_async_commit();
+  }
+  // Work split (flash-decoding inside the CTA; GM: heads per kv head, at
+  // most): warp w takes positions 8w .. 8w+7 of every 32-position tile with
+  // its own running max m, sum l and output o per head, so one CTA barrier
+  // per tile (the tile's arrival) is all the warps share:
+  //  * scores: lane -> position lane / 4 of the warp's eight and every
+  //    fourth float4 of its K row (lane & 3), all heads; the quarters meet
+  //    by two shuffles (K rows swizzled, see attn_kswz);
+  //  * softmax: max and sum over the warp's positions by shuffles; p goes
+  //    to a warp-private [8][GP] table;
+  //  * P.V: lane -> DL consecutive columns, all heads: V rows coalesced
+  //    across the warp, p by one broadcast float4 per 4 heads.
+  // The four warps' (m, l, o) meet in shared memory at the end.
+  constexpr int kWarps = kAttnThreads / 32;
+  constexpr int kPerW = kTileD / kWarps;  // positions per warp and tile (8)
+  constexpr int DL = D >= 32 ? D / 32 : 1;
+  const bool pv_lane = D >= 32 || lane < D;  // lanes with columns in P.V
+  const int tw = lane >> 2, dq = lane & 3;
+  float* pw = ps + warp * kPerW * GP;  // this warp's p table [kPerW][GP]
+  float m_g[GM], l_g[GM], o_acc[GM][DL];
+#pragma unroll
+  for (int g = 0; g < GM; ++g) {
+    m_g[g] = -INFINITY;
+    l_g[g] = 0.f;
+#pragma unroll
+    for (int e = 0; e < DL; ++e) o_acc[g][e] = 0.f;
+  }
 
   for (int t0 = c0, it = 0; t0 < c1; t0 += kTileD, ++it) {
     const int nt = min(kTileD, c1 - t0);
-    const int b = it & 1;
-    // the next tile loads into the other buffer while this one is used
-    const bool more = t0 + kTileD < c1;
-    if (more) load_tile(b ^ 1, t0 + kTileD, min(kTileD, c1 - t0 - kTileD));
-    if (more) cp_async_wait<1>();
-    else cp_async_wait<0>();
-    __syncthreads();
-    const float* kt = ks_ + b * kTileD * (d + 16);
-    const float* vt = vs + b * kTileD * d;
-    // raw scores s[t][g] = q_g . k_t * scale into ps
+    const int b = it % NB;
+    cp_async_wait<NB - 2>();  // this tile's group (one group is committed per tile)
+    __syncthreads();          // ... visible to all, and every warp is done with tile it - 1
     {
-      const int t = tid >> 2, dq = tid & 3;
-      float acc[GM];
+      const int tn = t0 + (NB - 1) * kTileD;  // into the buffer of tile it - 1
+      if (tn < c1) load_tile((it + NB - 1) % NB, tn, min(kTileD, c1 - tn));
+      cp_async_commit();
+    }
+    const float* kt = ks_ + b * kTileD * KS;
+    const float* vt = vs + b * kTileD * d;
+    const int tb = warp * kPerW;                    // first tile row of this warp
+    const int nw = max(0, min(kPerW, nt - tb));     // its rows in this tile
+    if (nw > 0) {
+      // raw scores of position tb + tw
+      const int t = tb + tw;
+      float sc[GM];
 #pragma unroll
-      for (int g = 0; g < GM; ++g) acc[g] = 0.f;
-      if (t < nt) {
-        const float* kr = kt + t * (d + 16) + dq * 4;
+      for (int g = 0; g < GM; ++g) sc[g] = 0.f;
+      if (tw < nw) {
+        const float* kr = kt + t * KS;
+        const int sw = attn_kswz<D>(t);
 #pragma unroll
         for (int j = 0; j < d; j += 16) {
-          const float4 k4 = *reinterpret_cast<const float4*>(kr + j);
+          const float4 k4 = *reinterpret_cast<const float4*>(kr + ((((j >> 2) + dq) ^ sw) << 2));
 #pragma unroll
           for (int g = 0; g < GM; ++g) {
             if (g < G) {
               const float4 q4 = *reinterpret_cast<const float4*>(qs + g * d + dq * 4 + j);
-              acc[g] = fmaf(q4.x, k4.x, acc[g]);
-              acc[g] = fmaf(q4.y, k4.y, acc[g]);
-              acc[g] = fmaf(q4.z, k4.z, acc[g]);
-              acc[g] = fmaf(q4.w, k4.w, acc[g]);
+              sc[g] = fmaf(q4.x, k4.x, sc[g]);
+              sc[g] = fmaf(q4.y, k4.y, sc[g]);
+              sc[g] = fmaf(q4.z, k4.z, sc[g]);
+              sc[g] = fmaf(q4.w, k4.w, sc[g]);
             }
           }
         }
       }
+      // online softmax over the warp's positions (lane bits 2..4), per head
 #pragma unroll
       for (int g = 0; g < GM; ++g) {
         if (g < G) {
-          float full = acc[g] + __shfl_xor_sync(0xffffffffu, acc[g], 1);
+          float full = sc[g] + __shfl_xor_sync(0xffffffffu, sc[g], 1);
           full += __shfl_xor_sync(0xffffffffu, full, 2);
-          if ((g & 3) == dq) ps[t * GP + g] = t < nt ? full * a.scale : -INFINITY;
+          const float s = tw < nw ? full * a.scale : -INFINITY;
+          float mt = fmaxf(s, __shfl_xor_sync(0xffffffffu, s, 4));
+          mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+          mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+          const float mn = fmaxf(m_g[g], mt);
+          const float p = tw < nw ? expf(s - mn) : 0.f;
+          float ls = p + __shfl_xor_sync(0xffffffffu, p, 4);
+          ls += __shfl_xor_sync(0xffffffffu, ls, 8);
+          ls += __shfl_xor_sync(0xffffffffu, ls, 16);
+          const float alpha = m_g[g] == -INFINITY ? 0.f : expf(m_g[g] - mn);
+          l_g[g] = l_g[g] * alpha + ls;
+          m_g[g] = mn;
+#pragma unroll
+          for (int e = 0; e < DL; ++e) o_acc[g][e] *= alpha;
+          if (dq == (g & 3)) pw[tw * GP + g] = p;
         }
       }
-    }
-    __syncthreads();
-    // online softmax per head: a warp per head, a lane per position
-    for (int g = warp; g < G; g += kAttnThreads / 32) {
-      const float s0 = ps[lane * GP + g];
-      const float m_old = m_s[g];
-      const float m_new = fmaxf(m_old, warp_max(s0));
-      const float p0 = lane < nt ? expf(s0 - m_new) : 0.f;
-      const float lsum = warp_sum(p0);
-      ps[lane * GP + g] = p0;
-      if (lane == 0) {
-        const float alpha = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
-        alpha_s[g] = alpha;
-        l_s[g] = l_s[g] * alpha + lsum;
-        m_s[g] = m_new;
-      }
-    }
-    __syncthreads();
-    // P.V over this thread's part of the tile's nt rows
-    if (ph < kParts) {
-#pragma unroll
-      for (int g = 0; g < GM; ++g)
-        if (g < G) o_acc[g] *= alpha_s[g];
-      const int tb = ph * kPer;
-      const int te = min(nt, tb + kPer);
+      __syncwarp();
+      // P.V over the warp's rows
+      if (pv_lane) {
 #pragma unroll 4
-      for (int t = tb; t < te; ++t) {
-        const float v = vt[t * d + pj];
+        for (int u = 0; u < nw; ++u) {
+          const float* vr = vt + (tb + u) * d + lane * DL;
+          float v[DL];
+          if (DL == 4) {
+            const float4 w4 = *reinterpret_cast<const float4*>(vr);
+            v[0] = w4.x; v[DL > 1 ? 1 : 0] = w4.y; v[DL > 2 ? 2 : 0] = w4.z; v[DL > 3 ? 3 : 0] = w4.w;
+          } else if (DL == 2) {
+            const float2 w2 = *reinterpret_cast<const float2*>(vr);
+            v[0] = w2.x; v[DL > 1 ? 1 : 0] = w2.y;
+          } else {
+            v[0] = vr[0];
+          }
 #pragma unroll
-        for (int c = 0; c < GM / 4; ++c) {
-          if (4 * c < G) {
-            const float4 p4 = *reinterpret_cast<const float4*>(ps + t * GP + 4 * c);
-            o_acc[4 * c] = fmaf(p4.x, v, o_acc[4 * c]);
-            if (4 * c + 1 < G) o_acc[4 * c + 1] = fmaf(p4.y, v, o_acc[4 * c + 1]);
-            if (4 * c + 2 < G) o_acc[4 * c + 2] = fmaf(p4.z, v, o_acc[4 * c + 2]);
-            if (4 * c + 3 < G) o_acc[4 * c + 3] = fmaf(p4.w, v, o_acc[4 * c + 3]);
+          for (int c = 0; c < GM / 4; ++c) {
+            if (4 * c < G) {
+              const float4 p4 = *reinterpret_cast<const float4*>(pw + u * GP + 4 * c);
+              const float pr[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                if (4 * c + q < G) {
+#pragma unroll
+                  for (int e = 0; e < DL; ++e)
+                    o_acc[4 * c + q][e] = fmaf(pr[q], v[e], o_acc[4 * c + q][e]);
+                }
+              }
+            }
           }
         }
       }
+      __syncwarp();
     }
-    __syncthreads();
   }
-  // the parts meet in part 0 (the tile buffers are free now)
-  if (kParts > 1) {
-    float* comb = ks_;  // [kParts - 1][G][d]
-    if (ph >= 1 && ph < kParts) {
+  cp_async_wait<0>();  // (only empty groups can remain)
+  __syncthreads();     // the tile buffers are free: the warps' (m, l, o) go there
+  {
+    float* wo = ks_;                      // [kWarps][G][d]
+    float* wm = ks_ + kWarps * G * d;     // [kWarps][GM]
+    float* wl = wm + kWarps * GM;         // [kWarps][GM]
 #pragma unroll
-      for (int g = 0; g < GM; ++g)
-        if (g < G) comb[((ph - 1) * G + g) * d + pj] = o_acc[g];
-    }
-    __syncthreads();
-    if (ph == 0) {
-      for (int q = 1; q < kParts; ++q) {
+    for (int g = 0; g < GM; ++g) {
+      if (g < G) {
+        if (pv_lane) {
 #pragma unroll
-        for (int g = 0; g < GM; ++g)
-          if (g < G) o_acc[g] += comb[((q - 1) * G + g) * d + pj];
+          for (int e = 0; e < DL; ++e) wo[(warp * G + g) * d + lane * DL + e] = o_acc[g][e];
+        }
+        if (lane == 0) {
+          wm[warp * GM + g] = m_g[g];
+          wl[warp * GM + g] = l_g[g];
+        }
       }
     }
     __syncthreads();
+    // one thread per (head, column): the CTA's (m, l) per head and o
+    if (tid < G) {
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) M = fmaxf(M, wm[w * GM + tid]);
+      float L = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        const float mw = wm[w * GM + tid];
+        L = fmaf(wl[w * GM + tid], mw == -INFINITY ? 0.f : expf(mw - M), L);
+      }
+      m_s[tid] = M;
+      l_s[tid] = L;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < G * d; idx += kAttnThreads) {
+      const int g = idx / d;
+      const float M = m_s[g];
+      float O = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        const float mw = wm[w * GM + g];
+        O = fmaf(wo[(w * G + g) * d + (idx % d)], mw == -INFINITY ? 0.f : expf(mw - M), O);
+      }
+      wo[kWarps * G * d + 2 * kWarps * GM + idx] = O;  // after wm/wl
+    }
+    __syncthreads();
   }
+  const float* ofin = ks_ + kWarps * G * d + 2 * kWarps * GM;  // [G][d] o of this CTA
   float* out = a.out + size_t(m) * a.nq * d + kvh * G * d;
   if (n_used == 1) {
     // the whole context in one CTA: finish here, no partials
-    if (split == 0 && ph == 0) {
-#pragma unroll
-      for (int g = 0; g < GM; ++g) {
-        if (g < G) {
-          const float L = l_s[g];
-          out[g * d + pj] = L > 0.f ? o_acc[g] / L : 0.f;
-        }
+    if (split == 0) {
+      for (int idx = tid; idx < G * d; idx += kAttnThreads) {
+        const float L = l_s[idx / d];
+        out[idx] = L > 0.f ? ofin[idx] / L : 0.f;
       }
     }
     if (tid == 0) trace_mark(a.trace, 3);
@@ -302,11 +364,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
   // partial (m, l, o[d]) per head
   if (split < n_used) {
     float* part = a.part + ((size_t(m) * a.nkv + kvh) * a.nsplit + split) * G * (d + 2);
-    if (ph == 0) {
-#pragma unroll
-      for (int g = 0; g < GM; ++g)
-        if (g < G) part[g * (d + 2) + 2 + pj] = o_acc[g];
-    }
+    for (int idx = tid; idx < G * d; idx += kAttnThreads)
+      part[(idx / d) * (d + 2) + 2 + (idx % d)] = ofin[idx];
     if (tid < G) {
       part[tid * (d + 2)] = m_s[tid];
       part[tid * (d + 2) + 1] = l_s[tid];
@@ -540,8 +599,10 @@ cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s, bool pdl
   }
   // tiles, or the combine's per-split weights when those are larger
   const size_t gp = (size_t(G) + 3) & ~size_t(3);
-  const size_t tiles = size_t(G) * a.d + size_t(kAttnBufs) * kTileD * (a.d + 16) +
+  const size_t ks = a.d >= 32 ? size_t(a.d) : size_t(a.d) + 16;  // attn_kstride<D>()
+  const size_t tiles = size_t(G) * a.d + size_t(kAttnBufs) * kTileD * ks +
                        size_t(kAttnBufs) * kTileD * a.d + kTileD * gp + 2 * size_t(a.d);
+  // (the end-of-loop combine of the warps reuses the K and V tiles)
   const size_t smem = sizeof(float) * std::max<size_t>(tiles, size_t(G) * a.nsplit);
   if (smem > size_t(kMaxAttnSmem)) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
