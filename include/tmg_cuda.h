@@ -211,15 +211,19 @@ int tmg_profile_decode(tmg_ctx* ctx, tmg_kv* kv, const uint32_t* tokens, int64_t
 int tmg_trace_decode(tmg_ctx* ctx, tmg_kv* kv, const uint32_t* tokens, uint64_t* out,
                      int32_t* kinds, int32_t max_slots, int32_t* n_slots);
 /* Profiling aid for the fused single-stream decode kernel: one greedy step
- * with %globaltimer stamps.  out receives n_ctas * (5 L + 1) records of 12
- * per CTA and phase (per layer: qkv, attention, o, gate/up, down; then the
- * LM head): the times (ns) its work ended, it passed the grid barrier, its
- * weight stream issued the phase's first and last copies, its input was
- * ready, its GEMV loop ended and its first stage was ready; its group count
- * (attention: tile loaded, partial written, merge done, merged or not);
- * then SM cycles: consumer warp 0 waiting for stages, consumer warp 0
- * computing, the producer waiting for free stages, the producer issuing.
- * max_u64 is the room in out; *n_ctas is set.  Appends one position. */
+ * with %globaltimer stamps (ns) and SM cycle counts.  out receives
+ * n_ctas * (5 L + 1) records of 12 words per CTA and phase (per layer: qkv,
+ * attention, o, gate/up, down; then the LM head).  GEMV phases: [0] entry,
+ * [1] input ready, [2] / [3] the weight stream's first / last copy of the
+ * phase issued, [4] cycles from the input loaded to the first stage ready,
+ * [5] GEMV loop end, [6] first stage ready, [7] groups (stages) of the CTA,
+ * [8] cycles loading the input into registers, [9] epilogue cycles (LM
+ * head: rmsnorm cycles), [10] / [11] producer cycles waiting for a free
+ * stage / issuing.  Attention phase (first item of the CTA): [0] entry,
+ * [1] q/k/v gathered, [2] first tile loaded, [3] its P.V done, [5] items
+ * done, [6] merges done, [8] outputs written, [9] after the item's closing
+ * barrier.  max_u64 is the room in out; *n_ctas is set.  Appends one
+ * position. */
 int tmg_trace_fused(tmg_ctx* ctx, tmg_kv* kv, uint32_t token, uint64_t* out, int64_t max_u64,
                     int32_t* n_ctas);
 

@@ -822,10 +822,7 @@ __device__ __forceinline__ int gemv_kseg(int ngroups, int K, int chunks, const f
       xb[c] = *reinterpret_cast<const float4*>(p + 128);
     }
   }
-  if (tw && threadIdx.x == 0) {
-    tw[8] = clock64() - c0;
-    tw[9] = 0;
-  }
+  if (tw && threadIdx.x == 0) tw[8] = clock64() - c0;
   const long long c2 = tw ? clock64() : 0;
   if (threadIdx.x == 0) S.streaming = 1;
   RingPos rp = rp_io;
