@@ -610,6 +610,9 @@ def run_c5(args, rank, world, local_rank):
         t_all = time.perf_counter() - t0
     dec = max(t_all - t_pre, 1e-9)
     n_tok = sum(len(o) for o in outs)
+    extra = {}
+    if not args.no_cpu_baseline:
+        extra = c5_cpu_leg(model, cache, cfg, w, T5, [int(o[0]) for o in outs])
     kv_step = M * cfg["num_hidden_layers"] * 2 * cfg["num_key_value_heads"] * cfg["head_dim"] * 4 * (T5 + G5 / 2)
     wbytes = sum(c2_bytes(cfg)[0].values()) * cfg["num_hidden_layers"] + c2_bytes(cfg)[1]
     gbs = (wbytes + kv_step) * G5 / dec / 1e9
@@ -623,10 +626,51 @@ def run_c5(args, rank, world, local_rank):
                               "frac": round(gbs / peak, 4), "traffic": None,
                               "peak_kind": peak_kind},
                     prefill_s=round(t_pre, 2), generate_batch_s=round(t_all, 2),
-                    timing="host wall clock: generate_batch minus the same prefills alone")
+                    timing="host wall clock: generate_batch minus the same prefills alone",
+                    **extra)
     print(json.dumps(res), flush=True)
     cache.close()
     model.close()
+
+
+def c5_cpu_leg(model, cache, cfg, w, T5, first, n_steps=8):
+    """The C5 host leg: a CPU prefill of 16 x 32K tokens is out of reach, so
+    the oracle (the reference's CPU algorithm) decodes stream 0 from the
+    GPU-prefilled f32 KV cache of its prompt: n_steps greedy steps, timed
+    (cpu_baseline), while the GPU decodes the same tokens from the same
+    cache; the logits of every step are compared (1e-3 relative / 1e-2
+    absolute) and so are the greedy ids."""
+    from oracle import oracle
+
+    M, L = cache.n_streams, cfg["num_hidden_layers"]
+    for i in range(M):
+        cache.truncate(T5, stream=i)
+    om = oracle.OracleModel(cfg, w)
+    for layer in range(L):
+        om.kv_load(layer, cache.keys_flat(layer, 0), cache.values_flat(layer, 0))
+    toks = np.asarray(first, np.uint32)
+    t_cpu, max_diff, within, ids_equal = 0.0, 0.0, True, True
+    for _ in range(n_steps):
+        g = model.forward_token(toks, cache)[0]
+        t0 = time.perf_counter()
+        ref = om.forward_token(int(toks[0]))
+        t_cpu += time.perf_counter() - t0
+        diff = np.abs(g - ref)
+        max_diff = max(max_diff, float(diff.max()))
+        within = within and bool(np.all(diff <= 1e-2 + 1e-3 * np.abs(ref)))
+        nxt = oracle.argmax(ref)
+        ids_equal = ids_equal and int(np.argmax(g)) == nxt
+        toks = np.full(M, nxt, np.uint32)
+    return {
+        "cpu_baseline": {"value": round(n_steps / t_cpu, 4), "unit": "tok/s",
+                         "cores": oracle.num_threads(), "kind": "port",
+                         "sample": f"stream 0 only: {n_steps} greedy decode steps at {T5} "
+                                   "context from the GPU-prefilled f32 KV cache (reference "
+                                   "thread policy; attention single-threaded)"},
+        "parity": {"stream": 0, "steps": n_steps, "context": T5,
+                   "max_abs_logit_diff": round(max_diff, 6),
+                   "logits_within_1e-3_rel_1e-2_abs": within, "greedy_ids_equal": ids_equal},
+    }
 
 
 def cache_trunc(cache, n):

@@ -178,3 +178,24 @@ def test_batched_long_prompts_match_single_streams(c2):
         single = generate(m, prompts[s], GenParams(max_tokens=steps))
         assert outs[s] == single.tokens, f"stream {s}"
     m.close()
+
+
+def test_bench_c5_host_leg_on_a_small_case():
+    # bench.py's C5 host leg (oracle decode from the GPU-prefilled KV cache,
+    # logits compared per step) on 3 streams of a 2-layer c2 shape
+    import bench
+
+    cfg = synth.with_layers(synth.CONFIGS["c2"], 2)
+    w = synth.make_weights(cfg, 5)
+    m = Model.from_tensors(cfg_obj(cfg), w)
+    M, T = 3, 300
+    prompts = [synth.random_prompt(cfg["vocab_size"], T, 40 + i) for i in range(M)]
+    cache = m.new_cache(T + 16, n_streams=M)
+    for i in range(M):
+        m.forward_seq(prompts[i], cache, stream=i, want_logits=False)
+    res = bench.c5_cpu_leg(m, cache, cfg, w, T, [int(p[-1]) for p in prompts], n_steps=4)
+    assert res["parity"]["logits_within_1e-3_rel_1e-2_abs"], res["parity"]
+    assert res["cpu_baseline"]["value"] > 0 and res["cpu_baseline"]["kind"] == "port"
+    assert cache.len(0, 0) == T + 4
+    cache.close()
+    m.close()
