@@ -478,6 +478,9 @@ def run_c3(args, rank, world, local_rank):
     tflops = flops / (ms / 1e3) / 1e12
     pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     peak = float(pk.get("bf16_tflops", 1590.0))
+    extra = {}
+    if not args.no_cpu_baseline:
+        extra = c3_cpu_leg(model, cfg, w, prompt)
     res = base_line(args, world, "prefill_tok_s", T / (ms / 1e3), "tok/s", ms,
                     {"workload": "c3: c2 shape, 2048-token random prompt, prefill", "global_batch": 1,
                      "seq_len": T, "parallelism": "single GPU"}, "weak", clk.summary(),
@@ -488,7 +491,8 @@ def run_c3(args, rank, world, local_rank):
                               "note": "f32 activations as bf16 hi+lo: the tensor cores run 2x these "
                                       "flops for the linear layers"},
                     e2e={"value": round(T / statistics.median(t_e), 2), "unit": "tok/s",
-                         "h2d_bytes_per_step": T * 4, "d2h_bytes_per_step": cfg["vocab_size"] * 4})
+                         "h2d_bytes_per_step": T * 4, "d2h_bytes_per_step": cfg["vocab_size"] * 4},
+                    **extra)
     print(json.dumps(res), flush=True)
     cache.close()
     model.close()
@@ -523,7 +527,9 @@ def run_c4(args, rank, world, local_rank):
         dist.broadcast(t, 0)
         tp = (bytes(t.cpu().tolist()), rank, world)
     model = Model.from_tensors(model_config(cfg), w, device=local_rank, tp=tp)
-    del w
+    host_leg = world == 1 and not args.no_cpu_baseline
+    if not host_leg:
+        del w
     prompt = synth.random_prompt(cfg["vocab_size"], P4, 17)
     cache = model.new_cache(P4 + G4 + 8)
     logits = model.forward_seq(prompt, cache)
@@ -557,6 +563,11 @@ def run_c4(args, rank, world, local_rank):
     per_gpu = (wbytes + kvb) / world
     gbs = per_gpu / (ms / 1e3 / G4) / 1e9
     peak, peak_kind = peaks()
+    extra = {}
+    if host_leg:
+        cache.truncate(P4)
+        gpu_ids = model.decode([tok], cache, 16)[0].tolist()
+        extra = c4_cpu_leg(cfg, w, prompt, logits, [tok] + gpu_ids[:15])
     if rank == 0:
         res = base_line(args, world, "decode_tok_s", value, "tok/s", ms,
                         {"workload": "c4: 8B-class, untied, 128-token prompt, greedy 512",
@@ -568,7 +579,7 @@ def run_c4(args, rank, world, local_rank):
                                   "frac": round(gbs / peak, 4), "traffic": None,
                                   "algorithmic_bytes_per_token_per_gpu": int(per_gpu),
                                   "peak_kind": peak_kind},
-                        gpu_launches=None)
+                        gpu_launches=None, **extra)
         print(json.dumps(res), flush=True)
     if dist is not None:
         dist.barrier()
@@ -631,6 +642,69 @@ def run_c5(args, rank, world, local_rank):
     print(json.dumps(res), flush=True)
     cache.close()
     model.close()
+
+
+def c3_cpu_leg(model, cfg, w, prompt, n=256):
+    """The C3 host leg: the oracle prefills the first n prompt tokens (timed,
+    reference thread policy: GEMM on every core, attention single-threaded);
+    the GPU prefills the same n tokens into a fresh cache; the last rows'
+    logits are compared (1e-3 relative / 1e-2 absolute)."""
+    from oracle import oracle
+
+    part = np.asarray(prompt[:n])
+    om = oracle.OracleModel(cfg, w)
+    t0 = time.perf_counter()
+    ref = om.forward_seq(part)
+    t_cpu = time.perf_counter() - t0
+    c = model.new_cache(n + 8)
+    g = model.forward_seq(part, c)
+    c.close()
+    diff = np.abs(g - ref)
+    return {
+        "cpu_baseline": {"value": round(n / t_cpu, 4), "unit": "tok/s", "cores": oracle.num_threads(),
+                         "kind": "port", "sample": f"prefill of the first {n} prompt tokens "
+                                                   "(reference thread policy)"},
+        "parity": {"tokens": n, "max_abs_logit_diff": round(float(diff.max()), 6),
+                   "logits_within_1e-3_rel_1e-2_abs": bool(np.all(diff <= 1e-2 + 1e-3 * np.abs(ref))),
+                   "argmax_equal": int(np.argmax(g)) == oracle.argmax(ref)},
+    }
+
+
+def c4_cpu_leg(cfg, w, prompt, gpu_logits, gpu_ids, n_steps=16):
+    """The C4 host leg (one GPU): the oracle prefills the 128-token prompt and
+    decodes n_steps greedy tokens (timed separately, reference thread
+    policy); parity: the prefill's logits against the GPU's, and the greedy
+    ids against the GPU's up to the first step whose top-2 margin is below
+    1e-3 (reported)."""
+    from oracle import oracle
+
+    om = oracle.OracleModel(cfg, w)
+    t0 = time.perf_counter()
+    logits = om.forward_seq(np.asarray(prompt))
+    t_pre = time.perf_counter() - t0
+    diff = np.abs(gpu_logits - logits)
+    ids, first_diff, tie = [], None, None
+    t0 = time.perf_counter()
+    for i in range(n_steps):
+        top = np.argsort(-logits)[:2]
+        tok = oracle.argmax(logits)
+        ids.append(tok)
+        if first_diff is None and i < len(gpu_ids) and gpu_ids[i] != tok:
+            first_diff = i
+            tie = float(logits[top[0]] - logits[top[1]])
+        logits = om.forward_token(tok)
+    t_dec = time.perf_counter() - t0
+    return {
+        "cpu_baseline": {"value": round(n_steps / t_dec, 4), "unit": "tok/s",
+                         "cores": oracle.num_threads(), "kind": "port",
+                         "sample": f"{len(prompt)}-token prefill ({len(prompt) / t_pre:.2f} tok/s) "
+                                   f"+ {n_steps} greedy decode tokens, reference thread policy"},
+        "parity": {"prefill_max_abs_logit_diff": round(float(diff.max()), 6),
+                   "prefill_logits_within_1e-3_rel_1e-2_abs":
+                       bool(np.all(diff <= 1e-2 + 1e-3 * np.abs(gpu_logits))),
+                   "greedy_steps": n_steps, "greedy_ids_equal": first_diff is None,
+                   "first_divergence": first_diff, "margin_there": tie},
+    }
 
 
 def c5_cpu_leg(model, cache, cfg, w, T5, first, n_steps=8):
