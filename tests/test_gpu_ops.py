@@ -134,9 +134,13 @@ def test_attn_decode(ctx, orc, n_ctx, nq, nkv, d):
     assert np.max(np.abs(od.cpu().numpy() - ref)) < attn_bound(q, keys, vals)
 
 
+# head dim 64 runs the register-tiled kernel (64-row blocks, 64-key tiles):
+# partial row blocks, starts inside a key tile, one row, GQA groups of 1-8
 @pytest.mark.parametrize("T,start,nq,nkv,d", [(1, 0, 4, 2, 16), (50, 0, 4, 2, 16),
                                                (50, 7, 32, 8, 64), (70, 3, 8, 2, 128),
-                                               (200, 0, 32, 8, 64)])
+                                               (200, 0, 32, 8, 64), (130, 61, 32, 8, 64),
+                                               (1, 5, 4, 2, 64), (64, 0, 4, 4, 64),
+                                               (257, 100, 16, 2, 64), (600, 1000, 8, 1, 64)])
 def test_attn_prefill(ctx, orc, T, start, nq, nkv, d):
     rng = np.random.default_rng(T + start + d)
     q = rng.normal(0, 1, (T, nq * d)).astype(np.float32)

@@ -11,8 +11,10 @@
 // per layer and stream.
 //
 // Prefill (attention_batch, src/tensor.rs:1099-1139): causal attention of T
-// query rows over the cache, one thread (or two, for head_dim 128) per
-// query row, K/V tiles staged in shared memory, online softmax in f32.
+// query rows over the cache with an online softmax in f32.  Head dim 64:
+// 64-row x 64-key register-tiled blocks (attn_prefill_tiled_kernel); other
+// head dims: one thread (or two, for head_dim 128) per query row, K/V tiles
+// staged in shared memory.
 #include <math.h>
 
 #include "common.cuh"
@@ -512,6 +514,183 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(
   }
 }
 
+// ---------------------------------------------------------------------------
+// Prefill causal attention, register-tiled (head_dim a multiple of 64).  A CTA
+// of 256 threads takes kPfBR query rows of one head (the longest row blocks
+// launch first) and walks the visible keys in kPfBC-position tiles, K and V
+// double-buffered in shared memory by cp.async.  Thread (ty, tx) = (tid / 16,
+// tid % 16) owns rows ty + 16 i (i < 4): S = Q K^T as a 4 x 4 register tile
+// over keys tx + 16 j (Q and K rows read as float4 along d; the K row stride
+// D + 4 puts the 8 rows of a 16-byte phase on distinct banks), the row max
+// and sum by shuffles over the 16 lanes that share a row, P through shared
+// memory, then O += P V as a 4-row x (D / 16)-column register tile (columns
+// tx * 4 + 64 c).  Every product is an f32 FMA; only the order of the sums
+// differs from the reference's sequential ones.
+// ---------------------------------------------------------------------------
+constexpr int kPfBR = 64, kPfBC = 64, kPfThreads = 256;
+
+template <int D>
+constexpr size_t attn_prefill_tiled_smem() {
+  return sizeof(float) * (size_t(kPfBR) * (D + 4) + 2 * size_t(kPfBC) * (D + 4) +
+                          2 * size_t(kPfBC) * D + size_t(kPfBR) * (kPfBC + 4));
+}
+
+template <int D>
+__global__ void __launch_bounds__(kPfThreads, 2) attn_prefill_tiled_kernel(
+    const float* __restrict__ q, int64_t q_ld, const float* __restrict__ kc,
+    const float* __restrict__ vc, int64_t T, int64_t pos0, int nq, int nkv, float scale,
+    float* __restrict__ out, int64_t out_ld) {
+  static_assert(D % 64 == 0, "columns are float4 groups of 16 lanes");
+  constexpr int QS = D + 4, PS = kPfBC + 4, NC = D / 64, D4 = D / 4;
+  extern __shared__ __align__(16) float pf_smem[];
+  float* qs = pf_smem;                 // [kPfBR][QS]
+  float* ks = qs + kPfBR * QS;         // [2][kPfBC][QS]
+  float* vs = ks + 2 * kPfBC * QS;     // [2][kPfBC][D]
+  float* ps = vs + 2 * kPfBC * D;      // [kPfBR][PS]
+  const int h = blockIdx.x;
+  const int kvh = h / (nq / nkv);
+  const int64_t kvd = int64_t(nkv) * D;
+  const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+  const int64_t r0 = int64_t(gridDim.y - 1 - blockIdx.y) * kPfBR;
+  const int64_t last_row = T - 1 < r0 + kPfBR - 1 ? T - 1 : r0 + kPfBR - 1;
+  const int64_t n_keys = pos0 + last_row + 1;  // keys 0 .. n_keys-1 are visible to some row
+  const int ntiles = int((n_keys + kPfBC - 1) / kPfBC);
+
+  for (int i = tid; i < kPfBR * D4; i += kPfThreads) {
+    const int r = i / D4, j4 = i % D4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r0 + r < T) v = *reinterpret_cast<const float4*>(q + (r0 + r) * q_ld + int64_t(h) * D + j4 * 4);
+    *reinterpret_cast<float4*>(qs + r * QS + j4 * 4) = v;
+  }
+  // positions past n_keys are zero-filled (never stale shared memory: 0 * NaN)
+  auto load_tile = [&](int n, int b) {
+    const int64_t t0 = int64_t(n) * kPfBC;
+    float* kb = ks + b * kPfBC * QS;
+    float* vb = vs + b * kPfBC * D;
+    for (int i = tid; i < kPfBC * D4; i += kPfThreads) {
+      const int t = i / D4, j4 = i % D4;
+      float* kd = kb + t * QS + j4 * 4;
+      float* vd = vb + t * D + j4 * 4;
+      if (t0 + t < n_keys) {
+        const int64_t off = (t0 + t) * kvd + int64_t(kvh) * D + j4 * 4;
+        cp_async16(kd, kc + off);
+        cp_async16(vd, vc + off);
+      } else {
+        *reinterpret_cast<float4*>(kd) = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(vd) = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    cp_async_commit();
+  };
+
+  // a row's position, clamped so rows past T (not stored) see only real keys
+  int64_t pos[4];
+  float m_run[4], l_run[4], o[4][4 * NC];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t p = pos0 + r0 + ty + 16 * i;
+    pos[i] = p < n_keys - 1 ? p : n_keys - 1;
+    m_run[i] = -INFINITY;
+    l_run[i] = 0.f;
+#pragma unroll
+    for (int c = 0; c < 4 * NC; ++c) o[i][c] = 0.f;
+  }
+
+  load_tile(0, 0);
+  for (int n = 0; n < ntiles; ++n) {
+    cp_async_wait<0>();
+    __syncthreads();  // tile n (and the Q tile) visible; tile n-1's P.V finished
+    if (n + 1 < ntiles) load_tile(n + 1, (n + 1) & 1);
+    const float* kb = ks + (n & 1) * kPfBC * QS;
+    const float* vb = vs + (n & 1) * kPfBC * D;
+    float s[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s[i][j] = 0.f;
+#pragma unroll
+    for (int k = 0; k < D; k += 4) {
+      float4 a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = *reinterpret_cast<const float4*>(qs + (ty + 16 * i) * QS + k);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4*>(kb + (tx + 16 * j) * QS + k);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float acc = s[i][j];
+          acc = fmaf(a[i].x, b[j].x, acc);
+          acc = fmaf(a[i].y, b[j].y, acc);
+          acc = fmaf(a[i].z, b[j].z, acc);
+          acc = fmaf(a[i].w, b[j].w, acc);
+          s[i][j] = acc;
+        }
+    }
+    const int64_t t0 = int64_t(n) * kPfBC;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float mt = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        s[i][j] = (t0 + tx + 16 * j) <= pos[i] ? s[i][j] * scale : -INFINITY;
+        mt = fmaxf(mt, s[i][j]);
+      }
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
+      const float m_new = fmaxf(m_run[i], mt);
+      const float alpha = m_run[i] == -INFINITY ? 0.f : expf(m_run[i] - m_new);
+      float ls = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float p = s[i][j] == -INFINITY ? 0.f : expf(s[i][j] - m_new);
+        ps[(ty + 16 * i) * PS + tx + 16 * j] = p;
+        ls += p;
+      }
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+      l_run[i] = l_run[i] * alpha + ls;
+      m_run[i] = m_new;
+#pragma unroll
+      for (int c = 0; c < 4 * NC; ++c) o[i][c] *= alpha;
+    }
+    __syncthreads();  // P visible
+#pragma unroll 4
+    for (int t = 0; t < kPfBC; t += 4) {
+      float4 pv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pv[i] = *reinterpret_cast<const float4*>(ps + (ty + 16 * i) * PS + t);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+          const float4 v = *reinterpret_cast<const float4*>(vb + (t + e) * D + 64 * c + tx * 4);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float p = e == 0 ? pv[i].x : e == 1 ? pv[i].y : e == 2 ? pv[i].z : pv[i].w;
+            o[i][4 * c + 0] = fmaf(p, v.x, o[i][4 * c + 0]);
+            o[i][4 * c + 1] = fmaf(p, v.y, o[i][4 * c + 1]);
+            o[i][4 * c + 2] = fmaf(p, v.z, o[i][4 * c + 2]);
+            o[i][4 * c + 3] = fmaf(p, v.w, o[i][4 * c + 3]);
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t row = r0 + ty + 16 * i;
+    if (row < T) {
+      const float inv = 1.0f / l_run[i];
+#pragma unroll
+      for (int c = 0; c < NC; ++c)
+        *reinterpret_cast<float4*>(out + row * out_ld + int64_t(h) * D + 64 * c + tx * 4) =
+            make_float4(o[i][4 * c] * inv, o[i][4 * c + 1] * inv, o[i][4 * c + 2] * inv,
+                        o[i][4 * c + 3] * inv);
+    }
+  }
+}
+
 // RoPE of q and k for T prefill rows + KV append (model.rs:533-553).
 // Grid (T); threads over (heads x half).
 __global__ void rope_append_kernel(float* qkv, int64_t ld, int nq, int nkv, int d,
@@ -577,6 +756,7 @@ cudaError_t attn_attr() {
 }
 
 cudaError_t attn_prepare() {
+  TMG_CUDA_TRY(set_carveout(attn_prefill_tiled_kernel<64>, int(attn_prefill_tiled_smem<64>())));
   TMG_CUDA_TRY(set_carveout(rope_append_kernel));
   TMG_CUDA_TRY(set_carveout(rope_rows_kernel));
   TMG_CUDA_TRY(attn_attr<16>());
@@ -622,6 +802,16 @@ cudaError_t launch_attn_prefill(const float* q, int64_t q_ld, const float* kc, c
                                 int64_t T, int64_t pos0, int nq, int nkv, int d, float scale,
                                 float* out, int64_t out_ld, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
+  // the register-tiled kernel reads q and writes out as float4 rows
+  const bool vec = ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out) |
+                     reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc)) & 15) == 0 &&
+                   q_ld % 4 == 0 && out_ld % 4 == 0;
+  if (d == 64 && vec && nkv > 0 && nq % nkv == 0) {
+    dim3 grid(nq, unsigned((T + kPfBR - 1) / kPfBR));
+    attn_prefill_tiled_kernel<64><<<grid, kPfThreads, attn_prefill_tiled_smem<64>(), s>>>(
+        q, q_ld, kc, vc, T, pos0, nq, nkv, scale, out, out_ld);
+    return cudaGetLastError();
+  }
   switch (d) {
 #define TMG_ATTN_CASE(D)                                                                   \
   case D: {                                                                                \
