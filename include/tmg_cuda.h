@@ -91,6 +91,15 @@ int tmg_safetensors_count(const char* path, int64_t* n, char* err, int errlen);
 int tmg_safetensors_info(const char* path, int64_t i, char* name, int namelen, int32_t* dtype,
                          int32_t* rank, int64_t shape[4], int64_t* offset, int64_t* nbytes,
                          char* err, int errlen);
+/* TMB1 (the reference's load-optimised repack) header inspection,
+ * parse_tmb_header, src/tmb.rs:80-121: the embedded config (cfg may be NULL;
+ * ModelConfig::from_json, src/config.rs:39-93, so an EOS list written under
+ * the repack's "eos_token_ids" key is not read back, as in the reference),
+ * the number of tensors, and for index i its name, absolute data offset and
+ * byte length.  TMG_ERR_IO with the reference's messages on a bad file. */
+int tmg_tmb_count(const char* path, tmg_config* cfg, int64_t* n, char* err, int errlen);
+int tmg_tmb_info(const char* path, int64_t i, char* name, int namelen, int64_t* offset,
+                 int64_t* nbytes, char* err, int errlen);
 /* The reference's f16 -> f32 widening, src/safetensors_loader.rs:149-173. */
 float tmg_f16_to_f32(uint16_t h);
 /* Library version string. */
@@ -115,6 +124,13 @@ const char* tmg_last_error(const tmg_ctx* ctx);
  * streams BF16 only.  A missing lm_head.weight ties the head to the
  * embedding (model.rs:230-233). */
 int tmg_load_safetensors(tmg_ctx* ctx, const char* path);
+/* Upload every tensor of a TMB1 file (load_model_tmb, src/model.rs:108-179)
+ * straight from its mapping: BF16 matrices bits unchanged, f32 norms, and the
+ * f32 embedding back to its BF16 bits (a value that is not a widened BF16 is
+ * refused with TMG_ERR_INVALID).  The file's model shape must equal the
+ * context's (create the context from tmg_tmb_count's config).  A missing
+ * lm_head.weight ties the head to the embedding. */
+int tmg_load_tmb(tmg_ctx* ctx, const char* path);
 /* Upload one tensor by its HF name from host memory (a WMat, src/tensor.rs:
  * 198-206, and the f32 vectors of src/model.rs:27-28).  dtype: 0 F32, 1 BF16.
  * Matrices must be BF16; vectors may be F32 or BF16. */

@@ -87,6 +87,54 @@ def test_c1_load_from_file_and_stepwise_logits(orc, c1, tmp_path):
     assert cache.len(0) == 0
 
 
+@pytest.mark.parametrize("tied", [False, True])
+def test_c1_load_from_tmb_repack(orc, c1, tmp_path, tied):
+    # load_model_tmb (src/model.rs:108-179): the repacked file gives the same
+    # greedy ids and first-step logits as the tensors it was written from
+    from tinyminigo_b200 import tmb
+
+    d, cfg, t = c1
+    if tied:
+        t = {k: v for k, v in t.items() if k != "lm_head.weight"}
+        cfg = dict(cfg, tie_word_embeddings=True)
+    p = tmp_path / "m.tmb"
+    tmb.write(p, dict(cfg, eos_token_ids=[d["greedy"][3]]), t)
+    m = Model.load(p)
+    assert m.config.eos_token_ids == []  # the repack's EOS key is not read back
+    ref = Model.from_tensors(cfg_obj(cfg), t)
+    a = generate(m, d["prompt"], GenParams(max_tokens=20))
+    b = generate(ref, d["prompt"], GenParams(max_tokens=20))
+    assert a.tokens == b.tokens
+    assert np.max(np.abs(a.logits_first_step - b.logits_first_step)) <= 1e-6
+    if not tied:
+        assert a.tokens == d["greedy"][:20]
+    m.close()
+    ref.close()
+
+
+def test_tmb_load_refusals(c1, tmp_path):
+    import ctypes
+
+    from tinyminigo_b200 import tmb
+    from tinyminigo_b200._lib import TmgError, check, lib
+
+    d, cfg, t = c1
+    # an f32 embedding that is not a widened BF16 cannot go to the BF16 table
+    t2 = dict(t)
+    t2["model.embed_tokens.weight"] = synth.bf16_to_f32(t["model.embed_tokens.weight"]) * np.float32(1.0001)
+    p = tmp_path / "f32.tmb"
+    tmb.write(p, cfg, t2)
+    with pytest.raises(TmgError, match="not a BF16 value"):
+        Model.load(p)
+    # the file's shape must be the context's
+    q = tmp_path / "ok.tmb"
+    tmb.write(q, cfg, t)
+    other = Model(cfg_obj(dict(cfg, intermediate_size=256)))
+    with pytest.raises(TmgError, match="does not match"):
+        check(lib().tmg_load_tmb(other._h, str(q).encode()), other._h, "load")
+    other.close()
+
+
 def test_c1_eos_stops_like_reference(orc, c1):
     d, cfg, t = c1
     eos = d["greedy"][5]

@@ -74,10 +74,13 @@ SIGNATURES = {
     "tmg_safetensors_count": (_I, [_CP, _PI64, _CP, _I]),
     "tmg_safetensors_info": (_I, [_CP, _I64, _CP, _I, ctypes.POINTER(_I32), ctypes.POINTER(_I32),
                                   ctypes.POINTER(_I64), _PI64, _PI64, _CP, _I]),
+    "tmg_tmb_count": (_I, [_CP, ctypes.POINTER(Config), _PI64, _CP, _I]),
+    "tmg_tmb_info": (_I, [_CP, _I64, _CP, _I, _PI64, _PI64, _CP, _I]),
     "tmg_create": (_I, [_I, ctypes.POINTER(Config), _PP]),
     "tmg_destroy": (_I, [_P]),
     "tmg_last_error": (_CP, [_P]),
     "tmg_load_safetensors": (_I, [_P, _CP]),
+    "tmg_load_tmb": (_I, [_P, _CP]),
     "tmg_set_tensor": (_I, [_P, _CP, _I32, _P, _I64]),
     "tmg_finalize": (_I, [_P]),
     "tmg_weight_bytes": (_I64, [_P]),

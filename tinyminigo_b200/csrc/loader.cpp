@@ -387,6 +387,79 @@ bool safetensors_parse(const uint8_t* bytes, size_t n, std::vector<StTensor>& ou
   return true;
 }
 
+namespace {
+uint64_t le_u64(const uint8_t* p) {
+  uint64_t v = 0;
+  for (int i = 7; i >= 0; --i) v = (v << 8) | p[i];
+  return v;
+}
+uint32_t le_u32(const uint8_t* p) {
+  return uint32_t(p[0]) | uint32_t(p[1]) << 8 | uint32_t(p[2]) << 16 | uint32_t(p[3]) << 24;
+}
+}  // namespace
+
+bool tmb_parse(const uint8_t* bytes, size_t n, tmg_config* cfg, std::vector<TmbTensor>& out,
+               std::string& err) {
+  out.clear();
+  if (n < 16) {
+    err = "TMB file too small";
+    return false;
+  }
+  if (std::memcmp(bytes, "TMB1", 4) != 0) {
+    err = "not a TMB1 file (wrong magic)";
+    return false;
+  }
+  const uint64_t cfg_len = le_u64(bytes + 4);
+  const uint32_t count = le_u32(bytes + 12);
+  // every step checks the bytes it reads against what is left of the file
+  uint64_t pos = 16;
+  auto need = [&](uint64_t k, const char* what) {
+    if (k > n - pos) {
+      err = std::string("TMB file truncated in the ") + what;
+      return false;
+    }
+    return true;
+  };
+  if (!need(cfg_len, "config")) return false;
+  Json cj;
+  if (!json_parse(reinterpret_cast<const char*>(bytes + pos), size_t(cfg_len), cj, err)) {
+    err = "TMB config JSON (" + err + ")";
+    return false;
+  }
+  tmg_config c{};
+  if (!config_from_json(cj, &c, err)) return false;
+  pos += cfg_len;
+  if (!need(8, "weights length")) return false;
+  const uint64_t weights_len = le_u64(bytes + pos);
+  const uint64_t weights_off = (pos + 8 + 7) & ~uint64_t(7);  // TENSOR_ALIGN = 8
+  if (weights_off > n || weights_len > n - weights_off) {
+    err = "TMB weights section runs past the end of the file";
+    return false;
+  }
+  pos = weights_off + weights_len;
+  out.reserve(count);
+  for (uint32_t i = 0; i < count; ++i) {
+    if (!need(4, "index")) return false;
+    const uint32_t name_len = le_u32(bytes + pos);
+    pos += 4;
+    if (!need(uint64_t(name_len) + 16, "index")) return false;
+    TmbTensor t;
+    t.name.assign(reinterpret_cast<const char*>(bytes + pos), name_len);
+    pos += name_len;
+    const uint64_t off = le_u64(bytes + pos), len = le_u64(bytes + pos + 8);
+    pos += 16;
+    if (off > n || len > n - off) {
+      err = "TMB tensor range out of bounds: " + t.name;
+      return false;
+    }
+    t.offset = int64_t(off);
+    t.nbytes = int64_t(len);
+    out.push_back(std::move(t));
+  }
+  if (cfg) *cfg = c;
+  return true;
+}
+
 // f16_to_f32, src/safetensors_loader.rs:149-173
 float f16_to_f32(uint16_t h) {
   uint32_t sign = uint32_t(h & 0x8000) << 16;

@@ -39,6 +39,23 @@ struct StTensor {
 bool safetensors_parse(const uint8_t* bytes, size_t n, std::vector<StTensor>& out,
                        std::string& err);
 
+// One tensor of a TMB1 file: where its bytes lie in the file (TensorRef,
+// src/tmb.rs:28-35).
+struct TmbTensor {
+  std::string name;
+  int64_t offset = 0;  // absolute file offset of the data
+  int64_t nbytes = 0;
+};
+
+// parse_tmb_header, src/tmb.rs:80-121: magic "TMB1", u64 config length, u32
+// tensor count, the config JSON (ModelConfig::from_json), the weights section
+// (u64 length, zero padding to 8 bytes, the tensors), then per tensor
+// (u32 name length, name, u64 offset, u64 length).  Ranges that fall outside
+// the file are errors here (the reference panics on a short header and checks
+// tensor ranges when it borrows them, TensorRef::bytes, src/tmb.rs:39-44).
+bool tmb_parse(const uint8_t* bytes, size_t n, tmg_config* cfg, std::vector<TmbTensor>& out,
+               std::string& err);
+
 struct MappedFile {
   int fd = -1;
   void* base = nullptr;

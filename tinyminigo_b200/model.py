@@ -158,11 +158,23 @@ class Model:
     # --- construction ---
     @staticmethod
     def load(model_path, device: int = 0, tp=None) -> "Model":
-        """Model::load (src/model.rs:384-389) of a safetensors file with a
-        config.json beside it; weights go to HBM once."""
+        """Model::load (src/model.rs:384-389): a TMB1 repack (recognised by its
+        magic, load_model, src/model.rs:90-96) carries its own config; a
+        safetensors file needs config.json beside it.  Weights go to HBM once."""
         p = Path(model_path)
         if not p.exists():
             raise FileNotFoundError(f"model file not found: {p}")
+        from . import tmb
+
+        if tmb.is_tmb(p):
+            cfg, _ = tmb.index(p)
+            m = Model(cfg, device, tp)
+            try:
+                check(lib().tmg_load_tmb(m._h, str(p).encode()), m._h, "load")
+            except TmgError:
+                m.close()
+                raise
+            return m
         cp = ModelConfig.config_path_for_model(p)
         if cp is None:
             raise FileNotFoundError(f"config.json not found next to {p}")
