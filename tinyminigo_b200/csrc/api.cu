@@ -705,14 +705,27 @@ int forward_seq(tmg_ctx* c, tmg_kv* kv, int stream, const uint32_t* tokens, int6
       }
       CK(launch_rmsnorm(c->X, Lw.post_norm, eps, c->h, Tc, 1, c->Xn, c->stream), "rmsnorm");
       CK(gemm(c, c->Xn, Lw.wg, Tc, c->I, c->h, c->G, c->I, false), "gemm gate");
-      CK(gemm(c, c->Xn, Lw.wu, Tc, c->I, c->h, c->U, c->I, false), "gemm up");
-      CK(launch_swiglu(c->G, c->U, Tc * c->I, c->G, c->stream), "swiglu");
-      if (tp) {
-        CK(gemm(c, c->G, Lw.wd, Tc, c->h, c->I, c->Xn, c->h, false), "gemm down");
-        CK(tp_reduce_add(c, c->Xn, c->X, Tc * c->h), "allreduce");
+      if (gemm_tc_supported(c->h, Lw.wg) && gemm_tc_supported(c->h, Lw.wu)) {
+        // gate and up read the same input: its hi/lo split from the gate GEMM
+        CK(launch_gemm_tc(c->sp_hi, c->sp_lo, Lw.wu, Tc, c->I, c->h, c->U, c->I, false, c->d_err,
+                          c->stream),
+           "gemm up");
       } else {
-        CK(gemm(c, c->G, Lw.wd, Tc, c->h, c->I, c->X, c->h, true), "gemm down");
+        CK(gemm(c, c->Xn, Lw.wu, Tc, c->I, c->h, c->U, c->I, false), "gemm up");
       }
+      float* down_y = tp ? c->Xn : c->X;
+      if (gemm_tc_supported(c->I, Lw.wd) && (ensure_split(c, size_t(Tc) * c->I) == cudaSuccess) &&
+          swiglu_split_supported(c->G, c->U, Tc * c->I, c->sp_hi, c->sp_lo)) {
+        // SwiGLU written straight as the down GEMM's hi/lo operands
+        CK(launch_swiglu_split(c->G, c->U, Tc * c->I, c->sp_hi, c->sp_lo, c->stream), "swiglu");
+        CK(launch_gemm_tc(c->sp_hi, c->sp_lo, Lw.wd, Tc, c->h, c->I, down_y, c->h, !tp, c->d_err,
+                          c->stream),
+           "gemm down");
+      } else {
+        CK(launch_swiglu(c->G, c->U, Tc * c->I, c->G, c->stream), "swiglu");
+        CK(gemm(c, c->G, Lw.wd, Tc, c->h, c->I, down_y, c->h, !tp), "gemm down");
+      }
+      if (tp) CK(tp_reduce_add(c, c->Xn, c->X, Tc * c->h), "allreduce");
     }
     if (t0 + Tc == T) {
       GemvArgs H;
@@ -1075,6 +1088,37 @@ int tmg_safetensors_info(const char* path, int64_t i, char* name, int namelen, i
   return TMG_OK;
 }
 
+int tmg_tmb_count(const char* path, tmg_config* cfg, int64_t* n, char* err, int errlen) {
+  MappedFile f;
+  std::string e;
+  std::vector<TmbTensor> ts;
+  if (!path || !n) return TMG_ERR_INVALID;
+  if (!f.open(path, e) || !tmb_parse(f.data(), f.size, cfg, ts, e)) {
+    if (err && errlen > 0) std::snprintf(err, size_t(errlen), "%s", e.c_str());
+    return TMG_ERR_IO;
+  }
+  *n = int64_t(ts.size());
+  return TMG_OK;
+}
+
+int tmg_tmb_info(const char* path, int64_t i, char* name, int namelen, int64_t* offset,
+                 int64_t* nbytes, char* err, int errlen) {
+  MappedFile f;
+  std::string e;
+  std::vector<TmbTensor> ts;
+  if (!path) return TMG_ERR_INVALID;
+  if (!f.open(path, e) || !tmb_parse(f.data(), f.size, nullptr, ts, e)) {
+    if (err && errlen > 0) std::snprintf(err, size_t(errlen), "%s", e.c_str());
+    return TMG_ERR_IO;
+  }
+  if (i < 0 || i >= int64_t(ts.size())) return TMG_ERR_INVALID;
+  const TmbTensor& t = ts[size_t(i)];
+  if (name && namelen > 0) std::snprintf(name, size_t(namelen), "%s", t.name.c_str());
+  if (offset) *offset = t.offset;
+  if (nbytes) *nbytes = t.nbytes;
+  return TMG_OK;
+}
+
 int tmg_rng_uniforms(uint64_t seed, int64_t n, float* out) {
   if (n < 0 || (n > 0 && !out)) return TMG_ERR_INVALID;
   stdrng_uniforms(seed, n, out);
@@ -1167,6 +1211,63 @@ int tmg_load_safetensors(tmg_ctx* c, const char* path) {
     int64_t numel = t.nbytes / (t.dtype == 0 ? 4 : 2);
     rc = set_tensor(c, t.name, t.dtype, f.data() + t.offset, numel);
     if (rc) return rc;
+  }
+  CK(cudaStreamSynchronize(c->stream), "load");
+  return finalize(c);
+}
+
+// load_model_tmb, src/model.rs:108-179: the file's BF16 matrices go to HBM
+// straight from the mapping, norms as f32; the embedding, stored as f32
+// there, returns to its BF16 bits (exact for a file repacked from a BF16
+// checkpoint; any other value is refused rather than rounded).
+int tmg_load_tmb(tmg_ctx* c, const char* path) {
+  if (!c || !path) return fail(c, TMG_ERR_INVALID, "bad argument");
+  if (!c->has_model) return fail(c, TMG_ERR_INVALID, "context has no model config");
+  cudaSetDevice(c->device);
+  MappedFile f;
+  std::string e;
+  std::vector<TmbTensor> ts;
+  tmg_config fc{};
+  if (!f.open(path, e) || !tmb_parse(f.data(), f.size, &fc, ts, e)) return fail(c, TMG_ERR_IO, e);
+  const tmg_config& cc = c->cfg;
+  if (fc.hidden_size != cc.hidden_size || fc.num_hidden_layers != cc.num_hidden_layers ||
+      fc.num_attention_heads != cc.num_attention_heads ||
+      fc.num_key_value_heads != cc.num_key_value_heads || fc.head_dim != cc.head_dim ||
+      fc.intermediate_size != cc.intermediate_size || fc.vocab_size != cc.vocab_size)
+    return fail(c, TMG_ERR_INVALID, "TMB config does not match the context's model shape");
+  int rc = ensure_alloc(c);
+  if (rc) return rc;
+  for (const TmbTensor& t : ts) {
+    const uint8_t* p = f.data() + t.offset;
+    const bool is_vec = t.name == "model.norm.weight" ||
+                        t.name.find("layernorm.weight") != std::string::npos;
+    if (t.name == "model.embed_tokens.weight") {
+      if (t.nbytes % 4) return fail(c, TMG_ERR_INVALID, "TMB f32 tensor has non-multiple-of-4 byte length");
+      const int64_t numel = t.nbytes / 4;
+      if (numel != int64_t(c->V) * c->h)
+        return fail(c, TMG_ERR_INVALID, "TMB embed size " + std::to_string(numel) +
+                                            " != vocab*hidden " + std::to_string(int64_t(c->V) * c->h));
+      std::vector<uint16_t> bits(static_cast<size_t>(numel));
+      for (int64_t i = 0; i < numel; ++i) {
+        uint32_t u;
+        std::memcpy(&u, p + 4 * i, 4);
+        if (u & 0xffffu)
+          return fail(c, TMG_ERR_INVALID, "TMB embedding value " + std::to_string(i) +
+                                              " is not a BF16 value (the device embedding is BF16)");
+        bits[size_t(i)] = uint16_t(u >> 16);
+      }
+      rc = set_tensor(c, t.name, 1, bits.data(), numel);
+      if (rc) return rc;
+      CK(cudaStreamSynchronize(c->stream), "load");  // `bits` is freed on return
+    } else if (is_vec) {
+      if (t.nbytes % 4) return fail(c, TMG_ERR_INVALID, "TMB f32 tensor has non-multiple-of-4 byte length");
+      rc = set_tensor(c, t.name, 0, p, t.nbytes / 4);
+      if (rc) return rc;
+    } else {
+      if (t.nbytes % 2) return fail(c, TMG_ERR_INVALID, "TMB BF16 tensor has odd byte length");
+      rc = set_tensor(c, t.name, 1, p, t.nbytes / 2);
+      if (rc) return rc;
+    }
   }
   CK(cudaStreamSynchronize(c->stream), "load");
   return finalize(c);

@@ -224,6 +224,44 @@ __global__ void split_kernel(const float* __restrict__ x, int64_t n, __nv_bfloat
   }
 }
 
+// Four elements per thread: a float4 in, the hi and lo halves out as 8-byte
+// words (element 0 in the low bits).
+__device__ __forceinline__ void split4(float4 v, uint2* hi, uint2* lo) {
+  const float a[4] = {v.x, v.y, v.z, v.w};
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const __nv_bfloat16 hb = __float2bfloat16_rn(a[e]);
+    h[e] = __bfloat16_as_ushort(hb);
+    l[e] = __bfloat16_as_ushort(__float2bfloat16_rn(a[e] - __bfloat162float(hb)));
+  }
+  *hi = make_uint2(h[0] | h[1] << 16, h[2] | h[3] << 16);
+  *lo = make_uint2(l[0] | l[1] << 16, l[2] | l[3] << 16);
+}
+
+__global__ void split4_kernel(const float4* __restrict__ x, int64_t n4, uint2* __restrict__ hi,
+                              uint2* __restrict__ lo) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n4;
+       i += int64_t(gridDim.x) * blockDim.x)
+    split4(x[i], hi + i, lo + i);
+}
+
+// SwiGLU (src/model.rs:473-475, the same arithmetic as swiglu_kernel:
+// g / (1 + exp(-g)) * u) written straight as the down GEMM's hi/lo operands.
+__global__ void swiglu_split4_kernel(const float4* __restrict__ g, const float4* __restrict__ u,
+                                     int64_t n4, uint2* __restrict__ hi, uint2* __restrict__ lo) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n4;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const float4 gv = g[i], uv = u[i];
+    float4 a;
+    a.x = (gv.x / (1.0f + expf(-gv.x))) * uv.x;
+    a.y = (gv.y / (1.0f + expf(-gv.y))) * uv.y;
+    a.z = (gv.z / (1.0f + expf(-gv.z))) * uv.z;
+    a.w = (gv.w / (1.0f + expf(-gv.w))) * uv.w;
+    split4(a, hi + i, lo + i);
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static bool tried = false;
@@ -261,14 +299,46 @@ bool gemm_tc_supported(int64_t K, const void* w) {
 
 cudaError_t gemm_tc_prepare() {
   TMG_CUDA_TRY(set_carveout(split_kernel));
+  TMG_CUDA_TRY(set_carveout(split4_kernel));
+  TMG_CUDA_TRY(set_carveout(swiglu_split4_kernel));
   return set_carveout(gemm_tc_kernel, SMEM_BYTES);
 }
 
+namespace {
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7) == 0; }
+}  // namespace
+
 cudaError_t launch_split(const float* x, int64_t n, uint16_t* hi, uint16_t* lo, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
+  if (n % 4 == 0 && aligned16(x) && aligned8(hi) && aligned8(lo)) {
+    const int64_t n4 = n / 4;
+    const int64_t blocks = std::min<int64_t>((n4 + 255) / 256, 148 * 16);
+    split4_kernel<<<unsigned(blocks), 256, 0, s>>>(reinterpret_cast<const float4*>(x), n4,
+                                                   reinterpret_cast<uint2*>(hi),
+                                                   reinterpret_cast<uint2*>(lo));
+    return cudaGetLastError();
+  }
   const int64_t blocks = std::min<int64_t>((n + 255) / 256, 148 * 16);
   split_kernel<<<unsigned(blocks), 256, 0, s>>>(x, n, reinterpret_cast<__nv_bfloat16*>(hi),
                                                 reinterpret_cast<__nv_bfloat16*>(lo));
+  return cudaGetLastError();
+}
+
+bool swiglu_split_supported(const float* g, const float* u, int64_t n, const uint16_t* hi,
+                            const uint16_t* lo) {
+  return n % 4 == 0 && aligned16(g) && aligned16(u) && aligned8(hi) && aligned8(lo);
+}
+
+cudaError_t launch_swiglu_split(const float* g, const float* u, int64_t n, uint16_t* hi,
+                                uint16_t* lo, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  if (!swiglu_split_supported(g, u, n, hi, lo)) return cudaErrorInvalidValue;
+  const int64_t n4 = n / 4;
+  const int64_t blocks = std::min<int64_t>((n4 + 255) / 256, 148 * 16);
+  swiglu_split4_kernel<<<unsigned(blocks), 256, 0, s>>>(
+      reinterpret_cast<const float4*>(g), reinterpret_cast<const float4*>(u), n4,
+      reinterpret_cast<uint2*>(hi), reinterpret_cast<uint2*>(lo));
   return cudaGetLastError();
 }
 

@@ -176,6 +176,12 @@ cudaError_t launch_gemm_simt(const float* x, const uint16_t* w, int64_t T, int64
 bool gemm_tc_supported(int64_t K, const void* w);
 cudaError_t gemm_tc_prepare();
 cudaError_t launch_split(const float* x, int64_t n, uint16_t* hi, uint16_t* lo, cudaStream_t s);
+// The SwiGLU of launch_swiglu written as the hi/lo BF16 split of its result
+// (the down GEMM's operands); needs n % 4 == 0, g and u 16-byte aligned.
+bool swiglu_split_supported(const float* g, const float* u, int64_t n, const uint16_t* hi,
+                            const uint16_t* lo);
+cudaError_t launch_swiglu_split(const float* g, const float* u, int64_t n, uint16_t* hi,
+                                uint16_t* lo, cudaStream_t s);
 cudaError_t launch_gemm_tc(const uint16_t* x_hi, const uint16_t* x_lo, const uint16_t* w,
                            int64_t T, int64_t N, int64_t K, float* y, int64_t ldy,
                            bool accumulate, int32_t* err, cudaStream_t s);
