@@ -17,6 +17,9 @@
 // staged in shared memory.
 #include <math.h>
 
+#include <algorithm>
+#include <stdlib.h>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -429,6 +432,316 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnDec
 }
 
 // ---------------------------------------------------------------------------
+// Decode attention for head dim 64 and at most 4 query heads per kv head (the
+// 1B-class shapes), with K and V streamed from HBM straight into registers:
+// each K/V element serves only the G heads of its group, so staging tiles in
+// shared memory bought nothing but shared-memory latency.  Same grid, split,
+// append, partials and ticketed merge as attn_decode_kernel.  Inside the CTA
+// eight row streams (4 warps x 2 half-warps) take blocks of kRegRows
+// consecutive positions in turn; lane l16 of a half-warp holds columns
+// 4 l16 .. 4 l16 + 3 of q (all heads), of each K/V row it loads (one 16-byte
+// non-coherent load per row, a half-warp reads a row's 256 contiguous bytes)
+// and of its output.  Scores meet over the 16 lanes by a shuffle butterfly;
+// each stream keeps its own running max, sum and output per head; the
+// streams meet in shared memory at the end.  The decoded position's row
+// comes from shared memory (this CTA wrote it to the cache).
+// Dynamic shared memory: the merge weights [G][nsplit].
+// ---------------------------------------------------------------------------
+constexpr int kRegRows = 4;
+
+__global__ void __launch_bounds__(kAttnThreads, 4) attn_decode_reg_kernel(const AttnDecodeArgs a) {
+  constexpr int D = 64, d = D, GM = 4, kWarps = kAttnThreads / 32;
+  extern __shared__ float wts_s[];
+  __shared__ __align__(16) float qs[GM * D];
+  __shared__ __align__(16) float kp_s[D];
+  __shared__ __align__(16) float vp_s[D];
+  __shared__ __align__(16) float wo[kWarps * GM * D];
+  __shared__ __align__(16) float ofin[GM * D];
+  __shared__ float wm[kWarps * GM], wl[kWarps * GM];
+  __shared__ float m_s[16], l_s[16];
+  __shared__ bool last_s;
+  const int kvh = blockIdx.x, split = blockIdx.y, m = blockIdx.z;
+  const int half = d / 2, G = a.nq / a.nkv, kvd = a.nkv * d;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  if (tid == 0) trace_mark(a.trace, 0);
+  pdl_trigger();
+  pdl_wait();
+  if (tid == 0) {
+    trace_mark(a.trace, 1);
+    trace_mark(a.trace, 2);
+  }
+
+  const bool fixed = a.pos_override != nullptr;
+  const int pos = fixed ? a.pos_override[m] : a.st.pos[m];
+  const bool done = fixed ? true : (a.st.done[m] != 0);
+  const bool append = !done && pos < a.cap;
+  const int n_ctx = fixed ? pos + 1 : (append ? pos + 1 : pos);
+  const float* qkv = a.qkv + size_t(m) * a.qkv_ld;
+  float* kc = a.kc + size_t(m) * a.cap * kvd;
+  float* vc = a.vc + size_t(m) * a.cap * kvd;
+
+  // context range of this split: at least kMinChunk positions per split, so
+  // short contexts use few CTAs (the rest only take their ticket)
+  int chunk = (n_ctx + a.nsplit - 1) / a.nsplit;
+  chunk = max(kMinChunk, (chunk + kTile - 1) / kTile * kTile);
+  const int n_used = (n_ctx + chunk - 1) / chunk;
+  const int c0 = split * chunk;
+  const int c1 = min(n_ctx, c0 + chunk);
+  if (n_used == 1 && split > 0) {  // one-split launches need no ticket
+    if (tid == 0) trace_mark(a.trace, 3);
+    return;
+  }
+  const bool own_pos = append && pos >= c0 && pos < c1;
+
+  // q heads of this group rotated at pos (model.rs:422-426)
+  const int rp = pos < a.cap ? pos : 0;
+  for (int i = tid; i < G * half; i += blockDim.x) {
+    const int g = i / half, j = i % half;
+    const float* qh = qkv + (kvh * G + g) * d;
+    if (fixed) {
+      qs[g * d + j] = qh[j];
+      qs[g * d + j + half] = qh[j + half];
+    } else {
+      float o0, o1;
+      rot(qh[j], qh[j + half], a.rope_cos[size_t(rp) * half + j], a.rope_sin[size_t(rp) * half + j],
+          &o0, &o1);
+      qs[g * d + j] = o0;
+      qs[g * d + j + half] = o1;
+    }
+  }
+  // the CTA whose range holds pos appends the rotated k and raw v
+  // (KvCache::push, model.rs:432) and keeps them for its own row
+  if (own_pos) {
+    const float* kh = qkv + a.nq * d + kvh * d;
+    const float* vh = qkv + (a.nq + a.nkv) * d + kvh * d;
+    float* kdst = kc + size_t(pos) * kvd + kvh * d;
+    float* vdst = vc + size_t(pos) * kvd + kvh * d;
+    for (int j = tid; j < half; j += blockDim.x) {
+      float o0, o1;
+      rot(kh[j], kh[j + half], a.rope_cos[size_t(pos) * half + j],
+          a.rope_sin[size_t(pos) * half + j], &o0, &o1);
+      kdst[j] = o0;
+      kdst[j + half] = o1;
+      kp_s[j] = o0;
+      kp_s[j + half] = o1;
+    }
+    for (int j = tid; j < d; j += blockDim.x) {
+      const float v = vh[j];
+      vdst[j] = v;
+      vp_s[j] = v;
+    }
+  }
+  __syncthreads();
+
+  const int hw = lane >> 4, l16 = lane & 15;
+  float4 q4[GM], o4[GM];
+  float m_g[GM], l_g[GM];
+#pragma unroll
+  for (int g = 0; g < GM; ++g) {
+    q4[g] = g < G ? *reinterpret_cast<const float4*>(qs + g * d + 4 * l16) : make_float4(0.f, 0.f, 0.f, 0.f);
+    o4[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    m_g[g] = -INFINITY;
+    l_g[g] = 0.f;
+  }
+  const float* kcol = kc + kvh * d + 4 * l16;
+  const float* vcol = vc + kvh * d + 4 * l16;
+  // warp-uniform trip count: the warp's two streams take the blocks at
+  // wb and wb + kRegRows; rows past c1 are masked
+  for (int wb = c0 + warp * 2 * kRegRows; wb < c1; wb += kWarps * 2 * kRegRows) {
+    const int rb = wb + hw * kRegRows;
+    float4 kr[kRegRows], vr[kRegRows];
+#pragma unroll
+    for (int r = 0; r < kRegRows; ++r) {
+      const int t = rb + r;
+      if (t < c1) {
+        if (own_pos && t == pos) {
+          kr[r] = *reinterpret_cast<const float4*>(kp_s + 4 * l16);
+          vr[r] = *reinterpret_cast<const float4*>(vp_s + 4 * l16);
+        } else {
+          const uint4 ku = ld_stream(kcol + size_t(t) * kvd);
+          const uint4 vu = ld_stream(vcol + size_t(t) * kvd);
+          kr[r] = make_float4(__uint_as_float(ku.x), __uint_as_float(ku.y), __uint_as_float(ku.z),
+                              __uint_as_float(ku.w));
+          vr[r] = make_float4(__uint_as_float(vu.x), __uint_as_float(vu.y), __uint_as_float(vu.z),
+                              __uint_as_float(vu.w));
+        }
+      } else {
+        kr[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+        vr[r] = kr[r];
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+      if (g < G) {
+        float sc[kRegRows];
+        float mt = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < kRegRows; ++r) {
+          float acc = q4[g].x * kr[r].x;
+          acc = fmaf(q4[g].y, kr[r].y, acc);
+          acc = fmaf(q4[g].z, kr[r].z, acc);
+          acc = fmaf(q4[g].w, kr[r].w, acc);
+          acc += __shfl_xor_sync(0xffffffffu, acc, 8);
+          acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+          acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+          acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+          sc[r] = rb + r < c1 ? acc * a.scale : -INFINITY;
+          mt = fmaxf(mt, sc[r]);
+        }
+        const float mn = fmaxf(m_g[g], mt);
+        const float alpha = m_g[g] == -INFINITY ? 0.f : expf(m_g[g] - mn);
+        float4 o = make_float4(o4[g].x * alpha, o4[g].y * alpha, o4[g].z * alpha, o4[g].w * alpha);
+        float ls = l_g[g] * alpha;
+#pragma unroll
+        for (int r = 0; r < kRegRows; ++r) {
+          const float p = sc[r] == -INFINITY ? 0.f : expf(sc[r] - mn);
+          ls += p;
+          o.x = fmaf(p, vr[r].x, o.x);
+          o.y = fmaf(p, vr[r].y, o.y);
+          o.z = fmaf(p, vr[r].z, o.z);
+          o.w = fmaf(p, vr[r].w, o.w);
+        }
+        o4[g] = o;
+        l_g[g] = ls;
+        m_g[g] = mn;
+      }
+    }
+  }
+  // the warp's two streams meet (lanes l16 and l16 + 16), then the warps
+#pragma unroll
+  for (int g = 0; g < GM; ++g) {
+    if (g < G) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m_g[g], 16);
+      const float l2 = __shfl_xor_sync(0xffffffffu, l_g[g], 16);
+      float4 o2;
+      o2.x = __shfl_xor_sync(0xffffffffu, o4[g].x, 16);
+      o2.y = __shfl_xor_sync(0xffffffffu, o4[g].y, 16);
+      o2.z = __shfl_xor_sync(0xffffffffu, o4[g].z, 16);
+      o2.w = __shfl_xor_sync(0xffffffffu, o4[g].w, 16);
+      const float M = fmaxf(m_g[g], m2);
+      const float a1 = m_g[g] == -INFINITY ? 0.f : expf(m_g[g] - M);
+      const float a2 = m2 == -INFINITY ? 0.f : expf(m2 - M);
+      if (hw == 0) {
+        float4 o;
+        o.x = fmaf(o2.x, a2, o4[g].x * a1);
+        o.y = fmaf(o2.y, a2, o4[g].y * a1);
+        o.z = fmaf(o2.z, a2, o4[g].z * a1);
+        o.w = fmaf(o2.w, a2, o4[g].w * a1);
+        *reinterpret_cast<float4*>(wo + (warp * G + g) * d + 4 * l16) = o;
+        if (l16 == 0) {
+          wm[warp * GM + g] = M;
+          wl[warp * GM + g] = fmaf(l2, a2, l_g[g] * a1);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  // one thread per head: the CTA's (m, l); then o per (head, column)
+  if (tid < G) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, wm[w * GM + tid]);
+    float L = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float mw = wm[w * GM + tid];
+      L = fmaf(wl[w * GM + tid], mw == -INFINITY ? 0.f : expf(mw - M), L);
+    }
+    m_s[tid] = M;
+    l_s[tid] = L;
+  }
+  __syncthreads();
+  for (int idx = tid; idx < G * d; idx += kAttnThreads) {
+    const int g = idx / d;
+    const float M = m_s[g];
+    float O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float mw = wm[w * GM + g];
+      O = fmaf(wo[(w * G + g) * d + (idx % d)], mw == -INFINITY ? 0.f : expf(mw - M), O);
+    }
+    ofin[idx] = O;
+  }
+  __syncthreads();
+  float* out = a.out + size_t(m) * a.nq * d + kvh * G * d;
+  if (n_used == 1) {
+    // the whole context in one CTA: finish here, no partials
+    if (split == 0) {
+      for (int idx = tid; idx < G * d; idx += kAttnThreads) {
+        const float L = l_s[idx / d];
+        out[idx] = L > 0.f ? ofin[idx] / L : 0.f;
+      }
+    }
+    if (tid == 0) trace_mark(a.trace, 3);
+    return;  // one-split launches need no ticket
+  }
+  // partial (m, l, o[d]) per head
+  if (split < n_used) {
+    float* part = a.part + ((size_t(m) * a.nkv + kvh) * a.nsplit + split) * G * (d + 2);
+    for (int idx = tid; idx < G * d; idx += kAttnThreads)
+      part[(idx / d) * (d + 2) + 2 + (idx % d)] = ofin[idx];
+    if (tid < G) {
+      part[tid * (d + 2)] = m_s[tid];
+      part[tid * (d + 2) + 1] = l_s[tid];
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    const unsigned int t = atomicAdd(&a.ticket[m * a.nkv + kvh], 1u);
+    last_s = (t == gridDim.y - 1);
+  }
+  __syncthreads();
+  if (!last_s) {
+    if (tid == 0) trace_mark(a.trace, 3);
+    return;
+  }
+  __threadfence();
+  // combine: the per-split weights w = exp(m_s - max) once per (split, head)
+  // in shared memory, then every output sums its column over the splits
+  const float* pb = a.part + (size_t(m) * a.nkv + kvh) * a.nsplit * G * (d + 2);
+  float* wts = wts_s;  // [G][n_used]
+  for (int g = warp; g < G; g += kAttnThreads / 32) {
+    float mx = -INFINITY;
+    for (int s = lane; s < n_used; s += 32) mx = fmaxf(mx, __ldcg(pb + (s * G + g) * (d + 2)));
+    mx = warp_max(mx);
+    float L = 0.f;
+    for (int s = lane; s < n_used; s += 32) {
+      const float ms = __ldcg(pb + (s * G + g) * (d + 2));
+      const float w = ms == -INFINITY ? 0.f : expf(ms - mx);
+      wts[g * n_used + s] = w;
+      L = fmaf(__ldcg(pb + (s * G + g) * (d + 2) + 1), w, L);
+    }
+    L = warp_sum(L);
+    if (lane == 0) l_s[g] = L;
+  }
+  __syncthreads();
+  for (int idx = tid; idx < G * d; idx += blockDim.x) {
+    const int g = idx / d, j = idx % d;
+    float acc = 0.f;
+    int s = 0;
+    for (; s + 4 <= n_used; s += 4) {
+      const float o0 = __ldcg(pb + ((s + 0) * G + g) * (d + 2) + 2 + j);
+      const float o1 = __ldcg(pb + ((s + 1) * G + g) * (d + 2) + 2 + j);
+      const float o2 = __ldcg(pb + ((s + 2) * G + g) * (d + 2) + 2 + j);
+      const float o3 = __ldcg(pb + ((s + 3) * G + g) * (d + 2) + 2 + j);
+      acc = fmaf(o0, wts[g * n_used + s], acc);
+      acc = fmaf(o1, wts[g * n_used + s + 1], acc);
+      acc = fmaf(o2, wts[g * n_used + s + 2], acc);
+      acc = fmaf(o3, wts[g * n_used + s + 3], acc);
+    }
+    for (; s < n_used; ++s) acc = fmaf(__ldcg(pb + (s * G + g) * (d + 2) + 2 + j), wts[g * n_used + s], acc);
+    const float L = l_s[g];
+    out[idx] = L > 0.f ? acc / L : 0.f;
+  }
+  if (tid == 0) {
+    a.ticket[m * a.nkv + kvh] = 0u;
+    trace_mark(a.trace, 3);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Prefill causal attention.  Template on head_dim; DPT dims per thread,
 // TPR = D / DPT threads per query row.  Grid (n_q, ceil(T / rows_per_cta)).
 // ---------------------------------------------------------------------------
@@ -756,6 +1069,7 @@ cudaError_t attn_attr() {
 }
 
 cudaError_t attn_prepare() {
+  TMG_CUDA_TRY(set_carveout(attn_decode_reg_kernel));
   TMG_CUDA_TRY(set_carveout(attn_prefill_tiled_kernel<64>, int(attn_prefill_tiled_smem<64>())));
   TMG_CUDA_TRY(set_carveout(rope_append_kernel));
   TMG_CUDA_TRY(set_carveout(rope_rows_kernel));
@@ -768,6 +1082,25 @@ cudaError_t attn_prepare() {
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) {
   const int G = a.nq / a.nkv;
   if (G * a.nkv != a.nq || G * a.d > 8 * kAttnThreads || G > 16) return cudaErrorInvalidValue;
+  // head dim 64 with at most 4 heads per kv head: K/V streamed into registers
+  // (TMG_ATTN_TILED=1 keeps the shared-memory tiled kernel, for comparison)
+  static const bool tiled_only = [] {
+    const char* e = getenv("TMG_ATTN_TILED");
+    return e && e[0] == '1';
+  }();
+  if (a.d == 64 && G <= 4 && !tiled_only) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.nkv, a.nsplit, a.M);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = sizeof(float) * std::max<size_t>(4, size_t(G) * a.nsplit);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, attn_decode_reg_kernel, a);
+  }
   void (*kern)(const AttnDecodeArgs) = nullptr;
   const bool g4 = G <= 4;
   switch (a.d) {
