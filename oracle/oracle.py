@@ -56,6 +56,7 @@ _U16 = ctypes.POINTER(ctypes.c_uint16)
 _U32 = ctypes.POINTER(ctypes.c_uint32)
 _I64 = ctypes.c_int64
 _P = ctypes.c_void_p
+_I8 = ctypes.POINTER(ctypes.c_int8)
 
 
 def lib() -> ctypes.CDLL:
@@ -71,6 +72,12 @@ def lib() -> ctypes.CDLL:
             "orc_matmul_w_bf16": (None, [_F, _U16, _I64, _I64, _F]),
             "orc_matmul_w_f32": (None, [_F, _F, _I64, _I64, _F]),
             "orc_matmul_batch_w_bf16": (None, [_F, _U16, _I64, _I64, _I64, _F]),
+            "orc_quantize_i8": (None, [_F, _I64, _I64, _I8, _F]),
+            "orc_quantize_row_i8": (ctypes.c_float, [_F, _I64, _I8]),
+            "orc_dot_i8": (ctypes.c_int32, [_I8, _I8, _I64]),
+            "orc_matmul_w_i8": (None, [_F, _I8, _F, _I64, _I64, _F]),
+            "orc_matmul_batch_w_i8": (None, [_F, _I8, _F, _I64, _I64, _I64, _F]),
+            "orc_model_set_i8": (None, [_P, ctypes.c_int]),
             "orc_rms_norm_into": (None, [_F, _F, ctypes.c_float, _I64, _F]),
             "orc_rms_norm_batch": (None, [_F, _F, ctypes.c_float, _I64, _I64]),
             "orc_rope_rotate": (None, [_F, _I64, _I64, ctypes.c_float]),
@@ -132,6 +139,55 @@ def set_num_threads(n: int) -> None:
 
 def num_threads() -> int:
     return int(lib().orc_num_threads())
+
+
+def _i8(a: np.ndarray):
+    assert a.dtype == np.int8 and a.flags.c_contiguous
+    return a.ctypes.data_as(_I8)
+
+
+def quantize_i8(w: np.ndarray):
+    """WMat::quantize_i8 (src/tensor.rs:282-297) of an f32 [out, in] matrix:
+    (int8 rows, per-row f32 scales)."""
+    w = np.ascontiguousarray(w, np.float32)
+    out, inn = w.shape
+    q = np.zeros((out, inn), np.int8)
+    sc = np.zeros(out, np.float32)
+    lib().orc_quantize_i8(_f(w), out, inn, _i8(q), _f(sc))
+    return q, sc
+
+
+def quantize_row_i8(x: np.ndarray):
+    """quantize_row_i8 (src/tensor.rs:128-141): (int8 values, scale)."""
+    x = np.ascontiguousarray(x, np.float32)
+    q = np.zeros(x.size, np.int8)
+    s = lib().orc_quantize_row_i8(_f(x), x.size, _i8(q))
+    return q, np.float32(s)
+
+
+def dot_i8(a: np.ndarray, b: np.ndarray) -> int:
+    return int(lib().orc_dot_i8(_i8(np.ascontiguousarray(a, np.int8)),
+                                _i8(np.ascontiguousarray(b, np.int8)), a.size))
+
+
+def matmul_w_i8(x: np.ndarray, q: np.ndarray, scales: np.ndarray) -> np.ndarray:
+    """The decode GEMV of an I8 matrix (src/tensor.rs:341-357)."""
+    out, inn = q.shape
+    y = np.zeros(out, np.float32)
+    lib().orc_matmul_w_i8(_f(np.ascontiguousarray(x, np.float32)), _i8(np.ascontiguousarray(q)),
+                          _f(np.ascontiguousarray(scales, np.float32)), out, inn, _f(y))
+    return y
+
+
+def matmul_batch_w_i8(x: np.ndarray, q: np.ndarray, scales: np.ndarray) -> np.ndarray:
+    """The prefill GEMM of an I8 matrix (src/tensor.rs:573-592, 799-858)."""
+    out, inn = q.shape
+    T = x.shape[0]
+    y = np.zeros((T, out), np.float32)
+    lib().orc_matmul_batch_w_i8(_f(np.ascontiguousarray(x, np.float32)),
+                                _i8(np.ascontiguousarray(q)),
+                                _f(np.ascontiguousarray(scales, np.float32)), out, inn, T, _f(y))
+    return y
 
 
 def matmul_w(x: np.ndarray, w: np.ndarray) -> np.ndarray:
@@ -252,12 +308,15 @@ class OracleModel:
     Matrices are borrowed: the arrays are kept alive by this object.
     """
 
-    def __init__(self, cfg: dict, tensors: dict):
+    def __init__(self, cfg: dict, tensors: dict, i8: bool = False):
+        """i8: the reference's TMG_I8=1 (layer matrices quantized at load,
+        src/model.rs:57-76; the LM head and norms keep their precision)."""
         self.cfg = cfg
         c = OrcConfig(cfg["hidden_size"], cfg["num_hidden_layers"], cfg["num_attention_heads"],
                       cfg["num_key_value_heads"], cfg["head_dim"], cfg["intermediate_size"],
                       cfg["vocab_size"], cfg["rms_norm_eps"], cfg["rope_theta"])
         self._h = lib().orc_model_new(ctypes.byref(c))
+        lib().orc_model_set_i8(self._h, 1 if i8 else 0)
         self._keep = []
         # the embedding first, so a dedicated lm_head (if any) overrides the tie
         names = sorted(tensors, key=lambda n: (n != "model.embed_tokens.weight", n))

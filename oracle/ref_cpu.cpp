@@ -38,6 +38,7 @@
 #include <string>
 #include <unordered_set>
 #include <chrono>
+#include <deque>
 
 namespace orc {
 
@@ -98,11 +99,69 @@ static float dot_bf16(const float* a, const uint16_t* b, size_t n) {
 struct WMat {
   const uint16_t* bf16 = nullptr;
   const float* f32 = nullptr;
+  const int8_t* i8 = nullptr;     // WMat::I8: quantized rows ...
+  const float* scale = nullptr;   // ... and their per-row scales
 };
 
+// w_row_scale, src/tensor.rs:887-893: 1 except for I8 rows.
+static inline float w_row_scale(const WMat& w, size_t o) { return w.i8 ? w.scale[o] : 1.0f; }
+
+// dot_w_row_avx2, src/tensor.rs:860-884 (the I8 arm is the scalar
+// dequant-accumulate: sum x * q in order, then one multiply by the scale).
 static inline float dot_w_row(const float* x, const WMat& w, size_t in, size_t o) {
+  if (w.i8) {
+    float acc = 0.0f;
+    const int8_t* q = w.i8 + o * in;
+    for (size_t k = 0; k < in; ++k) acc += x[k] * float(q[k]);
+    return acc * w.scale[o];
+  }
   if (w.bf16) return dot_bf16(x, w.bf16 + o * in, in);
   return dot_f32(x, w.f32 + o * in, in);
+}
+
+// ---------------------------------------------------------------------------
+// Int8 weights (TMG_I8=1), src/tensor.rs:128-170 and 282-297.
+// ---------------------------------------------------------------------------
+// f32::round: halves away from zero (roundf); clamp to +-127 before the cast.
+static inline int8_t q8(float v) {
+  float r = std::round(v);
+  r = r < -127.0f ? -127.0f : (r > 127.0f ? 127.0f : r);
+  return int8_t(r);
+}
+
+// WMat::quantize_i8, src/tensor.rs:282-297: per row scale = max|w| / 127
+// (1 for an all-zero row), q = round(w / scale).
+static void quantize_i8(const float* w, size_t out, size_t in, int8_t* q, float* scales) {
+  for (size_t o = 0; o < out; ++o) {
+    const float* row = w + o * in;
+    float maxabs = 0.0f;
+    for (size_t k = 0; k < in; ++k) maxabs = std::fmax(std::fabs(row[k]), maxabs);
+    const float sc = maxabs > 0.0f ? maxabs / 127.0f : 1.0f;
+    scales[o] = sc;
+    for (size_t k = 0; k < in; ++k) q[o * in + k] = q8(row[k] / sc);
+  }
+}
+
+// quantize_row_i8, src/tensor.rs:128-141: the activation's scale and
+// q = round(x * (1 / s)); an all-zero row gives scale 0.
+static float quantize_row_i8(const float* x, size_t n, int8_t* q) {
+  float maxabs = 0.0f;
+  for (size_t i = 0; i < n; ++i) maxabs = std::fmax(std::fabs(x[i]), maxabs);
+  if (maxabs == 0.0f) {
+    std::memset(q, 0, n);
+    return 0.0f;
+  }
+  const float s = maxabs / 127.0f;
+  const float inv = 1.0f / s;
+  for (size_t i = 0; i < n; ++i) q[i] = q8(x[i] * inv);
+  return s;
+}
+
+// dot_i8, src/tensor.rs:146-170: exact in i32 (the order does not matter).
+static int32_t dot_i8(const int8_t* a, const int8_t* b, size_t n) {
+  int32_t sum = 0;
+  for (size_t i = 0; i < n; ++i) sum += int32_t(a[i]) * int32_t(b[i]);
+  return sum;
 }
 
 // Thread policy, src/tensor.rs:172-191: TMG_THREADS (0 = all cores); gemv
@@ -117,6 +176,13 @@ static const size_t kMinRowsForThreads = 64;
 
 // matmul_w_into, src/tensor.rs:331-460 (BF16 / F32 arms).
 static void matmul_w_into(const float* x, const WMat& w, size_t out, size_t in, float* y) {
+  if (w.i8) {  // src/tensor.rs:341-357: the activation quantized once, integer dots
+    std::vector<int8_t> xq(in);
+    const float xs = quantize_row_i8(x, in, xq.data());
+    for (size_t o = 0; o < out; ++o)
+      y[o] = float(dot_i8(xq.data(), w.i8 + o * in, in)) * xs * w.scale[o];
+    return;
+  }
   size_t nth = std::min(std::max<size_t>(1, num_threads() / 4), out);
   if (nth <= 1 || out < kMinRowsForThreads) {
     for (size_t o = 0; o < out; ++o) y[o] = dot_w_row(x, w, in, o);
@@ -148,7 +214,12 @@ static void gemm_tile(const float* x, const WMat& w, size_t out, size_t in, size
       for (size_t k = 0; k < kchunks; ++k) {
         size_t ki = k * 8;
         __m256 w0, w1;
-        if (w.bf16) {
+        if (w.i8) {  // load_w_m256, src/tensor.rs:928-933: i8 -> i32 -> f32
+          w0 = _mm256_cvtepi32_ps(_mm256_cvtepi8_epi32(
+              _mm_loadl_epi64(reinterpret_cast<const __m128i*>(w.i8 + o * in + ki))));
+          w1 = _mm256_cvtepi32_ps(_mm256_cvtepi8_epi32(
+              _mm_loadl_epi64(reinterpret_cast<const __m128i*>(w.i8 + (o + 1) * in + ki))));
+        } else if (w.bf16) {
           w0 = widen8(w.bf16 + o * in + ki);
           w1 = widen8(w.bf16 + (o + 1) * in + ki);
         } else {
@@ -166,13 +237,21 @@ static void gemm_tile(const float* x, const WMat& w, size_t out, size_t in, size
         float s1 = lane_sum(acc[ti][1]);
         for (size_t k = kchunks * 8; k < kchunks * 8 + ktail; ++k) {
           float xk = x[(tb + ti) * in + k];
-          float a = w.bf16 ? bf16_to_f32(w.bf16[o * in + k]) : w.f32[o * in + k];
-          float b = w.bf16 ? bf16_to_f32(w.bf16[(o + 1) * in + k]) : w.f32[(o + 1) * in + k];
+          // wf_elem, src/tensor.rs:937-942: an I8 tail element is q * scale,
+          // and the row scale below multiplies it once more (as there)
+          float a, b;
+          if (w.i8) {
+            a = float(w.i8[o * in + k]) * w.scale[o];
+            b = float(w.i8[(o + 1) * in + k]) * w.scale[o + 1];
+          } else {
+            a = w.bf16 ? bf16_to_f32(w.bf16[o * in + k]) : w.f32[o * in + k];
+            b = w.bf16 ? bf16_to_f32(w.bf16[(o + 1) * in + k]) : w.f32[(o + 1) * in + k];
+          }
           s0 += xk * a;
           s1 += xk * b;
         }
-        y[(tb + ti) * out + o] = s0;
-        y[(tb + ti) * out + o + 1] = s1;
+        y[(tb + ti) * out + o] = s0 * w_row_scale(w, o);
+        y[(tb + ti) * out + o + 1] = s1 * w_row_scale(w, o + 1);
       }
     }
     for (size_t t = tblock; t < T; ++t) {
@@ -516,6 +595,11 @@ struct Model {
   std::vector<Layer> layers;
   std::vector<float> final_norm;
   WMat lm_head;  // BF16 when lm_head.weight exists, else F32 = embed (model.rs:230-233)
+  // TMG_I8=1 (wmat_maybe_i8, src/model.rs:57-76): layer matrices quantized at
+  // load and owned here; the LM head and the norms keep their precision
+  bool i8_mode = false;
+  std::deque<std::vector<int8_t>> q_store;
+  std::deque<std::vector<float>> s_store;
   Rope rope;
   // decode scratch, model.rs:348-381
   std::vector<float> x, attn_in, q_all, k_all, v_all, attn_out, proj, mlp_in, gate, up, down;
@@ -662,6 +746,21 @@ void orc_matmul_batch_w_bf16(const float* x, const uint16_t* w, int64_t out, int
                              int64_t T, float* y) {
   WMat m; m.bf16 = w; matmul_batch_w_into(x, m, out, in, T, y);
 }
+void orc_quantize_i8(const float* w, int64_t out, int64_t in, int8_t* q, float* scales) {
+  quantize_i8(w, out, in, q, scales);
+}
+float orc_quantize_row_i8(const float* x, int64_t n, int8_t* q) { return quantize_row_i8(x, n, q); }
+int32_t orc_dot_i8(const int8_t* a, const int8_t* b, int64_t n) { return dot_i8(a, b, n); }
+void orc_matmul_w_i8(const float* x, const int8_t* q, const float* scales, int64_t out, int64_t in,
+                     float* y) {
+  WMat m; m.i8 = q; m.scale = scales; matmul_w_into(x, m, out, in, y);
+}
+void orc_matmul_batch_w_i8(const float* x, const int8_t* q, const float* scales, int64_t out,
+                           int64_t in, int64_t T, float* y) {
+  WMat m; m.i8 = q; m.scale = scales; matmul_batch_w_into(x, m, out, in, T, y);
+}
+// Quantize layer matrices set after this call (TMG_I8=1).
+void orc_model_set_i8(void* mp, int on) { static_cast<Model*>(mp)->i8_mode = on != 0; }
 void orc_rms_norm_into(const float* x, const float* w, float eps, int64_t n, float* out) {
   rms_norm_into(x, w, eps, n, out);
 }
@@ -754,6 +853,27 @@ int orc_model_set(void* mp, const char* name, const void* data, int dtype, int64
     }
     return 0;
   }
+  // a layer matrix: borrowed as is, or (I8 mode) widened to f32 and quantized
+  auto as_layer_w = [&](WMat& w, size_t rows) {
+    if (!m->i8_mode) {
+      as_w(w);
+      return;
+    }
+    std::vector<float> f(n);
+    if (dtype == 1) {
+      const uint16_t* b = static_cast<const uint16_t*>(data);
+      for (int64_t i = 0; i < n; ++i) f[i] = bf16_to_f32(b[i]);
+    } else {
+      std::memcpy(f.data(), data, n * sizeof(float));
+    }
+    const size_t cols = size_t(n) / rows;
+    m->q_store.emplace_back(size_t(n));
+    m->s_store.emplace_back(rows);
+    quantize_i8(f.data(), rows, cols, m->q_store.back().data(), m->s_store.back().data());
+    w = WMat();
+    w.i8 = m->q_store.back().data();
+    w.scale = m->s_store.back().data();
+  };
   if (s == "model.norm.weight") { as_vec(m->final_norm); return 0; }
   if (s == "lm_head.weight") { as_w(m->lm_head); return 0; }
   const std::string pre = "model.layers.";
@@ -763,13 +883,16 @@ int orc_model_set(void* mp, const char* name, const void* data, int dtype, int64
   if (li < 0 || li >= m->c.num_hidden_layers) return -2;
   std::string suf = s.substr(dot + 1);
   Layer& L = m->layers[li];
-  if (suf == "self_attn.q_proj.weight") as_w(L.wq);
-  else if (suf == "self_attn.k_proj.weight") as_w(L.wk);
-  else if (suf == "self_attn.v_proj.weight") as_w(L.wv);
-  else if (suf == "self_attn.o_proj.weight") as_w(L.wo);
-  else if (suf == "mlp.gate_proj.weight") as_w(L.w_gate);
-  else if (suf == "mlp.up_proj.weight") as_w(L.w_up);
-  else if (suf == "mlp.down_proj.weight") as_w(L.w_down);
+  const size_t h = m->c.hidden_size, I = m->c.intermediate_size;
+  const size_t qd = size_t(m->c.num_attention_heads) * m->c.head_dim;
+  const size_t kd = size_t(m->c.num_key_value_heads) * m->c.head_dim;
+  if (suf == "self_attn.q_proj.weight") as_layer_w(L.wq, qd);
+  else if (suf == "self_attn.k_proj.weight") as_layer_w(L.wk, kd);
+  else if (suf == "self_attn.v_proj.weight") as_layer_w(L.wv, kd);
+  else if (suf == "self_attn.o_proj.weight") as_layer_w(L.wo, h);
+  else if (suf == "mlp.gate_proj.weight") as_layer_w(L.w_gate, I);
+  else if (suf == "mlp.up_proj.weight") as_layer_w(L.w_up, I);
+  else if (suf == "mlp.down_proj.weight") as_layer_w(L.w_down, h);
   else if (suf == "input_layernorm.weight") as_vec(L.in_norm);
   else if (suf == "post_attention_layernorm.weight") as_vec(L.post_norm);
   else return -3;
