@@ -2,7 +2,7 @@
 """Benchmark of the B200 token loop (HanzCEO/TinyMiniGo's decode path).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c2|c4]
+                    [--workload c2|c3|c4|c5|attn]
 
 Workload c2 (default): the 1B-class Llama decoder
 (hidden 2048, 16 layers, 32/8 heads, head_dim 64, intermediate 8192, vocab
@@ -648,6 +648,86 @@ def run_c5(args, rank, world, local_rank):
     model.close()
 
 
+def run_attn(args, rank, world, local_rank):
+    """Attention kernels alone, through the op-level C ABI (rank 0): decode
+    attention of one stream over 131072 cached positions (32 query / 8 kv
+    heads, head dim 64: 537 MB of f32 K/V, larger than L2, flushed between
+    runs) and causal prefill attention of 2048 rows (the c3 shape).  value =
+    the decode kernel's algorithmic GB/s (K and V read once); the prefill's
+    TFLOP/s rides along.  TMG_ATTN_TILED=1 selects the shared-memory tiled
+    decode kernel instead of the register-streaming one."""
+    import ctypes
+
+    import torch
+
+    if rank != 0:
+        return
+    torch.cuda.set_device(local_rank)
+    from tinyminigo_b200._lib import check, lib
+
+    h = ctypes.c_void_p()
+    check(lib().tmg_create(local_rank, None, ctypes.byref(h)))
+    stream = torch.cuda.ExternalStream(lib().tmg_stream(h), device=local_rank)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(1)
+    nq, nkv, d = 32, 8, 64
+
+    def timed(call):
+        for _ in range(args.warmup):
+            call()
+        ts = []
+        for _ in range(args.steps):
+            flush.zero_()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            call()
+            e1.record(stream)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+
+    n_ctx = 131072
+    q = torch.randn(nq * d, device="cuda", generator=g)
+    k = torch.randn(n_ctx, nkv * d, device="cuda", generator=g)
+    v = torch.randn(n_ctx, nkv * d, device="cuda", generator=g)
+    o = torch.zeros(nq * d, device="cuda")
+    with ClockSampler(local_rank) as clk:
+        ms_dec = timed(lambda: check(lib().tmg_op_attn_decode(h, P(q), P(k), P(v), n_ctx, nq, nkv,
+                                                              d, P(o)), h))
+        T = 2048
+        qp = torch.randn(T, nq * d, device="cuda", generator=g)
+        kp = torch.randn(T, nkv * d, device="cuda", generator=g)
+        vp = torch.randn(T, nkv * d, device="cuda", generator=g)
+        op = torch.zeros(T, nq * d, device="cuda")
+        ms_pf = timed(lambda: check(lib().tmg_op_attn_prefill(h, P(qp), P(kp), P(vp), T, 0, nq,
+                                                              nkv, d, P(op)), h))
+    lib().tmg_destroy(h)
+    dec_bytes = 2 * n_ctx * nkv * d * 4
+    gbs = dec_bytes / (ms_dec / 1e3) / 1e9
+    pf_flop = 4 * d * nq * T * (T + 1) // 2
+    peak, peak_kind = peaks()
+    tiled = os.environ.get("TMG_ATTN_TILED", "0") == "1"
+    res = base_line(args, world, "decode_attention_gbs", gbs, "GB/s", ms_dec,
+                    {"workload": "attention kernels: decode over 131072 positions (32/8 heads, "
+                                 "d 64, one stream); causal prefill of 2048 rows",
+                     "global_batch": 1, "seq_len": n_ctx, "parallelism": "single GPU",
+                     "l2": "flushed between runs (256 MB write)"}, "weak", clk.summary(),
+                    roofline={"bound": "hbm", "kernel": "attn_decode_kernel" if tiled
+                              else "attn_decode_reg_kernel", "achieved": round(gbs, 1),
+                              "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4),
+                              "traffic": None, "peak_kind": peak_kind},
+                    prefill_attention={"ms": round(ms_pf, 3),
+                                       "tflops": round(pf_flop / (ms_pf / 1e3) / 1e12, 1),
+                                       "kernel": "attn_prefill_tiled_kernel<64>"},
+                    timing="CUDA events around the op call (includes its ticket memset and "
+                           "position upload for decode)")
+    res["dtype"] = "f32"
+    res["data"] = "synthetic (random normal q, K, V)"
+    print(json.dumps(res), flush=True)
+
+
 def c3_cpu_leg(model, cfg, w, prompt, n=256):
     """The C3 host leg: the oracle prefills the first n prompt tokens (timed,
     reference thread policy: GEMM on every core, attention single-threaded);
@@ -761,10 +841,10 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5"], default="c2",
+    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "attn"], default="c2",
                     help="c2 (default): the headline decode; c3: 2048-token prefill; "
                          "c4: 8B tensor-parallel decode over the ranks; c5: 16 streams at 32K "
-                         "context, sampled")
+                         "context, sampled; attn: the attention kernels alone")
     ap.add_argument("--cpu-tokens", type=int, default=8)
     ap.add_argument("--c5-ctx", type=int, default=32768, help="c5: prompt length per stream")
     ap.add_argument("--c5-steps", type=int, default=256, help="c5: sampled steps")
@@ -791,6 +871,8 @@ def main():
         run_c4(args, rank, world, local_rank)
     elif args.workload == "c5":
         run_c5(args, rank, world, local_rank)
+    elif args.workload == "attn":
+        run_attn(args, rank, world, local_rank)
     else:
         run_ours(args, rank, world, local_rank)
 
