@@ -121,3 +121,45 @@ def test_writer_needs_bf16_matrices(tmp_path, c1w):
     t = {k: v for k, v in c1w.items() if k != "model.norm.weight"}
     with pytest.raises(KeyError):
         tmb.write(tmp_path / "y.tmb", C1, t)
+
+
+def test_repack_widens_f16_and_f32_norms(tmp_path, c1w):
+    # norm vectors may be F16 or F32 in the checkpoint; the repack stores f32
+    # (push_f32, src/tmb.rs:143-154; F16 widened as src/safetensors_loader.rs:149-173)
+    import json as _json
+    import struct as _struct
+
+    from tinyminigo_b200.model import f16_to_f32
+
+    t = dict(c1w)
+    n16 = np.array([1.0, -2.5, 0.0001, 65504.0] * 16, np.float16)
+    n32 = np.linspace(-1, 1, 64).astype(np.float32)
+    src = synth.write_model(tmp_path / "m", C1, {k: v for k, v in t.items()
+                                                 if k not in ("model.norm.weight",
+                                                              "model.layers.0.input_layernorm.weight")})
+    # rewrite the file with an F16 final norm and an F32 input norm
+    header = {}
+    blobs, off = [], 0
+    items = dict(t)
+    items["model.norm.weight"] = n16
+    items["model.layers.0.input_layernorm.weight"] = n32
+    for name, a in items.items():
+        a = np.ascontiguousarray(a)
+        dt = {np.dtype(np.uint16): "BF16", np.dtype(np.float16): "F16",
+              np.dtype(np.float32): "F32"}[a.dtype]
+        header[name] = {"dtype": dt, "shape": list(a.shape), "data_offsets": [off, off + a.nbytes]}
+        blobs.append(a.tobytes())
+        off += a.nbytes
+    hb = _json.dumps(header).encode()
+    hb += b" " * ((8 - len(hb) % 8) % 8)
+    src.write_bytes(_struct.pack("<Q", len(hb)) + hb + b"".join(blobs))
+    out = tmp_path / "n.tmb"
+    tmb.repack(src, out)
+    raw = out.read_bytes()
+    _, idx = tmb.index(out)
+    at = {n: (o, nb) for n, o, nb in idx}
+    o, nb = at["model.norm.weight"]
+    got = np.frombuffer(raw, np.float32, 64, o)
+    assert np.array_equal(got, np.float32([f16_to_f32(int(h)) for h in n16.view(np.uint16)]))
+    o, nb = at["model.layers.0.input_layernorm.weight"]
+    assert np.array_equal(np.frombuffer(raw, np.float32, 64, o), n32)
