@@ -6,9 +6,9 @@
 //  * a serving loop that hands out its whole device-memory budget at
 //    start-up and must not grow afterwards (an allocation there can fail or
 //    push a neighbour out of memory);
-//  * code enqueued while a stream is being captured into a CUDA graph
-//    (cudaMalloc and cudaFree are not stream operations: they synchronize
-//    the device, which capture does not allow);
+//  * an engine that owns the GPU's memory through its own pool or arena and
+//    forbids allocations behind its back (device memory it did not hand
+//    out is memory it cannot account for);
 //  * a latency-bound path that cannot afford the device-wide
 //    synchronization an allocation or free implies.
 // This variant takes its split-KV partials, the per-head tickets and the
