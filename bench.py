@@ -24,10 +24,21 @@ ncu capture of the same kernel on a smaller case, scaled per algorithmic
 byte (profiles/decode_fused_c2.json).
 
 With --gpus N > 1 every rank runs an independent replica of c2 (the 1B
-config fits one GPU; "replicas only", weak scaling).
+config fits one GPU; "replicas only", weak scaling): `value` is c2's
+whole-job throughput at every N.  The same line carries a `c4_tp` block: the
+8B-class config sharded tensor-parallel over the
+same N ranks in the same process group (q/k/v and gate/up split by heads and
+rows, o/down by input columns with one NCCL allreduce per sublayer, the LM
+head by vocabulary rows), 128-token prompt, greedy 512 per step: decode
+tok/s of the one sequence (strong scaling), per-GPU algorithmic GB/s and
+its fraction of the HBM peak, and the allreduce time per token from a
+profiling pass.  At N = 1 the block is c4 on one GPU.  NCCL logs its
+communicator set-up (NCCL_DEBUG=INFO, subsystem INIT) on stderr.
 
 --impl reference times the reference's CPU algorithm (the C++ restatement in
-oracle/, with the reference's thread policy) on the host cores, rank 0 only.
+oracle/, with the reference's thread policy) on the host cores, rank 0 only,
+for the same workload (c2); each step is a bounded sample of its decode loop
+(stated in cpu_baseline.sample).
 """
 from __future__ import annotations
 
@@ -131,8 +142,11 @@ def dist_init(world: int, local_rank: int, backend: str = "nccl"):
     import torch
     import torch.distributed as dist
 
-    # rank 0 prints exactly one JSON line on stdout: keep NCCL's banner off it
-    os.environ["NCCL_DEBUG"] = os.environ.get("TMG_BENCH_NCCL_DEBUG", "WARN")
+    # rank 0 prints exactly one JSON line on stdout: NCCL's log (the
+    # communicators it sets up, with their rank counts) goes to stderr
+    os.environ["NCCL_DEBUG"] = os.environ.get("TMG_BENCH_NCCL_DEBUG", "INFO")
+    os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     kw = {"device_id": torch.device("cuda", local_rank)} if backend == "nccl" else {}
     dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120), **kw)
     return dist
@@ -168,14 +182,28 @@ def cpu_decode_sample(cfg, tensors, prompt, n_tokens):
     t0 = time.perf_counter()
     logits = om.forward_seq(prompt)
     t_pre = time.perf_counter() - t0
-    tok = int(np.argmax(logits))
+    first = logits.copy()
+    tok = oracle.argmax(logits)
+    ids = [tok]
     t0 = time.perf_counter()
     for _ in range(n_tokens):
         logits = om.forward_token(tok)
         tok = oracle.argmax(logits)
+        ids.append(tok)
     t_dec = time.perf_counter() - t0
     return {"decode_tok_s": n_tokens / t_dec, "prefill_tok_s": len(prompt) / t_pre,
-            "cores": oracle.num_threads(), "decode_s": t_dec, "prefill_s": t_pre}
+            "cores": oracle.num_threads(), "decode_s": t_dec, "prefill_s": t_pre,
+            "ids": ids, "first_logits": first}
+
+
+C2_WORKLOAD = "c2: 1B-class Llama, tied, 64-token prompt, greedy 256 decode"
+
+
+def c2_config(world: int) -> dict:
+    """The `config` of a c2 line (both arms print the same one)."""
+    return {"workload": C2_WORKLOAD, "global_batch": world, "seq_len": PROMPT + GEN,
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+            "l2": "inputs larger than L2 (2.47 GB of weights per token)"}
 
 
 def make_c2(device: str, layers: int = 0):
@@ -214,15 +242,15 @@ def run_reference(args, rank):
             tok = oracle.argmax(om.forward_token(tok))
     dt = time.perf_counter() - t0
     v = args.steps * per_step / dt
-    sample = (f"c2 greedy decode, {per_step} tokens per step from a {PROMPT}-token prefill, "
-              f"reference thread policy (gemv nproc/4, gemm nproc)")
+    sample = (f"each step: {per_step} greedy decode tokens of the 256-token loop, after a "
+              f"{PROMPT}-token prefill; reference thread policy (gemv nproc/4, gemm nproc)")
     out = {
         "impl": "reference", "metric": "decode_tok_s", "value": round(v, 4), "unit": "tok/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dt * 1e3 / args.steps, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "c2: 1B-class, tied, 64-token prompt, greedy 256",
-                   "global_batch": 1, "seq_len": PROMPT + GEN},
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16 weights)",
+        "data": "synthetic (seeded N(0,0.02^2) bf16 weights, random prompt)",
+        "config": c2_config(args.gpus),
         "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": oracle.num_threads(),
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
@@ -361,13 +389,40 @@ def run_ours(args, rank, world, local_rank):
     e2e = statistics.median(e2e_vals) * world
     ok = out.tokens[1:] == [int(t) for t in dec_toks[:GEN - 1]] and out.tokens[0] == t0_tok
 
-    # --- CPU baseline (rank 0, N = 1) ---
+    # --- CPU baseline and oracle parity (rank 0, N = 1) ---
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             cpu = cpu_decode_sample(cfg, w, prompt, args.cpu_tokens)
         except Exception as e:  # pragma: no cover
             log("cpu baseline failed:", e)
+    parity = None
+    if cpu:
+        gpu_ids = [t0_tok] + [int(t) for t in dec_toks[:args.cpu_tokens]]
+        diff = np.abs(logits - cpu["first_logits"])
+        parity = {"checker": "oracle (C++ restatement of the reference's CPU path)",
+                  "first_step_max_abs_logit_diff": round(float(diff.max()), 6),
+                  "first_step_logits_within_1e-3_rel_1e-2_abs":
+                      bool(np.all(diff <= 1e-2 + 1e-3 * np.abs(cpu["first_logits"]))),
+                  "greedy_ids_compared": len(gpu_ids),
+                  "greedy_ids_equal": gpu_ids == cpu["ids"]}
+    cache.close()
+    model.close()
+
+    # --- the tensor-parallel 8B block over the same ranks ---
+    c4 = None
+    if not args.no_c4:
+        v4, ms4, gbs4, per_gpu4, extra4 = measure_c4(
+            args, rank, world, local_rank, dist, steps=min(args.steps, 3), warmup=3,
+            host_leg=world == 1 and not args.no_cpu_baseline)
+        peak4, _ = peaks()
+        c4 = {"workload": "c4: 8B-class Llama, untied, 128-token prompt, greedy 512 decode",
+              "parallelism": f"tp{world}" if world > 1 else "single GPU", "n_gpus": world,
+              "scaling": "strong", "steps": min(args.steps, 3), "warmup": 3,
+              "decode_tok_s": round(v4, 2), "ms_per_step": round(ms4, 3),
+              "per_gpu_algorithmic_gbs": round(gbs4, 1), "peak": peak4,
+              "frac": round(gbs4 / peak4, 4), "algorithmic_bytes_per_token_per_gpu": int(per_gpu4),
+              **extra4}
 
     if rank == 0:
         clocks = clk.summary()
@@ -377,10 +432,7 @@ def run_ours(args, rank, world, local_rank):
             "ms_per_step": round(elapsed_ms / args.steps, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16 weights)",
             "data": "synthetic (seeded N(0,0.02^2) bf16 weights, random prompt)",
-            "config": {"workload": "c2: 1B-class Llama, tied, 64-token prompt, greedy 256 decode",
-                       "global_batch": world, "seq_len": PROMPT + GEN,
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                       "l2": "inputs larger than L2 (2.47 GB of weights per token)"},
+            "config": c2_config(world),
             "decode_hbm_gbs": round(step_gbs, 1),
             "decode_hbm_frac": round(step_gbs / peak, 4),
             "prefill_tok_s": round(PROMPT / (prefill_ms / 1e3), 1),
@@ -395,6 +447,10 @@ def run_ours(args, rank, world, local_rank):
             "gpu_launches": args.steps,  # one decode_fused_kernel launch per step
             "greedy_consistent": bool(ok),
         }
+        if parity:
+            res["parity"] = parity
+        if c4:
+            res["c4_tp"] = c4
         if cpu:
             res["cpu_baseline"] = {
                 "value": round(cpu["decode_tok_s"], 4), "unit": "tok/s", "cores": cpu["cores"],
@@ -405,8 +461,6 @@ def run_ours(args, rank, world, local_rank):
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
-    cache.close()
-    model.close()
 
 
 def model_config(cfg):
@@ -498,26 +552,23 @@ def run_c3(args, rank, world, local_rank):
     model.close()
 
 
-def run_c4(args, rank, world, local_rank):
-    """C4: the 8B-class config sharded tensor-parallel over the ranks (one
-    process per GPU, NCCL allreduce per sublayer); 128-token prompt, then a
-    512-token greedy decode per step from the rewound cache.  value = decode
-    tok/s of the one sequence (strong scaling), max over ranks."""
+def measure_c4(args, rank, world, local_rank, dist, steps, warmup, host_leg):
+    """C4: the 8B-class config sharded tensor-parallel over the ranks of
+    `dist` (one process per GPU, NCCL allreduce per sublayer; world 1: one
+    GPU); 128-token prompt, then a 512-token greedy decode per step from the
+    rewound cache.  Returns (tok/s of the one sequence, max over ranks;
+    ms per step; per-GPU algorithmic GB/s; allreduce ms per token; extra
+    fields) on every rank.  Every rank takes the same collective steps."""
     import ctypes
 
     import torch
 
-    torch.cuda.set_device(local_rank)
-    dist = dist_init(world, local_rank)
     from tinyminigo_b200 import synth
     from tinyminigo_b200._lib import check, lib
     from tinyminigo_b200.model import Model
 
     P4, G4 = 128, 512
     cfg = synth.CONFIGS["c4"]
-    t0 = time.time()
-    w = synth.make_weights(cfg, 2025, device="cuda")
-    log(f"c4 weights generated in {time.time() - t0:.1f}s")
     tp = None
     if world > 1:
         uid = (ctypes.c_uint8 * 128)()
@@ -526,10 +577,16 @@ def run_c4(args, rank, world, local_rank):
         t = torch.tensor(list(bytes(uid)), dtype=torch.uint8, device="cuda")
         dist.broadcast(t, 0)
         tp = (bytes(t.cpu().tolist()), rank, world)
-    model = Model.from_tensors(model_config(cfg), w, device=local_rank, tp=tp)
-    host_leg = world == 1 and not args.no_cpu_baseline
-    if not host_leg:
-        del w
+    t0 = time.time()
+    if host_leg:  # the oracle needs every tensor in host memory
+        w = synth.make_weights(cfg, 2025, device="cuda")
+        model = Model.from_tensors(model_config(cfg), w, device=local_rank, tp=tp)
+    else:  # one tensor in host memory at a time
+        w = None
+        model = Model.from_tensors(model_config(cfg), synth.iter_weights(cfg, 2025, device="cuda"),
+                                   device=local_rank, tp=tp)
+    log(f"c4 weights generated and uploaded in {time.time() - t0:.1f}s "
+        f"({model.weight_bytes() / 1e9:.2f} GB on this rank)")
     prompt = synth.random_prompt(cfg["vocab_size"], P4, 17)
     cache = model.new_cache(P4 + G4 + 8)
     logits = model.forward_seq(prompt, cache)
@@ -541,37 +598,64 @@ def run_c4(args, rank, world, local_rank):
         cache.truncate(P4)
         model.decode([tok], cache, G4, wait=False)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     model.sync()
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local_rank) as clk:
-        ev0.record(stream)
-        for _ in range(args.steps):
-            step()
-        ev1.record(stream)
-        model.sync()
-        torch.cuda.synchronize()
-    ms = max_over_ranks(dist, ev0.elapsed_time(ev1)) / args.steps
+    ev0.record(stream)
+    for _ in range(steps):
+        step()
+    ev1.record(stream)
+    model.sync()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(dist, ev0.elapsed_time(ev1)) / steps
     value = G4 / (ms / 1e3)
+    # the collectives' share: one profiling pass (kernels launched one at a
+    # time with CUDA events around each, so slower than the graph)
+    cache.truncate(P4)
+    n_prof = 8
+    prof = model.profile_decode([tok], cache, n_prof)
+    ar_ms_tok = max_over_ranks(dist, prof["allreduce"][0] / n_prof)
+    ag_ms_tok = max_over_ranks(dist, prof["allgather_step_end"][0] / n_prof)
+    prof_ms_tok = max_over_ranks(dist, sum(v[0] for v in prof.values()) / n_prof)
     h, L, I, V = cfg["hidden_size"], cfg["num_hidden_layers"], cfg["intermediate_size"], cfg["vocab_size"]
     qd, kd = cfg["num_attention_heads"] * cfg["head_dim"], cfg["num_key_value_heads"] * cfg["head_dim"]
     wbytes = 2 * (L * ((qd + 2 * kd) * h + h * qd + 3 * I * h) + V * h)
     kvb = L * 2 * kd * 4 * (P4 + G4 / 2)
     per_gpu = (wbytes + kvb) / world
     gbs = per_gpu / (ms / 1e3 / G4) / 1e9
-    peak, peak_kind = peaks()
-    extra = {}
+    extra = {"profile_pass_ms_per_token": round(prof_ms_tok, 4),
+             "allreduce_ms_per_token": round(ar_ms_tok, 4),
+             "allreduces_per_token": int(prof["allreduce"][1] // n_prof),
+             "allgather_step_end_ms_per_token": round(ag_ms_tok, 4)}
     if host_leg:
         cache.truncate(P4)
         gpu_ids = model.decode([tok], cache, 16)[0].tolist()
-        extra = c4_cpu_leg(cfg, w, prompt, logits, [tok] + gpu_ids[:15])
+        extra.update(c4_cpu_leg(cfg, w, prompt, logits, [tok] + gpu_ids[:15]))
+    if dist is not None:
+        dist.barrier()
+    cache.close()
+    model.close()
+    return value, ms, gbs, per_gpu, extra
+
+
+def run_c4(args, rank, world, local_rank):
+    """C4 as its own line (see measure_c4)."""
+    import torch
+
+    torch.cuda.set_device(local_rank)
+    dist = dist_init(world, local_rank)
+    with ClockSampler(local_rank) as clk:
+        value, ms, gbs, per_gpu, extra = measure_c4(
+            args, rank, world, local_rank, dist, args.steps, args.warmup,
+            world == 1 and not args.no_cpu_baseline)
+    peak, peak_kind = peaks()
     if rank == 0:
         res = base_line(args, world, "decode_tok_s", value, "tok/s", ms,
                         {"workload": "c4: 8B-class, untied, 128-token prompt, greedy 512",
-                         "global_batch": 1, "seq_len": P4 + G4,
+                         "global_batch": 1, "seq_len": 128 + 512,
                          "parallelism": f"tp{world}" if world > 1 else "single GPU"},
                         "strong", clk.summary(),
                         roofline={"bound": "hbm", "kernel": "decode step (per-GPU bytes)",
@@ -581,10 +665,6 @@ def run_c4(args, rank, world, local_rank):
                                   "peak_kind": peak_kind},
                         gpu_launches=None, **extra)
         print(json.dumps(res), flush=True)
-    if dist is not None:
-        dist.barrier()
-    cache.close()
-    model.close()
     if dist is not None:
         dist.destroy_process_group()
 
@@ -597,7 +677,8 @@ def run_c5(args, rank, world, local_rank):
     alone (the API prefills inside generate).  The subtraction is paired:
     the same generate_batch with max_tokens = 1 (its 16 prefills and the
     first token) is timed right after, so the value is the 16 x (steps - 1)
-    tokens after the first over the time difference."""
+    tokens after the first over the time difference.  Both calls are timed
+    with CUDA events recorded on the library's stream around them."""
     import torch
 
     if rank != 0:
@@ -615,13 +696,18 @@ def run_c5(args, rank, world, local_rank):
                         repetition_penalty=1.1, seed=1000 + i) for i in range(M)]
     params1 = [GenParams(max_tokens=1, temperature=0.8, top_k=40, top_p=0.95,
                          repetition_penalty=1.1, seed=1000 + i) for i in range(M)]
+    stream = torch.cuda.ExternalStream(model.stream_handle(), device=local_rank)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     with ClockSampler(local_rank) as clk:  # the long call first: it sizes the token buffers
-        t0 = time.perf_counter()
+        ev[0].record(stream)
         outs = generate_batch(model, prompts, params, cache=cache)
-        t_all = time.perf_counter() - t0
-        t0 = time.perf_counter()
+        ev[1].record(stream)
+        ev[2].record(stream)
         generate_batch(model, prompts, params1, cache=cache)
-        t_pre = time.perf_counter() - t0
+        ev[3].record(stream)
+        ev[3].synchronize()
+    t_all = ev[0].elapsed_time(ev[1]) / 1e3
+    t_pre = ev[2].elapsed_time(ev[3]) / 1e3
     dec = max(t_all - t_pre, 1e-9)
     n_tok = sum(len(o) - 1 for o in outs)
     extra = {}
@@ -640,8 +726,8 @@ def run_c5(args, rank, world, local_rank):
                               "frac": round(gbs / peak, 4), "traffic": None,
                               "peak_kind": peak_kind},
                     prefill_and_first_token_s=round(t_pre, 2), generate_batch_s=round(t_all, 2),
-                    timing="host wall clock: generate_batch minus the same call with max_tokens 1 "
-                           "(16 prefills + the first token)",
+                    timing="CUDA events on the library's stream: generate_batch minus the same "
+                           "call with max_tokens 1 (16 prefills + the first token)",
                     **extra)
     print(json.dumps(res), flush=True)
     cache.close()
@@ -849,6 +935,8 @@ def main():
     ap.add_argument("--c5-ctx", type=int, default=32768, help="c5: prompt length per stream")
     ap.add_argument("--c5-steps", type=int, default=256, help="c5: sampled steps")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-c4", action="store_true",
+                    help="c2: leave out the tensor-parallel 8B block")
     ap.add_argument("--ncu-steps", type=int, default=0,
                     help="profiling mode: prefill + this many decode steps, no timing, no output")
     ap.add_argument("--trace", default="",

@@ -3,8 +3,8 @@
  *
  * This is the boundary that replaces the CPU kernels and the forward pass of
  * HanzCEO/TinyMiniGo (citations are `path:line` in that project).  A Rust
- * engine binds it with `extern "C"` (INTEGRATION.md shows the binding); the
- * parity tests and bench.py bind it with ctypes.
+ * engine binds it with an `extern "C"` block (the rust/tmg-cuda-sys crate of
+ * this repository); the parity tests and bench.py bind it with ctypes.
  *
  * Conventions
  *  - Every call returns an int status: TMG_OK (0) or a negative TMG_ERR_*.
@@ -69,6 +69,7 @@ typedef struct tmg_gen_params {
 
 typedef struct tmg_ctx tmg_ctx; /* Model: weights, scratch, stream (src/model.rs:338-346) */
 typedef struct tmg_kv tmg_kv;   /* KvCache on the device (src/model.rs:250-260) */
+typedef struct tmg_wmat tmg_wmat; /* WMat on the device (src/tensor.rs:198-206) */
 
 /* Called once per generated token from inside tmg_generate (the on_token
  * callback of src/model.rs:618; main.rs:94-100 detokenises there).  Return
@@ -213,9 +214,10 @@ int tmg_sync(tmg_ctx* ctx);
 void* tmg_stream(tmg_ctx* ctx);
 /* Profiling aid: the same greedy steps as tmg_decode, launched one kernel at
  * a time with CUDA events around each kernel (so without the overlap of the
- * captured graph).  ms[6] / launches[6] receive the summed device time and
+ * captured graph).  ms[8] / launches[8] receive the summed device time and
  * the launch count of: 0 qkv GEMV, 1 attention, 2 o GEMV, 3 gate/up GEMV,
- * 4 down GEMV, 5 LM head. */
+ * 4 down GEMV, 5 LM head, 6 allreduce + residual add and 7 logits
+ * allgather + end of step (6 and 7 under tensor parallelism only). */
 int tmg_profile_decode(tmg_ctx* ctx, tmg_kv* kv, const uint32_t* tokens, int64_t n_steps,
                        double* ms, int64_t* launches);
 /* Profiling aid: the device timeline of one captured greedy step (the real
@@ -249,6 +251,15 @@ int tmg_trace_fused(tmg_ctx* ctx, tmg_kv* kv, uint32_t token, uint64_t* out, int
  * column-split by heads and rows, o/down row-split, lm_head split by vocab).
  * ------------------------------------------------------------------------ */
 int tmg_tp_unique_id(uint8_t id[128]);
+/* Host-only: the block of the full tensor `name` (HF name, e.g.
+ * "model.layers.3.mlp.down_proj.weight") that rank `rank` of `world` keeps,
+ * as out = {row0, rows, col0, cols} of its [out, in] layout (vectors:
+ * [n, 1]).  q/k/v and gate/up are split by output rows (whole heads,
+ * I / world rows), o and down by input columns, lm_head by vocabulary rows
+ * (ceil(V / world) per rank); the embedding and norms are replicated.  This
+ * is the split tmg_set_tensor / tmg_load_* apply after tmg_tp_init. */
+int tmg_tp_shard(const tmg_config* cfg, const char* name, int32_t rank, int32_t world,
+                 int64_t out[4]);
 int tmg_tp_init(tmg_ctx* ctx, const uint8_t id[128], int32_t rank, int32_t world);
 
 /* ---------------------------------------------------------------------------
@@ -264,6 +275,21 @@ int tmg_op_gemv_bf16(tmg_ctx* ctx, const float* x, const uint16_t* w, int64_t N,
  * tensor cores): y[T, N] = x[T, K] . W[N, K]^T. */
 int tmg_op_gemm_bf16(tmg_ctx* ctx, const float* x, const uint16_t* w, int64_t N, int64_t K,
                      int64_t T, float* y);
+/* WMat handles (src/tensor.rs:198-206): a BF16 weight matrix [rows, cols]
+ * (row-major, [out, in]) uploaded once to HBM and owned by the handle; the
+ * host buffer (it may be the safetensors mapping) is not retained.  Free a
+ * handle with tmg_wmat_free before destroying its context (tmg_destroy
+ * releases any that are left, after which their pointers dangle). */
+int tmg_wmat_upload_bf16(tmg_ctx* ctx, const uint16_t* host, int64_t rows, int64_t cols,
+                         tmg_wmat** out);
+int tmg_wmat_free(tmg_wmat* w);
+int tmg_wmat_shape(const tmg_wmat* w, int64_t* rows, int64_t* cols);
+/* matmul_w_into(x, &WMat, out, in, y), src/tensor.rs:331-460, over a handle:
+ * y[M, rows] = x[M, cols] . W^T (device pointers, M <= 16). */
+int tmg_op_gemv_wmat(tmg_ctx* ctx, const float* x, const tmg_wmat* w, int32_t M, float* y);
+/* matmul_batch_w_into, src/tensor.rs:573-792, over a handle: y[T, rows] =
+ * x[T, cols] . W^T on the tcgen05 prefill GEMM (device pointers). */
+int tmg_op_gemm_wmat(tmg_ctx* ctx, const float* x, const tmg_wmat* w, int64_t T, float* y);
 /* rms_norm_into (mode 0, src/tensor.rs:969-977) or rms_norm_batch (mode 1,
  * 946-954) over `rows` rows of n. */
 int tmg_op_rmsnorm(tmg_ctx* ctx, const float* x, const float* w, float eps, int64_t n,
@@ -275,7 +301,9 @@ int tmg_op_rope(tmg_ctx* ctx, float* x, int64_t rows, int32_t n_heads, int32_t h
 /* SwiGLU, src/model.rs:473-475: out = gate / (1 + exp(-gate)) * up. */
 int tmg_op_swiglu(tmg_ctx* ctx, const float* gate, const float* up, int64_t n, float* out);
 /* Decode attention, src/model.rs:434-459: one query row of n_q heads over
- * n_ctx cached rows of [n_kv * head_dim] (keys already rotated). */
+ * n_ctx cached rows of [n_kv * head_dim] (keys already rotated).  head_dim
+ * 16, 32, 64 or 128; at most 16 query heads per kv head; other shapes return
+ * TMG_ERR_INVALID before anything is enqueued. */
 int tmg_op_attn_decode(tmg_ctx* ctx, const float* q, const float* keys, const float* values,
                        int64_t n_ctx, int32_t n_q, int32_t n_kv, int32_t head_dim, float* out);
 /* The same decode attention as tmg_op_attn_decode (same split count, same
@@ -284,9 +312,10 @@ int tmg_op_attn_decode(tmg_ctx* ctx, const float* q, const float* keys, const fl
  * tickets and the position word live in a 4 MiB static per-device scratch
  * (requests needing more return TMG_ERR_CAPACITY before enqueuing
  * anything).  It only enqueues on the context's stream (results are ready
- * after tmg_sync).  The first call on a device sets the scratch up and
- * should precede any stream capture.  Calls that overlap on one device race
- * on the shared scratch: order them. */
+ * after tmg_sync).  Shapes as tmg_op_attn_decode (others return
+ * TMG_ERR_INVALID before anything is enqueued).  The first call on a device
+ * sets the scratch up and should precede any stream capture.  Calls that
+ * overlap on one device race on the shared scratch: order them. */
 int tmg_op_attn_decode_noalloc(tmg_ctx* ctx, const float* q, const float* keys,
                                const float* values, int64_t n_ctx, int32_t n_q, int32_t n_kv,
                                int32_t head_dim, float* out);

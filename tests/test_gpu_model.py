@@ -169,19 +169,41 @@ def test_c1_greedy_with_penalty(orc, c1):
     assert out.tokens == ref.tolist()
 
 
-def test_c2_greedy_identical(orc, c2):
+def test_c2_generate_256_full_depth(orc, greedy, c2):
+    # BASELINE config C2 as stated: the 1B shape at full depth (16 layers,
+    # tied head), a 64-token random prompt, then 256 greedy steps through
+    # generate (every step inside the fused decode kernel), against the
+    # oracle's generate loop (src/model.rs:614-663)
     cfg, t = c2
     prompt = synth.random_prompt(cfg["vocab_size"], 64, 11)
     om = orc.OracleModel(cfg, t)
-    steps = 24
-    ref, ref_first, _, _ = om.generate(prompt, steps)
+    steps = 256
+    ids, margins, second, ref_first = greedy.oracle(om, prompt, steps)
     m = Model.from_tensors(cfg_obj(cfg), t)
     out = generate(m, prompt, GenParams(max_tokens=steps))
     assert close(out.logits_first_step, ref_first), np.max(np.abs(out.logits_first_step - ref_first))
-    if out.tokens != ref.tolist():
-        i = next(j for j, (a, b) in enumerate(zip(out.tokens, ref.tolist())) if a != b)
-        pytest.fail(f"greedy diverged at step {i}: gpu {out.tokens[i]} vs ref {ref[i]}")
+    greedy.agree("C2 1B, 16 layers, 64-token prompt, 256 steps (fused)", out.tokens, ids, margins,
+                 second)
     m.close()
+
+
+def test_c4_8b_shape_on_one_gpu(orc, greedy):
+    # BASELINE config C4's model (hidden 4096, 32 layers, 32 q / 8 kv heads of
+    # 128, intermediate 14336, vocab 128256, untied) on one GPU: a 128-token
+    # random prompt, first-step logits within 1e-3 rel / 1e-2 abs of the
+    # oracle's, then 16 greedy steps
+    cfg = synth.CONFIGS["c4"]
+    t = synth.make_weights(cfg, 4048, device="cuda")
+    prompt = synth.random_prompt(cfg["vocab_size"], 128, 17)
+    steps = 16
+    om = orc.OracleModel(cfg, t)
+    ids, margins, second, ref_first = greedy.oracle(om, prompt, steps)
+    m = Model.from_tensors(cfg_obj(cfg), t)
+    out = generate(m, prompt, GenParams(max_tokens=steps))
+    assert close(out.logits_first_step, ref_first), np.max(np.abs(out.logits_first_step - ref_first))
+    greedy.agree("C4 8B shape, 1 GPU, 128-token prompt, 16 steps", out.tokens, ids, margins, second)
+    m.close()
+    del om
 
 
 def test_c2_batched_streams_match_single(orc, c2):

@@ -79,6 +79,41 @@ def test_gemm_prefill(ctx, orc, T, N, K):
     assert np.all(np.abs(y - ref) <= bound(x, w))
 
 
+def test_wmat_handle(ctx, orc):
+    # WMat as a device handle (src/tensor.rs:198-206): upload once from host
+    # memory, then matmul_w_into (M rows) and matmul_batch_w_into over it
+    from tinyminigo_b200._lib import TmgError
+
+    rng = np.random.default_rng(77)
+    N, K = 1536, 2048
+    w = bf16(rng.normal(0, 0.02, (N, K)))
+    h = ctypes.c_void_p()
+    check(lib().tmg_wmat_upload_bf16(ctx, w.ctypes.data_as(ctypes.c_void_p), N, K,
+                                     ctypes.byref(h)), ctx)
+    r, c = ctypes.c_int64(), ctypes.c_int64()
+    check(lib().tmg_wmat_shape(h, ctypes.byref(r), ctypes.byref(c)))
+    assert (r.value, c.value) == (N, K)
+    w[:] = 0  # the handle holds its own copy
+    w = bf16(np.random.default_rng(77).normal(0, 0.02, (N, K)))
+    x = rng.normal(0, 1, (3, K)).astype(np.float32)
+    xd = dev(x)
+    yd = torch.zeros((3, N), dtype=torch.float32, device="cuda")
+    check(lib().tmg_op_gemv_wmat(ctx, P(xd), h, 3, P(yd)), ctx)
+    y = yd.cpu().numpy()
+    for m in range(3):
+        assert np.all(np.abs(y[m] - orc.matmul_w(x[m], w)) <= bound(x[m], w))
+    T = 40
+    xt = rng.normal(0, 1, (T, K)).astype(np.float32)
+    xtd = dev(xt)
+    ytd = torch.zeros((T, N), dtype=torch.float32, device="cuda")
+    check(lib().tmg_op_gemm_wmat(ctx, P(xtd), h, T, P(ytd)), ctx)
+    assert np.all(np.abs(ytd.cpu().numpy() - orc.matmul_batch_w(xt, w)) <= bound(xt, w))
+    check(lib().tmg_wmat_free(h))
+    with pytest.raises(TmgError):
+        check(lib().tmg_wmat_upload_bf16(ctx, w.ctypes.data_as(ctypes.c_void_p), 0, K,
+                                         ctypes.byref(h)), ctx)
+
+
 @pytest.mark.parametrize("mode", [0, 1])
 def test_rmsnorm(ctx, orc, mode):
     rng = np.random.default_rng(3)

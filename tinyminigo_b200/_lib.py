@@ -104,7 +104,13 @@ SIGNATURES = {
     "tmg_trace_fused": (_I, [_P, _P, ctypes.c_uint32, _P, ctypes.c_int64, ctypes.POINTER(_I32)]),
     "tmg_tp_unique_id": (_I, [_P]),
     "tmg_tp_init": (_I, [_P, _P, _I32, _I32]),
+    "tmg_tp_shard": (_I, [_P, ctypes.c_char_p, _I32, _I32, _P]),
     "tmg_op_gemv_bf16": (_I, [_P, _P, _P, _I64, _I64, _I32, _P]),
+    "tmg_wmat_upload_bf16": (_I, [_P, _P, _I64, _I64, _PP]),
+    "tmg_wmat_free": (_I, [_P]),
+    "tmg_wmat_shape": (_I, [_P, ctypes.POINTER(_I64), ctypes.POINTER(_I64)]),
+    "tmg_op_gemv_wmat": (_I, [_P, _P, _P, _I32, _P]),
+    "tmg_op_gemm_wmat": (_I, [_P, _P, _P, _I64, _P]),
     "tmg_op_gemm_bf16": (_I, [_P, _P, _P, _I64, _I64, _I64, _P]),
     "tmg_op_rmsnorm": (_I, [_P, _P, _P, _F, _I64, _I64, _I32, _P]),
     "tmg_op_rope": (_I, [_P, _P, _I64, _I32, _I32, _I64, _F]),

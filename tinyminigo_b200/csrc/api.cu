@@ -84,6 +84,11 @@ struct tmg_ctx {
   int fused_rep = 4;             // copies of its x/att/act exchange words (TMG_FUSED_REP)
   int fused_stages = 4;          // its ring depth cap (0: all that fit; TMG_FUSED_STAGES)
   bool fused_ok = false;         // the fused batch-1 decode kernel takes this shape
+  // failure-path test of the fused kernel (TMG_TEST_FUSED_STALL=<phase>,
+  // TMG_TEST_FUSED_POLL_MS=<ms>): the context's next fused launch waits in
+  // that phase for a tag nobody writes, with polls limited to that many ms
+  int test_stall = -1;
+  int test_poll_ms = 50;
   // prefill scratch
   int64_t pf_cap = 0;
   float *X = nullptr, *Xn = nullptr, *QKV = nullptr, *ATT = nullptr, *G = nullptr, *U = nullptr;
@@ -97,7 +102,17 @@ struct tmg_ctx {
   // pinned staging
   void* pinned = nullptr;
   size_t pinned_cap = 0;
+  // WMat handles still alive (released by tmg_destroy if the caller did not)
+  std::vector<tmg_wmat*> wmats;
   std::string err;
+};
+
+// A device weight matrix handle (WMat, src/tensor.rs:198-206): row-major
+// [rows, cols] BF16 bits in HBM, owned by the handle.
+struct tmg_wmat {
+  tmg_ctx* ctx = nullptr;
+  int64_t rows = 0, cols = 0;
+  uint16_t* w = nullptr;
 };
 
 struct tmg_kv {
@@ -257,6 +272,63 @@ int upload_vec(tmg_ctx* c, float* dst, int32_t dtype, const void* host, int64_t 
   return TMG_OK;
 }
 
+// The tensor-parallel split: the block of the full tensor `name` (HF name)
+// that `rank` of `world` keeps, as rows [r0, r0 + nr) x columns
+// [c0, c0 + nc) of its [rows, cols] layout (vectors are [n, 1]).  q/k/v and
+// gate/up are split by output rows (whole heads, I / world rows), o and down
+// by input columns, the LM head by vocabulary rows (ceil(V / world) per
+// rank, the last rank keeps the rest); the embedding and the norm vectors
+// are replicated.  With world 1 every block is the whole tensor.
+// full = {rows, cols} of the whole tensor.  False for an unknown name.
+bool tp_shard_rect(const tmg_config& f, const std::string& name, int rank, int world,
+                   int64_t rect[4], int64_t full[2]) {
+  const int64_t h = f.hidden_size, d = f.head_dim, V = f.vocab_size;
+  const int64_t qg = int64_t(f.num_attention_heads) * d, kg = int64_t(f.num_key_value_heads) * d;
+  const int64_t Ig = f.intermediate_size;
+  const int64_t ql = qg / world, kl = kg / world, Il = Ig / world;
+  auto set = [&](int64_t R, int64_t C, int64_t r0, int64_t nr, int64_t c0, int64_t nc) {
+    full[0] = R;
+    full[1] = C;
+    rect[0] = r0;
+    rect[1] = nr;
+    rect[2] = c0;
+    rect[3] = nc;
+    return true;
+  };
+  if (name == "model.embed_tokens.weight") return set(V, h, 0, V, 0, h);
+  if (name == "model.norm.weight") return set(h, 1, 0, h, 0, 1);
+  if (name == "lm_head.weight") {
+    const int64_t vl = (V + world - 1) / world, v0 = int64_t(rank) * vl;
+    return set(V, h, v0, std::max<int64_t>(0, std::min<int64_t>(vl, V - v0)), 0, h);
+  }
+  const std::string pre = "model.layers.";
+  if (name.compare(0, pre.size(), pre) != 0) return false;
+  const size_t dot = name.find('.', pre.size());
+  if (dot == std::string::npos) return false;
+  const std::string suf = name.substr(dot + 1);
+  if (suf == "self_attn.q_proj.weight") return set(qg, h, rank * ql, ql, 0, h);
+  if (suf == "self_attn.k_proj.weight" || suf == "self_attn.v_proj.weight")
+    return set(kg, h, rank * kl, kl, 0, h);
+  if (suf == "self_attn.o_proj.weight") return set(h, qg, 0, h, rank * ql, ql);
+  if (suf == "mlp.gate_proj.weight" || suf == "mlp.up_proj.weight")
+    return set(Ig, h, rank * Il, Il, 0, h);
+  if (suf == "mlp.down_proj.weight") return set(h, Ig, 0, h, rank * Il, Il);
+  if (suf == "input_layernorm.weight" || suf == "post_attention_layernorm.weight")
+    return set(h, 1, 0, h, 0, 1);
+  return false;
+}
+
+// Upload this rank's block of a full host matrix (tp_shard_rect) to dst.
+int upload_shard(tmg_ctx* c, const std::string& name, uint16_t* dst, const void* host,
+                 int64_t numel) {
+  int64_t r[4], full[2];
+  if (!tp_shard_rect(c->cfg, name, c->rank, c->world, r, full))
+    return fail(c, TMG_ERR_INVALID, "unknown tensor " + name);
+  int rc = check_shape(c, name, numel, full[0] * full[1]);
+  if (rc) return rc;
+  return upload_block(c, dst, static_cast<const uint16_t*>(host), full[1], r[0], r[1], r[2], r[3]);
+}
+
 int set_tensor(tmg_ctx* c, const std::string& name, int32_t dtype, const void* host,
                int64_t numel) {
   if (!c->has_model) return fail(c, TMG_ERR_INVALID, "context has no model config");
@@ -283,8 +355,7 @@ int set_tensor(tmg_ctx* c, const std::string& name, int32_t dtype, const void* h
       c->weight_bytes += c->V_l * h * 2;
       c->lm_tied = false;
     }
-    return upload_block(c, c->lm_head, static_cast<const uint16_t*>(host), h, c->v_off, c->V_l,
-                        0, h);
+    return upload_shard(c, name, c->lm_head, host, numel);
   }
   const std::string pre = "model.layers.";
   if (name.compare(0, pre.size(), pre) != 0)
@@ -295,39 +366,31 @@ int set_tensor(tmg_ctx* c, const std::string& name, int32_t dtype, const void* h
   if (li < 0 || li >= c->L) return fail(c, TMG_ERR_INVALID, "layer out of range: " + name);
   const std::string suf = name.substr(dot + 1);
   Layer& Lw = c->layers[li];
-  const uint16_t* src = static_cast<const uint16_t*>(host);
-  const int64_t qg = int64_t(c->nq_g) * d, kg = int64_t(c->nkv_g) * d;
   const int64_t ql = int64_t(c->nq) * d, kl = int64_t(c->nkv) * d;
   if (suf == "self_attn.q_proj.weight") {
-    if ((rc = check_shape(c, name, numel, qg * h))) return rc;
     Lw.have |= kHaveQ;
-    return upload_block(c, Lw.wqkv, src, h, c->rank * ql, ql, 0, h);
+    return upload_shard(c, name, Lw.wqkv, host, numel);
   }
   if (suf == "self_attn.k_proj.weight") {
-    if ((rc = check_shape(c, name, numel, kg * h))) return rc;
     Lw.have |= kHaveK;
-    return upload_block(c, Lw.wqkv + ql * h, src, h, c->rank * kl, kl, 0, h);
+    return upload_shard(c, name, Lw.wqkv + ql * h, host, numel);
   }
   if (suf == "self_attn.v_proj.weight") {
-    if ((rc = check_shape(c, name, numel, kg * h))) return rc;
     Lw.have |= kHaveV;
-    return upload_block(c, Lw.wqkv + (ql + kl) * h, src, h, c->rank * kl, kl, 0, h);
+    return upload_shard(c, name, Lw.wqkv + (ql + kl) * h, host, numel);
   }
   if (suf == "self_attn.o_proj.weight") {
-    if ((rc = check_shape(c, name, numel, h * qg))) return rc;
     Lw.have |= kHaveO;
-    return upload_block(c, Lw.wo, src, qg, 0, h, c->rank * ql, ql);
+    return upload_shard(c, name, Lw.wo, host, numel);
   }
   if (suf == "mlp.gate_proj.weight" || suf == "mlp.up_proj.weight") {
-    if ((rc = check_shape(c, name, numel, int64_t(c->I_g) * h))) return rc;
     const bool gate = suf[4] == 'g';
     Lw.have |= gate ? kHaveG : kHaveU;
-    return upload_block(c, gate ? Lw.wg : Lw.wu, src, h, int64_t(c->rank) * c->I, c->I, 0, h);
+    return upload_shard(c, name, gate ? Lw.wg : Lw.wu, host, numel);
   }
   if (suf == "mlp.down_proj.weight") {
-    if ((rc = check_shape(c, name, numel, h * int64_t(c->I_g)))) return rc;
     Lw.have |= kHaveD;
-    return upload_block(c, Lw.wd, src, c->I_g, 0, h, int64_t(c->rank) * c->I, c->I);
+    return upload_shard(c, name, Lw.wd, host, numel);
   }
   if (suf == "input_layernorm.weight" || suf == "post_attention_layernorm.weight") {
     if ((rc = check_shape(c, name, numel, h))) return rc;
@@ -402,6 +465,13 @@ int alloc_model(tmg_ctx* c) {
   if (const char* pf = getenv("TMG_FUSED_PF")) c->fused_pf = atoi(pf);
   if (const char* pp = getenv("TMG_FUSED_PF_PACE")) c->fused_pf_pace = atoi(pp);
   if (const char* ns = getenv("TMG_FUSED_STAGES")) c->fused_stages = atoi(ns);
+  if (const char* ts = getenv("TMG_TEST_FUSED_STALL")) {
+    // only a GEMV phase that gathers its input: O, GU, DOWN (p % 5 = 2, 3,
+    // 4), a later layer's QKV or the LM head (p % 5 = 0, p > 0)
+    const int p = atoi(ts);
+    if (p > 0 && p <= 5 * c->L && p % 5 != 1) c->test_stall = p;
+  }
+  if (const char* tm = getenv("TMG_TEST_FUSED_POLL_MS")) c->test_poll_ms = std::max(1, atoi(tm));
   c->has_model = true;
   return TMG_OK;
 }
@@ -485,7 +555,11 @@ cudaError_t tp_reduce_add(tmg_ctx* c, float* partial, float* dst, int64_t n) {
   return launch_add(partial, dst, n, c->stream);
 }
 
-// Per-kernel CUDA events of the profiling pass (tmg_profile_decode).
+// Per-kernel CUDA events of the profiling pass (tmg_profile_decode): classes
+// 0 qkv GEMV, 1 attention, 2 o GEMV, 3 gate/up GEMV, 4 down GEMV, 5 LM head,
+// 6 allreduce + residual add (tensor parallel), 7 logits allgather + end of
+// step (tensor parallel).
+constexpr int kProfClasses = 8;
 struct Prof {
   cudaStream_t s;
   std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> marks;
@@ -601,7 +675,11 @@ cudaError_t enqueue_forward(tmg_ctx* c, tmg_kv* kv, const StreamState& st, bool 
     B();
     TMG_CUDA_TRY(gemv(c, O, PRO_NONE, tp ? EPI_STORE : EPI_ADD, pdl));
     E(2);
-    if (tp) TMG_CUDA_TRY(tp_reduce_add(c, c->partial, c->x, int64_t(M) * c->h));
+    if (tp) {
+      B();
+      TMG_CUDA_TRY(tp_reduce_add(c, c->partial, c->x, int64_t(M) * c->h));
+      E(6);
+    }
     GemvArgs GU;
     GU.w = Lw.wg;
     GU.w2 = Lw.wu;
@@ -629,7 +707,11 @@ cudaError_t enqueue_forward(tmg_ctx* c, tmg_kv* kv, const StreamState& st, bool 
     B();
     TMG_CUDA_TRY(gemv(c, D, PRO_NONE, tp ? EPI_STORE : EPI_ADD, pdl));
     E(4);
-    if (tp) TMG_CUDA_TRY(tp_reduce_add(c, c->partial, c->x, int64_t(M) * c->h));
+    if (tp) {
+      B();
+      TMG_CUDA_TRY(tp_reduce_add(c, c->partial, c->x, int64_t(M) * c->h));
+      E(6);
+    }
   }
   GemvArgs H;
   H.w = c->lm_head;
@@ -653,9 +735,14 @@ cudaError_t enqueue_forward(tmg_ctx* c, tmg_kv* kv, const StreamState& st, bool 
     return e;
   }
   // TP: vocab-split head; gather the logits, then the same end of step
+  B();
   TMG_CUDA_TRY(gemv(c, H, PRO_NORM, EPI_STORE, pdl));
+  E(5);
+  B();
   TMG_CUDA_TRY(tp_allgather_rows(c->tp, c->logits, c->V_l, c->logits_full, c->V, M, c->stream));
-  return launch_step_end(st, M, argmax ? c->logits_full : nullptr, c->V, c->stream);
+  TMG_CUDA_TRY(launch_step_end(st, M, argmax ? c->logits_full : nullptr, c->V, c->stream));
+  E(7);
+  return cudaSuccess;
 }
 
 // forward_seq for one stream (model.rs:503-590): chunks of kPrefillChunk
@@ -830,6 +917,11 @@ cudaError_t launch_fused(tmg_ctx* c, tmg_kv* kv, const StreamState& st, int64_t 
   f.n_steps = int(n_steps);
   f.err = c->d_err;
   f.trace = trace;
+  if (c->test_stall >= 0) {
+    f.stall_phase = c->test_stall;
+    f.poll_ns = (unsigned long long)(c->test_poll_ms) * 1000000ull;
+    c->test_stall = -1;
+  }
   return launch_decode_fused(f, c->num_sms, c->stream);
 }
 
@@ -954,9 +1046,12 @@ int run_generate(tmg_ctx* c, tmg_kv* kv, const uint32_t* prompts, int64_t T,
   CK(cudaEventCreateWithFlags(&ev[0], cudaEventDisableTiming), "event");
   CK(cudaEventCreateWithFlags(&ev[1], cudaEventDisableTiming), "event");
   int32_t* pinned_state = nullptr;
-  CK(ensure_pinned(c, sizeof(int32_t) * 4 * kMaxStreams * 2 + size_t(M) * maxt * 4 * 2), "pinned");
+  CK(ensure_pinned(c, sizeof(int32_t) * (4 * kMaxStreams + 1) * 2 + size_t(M) * maxt * 4 * 2),
+     "pinned");
   pinned_state = static_cast<int32_t*>(c->pinned);
   uint32_t* pinned_gen = reinterpret_cast<uint32_t*>(pinned_state + 8 * kMaxStreams);
+  // the device error word after each chunk (a failed step ends the loop)
+  int32_t* pinned_err = reinterpret_cast<int32_t*>(pinned_gen + size_t(M) * maxt * 2);
   int pending = -1;
   auto drain = [&](int slot) -> int {
     CK(cudaEventSynchronize(ev[slot]), "sync");
@@ -971,7 +1066,7 @@ int run_generate(tmg_ctx* c, tmg_kv* kv, const uint32_t* prompts, int64_t T,
       reported[m] = ng;
       if (!s[2 * kMaxStreams + m]) all_done = false;
     }
-    if (all_done) stop = true;
+    if (all_done || pinned_err[slot] != 0) stop = true;
     return TMG_OK;
   };
   int n_chunks = 0;
@@ -989,6 +1084,7 @@ int run_generate(tmg_ctx* c, tmg_kv* kv, const uint32_t* prompts, int64_t T,
     CK(cudaMemcpyAsync(pinned_gen + size_t(slot) * M * maxt, kv->d_gen, size_t(M) * maxt * 4,
                        cudaMemcpyDeviceToHost, c->stream),
        "tokens");
+    CK(cudaMemcpyAsync(pinned_err + slot, c->d_err, 4, cudaMemcpyDeviceToHost, c->stream), "err");
     CK(cudaEventRecord(ev[slot], c->stream), "event");
     if (pending >= 0 && (rc = drain(pending))) return rc;
     pending = slot;
@@ -1175,6 +1271,10 @@ int tmg_destroy(tmg_ctx* c) {
                   (void*)c->U, (void*)c->d_tok, c->op_buf, (void*)c->sp_hi, (void*)c->sp_lo})
     if (p) cudaFree(p);
   if (c->pinned) cudaFreeHost(c->pinned);
+  for (tmg_wmat* m : c->wmats) {
+    cudaFree(m->w);
+    delete m;
+  }
   if (c->tp) tp_destroy(c->tp);
   cudaStreamDestroy(c->stream);
   delete c;
@@ -1599,7 +1699,7 @@ int tmg_profile_decode(tmg_ctx* c, tmg_kv* kv, const uint32_t* tokens, int64_t n
     if (e != cudaSuccess) return cuda_fail(c, e, "profile");
   }
   CK(cudaStreamSynchronize(c->stream), "profile");
-  for (int k = 0; k < 6; ++k) {
+  for (int k = 0; k < kProfClasses; ++k) {
     ms[k] = 0.0;
     launches[k] = 0;
   }
@@ -1682,6 +1782,16 @@ int tmg_trace_fused(tmg_ctx* c, tmg_kv* kv, uint32_t token, uint64_t* out, int64
   return sync_check(c, "trace");
 }
 
+int tmg_tp_shard(const tmg_config* cfg, const char* name, int32_t rank, int32_t world,
+                 int64_t out[4]) {
+  if (!cfg || !name || !out || world < 1 || rank < 0 || rank >= world) return TMG_ERR_INVALID;
+  if (cfg->num_attention_heads % world || cfg->num_key_value_heads % world ||
+      cfg->intermediate_size % world)
+    return TMG_ERR_INVALID;
+  int64_t full[2];
+  return tp_shard_rect(*cfg, name, rank, world, out, full) ? TMG_OK : TMG_ERR_INVALID;
+}
+
 int tmg_tp_unique_id(uint8_t id[128]) { return tp_unique_id(id) == 0 ? TMG_OK : TMG_ERR_NCCL; }
 
 int tmg_tp_init(tmg_ctx* c, const uint8_t id[128], int32_t rank, int32_t world) {
@@ -1691,6 +1801,21 @@ int tmg_tp_init(tmg_ctx* c, const uint8_t id[128], int32_t rank, int32_t world) 
   std::string e;
   c->tp = tp_create(id, rank, world, e);
   if (!c->tp) return fail(c, TMG_ERR_NCCL, e);
+  // one allreduce and one allgather before any stream capture: NCCL sets up
+  // its connections on a communicator's first collectives
+  float* w = nullptr;
+  cudaError_t ce = cudaMalloc(&w, sizeof(float) * (1 + world));
+  if (ce == cudaSuccess) ce = cudaMemsetAsync(w, 0, sizeof(float) * (1 + world), c->stream);
+  if (ce == cudaSuccess) ce = tp_allreduce_sum(c->tp, w, 1, c->stream);
+  if (ce == cudaSuccess) ce = tp_allgather_rows(c->tp, w, 1, w + 1, world, 1, c->stream);
+  if (ce == cudaSuccess) ce = cudaStreamSynchronize(c->stream);
+  if (w) cudaFree(w);
+  if (ce != cudaSuccess) {
+    tp_destroy(c->tp);
+    c->tp = nullptr;
+    return fail(c, TMG_ERR_NCCL, std::string("tmg_tp_init: first collectives failed: ") +
+                                     cudaGetErrorString(ce));
+  }
   c->rank = rank;
   c->world = world;
   return TMG_OK;
@@ -1723,6 +1848,59 @@ int tmg_op_gemm_bf16(tmg_ctx* c, const float* x, const uint16_t* w, int64_t N, i
   CK(gemm(c, x, w, T, N, K, y, N, false), "gemm");
   CK(cudaStreamSynchronize(c->stream), "gemm");
   return TMG_OK;
+}
+
+int tmg_wmat_upload_bf16(tmg_ctx* c, const uint16_t* host, int64_t rows, int64_t cols,
+                         tmg_wmat** out) {
+  if (!c || !host || !out || rows <= 0 || cols <= 0 || rows > INT32_MAX || cols > INT32_MAX)
+    return fail(c, TMG_ERR_INVALID, "bad argument");
+  *out = nullptr;
+  cudaSetDevice(c->device);
+  tmg_wmat* m = new tmg_wmat();
+  m->ctx = c;
+  m->rows = rows;
+  m->cols = cols;
+  const size_t bytes = size_t(rows) * size_t(cols) * 2;
+  cudaError_t e = cudaMalloc(&m->w, bytes);
+  if (e == cudaSuccess) e = copy_sync(c, m->w, host, bytes, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    if (m->w) cudaFree(m->w);
+    delete m;
+    return cuda_fail(c, e, "tmg_wmat_upload_bf16");
+  }
+  c->wmats.push_back(m);
+  *out = m;
+  return TMG_OK;
+}
+
+int tmg_wmat_free(tmg_wmat* m) {
+  if (!m) return TMG_ERR_INVALID;
+  tmg_ctx* c = m->ctx;
+  auto it = std::find(c->wmats.begin(), c->wmats.end(), m);
+  if (it == c->wmats.end()) return fail(c, TMG_ERR_INVALID, "unknown WMat handle");
+  c->wmats.erase(it);
+  cudaSetDevice(c->device);
+  cudaStreamSynchronize(c->stream);
+  cudaFree(m->w);
+  delete m;
+  return TMG_OK;
+}
+
+int tmg_wmat_shape(const tmg_wmat* m, int64_t* rows, int64_t* cols) {
+  if (!m || !rows || !cols) return TMG_ERR_INVALID;
+  *rows = m->rows;
+  *cols = m->cols;
+  return TMG_OK;
+}
+
+int tmg_op_gemv_wmat(tmg_ctx* c, const float* x, const tmg_wmat* w, int32_t M, float* y) {
+  if (!c || !w || w->ctx != c) return fail(c, TMG_ERR_INVALID, "bad WMat handle");
+  return tmg_op_gemv_bf16(c, x, w->w, w->rows, w->cols, M, y);
+}
+
+int tmg_op_gemm_wmat(tmg_ctx* c, const float* x, const tmg_wmat* w, int64_t T, float* y) {
+  if (!c || !w || w->ctx != c) return fail(c, TMG_ERR_INVALID, "bad WMat handle");
+  return tmg_op_gemm_bf16(c, x, w->w, w->rows, w->cols, T, y);
 }
 
 int tmg_op_rmsnorm(tmg_ctx* c, const float* x, const float* w, float eps, int64_t n, int64_t rows,
@@ -1772,8 +1950,14 @@ int tmg_op_attn_decode(tmg_ctx* c, const float* q, const float* keys, const floa
   cudaSetDevice(c->device);
   const int G = n_q / n_kv;
   const int nsplit = attn_decode_nsplit(n_kv, 1, n_ctx, c->num_sms);
-  const size_t part_f = size_t(n_kv) * nsplit * G * (head_dim + 2);
-  CK(ensure_op(c, part_f * 4 + 4096), "op scratch");
+  std::string why;
+  if (!attn_decode_shape_ok(n_q, n_kv, head_dim, n_ctx, nsplit, &why))
+    return fail(c, TMG_ERR_INVALID, "tmg_op_attn_decode: " + why);
+  // op scratch: the partials, then one ticket per kv head, then the
+  // position word (each region 256-byte aligned)
+  const size_t part_b = (size_t(n_kv) * nsplit * G * (head_dim + 2) * 4 + 255) & ~size_t(255);
+  const size_t tick_b = (size_t(n_kv) * 4 + 255) & ~size_t(255);
+  CK(ensure_op(c, part_b + tick_b + 256), "op scratch");
   AttnDecodeArgs a;
   a.qkv = q;
   a.qkv_ld = 0;
@@ -1782,10 +1966,10 @@ int tmg_op_attn_decode(tmg_ctx* c, const float* q, const float* keys, const floa
   a.cap = n_ctx;
   a.out = out;
   a.part = static_cast<float*>(c->op_buf);
-  a.ticket = reinterpret_cast<unsigned int*>(static_cast<char*>(c->op_buf) + part_f * 4);
-  int32_t* posv = reinterpret_cast<int32_t*>(static_cast<char*>(c->op_buf) + part_f * 4 + 2048);
+  a.ticket = reinterpret_cast<unsigned int*>(static_cast<char*>(c->op_buf) + part_b);
+  int32_t* posv = reinterpret_cast<int32_t*>(static_cast<char*>(c->op_buf) + part_b + tick_b);
   const int32_t pv = int32_t(n_ctx - 1);
-  CK(cudaMemsetAsync(a.ticket, 0, 1024, c->stream), "memset");
+  CK(cudaMemsetAsync(a.ticket, 0, size_t(n_kv) * 4, c->stream), "memset");
   CK(cudaMemcpyAsync(posv, &pv, 4, cudaMemcpyHostToDevice, c->stream), "pos");
   a.pos_override = posv;
   a.nq = n_q;

@@ -1079,6 +1079,38 @@ cudaError_t attn_prepare() {
   return attn_attr<128>();
 }
 
+// The shapes launch_attn_decode takes (checked before anything is enqueued
+// by the op entry points): head dim 16/32/64/128, at most 16 query heads
+// per kv head, and the tiled kernel's shared memory within kMaxAttnSmem.
+bool attn_decode_shape_ok(int nq, int nkv, int d, int64_t n_ctx, int nsplit, std::string* why) {
+  if (nkv <= 0 || nq <= 0 || nq % nkv) {
+    *why = "n_q must be a positive multiple of n_kv";
+    return false;
+  }
+  const int G = nq / nkv;
+  if (d != 16 && d != 32 && d != 64 && d != 128) {
+    *why = "head_dim must be 16, 32, 64 or 128";
+    return false;
+  }
+  if (G > 16 || G * d > 8 * kAttnThreads) {
+    *why = "at most 16 query heads per kv head (and n_q/n_kv * head_dim <= 1024)";
+    return false;
+  }
+  if (n_ctx < 1 || n_ctx > int64_t(INT32_MAX)) {
+    *why = "n_ctx must be in [1, 2^31 - 1]";
+    return false;
+  }
+  const size_t gp = (size_t(G) + 3) & ~size_t(3);
+  const size_t ks = d >= 32 ? size_t(d) : size_t(d) + 16;
+  const size_t tiles = size_t(G) * d + size_t(kAttnBufs) * kTileD * ks +
+                       size_t(kAttnBufs) * kTileD * d + kTileD * gp + 2 * size_t(d);
+  if (sizeof(float) * std::max<size_t>(tiles, size_t(G) * nsplit) > size_t(kMaxAttnSmem)) {
+    *why = "shape needs more shared memory than the decode attention kernel has";
+    return false;
+  }
+  return true;
+}
+
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) {
   const int G = a.nq / a.nkv;
   if (G * a.nkv != a.nq || G * a.d > 8 * kAttnThreads || G > 16) return cudaErrorInvalidValue;

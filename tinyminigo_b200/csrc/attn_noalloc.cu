@@ -19,7 +19,10 @@
 //  * kScratchBytes (4 MiB) bounds the partials; larger requests are rejected
 //    before anything is enqueued.
 //  * The first call on a device does the setup (cudaGetSymbolAddress, which
-//    also loads this module); make it before any stream capture.
+//    also loads this module); make it before any stream capture.  Only a
+//    successful lookup is kept: a failed one is tried again on the next
+//    call.  The address belongs to the device's primary context (the one
+//    the CUDA runtime uses), for the life of the process.
 //  * The tickets must be zero when the attention kernel starts: static
 //    storage starts zeroed, the kernel's last split of each head resets its
 //    ticket, and every call also zeroes them (with the position word) in a
@@ -45,17 +48,20 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 
-std::once_flag g_once[kMaxDevices];
-void* g_addr[kMaxDevices];
-cudaError_t g_setup_err[kMaxDevices];
+std::mutex g_mu[kMaxDevices];
+void* g_addr[kMaxDevices];  // non-null once the lookup on that device succeeded
 
 // The scratch address on `device`, which must be the current device.
 cudaError_t scratch_on(int device, unsigned char** out) {
-  std::call_once(g_once[device], [device] {
-    g_setup_err[device] = cudaGetSymbolAddress(&g_addr[device], g_scratch);
-  });
+  std::lock_guard<std::mutex> lk(g_mu[device]);
+  if (!g_addr[device]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);
+    if (e != cudaSuccess) return e;
+    g_addr[device] = p;
+  }
   *out = static_cast<unsigned char*>(g_addr[device]);
-  return g_setup_err[device];
+  return cudaSuccess;
 }
 
 // The per-call state the attention kernel expects at its start: the query
@@ -76,6 +82,7 @@ int attn_decode_noalloc(int device, int num_sms, cudaStream_t s, const float* q,
   }
   const int G = n_q / n_kv;
   const int nsplit = attn_decode_nsplit(n_kv, 1, n_ctx, num_sms);
+  if (!attn_decode_shape_ok(n_q, n_kv, head_dim, n_ctx, nsplit, why)) return 1;
   const size_t part_bytes = size_t(n_kv) * nsplit * G * (head_dim + 2) * sizeof(float);
   if (n_kv > kMaxTickets || part_bytes > kScratchBytes - kHeaderBytes) {
     *why = "needs " + std::to_string(part_bytes + kHeaderBytes) + " bytes of scratch (" +

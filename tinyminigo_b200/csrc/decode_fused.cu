@@ -2,40 +2,42 @@
 // (src/model.rs:631-656: forward_token, src/model.rs:392-491, then argmax,
 // src/tensor.rs:1063-1073) in ONE persistent kernel.
 //
-// One CTA per SM (cooperative launch), 9 warps:
+// One CTA per SM (cooperative launch), three warpgroups:
 //  * a producer warp streams, in consumption order, every weight row this
 //    CTA needs for all n_steps tokens -- q/k/v, o, gate/up, down of each
 //    layer, then the LM head -- through a ring of 32 KB shared-memory stages
 //    with cp.async.bulk (TMA) and mbarriers.  Weights never depend on
 //    activations, so the stream runs ahead of the math across phase and
-//    token boundaries.  Further ahead still, it prefetches the rows of later
-//    stages into L2 (cp.async.bulk.prefetch), so HBM keeps streaming while
-//    the consumers sit in attention or at a grid barrier, and the ring
-//    refills from L2 afterwards.
-//  * eight consumer warps run the phases of each layer, each followed by a
-//    grid barrier (bounded spin; a barrier that gives up sets the error word
-//    and every CTA leaves):
+//    token boundaries.  (An optional L2 prefetch of the stages past the
+//    ring while the consumers sit in the attention chain exists for
+//    measurement; it is off by default.)
+//  * eight consumer warps run the phases of each layer:
 //      QKV   rmsnorm(x) . Wqkv^T; RoPE on q and k, k/v appended at pos
-//      ATTN  split-KV attention per (kv head, split); the last split of a
-//            head to finish merges the partials into the attention output
+//      ATTN  split-KV attention per (kv head, split); the owner of a head's
+//            first split merges the partials into the attention output
 //      O     att . Wo^T              -> x += ...
 //      GU    rmsnorm(x) . Wgate^T, Wup^T -> act = silu(g) * u
 //      DOWN  act . Wdown^T           -> x += ...
-//    then HEAD: rmsnorm(x) . Wlm^T -> logits + per-CTA argmax; after one more
-//    barrier every CTA reduces the argmax (the same token everywhere), CTA 0
-//    records it, and the next token starts.
+//    then HEAD: rmsnorm(x) . Wlm^T -> logits + per-CTA argmax.
+//  * Between phases CTAs exchange activations as tagged {value, tag}
+//    words (see ll_store): a reader polls the words it needs until each
+//    carries the producing phase's tag, so no grid barrier sits inside a
+//    token.  One grid barrier per token (after HEAD) publishes the argmax
+//    partials and the cache rows appended during the step; every CTA then
+//    reduces the argmax (the same token everywhere), CTA 0 records it, and
+//    the next token starts.  Every wait (mbarrier, tag poll, grid barrier)
+//    is bounded in time and sets the error word instead of hanging.
 // Inside a GEMV phase each warp works alone: it waits for a stage, dots its
-// row (or K segment of a row) against the input it holds in registers and
-// parks the sum in shared memory; one epilogue at the end of the phase
-// combines the K segments and applies the phase's output step.  Residual
-// rows are updated with one red.add each (each row has a single writer per
-// phase, so the result is x + y exactly, as with a plain add).
+// K segment of the stage's rows against the input it holds in registers and
+// parks the partial sums in shared memory; one epilogue at the end of the
+// phase combines the K segments in warp order and applies the phase's
+// output step.
 // Row groups of a phase are dealt to CTAs round-robin with a rotating offset
 // so every CTA streams the same number of bytes per token within one group.
 // QKV groups pair rows j and j + d/2 of one q or k head (RoPE partners), so
 // the rotation and the KV append happen in the QKV epilogue.
 // All arithmetic is f32 with BF16 weights widened exactly, as in the
-// separate kernels; cross-CTA activations are read through L2 (ld.cg).
+// separate kernels.
 #include <math.h>
 
 #include "common.cuh"
@@ -274,6 +276,7 @@ struct Shared {
   unsigned long long best[kCWarps];
   float m_s[8], l_s[8], alpha_s[8];
   int fail[2];  // a poll gave up (indexed by the parity of the poll count)
+  unsigned long long poll_ns;  // limit of one tag poll
   int gen_ok;
   volatile int abort;      // stop issuing / waiting (error or early end)
   volatile int issued;     // producer: stages issued so far
@@ -302,7 +305,7 @@ __device__ bool grid_sync(const FusedArgs& a, unsigned int& target, Shared& S,
       unsigned int spins = 0;
       while (int(ld_acquire(a.bar) - target) < 0) {
         if ((++spins & 255) == 0) {
-          if (ld_acquire(a.bar + 2) != 0 || global_ns() - t0 > kWaitNs) {
+          if (ld_acquire(a.bar + 2) != 0 || global_ns() - t0 > S.poll_ns) {
             ok = 0;
             break;
           }
@@ -546,7 +549,7 @@ __device__ __noinline__ bool ll_gather(float* dst, const unsigned long long* src
       }
     }
     if (!need) break;
-    if ((++spins & 15) == 0 && (ld_acquire(abort_word) != 0 || global_ns() - t0 > kWaitNs)) {
+    if ((++spins & 15) == 0 && (ld_acquire(abort_word) != 0 || global_ns() - t0 > S.poll_ns)) {
       ok = false;
       break;
     }
@@ -597,7 +600,7 @@ __device__ __forceinline__ bool ll_gather3(const LLRange* r, int nr, uint32_t ta
       }
     }
     if (!need) break;
-    if ((++spins & 15) == 0 && (ld_acquire(abort_word) != 0 || global_ns() - t0 > kWaitNs)) {
+    if ((++spins & 15) == 0 && (ld_acquire(abort_word) != 0 || global_ns() - t0 > S.poll_ns)) {
       ok = false;
       break;
     }
@@ -1189,6 +1192,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
     S.streaming = 0;
     S.in_attn = 0;
     S.fail[0] = S.fail[1] = 0;
+    S.poll_ns = a.poll_ns ? a.poll_ns : kWaitNs;
     mbar_fence_init();
   }
   __syncthreads();
@@ -1282,6 +1286,9 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
       // S.ssq; the 1/rms factor goes on each row's dot product in the
       // epilogue); x for HEAD (normalised per warp); att for O; act for DOWN
       const float* src = x_s;
+      // the tag this phase's input carries (a never-written one in the
+      // failure-path test)
+      const uint32_t want = step == 0 && p == a.stall_phase ? (tag - 1u) ^ 0x80000000u : tag - 1u;
       if (ph == PH_QKV && l == 0) {
         cp_async_wait_all();  // nw_s (staged at the step's start)
         csync();
@@ -1310,18 +1317,17 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
         if (lane == 0) S.ssq[warp] = ss;
         csync();
       } else if (ph == PH_O) {
-        ok = ll_gather(asm_, ll_mine(a.att_ll, a.nq * a.d, a.ll_rep), a.nq * a.d, tag - 1u,
+        ok = ll_gather(asm_, ll_mine(a.att_ll, a.nq * a.d, a.ll_rep), a.nq * a.d, want,
                        a.bar + 2, S, gc, true);
         if (threadIdx.x == 0) S.in_attn = 0;  // the attention chain ends with att here
         src = asm_;
       } else if (ph == PH_DOWN) {
-        ok = ll_gather(asm_, ll_mine(a.act_ll, a.I, a.ll_rep), a.I, tag - 1u, a.bar + 2, S, gc,
-                       true);
+        ok = ll_gather(asm_, ll_mine(a.act_ll, a.I, a.ll_rep), a.I, want, a.bar + 2, S, gc, true);
         src = asm_;
       } else {
         // x after the phase just before: the previous layer's DOWN (QKV,
         // HEAD) or this layer's O (GU)
-        ok = ll_gather(x_s, ll_mine(a.x_ll, a.h, a.ll_rep), a.h, tag - 1u, a.bar + 2, S, gc, true);
+        ok = ll_gather(x_s, ll_mine(a.x_ll, a.h, a.ll_rep), a.h, want, a.bar + 2, S, gc, true);
         cp_async_wait_all();  // nw_s (staged a phase or more ago)
         if (ok && ph != PH_HEAD) {
           // nw_s <- nw_s * x (same layout) and each warp's share of sum(x^2)

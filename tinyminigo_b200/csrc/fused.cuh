@@ -55,6 +55,13 @@ struct FusedArgs {
   StreamState st{};
   int n_steps = 0;
   int32_t* err = nullptr;
+  // limit of the tag polls and the grid barrier (ns; 0: the 2 s default)
+  unsigned long long poll_ns = 0;
+  // failure-path test only (-1: off): in the first step, the input gather of
+  // phase stall_phase (a GEMV phase that gathers: O, GU, DOWN, a later
+  // layer's QKV, HEAD) waits for a tag no phase writes, so the poll gives up
+  // after poll_ns and the launch ends with the timeout error word
+  int stall_phase = -1;
   // diagnostics: [grid][L * 5 + 1][12] records of the first step per CTA
   // and phase (globaltimer ns: work done, barrier passed, producer's first
   // and last issue, input ready, GEMV done, first stage ready; the group

@@ -134,6 +134,9 @@ struct AttnDecodeArgs {
 };
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);
 int attn_decode_nsplit(int nkv, int M, int64_t cap, int num_sms);
+// Whether launch_attn_decode takes this op-level shape (n_q, n_kv, head dim,
+// context length, split count); *why says why not.
+bool attn_decode_shape_ok(int nq, int nkv, int d, int64_t n_ctx, int nsplit, std::string* why);
 // Decode attention on the static per-device scratch (attn_noalloc.cu):
 // enqueues on s, allocates nothing.  0 = enqueued; 1 bad device, 2 too
 // large for the scratch, 3 CUDA error; *why says which.

@@ -1,10 +1,22 @@
 // NCCL over NVLink / NVSwitch for the tensor-parallel decode (one allreduce
 // after o_proj and one after down_proj per layer; an allgather of the
 // vocab-split logits).
+//
+// The communicator is non-blocking (ncclConfig_t.blocking = 0): every NCCL
+// call that reports ncclInProgress is polled with ncclCommGetAsyncError
+// against a deadline, so a rank whose peers never join (or never enqueue)
+// gets TMG_ERR_NCCL back instead of blocking in the host call for good.
+// The deadline is TMG_TP_TIMEOUT_S seconds (default 300); on expiry the
+// communicator is aborted (ncclCommAbort) and is unusable afterwards.
+// A collective already running on the GPU waits for its peers there: that
+// wait is NCCL's, not bounded by this file.
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <chrono>
+#include <cstdlib>
 #include <cstring>
+#include <thread>
 
 #include "common.cuh"
 #include "tp.h"
@@ -16,7 +28,9 @@ namespace {
 struct NcclApi {
   void* h = nullptr;
   ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
-  ncclResult_t (*init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*init_rank_config)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+  ncclResult_t (*get_async_error)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*abort)(ncclComm_t) = nullptr;
   ncclResult_t (*destroy)(ncclComm_t) = nullptr;
   ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                              cudaStream_t) = nullptr;
@@ -36,13 +50,17 @@ NcclApi& api() {
     if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
     if (h) {
       a.get_unique_id = reinterpret_cast<decltype(a.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
-      a.init_rank = reinterpret_cast<decltype(a.init_rank)>(dlsym(h, "ncclCommInitRank"));
+      a.init_rank_config =
+          reinterpret_cast<decltype(a.init_rank_config)>(dlsym(h, "ncclCommInitRankConfig"));
+      a.get_async_error =
+          reinterpret_cast<decltype(a.get_async_error)>(dlsym(h, "ncclCommGetAsyncError"));
+      a.abort = reinterpret_cast<decltype(a.abort)>(dlsym(h, "ncclCommAbort"));
       a.destroy = reinterpret_cast<decltype(a.destroy)>(dlsym(h, "ncclCommDestroy"));
       a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(h, "ncclAllReduce"));
       a.all_gather = reinterpret_cast<decltype(a.all_gather)>(dlsym(h, "ncclAllGather"));
       a.err_string = reinterpret_cast<decltype(a.err_string)>(dlsym(h, "ncclGetErrorString"));
-      if (a.get_unique_id && a.init_rank && a.destroy && a.all_reduce && a.all_gather &&
-          a.err_string)
+      if (a.get_unique_id && a.init_rank_config && a.get_async_error && a.abort && a.destroy &&
+          a.all_reduce && a.all_gather && a.err_string)
         a.h = h;
     }
   }
@@ -62,14 +80,50 @@ __global__ void interleave_kernel(const float* __restrict__ g, int64_t n_local, 
   }
 }
 
+double tp_timeout_s() {
+  const char* e = getenv("TMG_TP_TIMEOUT_S");
+  const double v = e ? atof(e) : 0.0;
+  return v > 0.0 ? v : 300.0;
+}
+
 }  // namespace
 
 struct TpComm {
   ncclComm_t comm = nullptr;
   int rank = 0, world = 1;
+  bool aborted = false;
   float* gather_tmp = nullptr;
   size_t gather_cap = 0;
 };
+
+namespace {
+
+// r is the result of an NCCL call on t->comm: while it is ncclInProgress,
+// poll the communicator until the call has completed or the deadline has
+// passed (then abort the communicator and report ncclInProgress).
+ncclResult_t settle(TpComm* t, ncclResult_t r, double timeout_s) {
+  if (r != ncclInProgress) return r;
+  NcclApi& a = api();
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    ncclResult_t st = ncclSuccess;
+    const ncclResult_t q = a.get_async_error(t->comm, &st);
+    if (q != ncclSuccess) return q;
+    if (st != ncclInProgress) return st;
+    const double el =
+        std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (el > timeout_s) {
+      a.abort(t->comm);
+      t->aborted = true;
+      return ncclInProgress;
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(200));
+  }
+}
+
+cudaError_t as_cuda(ncclResult_t r) { return r == ncclSuccess ? cudaSuccess : cudaErrorUnknown; }
+
+}  // namespace
 
 int tp_unique_id(uint8_t id[128]) {
   NcclApi& a = api();
@@ -92,9 +146,19 @@ TpComm* tp_create(const uint8_t id[128], int rank, int world, std::string& err) 
   TpComm* t = new TpComm();
   t->rank = rank;
   t->world = world;
-  ncclResult_t r = a.init_rank(&t->comm, world, u, rank);
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  const double limit = tp_timeout_s();
+  ncclResult_t r = settle(t, a.init_rank_config(&t->comm, world, u, rank, &cfg), limit);
+  if (r == ncclInProgress) {
+    err = "ncclCommInitRankConfig: the other ranks did not join within " +
+          std::to_string(int(limit)) + " s (communicator aborted)";
+    delete t;
+    return nullptr;
+  }
   if (r != ncclSuccess) {
-    err = std::string("ncclCommInitRank: ") + a.err_string(r);
+    err = std::string("ncclCommInitRankConfig: ") + a.err_string(r);
+    if (t->comm) a.abort(t->comm);
     delete t;
     return nullptr;
   }
@@ -103,24 +167,23 @@ TpComm* tp_create(const uint8_t id[128], int rank, int world, std::string& err) 
 
 void tp_destroy(TpComm* t) {
   if (!t) return;
-  if (t->comm) api().destroy(t->comm);
+  if (t->comm && !t->aborted) api().destroy(t->comm);
   if (t->gather_tmp) cudaFree(t->gather_tmp);
   delete t;
 }
 
 cudaError_t tp_allreduce_sum(TpComm* t, float* buf, int64_t n, cudaStream_t s) {
-  if (!t) return cudaErrorInvalidValue;
-  ncclResult_t r = api().all_reduce(buf, buf, size_t(n), ncclFloat32, ncclSum, t->comm, s);
-  return r == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
+  if (!t || t->aborted) return cudaErrorInvalidValue;
+  return as_cuda(settle(t, api().all_reduce(buf, buf, size_t(n), ncclFloat32, ncclSum, t->comm, s),
+                        tp_timeout_s()));
 }
 
 cudaError_t tp_allgather_rows(TpComm* t, const float* local, int64_t n_local, float* out,
                               int64_t n_full, int M, cudaStream_t s) {
-  if (!t || n_full != n_local * t->world) return cudaErrorInvalidValue;
-  if (M == 1) {
-    ncclResult_t r = api().all_gather(local, out, size_t(n_local), ncclFloat32, t->comm, s);
-    return r == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
-  }
+  if (!t || t->aborted || n_full != n_local * t->world) return cudaErrorInvalidValue;
+  if (M == 1)
+    return as_cuda(settle(t, api().all_gather(local, out, size_t(n_local), ncclFloat32, t->comm, s),
+                          tp_timeout_s()));
   const size_t need = size_t(n_full) * M;
   if (t->gather_cap < need) {
     if (t->gather_tmp) cudaFree(t->gather_tmp);
@@ -129,8 +192,9 @@ cudaError_t tp_allgather_rows(TpComm* t, const float* local, int64_t n_local, fl
     TMG_CUDA_TRY(cudaMalloc(&t->gather_tmp, need * sizeof(float)));
     t->gather_cap = need;
   }
-  ncclResult_t r =
-      api().all_gather(local, t->gather_tmp, size_t(n_local) * M, ncclFloat32, t->comm, s);
+  const ncclResult_t r = settle(
+      t, api().all_gather(local, t->gather_tmp, size_t(n_local) * M, ncclFloat32, t->comm, s),
+      tp_timeout_s());
   if (r != ncclSuccess) return cudaErrorUnknown;
   interleave_kernel<<<296, 256, 0, s>>>(t->gather_tmp, n_local, t->world, M, out);
   return cudaGetLastError();

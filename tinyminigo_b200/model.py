@@ -185,9 +185,11 @@ class Model:
     @staticmethod
     def from_tensors(config: ModelConfig, tensors: dict, device: int = 0, tp=None) -> "Model":
         """Build from in-memory tensors keyed by HF name: BF16 bit patterns as
-        uint16 arrays (matrices must be BF16), norms as f32 or BF16."""
+        uint16 arrays (matrices must be BF16), norms as f32 or BF16.
+        `tensors` is a dict or an iterable of (name, array) pairs (each array
+        may be dropped once it has been uploaded)."""
         m = Model(config, device, tp)
-        for name, a in tensors.items():
+        for name, a in (tensors.items() if hasattr(tensors, "items") else tensors):
             a = np.ascontiguousarray(a)
             dtype = 1 if a.dtype == np.uint16 else 0
             if dtype == 0:
@@ -279,11 +281,12 @@ class Model:
         """Per-kernel-class device time (ms) and launches of n_steps greedy
         steps launched one kernel at a time with CUDA events between them."""
         t = np.ascontiguousarray(np.atleast_1d(np.asarray(tokens, np.uint32)))
-        ms = np.zeros(6, np.float64)
-        n = np.zeros(6, np.int64)
+        ms = np.zeros(8, np.float64)
+        n = np.zeros(8, np.int64)
         check(lib().tmg_profile_decode(self._h, cache._h, _ptr(t), n_steps, _ptr(ms), _ptr(n)),
               self._h, "profile_decode")
-        names = ["qkv_gemv", "attn_decode", "o_gemv", "gateup_gemv", "down_gemv", "lm_head"]
+        names = ["qkv_gemv", "attn_decode", "o_gemv", "gateup_gemv", "down_gemv", "lm_head",
+                 "allreduce", "allgather_step_end"]
         return {k: (float(ms[i]), int(n[i])) for i, k in enumerate(names)}
 
     def trace_decode(self, tokens, cache: "KvCache") -> list:

@@ -64,14 +64,15 @@ def tensor_specs(cfg: dict):
     return specs
 
 
-def make_weights(cfg: dict, seed: int, device: str = "cpu", std: float = 0.02) -> dict:
-    """BF16 bit patterns (numpy uint16) for every tensor, drawn in file order
-    from one torch Generator seeded with `seed` on `device`."""
+def iter_weights(cfg: dict, seed: int, device: str = "cpu", std: float = 0.02):
+    """(name, BF16 bit patterns as numpy uint16) for every tensor, drawn in
+    file order from one torch Generator seeded with `seed` on `device`, one
+    tensor at a time (a consumer that uploads and drops each holds one
+    tensor in host memory at most)."""
     import torch
 
     g = torch.Generator(device=device)
     g.manual_seed(seed)
-    out = {}
     for name, shape, kind in tensor_specs(cfg):
         if kind == "norm":
             t = torch.ones(shape, dtype=torch.bfloat16)
@@ -79,8 +80,12 @@ def make_weights(cfg: dict, seed: int, device: str = "cpu", std: float = 0.02) -
             t = torch.empty(shape, dtype=torch.float32, device=device)
             t.normal_(0.0, std, generator=g)
             t = t.to(torch.bfloat16)
-        out[name] = t.view(torch.int16).cpu().numpy().view(np.uint16)
-    return out
+        yield name, t.view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def make_weights(cfg: dict, seed: int, device: str = "cpu", std: float = 0.02) -> dict:
+    """iter_weights collected into a dict keyed by tensor name."""
+    return dict(iter_weights(cfg, seed, device, std))
 
 
 def bf16_to_f32(bits: np.ndarray) -> np.ndarray:
