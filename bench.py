@@ -627,6 +627,8 @@ def measure_c4(args, rank, world, local_rank, dist, steps, warmup, host_leg):
     per_gpu = (wbytes + kvb) / world
     gbs = per_gpu / (ms / 1e3 / G4) / 1e9
     extra = {"profile_pass_ms_per_token": round(prof_ms_tok, 4),
+             "profile_pass_ms_per_token_by_kernel": {k: round(v[0] / n_prof, 4)
+                                                     for k, v in prof.items() if v[1]},
              "allreduce_ms_per_token": round(ar_ms_tok, 4),
              "allreduces_per_token": int(prof["allreduce"][1] // n_prof),
              "allgather_step_end_ms_per_token": round(ag_ms_tok, 4)}
@@ -734,14 +736,99 @@ def run_c5(args, rank, world, local_rank):
     model.close()
 
 
+def run_c2i8(args, rank, world, local_rank):
+    """C2 with int8 layer weights (the reference's TMG_I8=1: per-row
+    quantized q/k/v/o/gate/up/down, BF16 LM head): 64-token prompt, 256
+    greedy tokens per step through the per-step graph of int8 GEMVs.  value
+    = decode tok/s on the device; roofline = algorithmic bytes per token
+    (int8 layer weights + row scales + BF16 LM head + KV) over the step
+    time.  Parity rides along: the first 8 greedy ids and the first-step
+    logits against the oracle's int8 model."""
+    import torch
+
+    if rank != 0:
+        return
+    torch.cuda.set_device(local_rank)
+    from tinyminigo_b200 import synth
+    from tinyminigo_b200.model import Model
+
+    cfg, w = make_c2("cuda")
+    os.environ["TMG_I8"] = "1"
+    try:
+        model = Model.from_tensors(model_config(cfg), w, device=local_rank)
+    finally:
+        del os.environ["TMG_I8"]
+    prompt = synth.random_prompt(cfg["vocab_size"], PROMPT, 7)
+    cache = model.new_cache(PROMPT + GEN + 8)
+    logits = model.forward_seq(prompt, cache)
+    t0_tok = int(np.argmax(logits))
+    stream = torch.cuda.ExternalStream(model.stream_handle(), device=local_rank)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def step():
+        cache.truncate(PROMPT)
+        model.decode([t0_tok], cache, GEN, wait=False)
+
+    for _ in range(args.warmup):
+        step()
+    model.sync()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        model.sync()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    cache.truncate(PROMPT)
+    gpu_ids = [t0_tok] + [int(t) for t in model.decode([t0_tok], cache, 8)[0]]
+    h, L, I, V = cfg["hidden_size"], cfg["num_hidden_layers"], cfg["intermediate_size"], cfg["vocab_size"]
+    qd = cfg["num_attention_heads"] * cfg["head_dim"]
+    kd = cfg["num_key_value_heads"] * cfg["head_dim"]
+    layer_b = (qd + 2 * kd) * h + h * qd + 3 * I * h + 4 * (qd + 2 * kd + 2 * h + 2 * I)
+    kvb = L * (2 * kd * 4 * (PROMPT + GEN / 2) + 2 * kd * 4)
+    tok_b = L * layer_b + 2 * V * h + kvb
+    gbs = tok_b / (ms / 1e3 / GEN) / 1e9
+    peak, peak_kind = peaks()
+    extra = {}
+    if not args.no_cpu_baseline:
+        from oracle import oracle
+
+        om = oracle.OracleModel(cfg, w, i8=True)
+        ref = om.forward_seq(prompt)
+        ids = [oracle.argmax(ref)]
+        for _ in range(8):
+            ids.append(oracle.argmax(om.forward_token(ids[-1])))
+        diff = np.abs(logits - ref)
+        extra["parity"] = {"checker": "oracle int8 model (TMG_I8=1 arms)",
+                           "first_step_max_abs_logit_diff": round(float(diff.max()), 6),
+                           "first_step_logits_within_1e-3_rel_1e-2_abs":
+                               bool(np.all(diff <= 1e-2 + 1e-3 * np.abs(ref))),
+                           "greedy_ids_compared": len(ids), "greedy_ids_equal": gpu_ids == ids}
+    res = base_line(args, world, "decode_tok_s", GEN / (ms / 1e3), "tok/s", ms,
+                    {"workload": "c2 with int8 layer weights (TMG_I8=1): 1B-class, tied, "
+                                 "64-token prompt, greedy 256 decode", "global_batch": 1,
+                     "seq_len": PROMPT + GEN, "parallelism": "single GPU"}, "weak", clk.summary(),
+                    roofline={"bound": "hbm", "kernel": "decode step (int8 GEMVs + BF16 LM head)",
+                              "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                              "frac": round(gbs / peak, 4), "traffic": None,
+                              "algorithmic_bytes_per_token": int(tok_b), "peak_kind": peak_kind},
+                    **extra)
+    res["dtype"] = "int8 weights, f32 activations, i32 dots"
+    print(json.dumps(res), flush=True)
+    cache.close()
+    model.close()
+
+
 def run_attn(args, rank, world, local_rank):
     """Attention kernels alone, through the op-level C ABI (rank 0): decode
-    attention of one stream over 131072 cached positions (32 query / 8 kv
-    heads, head dim 64: 537 MB of f32 K/V, larger than L2, flushed between
-    runs) and causal prefill attention of 2048 rows (the c3 shape).  value =
-    the decode kernel's algorithmic GB/s (K and V read once); the prefill's
-    TFLOP/s rides along.  TMG_ATTN_TILED=1 selects the shared-memory tiled
-    decode kernel instead of the register-streaming one."""
+    attention of one stream over --attn-ctx cached positions (default 131072;
+    32 query / 8 kv heads, head dim 64: 537 MB of f32 K/V, larger than L2,
+    flushed between runs) and causal prefill attention of 2048 rows (the c3
+    shape).  value = the decode kernel's algorithmic GB/s (K and V read
+    once); the prefill's TFLOP/s rides along.  The decode kernel is the
+    TMA-staged one; TMG_ATTN_KERNEL=reg or tiled selects the register-
+    streaming or the cp.async tiled kernel instead, for comparison."""
     import ctypes
 
     import torch
@@ -774,7 +861,7 @@ def run_attn(args, rank, world, local_rank):
             ts.append(e0.elapsed_time(e1))
         return statistics.median(ts)
 
-    n_ctx = 131072
+    n_ctx = args.attn_ctx
     q = torch.randn(nq * d, device="cuda", generator=g)
     k = torch.randn(n_ctx, nkv * d, device="cuda", generator=g)
     v = torch.randn(n_ctx, nkv * d, device="cuda", generator=g)
@@ -794,14 +881,16 @@ def run_attn(args, rank, world, local_rank):
     gbs = dec_bytes / (ms_dec / 1e3) / 1e9
     pf_flop = 4 * d * nq * T * (T + 1) // 2
     peak, peak_kind = peaks()
-    tiled = os.environ.get("TMG_ATTN_TILED", "0") == "1"
+    kern = {"r": "attn_decode_reg_kernel", "t": "attn_decode_kernel"}.get(
+        os.environ.get("TMG_ATTN_KERNEL", "tma")[:1], "attn_decode_tma_kernel<64>")
+    if os.environ.get("TMG_ATTN_TILED", "0") == "1":
+        kern = "attn_decode_kernel"
     res = base_line(args, world, "decode_attention_gbs", gbs, "GB/s", ms_dec,
-                    {"workload": "attention kernels: decode over 131072 positions (32/8 heads, "
+                    {"workload": f"attention kernels: decode over {n_ctx} positions (32/8 heads, "
                                  "d 64, one stream); causal prefill of 2048 rows",
                      "global_batch": 1, "seq_len": n_ctx, "parallelism": "single GPU",
                      "l2": "flushed between runs (256 MB write)"}, "weak", clk.summary(),
-                    roofline={"bound": "hbm", "kernel": "attn_decode_kernel" if tiled
-                              else "attn_decode_reg_kernel", "achieved": round(gbs, 1),
+                    roofline={"bound": "hbm", "kernel": kern, "achieved": round(gbs, 1),
                               "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4),
                               "traffic": None, "peak_kind": peak_kind},
                     prefill_attention={"ms": round(ms_pf, 3),
@@ -927,13 +1016,16 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "attn"], default="c2",
+    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "attn", "c2i8"], default="c2",
                     help="c2 (default): the headline decode; c3: 2048-token prefill; "
                          "c4: 8B tensor-parallel decode over the ranks; c5: 16 streams at 32K "
-                         "context, sampled; attn: the attention kernels alone")
+                         "context, sampled; attn: the attention kernels alone; c2i8: c2 with "
+                         "int8 layer weights (TMG_I8=1)")
     ap.add_argument("--cpu-tokens", type=int, default=8)
     ap.add_argument("--c5-ctx", type=int, default=32768, help="c5: prompt length per stream")
     ap.add_argument("--c5-steps", type=int, default=256, help="c5: sampled steps")
+    ap.add_argument("--attn-ctx", type=int, default=131072,
+                    help="attn: cached positions of the decode attention")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-c4", action="store_true",
                     help="c2: leave out the tensor-parallel 8B block")
@@ -961,6 +1053,8 @@ def main():
         run_c5(args, rank, world, local_rank)
     elif args.workload == "attn":
         run_attn(args, rank, world, local_rank)
+    elif args.workload == "c2i8":
+        run_c2i8(args, rank, world, local_rank)
     else:
         run_ours(args, rank, world, local_rank)
 

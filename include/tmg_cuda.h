@@ -290,6 +290,22 @@ int tmg_op_gemv_wmat(tmg_ctx* ctx, const float* x, const tmg_wmat* w, int32_t M,
 /* matmul_batch_w_into, src/tensor.rs:573-792, over a handle: y[T, rows] =
  * x[T, cols] . W^T on the tcgen05 prefill GEMM (device pointers). */
 int tmg_op_gemm_wmat(tmg_ctx* ctx, const float* x, const tmg_wmat* w, int64_t T, float* y);
+/* Int8 weights: the reference's TMG_I8=1 (wmat_maybe_i8, src/model.rs:
+ * 57-76).  With TMG_I8=1 in the environment when a model's weights are
+ * first set, its layer matrices (q/k/v/o, gate/up/down) are quantized at
+ * upload and every forward runs the int8 path (the LM head and norms stay
+ * BF16 / f32, as there); single GPU only (tmg_tp_init + TMG_I8=1 is
+ * refused).  The two op entries below expose its kernels.
+ * WMat::quantize_i8, src/tensor.rs:282-297, of a BF16 [N, K] matrix:
+ * q[N, K] int8 and scales[N] (device pointers). */
+int tmg_op_quantize_i8(tmg_ctx* ctx, const uint16_t* w, int64_t N, int64_t K, int8_t* q,
+                       float* scales);
+/* The I8 arm of matmul_w_into, src/tensor.rs:341-357, for M <= 16 rows:
+ * each row of x[M, K] quantized (quantize_row_i8, src/tensor.rs:128-141),
+ * integer dots with q[N, K] (dot_i8, 146-170), y[M, N] = f32(dot) * s_x *
+ * scales[n].  K % 16 == 0, K <= 16384. */
+int tmg_op_gemv_i8(tmg_ctx* ctx, const float* x, const int8_t* q, const float* scales, int64_t N,
+                   int64_t K, int32_t M, float* y);
 /* rms_norm_into (mode 0, src/tensor.rs:969-977) or rms_norm_batch (mode 1,
  * 946-954) over `rows` rows of n. */
 int tmg_op_rmsnorm(tmg_ctx* ctx, const float* x, const float* w, float eps, int64_t n,

@@ -136,6 +136,10 @@ unsafe extern "C" {
     pub fn tmg_wmat_shape(w: *const TmgWmat, rows: *mut i64, cols: *mut i64) -> i32;
     pub fn tmg_op_gemv_wmat(ctx: *mut TmgCtx, x: *const f32, w: *const TmgWmat, m: i32, y: *mut f32) -> i32;
     pub fn tmg_op_gemm_wmat(ctx: *mut TmgCtx, x: *const f32, w: *const TmgWmat, t: i64, y: *mut f32) -> i32;
+    pub fn tmg_op_quantize_i8(ctx: *mut TmgCtx, w: *const u16, n: i64, k: i64, q: *mut i8,
+                              scales: *mut f32) -> i32;
+    pub fn tmg_op_gemv_i8(ctx: *mut TmgCtx, x: *const f32, q: *const i8, scales: *const f32, n: i64,
+                          k: i64, m: i32, y: *mut f32) -> i32;
     pub fn tmg_op_gemv_bf16(ctx: *mut TmgCtx, x: *const f32, w: *const u16, n: i64, k: i64, m: i32,
                             y: *mut f32) -> i32;
     pub fn tmg_op_gemm_bf16(ctx: *mut TmgCtx, x: *const f32, w: *const u16, n: i64, k: i64, t: i64,

@@ -56,7 +56,10 @@ class GreedyCheck:
             logits = om.forward_token(int(top[0]))
         return ids, margins, second, first
 
-    def agree(self, name, gpu, ref, margins, second):
+    def agree(self, name, gpu, ref, margins, second, near_tie=None):
+        """near_tie: the margin below which a flip is allowed (NEAR_TIE
+        unless a test states a wider one, with its reason)."""
+        tie = self.NEAR_TIE if near_tie is None else near_tie
         gpu = [int(t) for t in gpu]
         assert len(gpu) == len(ref), (len(gpu), len(ref))
         i = next((j for j, (a, b) in enumerate(zip(gpu, ref)) if a != b), None)
@@ -64,7 +67,7 @@ class GreedyCheck:
         _GREEDY_REPORT.append((name, len(ref), min(margins[:upto]), i))
         if i is None:
             return
-        assert margins[i] < self.NEAR_TIE and gpu[i] == second[i], (
+        assert margins[i] < tie and gpu[i] == second[i], (
             f"{name}: greedy diverged at step {i} (oracle margin {margins[i]:.2e}): gpu {gpu[i]} "
             f"vs oracle {ref[i]} (runner-up {second[i]})")
 

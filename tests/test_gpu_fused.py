@@ -161,3 +161,26 @@ def test_fused_head_dim_128_matches_oracle(orc, greedy):
     assert tr.shape[1] == 5 * 2 + 1
     c.close()
     m.close()
+
+
+def test_fused_8b_shape_matches_oracle(orc, greedy):
+    # the 8B-class kernel instance (hidden 4096, head dim 128, 32 / 8 heads,
+    # intermediate 14336: 4 rows per stage, the down rows one per stage, act
+    # gathered in two pieces), 2 layers of the C4 shape, 48 greedy steps
+    cfg = synth.with_layers(synth.CONFIGS["c4"], 2)
+    t = synth.make_weights(cfg, 44, device="cuda")
+    prompt = synth.random_prompt(cfg["vocab_size"], 40, 45)
+    steps = 48
+    ids, margins, second, first = greedy.oracle(orc.OracleModel(cfg, t), prompt, steps)
+    m = Model.from_tensors(cfg_obj(cfg), t)
+    out = generate(m, prompt, GenParams(max_tokens=steps))
+    greedy.agree("C4 shape, 2 layers (fused, 8B instance)", out.tokens, ids, margins, second)
+    c = m.new_cache(128)
+    tok0 = int(np.argmax(m.forward_seq(prompt, c)))
+    tr = m.trace_fused(tok0, c)  # the fused kernel ran for this shape
+    assert tr.shape[1] == 5 * 2 + 1
+    groups = tr[:, :, 7].astype(np.int64).sum(axis=0)
+    # QKV 6144 rows / 4, O 4096 / 4, GU 14336 / 2, DOWN 4096 / 1
+    assert list(groups[:5]) == [6144 // 4, 0, 4096 // 4, 14336 // 2, 4096]
+    c.close()
+    m.close()

@@ -111,6 +111,8 @@ SIGNATURES = {
     "tmg_wmat_shape": (_I, [_P, ctypes.POINTER(_I64), ctypes.POINTER(_I64)]),
     "tmg_op_gemv_wmat": (_I, [_P, _P, _P, _I32, _P]),
     "tmg_op_gemm_wmat": (_I, [_P, _P, _P, _I64, _P]),
+    "tmg_op_quantize_i8": (_I, [_P, _P, _I64, _I64, _P, _P]),
+    "tmg_op_gemv_i8": (_I, [_P, _P, _P, _P, _I64, _I64, _I32, _P]),
     "tmg_op_gemm_bf16": (_I, [_P, _P, _P, _I64, _I64, _I64, _P]),
     "tmg_op_rmsnorm": (_I, [_P, _P, _P, _F, _I64, _I64, _I32, _P]),
     "tmg_op_rope": (_I, [_P, _P, _I64, _I32, _I32, _I64, _F]),

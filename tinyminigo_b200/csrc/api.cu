@@ -37,6 +37,10 @@ struct Layer {
   uint16_t* wg = nullptr;    // [I, h]
   uint16_t* wu = nullptr;    // [I, h]
   uint16_t* wd = nullptr;    // [h, I]
+  // int8 weights (TMG_I8=1): the same matrices quantized per row, and
+  // their row scales (the BF16 pointers above are then null)
+  int8_t *qqkv = nullptr, *qo = nullptr, *qg = nullptr, *qu = nullptr, *qd = nullptr;
+  float *sqkv = nullptr, *so = nullptr, *sg = nullptr, *su = nullptr, *sd = nullptr;
   float* in_norm = nullptr;
   float* post_norm = nullptr;
   unsigned have = 0;  // bit per tensor
@@ -81,9 +85,21 @@ struct tmg_ctx {
   unsigned long long* ll = nullptr;  // its tagged exchange words (x, att, act, qkv)
   int fused_pf = 0;              // its stall-time L2 prefetch distance (stages; TMG_FUSED_PF)
   int fused_pf_pace = 0;         // cycles between those prefetches (TMG_FUSED_PF_PACE)
+  int fused_pf_mode = 0;         // when: 0 attention chain only, 1 ring full (TMG_FUSED_PF_MODE)
   int fused_rep = 4;             // copies of its x/att/act exchange words (TMG_FUSED_REP)
   int fused_stages = 4;          // its ring depth cap (0: all that fit; TMG_FUSED_STAGES)
   bool fused_ok = false;         // the fused batch-1 decode kernel takes this shape
+  // int8 layer weights (the reference's TMG_I8=1, read when the weights are
+  // allocated): BF16 staging for the load-time quantization, the quantized
+  // activation rows of the multi-stream GEMV, and the prefill's widened
+  // weights and accumulator
+  bool i8 = false;
+  uint16_t* i8_stage = nullptr;
+  int8_t* xq8 = nullptr;
+  float* xs8 = nullptr;
+  uint16_t* dq = nullptr;
+  size_t dq_cap = 0;
+  float* i8acc = nullptr;
   // failure-path test of the fused kernel (TMG_TEST_FUSED_STALL=<phase>,
   // TMG_TEST_FUSED_POLL_MS=<ms>): the context's next fused launch waits in
   // that phase for a tag nobody writes, with polls limited to that many ms
@@ -329,6 +345,21 @@ int upload_shard(tmg_ctx* c, const std::string& name, uint16_t* dst, const void*
   return upload_block(c, dst, static_cast<const uint16_t*>(host), full[1], r[0], r[1], r[2], r[3]);
 }
 
+// The same through the BF16 staging buffer, quantized on the device into
+// int8 rows at q with their scales (wmat_maybe_i8, src/model.rs:57-76).
+// Stream order keeps the staging buffer's next upload behind this
+// quantization.
+int upload_shard_i8(tmg_ctx* c, const std::string& name, int8_t* q, float* scales,
+                    const void* host, int64_t numel) {
+  int64_t r[4], full[2];
+  if (!tp_shard_rect(c->cfg, name, c->rank, c->world, r, full))
+    return fail(c, TMG_ERR_INVALID, "unknown tensor " + name);
+  int rc = upload_shard(c, name, c->i8_stage, host, numel);
+  if (rc) return rc;
+  CK(launch_quantize_w_i8(c->i8_stage, r[1], int(r[3]), q, scales, c->stream), "quantize");
+  return TMG_OK;
+}
+
 int set_tensor(tmg_ctx* c, const std::string& name, int32_t dtype, const void* host,
                int64_t numel) {
   if (!c->has_model) return fail(c, TMG_ERR_INVALID, "context has no model config");
@@ -367,30 +398,38 @@ int set_tensor(tmg_ctx* c, const std::string& name, int32_t dtype, const void* h
   const std::string suf = name.substr(dot + 1);
   Layer& Lw = c->layers[li];
   const int64_t ql = int64_t(c->nq) * d, kl = int64_t(c->nkv) * d;
+  const bool q8 = c->i8;
   if (suf == "self_attn.q_proj.weight") {
     Lw.have |= kHaveQ;
-    return upload_shard(c, name, Lw.wqkv, host, numel);
+    return q8 ? upload_shard_i8(c, name, Lw.qqkv, Lw.sqkv, host, numel)
+              : upload_shard(c, name, Lw.wqkv, host, numel);
   }
   if (suf == "self_attn.k_proj.weight") {
     Lw.have |= kHaveK;
-    return upload_shard(c, name, Lw.wqkv + ql * h, host, numel);
+    return q8 ? upload_shard_i8(c, name, Lw.qqkv + ql * h, Lw.sqkv + ql, host, numel)
+              : upload_shard(c, name, Lw.wqkv + ql * h, host, numel);
   }
   if (suf == "self_attn.v_proj.weight") {
     Lw.have |= kHaveV;
-    return upload_shard(c, name, Lw.wqkv + (ql + kl) * h, host, numel);
+    return q8 ? upload_shard_i8(c, name, Lw.qqkv + (ql + kl) * h, Lw.sqkv + ql + kl, host, numel)
+              : upload_shard(c, name, Lw.wqkv + (ql + kl) * h, host, numel);
   }
   if (suf == "self_attn.o_proj.weight") {
     Lw.have |= kHaveO;
-    return upload_shard(c, name, Lw.wo, host, numel);
+    return q8 ? upload_shard_i8(c, name, Lw.qo, Lw.so, host, numel)
+              : upload_shard(c, name, Lw.wo, host, numel);
   }
   if (suf == "mlp.gate_proj.weight" || suf == "mlp.up_proj.weight") {
     const bool gate = suf[4] == 'g';
     Lw.have |= gate ? kHaveG : kHaveU;
+    if (q8)
+      return upload_shard_i8(c, name, gate ? Lw.qg : Lw.qu, gate ? Lw.sg : Lw.su, host, numel);
     return upload_shard(c, name, gate ? Lw.wg : Lw.wu, host, numel);
   }
   if (suf == "mlp.down_proj.weight") {
     Lw.have |= kHaveD;
-    return upload_shard(c, name, Lw.wd, host, numel);
+    return q8 ? upload_shard_i8(c, name, Lw.qd, Lw.sd, host, numel)
+              : upload_shard(c, name, Lw.wd, host, numel);
   }
   if (suf == "input_layernorm.weight" || suf == "post_attention_layernorm.weight") {
     if ((rc = check_shape(c, name, numel, h))) return rc;
@@ -426,16 +465,45 @@ int alloc_model(tmg_ctx* c) {
   c->V_l = std::min<int64_t>(c->V_l, int64_t(c->V) - c->v_off);
   c->qkv_rows = (c->nq + 2 * c->nkv) * c->d;
   const int64_t h = c->h;
+  if (const char* e8 = getenv("TMG_I8")) c->i8 = std::strcmp(e8, "1") == 0;
+  if (c->i8 && c->world > 1)
+    return fail(c, TMG_ERR_INVALID, "int8 weights (TMG_I8=1) with tensor parallelism are not supported");
+  if (c->i8 && (h % 16 || (int64_t(c->nq) * c->d) % 16 || c->I % 16))
+    return fail(c, TMG_ERR_INVALID, "int8 weights need hidden, n_q * head_dim and intermediate % 16 == 0");
   c->layers.assign(c->L, Layer());
+  const int64_t qd = int64_t(c->nq) * c->d;
   for (auto& Lw : c->layers) {
-    CK(dalloc(c->allocs, &Lw.wqkv, size_t(c->qkv_rows) * h), "alloc weights");
-    CK(dalloc(c->allocs, &Lw.wo, size_t(h) * c->nq * c->d), "alloc weights");
-    CK(dalloc(c->allocs, &Lw.wg, size_t(c->I) * h), "alloc weights");
-    CK(dalloc(c->allocs, &Lw.wu, size_t(c->I) * h), "alloc weights");
-    CK(dalloc(c->allocs, &Lw.wd, size_t(h) * c->I), "alloc weights");
+    if (c->i8) {
+      CK(dalloc(c->allocs, &Lw.qqkv, size_t(c->qkv_rows) * h), "alloc weights");
+      CK(dalloc(c->allocs, &Lw.qo, size_t(h) * qd), "alloc weights");
+      CK(dalloc(c->allocs, &Lw.qg, size_t(c->I) * h), "alloc weights");
+      CK(dalloc(c->allocs, &Lw.qu, size_t(c->I) * h), "alloc weights");
+      CK(dalloc(c->allocs, &Lw.qd, size_t(h) * c->I), "alloc weights");
+      CK(dalloc(c->allocs, &Lw.sqkv, size_t(c->qkv_rows)), "alloc weights");
+      CK(dalloc(c->allocs, &Lw.so, size_t(h)), "alloc weights");
+      CK(dalloc(c->allocs, &Lw.sg, size_t(c->I)), "alloc weights");
+      CK(dalloc(c->allocs, &Lw.su, size_t(c->I)), "alloc weights");
+      CK(dalloc(c->allocs, &Lw.sd, size_t(h)), "alloc weights");
+      c->weight_bytes += (int64_t(c->qkv_rows) * h + h * qd + 3 * int64_t(c->I) * h) +
+                         4 * (int64_t(c->qkv_rows) + 2 * h + 2 * int64_t(c->I));
+    } else {
+      CK(dalloc(c->allocs, &Lw.wqkv, size_t(c->qkv_rows) * h), "alloc weights");
+      CK(dalloc(c->allocs, &Lw.wo, size_t(h) * qd), "alloc weights");
+      CK(dalloc(c->allocs, &Lw.wg, size_t(c->I) * h), "alloc weights");
+      CK(dalloc(c->allocs, &Lw.wu, size_t(c->I) * h), "alloc weights");
+      CK(dalloc(c->allocs, &Lw.wd, size_t(h) * c->I), "alloc weights");
+      c->weight_bytes += 2 * (int64_t(c->qkv_rows) * h + h * qd + 3 * int64_t(c->I) * h);
+    }
     CK(dalloc(c->allocs, &Lw.in_norm, size_t(h)), "alloc weights");
     CK(dalloc(c->allocs, &Lw.post_norm, size_t(h)), "alloc weights");
-    c->weight_bytes += 2 * (int64_t(c->qkv_rows) * h + h * c->nq * c->d + 3 * int64_t(c->I) * h);
+  }
+  if (c->i8) {
+    // staging of one BF16 matrix (the largest of a layer) for quantization
+    const size_t most = std::max<size_t>({size_t(c->qkv_rows) * h, size_t(h) * qd, size_t(c->I) * h});
+    CK(dalloc(c->allocs, &c->i8_stage, most), "alloc staging");
+    const int64_t kmax = std::max<int64_t>({h, qd, int64_t(c->I)});
+    CK(dalloc(c->allocs, &c->xq8, size_t(kMaxStreams) * kmax), "alloc scratch");
+    CK(dalloc(c->allocs, &c->xs8, size_t(kMaxStreams)), "alloc scratch");
   }
   CK(dalloc(c->allocs, &c->embed, size_t(c->V) * h), "alloc weights");
   CK(dalloc(c->allocs, &c->final_norm, size_t(h)), "alloc weights");
@@ -461,9 +529,11 @@ int alloc_model(tmg_ctx* c) {
      "alloc scratch");
   CK(dalloc(c->allocs, &c->bar, fused_bar_words()), "alloc scratch");
   CK(zero_sync(c, c->bar, fused_bar_words() * sizeof(unsigned int)), "memset");
-  c->fused_ok = c->world == 1 && fused_supported(c->h, c->nq, c->nkv, c->d, c->I, c->V_l, c->num_sms);
+  c->fused_ok = c->world == 1 && !c->i8 &&
+                fused_supported(c->h, c->nq, c->nkv, c->d, c->I, c->V_l, c->num_sms);
   if (const char* pf = getenv("TMG_FUSED_PF")) c->fused_pf = atoi(pf);
   if (const char* pp = getenv("TMG_FUSED_PF_PACE")) c->fused_pf_pace = atoi(pp);
+  if (const char* pm = getenv("TMG_FUSED_PF_MODE")) c->fused_pf_mode = atoi(pm);
   if (const char* ns = getenv("TMG_FUSED_STAGES")) c->fused_stages = atoi(ns);
   if (const char* ts = getenv("TMG_TEST_FUSED_STALL")) {
     // only a GEMV phase that gathers its input: O, GU, DOWN (p % 5 = 2, 3,
@@ -493,10 +563,12 @@ int ensure_prefill(tmg_ctx* c, int64_t T) {
   const int64_t Tc = std::min<int64_t>(T, kPrefillChunk);
   if (c->pf_cap >= Tc) return TMG_OK;
   for (void* p : {(void*)c->X, (void*)c->Xn, (void*)c->QKV, (void*)c->ATT, (void*)c->G,
-                  (void*)c->U, (void*)c->d_tok})
+                  (void*)c->U, (void*)c->d_tok, (void*)c->i8acc})
     if (p) cudaFree(p);
+  c->i8acc = nullptr;
   c->pf_cap = 0;
   std::vector<void*> tmp;
+  if (c->i8) CK(dalloc(tmp, &c->i8acc, size_t(Tc) * c->h), "alloc prefill");
   CK(dalloc(tmp, &c->X, size_t(Tc) * c->h), "alloc prefill");
   CK(dalloc(tmp, &c->Xn, size_t(Tc) * c->h), "alloc prefill");
   CK(dalloc(tmp, &c->QKV, size_t(Tc) * c->qkv_rows), "alloc prefill");
@@ -531,6 +603,30 @@ cudaError_t gemm(tmg_ctx* c, const float* x, const uint16_t* w, int64_t T, int64
     return launch_gemm_tc(c->sp_hi, c->sp_lo, w, T, N, K, y, ldy, acc, c->d_err, c->stream);
   }
   return launch_gemm_simt(x, w, T, N, K, y, ldy, acc, c->stream);
+}
+
+// The prefill GEMM of one layer matrix: BF16 as is, or (TMG_I8=1) the int8
+// rows widened to BF16 (exact) for the tensor cores, then scaled per row
+// (matmul_batch_w_into's I8 writeback: acc * scale[o], src/tensor.rs:
+// 736-738), and added into y when acc.
+cudaError_t gemm_layer(tmg_ctx* c, const float* x, const uint16_t* w, const int8_t* q,
+                       const float* sc, int64_t T, int64_t N, int64_t K, float* y, int64_t ldy,
+                       bool acc) {
+  if (!q) return gemm(c, x, w, T, N, K, y, ldy, acc);
+  const size_t n = size_t(N) * size_t(K);
+  if (c->dq_cap < n) {
+    TMG_CUDA_TRY(cudaStreamSynchronize(c->stream));
+    if (c->dq) cudaFree(c->dq);
+    c->dq = nullptr;
+    c->dq_cap = 0;
+    TMG_CUDA_TRY(cudaMalloc(&c->dq, n * 2));
+    c->dq_cap = n;
+  }
+  TMG_CUDA_TRY(launch_widen_i8(q, n, c->dq, c->stream));
+  float* tmp = (acc || ldy != N) ? c->i8acc : y;
+  if (tmp == nullptr) return cudaErrorInvalidValue;
+  TMG_CUDA_TRY(gemm(c, x, c->dq, T, N, K, tmp, N, false));
+  return launch_scale_rows(tmp, T, N, sc, y, ldy, acc, c->stream);
 }
 
 // GEMV with an optional fused prologue; falls back to separate embedding /
@@ -615,8 +711,39 @@ cudaError_t enqueue_forward(tmg_ctx* c, tmg_kv* kv, const StreamState& st, bool 
   };
   const float eps = c->cfg.rms_norm_eps;
   const bool tp = c->world > 1;
+  // an int8 GEMV of this forward (TMG_I8=1): x (RMSNorm'd by norm_w when
+  // given) quantized per row, integer dots, y (+)= the scaled result
+  auto gemv8 = [&](const int8_t* q, const float* sc, const int8_t* q2, const float* sc2,
+                   const float* x, const float* norm_w, float* y, int64_t ldy, int64_t N, int K,
+                   GemvEpi epi) {
+    GemvI8Args a;
+    a.q = q;
+    a.scales = sc;
+    a.q2 = q2;
+    a.scales2 = sc2;
+    a.x = x;
+    a.norm_w = norm_w;
+    a.eps = eps;
+    a.norm_mode = 0;
+    a.xq = c->xq8;
+    a.xs = c->xs8;
+    a.y = y;
+    a.ldy = ldy;
+    a.N = N;
+    a.K = K;
+    a.M = M;
+    a.err = c->d_err;
+    return launch_gemv_i8(a, epi, c->stream, pdl, c->num_sms);
+  };
   for (int l = 0; l < c->L; ++l) {
     const Layer& Lw = c->layers[l];
+    if (c->i8) {
+      B();
+      if (l == 0) TMG_CUDA_TRY(launch_embed(c->embed, st.token, M, c->h, c->x, c->stream));
+      TMG_CUDA_TRY(gemv8(Lw.qqkv, Lw.sqkv, nullptr, nullptr, c->x, Lw.in_norm, c->qkv,
+                         c->qkv_rows, c->qkv_rows, c->h, EPI_STORE));
+      E(0);
+    }
     GemvArgs A;
     A.w = Lw.wqkv;
     A.N = c->qkv_rows;
@@ -628,7 +755,9 @@ cudaError_t enqueue_forward(tmg_ctx* c, tmg_kv* kv, const StreamState& st, bool 
     A.eps = eps;
     A.norm_mode = 0;
     A.trace = tc.take(0);
-    if (l == 0) {
+    if (c->i8) {
+      // done above
+    } else if (l == 0) {
       A.embed = c->embed;
       A.tokens = st.token;
       A.x_out = c->x;
@@ -659,6 +788,7 @@ cudaError_t enqueue_forward(tmg_ctx* c, tmg_kv* kv, const StreamState& st, bool 
     T.nsplit = kv->nsplit;
     T.M = M;
     T.scale = 1.0f / sqrtf(float(c->d));
+    T.err = c->d_err;
     T.trace = tc.take(1);
     B();
     TMG_CUDA_TRY(launch_attn_decode(T, c->stream, pdl));
@@ -673,7 +803,11 @@ cudaError_t enqueue_forward(tmg_ctx* c, tmg_kv* kv, const StreamState& st, bool 
     O.ldy = c->h;
     O.trace = tc.take(2);
     B();
-    TMG_CUDA_TRY(gemv(c, O, PRO_NONE, tp ? EPI_STORE : EPI_ADD, pdl));
+    if (c->i8)
+      TMG_CUDA_TRY(gemv8(Lw.qo, Lw.so, nullptr, nullptr, c->attn, nullptr, c->x, c->h, c->h,
+                         c->nq * c->d, EPI_ADD));
+    else
+      TMG_CUDA_TRY(gemv(c, O, PRO_NONE, tp ? EPI_STORE : EPI_ADD, pdl));
     E(2);
     if (tp) {
       B();
@@ -693,7 +827,11 @@ cudaError_t enqueue_forward(tmg_ctx* c, tmg_kv* kv, const StreamState& st, bool 
     GU.ldy = c->I;
     GU.trace = tc.take(3);
     B();
-    TMG_CUDA_TRY(gemv(c, GU, PRO_NORM, EPI_SWIGLU, pdl));
+    if (c->i8)
+      TMG_CUDA_TRY(gemv8(Lw.qg, Lw.sg, Lw.qu, Lw.su, c->x, Lw.post_norm, c->act, c->I, c->I, c->h,
+                         EPI_SWIGLU));
+    else
+      TMG_CUDA_TRY(gemv(c, GU, PRO_NORM, EPI_SWIGLU, pdl));
     E(3);
     GemvArgs D;
     D.w = Lw.wd;
@@ -705,7 +843,11 @@ cudaError_t enqueue_forward(tmg_ctx* c, tmg_kv* kv, const StreamState& st, bool 
     D.ldy = c->h;
     D.trace = tc.take(4);
     B();
-    TMG_CUDA_TRY(gemv(c, D, PRO_NONE, tp ? EPI_STORE : EPI_ADD, pdl));
+    if (c->i8)
+      TMG_CUDA_TRY(gemv8(Lw.qd, Lw.sd, nullptr, nullptr, c->act, nullptr, c->x, c->h, c->h, c->I,
+                         EPI_ADD));
+    else
+      TMG_CUDA_TRY(gemv(c, D, PRO_NONE, tp ? EPI_STORE : EPI_ADD, pdl));
     E(4);
     if (tp) {
       B();
@@ -777,7 +919,9 @@ int forward_seq(tmg_ctx* c, tmg_kv* kv, int stream, const uint32_t* tokens, int6
       float* kc = kv->k[l] + size_t(stream) * kv->cap * kvd;
       float* vc = kv->v[l] + size_t(stream) * kv->cap * kvd;
       CK(launch_rmsnorm(c->X, Lw.in_norm, eps, c->h, Tc, 1, c->Xn, c->stream), "rmsnorm");
-      CK(gemm(c, c->Xn, Lw.wqkv, Tc, c->qkv_rows, c->h, c->QKV, c->qkv_rows, false), "gemm qkv");
+      CK(gemm_layer(c, c->Xn, Lw.wqkv, Lw.qqkv, Lw.sqkv, Tc, c->qkv_rows, c->h, c->QKV, c->qkv_rows,
+                    false),
+         "gemm qkv");
       CK(launch_rope_append(c->QKV, c->qkv_rows, Tc, c->nq, c->nkv, c->d, kv->rope_cos,
                             kv->rope_sin, pos0, kc, vc, c->stream),
          "rope");
@@ -788,11 +932,15 @@ int forward_seq(tmg_ctx* c, tmg_kv* kv, int stream, const uint32_t* tokens, int6
         CK(gemm(c, c->ATT, Lw.wo, Tc, c->h, int64_t(c->nq) * c->d, c->Xn, c->h, false), "gemm o");
         CK(tp_reduce_add(c, c->Xn, c->X, Tc * c->h), "allreduce");
       } else {
-        CK(gemm(c, c->ATT, Lw.wo, Tc, c->h, int64_t(c->nq) * c->d, c->X, c->h, true), "gemm o");
+        CK(gemm_layer(c, c->ATT, Lw.wo, Lw.qo, Lw.so, Tc, c->h, int64_t(c->nq) * c->d, c->X, c->h,
+                      true),
+           "gemm o");
       }
       CK(launch_rmsnorm(c->X, Lw.post_norm, eps, c->h, Tc, 1, c->Xn, c->stream), "rmsnorm");
-      CK(gemm(c, c->Xn, Lw.wg, Tc, c->I, c->h, c->G, c->I, false), "gemm gate");
-      if (gemm_tc_supported(c->h, Lw.wg) && gemm_tc_supported(c->h, Lw.wu)) {
+      CK(gemm_layer(c, c->Xn, Lw.wg, Lw.qg, Lw.sg, Tc, c->I, c->h, c->G, c->I, false), "gemm gate");
+      if (c->i8) {
+        CK(gemm_layer(c, c->Xn, nullptr, Lw.qu, Lw.su, Tc, c->I, c->h, c->U, c->I, false), "gemm up");
+      } else if (gemm_tc_supported(c->h, Lw.wg) && gemm_tc_supported(c->h, Lw.wu)) {
         // gate and up read the same input: its hi/lo split from the gate GEMM
         CK(launch_gemm_tc(c->sp_hi, c->sp_lo, Lw.wu, Tc, c->I, c->h, c->U, c->I, false, c->d_err,
                           c->stream),
@@ -801,7 +949,10 @@ int forward_seq(tmg_ctx* c, tmg_kv* kv, int stream, const uint32_t* tokens, int6
         CK(gemm(c, c->Xn, Lw.wu, Tc, c->I, c->h, c->U, c->I, false), "gemm up");
       }
       float* down_y = tp ? c->Xn : c->X;
-      if (gemm_tc_supported(c->I, Lw.wd) && (ensure_split(c, size_t(Tc) * c->I) == cudaSuccess) &&
+      if (c->i8) {
+        CK(launch_swiglu(c->G, c->U, Tc * c->I, c->G, c->stream), "swiglu");
+        CK(gemm_layer(c, c->G, nullptr, Lw.qd, Lw.sd, Tc, c->h, c->I, down_y, c->h, !tp), "gemm down");
+      } else if (gemm_tc_supported(c->I, Lw.wd) && (ensure_split(c, size_t(Tc) * c->I) == cudaSuccess) &&
           swiglu_split_supported(c->G, c->U, Tc * c->I, c->sp_hi, c->sp_lo)) {
         // SwiGLU written straight as the down GEMM's hi/lo operands
         CK(launch_swiglu_split(c->G, c->U, Tc * c->I, c->sp_hi, c->sp_lo, c->stream), "swiglu");
@@ -912,6 +1063,7 @@ cudaError_t launch_fused(tmg_ctx* c, tmg_kv* kv, const StreamState& st, int64_t 
   f.nsplit = kv->nsplit_f;
   f.pf_ahead = c->fused_pf;
   f.pf_pace = c->fused_pf_pace;
+  f.pf_mode = c->fused_pf_mode;
   f.max_stages = c->fused_stages;
   f.st = st;
   f.n_steps = int(n_steps);
@@ -1245,6 +1397,7 @@ int tmg_create(int device, const tmg_config* cfg, tmg_ctx** out) {
       run("gemv_prepare", gemv_prepare()) && run("attn_prepare", attn_prepare()) &&
       run("gemm_tc_prepare", gemm_tc_prepare()) && run("prefill_prepare", prefill_prepare()) &&
       run("fused_prepare", fused_prepare()) && run("sample_prepare", sample_prepare()) &&
+      run("gemv_i8_prepare", gemv_i8_prepare()) && run("attn_tma_prepare", attn_tma_prepare()) &&
       run("error word", dalloc(c->allocs, &c->d_err, 4)) && run("error word", zero_sync(c, c->d_err, 16));
   if (step) {
     g_create_err = std::string("tmg_create: ") + step + ": " + cudaGetErrorString(ce);
@@ -1268,7 +1421,8 @@ int tmg_destroy(tmg_ctx* c) {
   cudaStreamSynchronize(c->stream);
   free_all(c->allocs);
   for (void* p : {(void*)c->X, (void*)c->Xn, (void*)c->QKV, (void*)c->ATT, (void*)c->G,
-                  (void*)c->U, (void*)c->d_tok, c->op_buf, (void*)c->sp_hi, (void*)c->sp_lo})
+                  (void*)c->U, (void*)c->d_tok, c->op_buf, (void*)c->sp_hi, (void*)c->sp_lo,
+                  (void*)c->dq, (void*)c->i8acc})
     if (p) cudaFree(p);
   if (c->pinned) cudaFreeHost(c->pinned);
   for (tmg_wmat* m : c->wmats) {
@@ -1901,6 +2055,41 @@ int tmg_op_gemv_wmat(tmg_ctx* c, const float* x, const tmg_wmat* w, int32_t M, f
 int tmg_op_gemm_wmat(tmg_ctx* c, const float* x, const tmg_wmat* w, int64_t T, float* y) {
   if (!c || !w || w->ctx != c) return fail(c, TMG_ERR_INVALID, "bad WMat handle");
   return tmg_op_gemm_bf16(c, x, w->w, w->rows, w->cols, T, y);
+}
+
+int tmg_op_quantize_i8(tmg_ctx* c, const uint16_t* w, int64_t N, int64_t K, int8_t* q,
+                       float* scales) {
+  if (!c || !w || !q || !scales || N <= 0 || K <= 0 || K > INT32_MAX)
+    return fail(c, TMG_ERR_INVALID, "bad argument");
+  cudaSetDevice(c->device);
+  CK(launch_quantize_w_i8(w, N, int(K), q, scales, c->stream), "quantize");
+  CK(cudaStreamSynchronize(c->stream), "quantize");
+  return TMG_OK;
+}
+
+int tmg_op_gemv_i8(tmg_ctx* c, const float* x, const int8_t* q, const float* scales, int64_t N,
+                   int64_t K, int32_t M, float* y) {
+  if (!c || !x || !q || !scales || !y || N <= 0 || K <= 0 || K % 16 || K > 16384 || M < 1 ||
+      M > kMaxStreams)
+    return fail(c, TMG_ERR_INVALID, "bad argument (K % 16 == 0, K <= 16384, 1 <= M <= 16)");
+  cudaSetDevice(c->device);
+  GemvI8Args a;
+  a.q = q;
+  a.scales = scales;
+  a.x = x;
+  a.y = y;
+  a.ldy = N;
+  a.N = N;
+  a.K = int(K);
+  a.M = M;
+  if (!gemv_i8_tma_ok(a.K, M)) {
+    CK(ensure_op(c, size_t(M) * K + 256 + 4 * kMaxStreams), "op scratch");
+    a.xs = static_cast<float*>(c->op_buf);
+    a.xq = static_cast<int8_t*>(c->op_buf) + 256;
+  }
+  CK(launch_gemv_i8(a, EPI_STORE, c->stream, false, c->num_sms), "gemv_i8");
+  CK(cudaStreamSynchronize(c->stream), "gemv_i8");
+  return TMG_OK;
 }
 
 int tmg_op_rmsnorm(tmg_ctx* c, const float* x, const float* w, float eps, int64_t n, int64_t rows,

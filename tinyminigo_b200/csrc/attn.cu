@@ -1114,13 +1114,21 @@ bool attn_decode_shape_ok(int nq, int nkv, int d, int64_t n_ctx, int nsplit, std
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) {
   const int G = a.nq / a.nkv;
   if (G * a.nkv != a.nq || G * a.d > 8 * kAttnThreads || G > 16) return cudaErrorInvalidValue;
-  // head dim 64 with at most 4 heads per kv head: K/V streamed into registers
-  // (TMG_ATTN_TILED=1 keeps the shared-memory tiled kernel, for comparison)
-  static const bool tiled_only = [] {
-    const char* e = getenv("TMG_ATTN_TILED");
-    return e && e[0] == '1';
+  // head dim 64 or 128 with at most 4 heads per kv head: the TMA-staged
+  // kernel (attn_tma.cu).  TMG_ATTN_KERNEL=reg / tiled selects the
+  // register-streaming kernel (head dim 64) or the cp.async tiled one, for
+  // comparison.
+  static const int choice = [] {
+    const char* e = getenv("TMG_ATTN_KERNEL");
+    if (e && e[0] == 'r') return 1;
+    if (e && e[0] == 't') return 2;
+    const char* t = getenv("TMG_ATTN_TILED");
+    return t && t[0] == '1' ? 2 : 0;
   }();
-  if (a.d == 64 && G <= 4 && !tiled_only) {
+  if (choice == 0 && attn_decode_tma_ok(a.nq, a.nkv, a.d, a.cap, a.M, a.kc, a.vc) &&
+      size_t(G) * a.nsplit * 4 <= attn_decode_tma_smem(a.d))
+    return launch_attn_decode_tma(a, s, pdl);
+  if (a.d == 64 && G <= 4 && choice != 2) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.nkv, a.nsplit, a.M);
     cfg.blockDim = dim3(kAttnThreads);

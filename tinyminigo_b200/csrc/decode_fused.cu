@@ -399,7 +399,7 @@ __device__ void producer(const FusedArgs& a, const FusedLayer* layers, Shared& S
       // time like mbar_wait)
       const unsigned long long tw0 = global_ns();
       for (unsigned int i = 1; !got; ++i) {
-        if (S.in_attn != 0 && pc.valid && pf < it + nst + a.pf_ahead) {
+        if ((a.pf_mode == 1 || S.in_attn != 0) && pc.valid && pf < it + nst + a.pf_ahead) {
           const long long now = clock64();
           if (now >= pf_next) {
             const Ranges r = group_ranges(pc.g, pc.grp);
@@ -999,11 +999,35 @@ struct AttnArgs {
 // position is in range, its k and v come as tagged words from the QKV
 // epilogues; earlier positions from the cache.  A single split writes the
 // output; otherwise the partial (m, l, o) goes out for the merge.
+// Start loading the cached K/V rows of the first tile of attention item
+// (kvh, split) into its tile buffers in sm (the layout attn_item uses).  The
+// rows below the decoded position do not depend on this step, so a CTA
+// issues this as soon as the region is free (in its QKV phase) and the load
+// overlaps the QKV GEMV instead of sitting in the attention chain.  The
+// copies complete at attn_item's cp.async wait.
+template <int D>
+__device__ __forceinline__ void attn_prefetch(const float* kc, const float* vc, int nkv, int G,
+                                              int kvh, int split, int chunk, int n_ctx,
+                                              int cache_end, float* sm) {
+  float* ks_ = sm + G * D;
+  float* vs = ks_ + kTileF * (D + 4);
+  const int kvd = nkv * D;
+  const int c0 = split * chunk, c1 = min(n_ctx, c0 + chunk);
+  const int nt = min(kTileF, c1 - c0);
+  const int nc = max(0, min(nt, cache_end - c0));
+  for (int i = threadIdx.x; i < nc * (D / 4); i += kCThreads) {
+    const int t = i / (D / 4), j4 = i % (D / 4);
+    cp_async16(ks_ + t * (D + 4) + j4 * 4, kc + size_t(c0 + t) * kvd + kvh * D + j4 * 4);
+    cp_async16(vs + t * D + j4 * 4, vc + size_t(c0 + t) * kvd + kvh * D + j4 * 4);
+  }
+}
+
+// tile0_ready: attn_prefetch already issued the first tile's cache rows.
 template <int D>
 __device__ __forceinline__ bool attn_item(const AttnArgs a, int kvh, int split, int chunk, int n_ctx,
                                        int pos, bool append, int n_used, uint32_t tag_qkv,
                                        uint32_t tag_att, float* sm, Shared& S, uint32_t& gc,
-                                       unsigned long long* tp) {
+                                       unsigned long long* tp, bool tile0_ready) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = a.nq / a.nkv, kvd = a.nkv * D;
   float* qs = sm;                       // [G][D]
@@ -1020,10 +1044,12 @@ __device__ __forceinline__ bool attn_item(const AttnArgs a, int kvh, int split, 
   for (int t0 = c0; t0 < c1; t0 += kTileF) {
     const int nt = min(kTileF, c1 - t0);
     const int nc = max(0, min(nt, cache_end - t0));
-    for (int i = tid; i < nc * (D / 4); i += kCThreads) {
-      const int t = i / (D / 4), j4 = i % (D / 4);
-      cp_async16(ks_ + t * (D + 4) + j4 * 4, a.kc + size_t(t0 + t) * kvd + kvh * D + j4 * 4);
-      cp_async16(vs + t * D + j4 * 4, a.vc + size_t(t0 + t) * kvd + kvh * D + j4 * 4);
+    if (!(t0 == c0 && tile0_ready)) {
+      for (int i = tid; i < nc * (D / 4); i += kCThreads) {
+        const int t = i / (D / 4), j4 = i % (D / 4);
+        cp_async16(ks_ + t * (D + 4) + j4 * 4, a.kc + size_t(t0 + t) * kvd + kvh * D + j4 * 4);
+        cp_async16(vs + t * D + j4 * 4, a.vc + size_t(t0 + t) * kvd + kvh * D + j4 * 4);
+      }
     }
     if (t0 == c0 || nc < nt) {
       // q (first tile) and the position's own k and v (its last row) in one poll
@@ -1262,7 +1288,8 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
         aa.scale = a.scale;
         for (int item = blockIdx.x; item < a.nkv * n_used && ok; item += gridDim.x)
           ok = attn_item<D>(aa, item / n_used, item % n_used, chunk, n_ctx, pos, append, n_used,
-                            tag - 1u, tag, asm_, S, gc, item == int(blockIdx.x) ? tp : nullptr);
+                            tag - 1u, tag, asm_, S, gc, item == int(blockIdx.x) ? tp : nullptr,
+                            item == int(blockIdx.x));
         if (tp && threadIdx.x == 0) tp[5] = global_ns();
         if (n_used > 1)
           for (int item = blockIdx.x; item < a.nkv * n_used && ok; item += gridDim.x)
@@ -1322,7 +1349,10 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
         if (threadIdx.x == 0) S.in_attn = 0;  // the attention chain ends with att here
         src = asm_;
       } else if (ph == PH_DOWN) {
-        ok = ll_gather(asm_, ll_mine(a.act_ll, a.I, a.ll_rep), a.I, want, a.bar + 2, S, gc, true);
+        // act in pieces of at most one gather (whole 256-element chunks)
+        const unsigned long long* act = ll_mine(a.act_ll, a.I, a.ll_rep);
+        for (int o = 0; o < a.I && ok; o += kMaxGather)
+          ok = ll_gather(asm_ + o, act + o, min(kMaxGather, a.I - o), want, a.bar + 2, S, gc, true);
         src = asm_;
       } else {
         // x after the phase just before: the previous layer's DOWN (QKV,
@@ -1351,6 +1381,14 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
       if (!ok) {
         raise_abort(a);
         break;
+      }
+      // the cache rows of this CTA's first attention item of the layer start
+      // loading now (the region is free until the attention phase; no
+      // cp.async wait comes before attn_item's)
+      if (ph == PH_QKV && int(blockIdx.x) < a.nkv * n_used) {
+        const int item = blockIdx.x;
+        attn_prefetch<D>(layers_s[l].kc, layers_s[l].vc, a.nkv, a.nq / a.nkv, item / n_used,
+                         item % n_used, chunk, n_ctx, append ? pos : n_ctx, asm_);
       }
       if (tp && threadIdx.x == 0) tp[1] = global_ns();
       const bool imm = ph == PH_HEAD && g.ks == 1;
@@ -1497,10 +1535,10 @@ bool seg_ok(int K) {
 bool local_ok(int64_t ngroups, int num_sms) {
   return (ngroups + num_sms - 1) / num_sms <= kMaxLocal;
 }
-// The (QKV/O/GU, DOWN) rows-per-stage pair with a kernel instance: 2048-
-// and 8192-wide rows (1B-class shapes; wider intermediate sizes also exceed
-// one exchange gather).
-bool rows_ok(int ra, int rb) { return ra == 8 && rb == 2; }
+// The (QKV/O/GU, DOWN) rows-per-stage pairs with a kernel instance: 2048-
+// and 8192-wide rows (1B-class shapes), 4096- and 14336-wide rows (8B-class
+// shapes).
+bool rows_ok(int ra, int rb) { return (ra == 8 && rb == 2) || (ra == 4 && rb == 1); }
 
 // The same for a layer phase of rpc rows per group (8 partial sums per row).
 bool local_ok_k(int64_t ngroups, int num_sms, int rpc) {
@@ -1523,11 +1561,13 @@ bool fused_supported(int h, int nq, int nkv, int d, int I, int64_t V, int num_sm
   if (!(seg_ok(h) && seg_ok(q_dim) && seg_ok(I) && (d == 64 || d == 128) && G >= 1 && G <= 8 &&
         G * d <= 4 * kCThreads))
     return false;
-  // every tagged exchange fits one gather (a kv head's queries: one word
-  // pair per thread)
-  if (h > kMaxGather || q_dim > kMaxGather || I > kMaxGather || G * (d + 2) > kMaxGather ||
-      G * d > 2 * kCThreads)
+  // every tagged exchange but act fits one gather (a kv head's queries: one
+  // word pair per thread; act is gathered in pieces)
+  if (h > kMaxGather || q_dim > kMaxGather || G * (d + 2) > kMaxGather || G * d > 2 * kCThreads)
     return false;
+  if ((d == 64 && !rows_ok(8, kCWarps / ksplit_host(I))) ||
+      (kCWarps / ksplit_host(h) == 4 && d != 128))
+    return false;  // the kernel instances: <64, 8, 2>, <128, 8, 2>, <128, 4, 1>
   // QKV groups hold rpc/2 rows from each RoPE half of a head
   const int rpc_h = kCWarps / ksplit_host(h);
   if (rpc_h < 2 || d % rpc_h != 0 || (d / 2) % (rpc_h / 2) != 0) return false;
@@ -1581,6 +1621,7 @@ size_t fused_smem(int h, int q_dim, int I, int d, int G, int nsplit, int L, int 
 
 cudaError_t fused_prepare() {
   TMG_CUDA_TRY((prepare_one<64, 8, 2>()));
+  TMG_CUDA_TRY((prepare_one<128, 4, 1>()));
   return prepare_one<128, 8, 2>();
 }
 
@@ -1611,8 +1652,11 @@ cudaError_t launch_decode_fused(const FusedArgs& args, int num_sms, cudaStream_t
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (a.d == 64) return cudaLaunchKernelEx(&cfg, decode_fused_kernel<64, 8, 2>, a, nst);
-  if (a.d == 128) return cudaLaunchKernelEx(&cfg, decode_fused_kernel<128, 8, 2>, a, nst);
+  if (a.d == 64 && ra == 8 && rb == 2) return cudaLaunchKernelEx(&cfg, decode_fused_kernel<64, 8, 2>, a, nst);
+  if (a.d == 128 && ra == 8 && rb == 2)
+    return cudaLaunchKernelEx(&cfg, decode_fused_kernel<128, 8, 2>, a, nst);
+  if (a.d == 128 && ra == 4 && rb == 1)
+    return cudaLaunchKernelEx(&cfg, decode_fused_kernel<128, 4, 1>, a, nst);
   return cudaErrorInvalidValue;
 }
 

@@ -48,6 +48,7 @@ struct FusedArgs {
   int nsplit = 1;
   int pf_ahead = 0;    // stages of stall-time L2 prefetch beyond the ring
   int pf_pace = 0;     // clock cycles between two such prefetches
+  int pf_mode = 0;     // 0: prefetch only in the attention chain; 1: whenever the ring is full
   int ll_rep = 1;      // copies of x_ll, att_ll and act_ll (each n words apart)
   int max_stages = 0;  // cap on the ring's stages (0: as many as fit)
   int attn_floats = 0; // set by the launcher: attention region of shared memory

@@ -100,6 +100,42 @@ struct GemvArgs {
 
 cudaError_t launch_gemv(const GemvArgs& a, GemvPro pro, GemvEpi epi, cudaStream_t s, bool pdl,
                         int num_sms);
+
+// ---------------------------------------------------------------------------
+// Int8 weights (gemv_i8.cu): per-row quantized matrices, the reference's
+// TMG_I8=1 path.
+// ---------------------------------------------------------------------------
+struct GemvI8Args {
+  const int8_t* q = nullptr;        // [N, K] (gate rows for SwiGLU)
+  const int8_t* q2 = nullptr;       // [N, K] up rows (SwiGLU)
+  const float* scales = nullptr;    // [N]
+  const float* scales2 = nullptr;   // [N] (SwiGLU up rows)
+  const float* x = nullptr;         // [M, K] activation rows (f32)
+  const float* norm_w = nullptr;    // RMSNorm weights applied to x first, or null
+  float eps = 0.f;
+  int norm_mode = 0;
+  int8_t* xq = nullptr;             // [M, K] scratch: quantized rows (M > 1)
+  float* xs = nullptr;              // [M] scratch: their scales (M > 1)
+  float* y = nullptr;               // [M, ldy]
+  int64_t ldy = 0;
+  int64_t N = 0;
+  int K = 0;
+  int M = 1;
+  int32_t* err = nullptr;
+};
+// y = quantize_row_i8(x) . Q^T scaled (EPI_STORE, EPI_ADD or EPI_SWIGLU).
+cudaError_t launch_gemv_i8(const GemvI8Args& a, GemvEpi epi, cudaStream_t s, bool pdl, int num_sms);
+// Whether one activation row of this K takes the fused-prologue TMA kernel.
+bool gemv_i8_tma_ok(int K, int M);
+// WMat::quantize_i8 of a BF16 [N, K] matrix: q [N, K], scales [N].
+cudaError_t launch_quantize_w_i8(const uint16_t* w, int64_t N, int K, int8_t* q, float* scales,
+                                 cudaStream_t s);
+// out = q widened to BF16 (exact), n % 4 == 0.
+cudaError_t launch_widen_i8(const int8_t* q, size_t n, uint16_t* out, cudaStream_t s);
+// y[t, o] (+)= acc[t, o] * scales[o] for T rows of N.
+cudaError_t launch_scale_rows(const float* acc, int64_t T, int64_t N, const float* scales, float* y,
+                              int64_t ldy, bool add, cudaStream_t s);
+cudaError_t gemv_i8_prepare();
 // True when the fused one-row kernel takes this shape (prologues need it).
 bool gemv_fused_ok(const GemvArgs& a, GemvEpi epi);
 // Once per device, before any launch or capture: kernel attributes
@@ -128,11 +164,18 @@ struct AttnDecodeArgs {
   unsigned int* ticket = nullptr;  // [M, n_kv]
   StreamState st{};
   const int32_t* pos_override = nullptr;  // op-level: fixed n_ctx - 1 (no append)
+  int32_t* err = nullptr;  // device error word (2 = a bounded wait gave up), or null
   int nq = 0, nkv = 0, d = 0, nsplit = 1, M = 1;
   float scale = 1.f;
   Trace trace{};
 };
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);
+// The TMA-staged decode attention (attn_tma.cu): head dim 64 or 128, at most
+// 4 query heads per kv head; launch_attn_decode picks it when it applies.
+bool attn_decode_tma_ok(int nq, int nkv, int d, int64_t cap, int M, const void* kc, const void* vc);
+size_t attn_decode_tma_smem(int d);
+cudaError_t launch_attn_decode_tma(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);
+cudaError_t attn_tma_prepare();
 int attn_decode_nsplit(int nkv, int M, int64_t cap, int num_sms);
 // Whether launch_attn_decode takes this op-level shape (n_q, n_kv, head dim,
 // context length, split count); *why says why not.

@@ -105,7 +105,7 @@ ncclResult_t settle(TpComm* t, ncclResult_t r, double timeout_s) {
   if (r != ncclInProgress) return r;
   NcclApi& a = api();
   const auto t0 = std::chrono::steady_clock::now();
-  for (;;) {
+  for (unsigned int i = 0;; ++i) {
     ncclResult_t st = ncclSuccess;
     const ncclResult_t q = a.get_async_error(t->comm, &st);
     if (q != ncclSuccess) return q;
@@ -117,7 +117,10 @@ ncclResult_t settle(TpComm* t, ncclResult_t r, double timeout_s) {
       t->aborted = true;
       return ncclInProgress;
     }
-    std::this_thread::sleep_for(std::chrono::microseconds(200));
+    // an enqueue usually settles within microseconds: spin first, then
+    // sleep (communicator set-up can take seconds)
+    if (i < 4096) std::this_thread::yield();
+    else std::this_thread::sleep_for(std::chrono::microseconds(100));
   }
 }
 
