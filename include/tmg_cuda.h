@@ -113,6 +113,9 @@ const char* tmg_version(void);
 /* A context on `device` for a model of shape `cfg` (NULL: an op-only
  * context for the tmg_op_* calls). */
 int tmg_create(int device, const tmg_config* cfg, tmg_ctx** out);
+/* Frees the context.  KV caches and WMat handles still alive lose their
+ * device memory here; their handles then accept only tmg_kv_destroy /
+ * tmg_wmat_free (in either order relative to this call). */
 int tmg_destroy(tmg_ctx* ctx);
 /* The message of the last failure on ctx; with ctx NULL, why the last
  * tmg_create on the calling thread failed. */

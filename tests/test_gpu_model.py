@@ -269,3 +269,26 @@ def test_bench_c5_host_leg_on_a_small_case():
     assert cache.len(0, 0) == T + 4
     cache.close()
     m.close()
+
+
+def test_cache_destroyed_after_its_context(c1):
+    # a KV cache and a WMat handle that outlive their context (garbage
+    # collection can order the destructors either way) are released with
+    # the context; their own destroy calls afterwards are safe
+    import ctypes
+
+    from tinyminigo_b200._lib import check, lib
+
+    d, cfg, t = c1
+    m = Model.from_tensors(cfg_obj(cfg), t)
+    cache = m.new_cache(64)
+    w = np.zeros((16, 16), np.uint16)
+    wm = ctypes.c_void_p()
+    check(lib().tmg_wmat_upload_bf16(m._h, w.ctypes.data_as(ctypes.c_void_p), 16, 16,
+                                     ctypes.byref(wm)), m._h)
+    check(lib().tmg_destroy(m._h))
+    m._h = None
+    m._caches = []
+    assert lib().tmg_kv_destroy(cache._h) == 0
+    cache._h = None
+    assert lib().tmg_wmat_free(wm) == 0

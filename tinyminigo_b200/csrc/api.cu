@@ -118,8 +118,11 @@ struct tmg_ctx {
   // pinned staging
   void* pinned = nullptr;
   size_t pinned_cap = 0;
-  // WMat handles still alive (released by tmg_destroy if the caller did not)
+  // WMat handles and KV caches still alive: tmg_destroy releases their
+  // device memory and detaches them (the handles then only accept their
+  // own destroy call, in any order relative to the context's)
   std::vector<tmg_wmat*> wmats;
+  std::vector<tmg_kv*> kvs;
   std::string err;
 };
 
@@ -1415,10 +1418,16 @@ int tmg_create(int device, const tmg_config* cfg, tmg_ctx** out) {
   return TMG_OK;
 }
 
+static void kv_release(tmg_kv* kv);
+
 int tmg_destroy(tmg_ctx* c) {
   if (!c) return TMG_ERR_INVALID;
   cudaSetDevice(c->device);
   cudaStreamSynchronize(c->stream);
+  for (tmg_kv* kv : c->kvs) {  // caches the caller did not destroy first
+    kv_release(kv);
+    kv->ctx = nullptr;
+  }
   free_all(c->allocs);
   for (void* p : {(void*)c->X, (void*)c->Xn, (void*)c->QKV, (void*)c->ATT, (void*)c->G,
                   (void*)c->U, (void*)c->d_tok, c->op_buf, (void*)c->sp_hi, (void*)c->sp_lo,
@@ -1427,7 +1436,8 @@ int tmg_destroy(tmg_ctx* c) {
   if (c->pinned) cudaFreeHost(c->pinned);
   for (tmg_wmat* m : c->wmats) {
     cudaFree(m->w);
-    delete m;
+    m->w = nullptr;
+    m->ctx = nullptr;  // the handle stays valid for tmg_wmat_free only
   }
   if (c->tp) tp_destroy(c->tp);
   cudaStreamDestroy(c->stream);
@@ -1595,13 +1605,13 @@ int tmg_kv_create(tmg_ctx* c, int32_t n_streams, int64_t capacity, tmg_kv** out)
   if ((e = dalloc(kv->allocs, &kv->part, size_t(n_streams) * c->nkv * kv->nsplit * G * (c->d + 2))) != cudaSuccess) return bail(e);
   if ((e = dalloc(kv->allocs, &kv->att_ticket, size_t(n_streams) * c->nkv)) != cudaSuccess) return bail(e);
   if ((e = zero_sync(c, kv->att_ticket, size_t(n_streams) * c->nkv * 4)) != cudaSuccess) return bail(e);
+  c->kvs.push_back(kv);
   *out = kv;
   return TMG_OK;
 }
 
-int tmg_kv_destroy(tmg_kv* kv) {
-  if (!kv) return TMG_ERR_INVALID;
-  cudaSetDevice(kv->ctx->device);
+// Free a KV cache's device resources (its context is current and alive).
+static void kv_release(tmg_kv* kv) {
   cudaStreamSynchronize(kv->ctx->stream);
   if (kv->g_plain) cudaGraphExecDestroy(kv->g_plain);
   if (kv->g_dec) cudaGraphExecDestroy(kv->g_dec);
@@ -1610,19 +1620,34 @@ int tmg_kv_destroy(tmg_kv* kv) {
   if (kv->d_gen) cudaFree(kv->d_gen);
   if (kv->d_uni) cudaFree(kv->d_uni);
   free_all(kv->allocs);
+  kv->g_plain = kv->g_dec = nullptr;
+  kv->state_ev = nullptr;
+  kv->h_state = nullptr;
+  kv->d_gen = nullptr;
+  kv->d_uni = nullptr;
+}
+
+int tmg_kv_destroy(tmg_kv* kv) {
+  if (!kv) return TMG_ERR_INVALID;
+  if (kv->ctx) {  // null: released with its context already
+    cudaSetDevice(kv->ctx->device);
+    kv_release(kv);
+    auto& v = kv->ctx->kvs;
+    v.erase(std::remove(v.begin(), v.end(), kv), v.end());
+  }
   delete kv;
   return TMG_OK;
 }
 
 int tmg_kv_len(const tmg_kv* kv, int32_t layer, int32_t stream, int64_t* out) {
-  if (!kv || !out || stream < 0 || stream >= kv->M || layer < 0 || layer >= kv->ctx->L)
+  if (!kv || !kv->ctx || !out || stream < 0 || stream >= kv->M || layer < 0 || layer >= kv->ctx->L)
     return TMG_ERR_INVALID;
   *out = kv->lens[stream];
   return TMG_OK;
 }
 
 int tmg_kv_reset(tmg_kv* kv) {
-  if (!kv) return TMG_ERR_INVALID;
+  if (!kv || !kv->ctx) return TMG_ERR_INVALID;
   tmg_ctx* c = kv->ctx;
   cudaSetDevice(c->device);
   int rc = reset_state(c, kv);
@@ -1632,14 +1657,14 @@ int tmg_kv_reset(tmg_kv* kv) {
 }
 
 int tmg_kv_truncate(tmg_kv* kv, int32_t stream, int64_t len) {
-  if (!kv || stream < 0 || stream >= kv->M || len < 0 || len > kv->lens[stream])
+  if (!kv || !kv->ctx || stream < 0 || stream >= kv->M || len < 0 || len > kv->lens[stream])
     return fail(kv ? kv->ctx : nullptr, TMG_ERR_INVALID, "bad truncate length");
   kv->lens[stream] = len;  // the device position is uploaded by the next forward
   return TMG_OK;
 }
 
 int tmg_kv_read(tmg_kv* kv, int32_t layer, int32_t stream, float* keys, float* values) {
-  if (!kv || stream < 0 || stream >= kv->M || layer < 0 || layer >= kv->ctx->L)
+  if (!kv || !kv->ctx || stream < 0 || stream >= kv->M || layer < 0 || layer >= kv->ctx->L)
     return TMG_ERR_INVALID;
   tmg_ctx* c = kv->ctx;
   cudaSetDevice(c->device);
@@ -2030,6 +2055,10 @@ int tmg_wmat_upload_bf16(tmg_ctx* c, const uint16_t* host, int64_t rows, int64_t
 int tmg_wmat_free(tmg_wmat* m) {
   if (!m) return TMG_ERR_INVALID;
   tmg_ctx* c = m->ctx;
+  if (!c) {  // released with its context already
+    delete m;
+    return TMG_OK;
+  }
   auto it = std::find(c->wmats.begin(), c->wmats.end(), m);
   if (it == c->wmats.end()) return fail(c, TMG_ERR_INVALID, "unknown WMat handle");
   c->wmats.erase(it);
