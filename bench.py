@@ -26,14 +26,19 @@ byte (profiles/decode_fused_c2.json).
 With --gpus N > 1 every rank runs an independent replica of c2 (the 1B
 config fits one GPU; "replicas only", weak scaling): `value` is c2's
 whole-job throughput at every N.  The same line carries a `c4_tp` block: the
-8B-class config sharded tensor-parallel over the
-same N ranks in the same process group (q/k/v and gate/up split by heads and
-rows, o/down by input columns with one NCCL allreduce per sublayer, the LM
-head by vocabulary rows), 128-token prompt, greedy 512 per step: decode
-tok/s of the one sequence (strong scaling), per-GPU algorithmic GB/s and
-its fraction of the HBM peak, and the allreduce time per token from a
-profiling pass.  At N = 1 the block is c4 on one GPU.  NCCL logs its
-communicator set-up (NCCL_DEBUG=INFO, subsystem INIT) on stderr.
+8B-class config decoded as ONE sequence by all N
+ranks of the same process group, 128-token prompt, greedy 512 per step:
+decode tok/s of the one sequence (strong scaling), per-GPU algorithmic GB/s
+and its fraction of the HBM peak.  By default (TMG_C4_MULTI=fused) one
+fused decode kernel is spread over every rank's SMs: each GPU holds the full
+weights, reads only the rows its CTAs own, and stores every exchanged value
+and KV row into every GPU's memory over NVLink (tmg_fused_group_init).
+TMG_C4_MULTI=nccl shards the weights tensor-parallel instead (q/k/v and
+gate/up split by heads and rows, o/down by input columns with one NCCL
+allreduce per sublayer, the LM head by vocabulary rows) and adds the
+allreduce time per token from a profiling pass.  At N = 1 the block is c4
+on one GPU.  NCCL logs its communicator set-up (NCCL_DEBUG=INFO, subsystem
+INIT) on stderr.
 
 --impl reference times the reference's CPU algorithm (the C++ restatement in
 oracle/, with the reference's thread policy) on the host cores, rank 0 only,
@@ -417,7 +422,7 @@ def run_ours(args, rank, world, local_rank):
             host_leg=world == 1 and not args.no_cpu_baseline)
         peak4, _ = peaks()
         c4 = {"workload": "c4: 8B-class Llama, untied, 128-token prompt, greedy 512 decode",
-              "parallelism": f"tp{world}" if world > 1 else "single GPU", "n_gpus": world,
+              "parallelism": c4_parallelism(world), "n_gpus": world,
               "scaling": "strong", "steps": min(args.steps, 3), "warmup": 3,
               "decode_tok_s": round(v4, 2), "ms_per_step": round(ms4, 3),
               "per_gpu_algorithmic_gbs": round(gbs4, 1), "peak": peak4,
@@ -552,6 +557,26 @@ def run_c3(args, rank, world, local_rank):
     model.close()
 
 
+def c4_mode(world):
+    """How c4 runs over `world` ranks: "single" on one GPU; "fused" (the
+    default at world > 1, TMG_C4_MULTI=fused) spreads the fused decode
+    kernel over every rank's SMs with the full weights on each GPU;
+    TMG_C4_MULTI=nccl shards the weights tensor-parallel with NCCL
+    allreduces between per-kernel launches."""
+    if world == 1:
+        return "single"
+    mode = os.environ.get("TMG_C4_MULTI", "fused")
+    if mode not in ("fused", "nccl"):
+        raise SystemExit(f"TMG_C4_MULTI={mode!r}: expected fused or nccl")
+    return mode
+
+
+def c4_parallelism(world):
+    mode = c4_mode(world)
+    return {"single": "single GPU", "fused": f"fused kernel over {world} GPUs",
+            "nccl": f"tp{world}"}[mode]
+
+
 def measure_c4(args, rank, world, local_rank, dist, steps, warmup, host_leg):
     """C4: the 8B-class config sharded tensor-parallel over the ranks of
     `dist` (one process per GPU, NCCL allreduce per sublayer; world 1: one
@@ -569,14 +594,17 @@ def measure_c4(args, rank, world, local_rank, dist, steps, warmup, host_leg):
 
     P4, G4 = 128, 512
     cfg = synth.CONFIGS["c4"]
-    tp = None
+    mode = c4_mode(world)
+    tp = uid_b = None
     if world > 1:
         uid = (ctypes.c_uint8 * 128)()
         if rank == 0:
             check(lib().tmg_tp_unique_id(uid))
         t = torch.tensor(list(bytes(uid)), dtype=torch.uint8, device="cuda")
         dist.broadcast(t, 0)
-        tp = (bytes(t.cpu().tolist()), rank, world)
+        uid_b = bytes(t.cpu().tolist())
+        if mode == "nccl":
+            tp = (uid_b, rank, world)
     t0 = time.time()
     if host_leg:  # the oracle needs every tensor in host memory
         w = synth.make_weights(cfg, 2025, device="cuda")
@@ -591,6 +619,8 @@ def measure_c4(args, rank, world, local_rank, dist, steps, warmup, host_leg):
     cache = model.new_cache(P4 + G4 + 8)
     logits = model.forward_seq(prompt, cache)
     tok = int(np.argmax(logits))
+    if mode == "fused":
+        model.fused_group(cache, uid_b, rank, world)
     stream = torch.cuda.ExternalStream(model.stream_handle(), device=local_rank)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
@@ -612,26 +642,32 @@ def measure_c4(args, rank, world, local_rank, dist, steps, warmup, host_leg):
     torch.cuda.synchronize()
     ms = max_over_ranks(dist, ev0.elapsed_time(ev1)) / steps
     value = G4 / (ms / 1e3)
-    # the collectives' share: one profiling pass (kernels launched one at a
-    # time with CUDA events around each, so slower than the graph)
-    cache.truncate(P4)
-    n_prof = 8
-    prof = model.profile_decode([tok], cache, n_prof)
-    ar_ms_tok = max_over_ranks(dist, prof["allreduce"][0] / n_prof)
-    ag_ms_tok = max_over_ranks(dist, prof["allgather_step_end"][0] / n_prof)
-    prof_ms_tok = max_over_ranks(dist, sum(v[0] for v in prof.values()) / n_prof)
+    extra = {"multi_gpu_path": {"single": "fused kernel on one GPU",
+                                "fused": "one fused kernel spread over all ranks' SMs "
+                                         "(peer stores over NVLink, full weights per rank)",
+                                "nccl": "tensor-parallel shards, NCCL allreduce per sublayer"}[mode]}
+    if mode != "fused":
+        # the collectives' share: one profiling pass (kernels launched one
+        # at a time with CUDA events around each, so slower than the graph)
+        cache.truncate(P4)
+        n_prof = 8
+        prof = model.profile_decode([tok], cache, n_prof)
+        ar_ms_tok = max_over_ranks(dist, prof["allreduce"][0] / n_prof)
+        ag_ms_tok = max_over_ranks(dist, prof["allgather_step_end"][0] / n_prof)
+        prof_ms_tok = max_over_ranks(dist, sum(v[0] for v in prof.values()) / n_prof)
+        extra.update({
+            "profile_pass_ms_per_token": round(prof_ms_tok, 4),
+            "profile_pass_ms_per_token_by_kernel": {k: round(v[0] / n_prof, 4)
+                                                    for k, v in prof.items() if v[1]},
+            "allreduce_ms_per_token": round(ar_ms_tok, 4),
+            "allreduces_per_token": int(prof["allreduce"][1] // n_prof),
+            "allgather_step_end_ms_per_token": round(ag_ms_tok, 4)})
     h, L, I, V = cfg["hidden_size"], cfg["num_hidden_layers"], cfg["intermediate_size"], cfg["vocab_size"]
     qd, kd = cfg["num_attention_heads"] * cfg["head_dim"], cfg["num_key_value_heads"] * cfg["head_dim"]
     wbytes = 2 * (L * ((qd + 2 * kd) * h + h * qd + 3 * I * h) + V * h)
     kvb = L * 2 * kd * 4 * (P4 + G4 / 2)
     per_gpu = (wbytes + kvb) / world
     gbs = per_gpu / (ms / 1e3 / G4) / 1e9
-    extra = {"profile_pass_ms_per_token": round(prof_ms_tok, 4),
-             "profile_pass_ms_per_token_by_kernel": {k: round(v[0] / n_prof, 4)
-                                                     for k, v in prof.items() if v[1]},
-             "allreduce_ms_per_token": round(ar_ms_tok, 4),
-             "allreduces_per_token": int(prof["allreduce"][1] // n_prof),
-             "allgather_step_end_ms_per_token": round(ag_ms_tok, 4)}
     if host_leg:
         cache.truncate(P4)
         gpu_ids = model.decode([tok], cache, 16)[0].tolist()
@@ -658,7 +694,7 @@ def run_c4(args, rank, world, local_rank):
         res = base_line(args, world, "decode_tok_s", value, "tok/s", ms,
                         {"workload": "c4: 8B-class, untied, 128-token prompt, greedy 512",
                          "global_batch": 1, "seq_len": 128 + 512,
-                         "parallelism": f"tp{world}" if world > 1 else "single GPU"},
+                         "parallelism": c4_parallelism(world)},
                         "strong", clk.summary(),
                         roofline={"bound": "hbm", "kernel": "decode step (per-GPU bytes)",
                                   "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
@@ -881,8 +917,8 @@ def run_attn(args, rank, world, local_rank):
     gbs = dec_bytes / (ms_dec / 1e3) / 1e9
     pf_flop = 4 * d * nq * T * (T + 1) // 2
     peak, peak_kind = peaks()
-    kern = {"r": "attn_decode_reg_kernel", "t": "attn_decode_kernel"}.get(
-        os.environ.get("TMG_ATTN_KERNEL", "tma")[:1], "attn_decode_tma_kernel<64>")
+    kern = {"reg": "attn_decode_reg_kernel", "tiled": "attn_decode_kernel"}.get(
+        os.environ.get("TMG_ATTN_KERNEL", "tma"), "attn_decode_tma_kernel<64>")
     if os.environ.get("TMG_ATTN_TILED", "0") == "1":
         kern = "attn_decode_kernel"
     res = base_line(args, world, "decode_attention_gbs", gbs, "GB/s", ms_dec,

@@ -254,6 +254,24 @@ int tmg_trace_fused(tmg_ctx* ctx, tmg_kv* kv, uint32_t token, uint64_t* out, int
  * column-split by heads and rows, o/down row-split, lm_head split by vocab).
  * ------------------------------------------------------------------------ */
 int tmg_tp_unique_id(uint8_t id[128]);
+/* Greedy decode of one sequence spread over `world` GPUs of one node (2 to
+ * 8, one process per GPU) by the fused decode kernel.  No counterpart in the
+ * reference (tensor parallelism of the 8B config).  Every rank calls this
+ * with its own context (created WITHOUT tmg_tp_init, holding the full
+ * weights: the 8B model is 16 GB of a B200's 180 GB) and a 1-stream cache of
+ * the same capacity, and the same `id` (tmg_tp_unique_id on rank 0).
+ * Afterwards tmg_decode / tmg_generate (greedy) on that cache run the fused
+ * kernel with its row groups and attention items dealt over the SMs of all
+ * ranks, so each GPU streams 1/world of the weights per token; every
+ * exchanged value, KV-cache row and argmax candidate is written into every
+ * rank's memory over NVLink (peer stores), so each output row is computed
+ * whole on one GPU and the tokens are bit-identical to one GPU's.  All ranks
+ * must make the same decode calls (prefill runs on each rank alone).  The
+ * group ends with the cache (tmg_kv_destroy on every rank).  Returns
+ * TMG_ERR_INVALID for a shape the fused kernel does not take or with too
+ * few row groups for `world`, or when two ranks share a GPU. */
+int tmg_fused_group_init(tmg_ctx* ctx, tmg_kv* kv, const uint8_t id[128], int32_t rank,
+                         int32_t world);
 /* Host-only: the block of the full tensor `name` (HF name, e.g.
  * "model.layers.3.mlp.down_proj.weight") that rank `rank` of `world` keeps,
  * as out = {row0, rows, col0, cols} of its [out, in] layout (vectors:

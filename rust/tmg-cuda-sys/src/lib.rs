@@ -128,6 +128,8 @@ unsafe extern "C" {
     pub fn tmg_tp_init(ctx: *mut TmgCtx, id: *const u8, rank: i32, world: i32) -> i32;
     pub fn tmg_tp_shard(cfg: *const TmgConfig, name: *const c_char, rank: i32, world: i32,
                         out: *mut i64) -> i32;
+    pub fn tmg_fused_group_init(ctx: *mut TmgCtx, kv: *mut TmgKv, id: *const u8, rank: i32,
+                                world: i32) -> i32;
 
     // WMat handles and op-level entry points (device pointers)
     pub fn tmg_wmat_upload_bf16(ctx: *mut TmgCtx, host: *const u16, rows: i64, cols: i64,

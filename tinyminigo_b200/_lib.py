@@ -105,6 +105,7 @@ SIGNATURES = {
     "tmg_tp_unique_id": (_I, [_P]),
     "tmg_tp_init": (_I, [_P, _P, _I32, _I32]),
     "tmg_tp_shard": (_I, [_P, ctypes.c_char_p, _I32, _I32, _P]),
+    "tmg_fused_group_init": (_I, [_P, _P, _P, _I32, _I32]),
     "tmg_op_gemv_bf16": (_I, [_P, _P, _P, _I64, _I64, _I32, _P]),
     "tmg_wmat_upload_bf16": (_I, [_P, _P, _I64, _I64, _PP]),
     "tmg_wmat_free": (_I, [_P]),

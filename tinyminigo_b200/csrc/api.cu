@@ -126,6 +126,24 @@ struct tmg_ctx {
   std::string err;
 };
 
+// One fused decode spread over several GPUs (tmg_fused_group_init): every
+// rank's exchange buffers, argmax table, barrier words and KV caches mapped
+// into this process (CUDA IPC), and the communicator whose collectives
+// separate the launches (no rank zeroes its buffers while another still
+// writes into them, none starts before all have zeroed).
+struct FusedGroup {
+  TpComm* comm = nullptr;
+  int rank = 0, world = 1, ctas = 0;
+  unsigned long long* ll_peer[tmg::kMaxGroupRanks] = {};
+  unsigned long long* part_peer[tmg::kMaxGroupRanks] = {};
+  unsigned int* bar_peer[tmg::kMaxGroupRanks] = {};
+  unsigned long long* am_peer[tmg::kMaxGroupRanks] = {};
+  float** d_kv_peer = nullptr;         // [world][L][2] on the device
+  unsigned long long* am = nullptr;    // this rank's argmax table [world * ctas]
+  float* sync = nullptr;               // the barriers' one float
+  std::vector<void*> opened;           // peer mappings to close
+};
+
 // A device weight matrix handle (WMat, src/tensor.rs:198-206): row-major
 // [rows, cols] BF16 bits in HBM, owned by the handle.
 struct tmg_wmat {
@@ -159,6 +177,7 @@ struct tmg_kv {
   unsigned long long* part_ll = nullptr;  // its tagged attention partials
   int nsplit_f = 1;                       // their split capacity per kv head
   cudaEvent_t state_ev = nullptr;  // the last upload from h_state
+  FusedGroup* grp = nullptr;       // set by tmg_fused_group_init
   std::vector<void*> allocs;
 };
 
@@ -1077,7 +1096,25 @@ cudaError_t launch_fused(tmg_ctx* c, tmg_kv* kv, const StreamState& st, int64_t 
     f.poll_ns = (unsigned long long)(c->test_poll_ms) * 1000000ull;
     c->test_stall = -1;
   }
-  return launch_decode_fused(f, c->num_sms, c->stream);
+  FusedGroup* g = kv->grp;
+  if (!g) return launch_decode_fused(f, c->num_sms, c->stream);
+  f.rank = g->rank;
+  f.world = g->world;
+  for (int r = 0; r < g->world; ++r) {
+    f.ll_peer[r] = g->ll_peer[r];
+    f.part_peer[r] = g->part_peer[r];
+    f.bar_peer[r] = g->bar_peer[r];
+    f.am_peer[r] = g->am_peer[r];
+  }
+  f.kv_peer = g->d_kv_peer;
+  f.am_part = g->am;
+  // every rank has finished the previous launch (its writes into this
+  // rank's buffers included) before any zeroes; every rank has zeroed
+  // before any starts
+  TMG_CUDA_TRY(tp_barrier(g->comm, g->sync, c->stream));
+  TMG_CUDA_TRY(fused_zero(f, c->stream));
+  TMG_CUDA_TRY(tp_barrier(g->comm, g->sync, c->stream));
+  return launch_decode_fused(f, g->ctas, c->stream, false);
 }
 
 bool use_fused(tmg_ctx* c, tmg_kv* kv) { return c->fused_ok && kv->M == 1 && kv->d_layers && kv->part_ll; }
@@ -1612,6 +1649,18 @@ int tmg_kv_create(tmg_ctx* c, int32_t n_streams, int64_t capacity, tmg_kv** out)
 
 // Free a KV cache's device resources (its context is current and alive).
 static void kv_release(tmg_kv* kv) {
+  if (FusedGroup* g = kv->grp) {
+    // the other ranks stop writing into this rank's memory first
+    tp_barrier(g->comm, g->sync, kv->ctx->stream);
+    cudaStreamSynchronize(kv->ctx->stream);
+    for (void* p : g->opened) cudaIpcCloseMemHandle(p);
+    if (g->d_kv_peer) cudaFree(g->d_kv_peer);
+    if (g->am) cudaFree(g->am);
+    if (g->sync) cudaFree(g->sync);
+    tp_destroy(g->comm);
+    delete g;
+    kv->grp = nullptr;
+  }
   cudaStreamSynchronize(kv->ctx->stream);
   if (kv->g_plain) cudaGraphExecDestroy(kv->g_plain);
   if (kv->g_dec) cudaGraphExecDestroy(kv->g_dec);
@@ -1972,6 +2021,123 @@ int tmg_tp_shard(const tmg_config* cfg, const char* name, int32_t rank, int32_t 
 }
 
 int tmg_tp_unique_id(uint8_t id[128]) { return tp_unique_id(id) == 0 ? TMG_OK : TMG_ERR_NCCL; }
+
+int tmg_fused_group_init(tmg_ctx* c, tmg_kv* kv, const uint8_t id[128], int32_t rank,
+                         int32_t world) {
+  if (!c || !kv || kv->ctx != c || !id || world < 2 || world > kMaxGroupRanks || rank < 0 ||
+      rank >= world)
+    return fail(c, TMG_ERR_INVALID, "bad argument");
+  if (c->world != 1 || !use_fused(c, kv) || kv->grp)
+    return fail(c, TMG_ERR_INVALID,
+                "a fused group needs a single-GPU context with full weights whose shape the fused "
+                "decode kernel takes, and a 1-stream cache not yet in a group");
+  cudaSetDevice(c->device);
+  const int ctas = fused_group_ctas(c->h, c->nq, c->nkv, c->d, c->I, c->V_l, c->num_sms, world);
+  if (ctas < 1)
+    return fail(c, TMG_ERR_INVALID, "the model's phases have too few row groups for this many GPUs");
+  std::string e;
+  TpComm* comm = tp_create(id, rank, world, e);
+  if (!comm) return fail(c, TMG_ERR_NCCL, e);
+  FusedGroup* g = new FusedGroup();
+  g->comm = comm;
+  g->rank = rank;
+  g->world = world;
+  g->ctas = ctas;
+  float* dbuf = nullptr;
+  auto bail = [&](int code, const std::string& m) {
+    for (void* p : g->opened) cudaIpcCloseMemHandle(p);
+    if (g->d_kv_peer) cudaFree(g->d_kv_peer);
+    if (g->am) cudaFree(g->am);
+    if (g->sync) cudaFree(g->sync);
+    if (dbuf) cudaFree(dbuf);
+    tp_destroy(g->comm);
+    delete g;
+    return fail(c, code, "tmg_fused_group_init: " + m);
+  };
+  cudaError_t ce = cudaMalloc(&g->am, size_t(world) * ctas * sizeof(unsigned long long));
+  if (ce == cudaSuccess) ce = cudaMalloc(&g->sync, sizeof(float));
+  if (ce == cudaSuccess) ce = zero_sync(c, g->sync, sizeof(float));
+  if (ce != cudaSuccess) return bail(TMG_ERR_CUDA, cudaGetErrorString(ce));
+  // what every rank publishes: its GPU, shape, and the IPC handles of its
+  // exchange words, partials, barrier words, argmax table and KV caches
+  struct Head {
+    char bus[32];
+    int32_t h, L, ctas, pad;
+    int64_t cap;
+  };
+  const int nh = 4 + 2 * c->L;
+  const size_t blob = (sizeof(Head) + size_t(nh) * sizeof(cudaIpcMemHandle_t) + 15) / 16 * 16;
+  std::vector<char> mine(blob, 0), all(blob * world, 0);
+  Head hd{};
+  hd.h = c->h;
+  hd.L = c->L;
+  hd.ctas = ctas;
+  hd.cap = kv->cap;
+  ce = cudaDeviceGetPCIBusId(hd.bus, sizeof(hd.bus), c->device);
+  std::memcpy(mine.data(), &hd, sizeof(hd));
+  std::vector<void*> bases = {c->ll, kv->part_ll, c->bar, g->am};
+  for (int l = 0; l < c->L; ++l) {
+    bases.push_back(kv->k[l]);
+    bases.push_back(kv->v[l]);
+  }
+  for (int i = 0; i < nh && ce == cudaSuccess; ++i) {
+    cudaIpcMemHandle_t hh;
+    ce = cudaIpcGetMemHandle(&hh, bases[i]);
+    std::memcpy(mine.data() + sizeof(Head) + size_t(i) * sizeof(hh), &hh, sizeof(hh));
+  }
+  if (ce != cudaSuccess) return bail(TMG_ERR_CUDA, cudaGetErrorString(ce));
+  const int64_t nf = int64_t(blob / 4);
+  ce = cudaMalloc(&dbuf, blob * (world + 1));
+  if (ce == cudaSuccess) ce = copy_sync(c, dbuf, mine.data(), blob, cudaMemcpyHostToDevice);
+  if (ce == cudaSuccess) ce = tp_allgather_rows(comm, dbuf, nf, dbuf + nf, nf * world, 1, c->stream);
+  if (ce == cudaSuccess) ce = copy_sync(c, all.data(), dbuf + nf, blob * world, cudaMemcpyDeviceToHost);
+  cudaFree(dbuf);
+  dbuf = nullptr;
+  if (ce != cudaSuccess) return bail(TMG_ERR_NCCL, std::string("handle exchange: ") + cudaGetErrorString(ce));
+  // one distinct GPU per rank, and the same model shape and cache everywhere
+  // (ranks that wait on one another must run at the same time)
+  for (int r = 0; r < world; ++r) {
+    Head o;
+    std::memcpy(&o, all.data() + size_t(r) * blob, sizeof(o));
+    if (o.h != hd.h || o.L != hd.L || o.ctas != hd.ctas || o.cap != hd.cap)
+      return bail(TMG_ERR_INVALID, "the ranks' model shapes or cache capacities differ");
+    for (int q = 0; q < r; ++q)
+      if (std::strncmp(o.bus, all.data() + size_t(q) * blob, sizeof(o.bus)) == 0)
+        return bail(TMG_ERR_INVALID, "two ranks share one GPU");
+  }
+  std::vector<float*> kvp(size_t(world) * c->L * 2);
+  for (int r = 0; r < world; ++r) {
+    std::vector<void*> p(nh);
+    for (int i = 0; i < nh; ++i) {
+      if (r == rank) {
+        p[i] = bases[i];
+        continue;
+      }
+      cudaIpcMemHandle_t hh;
+      std::memcpy(&hh, all.data() + size_t(r) * blob + sizeof(Head) + size_t(i) * sizeof(hh),
+                  sizeof(hh));
+      ce = cudaIpcOpenMemHandle(&p[i], hh, cudaIpcMemLazyEnablePeerAccess);
+      if (ce != cudaSuccess) return bail(TMG_ERR_CUDA, std::string("peer mapping: ") + cudaGetErrorString(ce));
+      g->opened.push_back(p[i]);
+    }
+    g->ll_peer[r] = static_cast<unsigned long long*>(p[0]);
+    g->part_peer[r] = static_cast<unsigned long long*>(p[1]);
+    g->bar_peer[r] = static_cast<unsigned int*>(p[2]);
+    g->am_peer[r] = static_cast<unsigned long long*>(p[3]);
+    for (int l = 0; l < c->L; ++l) {
+      kvp[(size_t(r) * c->L + l) * 2] = static_cast<float*>(p[4 + 2 * l]);
+      kvp[(size_t(r) * c->L + l) * 2 + 1] = static_cast<float*>(p[5 + 2 * l]);
+    }
+  }
+  ce = cudaMalloc(&g->d_kv_peer, kvp.size() * sizeof(float*));
+  if (ce == cudaSuccess)
+    ce = copy_sync(c, g->d_kv_peer, kvp.data(), kvp.size() * sizeof(float*), cudaMemcpyHostToDevice);
+  if (ce == cudaSuccess) ce = tp_barrier(comm, g->sync, c->stream);  // every rank mapped
+  if (ce == cudaSuccess) ce = cudaStreamSynchronize(c->stream);
+  if (ce != cudaSuccess) return bail(TMG_ERR_CUDA, cudaGetErrorString(ce));
+  kv->grp = g;
+  return TMG_OK;
+}
 
 int tmg_tp_init(tmg_ctx* c, const uint8_t id[128], int32_t rank, int32_t world) {
   if (!c || !id || world < 1 || rank < 0 || rank >= world) return fail(c, TMG_ERR_INVALID, "bad argument");

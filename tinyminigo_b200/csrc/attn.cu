@@ -18,6 +18,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <cstring>
 #include <stdlib.h>
 
 #include "common.cuh"
@@ -1120,8 +1121,8 @@ cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s, bool pdl
   // comparison.
   static const int choice = [] {
     const char* e = getenv("TMG_ATTN_KERNEL");
-    if (e && e[0] == 'r') return 1;
-    if (e && e[0] == 't') return 2;
+    if (e && std::strcmp(e, "reg") == 0) return 1;
+    if (e && std::strcmp(e, "tiled") == 0) return 2;
     const char* t = getenv("TMG_ATTN_TILED");
     return t && t[0] == '1' ? 2 : 0;
   }();

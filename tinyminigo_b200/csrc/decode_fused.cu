@@ -78,6 +78,12 @@ __device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+// The same at system scope (a word other GPUs write over NVLink).
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
@@ -258,11 +264,11 @@ __device__ __forceinline__ Ranges group_ranges(const PhaseGeo& g, int grp) {
   return r;
 }
 
-// First group of this CTA in a phase whose groups start at rotation `off`
-// (0 <= off < gridDim.x).
-__device__ __forceinline__ int first_group(int off) {
-  const int d = int(blockIdx.x) - off;
-  return d < 0 ? d + int(gridDim.x) : d;
+// First group of CTA gid of a grid of gn CTAs (all ranks') in a phase whose
+// groups start at rotation `off` (0 <= off < gn).
+__device__ __forceinline__ int first_group(int off, int gid, int gn) {
+  const int d = gid - off;
+  return d < 0 ? d + gn : d;
 }
 
 // Upper bound on the kernel's static shared memory, checked at prepare time.
@@ -277,6 +283,12 @@ struct Shared {
   float m_s[8], l_s[8], alpha_s[8];
   int fail[2];  // a poll gave up (indexed by the parity of the poll count)
   unsigned long long poll_ns;  // limit of one tag poll
+  int gid, gn;                 // this CTA in the grid of all ranks, and its size
+  int world;                   // GPUs of that grid (1: this one alone)
+  unsigned long long* ll_base;    // this rank's exchange words and partials ...
+  unsigned long long* part_base;
+  unsigned long long* ll_peer[kMaxGroupRanks];    // ... and every rank's (by rank)
+  unsigned long long* part_peer[kMaxGroupRanks];
   int gen_ok;
   volatile int abort;      // stop issuing / waiting (error or early end)
   volatile int issued;     // producer: stages issued so far
@@ -288,7 +300,8 @@ struct Shared {
 // ---------------------------------------------------------------------------
 // Grid barrier among the consumer warps of all CTAs: one monotonic arrival
 // counter (zeroed before the launch); the k-th barrier waits until it reaches
-// k * gridDim.x.  Every wait is bounded in time; a CTA that has aborted does
+// k times the CTAs of the grid (of all ranks: on several GPUs every CTA adds
+// to every rank's counter and waits on its own).  Every wait is bounded in time; a CTA that has aborted does
 // not arrive and raises bar[2], which releases the others.
 // ---------------------------------------------------------------------------
 __device__ bool grid_sync(const FusedArgs& a, unsigned int& target, Shared& S,
@@ -297,15 +310,25 @@ __device__ bool grid_sync(const FusedArgs& a, unsigned int& target, Shared& S,
   if (threadIdx.x == 0) {
     if (tr) tr[0] = global_ns();
     int ok = S.abort ? 0 : 1;
-    target += gridDim.x;
+    target += S.gn;
+    const bool sys = a.world > 1;
     if (ok) {
-      asm volatile("fence.acq_rel.gpu;" ::: "memory");
-      asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
+      if (sys) {
+        // every rank's counter: this CTA's writes of the step (KV appends,
+        // argmax partial) are released to all GPUs first
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        for (int r = 0; r < a.world; ++r)
+          asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(a.bar_peer[r]) : "memory");
+      } else {
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
+      }
       const unsigned long long t0 = global_ns();
       unsigned int spins = 0;
-      while (int(ld_acquire(a.bar) - target) < 0) {
+      while (int((sys ? ld_acquire_sys(a.bar) : ld_acquire(a.bar)) - target) < 0) {
         if ((++spins & 255) == 0) {
-          if (ld_acquire(a.bar + 2) != 0 || global_ns() - t0 > S.poll_ns) {
+          if ((sys ? ld_acquire_sys(a.bar + 2) : ld_acquire(a.bar + 2)) != 0 ||
+              global_ns() - t0 > S.poll_ns) {
             ok = 0;
             break;
           }
@@ -313,7 +336,10 @@ __device__ bool grid_sync(const FusedArgs& a, unsigned int& target, Shared& S,
       }
     }
     if (!ok) {
-      atomicExch(a.bar + 2, 1u);
+      if (sys)
+        for (int r = 0; r < a.world; ++r) atomicExch_system(a.bar_peer[r] + 2, 1u);
+      else
+        atomicExch(a.bar + 2, 1u);
       if (a.err) atomicExch(a.err, 2);
     }
     if (tr) tr[1] = global_ns();
@@ -330,13 +356,14 @@ struct Cursor {
   const FusedLayer* layers;  // the per-layer table in shared memory
   int step, l, ph, off;
   int grp;
+  int gid, gn;  // this CTA in the grid of all ranks
   PhaseGeo g;
   bool valid;
 };
 
 __device__ __forceinline__ void cur_settle(const FusedArgs& a, Cursor& c) {
   while (c.valid && c.grp >= c.g.ngroups) {
-    c.off = (c.off + c.g.ngroups) % int(gridDim.x);
+    c.off = (c.off + c.g.ngroups) % c.gn;
     if (c.ph == PH_HEAD) {
       if (++c.step >= a.n_steps) {
         c.valid = false;
@@ -351,22 +378,25 @@ __device__ __forceinline__ void cur_settle(const FusedArgs& a, Cursor& c) {
       ++c.ph;
     }
     c.g = geo(a, c.layers, c.ph, c.l < a.L ? c.l : 0);
-    c.grp = first_group(c.off);
+    c.grp = first_group(c.off, c.gid, c.gn);
   }
 }
-__device__ __forceinline__ void cur_begin(const FusedArgs& a, const FusedLayer* layers, Cursor& c) {
+__device__ __forceinline__ void cur_begin(const FusedArgs& a, const FusedLayer* layers,
+                                          const Shared& S, Cursor& c) {
   c.layers = layers;
+  c.gid = S.gid;
+  c.gn = S.gn;
   c.step = 0;
   c.l = 0;
   c.ph = PH_QKV;
   c.off = 0;
   c.g = geo(a, c.layers, PH_QKV, 0);
-  c.grp = first_group(0);
+  c.grp = first_group(0, c.gid, c.gn);
   c.valid = a.n_steps > 0;
   cur_settle(a, c);
 }
 __device__ __forceinline__ void cur_next(const FusedArgs& a, Cursor& c) {
-  c.grp += gridDim.x;
+  c.grp += c.gn;
   cur_settle(a, c);
 }
 
@@ -375,7 +405,7 @@ __device__ void producer(const FusedArgs& a, const FusedLayer* layers, Shared& S
   const uint64_t pol = evict_first_policy();
   const int nph = a.L * 5 + 1;
   Cursor ic, pc;
-  cur_begin(a, layers, ic);
+  cur_begin(a, layers, S, ic);
   // pc: the first stage past the ring (stage it + nst), the next one the
   // stall-time L2 prefetch may bring in; pf counts the stages it passed
   pc = ic;
@@ -470,22 +500,58 @@ __device__ void producer(const FusedArgs& a, const FusedLayer* layers, Shared& S
 // buffers before each launch).  A buffer is written again only after a
 // chain of phases that needs every CTA to have finished reading it (every
 // CTA owns groups in every GEMV phase), so a reader never misses its tag.
+// On several GPUs the writer stores each word into every rank's copy (peer
+// stores over NVLink, system scope) and readers poll their own copy.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void ll_store(unsigned long long* p, float v, uint32_t tag) {
-  const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
-  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+__device__ __forceinline__ void st_tag(unsigned long long* p, unsigned long long w, bool sys) {
+  if (sys) asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+  else asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
-__device__ __forceinline__ void ll_store_rep(unsigned long long* base, int n, int rep, int r,
-                                             float v, uint32_t tag) {
-  for (int c = 0; c < rep; ++c) ll_store(base + size_t(c) * n + r, v, tag);
+__device__ __forceinline__ unsigned long long tag_word(float v, uint32_t tag) {
+  return (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
 }
-__device__ __forceinline__ ulonglong2 ll_load2(const unsigned long long* p) {
+// (v, tag) at word p of this rank's exchange block, and of every rank's.
+__device__ __forceinline__ void ll_store(const Shared& S, unsigned long long* p, float v,
+                                         uint32_t tag) {
+  const unsigned long long w = tag_word(v, tag);
+  if (S.world == 1) {
+    st_tag(p, w, false);
+    return;
+  }
+  const size_t o = size_t(p - S.ll_base);
+  for (int r = 0; r < S.world; ++r) st_tag(S.ll_peer[r] + o, w, true);
+}
+// The same for a word of the attention partials.
+__device__ __forceinline__ void part_store(const Shared& S, unsigned long long* p, float v,
+                                           uint32_t tag) {
+  const unsigned long long w = tag_word(v, tag);
+  if (S.world == 1) {
+    st_tag(p, w, false);
+    return;
+  }
+  const size_t o = size_t(p - S.part_base);
+  for (int r = 0; r < S.world; ++r) st_tag(S.part_peer[r] + o, w, true);
+}
+__device__ __forceinline__ void ll_store_rep(const Shared& S, unsigned long long* base, int n,
+                                             int rep, int r, float v, uint32_t tag) {
+  for (int c = 0; c < rep; ++c) ll_store(S, base + size_t(c) * n + r, v, tag);
+}
+__device__ __forceinline__ ulonglong2 ll_load2(const unsigned long long* p, bool sys) {
   ulonglong2 r;
-  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];"
-               : "=l"(r.x), "=l"(r.y)
-               : "l"(p)
-               : "memory");
+  if (sys)
+    asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];"
+                 : "=l"(r.x), "=l"(r.y)
+                 : "l"(p)
+                 : "memory");
+  else
+    asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];"
+                 : "=l"(r.x), "=l"(r.y)
+                 : "l"(p)
+                 : "memory");
   return r;
+}
+__device__ __forceinline__ unsigned int ld_abort(const unsigned int* p, bool sys) {
+  return sys ? ld_acquire_sys(p) : ld_acquire(p);
 }
 
 // The copy of a replicated exchange vector (n words per copy) this CTA reads.
@@ -493,9 +559,6 @@ __device__ __forceinline__ const unsigned long long* ll_mine(const unsigned long
                                                              int rep) {
   return base + size_t(blockIdx.x % unsigned(rep)) * n;
 }
-// Store v at word r of every copy.
-__device__ __forceinline__ void ll_store_rep(unsigned long long* base, int n, int rep, int r,
-                                             float v, uint32_t tag);
 
 constexpr int kGatherPairs = 16;                            // word pairs per thread
 constexpr unsigned kBackoffNs = 0;                          // pause between polls
@@ -516,13 +579,14 @@ __device__ __noinline__ bool ll_gather(float* dst, const unsigned long long* src
   unsigned int spins = 0;
   bool ok = true;
   float ss = 0.f;
+  const bool sys = S.world > 1;
   ulonglong2 v[kGatherPairs];
   uint32_t need = 0;  // bit k: pair k still to come
 #pragma unroll
   for (int k = 0; k < kGatherPairs; ++k) {
     const int i = (threadIdx.x + k * kCThreads) * 2;
     if (i < n) {
-      v[k] = ll_load2(src + i);
+      v[k] = ll_load2(src + i, sys);
       need |= 1u << k;
     }
   }
@@ -549,14 +613,14 @@ __device__ __noinline__ bool ll_gather(float* dst, const unsigned long long* src
       }
     }
     if (!need) break;
-    if ((++spins & 15) == 0 && (ld_acquire(abort_word) != 0 || global_ns() - t0 > S.poll_ns)) {
+    if ((++spins & 15) == 0 && (ld_abort(abort_word, sys) != 0 || global_ns() - t0 > S.poll_ns)) {
       ok = false;
       break;
     }
     if (kBackoffNs) __nanosleep(kBackoffNs);
 #pragma unroll
     for (int k = 0; k < kGatherPairs; ++k)
-      if ((need >> k) & 1u) v[k] = ll_load2(src + (threadIdx.x + k * kCThreads) * 2);
+      if ((need >> k) & 1u) v[k] = ll_load2(src + (threadIdx.x + k * kCThreads) * 2, sys);
   }
   if (wx) {
     ss = warp_sum(ss);
@@ -580,10 +644,11 @@ __device__ __forceinline__ bool ll_gather3(const LLRange* r, int nr, uint32_t ta
                                         const unsigned int* abort_word, Shared& S, uint32_t& gc) {
   ulonglong2 v[3];
   uint32_t need = 0;
+  const bool sys = S.world > 1;
 #pragma unroll
   for (int k = 0; k < 3; ++k) {
     if (k < nr && threadIdx.x * 2 < r[k].n) {
-      v[k] = ll_load2(r[k].src + threadIdx.x * 2);
+      v[k] = ll_load2(r[k].src + threadIdx.x * 2, sys);
       need |= 1u << k;
     }
   }
@@ -600,14 +665,14 @@ __device__ __forceinline__ bool ll_gather3(const LLRange* r, int nr, uint32_t ta
       }
     }
     if (!need) break;
-    if ((++spins & 15) == 0 && (ld_acquire(abort_word) != 0 || global_ns() - t0 > S.poll_ns)) {
+    if ((++spins & 15) == 0 && (ld_abort(abort_word, sys) != 0 || global_ns() - t0 > S.poll_ns)) {
       ok = false;
       break;
     }
     if (kBackoffNs) __nanosleep(kBackoffNs);
 #pragma unroll
     for (int k = 0; k < 3; ++k)
-      if ((need >> k) & 1u) v[k] = ll_load2(r[k].src + threadIdx.x * 2);
+      if ((need >> k) & 1u) v[k] = ll_load2(r[k].src + threadIdx.x * 2, sys);
   }
   const int slot = gc & 1;
   ++gc;
@@ -619,7 +684,10 @@ __device__ __forceinline__ bool ll_gather3(const LLRange* r, int nr, uint32_t ta
 // Give up: raise the kernel-wide abort word and the error word.
 __device__ __forceinline__ void raise_abort(const FusedArgs& a) {
   if (threadIdx.x == 0) {
-    atomicExch(a.bar + 2, 1u);
+    if (a.world > 1)
+      for (int r = 0; r < a.world; ++r) atomicExch_system(a.bar_peer[r] + 2, 1u);
+    else
+      atomicExch(a.bar + 2, 1u);
     if (a.err) atomicExch(a.err, 2);
   }
 }
@@ -741,7 +809,7 @@ __device__ __forceinline__ int gemv_block(int ngroups, int K, int ks, int rpg, i
   const uint16_t* wbase =
       reinterpret_cast<const uint16_t*>(ring + size_t(slot) * K * 2) + kbase + lane * 8;
   int kl = 0;
-  for (int grp = first_group(off); grp < ngroups; grp += gridDim.x, rp.next(nst), ++kl) {
+  for (int grp = first_group(off, S.gid, S.gn); grp < ngroups; grp += S.gn, rp.next(nst), ++kl) {
     const int s = rp.s;
     float acc = 0.f;
     const bool ok = !S.abort && mbar_wait(&S.full[s], rp.par);
@@ -833,7 +901,7 @@ __device__ __forceinline__ int gemv_kseg(int ngroups, int K, int chunks, const f
   const int myrow = M > 0 ? (lane >> (5 - M)) & (R - 1) : 0;
   const bool writer = (lane & ((32 >> M) - 1)) == 0;
   int kl = 0;
-  for (int grp = first_group(off); grp < ngroups; grp += gridDim.x, rp.next(nst), ++kl) {
+  for (int grp = first_group(off, S.gid, S.gn); grp < ngroups; grp += S.gn, rp.next(nst), ++kl) {
     const int s = rp.s;
     float acc[R][NA];
 #pragma unroll
@@ -903,15 +971,26 @@ __device__ __forceinline__ int gemv_kseg(int ngroups, int K, int chunks, const f
 // rows at position pos (rope_s: the cos then sin row of pos).  q, k and v of the position go out as tagged
 // words; k and v are also appended to the cache at pos (when there is room),
 // where later steps read them.
-__device__ __forceinline__ void epi_qkv(const FusedArgs& a, const FusedLayer& L, const PhaseGeo& g,
-                                        int off, int nloc, int pos, bool append,
+// On several GPUs the appends go to every rank's cache (plain stores; the
+// step's grid barrier releases them before any rank reads those rows).
+__device__ __forceinline__ void kv_put(const FusedArgs& a, const FusedLayer& L, int l, int which,
+                                       size_t idx, float v) {
+  if (a.world == 1) {
+    (which ? L.vc : L.kc)[idx] = v;
+    return;
+  }
+  for (int r = 0; r < a.world; ++r) a.kv_peer[(size_t(r) * a.L + l) * 2 + which][idx] = v;
+}
+
+__device__ __forceinline__ void epi_qkv(const FusedArgs& a, const FusedLayer& L, int l,
+                                        const PhaseGeo& g, int off, int nloc, int pos, bool append,
                                         const float* rope_s, float scale, uint32_t tag, Shared& S) {
   const int D = g.D, half = D / 2, hp = g.rpc / 2, kvd = a.nkv * D;
-  const int f = first_group(off);
+  const int f = first_group(off, S.gid, S.gn);
   const int vbase = (a.nq + a.nkv) * D;
   for (int i = threadIdx.x; i < (nloc << g.lrpc); i += kCThreads) {
     const int kl = i >> g.lrpc, slot = i & (g.rpc - 1);
-    const int grp = f + kl * int(gridDim.x);
+    const int grp = f + kl * S.gn;
     if (grp < g.pair_groups) {
       if (slot >= hp) continue;  // done with its partner
       const int ra = slot_row(g, grp, slot);
@@ -920,18 +999,18 @@ __device__ __forceinline__ void epi_qkv(const FusedArgs& a, const FusedLayer& L,
       float o0, o1;
       rot(res_k(S, kl, slot, g.rpc) * scale, res_k(S, kl, slot + hp, g.rpc) * scale, rope_s[j],
           rope_s[half + j], &o0, &o1);
-      ll_store(a.qkv_ll + ra, o0, tag);
-      ll_store(a.qkv_ll + ra + half, o1, tag);
+      ll_store(S, a.qkv_ll + ra, o0, tag);
+      ll_store(S, a.qkv_ll + ra + half, o1, tag);
       if (head >= a.nq && append) {
-        float* kr = L.kc + size_t(pos) * kvd + (head - a.nq) * D;
-        kr[j] = o0;
-        kr[j + half] = o1;
+        const size_t kb = size_t(pos) * kvd + (head - a.nq) * D;
+        kv_put(a, L, l, 0, kb + j, o0);
+        kv_put(a, L, l, 0, kb + j + half, o1);
       }
     } else {
       const int r = slot_row(g, grp, slot);
       const float v = res_k(S, kl, slot, g.rpc) * scale;
-      ll_store(a.qkv_ll + r, v, tag);
-      if (append) L.vc[size_t(pos) * kvd + (r - vbase)] = v;
+      ll_store(S, a.qkv_ll + r, v, tag);
+      if (append) kv_put(a, L, l, 1, size_t(pos) * kvd + (r - vbase), v);
     }
   }
 }
@@ -941,11 +1020,12 @@ __device__ __forceinline__ void epi_qkv(const FusedArgs& a, const FusedLayer& L,
 __device__ __forceinline__ void epi_residual(unsigned long long* x_ll, int rep, const float* x_s,
                                              const PhaseGeo& g, int off, int nloc, uint32_t tag,
                                              const Shared& S) {
-  const int f = first_group(off);
+  const int f = first_group(off, S.gid, S.gn);
   for (int i = threadIdx.x; i < (nloc << g.lrpc); i += kCThreads) {
     const int kl = i >> g.lrpc, slot = i & (g.rpc - 1);
-    const int r = ((f + kl * int(gridDim.x)) << g.lrpg) + slot;
-    if (r < g.N) ll_store_rep(x_ll, g.N, rep, r, x_s[perm_idx(r)] + res_k(S, kl, slot, g.rpc), tag);
+    const int r = ((f + kl * S.gn) << g.lrpg) + slot;
+    if (r < g.N)
+      ll_store_rep(S, x_ll, g.N, rep, r, x_s[perm_idx(r)] + res_k(S, kl, slot, g.rpc), tag);
   }
 }
 
@@ -954,13 +1034,13 @@ __device__ __forceinline__ void epi_residual(unsigned long long* x_ll, int rep, 
 __device__ __forceinline__ void epi_swiglu(unsigned long long* act_ll, int rep, const PhaseGeo& g,
                                            int off, int nloc, float scale, uint32_t tag,
                                            const Shared& S) {
-  const int f = first_group(off);
+  const int f = first_group(off, S.gid, S.gn);
   for (int i = threadIdx.x; i < (nloc << g.lrpg); i += kCThreads) {
     const int kl = i >> g.lrpg, q = i & (g.rpg - 1);
-    const int r = ((f + kl * int(gridDim.x)) << g.lrpg) + q;
+    const int r = ((f + kl * S.gn) << g.lrpg) + q;
     if (r < g.N) {
       const float gv = res_k(S, kl, q, g.rpc) * scale, uv = res_k(S, kl, q + g.rpg, g.rpc) * scale;
-      ll_store_rep(act_ll, g.N, rep, r, gv / (1.0f + expf(-gv)) * uv, tag);
+      ll_store_rep(S, act_ll, g.N, rep, r, gv / (1.0f + expf(-gv)) * uv, tag);
     }
   }
 }
@@ -968,10 +1048,10 @@ __device__ __forceinline__ void epi_swiglu(unsigned long long* act_ll, int rep, 
 // LM head epilogue (ks > 1): logits and this thread's argmax candidate.
 __device__ __forceinline__ void epi_head(float* logits, const PhaseGeo& g, int off, int nloc,
                                          const Shared& S, unsigned long long& best) {
-  const int f = first_group(off);
+  const int f = first_group(off, S.gid, S.gn);
   for (int i = threadIdx.x; i < (nloc << g.lrpc); i += kCThreads) {
     const int kl = i >> g.lrpc, slot = i & (g.rpc - 1);
-    const int r = ((f + kl * int(gridDim.x)) << g.lrpg) + slot;
+    const int r = ((f + kl * S.gn) << g.lrpg) + slot;
     if (r < g.N) {
       const float v = res_val(S, kl, slot, g.ks);
       logits[r] = v;
@@ -1127,7 +1207,7 @@ __device__ __forceinline__ bool attn_item(const AttnArgs a, int kvh, int split, 
       const int idx = tid + r * kCThreads;
       if (idx < G * D) {
         const float l = S.l_s[idx / D];
-        ll_store_rep(a.att_ll, a.nq * D, a.rep, kvh * G * D + idx, l > 0.f ? o_acc[r] / l : 0.f,
+        ll_store_rep(S, a.att_ll, a.nq * D, a.rep, kvh * G * D + idx, l > 0.f ? o_acc[r] / l : 0.f,
                      tag_att);
       }
     }
@@ -1136,11 +1216,11 @@ __device__ __forceinline__ bool attn_item(const AttnArgs a, int kvh, int split, 
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const int idx = tid + r * kCThreads;
-      if (idx < G * D) ll_store(part + (idx / D) * (D + 2) + 2 + (idx % D), o_acc[r], tag_att);
+      if (idx < G * D) part_store(S, part + (idx / D) * (D + 2) + 2 + (idx % D), o_acc[r], tag_att);
     }
     if (tid < G) {
-      ll_store(part + tid * (D + 2), S.m_s[tid], tag_att);
-      ll_store(part + tid * (D + 2) + 1, S.l_s[tid], tag_att);
+      part_store(S, part + tid * (D + 2), S.m_s[tid], tag_att);
+      part_store(S, part + tid * (D + 2) + 1, S.l_s[tid], tag_att);
     }
   }
   if (tp && tid == 0) tp[8] = global_ns();
@@ -1178,7 +1258,7 @@ __device__ __forceinline__ bool merge_head(const AttnArgs a, int kvh, int n_used
     float acc = 0.f;
     for (int s = 0; s < n_used; ++s) acc = fmaf(P[s * rec + g * (D + 2) + 2 + j], wv[g * n_used + s], acc);
     const float L = Ls[g];
-    ll_store_rep(a.att_ll, a.nq * D, a.rep, kvh * G * D + idx, L > 0.f ? acc / L : 0.f, tag_att);
+    ll_store_rep(S, a.att_ll, a.nq * D, a.rep, kvh * G * D + idx, L > 0.f ? acc / L : 0.f, tag_att);
   }
   csync();
   return true;
@@ -1219,6 +1299,15 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
     S.in_attn = 0;
     S.fail[0] = S.fail[1] = 0;
     S.poll_ns = a.poll_ns ? a.poll_ns : kWaitNs;
+    S.world = a.world;
+    S.gid = a.rank * int(gridDim.x) + int(blockIdx.x);
+    S.gn = a.world * int(gridDim.x);
+    S.ll_base = a.ll_base;
+    S.part_base = a.part_ll;
+    for (int r = 0; r < kMaxGroupRanks; ++r) {
+      S.ll_peer[r] = a.ll_peer[r];
+      S.part_peer[r] = a.part_peer[r];
+    }
     mbar_fence_init();
   }
   __syncthreads();
@@ -1286,13 +1375,13 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
         aa.nkv = a.nkv;
         aa.nsplit = a.nsplit;
         aa.scale = a.scale;
-        for (int item = blockIdx.x; item < a.nkv * n_used && ok; item += gridDim.x)
+        for (int item = S.gid; item < a.nkv * n_used && ok; item += S.gn)
           ok = attn_item<D>(aa, item / n_used, item % n_used, chunk, n_ctx, pos, append, n_used,
-                            tag - 1u, tag, asm_, S, gc, item == int(blockIdx.x) ? tp : nullptr,
-                            item == int(blockIdx.x));
+                            tag - 1u, tag, asm_, S, gc, item == S.gid ? tp : nullptr,
+                            item == S.gid);
         if (tp && threadIdx.x == 0) tp[5] = global_ns();
         if (n_used > 1)
-          for (int item = blockIdx.x; item < a.nkv * n_used && ok; item += gridDim.x)
+          for (int item = S.gid; item < a.nkv * n_used && ok; item += S.gn)
             if (item % n_used == 0) ok = merge_head<D>(aa, item / n_used, n_used, tag, asm_, S, gc);
         if (tp && threadIdx.x == 0) tp[6] = global_ns();
         if (!ok) raise_abort(a);
@@ -1385,8 +1474,8 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
       // the cache rows of this CTA's first attention item of the layer start
       // loading now (the region is free until the attention phase; no
       // cp.async wait comes before attn_item's)
-      if (ph == PH_QKV && int(blockIdx.x) < a.nkv * n_used) {
-        const int item = blockIdx.x;
+      if (ph == PH_QKV && S.gid < a.nkv * n_used) {
+        const int item = S.gid;
         attn_prefetch<D>(layers_s[l].kc, layers_s[l].vc, a.nkv, a.nq / a.nkv, item / n_used,
                          item % n_used, chunk, n_ctx, append ? pos : n_ctx, asm_);
       }
@@ -1414,7 +1503,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
         const long long ce = tp ? clock64() : 0;
         switch (ph) {
           case PH_QKV:
-            epi_qkv(a, layers_s[lw], g, off, nloc, pos, append, rope_s, rscale, tag, S);
+            epi_qkv(a, layers_s[lw], lw, g, off, nloc, pos, append, rope_s, rscale, tag, S);
             break;
           case PH_GU: epi_swiglu(a.act_ll, a.ll_rep, g, off, nloc, rscale, tag, S); break;
           case PH_HEAD: epi_head(a.logits, g, off, nloc, S, best); break;
@@ -1423,7 +1512,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
         if (tp && threadIdx.x == 0) tp[9] = clock64() - ce;
       }
       csync();  // x_s, asm_ and S.res are free for the next phase
-      off = (off + g.ngroups) % int(gridDim.x);
+      off = (off + g.ngroups) % S.gn;
       if (ph == PH_HEAD) {
         best = warp_max_u64(best);
         if (lane == 0) S.best[warp] = best;
@@ -1431,7 +1520,14 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
         if (threadIdx.x == 0) {
           unsigned long long bb = 0;
           for (int w = 0; w < kCWarps; ++w) bb = S.best[w] > bb ? S.best[w] : bb;
-          a.am_part[blockIdx.x] = bb;
+          if (a.world == 1) {
+            a.am_part[blockIdx.x] = bb;
+          } else {  // every rank's table, at this CTA's index in the joint grid
+            for (int r = 0; r < a.world; ++r)
+              asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(a.am_peer[r] + S.gid),
+                           "l"(bb)
+                           : "memory");
+          }
         }
         // the one grid barrier of a step: the argmax partials, and the cache
         // rows appended this step, are visible everywhere after it
@@ -1442,7 +1538,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
     // every CTA reduces the argmax partials: the same token everywhere
     {
       unsigned long long b = 0;
-      for (int i = threadIdx.x; i < int(gridDim.x); i += kCThreads) {
+      for (int i = threadIdx.x; i < S.gn; i += kCThreads) {
         const unsigned long long v = __ldcg(a.am_part + i);
         b = v > b ? v : b;
       }
@@ -1625,25 +1721,51 @@ cudaError_t fused_prepare() {
   return prepare_one<128, 8, 2>();
 }
 
-cudaError_t launch_decode_fused(const FusedArgs& args, int num_sms, cudaStream_t s) {
+int fused_group_ctas(int h, int nq, int nkv, int d, int I, int64_t V, int num_sms, int world) {
+  if (world < 1 || world > kMaxGroupRanks || !fused_supported(h, nq, nkv, d, I, V, num_sms))
+    return 0;
+  const int rpc_h = kCWarps / ksplit_host(h), rpc_q = kCWarps / ksplit_host(nq * d),
+            rpc_i = kCWarps / ksplit_host(I);
+  const int64_t groups[5] = {int64_t(nq + 2 * nkv) * d / rpc_h, (h + rpc_q - 1) / rpc_q,
+                             (I + rpc_h / 2 - 1) / (rpc_h / 2), (h + rpc_i - 1) / rpc_i,
+                             (V + rpc_h - 1) / rpc_h};
+  // every CTA of the joint grid owns a group of every phase
+  int64_t ctas = num_sms;
+  for (int i = 0; i < 5; ++i) ctas = std::min<int64_t>(ctas, groups[i] / world);
+  return int(std::max<int64_t>(ctas, 0));
+}
+
+cudaError_t fused_zero(const FusedArgs& a, cudaStream_t s) {
+  // the grid barrier counts from zero in every launch, and the tagged
+  // exchange buffers hold no tag of this launch
+  const int G = a.nq / a.nkv;
+  TMG_CUDA_TRY(cudaMemsetAsync(a.bar, 0, 4 * sizeof(unsigned int), s));
+  TMG_CUDA_TRY(cudaMemsetAsync(a.ll_base, 0, a.ll_bytes, s));
+  return cudaMemsetAsync(a.part_ll, 0,
+                         size_t(a.nkv) * a.nsplit * G * (a.d + 2) * sizeof(unsigned long long), s);
+}
+
+cudaError_t launch_decode_fused(const FusedArgs& args, int grid, cudaStream_t s, bool zero) {
   FusedArgs a = args;
   int nst = 0;
   const int G = a.nq / a.nkv;
   const size_t smem = fused_smem(a.h, a.nq * a.d, a.I, a.d, G, a.nsplit, a.L, a.max_stages, &nst,
                                  &a.attn_floats, &a.max_splits);
   if (nst < 2 || !a.x_ll || !a.att_ll || !a.act_ll || !a.qkv_ll || !a.part_ll || a.pf_ahead < 0 || a.pf_pace < 0 ||
-      a.ll_rep < 1)
+      a.ll_rep < 1 || grid < 1 || a.world < 1 || a.world > kMaxGroupRanks || a.rank < 0 ||
+      a.rank >= a.world)
     return cudaErrorInvalidValue;
+  if (a.world > 1) {
+    for (int r = 0; r < a.world; ++r)
+      if (!a.ll_peer[r] || !a.part_peer[r] || !a.bar_peer[r] || !a.am_peer[r])
+        return cudaErrorInvalidValue;
+    if (!a.kv_peer || a.trace) return cudaErrorInvalidValue;
+  }
   const int ra = kCWarps / ksplit_host(a.h), rb = kCWarps / ksplit_host(a.I);
   if (!rows_ok(ra, rb)) return cudaErrorInvalidValue;
-  // the grid barrier counts from zero in every launch, and the tagged
-  // exchange buffers hold no tag of this launch
-  TMG_CUDA_TRY(cudaMemsetAsync(a.bar, 0, 4 * sizeof(unsigned int), s));
-  TMG_CUDA_TRY(cudaMemsetAsync(a.ll_base, 0, a.ll_bytes, s));
-  TMG_CUDA_TRY(cudaMemsetAsync(a.part_ll, 0,
-                               size_t(a.nkv) * a.nsplit * G * (a.d + 2) * sizeof(unsigned long long), s));
+  if (zero) TMG_CUDA_TRY(fused_zero(a, s));
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(num_sms);
+  cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kFThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;

@@ -21,6 +21,9 @@ struct FusedLayer {
   float* vc;
 };
 
+// Most GPUs one fused decode can span (fused_group in api.cu).
+constexpr int kMaxGroupRanks = 8;
+
 struct FusedArgs {
   const FusedLayer* layers = nullptr;
   int L = 0, h = 0, nq = 0, nkv = 0, d = 0, I = 0, V = 0;
@@ -58,6 +61,18 @@ struct FusedArgs {
   int32_t* err = nullptr;
   // limit of the tag polls and the grid barrier (ns; 0: the 2 s default)
   unsigned long long poll_ns = 0;
+  // Several GPUs (world > 1): the CTAs of all ranks form one grid of world
+  // x gridDim.x CTAs (this rank's are rank x gridDim.x + blockIdx.x); every
+  // exchange word, attention partial, KV-cache append, argmax partial and
+  // barrier arrival is written into every rank's copy (index: rank; the own
+  // rank's entry is the local buffer).  Each rank holds the full weights and
+  // streams the row groups its CTAs own.
+  int rank = 0, world = 1;
+  unsigned long long* ll_peer[kMaxGroupRanks] = {};
+  unsigned long long* part_peer[kMaxGroupRanks] = {};
+  unsigned int* bar_peer[kMaxGroupRanks] = {};
+  unsigned long long* am_peer[kMaxGroupRanks] = {};
+  float* const* kv_peer = nullptr;  // [world][L][2]: every rank's K and V cache of each layer
   // failure-path test only (-1: off): in the first step, the input gather of
   // phase stall_phase (a GEMV phase that gathers: O, GU, DOWN, a later
   // layer's QKV, HEAD) waits for a tag no phase writes, so the poll gives up
@@ -83,7 +98,14 @@ inline size_t fused_ll_words(int h, int q_dim, int I, int qkv_rows, int rep) {
   return size_t(rep) * (size_t(h) + q_dim + I) + qkv_rows;
 }
 cudaError_t fused_prepare();
-// Cooperative launch: one CTA per SM (num_sms CTAs).
-cudaError_t launch_decode_fused(const FusedArgs& a, int num_sms, cudaStream_t s);
+// CTAs per rank when `world` GPUs share one fused decode of this shape (every
+// CTA of the joint grid must own a row group of every phase), or 0.
+int fused_group_ctas(int h, int nq, int nkv, int d, int I, int64_t V, int num_sms, int world);
+// Zero the launch's barrier and tagged-exchange words (the launcher does it
+// unless told not to: a multi-GPU launch zeroes every rank before any rank
+// starts, between two host-side barriers).
+cudaError_t fused_zero(const FusedArgs& a, cudaStream_t s);
+// Cooperative launch of `grid` CTAs (one per SM at most).
+cudaError_t launch_decode_fused(const FusedArgs& a, int grid, cudaStream_t s, bool zero = true);
 
 }  // namespace tmg

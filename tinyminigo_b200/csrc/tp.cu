@@ -203,4 +203,8 @@ cudaError_t tp_allgather_rows(TpComm* t, const float* local, int64_t n_local, fl
   return cudaGetLastError();
 }
 
+cudaError_t tp_barrier(TpComm* t, float* scratch, cudaStream_t s) {
+  return tp_allreduce_sum(t, scratch, 1, s);
+}
+
 }  // namespace tmg

@@ -21,5 +21,8 @@ cudaError_t tp_allreduce_sum(TpComm* t, float* buf, int64_t n, cudaStream_t s);
 // receives the shards side by side (n_full = world * n_local).
 cudaError_t tp_allgather_rows(TpComm* t, const float* local, int64_t n_local, float* out,
                               int64_t n_full, int M, cudaStream_t s);
+// Every rank's stream reaches this point before any passes it (a one-float
+// allreduce on `scratch`, a device float).
+cudaError_t tp_barrier(TpComm* t, float* scratch, cudaStream_t s);
 
 }  // namespace tmg

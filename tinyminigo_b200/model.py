@@ -277,6 +277,14 @@ class Model:
         """The library's cudaStream_t (for CUDA events on the launching stream)."""
         return int(lib().tmg_stream(self._h) or 0)
 
+    def fused_group(self, cache: "KvCache", uid: bytes, rank: int, world: int):
+        """Join `cache` to a greedy decode spread over `world` GPUs (one
+        process each, every rank holding the full weights): tmg_decode on it
+        then deals the fused kernel's work over all ranks' SMs."""
+        buf = (ctypes.c_uint8 * 128).from_buffer_copy(bytes(uid))
+        check(lib().tmg_fused_group_init(self._h, cache._h, buf, rank, world), self._h,
+              "tmg_fused_group_init")
+
     def profile_decode(self, tokens, cache: "KvCache", n_steps: int) -> dict:
         """Per-kernel-class device time (ms) and launches of n_steps greedy
         steps launched one kernel at a time with CUDA events between them."""
