@@ -44,6 +44,32 @@ __device__ __forceinline__ void rot_rn(float a, float b, float c, float s, float
   *o1 = __fadd_rn(as, bc);
 }
 
+constexpr float kLog2e = 1.4426950408889634f;
+
+// 2^x by the SFU's ex2 instruction (relative error about 2^-22; 2^-inf = 0)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Reduce-scatter of 16 values over the 16 lanes of a half-warp: afterwards
+// v[0] of lane l16 holds the sum over the half-warp of value l16.  Level
+// xor m (8, 4, 2, 1) pairs value j with j + m among the values still held;
+// a lane keeps the half its lane bit selects and adds the partner's copy.
+__device__ __forceinline__ void reduce_scatter16(float (&v)[16], int l16) {
+#pragma unroll
+  for (int m = 8; m >= 1; m >>= 1) {
+    const bool hi = (l16 & m) != 0;
+#pragma unroll
+    for (int j = 0; j < m; ++j) {
+      const float keep = hi ? v[j + m] : v[j];
+      const float send = hi ? v[j] : v[j + m];
+      v[j] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+    }
+  }
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int x, int y) {
   asm volatile(
@@ -181,9 +207,21 @@ __global__ void __launch_bounds__(kTmaThreads, D == 64 ? 3 : 2)
     }
   } else {
     // ---- consumers ----
-    const int hw = lane >> 4, l16 = lane & 15;
+    // A half-warp takes 4 rows of each tile.  Each lane dots its columns of
+    // the 4 rows with its columns of the G <= 4 q heads (16 partial sums),
+    // then a reduce-scatter over the half-warp's 16 lanes (xor 8, 4, 2, 1:
+    // the same pairs, so the same sums, as a butterfly) leaves lane l16
+    // with the whole score of row l16 / 4 and head l16 % 4.  Scores are
+    // kept in base-2 units (scale * log2 e folded into the scale), so one
+    // ex2 per lane gives its probability; the lane keeps its head's running
+    // max and its own share of the head's running sum, and the 16
+    // probabilities reach every lane by shuffles for the weighted sum of
+    // the values it holds.  The outputs are rescaled only in tiles where
+    // some head's max grew (alpha is exactly 1 otherwise).
+    const int hw = lane >> 4, l16 = lane & 15, hb = lane & 16;
+    const int my_g = l16 & 3, my_r = l16 >> 2;
+    const float qscale = a.scale * kLog2e;
     float4 q4[GM][DL], o4[GM][DL];
-    float m_g[GM], l_g[GM];
 #pragma unroll
     for (int g = 0; g < GM; ++g) {
 #pragma unroll
@@ -192,9 +230,9 @@ __global__ void __launch_bounds__(kTmaThreads, D == 64 ? 3 : 2)
                          : make_float4(0.f, 0.f, 0.f, 0.f);
         o4[g][c] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      m_g[g] = -INFINITY;
-      l_g[g] = 0.f;
     }
+    float m_own = -INFINITY;  // running max of head my_g (equal in its 4 lanes)
+    float l_own = 0.f;        // this lane's rows' share of head my_g's running sum
     for (int i = 0; i < ntiles; ++i) {
       const int s = i % NS;
       const uint32_t ph = (i / NS) & 1;
@@ -232,54 +270,71 @@ __global__ void __launch_bounds__(kTmaThreads, D == 64 ? 3 : 2)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);  // the tile is in registers
+      // partial scores over this lane's columns, index r * 4 + g
+      float sp[16];
 #pragma unroll
-      for (int g = 0; g < GM; ++g) {
-        if (g < G) {
-          float sc[kTmaRowsPerHalf];
-          float mt = -INFINITY;
+      for (int r = 0; r < kTmaRowsPerHalf; ++r) {
 #pragma unroll
-          for (int r = 0; r < kTmaRowsPerHalf; ++r) {
-            float acc = q4[g][0].x * kr[r][0].x;
-            acc = fmaf(q4[g][0].y, kr[r][0].y, acc);
-            acc = fmaf(q4[g][0].z, kr[r][0].z, acc);
-            acc = fmaf(q4[g][0].w, kr[r][0].w, acc);
+        for (int g = 0; g < GM; ++g) {
+          float acc = q4[g][0].x * kr[r][0].x;
+          acc = fmaf(q4[g][0].y, kr[r][0].y, acc);
+          acc = fmaf(q4[g][0].z, kr[r][0].z, acc);
+          acc = fmaf(q4[g][0].w, kr[r][0].w, acc);
 #pragma unroll
-            for (int c = 1; c < DL; ++c) {
-              acc = fmaf(q4[g][c].x, kr[r][c].x, acc);
-              acc = fmaf(q4[g][c].y, kr[r][c].y, acc);
-              acc = fmaf(q4[g][c].z, kr[r][c].z, acc);
-              acc = fmaf(q4[g][c].w, kr[r][c].w, acc);
-            }
-            acc += __shfl_xor_sync(0xffffffffu, acc, 8);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 4);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-            sc[r] = tb + r < c1 ? acc * a.scale : -INFINITY;
-            mt = fmaxf(mt, sc[r]);
+          for (int c = 1; c < DL; ++c) {
+            acc = fmaf(q4[g][c].x, kr[r][c].x, acc);
+            acc = fmaf(q4[g][c].y, kr[r][c].y, acc);
+            acc = fmaf(q4[g][c].z, kr[r][c].z, acc);
+            acc = fmaf(q4[g][c].w, kr[r][c].w, acc);
           }
-          const float mn = fmaxf(m_g[g], mt);
-          const float alpha = m_g[g] == -INFINITY ? 0.f : expf(m_g[g] - mn);
-          float ls = l_g[g] * alpha;
-#pragma unroll
-          for (int c = 0; c < DL; ++c)
-            o4[g][c] = make_float4(o4[g][c].x * alpha, o4[g][c].y * alpha, o4[g][c].z * alpha,
-                                   o4[g][c].w * alpha);
-#pragma unroll
-          for (int r = 0; r < kTmaRowsPerHalf; ++r) {
-            const float p = sc[r] == -INFINITY ? 0.f : expf(sc[r] - mn);
-            ls += p;
-#pragma unroll
-            for (int c = 0; c < DL; ++c) {
-              o4[g][c].x = fmaf(p, vr[r][c].x, o4[g][c].x);
-              o4[g][c].y = fmaf(p, vr[r][c].y, o4[g][c].y);
-              o4[g][c].z = fmaf(p, vr[r][c].z, o4[g][c].z);
-              o4[g][c].w = fmaf(p, vr[r][c].w, o4[g][c].w);
-            }
-          }
-          l_g[g] = ls;
-          m_g[g] = mn;
+          sp[r * 4 + g] = acc;
         }
       }
+      reduce_scatter16(sp, l16);
+      const bool live = tb + my_r < c1 && my_g < G;
+      const float sc = live ? sp[0] * qscale : -INFINITY;
+      float mt = fmaxf(sc, __shfl_xor_sync(0xffffffffu, sc, 4));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+      const float mn = fmaxf(m_own, mt);
+      const float p = sc == -INFINITY ? 0.f : ex2_approx(sc - mn);
+      if (__any_sync(0xffffffffu, mn != m_own)) {
+        const float alpha = mn == m_own ? 1.f : (m_own == -INFINITY ? 0.f : ex2_approx(m_own - mn));
+        l_own *= alpha;
+#pragma unroll
+        for (int g = 0; g < GM; ++g) {
+          const float ag = __shfl_sync(0xffffffffu, alpha, hb + g);
+#pragma unroll
+          for (int c = 0; c < DL; ++c)
+            o4[g][c] = make_float4(o4[g][c].x * ag, o4[g][c].y * ag, o4[g][c].z * ag,
+                                   o4[g][c].w * ag);
+        }
+      }
+      m_own = mn;
+      l_own += p;
+#pragma unroll
+      for (int r = 0; r < kTmaRowsPerHalf; ++r) {
+#pragma unroll
+        for (int g = 0; g < GM; ++g) {
+          const float pg = __shfl_sync(0xffffffffu, p, hb + r * 4 + g);
+#pragma unroll
+          for (int c = 0; c < DL; ++c) {
+            o4[g][c].x = fmaf(pg, vr[r][c].x, o4[g][c].x);
+            o4[g][c].y = fmaf(pg, vr[r][c].y, o4[g][c].y);
+            o4[g][c].z = fmaf(pg, vr[r][c].z, o4[g][c].z);
+            o4[g][c].w = fmaf(pg, vr[r][c].w, o4[g][c].w);
+          }
+        }
+      }
+    }
+    // per head: the half-warp's max and sum (the 4 lanes of a head hold
+    // shares of its sum)
+    float l_h = l_own + __shfl_xor_sync(0xffffffffu, l_own, 4);
+    l_h += __shfl_xor_sync(0xffffffffu, l_h, 8);
+    float m_g[GM], l_g[GM];
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+      m_g[g] = __shfl_sync(0xffffffffu, m_own, hb + g);
+      l_g[g] = __shfl_sync(0xffffffffu, l_h, hb + g);
     }
     // the warp's two half-warps meet (lanes l16 and l16 + 16)
 #pragma unroll
@@ -288,8 +343,8 @@ __global__ void __launch_bounds__(kTmaThreads, D == 64 ? 3 : 2)
         const float m2 = __shfl_xor_sync(0xffffffffu, m_g[g], 16);
         const float l2 = __shfl_xor_sync(0xffffffffu, l_g[g], 16);
         const float M = fmaxf(m_g[g], m2);
-        const float a1 = m_g[g] == -INFINITY ? 0.f : expf(m_g[g] - M);
-        const float a2 = m2 == -INFINITY ? 0.f : expf(m2 - M);
+        const float a1 = m_g[g] == -INFINITY ? 0.f : ex2_approx(m_g[g] - M);
+        const float a2 = m2 == -INFINITY ? 0.f : ex2_approx(m2 - M);
 #pragma unroll
         for (int c = 0; c < DL; ++c) {
           float4 o2;
@@ -336,7 +391,7 @@ __global__ void __launch_bounds__(kTmaThreads, D == 64 ? 3 : 2)
 #pragma unroll
     for (int w = 0; w < kTmaConsumers; ++w) {
       const float mw = wm[w * GM + tid];
-      L = fmaf(wl[w * GM + tid], mw == -INFINITY ? 0.f : expf(mw - M), L);
+      L = fmaf(wl[w * GM + tid], mw == -INFINITY ? 0.f : ex2_approx(mw - M), L);
     }
     m_s[tid] = M;
     l_s[tid] = L;
@@ -349,7 +404,7 @@ __global__ void __launch_bounds__(kTmaThreads, D == 64 ? 3 : 2)
 #pragma unroll
     for (int w = 0; w < kTmaConsumers; ++w) {
       const float mw = wm[w * GM + g];
-      O = fmaf(wo[(w * G + g) * d + (idx % d)], mw == -INFINITY ? 0.f : expf(mw - M), O);
+      O = fmaf(wo[(w * G + g) * d + (idx % d)], mw == -INFINITY ? 0.f : ex2_approx(mw - M), O);
     }
     ofin[idx] = O;
   }
@@ -398,7 +453,7 @@ __global__ void __launch_bounds__(kTmaThreads, D == 64 ? 3 : 2)
     float L = 0.f;
     for (int s = lane; s < n_used; s += 32) {
       const float ms = __ldcg(pb + (s * G + g) * (d + 2));
-      const float w = ms == -INFINITY ? 0.f : expf(ms - mx);
+      const float w = ms == -INFINITY ? 0.f : ex2_approx(ms - mx);
       wts[g * n_used + s] = w;
       L = fmaf(__ldcg(pb + (s * G + g) * (d + 2) + 1), w, L);
     }
