@@ -305,6 +305,11 @@ def run_ours(args, rank, world, local_rank):
         return
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     pe0, pe1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # one untimed prefill first (first-use allocations of the prefill scratch)
+    warm = model.new_cache(PROMPT + 8)
+    model.forward_seq(prompt, warm)
+    model.sync()
+    warm.close()
     with torch.cuda.stream(stream):
         pe0.record(stream)
         logits = model.forward_seq(prompt, cache)

@@ -26,7 +26,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O3", "--expt-relaxed-constexpr",
               "-I", str(CSRC), "-I", str(INC)]
 SOURCES = ["api.cu", "gemv.cu", "attn.cu", "prefill.cu", "sample.cu", "tp.cu", "gemm_sm100.cu",
-           "decode_fused.cu", "attn_noalloc.cu", "gemv_i8.cu", "attn_tma.cu",
+           "decode_fused.cu", "decode_fused_group.cu", "attn_noalloc.cu", "gemv_i8.cu", "attn_tma.cu", "attn_prefill_tc.cu",
            "loader.cpp", "rng.cpp"]
 
 

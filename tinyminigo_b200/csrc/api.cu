@@ -115,6 +115,9 @@ struct tmg_ctx {
   // hi/lo BF16 split of the prefill GEMM's activations
   uint16_t *sp_hi = nullptr, *sp_lo = nullptr;
   size_t sp_cap = 0;
+  // BF16 parts of q, k and v^T for the tensor-core prefill attention
+  void* pfa = nullptr;
+  size_t pfa_cap = 0;
   // pinned staging
   void* pinned = nullptr;
   size_t pinned_cap = 0;
@@ -615,6 +618,33 @@ cudaError_t ensure_split(tmg_ctx* c, size_t n) {
   return cudaSuccess;
 }
 
+// Causal prefill attention of T query rows at pos0.. over cache rows
+// [0, pos0 + T): the tcgen05 kernel for head dim 64 (TMG_PREFILL_ATTN=simt
+// keeps the CUDA-core kernel), else the CUDA-core one.
+cudaError_t prefill_attention(tmg_ctx* c, const float* q, int64_t q_ld, const float* kc,
+                              const float* vc, int64_t T, int64_t pos0, float scale, float* out,
+                              int64_t out_ld, int nq, int nkv, int d) {
+  static const bool simt = [] {
+    const char* e = std::getenv("TMG_PREFILL_ATTN");
+    return e && std::strcmp(e, "simt") == 0;
+  }();
+  if (!simt && attn_prefill_tc_ok(q, q_ld, kc, vc, T, pos0, nq, nkv, d, out, out_ld)) {
+    const size_t need = attn_prefill_tc_scratch(nq, nkv, T, pos0 + T);
+    if (c->pfa_cap < need) {
+      TMG_CUDA_TRY(cudaStreamSynchronize(c->stream));
+      if (c->pfa) cudaFree(c->pfa);
+      c->pfa = nullptr;
+      c->pfa_cap = 0;
+      const size_t bytes = need + need / 4;  // room for a few more keys
+      TMG_CUDA_TRY(cudaMalloc(&c->pfa, bytes));
+      c->pfa_cap = bytes;
+    }
+    return launch_attn_prefill_tc(q, q_ld, kc, vc, T, pos0, nq, nkv, scale, out, out_ld, c->pfa,
+                                  c->pfa_cap, c->d_err, c->stream);
+  }
+  return launch_attn_prefill(q, q_ld, kc, vc, T, pos0, nq, nkv, d, scale, out, out_ld, c->stream);
+}
+
 // y (+)= x . W^T for T rows (the prefill GEMM): tcgen05 tensor cores on the
 // hi/lo BF16 split of x; the SIMT kernel only for rows of K % 8 != 0.
 cudaError_t gemm(tmg_ctx* c, const float* x, const uint16_t* w, int64_t T, int64_t N, int64_t K,
@@ -947,8 +977,8 @@ int forward_seq(tmg_ctx* c, tmg_kv* kv, int stream, const uint32_t* tokens, int6
       CK(launch_rope_append(c->QKV, c->qkv_rows, Tc, c->nq, c->nkv, c->d, kv->rope_cos,
                             kv->rope_sin, pos0, kc, vc, c->stream),
          "rope");
-      CK(launch_attn_prefill(c->QKV, c->qkv_rows, kc, vc, Tc, pos0, c->nq, c->nkv, c->d, scale,
-                             c->ATT, int64_t(c->nq) * c->d, c->stream),
+      CK(prefill_attention(c, c->QKV, c->qkv_rows, kc, vc, Tc, pos0, scale, c->ATT,
+                           int64_t(c->nq) * c->d, c->nq, c->nkv, c->d),
          "attention");
       if (tp) {
         CK(gemm(c, c->ATT, Lw.wo, Tc, c->h, int64_t(c->nq) * c->d, c->Xn, c->h, false), "gemm o");
@@ -1438,6 +1468,7 @@ int tmg_create(int device, const tmg_config* cfg, tmg_ctx** out) {
       run("gemm_tc_prepare", gemm_tc_prepare()) && run("prefill_prepare", prefill_prepare()) &&
       run("fused_prepare", fused_prepare()) && run("sample_prepare", sample_prepare()) &&
       run("gemv_i8_prepare", gemv_i8_prepare()) && run("attn_tma_prepare", attn_tma_prepare()) &&
+      run("attn_prefill_tc_prepare", attn_prefill_tc_prepare()) &&
       run("error word", dalloc(c->allocs, &c->d_err, 4)) && run("error word", zero_sync(c, c->d_err, 16));
   if (step) {
     g_create_err = std::string("tmg_create: ") + step + ": " + cudaGetErrorString(ce);
@@ -1467,7 +1498,7 @@ int tmg_destroy(tmg_ctx* c) {
   }
   free_all(c->allocs);
   for (void* p : {(void*)c->X, (void*)c->Xn, (void*)c->QKV, (void*)c->ATT, (void*)c->G,
-                  (void*)c->U, (void*)c->d_tok, c->op_buf, (void*)c->sp_hi, (void*)c->sp_lo,
+                  (void*)c->U, (void*)c->d_tok, c->op_buf, (void*)c->sp_hi, (void*)c->sp_lo, c->pfa,
                   (void*)c->dq, (void*)c->i8acc})
     if (p) cudaFree(p);
   if (c->pinned) cudaFreeHost(c->pinned);
@@ -2390,12 +2421,11 @@ int tmg_op_attn_prefill(tmg_ctx* c, const float* q, const float* keys, const flo
       n_kv <= 0 || n_q % n_kv)
     return fail(c, TMG_ERR_INVALID, "bad argument");
   cudaSetDevice(c->device);
-  CK(launch_attn_prefill(q, int64_t(n_q) * head_dim, keys, values, T, start_pos, n_q, n_kv,
-                         head_dim, 1.0f / sqrtf(float(head_dim)), out, int64_t(n_q) * head_dim,
-                         c->stream),
+  CK(prefill_attention(c, q, int64_t(n_q) * head_dim, keys, values, T, start_pos,
+                       1.0f / sqrtf(float(head_dim)), out, int64_t(n_q) * head_dim, n_q, n_kv,
+                       head_dim),
      "attention");
-  CK(cudaStreamSynchronize(c->stream), "attention");
-  return TMG_OK;
+  return sync_check(c, "tmg_op_attn_prefill");
 }
 
 int tmg_op_argmax(tmg_ctx* c, const float* logits, int64_t V, int32_t rows, uint32_t* out) {

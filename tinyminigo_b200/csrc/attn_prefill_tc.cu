@@ -1,0 +1,560 @@
+// Causal prefill attention on the 5th-generation tensor cores (tcgen05 +
+// TMEM + TMA), head dim 64.
+//
+// The reference's prefill attention (src/model.rs:526-571: per query row t
+// and head, scores q.k * scale over keys 0..pos0+t, softmax, weighted sum of
+// the values) in f32.  Here S = Q K^T and O = P V are tcgen05 MMAs on BF16
+// operands that together carry the f32 values:
+//   * scores: q (pre-multiplied by scale * log2 e, so S comes out in base-2
+//     units) and k are each split into three BF16 parts x = hi + mid + lo
+//     (hi = bf16(x), mid = bf16(x - hi), lo = bf16(x - hi - mid): ~24 bits)
+//     and S accumulates the six products hi.hi, hi.mid, mid.hi, hi.lo,
+//     lo.hi, mid.mid in f32 (the dropped terms are below 2^-26 relative);
+//   * values: p and v are split in two (~16 bits each) and O accumulates
+//     p_hi.v_hi + p_hi.v_lo + p_lo.v_hi.  p lies in [0, 1] and O is a
+//     weighted mean, so this keeps the output within ~2^-16 of |v|.
+// The splits are written by attn_pf_split_* into scratch arrays laid out
+// for TMA: q parts [n_q][Tq][64], k parts [n_kv][Lk][64] and the value
+// parts transposed, [n_kv][64][Lk] (the PV MMA's B operand is K-major).
+//
+// One CTA = 128 query rows of one q head; grid (n_q, query blocks), the
+// heaviest (last) query blocks first.  192 threads:
+//   warp 0     TMA producer: the q parts once, then per 64-key block the k
+//              and v parts into a 2-stage ring (128-byte swizzle);
+//   warp 1     allocates 256 TMEM columns and issues the MMAs (one lane):
+//              S_j into one of two S buffers, then, once the softmax has
+//              written P_j, O_j = P_j V_j into one of two O buffers;
+//   warps 2-5  softmax, one query row per thread (TMEM lane = row): load
+//              S_j (tcgen05.ld), mask (key > query position or past the
+//              keys), running max and sum, p = 2^(s - m) into the P buffer
+//              as BF16 hi/lo in the swizzled K-major layout the MMA reads,
+//              then fold O_{j-1} from TMEM into registers (o = o * alpha +
+//              O_blk), one block behind so that PV_j overlaps softmax_j+1.
+// Every mbarrier wait is bounded; a wait that gives up sets the error word
+// and the CTA stops (the host reports TMG_ERR_TIMEOUT).  Single-GPU code:
+// every CTA loads its own tiles; no peer memory.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace tmg {
+
+namespace {
+
+constexpr int kPD = 64;                       // head dim
+constexpr int kQB = 128;                      // query rows per CTA (MMA M)
+constexpr int kKB = 64;                       // keys per block (S: N; PV: K)
+constexpr int kPfStages = 2;
+constexpr int kQPart = kQB * kPD * 2;         // 16 KB: one BF16 part of the q tile
+constexpr int kKPart = kKB * kPD * 2;         // 8 KB: one part of a k block
+constexpr int kVPart = kPD * kKB * 2;         // 8 KB: one part of a v^T block
+constexpr int kStage = 3 * kKPart + 2 * kVPart;  // 40 KB
+constexpr int kPPart = kQB * kKB * 2;         // 16 KB: one part of a P block
+constexpr int kOffQ = 0;                      // q hi, mid, lo
+constexpr int kOffStage = 3 * kQPart;         // 48 KB
+constexpr int kOffP = kOffStage + kPfStages * kStage;  // 128 KB; P[2] x {hi, lo}
+constexpr int kOffBar = kOffP + 2 * 2 * kPPart;        // 192 KB
+constexpr int kSmemPf = kOffBar + 256 + 1024;          // + barriers + alignment slack
+constexpr int kPfThreads = 192;
+constexpr uint32_t kPfTmemCols = 256;  // S[2] at 0, 64; O[2] at 128, 192
+// kind::f16: BF16 x BF16 -> F32, both K-major, M = 128, N = 64.
+constexpr uint32_t kIdescPf =
+    (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(64 >> 3) << 17) | (uint32_t(128 >> 4) << 24);
+constexpr float kLog2ePf = 1.4426950408889634f;
+
+__device__ __forceinline__ void tma2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0,
+                                      int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// Shared-memory descriptor of a K-major BF16 tile of 128-byte rows written
+// with the 128-byte swizzle (8-row groups 1024 B apart).
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= uint64_t((saddr >> 4) & 0x3fff);
+  d |= uint64_t(1) << 16;
+  d |= uint64_t(1024 >> 4) << 32;
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(2) << 61;
+  return d;
+}
+
+__device__ __forceinline__ void mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+      ::"r"(tmem_d), "l"(da), "l"(db), "r"(kIdescPf), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+__device__ __forceinline__ void commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+// 64 consecutive TMEM columns of this warp's 32 lanes (one row per thread).
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
+  uint32_t r[64];
+#pragma unroll
+  for (int c = 0; c < 64; c += 16)
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+        "%14,%15}, [%16];"
+        : "=r"(r[c + 0]), "=r"(r[c + 1]), "=r"(r[c + 2]), "=r"(r[c + 3]), "=r"(r[c + 4]),
+          "=r"(r[c + 5]), "=r"(r[c + 6]), "=r"(r[c + 7]), "=r"(r[c + 8]), "=r"(r[c + 9]),
+          "=r"(r[c + 10]), "=r"(r[c + 11]), "=r"(r[c + 12]), "=r"(r[c + 13]), "=r"(r[c + 14]),
+          "=r"(r[c + 15])
+        : "r"(taddr + uint32_t(c)));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t bf16_bits(float x) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+
+struct PfArgs {
+  float* out;        // [T, out_ld]: head h at columns h * 64
+  int64_t out_ld;
+  int32_t* err;
+  int T;             // query rows
+  int64_t pos0;      // position of query row 0
+  int Lk;            // keys: pos0 + T
+  int Tq;            // query rows per head in the q arrays (multiple of 128)
+  int Lkp;           // keys per kv head in the k arrays (multiple of 64)
+  int G;             // q heads per kv head
+};
+
+__global__ void __launch_bounds__(kPfThreads, 1)
+    attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap mq_hi,
+                           const __grid_constant__ CUtensorMap mq_mid,
+                           const __grid_constant__ CUtensorMap mq_lo,
+                           const __grid_constant__ CUtensorMap mk_hi,
+                           const __grid_constant__ CUtensorMap mk_mid,
+                           const __grid_constant__ CUtensorMap mk_lo,
+                           const __grid_constant__ CUtensorMap mv_hi,
+                           const __grid_constant__ CUtensorMap mv_lo, const PfArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                           ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kOffBar);  // [2] k/v stage loaded
+  uint64_t* empty = full + kPfStages;                            // [2] k/v stage free
+  uint64_t* qfull = empty + kPfStages;                           // q parts loaded
+  uint64_t* s_full = qfull + 1;                                  // [2] S_j in TMEM
+  uint64_t* p_full = s_full + 2;                                 // [2] P_j in smem (S_j read)
+  uint64_t* o_full = p_full + 2;                                 // [2] O_j in TMEM
+  uint64_t* o_free = o_full + 2;                                 // [2] O_j read
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 2);
+  __shared__ volatile int failed;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.x, kvh = h / a.G;
+  const int qb = int(gridDim.y) - 1 - int(blockIdx.y);
+  const int q0 = qb * kQB;
+  const int64_t last_key = min(int64_t(a.Lk), a.pos0 + q0 + kQB);  // keys [0, last_key)
+  const int nb = int((last_key + kKB - 1) / kKB);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPfStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(qfull, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], 4);
+      mbar_init(&o_full[b], 1);
+      mbar_init(&o_free[b], 4);
+    }
+    failed = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kPfTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer ----
+      mbar_expect_tx(qfull, 3 * kQPart);
+      const int qy = h * a.Tq + q0;
+      tma2d(sm + kOffQ, &mq_hi, qfull, 0, qy);
+      tma2d(sm + kOffQ + kQPart, &mq_mid, qfull, 0, qy);
+      tma2d(sm + kOffQ + 2 * kQPart, &mq_lo, qfull, 0, qy);
+      for (int j = 0; j < nb; ++j) {
+        const int s = j % kPfStages;
+        if (failed || !mbar_wait(&empty[s], ((j / kPfStages) & 1) ^ 1)) {
+          failed = 1;
+          atomicExch(a.err, 2);
+          break;
+        }
+        uint8_t* st = sm + kOffStage + s * kStage;
+        mbar_expect_tx(&full[s], kStage);
+        const int ky = kvh * a.Lkp + j * kKB;
+        tma2d(st, &mk_hi, &full[s], 0, ky);
+        tma2d(st + kKPart, &mk_mid, &full[s], 0, ky);
+        tma2d(st + 2 * kKPart, &mk_lo, &full[s], 0, ky);
+        tma2d(st + 3 * kKPart, &mv_hi, &full[s], j * kKB, kvh * kPD);
+        tma2d(st + 3 * kKPart + kVPart, &mv_lo, &full[s], j * kKB, kvh * kPD);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer ----
+      bool ok = mbar_wait(qfull, 0);
+      const uint32_t qa = smem_u32(sm + kOffQ);
+      const uint32_t qh = qa, qm = qa + kQPart, ql = qa + 2 * kQPart;
+      for (int j = 0; j <= nb && ok; ++j) {
+        if (j < nb) {
+          // S_j = Q K_j^T into S buffer j & 1 (its previous user, S_{j-2},
+          // was read before P_{j-2} arrived, which PV_{j-2} waited for)
+          const int s = j % kPfStages;
+          if (failed || !mbar_wait(&full[s], (j / kPfStages) & 1)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t kb = smem_u32(sm + kOffStage + s * kStage);
+          const uint32_t kh = kb, km = kb + kKPart, kl = kb + 2 * kKPart;
+          const uint32_t ts = tmem + uint32_t((j & 1) * 64);
+#pragma unroll
+          for (int k = 0; k < kPD / 16; ++k) {
+            const uint32_t o = uint32_t(k * 32);
+            mma(ts, sdesc(qh + o), sdesc(kh + o), k != 0);
+            mma(ts, sdesc(qh + o), sdesc(km + o), 1);
+            mma(ts, sdesc(qm + o), sdesc(kh + o), 1);
+            mma(ts, sdesc(qh + o), sdesc(kl + o), 1);
+            mma(ts, sdesc(ql + o), sdesc(kh + o), 1);
+            mma(ts, sdesc(qm + o), sdesc(km + o), 1);
+          }
+          commit(&s_full[j & 1]);
+        }
+        if (j >= 1) {
+          // O_i = P_i V_i for i = j - 1 into O buffer i & 1
+          const int i = j - 1, b = i & 1;
+          if (failed || !mbar_wait(&p_full[b], (i >> 1) & 1) ||
+              (i >= 2 && !mbar_wait(&o_free[b], ((i - 2) >> 1) & 1))) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const int s = i % kPfStages;
+          const uint32_t vb = smem_u32(sm + kOffStage + s * kStage + 3 * kKPart);
+          const uint32_t vh = vb, vl = vb + kVPart;
+          const uint32_t pb = smem_u32(sm + kOffP + b * 2 * kPPart);
+          const uint32_t ph = pb, pl = pb + kPPart;
+          const uint32_t to = tmem + 128u + uint32_t(b * 64);
+#pragma unroll
+          for (int k = 0; k < kKB / 16; ++k) {
+            const uint32_t o = uint32_t(k * 32);
+            mma(to, sdesc(ph + o), sdesc(vh + o), k != 0);
+            mma(to, sdesc(ph + o), sdesc(vl + o), 1);
+            mma(to, sdesc(pl + o), sdesc(vh + o), 1);
+          }
+          commit(&o_full[b]);
+          commit(&empty[s]);  // k/v stage s is free once these MMAs have read it
+        }
+      }
+      if (!ok) {
+        failed = 1;
+        atomicExch(a.err, 2);
+      }
+    }
+  } else {
+    // ---- softmax / output: one query row per thread ----
+    const int qd = warp & 3;                 // TMEM lane quadrant of this warp
+    const int r = qd * 32 + lane;            // row in the query block
+    const int64_t tq = a.pos0 + q0 + r;      // its position
+    const uint32_t lanes = uint32_t(qd * 32) << 16;
+    float o[kPD];
+#pragma unroll
+    for (int c = 0; c < kPD; ++c) o[c] = 0.f;
+    float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nb; ++j) {
+      const int b = j & 1;
+      if (!mbar_wait(&s_full[b], (j >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      float s[kKB];
+      tmem_ld64(tmem + lanes + uint32_t(b * 64), s);
+      const int64_t k0 = int64_t(j) * kKB;
+      float mx = m;
+#pragma unroll
+      for (int c = 0; c < kKB; ++c) {
+        const int64_t key = k0 + c;
+        if (key > tq || key >= a.Lk) s[c] = -INFINITY;
+        mx = fmaxf(mx, s[c]);
+      }
+      const float alpha = m == -INFINITY ? 0.f : ex2f(m - mx);
+      float sum = 0.f;
+      // P_j (row r) into P buffer b: BF16 hi and lo, 16-byte chunk e of the
+      // 128-byte row at chunk e ^ (r & 7) (the 128-byte swizzle).  The buffer
+      // was last read by PV_{j-2}, which completed before O_{j-2} was folded.
+      uint8_t* prow_h = sm + kOffP + b * 2 * kPPart + r * 128;
+      uint8_t* prow_l = prow_h + kPPart;
+#pragma unroll
+      for (int e = 0; e < kKB / 8; ++e) {
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int t = 0; t < 8; t += 2) {
+          const float p0 = s[8 * e + t] == -INFINITY ? 0.f : ex2f(s[8 * e + t] - mx);
+          const float p1 = s[8 * e + t + 1] == -INFINITY ? 0.f : ex2f(s[8 * e + t + 1] - mx);
+          sum += p0;
+          sum += p1;
+          const uint32_t h0 = bf16_bits(p0), h1 = bf16_bits(p1);
+          const float r0 = p0 - __bfloat162float(__ushort_as_bfloat16(uint16_t(h0)));
+          const float r1 = p1 - __bfloat162float(__ushort_as_bfloat16(uint16_t(h1)));
+          hw[t / 2] = h0 | (h1 << 16);
+          lw[t / 2] = bf16_bits(r0) | (bf16_bits(r1) << 16);
+        }
+        const int off = ((e ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(prow_h + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(prow_l + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+      }
+      l = l * alpha + sum;
+      m = mx;
+      // the P writes (generic proxy) before the MMA (async proxy) reads them
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[b]);
+      if (j >= 1) {
+        const int i = j - 1, bi = i & 1;
+        if (!mbar_wait(&o_full[bi], (i >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        float ob[kPD];
+        tmem_ld64(tmem + lanes + 128u + uint32_t(bi * 64), ob);
+#pragma unroll
+        for (int c = 0; c < kPD; ++c) o[c] = fmaf(o[c], alpha_prev, ob[c]);
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&o_free[bi]);
+      }
+      alpha_prev = alpha;
+    }
+    if (ok) {
+      const int i = nb - 1, bi = i & 1;
+      if (!mbar_wait(&o_full[bi], (i >> 1) & 1)) {
+        ok = false;
+      } else {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        float ob[kPD];
+        tmem_ld64(tmem + lanes + 128u + uint32_t(bi * 64), ob);
+#pragma unroll
+        for (int c = 0; c < kPD; ++c) o[c] = fmaf(o[c], alpha_prev, ob[c]);
+      }
+    }
+    if (!ok) {
+      failed = 1;
+      atomicExch(a.err, 2);
+    } else if (q0 + r < a.T) {
+      float* dst = a.out + int64_t(q0 + r) * a.out_ld + int64_t(h) * kPD;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+      for (int c = 0; c < kPD; c += 4)
+        *reinterpret_cast<float4*>(dst + c) =
+            make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kPfTmemCols));
+  }
+}
+
+// Three-way BF16 split of x: hi = bf16(x), mid = bf16(x - hi), lo = bf16(x - hi - mid).
+__device__ __forceinline__ void split3(float x, uint16_t* hi, uint16_t* mid, uint16_t* lo) {
+  const __nv_bfloat16 h = __float2bfloat16_rn(x);
+  const float r1 = x - __bfloat162float(h);
+  const __nv_bfloat16 m = __float2bfloat16_rn(r1);
+  const float r2 = r1 - __bfloat162float(m);
+  *hi = __bfloat16_as_ushort(h);
+  *mid = __bfloat16_as_ushort(m);
+  *lo = __bfloat16_as_ushort(__float2bfloat16_rn(r2));
+}
+
+// q rows (T of them, row stride q_ld, head h at columns h * 64) times qs,
+// split three ways into [n_q][Tq][64] (rows T..Tq-1 zero).  Grid (Tq / 4,
+// n_q), 256 threads: 4 rows of 64 per block.
+__global__ void attn_pf_split_q_kernel(const float* __restrict__ q, int64_t q_ld, int T, int Tq,
+                                       float qs, uint16_t* __restrict__ hi,
+                                       uint16_t* __restrict__ mid, uint16_t* __restrict__ lo) {
+  const int h = blockIdx.y;
+  const int t = blockIdx.x * 4 + (threadIdx.x >> 6), c = threadIdx.x & 63;
+  const float x = t < T ? q[int64_t(t) * q_ld + int64_t(h) * kPD + c] * qs : 0.f;
+  const int64_t o = (int64_t(h) * Tq + t) * kPD + c;
+  split3(x, hi + o, mid + o, lo + o);
+}
+
+// The cache rows [0, Lk) of one kv head: k split three ways into
+// [n_kv][Lkp][64]; v split in two and transposed into [n_kv][64][Lkp]
+// (keys Lk..Lkp-1 zero).  Grid (Lkp / 64, n_kv), 256 threads: one 64-key
+// block per CTA.
+__global__ void attn_pf_split_kv_kernel(const float* __restrict__ kc, const float* __restrict__ vc,
+                                        int64_t kvd, int Lk, int Lkp, uint16_t* __restrict__ khi,
+                                        uint16_t* __restrict__ kmid, uint16_t* __restrict__ klo,
+                                        uint16_t* __restrict__ vhi, uint16_t* __restrict__ vlo) {
+  __shared__ float vs[kKB][kPD + 1];
+  const int kvh = blockIdx.y, key0 = blockIdx.x * kKB;
+  for (int i = threadIdx.x; i < kKB * kPD; i += blockDim.x) {
+    const int kk = i / kPD, c = i % kPD;
+    const int key = key0 + kk;
+    const bool in = key < Lk;
+    const float kx = in ? kc[int64_t(key) * kvd + int64_t(kvh) * kPD + c] : 0.f;
+    vs[kk][c] = in ? vc[int64_t(key) * kvd + int64_t(kvh) * kPD + c] : 0.f;
+    const int64_t o = (int64_t(kvh) * Lkp + key) * kPD + c;
+    split3(kx, khi + o, kmid + o, klo + o);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < kKB * kPD; i += blockDim.x) {
+    const int c = i / kKB, kk = i % kKB;
+    const float v = vs[kk][c];
+    const __nv_bfloat16 hb = __float2bfloat16_rn(v);
+    const int64_t o = (int64_t(kvh) * kPD + c) * Lkp + key0 + kk;
+    vhi[o] = __bfloat16_as_ushort(hb);
+    vlo[o] = __bfloat16_as_ushort(__float2bfloat16_rn(v - __bfloat162float(hb)));
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_pf() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &qr) ==
+            cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2D BF16 [rows, cols] row-major map with a (64 x box_rows) box and the
+// 128-byte swizzle.
+bool map_bf16(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows) {
+  auto fn = encode_pf();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(cols) * 2};
+  cuuint32_t box[2] = {64u, cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+}  // namespace
+
+size_t attn_prefill_tc_scratch(int nq, int nkv, int64_t T, int64_t Lk) {
+  const int64_t Tq = round_up(T, kQB), Lkp = round_up(Lk, kKB);
+  return size_t(3 * nq * Tq * kPD + 3 * nkv * Lkp * kPD + 2 * nkv * kPD * Lkp) * 2 + 6 * 256;
+}
+
+bool attn_prefill_tc_ok(const float* q, int64_t q_ld, const float* kc, const float* vc, int64_t T,
+                        int64_t pos0, int nq, int nkv, int d, const float* out, int64_t out_ld) {
+  if (d != kPD || nkv <= 0 || nq % nkv || T <= 0 || pos0 < 0) return false;
+  if (pos0 + T > (int64_t(1) << 30) || int64_t(nq) * round_up(T, kQB) > (int64_t(1) << 30) ||
+      int64_t(nkv) * round_up(pos0 + T, kKB) > (int64_t(1) << 30))
+    return false;
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || out_ld % 4) return false;
+  (void)q;
+  (void)q_ld;
+  (void)kc;
+  (void)vc;
+  return encode_pf() != nullptr;
+}
+
+cudaError_t attn_prefill_tc_prepare() {
+  return set_carveout(attn_prefill_tc_kernel, kSmemPf);
+}
+
+cudaError_t launch_attn_prefill_tc(const float* q, int64_t q_ld, const float* kc, const float* vc,
+                                   int64_t T, int64_t pos0, int nq, int nkv, float scale,
+                                   float* out, int64_t out_ld, void* scratch, size_t scratch_bytes,
+                                   int32_t* err, cudaStream_t s) {
+  if (!attn_prefill_tc_ok(q, q_ld, kc, vc, T, pos0, nq, nkv, kPD, out, out_ld) || !err)
+    return cudaErrorInvalidValue;
+  const int64_t Lk = pos0 + T;
+  const int64_t Tq = round_up(T, kQB), Lkp = round_up(Lk, kKB);
+  if (scratch_bytes < attn_prefill_tc_scratch(nq, nkv, T, Lk)) return cudaErrorInvalidValue;
+  // carve the scratch: every array 256-byte aligned
+  uint8_t* p = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(scratch) + 255) &
+                                          ~uintptr_t(255));
+  auto take = [&](int64_t elems) {
+    uint16_t* r = reinterpret_cast<uint16_t*>(p);
+    p += (elems * 2 + 255) / 256 * 256;
+    return r;
+  };
+  const int64_t nqe = int64_t(nq) * Tq * kPD, nke = int64_t(nkv) * Lkp * kPD;
+  uint16_t *qh = take(nqe), *qm = take(nqe), *ql = take(nqe);
+  uint16_t *kh = take(nke), *km = take(nke), *kl = take(nke);
+  uint16_t *vh = take(nke), *vl = take(nke);
+  if (p > reinterpret_cast<uint8_t*>(scratch) + scratch_bytes) return cudaErrorInvalidValue;
+  const int64_t kvd = int64_t(nkv) * kPD;
+  attn_pf_split_q_kernel<<<dim3(unsigned(Tq / 4), unsigned(nq)), 256, 0, s>>>(
+      q, q_ld, int(T), int(Tq), scale * kLog2ePf, qh, qm, ql);
+  TMG_CUDA_TRY(cudaGetLastError());
+  attn_pf_split_kv_kernel<<<dim3(unsigned(Lkp / kKB), unsigned(nkv)), 256, 0, s>>>(
+      kc, vc, kvd, int(Lk), int(Lkp), kh, km, kl, vh, vl);
+  TMG_CUDA_TRY(cudaGetLastError());
+  CUtensorMap mqh, mqm, mql, mkh, mkm, mkl, mvh, mvl;
+  if (!map_bf16(&mqh, qh, int64_t(nq) * Tq, kPD, kQB) ||
+      !map_bf16(&mqm, qm, int64_t(nq) * Tq, kPD, kQB) ||
+      !map_bf16(&mql, ql, int64_t(nq) * Tq, kPD, kQB) ||
+      !map_bf16(&mkh, kh, int64_t(nkv) * Lkp, kPD, kKB) ||
+      !map_bf16(&mkm, km, int64_t(nkv) * Lkp, kPD, kKB) ||
+      !map_bf16(&mkl, kl, int64_t(nkv) * Lkp, kPD, kKB) ||
+      !map_bf16(&mvh, vh, int64_t(nkv) * kPD, Lkp, kPD) ||
+      !map_bf16(&mvl, vl, int64_t(nkv) * kPD, Lkp, kPD))
+    return cudaErrorInvalidValue;
+  PfArgs a;
+  a.out = out;
+  a.out_ld = out_ld;
+  a.err = err;
+  a.T = int(T);
+  a.pos0 = pos0;
+  a.Lk = int(Lk);
+  a.Tq = int(Tq);
+  a.Lkp = int(Lkp);
+  a.G = nq / nkv;
+  attn_prefill_tc_kernel<<<dim3(unsigned(nq), unsigned(Tq / kQB)), kPfThreads, kSmemPf, s>>>(
+      mqh, mqm, mql, mkh, mkm, mkl, mvh, mvl, a);
+  return cudaGetLastError();
+}
+
+}  // namespace tmg

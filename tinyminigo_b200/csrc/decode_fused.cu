@@ -43,9 +43,19 @@
 #include "common.cuh"
 #include "fused.cuh"
 
+// 0: the single-GPU kernels (and the host side); 1: the same kernels for a
+// group of GPUs (decode_fused_group.cu), where exchanged words, KV appends
+// and the grid barrier reach every rank.  A compile-time switch, so the
+// single-GPU kernels carry none of the group's branches.
+#ifndef TMG_FUSED_GROUP
+#define TMG_FUSED_GROUP 0
+#endif
+
 namespace tmg {
 
 namespace {
+
+constexpr bool kGroup = TMG_FUSED_GROUP != 0;
 
 constexpr int kCWarps = 8;                         // consumer warps
 constexpr int kCThreads = kCWarps * kWarp;         // 256
@@ -311,7 +321,7 @@ __device__ bool grid_sync(const FusedArgs& a, unsigned int& target, Shared& S,
     if (tr) tr[0] = global_ns();
     int ok = S.abort ? 0 : 1;
     target += S.gn;
-    const bool sys = a.world > 1;
+    constexpr bool sys = kGroup;
     if (ok) {
       if (sys) {
         // every rank's counter: this CTA's writes of the step (KV appends,
@@ -514,7 +524,7 @@ __device__ __forceinline__ unsigned long long tag_word(float v, uint32_t tag) {
 __device__ __forceinline__ void ll_store(const Shared& S, unsigned long long* p, float v,
                                          uint32_t tag) {
   const unsigned long long w = tag_word(v, tag);
-  if (S.world == 1) {
+  if (!kGroup) {
     st_tag(p, w, false);
     return;
   }
@@ -525,7 +535,7 @@ __device__ __forceinline__ void ll_store(const Shared& S, unsigned long long* p,
 __device__ __forceinline__ void part_store(const Shared& S, unsigned long long* p, float v,
                                            uint32_t tag) {
   const unsigned long long w = tag_word(v, tag);
-  if (S.world == 1) {
+  if (!kGroup) {
     st_tag(p, w, false);
     return;
   }
@@ -579,7 +589,7 @@ __device__ __noinline__ bool ll_gather(float* dst, const unsigned long long* src
   unsigned int spins = 0;
   bool ok = true;
   float ss = 0.f;
-  const bool sys = S.world > 1;
+  constexpr bool sys = kGroup;
   ulonglong2 v[kGatherPairs];
   uint32_t need = 0;  // bit k: pair k still to come
 #pragma unroll
@@ -644,7 +654,7 @@ __device__ __forceinline__ bool ll_gather3(const LLRange* r, int nr, uint32_t ta
                                         const unsigned int* abort_word, Shared& S, uint32_t& gc) {
   ulonglong2 v[3];
   uint32_t need = 0;
-  const bool sys = S.world > 1;
+  constexpr bool sys = kGroup;
 #pragma unroll
   for (int k = 0; k < 3; ++k) {
     if (k < nr && threadIdx.x * 2 < r[k].n) {
@@ -684,7 +694,7 @@ __device__ __forceinline__ bool ll_gather3(const LLRange* r, int nr, uint32_t ta
 // Give up: raise the kernel-wide abort word and the error word.
 __device__ __forceinline__ void raise_abort(const FusedArgs& a) {
   if (threadIdx.x == 0) {
-    if (a.world > 1)
+    if (kGroup)
       for (int r = 0; r < a.world; ++r) atomicExch_system(a.bar_peer[r] + 2, 1u);
     else
       atomicExch(a.bar + 2, 1u);
@@ -975,7 +985,7 @@ __device__ __forceinline__ int gemv_kseg(int ngroups, int K, int chunks, const f
 // step's grid barrier releases them before any rank reads those rows).
 __device__ __forceinline__ void kv_put(const FusedArgs& a, const FusedLayer& L, int l, int which,
                                        size_t idx, float v) {
-  if (a.world == 1) {
+  if (!kGroup) {
     (which ? L.vc : L.kc)[idx] = v;
     return;
   }
@@ -1520,7 +1530,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
         if (threadIdx.x == 0) {
           unsigned long long bb = 0;
           for (int w = 0; w < kCWarps; ++w) bb = S.best[w] > bb ? S.best[w] : bb;
-          if (a.world == 1) {
+          if (!kGroup) {
             a.am_part[blockIdx.x] = bb;
           } else {  // every rank's table, at this CTA's index in the joint grid
             for (int r = 0; r < a.world; ++r)
@@ -1643,6 +1653,31 @@ bool local_ok_k(int64_t ngroups, int num_sms, int rpc) {
 
 }  // namespace
 
+#if TMG_FUSED_GROUP
+// The group instances: prepared with the single-GPU ones and launched by
+// launch_decode_fused when the arguments name more than one rank.
+cudaError_t fused_group_prepare(bool* regs_ok) {
+  TMG_CUDA_TRY((prepare_one<64, 8, 2>()));
+  TMG_CUDA_TRY((prepare_one<128, 4, 1>()));
+  TMG_CUDA_TRY((prepare_one<128, 8, 2>()));
+  *regs_ok = g_regs_ok;
+  return cudaSuccess;
+}
+
+cudaError_t fused_group_launch(const cudaLaunchConfig_t& cfg, const FusedArgs& a, int nst, int ra,
+                               int rb) {
+  if (a.d == 64 && ra == 8 && rb == 2) return cudaLaunchKernelEx(&cfg, decode_fused_kernel<64, 8, 2>, a, nst);
+  if (a.d == 128 && ra == 8 && rb == 2)
+    return cudaLaunchKernelEx(&cfg, decode_fused_kernel<128, 8, 2>, a, nst);
+  if (a.d == 128 && ra == 4 && rb == 1)
+    return cudaLaunchKernelEx(&cfg, decode_fused_kernel<128, 4, 1>, a, nst);
+  return cudaErrorInvalidValue;
+}
+#else
+namespace {
+bool g_group_regs_ok = true;  // the group instances' register counts (fused_group_prepare)
+}  // namespace
+
 bool fused_supported(int h, int nq, int nkv, int d, int I, int64_t V, int num_sms) {
   if (!g_regs_ok || nkv <= 0 || nq % nkv != 0) return false;
   const int G = nq / nkv, q_dim = nq * d;
@@ -1718,11 +1753,13 @@ size_t fused_smem(int h, int q_dim, int I, int d, int G, int nsplit, int L, int 
 cudaError_t fused_prepare() {
   TMG_CUDA_TRY((prepare_one<64, 8, 2>()));
   TMG_CUDA_TRY((prepare_one<128, 4, 1>()));
-  return prepare_one<128, 8, 2>();
+  TMG_CUDA_TRY((prepare_one<128, 8, 2>()));
+  return fused_group_prepare(&g_group_regs_ok);
 }
 
 int fused_group_ctas(int h, int nq, int nkv, int d, int I, int64_t V, int num_sms, int world) {
-  if (world < 1 || world > kMaxGroupRanks || !fused_supported(h, nq, nkv, d, I, V, num_sms))
+  if (world < 1 || world > kMaxGroupRanks || !fused_supported(h, nq, nkv, d, I, V, num_sms) ||
+      (world > 1 && !g_group_regs_ok))
     return 0;
   const int rpc_h = kCWarps / ksplit_host(h), rpc_q = kCWarps / ksplit_host(nq * d),
             rpc_i = kCWarps / ksplit_host(I);
@@ -1774,6 +1811,7 @@ cudaError_t launch_decode_fused(const FusedArgs& args, int grid, cudaStream_t s,
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (a.world > 1) return fused_group_launch(cfg, a, nst, ra, rb);
   if (a.d == 64 && ra == 8 && rb == 2) return cudaLaunchKernelEx(&cfg, decode_fused_kernel<64, 8, 2>, a, nst);
   if (a.d == 128 && ra == 8 && rb == 2)
     return cudaLaunchKernelEx(&cfg, decode_fused_kernel<128, 8, 2>, a, nst);
@@ -1781,5 +1819,6 @@ cudaError_t launch_decode_fused(const FusedArgs& args, int grid, cudaStream_t s,
     return cudaLaunchKernelEx(&cfg, decode_fused_kernel<128, 4, 1>, a, nst);
   return cudaErrorInvalidValue;
 }
+#endif  // TMG_FUSED_GROUP
 
 }  // namespace tmg

@@ -107,5 +107,10 @@ int fused_group_ctas(int h, int nq, int nkv, int d, int I, int64_t V, int num_sm
 cudaError_t fused_zero(const FusedArgs& a, cudaStream_t s);
 // Cooperative launch of `grid` CTAs (one per SM at most).
 cudaError_t launch_decode_fused(const FusedArgs& a, int grid, cudaStream_t s, bool zero = true);
+// The group instances (decode_fused_group.cu): prepared by fused_prepare,
+// launched by launch_decode_fused for world > 1.
+cudaError_t fused_group_prepare(bool* regs_ok);
+cudaError_t fused_group_launch(const cudaLaunchConfig_t& cfg, const FusedArgs& a, int nst, int ra,
+                               int rb);
 
 }  // namespace tmg

@@ -210,6 +210,17 @@ cudaError_t launch_rope_rows(float* x, int64_t ld, int64_t rows, int n_heads, in
 cudaError_t launch_attn_prefill(const float* q, int64_t q_ld, const float* kc, const float* vc,
                                 int64_t T, int64_t pos0, int nq, int nkv, int d, float scale,
                                 float* out, int64_t out_ld, cudaStream_t s);
+// The same attention on tcgen05 tensor cores (attn_prefill_tc.cu), head dim
+// 64: q, k and v^T are split into BF16 parts in `scratch` (at least
+// attn_prefill_tc_scratch bytes) by two kernels before the MMA kernel.
+bool attn_prefill_tc_ok(const float* q, int64_t q_ld, const float* kc, const float* vc, int64_t T,
+                        int64_t pos0, int nq, int nkv, int d, const float* out, int64_t out_ld);
+size_t attn_prefill_tc_scratch(int nq, int nkv, int64_t T, int64_t Lk);
+cudaError_t attn_prefill_tc_prepare();
+cudaError_t launch_attn_prefill_tc(const float* q, int64_t q_ld, const float* kc, const float* vc,
+                                   int64_t T, int64_t pos0, int nq, int nkv, float scale,
+                                   float* out, int64_t out_ld, void* scratch, size_t scratch_bytes,
+                                   int32_t* err, cudaStream_t s);
 // out = gate / (1 + exp(-gate)) * up.
 cudaError_t launch_swiglu(const float* gate, const float* up, int64_t n, float* out,
                           cudaStream_t s);
