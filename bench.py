@@ -936,7 +936,11 @@ def run_attn(args, rank, world, local_rank):
                               "traffic": None, "peak_kind": peak_kind},
                     prefill_attention={"ms": round(ms_pf, 3),
                                        "tflops": round(pf_flop / (ms_pf / 1e3) / 1e12, 1),
-                                       "kernel": "attn_prefill_tiled_kernel<64>"},
+                                       "kernel": ("attn_prefill_tiled_kernel<64>"
+                                                  if os.environ.get("TMG_PREFILL_ATTN") == "simt"
+                                                  else "attn_pf_split_q/kv_kernel + "
+                                                       "attn_prefill_tc_kernel"),
+                                       "flops": "algorithmic: 4 d per (q head, row, visible key)"},
                     timing="CUDA events around the op call (includes its ticket memset and "
                            "position upload for decode)")
     res["dtype"] = "f32"

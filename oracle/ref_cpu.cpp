@@ -29,6 +29,7 @@
 #include <immintrin.h>
 #include <cmath>
 #include <cstdint>
+#include <cstdio>
 #include <cstring>
 #include <cstdlib>
 #include <vector>
@@ -620,6 +621,8 @@ struct Model {
            nkv = c.num_key_value_heads, I = c.intermediate_size;
     size_t group = nq / nkv;
     std::memcpy(x.data(), &embed[size_t(token) * h], h * sizeof(float));
+    const bool debug = std::getenv("TMG_DEBUG") != nullptr;  // src/model.rs:406-409
+    if (debug) debug_first8("embed first8: ", x.data(), h);
     for (int li = 0; li < c.num_hidden_layers; ++li) {
       Layer& lw = layers[li];
       rms_norm_into(x.data(), lw.in_norm.data(), c.rms_norm_eps, h, attn_in.data());
@@ -656,6 +659,8 @@ struct Model {
       for (size_t j = 0; j < h; ++j) x[j] += proj[j];
 
       rms_norm_into(x.data(), lw.post_norm.data(), c.rms_norm_eps, h, mlp_in.data());
+      if (debug)  // src/model.rs:468-470
+        debug_first8(("L" + std::to_string(li) + " attn_out first8: ").c_str(), x.data(), h);
       matmul_w_into(mlp_in.data(), lw.w_gate, I, h, gate.data());
       matmul_w_into(mlp_in.data(), lw.w_up, I, h, up.data());
       for (size_t j = 0; j < I; ++j) {
@@ -665,9 +670,29 @@ struct Model {
       }
       matmul_w_into(gate.data(), lw.w_down, h, I, down.data());
       for (size_t j = 0; j < h; ++j) x[j] += down[j];
+      if (debug)  // src/model.rs:480-482
+        debug_first8(("L" + std::to_string(li) + " out first8: ").c_str(), x.data(), h);
     }
     rms_norm_into(x.data(), final_norm.data(), c.rms_norm_eps, h, attn_in.data());
     matmul_w_into(attn_in.data(), lm_head, c.vocab_size, h, logits);
+  }
+
+  // eprintln!("{label}{:?}", &x[..8]): the slice in Rust's Debug form (every
+  // value the shortest decimal that reads back as the same f32).
+  static void debug_first8(const char* label, const float* v, size_t h) {
+    std::string line(label);
+    line += "[";
+    for (size_t i = 0; i < std::min<size_t>(8, h); ++i) {
+      char buf[48];
+      for (int prec = 1; prec <= 9; ++prec) {
+        std::snprintf(buf, sizeof buf, "%.*g", prec, double(v[i]));
+        if (std::strtof(buf, nullptr) == v[i]) break;
+      }
+      line += (i ? ", " : "");
+      line += buf;
+    }
+    line += "]\n";
+    std::fputs(line.c_str(), stderr);
   }
 
   // forward_seq, src/model.rs:503-590

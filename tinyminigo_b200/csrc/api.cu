@@ -13,10 +13,14 @@
 #include <dlfcn.h>
 #include <math.h>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include <algorithm>
 #include <chrono>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <functional>
 #include <string>
 #include <vector>
 
@@ -57,6 +61,10 @@ struct tmg_ctx {
   int num_sms = 148;
   bool has_model = false;
   bool finalized = false;
+  // TMG_DEBUG set when the context was created (src/model.rs:406): the
+  // per-token forward prints the first 8 values of the embedding and of
+  // each layer's residual stream after attention and after the MLP
+  bool debug = false;
   tmg_config cfg{};
   // tensor parallel
   int rank = 0, world = 1;
@@ -567,6 +575,7 @@ int alloc_model(tmg_ctx* c) {
     if (p > 0 && p <= 5 * c->L && p % 5 != 1) c->test_stall = p;
   }
   if (const char* tm = getenv("TMG_TEST_FUSED_POLL_MS")) c->test_poll_ms = std::max(1, atoi(tm));
+  c->debug = getenv("TMG_DEBUG") != nullptr;
   c->has_model = true;
   return TMG_OK;
 }
@@ -604,6 +613,14 @@ int ensure_prefill(tmg_ctx* c, int64_t T) {
   c->pf_cap = Tc;
   return TMG_OK;
 }
+
+// A profiler (NVTX) range for the life of a scope; no cost without a tool.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 cudaError_t ensure_split(tmg_ctx* c, size_t n) {
   if (c->sp_cap >= n) return cudaSuccess;
@@ -749,12 +766,18 @@ struct TraceCtx {
   }
 };
 
+// A host callback at a point of the forward (debug prints): (layer, what)
+// with what 0 = the embedding (layer -1), 1 = after the attention residual,
+// 2 = after the MLP residual.  The forward is then enqueued eagerly.
+using DebugHook = std::function<cudaError_t(int, int)>;
+
 cudaError_t enqueue_forward(tmg_ctx* c, tmg_kv* kv, const StreamState& st, bool argmax,
-                            Prof* prof = nullptr, TraceCtx* trc = nullptr) {
+                            Prof* prof = nullptr, TraceCtx* trc = nullptr,
+                            const DebugHook* dbg = nullptr) {
   TraceCtx none;
   TraceCtx& tc = trc ? *trc : none;
   const int M = kv->M;
-  const bool pdl = prof == nullptr;
+  const bool pdl = prof == nullptr && dbg == nullptr;
   auto B = [&]() {
     if (prof) prof->begin();
   };
@@ -792,6 +815,7 @@ cudaError_t enqueue_forward(tmg_ctx* c, tmg_kv* kv, const StreamState& st, bool 
     if (c->i8) {
       B();
       if (l == 0) TMG_CUDA_TRY(launch_embed(c->embed, st.token, M, c->h, c->x, c->stream));
+      if (l == 0 && dbg) TMG_CUDA_TRY((*dbg)(-1, 0));
       TMG_CUDA_TRY(gemv8(Lw.qqkv, Lw.sqkv, nullptr, nullptr, c->x, Lw.in_norm, c->qkv,
                          c->qkv_rows, c->qkv_rows, c->h, EPI_STORE));
       E(0);
@@ -816,6 +840,7 @@ cudaError_t enqueue_forward(tmg_ctx* c, tmg_kv* kv, const StreamState& st, bool 
       B();
       TMG_CUDA_TRY(gemv(c, A, PRO_EMBED_NORM, EPI_STORE, pdl));
       E(0);
+      if (dbg) TMG_CUDA_TRY((*dbg)(-1, 0));
     } else {
       A.x = c->x;
       B();
@@ -866,6 +891,7 @@ cudaError_t enqueue_forward(tmg_ctx* c, tmg_kv* kv, const StreamState& st, bool 
       TMG_CUDA_TRY(tp_reduce_add(c, c->partial, c->x, int64_t(M) * c->h));
       E(6);
     }
+    if (dbg) TMG_CUDA_TRY((*dbg)(l, 1));
     GemvArgs GU;
     GU.w = Lw.wg;
     GU.w2 = Lw.wu;
@@ -906,6 +932,7 @@ cudaError_t enqueue_forward(tmg_ctx* c, tmg_kv* kv, const StreamState& st, bool 
       TMG_CUDA_TRY(tp_reduce_add(c, c->partial, c->x, int64_t(M) * c->h));
       E(6);
     }
+    if (dbg) TMG_CUDA_TRY((*dbg)(l, 2));
   }
   GemvArgs H;
   H.w = c->lm_head;
@@ -968,6 +995,10 @@ int forward_seq(tmg_ctx* c, tmg_kv* kv, int stream, const uint32_t* tokens, int6
     CK(launch_embed(c->embed, dtok, Tc, c->h, c->X, c->stream), "embed");
     for (int l = 0; l < c->L; ++l) {
       const Layer& Lw = c->layers[l];
+      // one profiler range per layer of the chunk (host side: the enqueues)
+      char rname[48];
+      std::snprintf(rname, sizeof rname, "prefill layer %d", l);
+      NvtxRange layer_range(rname);
       float* kc = kv->k[l] + size_t(stream) * kv->cap * kvd;
       float* vc = kv->v[l] + size_t(stream) * kv->cap * kvd;
       CK(launch_rmsnorm(c->X, Lw.in_norm, eps, c->h, Tc, 1, c->Xn, c->stream), "rmsnorm");
@@ -1757,6 +1788,46 @@ int tmg_kv_read(tmg_kv* kv, int32_t layer, int32_t stream, float* keys, float* v
   return TMG_OK;
 }
 
+// One f32 as Rust's `{:?}` writes it: the shortest decimal that reads back
+// as the same f32, with ".0" on integral values.
+std::string f32_debug(float v) {
+  if (std::isnan(v)) return "NaN";
+  if (std::isinf(v)) return v > 0 ? "inf" : "-inf";
+  char buf[48];
+  for (int prec = 1; prec <= 9; ++prec) {
+    std::snprintf(buf, sizeof buf, "%.*g", prec, double(v));
+    if (std::strtof(buf, nullptr) == v) break;
+  }
+  std::string t(buf);
+  const size_t e = t.find('e');
+  if (e != std::string::npos) {  // 1e-07 -> 1e-7
+    std::string mant = t.substr(0, e), ex = t.substr(e + 1);
+    const bool neg = !ex.empty() && ex[0] == '-';
+    if (!ex.empty() && (ex[0] == '-' || ex[0] == '+')) ex = ex.substr(1);
+    while (ex.size() > 1 && ex[0] == '0') ex = ex.substr(1);
+    return mant + "e" + (neg ? "-" : "") + ex;
+  }
+  if (t.find('.') == std::string::npos) t += ".0";
+  return t;
+}
+
+// The TMG_DEBUG lines of src/model.rs:406-409, 468-470, 480-482 for stream
+// 0 of a per-token forward: "embed first8: [...]", "L<i> attn_out first8:
+// [...]" (the residual stream after attention), "L<i> out first8: [...]".
+cudaError_t debug_print(tmg_ctx* c, int layer, int what) {
+  TMG_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  float v[8];
+  const int n = std::min(8, c->h);
+  TMG_CUDA_TRY(cudaMemcpy(v, c->x, size_t(n) * 4, cudaMemcpyDeviceToHost));
+  std::string line = what == 0 ? std::string("embed first8: [")
+                               : "L" + std::to_string(layer) +
+                                     (what == 1 ? " attn_out first8: [" : " out first8: [");
+  for (int i = 0; i < n; ++i) line += (i ? ", " : "") + f32_debug(v[i]);
+  line += "]\n";
+  std::fputs(line.c_str(), stderr);
+  return cudaSuccess;
+}
+
 int tmg_forward_token(tmg_ctx* c, tmg_kv* kv, const uint32_t* tokens, float* logits) {
   if (!c || !kv || !tokens || kv->ctx != c) return fail(c, TMG_ERR_INVALID, "bad argument");
   if (!c->finalized) return fail(c, TMG_ERR_INVALID, "weights not finalized");
@@ -1776,7 +1847,14 @@ int tmg_forward_token(tmg_ctx* c, tmg_kv* kv, const uint32_t* tokens, float* log
   std::memcpy(c->pinned, s.data(), s.size() * 4);
   CK(cudaMemcpyAsync(kv->d_state, c->pinned, s.size() * 4, cudaMemcpyHostToDevice, c->stream),
      "tokens");
-  if (!kv->g_plain) {
+  if (c->debug) {
+    // eagerly, with the reference's debug lines between the sublayers
+    const DebugHook hook = [c](int l, int what) { return debug_print(c, l, what); };
+    nvtxRangePushA("forward_token");
+    const cudaError_t ce = enqueue_forward(c, kv, kv->st, false, nullptr, nullptr, &hook);
+    nvtxRangePop();
+    CK(ce, "forward (TMG_DEBUG)");
+  } else if (!kv->g_plain) {
     cudaGraph_t g = nullptr;
     CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "capture");
     cudaError_t ce = enqueue_forward(c, kv, kv->st, false);
@@ -1790,7 +1868,12 @@ int tmg_forward_token(tmg_ctx* c, tmg_kv* kv, const uint32_t* tokens, float* log
     cudaGraphDestroy(g);
     CK(ce, "instantiate");
   }
-  CK(cudaGraphLaunch(kv->g_plain, c->stream), "forward");
+  if (!c->debug) {
+    nvtxRangePushA("forward_token");
+    const cudaError_t ce = cudaGraphLaunch(kv->g_plain, c->stream);
+    nvtxRangePop();
+    CK(ce, "forward");
+  }
   if (logits)
     for (int m = 0; m < kv->M; ++m)
       CK(cudaMemcpyAsync(logits + size_t(m) * c->V, logits_row(c, m), size_t(c->V) * 4,
@@ -1896,6 +1979,7 @@ static int prepare_decode(tmg_ctx* c, tmg_kv* kv, const uint32_t* tokens, int64_
 int tmg_decode(tmg_ctx* c, tmg_kv* kv, const uint32_t* tokens, int64_t n_steps, uint32_t* out) {
   if (!c || !kv || kv->ctx != c || !tokens) return fail(c, TMG_ERR_INVALID, "bad argument");
   cudaSetDevice(c->device);
+  NvtxRange range("decode");
   StreamState st;
   int rc = prepare_decode(c, kv, tokens, n_steps, &st);
   if (rc) return rc;

@@ -18,18 +18,22 @@
 // parts transposed, [n_kv][64][Lk] (the PV MMA's B operand is K-major).
 //
 // One CTA = 128 query rows of one q head; grid (n_q, query blocks), the
-// heaviest (last) query blocks first.  192 threads:
+// heaviest (last) query blocks first.  320 threads:
 //   warp 0     TMA producer: the q parts once, then per 64-key block the k
-//              and v parts into a 2-stage ring (128-byte swizzle);
+//              parts into a 3-stage ring (free again once S_j is computed)
+//              and the v parts into a 2-stage ring (free once O_j is), with
+//              the 128-byte swizzle;
 //   warp 1     allocates 256 TMEM columns and issues the MMAs (one lane):
 //              S_j into one of two S buffers, then, once the softmax has
 //              written P_j, O_j = P_j V_j into one of two O buffers;
-//   warps 2-5  softmax, one query row per thread (TMEM lane = row): load
-//              S_j (tcgen05.ld), mask (key > query position or past the
-//              keys), running max and sum, p = 2^(s - m) into the P buffer
-//              as BF16 hi/lo in the swizzled K-major layout the MMA reads,
-//              then fold O_{j-1} from TMEM into registers (o = o * alpha +
-//              O_blk), one block behind so that PV_j overlaps softmax_j+1.
+//   warps 2-9  softmax, two threads per query row (TMEM lane = row; one
+//              takes keys and output dims 0-31, the other 32-63): load S_j
+//              (tcgen05.ld), mask the blocks that reach the diagonal or past
+//              the keys, running max (shared by the pair through shared
+//              memory) and sum, p = 2^(s - m) into the P buffer as BF16
+//              hi/lo in the swizzled K-major layout the MMA reads, then fold
+//              O_{j-1} from TMEM into registers (o = o * alpha + O_blk), one
+//              block behind so that PV_j overlaps softmax_{j+1}.
 // Every mbarrier wait is bounded; a wait that gives up sets the error word
 // and the CTA stops (the host reports TMG_ERR_TIMEOUT).  Single-GPU code:
 // every CTA loads its own tiles; no peer memory.
@@ -47,18 +51,21 @@ namespace {
 constexpr int kPD = 64;                       // head dim
 constexpr int kQB = 128;                      // query rows per CTA (MMA M)
 constexpr int kKB = 64;                       // keys per block (S: N; PV: K)
-constexpr int kPfStages = 2;
+constexpr int kKStages = 3;  // k ring: a stage is free once S_j has read it
+constexpr int kVStages = 2;  // v ring: once O_j = P_j V_j has
 constexpr int kQPart = kQB * kPD * 2;         // 16 KB: one BF16 part of the q tile
 constexpr int kKPart = kKB * kPD * 2;         // 8 KB: one part of a k block
 constexpr int kVPart = kPD * kKB * 2;         // 8 KB: one part of a v^T block
-constexpr int kStage = 3 * kKPart + 2 * kVPart;  // 40 KB
+constexpr int kKStage = 3 * kKPart;          // 24 KB: k hi, mid, lo
+constexpr int kVStage = 2 * kVPart;          // 16 KB: v^T hi, lo
 constexpr int kPPart = kQB * kKB * 2;         // 16 KB: one part of a P block
 constexpr int kOffQ = 0;                      // q hi, mid, lo
-constexpr int kOffStage = 3 * kQPart;         // 48 KB
-constexpr int kOffP = kOffStage + kPfStages * kStage;  // 128 KB; P[2] x {hi, lo}
-constexpr int kOffBar = kOffP + 2 * 2 * kPPart;        // 192 KB
+constexpr int kOffK = 3 * kQPart;                      // 48 KB
+constexpr int kOffV = kOffK + kKStages * kKStage;      // 120 KB
+constexpr int kOffP = kOffV + kVStages * kVStage;      // 152 KB; P[2] x {hi, lo}
+constexpr int kOffBar = kOffP + 2 * 2 * kPPart;        // 216 KB
 constexpr int kSmemPf = kOffBar + 256 + 1024;          // + barriers + alignment slack
-constexpr int kPfThreads = 192;
+constexpr int kPfThreads = 320;  // producer, MMA, 8 softmax warps
 constexpr uint32_t kPfTmemCols = 256;  // S[2] at 0, 64; O[2] at 128, 192
 // kind::f16: BF16 x BF16 -> F32, both K-major, M = 128, N = 64.
 constexpr uint32_t kIdescPf =
@@ -100,11 +107,11 @@ __device__ __forceinline__ void commit(uint64_t* bar) {
                : "memory");
 }
 
-// 64 consecutive TMEM columns of this warp's 32 lanes (one row per thread).
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
-  uint32_t r[64];
+// 32 consecutive TMEM columns of this warp's 32 lanes (one row per thread).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
 #pragma unroll
-  for (int c = 0; c < 64; c += 16)
+  for (int c = 0; c < 32; c += 16)
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
         "%14,%15}, [%16];"
@@ -115,17 +122,37 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
         : "r"(taddr + uint32_t(c)));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Barrier `id` (1..15) among `n` threads (whole warps).
+__device__ __forceinline__ void named_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+// The same barrier, returning the AND of every participant's `pred`.
+__device__ __forceinline__ bool bar_and(int id, int n, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(uint32_t(pred)), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
+// (bf16(a), bf16(b)) packed, a in the low half.
+__device__ __forceinline__ uint32_t bf16x2_bits(float a, float b) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&v);
 }
 
 __device__ __forceinline__ float ex2f(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-__device__ __forceinline__ uint32_t bf16_bits(float x) {
-  return __bfloat16_as_ushort(__float2bfloat16_rn(x));
 }
 
 struct PfArgs {
@@ -152,15 +179,19 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kOffBar);  // [2] k/v stage loaded
-  uint64_t* empty = full + kPfStages;                            // [2] k/v stage free
-  uint64_t* qfull = empty + kPfStages;                           // q parts loaded
+  uint64_t* kfull = reinterpret_cast<uint64_t*>(sm + kOffBar);  // [3] k stage loaded
+  uint64_t* kempty = kfull + kKStages;                             // [3] k stage free
+  uint64_t* vfull = kempty + kKStages;                             // [2] v stage loaded
+  uint64_t* vempty = vfull + kVStages;                             // [2] v stage free
+  uint64_t* qfull = vempty + kVStages;                             // q parts loaded
   uint64_t* s_full = qfull + 1;                                  // [2] S_j in TMEM
   uint64_t* p_full = s_full + 2;                                 // [2] P_j in smem (S_j read)
   uint64_t* o_full = p_full + 2;                                 // [2] O_j in TMEM
   uint64_t* o_free = o_full + 2;                                 // [2] O_j read
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 2);
   __shared__ volatile int failed;
+  __shared__ float red_mx[2][2][kQB];  // [block parity][half][row]: a half's max of the block
+  __shared__ float red_l[2][kQB];      // [half][row]: a half's share of the row's sum
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.x, kvh = h / a.G;
@@ -170,16 +201,20 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const int nb = int((last_key + kKB - 1) / kKB);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kPfStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < kKStages; ++s) {
+      mbar_init(&kfull[s], 1);
+      mbar_init(&kempty[s], 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
+      mbar_init(&vfull[s], 1);
+      mbar_init(&vempty[s], 1);
     }
     mbar_init(qfull, 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&p_full[b], 4);
+      mbar_init(&p_full[b], 8);
       mbar_init(&o_full[b], 1);
-      mbar_init(&o_free[b], 4);
+      mbar_init(&o_free[b], 8);
     }
     failed = 0;
     mbar_fence_init();
@@ -204,20 +239,27 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       tma2d(sm + kOffQ + kQPart, &mq_mid, qfull, 0, qy);
       tma2d(sm + kOffQ + 2 * kQPart, &mq_lo, qfull, 0, qy);
       for (int j = 0; j < nb; ++j) {
-        const int s = j % kPfStages;
-        if (failed || !mbar_wait(&empty[s], ((j / kPfStages) & 1) ^ 1)) {
+        const int sk = j % kKStages, sv = j % kVStages;
+        if (failed || !mbar_wait(&kempty[sk], ((j / kKStages) & 1) ^ 1)) {
           failed = 1;
           atomicExch(a.err, 2);
           break;
         }
-        uint8_t* st = sm + kOffStage + s * kStage;
-        mbar_expect_tx(&full[s], kStage);
+        uint8_t* kst = sm + kOffK + sk * kKStage;
+        mbar_expect_tx(&kfull[sk], kKStage);
         const int ky = kvh * a.Lkp + j * kKB;
-        tma2d(st, &mk_hi, &full[s], 0, ky);
-        tma2d(st + kKPart, &mk_mid, &full[s], 0, ky);
-        tma2d(st + 2 * kKPart, &mk_lo, &full[s], 0, ky);
-        tma2d(st + 3 * kKPart, &mv_hi, &full[s], j * kKB, kvh * kPD);
-        tma2d(st + 3 * kKPart + kVPart, &mv_lo, &full[s], j * kKB, kvh * kPD);
+        tma2d(kst, &mk_hi, &kfull[sk], 0, ky);
+        tma2d(kst + kKPart, &mk_mid, &kfull[sk], 0, ky);
+        tma2d(kst + 2 * kKPart, &mk_lo, &kfull[sk], 0, ky);
+        if (failed || !mbar_wait(&vempty[sv], ((j / kVStages) & 1) ^ 1)) {
+          failed = 1;
+          atomicExch(a.err, 2);
+          break;
+        }
+        uint8_t* vst = sm + kOffV + sv * kVStage;
+        mbar_expect_tx(&vfull[sv], kVStage);
+        tma2d(vst, &mv_hi, &vfull[sv], j * kKB, kvh * kPD);
+        tma2d(vst + kVPart, &mv_lo, &vfull[sv], j * kKB, kvh * kPD);
       }
     }
   } else if (warp == 1) {
@@ -230,13 +272,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         if (j < nb) {
           // S_j = Q K_j^T into S buffer j & 1 (its previous user, S_{j-2},
           // was read before P_{j-2} arrived, which PV_{j-2} waited for)
-          const int s = j % kPfStages;
-          if (failed || !mbar_wait(&full[s], (j / kPfStages) & 1)) {
+          const int s = j % kKStages;
+          if (failed || !mbar_wait(&kfull[s], (j / kKStages) & 1)) {
             ok = false;
             break;
           }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t kb = smem_u32(sm + kOffStage + s * kStage);
+          const uint32_t kb = smem_u32(sm + kOffK + s * kKStage);
           const uint32_t kh = kb, km = kb + kKPart, kl = kb + 2 * kKPart;
           const uint32_t ts = tmem + uint32_t((j & 1) * 64);
 #pragma unroll
@@ -250,18 +292,20 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             mma(ts, sdesc(qm + o), sdesc(km + o), 1);
           }
           commit(&s_full[j & 1]);
+          commit(&kempty[s]);  // k stage s is free once these MMAs have read it
         }
         if (j >= 1) {
           // O_i = P_i V_i for i = j - 1 into O buffer i & 1
           const int i = j - 1, b = i & 1;
+          const int s = i % kVStages;
           if (failed || !mbar_wait(&p_full[b], (i >> 1) & 1) ||
-              (i >= 2 && !mbar_wait(&o_free[b], ((i - 2) >> 1) & 1))) {
+              (i >= 2 && !mbar_wait(&o_free[b], ((i - 2) >> 1) & 1)) ||
+              !mbar_wait(&vfull[s], (i / kVStages) & 1)) {
             ok = false;
             break;
           }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const int s = i % kPfStages;
-          const uint32_t vb = smem_u32(sm + kOffStage + s * kStage + 3 * kKPart);
+          const uint32_t vb = smem_u32(sm + kOffV + s * kVStage);
           const uint32_t vh = vb, vl = vb + kVPart;
           const uint32_t pb = smem_u32(sm + kOffP + b * 2 * kPPart);
           const uint32_t ph = pb, pl = pb + kPPart;
@@ -274,7 +318,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             mma(to, sdesc(pl + o), sdesc(vh + o), 1);
           }
           commit(&o_full[b]);
-          commit(&empty[s]);  // k/v stage s is free once these MMAs have read it
+          commit(&vempty[s]);  // v stage s is free once these MMAs have read it
         }
       }
       if (!ok) {
@@ -283,56 +327,75 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
     }
   } else {
-    // ---- softmax / output: one query row per thread ----
+    // ---- softmax / output: two threads per query row ----
+    // Warps 2-5 and 6-9: warp w reads TMEM lanes 32 (w % 4) .. (its rows);
+    // the first four take keys 0-31 of each block and dims 0-31 of O, the
+    // other four keys 32-63 and dims 32-63.  The two threads of a row
+    // agree on the row's running max through shared memory (named barrier
+    // of the two warps); each keeps its share of the running sum.
     const int qd = warp & 3;                 // TMEM lane quadrant of this warp
+    const int hf = (warp - 2) >> 2;          // which half of the keys and dims
     const int r = qd * 32 + lane;            // row in the query block
     const int64_t tq = a.pos0 + q0 + r;      // its position
     const uint32_t lanes = uint32_t(qd * 32) << 16;
-    float o[kPD];
+    const uint32_t cofs = uint32_t(hf * 32);
+    const int64_t row0 = a.pos0 + q0;        // the first row's position
+    float o[32];
 #pragma unroll
-    for (int c = 0; c < kPD; ++c) o[c] = 0.f;
+    for (int c = 0; c < 32; ++c) o[c] = 0.f;
     float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
     bool ok = true;
+    // A failed wait does not leave the loop on its own: the pair's barrier
+    // below ANDs both threads' status, so both leave at the same block and
+    // every barrier of the pair is met.
     for (int j = 0; j < nb; ++j) {
       const int b = j & 1;
-      if (!mbar_wait(&s_full[b], (j >> 1) & 1)) {
+      const bool got = mbar_wait(&s_full[b], (j >> 1) & 1);
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      float sv[32];
+      tmem_ld32(tmem + lanes + uint32_t(b * 64) + cofs, sv);
+      const int64_t k0 = int64_t(j) * kKB + hf * 32;
+      // only blocks that reach past the first row's position or past the
+      // keys need the mask (the same for every row of the CTA)
+      if (int64_t(j) * kKB + kKB - 1 > row0 || int64_t(j) * kKB + kKB > a.Lk) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+          if (k0 + c > tq || k0 + c >= a.Lk) sv[c] = -INFINITY;
+      }
+      float lmx = sv[0];
+#pragma unroll
+      for (int c = 1; c < 32; ++c) lmx = fmaxf(lmx, sv[c]);
+      red_mx[b][hf][r] = lmx;
+      if (!bar_and(2 + qd, 64, ok && got)) {
         ok = false;
         break;
       }
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      float s[kKB];
-      tmem_ld64(tmem + lanes + uint32_t(b * 64), s);
-      const int64_t k0 = int64_t(j) * kKB;
-      float mx = m;
-#pragma unroll
-      for (int c = 0; c < kKB; ++c) {
-        const int64_t key = k0 + c;
-        if (key > tq || key >= a.Lk) s[c] = -INFINITY;
-        mx = fmaxf(mx, s[c]);
-      }
+      const float mx = fmaxf(m, fmaxf(lmx, red_mx[b][hf ^ 1][r]));
       const float alpha = m == -INFINITY ? 0.f : ex2f(m - mx);
       float sum = 0.f;
-      // P_j (row r) into P buffer b: BF16 hi and lo, 16-byte chunk e of the
-      // 128-byte row at chunk e ^ (r & 7) (the 128-byte swizzle).  The buffer
-      // was last read by PV_{j-2}, which completed before O_{j-2} was folded.
+      // P_j (row r, this half's 32 keys) into P buffer b: BF16 hi and lo,
+      // 16-byte chunk e of the 128-byte row at chunk e ^ (r & 7) (the
+      // 128-byte swizzle).  The buffer was last read by PV_{j-2}, which
+      // completed before O_{j-2} was folded.
       uint8_t* prow_h = sm + kOffP + b * 2 * kPPart + r * 128;
       uint8_t* prow_l = prow_h + kPPart;
 #pragma unroll
-      for (int e = 0; e < kKB / 8; ++e) {
+      for (int e = 0; e < 4; ++e) {
         uint32_t hw[4], lw[4];
 #pragma unroll
         for (int t = 0; t < 8; t += 2) {
-          const float p0 = s[8 * e + t] == -INFINITY ? 0.f : ex2f(s[8 * e + t] - mx);
-          const float p1 = s[8 * e + t + 1] == -INFINITY ? 0.f : ex2f(s[8 * e + t + 1] - mx);
+          const float x0 = sv[8 * e + t], x1 = sv[8 * e + t + 1];
+          const float p0 = x0 == -INFINITY ? 0.f : ex2f(x0 - mx);
+          const float p1 = x1 == -INFINITY ? 0.f : ex2f(x1 - mx);
           sum += p0;
           sum += p1;
-          const uint32_t h0 = bf16_bits(p0), h1 = bf16_bits(p1);
-          const float r0 = p0 - __bfloat162float(__ushort_as_bfloat16(uint16_t(h0)));
-          const float r1 = p1 - __bfloat162float(__ushort_as_bfloat16(uint16_t(h1)));
-          hw[t / 2] = h0 | (h1 << 16);
-          lw[t / 2] = bf16_bits(r0) | (bf16_bits(r1) << 16);
+          const uint32_t hb = bf16x2_bits(p0, p1);
+          const float r0 = p0 - __uint_as_float(hb << 16);
+          const float r1 = p1 - __uint_as_float(hb & 0xffff0000u);
+          hw[t / 2] = hb;
+          lw[t / 2] = bf16x2_bits(r0, r1);
         }
-        const int off = ((e ^ (r & 7)) << 4);
+        const int off = (((hf * 4 + e) ^ (r & 7)) << 4);
         *reinterpret_cast<uint4*>(prow_h + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
         *reinterpret_cast<uint4*>(prow_l + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
       }
@@ -345,15 +408,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (lane == 0) mbar_arrive(&p_full[b]);
       if (j >= 1) {
         const int i = j - 1, bi = i & 1;
-        if (!mbar_wait(&o_full[bi], (i >> 1) & 1)) {
-          ok = false;
-          break;
-        }
+        if (!mbar_wait(&o_full[bi], (i >> 1) & 1)) ok = false;  // leaves at the next barrier
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        float ob[kPD];
-        tmem_ld64(tmem + lanes + 128u + uint32_t(bi * 64), ob);
+        float ob[32];
+        tmem_ld32(tmem + lanes + 128u + uint32_t(bi * 64) + cofs, ob);
 #pragma unroll
-        for (int c = 0; c < kPD; ++c) o[c] = fmaf(o[c], alpha_prev, ob[c]);
+        for (int c = 0; c < 32; ++c) o[c] = fmaf(o[c], alpha_prev, ob[c]);
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncwarp();
         if (lane == 0) mbar_arrive(&o_free[bi]);
@@ -366,20 +426,25 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         ok = false;
       } else {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        float ob[kPD];
-        tmem_ld64(tmem + lanes + 128u + uint32_t(bi * 64), ob);
+        float ob[32];
+        tmem_ld32(tmem + lanes + 128u + uint32_t(bi * 64) + cofs, ob);
 #pragma unroll
-        for (int c = 0; c < kPD; ++c) o[c] = fmaf(o[c], alpha_prev, ob[c]);
+        for (int c = 0; c < 32; ++c) o[c] = fmaf(o[c], alpha_prev, ob[c]);
       }
     }
+    // the row's sum: this thread's share and its partner's (every thread
+    // reaches this barrier, also after a failed wait)
+    red_l[hf][r] = l;
+    named_sync(2 + qd, 64);
+    const float lt = l + red_l[hf ^ 1][r];
     if (!ok) {
       failed = 1;
       atomicExch(a.err, 2);
     } else if (q0 + r < a.T) {
-      float* dst = a.out + int64_t(q0 + r) * a.out_ld + int64_t(h) * kPD;
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+      float* dst = a.out + int64_t(q0 + r) * a.out_ld + int64_t(h) * kPD + hf * 32;
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
 #pragma unroll
-      for (int c = 0; c < kPD; c += 4)
+      for (int c = 0; c < 32; c += 4)
         *reinterpret_cast<float4*>(dst + c) =
             make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
     }

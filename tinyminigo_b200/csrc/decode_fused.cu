@@ -307,6 +307,16 @@ struct Shared {
   volatile int in_attn;    // consumers: in an attention phase
 };
 
+// This CTA's index in the grid of all ranks, and that grid's size: the
+// special registers on one GPU, the values the kernel computed at entry in a
+// group (kept in shared memory).
+__device__ __forceinline__ int cta_gid(const Shared& S) {
+  return kGroup ? S.gid : int(blockIdx.x);
+}
+__device__ __forceinline__ int cta_gn(const Shared& S) {
+  return kGroup ? S.gn : int(gridDim.x);
+}
+
 // ---------------------------------------------------------------------------
 // Grid barrier among the consumer warps of all CTAs: one monotonic arrival
 // counter (zeroed before the launch); the k-th barrier waits until it reaches
@@ -320,7 +330,7 @@ __device__ bool grid_sync(const FusedArgs& a, unsigned int& target, Shared& S,
   if (threadIdx.x == 0) {
     if (tr) tr[0] = global_ns();
     int ok = S.abort ? 0 : 1;
-    target += S.gn;
+    target += cta_gn(S);
     constexpr bool sys = kGroup;
     if (ok) {
       if (sys) {
@@ -394,8 +404,8 @@ __device__ __forceinline__ void cur_settle(const FusedArgs& a, Cursor& c) {
 __device__ __forceinline__ void cur_begin(const FusedArgs& a, const FusedLayer* layers,
                                           const Shared& S, Cursor& c) {
   c.layers = layers;
-  c.gid = S.gid;
-  c.gn = S.gn;
+  c.gid = cta_gid(S);
+  c.gn = cta_gn(S);
   c.step = 0;
   c.l = 0;
   c.ph = PH_QKV;
@@ -819,7 +829,8 @@ __device__ __forceinline__ int gemv_block(int ngroups, int K, int ks, int rpg, i
   const uint16_t* wbase =
       reinterpret_cast<const uint16_t*>(ring + size_t(slot) * K * 2) + kbase + lane * 8;
   int kl = 0;
-  for (int grp = first_group(off, S.gid, S.gn); grp < ngroups; grp += S.gn, rp.next(nst), ++kl) {
+  for (int grp = first_group(off, cta_gid(S), cta_gn(S)); grp < ngroups;
+       grp += cta_gn(S), rp.next(nst), ++kl) {
     const int s = rp.s;
     float acc = 0.f;
     const bool ok = !S.abort && mbar_wait(&S.full[s], rp.par);
@@ -911,7 +922,8 @@ __device__ __forceinline__ int gemv_kseg(int ngroups, int K, int chunks, const f
   const int myrow = M > 0 ? (lane >> (5 - M)) & (R - 1) : 0;
   const bool writer = (lane & ((32 >> M) - 1)) == 0;
   int kl = 0;
-  for (int grp = first_group(off, S.gid, S.gn); grp < ngroups; grp += S.gn, rp.next(nst), ++kl) {
+  for (int grp = first_group(off, cta_gid(S), cta_gn(S)); grp < ngroups;
+       grp += cta_gn(S), rp.next(nst), ++kl) {
     const int s = rp.s;
     float acc[R][NA];
 #pragma unroll
@@ -996,11 +1008,11 @@ __device__ __forceinline__ void epi_qkv(const FusedArgs& a, const FusedLayer& L,
                                         const PhaseGeo& g, int off, int nloc, int pos, bool append,
                                         const float* rope_s, float scale, uint32_t tag, Shared& S) {
   const int D = g.D, half = D / 2, hp = g.rpc / 2, kvd = a.nkv * D;
-  const int f = first_group(off, S.gid, S.gn);
+  const int f = first_group(off, cta_gid(S), cta_gn(S));
   const int vbase = (a.nq + a.nkv) * D;
   for (int i = threadIdx.x; i < (nloc << g.lrpc); i += kCThreads) {
     const int kl = i >> g.lrpc, slot = i & (g.rpc - 1);
-    const int grp = f + kl * S.gn;
+    const int grp = f + kl * cta_gn(S);
     if (grp < g.pair_groups) {
       if (slot >= hp) continue;  // done with its partner
       const int ra = slot_row(g, grp, slot);
@@ -1030,10 +1042,10 @@ __device__ __forceinline__ void epi_qkv(const FusedArgs& a, const FusedLayer& L,
 __device__ __forceinline__ void epi_residual(unsigned long long* x_ll, int rep, const float* x_s,
                                              const PhaseGeo& g, int off, int nloc, uint32_t tag,
                                              const Shared& S) {
-  const int f = first_group(off, S.gid, S.gn);
+  const int f = first_group(off, cta_gid(S), cta_gn(S));
   for (int i = threadIdx.x; i < (nloc << g.lrpc); i += kCThreads) {
     const int kl = i >> g.lrpc, slot = i & (g.rpc - 1);
-    const int r = ((f + kl * S.gn) << g.lrpg) + slot;
+    const int r = ((f + kl * cta_gn(S)) << g.lrpg) + slot;
     if (r < g.N)
       ll_store_rep(S, x_ll, g.N, rep, r, x_s[perm_idx(r)] + res_k(S, kl, slot, g.rpc), tag);
   }
@@ -1044,10 +1056,10 @@ __device__ __forceinline__ void epi_residual(unsigned long long* x_ll, int rep, 
 __device__ __forceinline__ void epi_swiglu(unsigned long long* act_ll, int rep, const PhaseGeo& g,
                                            int off, int nloc, float scale, uint32_t tag,
                                            const Shared& S) {
-  const int f = first_group(off, S.gid, S.gn);
+  const int f = first_group(off, cta_gid(S), cta_gn(S));
   for (int i = threadIdx.x; i < (nloc << g.lrpg); i += kCThreads) {
     const int kl = i >> g.lrpg, q = i & (g.rpg - 1);
-    const int r = ((f + kl * S.gn) << g.lrpg) + q;
+    const int r = ((f + kl * cta_gn(S)) << g.lrpg) + q;
     if (r < g.N) {
       const float gv = res_k(S, kl, q, g.rpc) * scale, uv = res_k(S, kl, q + g.rpg, g.rpc) * scale;
       ll_store_rep(S, act_ll, g.N, rep, r, gv / (1.0f + expf(-gv)) * uv, tag);
@@ -1058,10 +1070,10 @@ __device__ __forceinline__ void epi_swiglu(unsigned long long* act_ll, int rep, 
 // LM head epilogue (ks > 1): logits and this thread's argmax candidate.
 __device__ __forceinline__ void epi_head(float* logits, const PhaseGeo& g, int off, int nloc,
                                          const Shared& S, unsigned long long& best) {
-  const int f = first_group(off, S.gid, S.gn);
+  const int f = first_group(off, cta_gid(S), cta_gn(S));
   for (int i = threadIdx.x; i < (nloc << g.lrpc); i += kCThreads) {
     const int kl = i >> g.lrpc, slot = i & (g.rpc - 1);
-    const int r = ((f + kl * S.gn) << g.lrpg) + slot;
+    const int r = ((f + kl * cta_gn(S)) << g.lrpg) + slot;
     if (r < g.N) {
       const float v = res_val(S, kl, slot, g.ks);
       logits[r] = v;
@@ -1385,13 +1397,13 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
         aa.nkv = a.nkv;
         aa.nsplit = a.nsplit;
         aa.scale = a.scale;
-        for (int item = S.gid; item < a.nkv * n_used && ok; item += S.gn)
+        for (int item = cta_gid(S); item < a.nkv * n_used && ok; item += cta_gn(S))
           ok = attn_item<D>(aa, item / n_used, item % n_used, chunk, n_ctx, pos, append, n_used,
-                            tag - 1u, tag, asm_, S, gc, item == S.gid ? tp : nullptr,
-                            item == S.gid);
+                            tag - 1u, tag, asm_, S, gc, item == cta_gid(S) ? tp : nullptr,
+                            item == cta_gid(S));
         if (tp && threadIdx.x == 0) tp[5] = global_ns();
         if (n_used > 1)
-          for (int item = S.gid; item < a.nkv * n_used && ok; item += S.gn)
+          for (int item = cta_gid(S); item < a.nkv * n_used && ok; item += cta_gn(S))
             if (item % n_used == 0) ok = merge_head<D>(aa, item / n_used, n_used, tag, asm_, S, gc);
         if (tp && threadIdx.x == 0) tp[6] = global_ns();
         if (!ok) raise_abort(a);
@@ -1484,8 +1496,8 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
       // the cache rows of this CTA's first attention item of the layer start
       // loading now (the region is free until the attention phase; no
       // cp.async wait comes before attn_item's)
-      if (ph == PH_QKV && S.gid < a.nkv * n_used) {
-        const int item = S.gid;
+      if (ph == PH_QKV && cta_gid(S) < a.nkv * n_used) {
+        const int item = cta_gid(S);
         attn_prefetch<D>(layers_s[l].kc, layers_s[l].vc, a.nkv, a.nq / a.nkv, item / n_used,
                          item % n_used, chunk, n_ctx, append ? pos : n_ctx, asm_);
       }
@@ -1522,7 +1534,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
         if (tp && threadIdx.x == 0) tp[9] = clock64() - ce;
       }
       csync();  // x_s, asm_ and S.res are free for the next phase
-      off = (off + g.ngroups) % S.gn;
+      off = (off + g.ngroups) % cta_gn(S);
       if (ph == PH_HEAD) {
         best = warp_max_u64(best);
         if (lane == 0) S.best[warp] = best;
@@ -1534,7 +1546,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
             a.am_part[blockIdx.x] = bb;
           } else {  // every rank's table, at this CTA's index in the joint grid
             for (int r = 0; r < a.world; ++r)
-              asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(a.am_peer[r] + S.gid),
+              asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(a.am_peer[r] + cta_gid(S)),
                            "l"(bb)
                            : "memory");
           }
@@ -1548,7 +1560,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
     // every CTA reduces the argmax partials: the same token everywhere
     {
       unsigned long long b = 0;
-      for (int i = threadIdx.x; i < S.gn; i += kCThreads) {
+      for (int i = threadIdx.x; i < cta_gn(S); i += kCThreads) {
         const unsigned long long v = __ldcg(a.am_part + i);
         b = v > b ? v : b;
       }
