@@ -1,17 +1,18 @@
-"""Greedy decode of one sequence spread over 2 GPUs by the fused decode
+"""Greedy decode of one sequence spread over 2, 4 or 8 GPUs by the fused decode
 kernel (tmg_fused_group_init): the row groups and attention items of every
-phase are dealt over both GPUs' SMs, and every exchanged value, KV-cache
-row and argmax candidate is written into both GPUs' memory over NVLink.
+phase are dealt over all the GPUs' SMs, and every exchanged value, KV-cache
+row and argmax candidate is written into every GPU's memory over NVLink.
 
 Each rank is a process with its own context holding the full weights; rank
-0's NCCL unique id reaches the other rank through the spawning test.  Each
+0's NCCL unique id reaches the other ranks through the spawning test.  Each
 output row is computed whole on one GPU, so the tokens must be identical,
 bit for bit, to the same decode on one GPU (which each rank runs first on
-a cache of its own), and the same on both ranks; the single-GPU tokens are
+a cache of its own), and the same on every rank; the single-GPU tokens are
 checked against the CPU oracle (generate's argmax loop, src/model.rs:
 614-663) with conftest.GreedyCheck.  Shapes: the 8B-class instance (C4
-shape, 2 layers) and the 1B-class one (c2 shape, 2 layers: its O phase has
-256 row groups, so each GPU runs 128 CTAs).
+shape, 2 layers, on 2, 4 and 8 GPUs as the box has them) and the 1B-class
+one (c2 shape, 2 layers, 2 GPUs: its O phase has 256 row groups, so each
+GPU runs 128 CTAs).
 """
 import ctypes
 
@@ -67,16 +68,17 @@ def _rank(which, rank, world, uid, q):
         q.put((rank, None, repr(e), None))
 
 
-@pytest.mark.parametrize("which", ["c4", "c2"])
-def test_fused_group_of_two_matches_one_gpu(orc, greedy, which):
+@pytest.mark.parametrize("which,world", [("c4", 2), ("c2", 2), ("c4", 4), ("c4", 8)])
+def test_fused_group_matches_one_gpu(orc, greedy, which, world):
     from tinyminigo_b200 import synth
     from tinyminigo_b200._lib import check, lib
 
+    if torch.cuda.device_count() < world:  # pragma: no cover
+        pytest.skip(f"needs {world} GPUs")
     uid = (ctypes.c_uint8 * 128)()
     check(lib().tmg_tp_unique_id(uid))
     ctx = torch.multiprocessing.get_context("spawn")
     q = ctx.Queue()
-    world = 2
     procs = [ctx.Process(target=_rank, args=(which, r, world, bytes(uid), q)) for r in range(world)]
     for p in procs:
         p.start()
@@ -94,10 +96,11 @@ def test_fused_group_of_two_matches_one_gpu(orc, greedy, which):
         assert res[r][0] is not None, f"rank {r} failed: {res[r][1]}"
     for r in range(world):
         tok0, solo, grp = res[r]
-        assert grp == solo, f"rank {r}: the 2-GPU decode differs from one GPU's"
-    assert res[0] == res[1]
+        assert grp == solo, f"rank {r}: the {world}-GPU decode differs from one GPU's"
+        assert res[r] == res[0]
     cfg, prompt = _setup(which)
     w = synth.make_weights(cfg, 62, device="cuda")
     ids, margins, second, _ = greedy.oracle(orc.OracleModel(cfg, w), prompt, STEPS + 1)
     tok0, solo, _ = res[0]
-    greedy.agree(f"{which} shape, 2 layers, fused on 2 GPUs", [tok0] + solo, ids, margins, second)
+    greedy.agree(f"{which} shape, 2 layers, fused on {world} GPUs", [tok0] + solo, ids, margins,
+                 second)
