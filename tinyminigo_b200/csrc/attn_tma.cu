@@ -101,6 +101,7 @@ __global__ void __launch_bounds__(kTmaThreads, D == 64 ? 3 : 2)
   __shared__ __align__(16) float ofin[GM * D];
   __shared__ float wm[kTmaConsumers * GM], wl[kTmaConsumers * GM];
   __shared__ float m_s[16], l_s[16];
+  __shared__ __align__(16) float p_s[kTmaConsumers][2][16];  // [warp][half-warp][row * 4 + head]
   __shared__ volatile int abort_s;
   __shared__ volatile int issued_s;  // tiles the producer has issued
   __shared__ bool last_s;
@@ -215,8 +216,8 @@ __global__ void __launch_bounds__(kTmaThreads, D == 64 ? 3 : 2)
     // kept in base-2 units (scale * log2 e folded into the scale), so one
     // ex2 per lane gives its probability; the lane keeps its head's running
     // max and its own share of the head's running sum, and the 16
-    // probabilities reach every lane by shuffles for the weighted sum of
-    // the values it holds.  The outputs are rescaled only in tiles where
+    // probabilities reach every lane through shared memory for the weighted
+    // sum of the values it holds.  The outputs are rescaled only in tiles where
     // some head's max grew (alpha is exactly 1 otherwise).
     const int hw = lane >> 4, l16 = lane & 15, hb = lane & 16;
     const int my_g = l16 & 3, my_r = l16 >> 2;
@@ -249,22 +250,36 @@ __global__ void __launch_bounds__(kTmaThreads, D == 64 ? 3 : 2)
       const int r0 = warp * 2 * kTmaRowsPerHalf + hw * kTmaRowsPerHalf;  // row in the tile
       const int tb = c0 + i * kTmaRows + r0;                               // its position
       float4 kr[kTmaRowsPerHalf][DL], vr[kTmaRowsPerHalf][DL];
+      // the tile's rows as loaded, unless it reaches past the range or holds
+      // the decoded position (the same for the whole CTA)
+      const int tile0 = c0 + i * kTmaRows;
+      if (tile0 + kTmaRows <= c1 && !(own_pos && pos >= tile0 && pos < tile0 + kTmaRows)) {
 #pragma unroll
-      for (int r = 0; r < kTmaRowsPerHalf; ++r) {
-        // rows past the range hold whatever the cache held (or the map's
-        // zero fill): they enter as zeros with a masked score
-        const bool mine = own_pos && tb + r == pos;
-        const bool live = tb + r < c1;
+        for (int r = 0; r < kTmaRowsPerHalf; ++r)
 #pragma unroll
-        for (int c = 0; c < DL; ++c) {
-          const int col = 64 * c + 4 * l16;
-          kr[r][c] = mine ? *reinterpret_cast<const float4*>(kp_s + col)
-                          : *reinterpret_cast<const float4*>(kt + (r0 + r) * d + col);
-          vr[r][c] = mine ? *reinterpret_cast<const float4*>(vp_s + col)
-                          : *reinterpret_cast<const float4*>(vt + (r0 + r) * d + col);
-          if (!live) {
-            kr[r][c] = make_float4(0.f, 0.f, 0.f, 0.f);
-            vr[r][c] = kr[r][c];
+          for (int c = 0; c < DL; ++c) {
+            const int col = 64 * c + 4 * l16;
+            kr[r][c] = *reinterpret_cast<const float4*>(kt + (r0 + r) * d + col);
+            vr[r][c] = *reinterpret_cast<const float4*>(vt + (r0 + r) * d + col);
+          }
+      } else {
+#pragma unroll
+        for (int r = 0; r < kTmaRowsPerHalf; ++r) {
+          // rows past the range hold whatever the cache held (or the map's
+          // zero fill): they enter as zeros with a masked score
+          const bool mine = own_pos && tb + r == pos;
+          const bool live = tb + r < c1;
+#pragma unroll
+          for (int c = 0; c < DL; ++c) {
+            const int col = 64 * c + 4 * l16;
+            kr[r][c] = mine ? *reinterpret_cast<const float4*>(kp_s + col)
+                            : *reinterpret_cast<const float4*>(kt + (r0 + r) * d + col);
+            vr[r][c] = mine ? *reinterpret_cast<const float4*>(vp_s + col)
+                            : *reinterpret_cast<const float4*>(vt + (r0 + r) * d + col);
+            if (!live) {
+              kr[r][c] = make_float4(0.f, 0.f, 0.f, 0.f);
+              vr[r][c] = kr[r][c];
+            }
           }
         }
       }
@@ -311,17 +326,24 @@ __global__ void __launch_bounds__(kTmaThreads, D == 64 ? 3 : 2)
       }
       m_own = mn;
       l_own += p;
+      // the half-warp's 16 probabilities to every lane of it: one store and
+      // four broadcast loads (row r's heads at p_s[r * 4 ..])
+      float* ps_h = p_s[warp][hw];
+      __syncwarp();  // the previous tile's reads are done
+      ps_h[l16] = p;
+      __syncwarp();
 #pragma unroll
       for (int r = 0; r < kTmaRowsPerHalf; ++r) {
+        const float4 pr = *reinterpret_cast<const float4*>(ps_h + r * 4);
+        const float pv[4] = {pr.x, pr.y, pr.z, pr.w};
 #pragma unroll
         for (int g = 0; g < GM; ++g) {
-          const float pg = __shfl_sync(0xffffffffu, p, hb + r * 4 + g);
 #pragma unroll
           for (int c = 0; c < DL; ++c) {
-            o4[g][c].x = fmaf(pg, vr[r][c].x, o4[g][c].x);
-            o4[g][c].y = fmaf(pg, vr[r][c].y, o4[g][c].y);
-            o4[g][c].z = fmaf(pg, vr[r][c].z, o4[g][c].z);
-            o4[g][c].w = fmaf(pg, vr[r][c].w, o4[g][c].w);
+            o4[g][c].x = fmaf(pv[g], vr[r][c].x, o4[g][c].x);
+            o4[g][c].y = fmaf(pv[g], vr[r][c].y, o4[g][c].y);
+            o4[g][c].z = fmaf(pv[g], vr[r][c].z, o4[g][c].z);
+            o4[g][c].w = fmaf(pv[g], vr[r][c].w, o4[g][c].w);
           }
         }
       }
