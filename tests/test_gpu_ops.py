@@ -66,7 +66,11 @@ def test_gemv(ctx, orc, N, K, M):
         assert np.all(np.abs(y[m] - ref) <= bound(x[m], w)), (m, np.max(np.abs(y[m] - ref)))
 
 
-@pytest.mark.parametrize("T,N,K", [(37, 300, 256), (128, 3072, 2048), (1, 64, 64), (5, 9, 13)])
+# (2048, 3072, 1024): 192-wide tiles, two rounds of the persistent grid (both
+# TMEM accumulators in turn); (1000, 4100, 512): partial row and column tiles
+# over several rounds
+@pytest.mark.parametrize("T,N,K", [(37, 300, 256), (128, 3072, 2048), (1, 64, 64), (5, 9, 13),
+                                   (2048, 3072, 1024), (1000, 4100, 512)])
 def test_gemm_prefill(ctx, orc, T, N, K):
     rng = np.random.default_rng(T + N + K)
     w = bf16(rng.normal(0, 0.02, (N, K)))

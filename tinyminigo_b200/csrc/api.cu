@@ -1020,15 +1020,20 @@ int forward_seq(tmg_ctx* c, tmg_kv* kv, int stream, const uint32_t* tokens, int6
            "gemm o");
       }
       CK(launch_rmsnorm(c->X, Lw.post_norm, eps, c->h, Tc, 1, c->Xn, c->stream), "rmsnorm");
-      CK(gemm_layer(c, c->Xn, Lw.wg, Lw.qg, Lw.sg, Tc, c->I, c->h, c->G, c->I, false), "gemm gate");
       if (c->i8) {
+        CK(gemm_layer(c, c->Xn, Lw.wg, Lw.qg, Lw.sg, Tc, c->I, c->h, c->G, c->I, false),
+           "gemm gate");
         CK(gemm_layer(c, c->Xn, nullptr, Lw.qu, Lw.su, Tc, c->I, c->h, c->U, c->I, false), "gemm up");
       } else if (gemm_tc_supported(c->h, Lw.wg) && gemm_tc_supported(c->h, Lw.wu)) {
-        // gate and up read the same input: its hi/lo split from the gate GEMM
-        CK(launch_gemm_tc(c->sp_hi, c->sp_lo, Lw.wu, Tc, c->I, c->h, c->U, c->I, false, c->d_err,
-                          c->stream),
-           "gemm up");
+        // gate and up read the same input: one hi/lo split, one launch whose
+        // tiles cover both outputs
+        CK(ensure_split(c, size_t(Tc) * c->h), "split");
+        CK(launch_split(c->Xn, Tc * c->h, c->sp_hi, c->sp_lo, c->stream), "split");
+        CK(launch_gemm_tc2(c->sp_hi, c->sp_lo, Lw.wg, c->I, c->G, c->I, Lw.wu, c->I, c->U, c->I,
+                           Tc, c->h, false, c->d_err, c->stream),
+           "gemm gate/up");
       } else {
+        CK(gemm(c, c->Xn, Lw.wg, Tc, c->I, c->h, c->G, c->I, false), "gemm gate");
         CK(gemm(c, c->Xn, Lw.wu, Tc, c->I, c->h, c->U, c->I, false), "gemm up");
       }
       float* down_y = tp ? c->Xn : c->X;

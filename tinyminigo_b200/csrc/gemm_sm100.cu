@@ -7,14 +7,20 @@
 // bf16(X - Xhi), ~16 bits together), and every K step issues two MMAs into
 // the same f32 TMEM accumulator: Xhi.W and Xlo.W.  W is exact in BF16.
 //
-// One CTA computes a 128 x BN tile (BN = 256):
+// Persistent: one CTA per SM walks the output tiles t = blockIdx.x,
+// blockIdx.x + gridDim.x, ... (128 x bn, bn <= 256 chosen per launch so the
+// tiles fill the SMs evenly; consecutive tiles share their 128 rows of X).
+// An optional second (W, Y) segment extends N (gate and up from one split
+// of their common input in one launch).  Roles:
 //   warp 0      TMA producer: per 64-wide K block, Xhi / Xlo [128 x 64] and
-//               W [BN x 64] tiles (128-byte swizzle) into a 3-stage ring;
-//   warp 1      allocates BN TMEM columns, issues tcgen05.mma (one elected
-//               lane; M=128, N=BN, K=16 per instruction) and commits each
-//               stage back to the producer, then the tile to the epilogue;
+//               W [bn x 64] tiles (128-byte swizzle) into a 3-stage ring;
+//   warp 1      allocates 2 x 256 TMEM columns (two accumulators), issues
+//               tcgen05.mma (one elected lane; M=128, N=bn, K=16 per
+//               instruction) into the tile's accumulator, commits each stage
+//               back to the producer and the finished tile to the epilogue;
 //   warps 2..5  epilogue: tcgen05.ld 32 lanes x 16 columns at a time, then
-//               store (or add into) Y in f32.
+//               store (or add into) Y in f32, and hand the accumulator back,
+//               so tile i's epilogue overlaps tile i+1's MMAs.
 // Every mbarrier wait is bounded; a wait that gives up sets the error word
 // and the CTA skips the rest of its work (the host reports TMG_ERR_TIMEOUT).
 // Single-GPU code: every CTA loads its own tiles; no peer memory.
@@ -31,11 +37,25 @@ namespace {
 
 constexpr int BM = 128, BN = 256, BK = 64, STAGES = 3;
 constexpr int A_BYTES = BM * BK * 2;  // 16 KB
-constexpr int B_BYTES = BN * BK * 2;  // 32 KB
+constexpr int B_BYTES = BN * BK * 2;  // 32 KB (a narrower tile uses its first bn rows)
 constexpr int STAGE_BYTES = 2 * A_BYTES + B_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 constexpr int kThreadsG = 192;
-constexpr uint32_t kTmemCols = BN;
+constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
+
+// The launch: rows T of X; output columns [0, N1) from W1 into Y1 and
+// [N1, N1 + N2) from W2 into Y2 (N2 = 0: one segment).
+struct GemmTcArgs {
+  float* y1;
+  int64_t ldy1;
+  float* y2;
+  int64_t ldy2;
+  int T, K, N1, N2;
+  int bn;              // tile width (multiple of 16, <= 256)
+  int nt1, nt2, mt;    // tiles along N1, N2 and T
+  int accumulate;
+  int32_t* err;
+};
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int c0, int c1) {
@@ -59,16 +79,19 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
   return d;
 }
 
-// kind::f16 instruction descriptor: BF16 x BF16 -> F32, both K-major.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) |
-                            (uint32_t(BM >> 4) << 24);
+// kind::f16 instruction descriptor: BF16 x BF16 -> F32, both K-major, M = 128, N = bn.
+__host__ __device__ constexpr uint32_t idesc_for(int bn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(bn >> 3) << 17) |
+         (uint32_t(BM >> 4) << 24);
+}
 
-__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t acc) {
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                     uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-      ::"r"(tmem_d), "l"(da), "l"(db), "r"(kIdesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
+      ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -93,26 +116,33 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
 
 __global__ void __launch_bounds__(kThreadsG, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_lo,
-                   const __grid_constant__ CUtensorMap map_w, float* __restrict__ y, int64_t ldy,
-                   int T, int N, int K, int accumulate, int32_t* err) {
+                   const __grid_constant__ CUtensorMap map_w1,
+                   const __grid_constant__ CUtensorMap map_w2, const GemmTcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* accum = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
-  __shared__ int failed;
+  uint64_t* acc_full = empty + STAGES;   // [2] a tile's accumulator is complete
+  uint64_t* acc_empty = acc_full + 2;    // [2] the epilogue has read it
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  __shared__ volatile int failed;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-  const int nk = (K + BK - 1) / BK;
+  const int nk = (a.K + BK - 1) / BK;
+  const int ntn = a.nt1 + a.nt2;
+  const int tiles = a.mt * ntn;
+  const uint32_t b_bytes = uint32_t(a.bn) * BK * 2;
+  const uint32_t idesc = idesc_for(a.bn);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
     failed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -128,66 +158,97 @@ __global__ void __launch_bounds__(kThreadsG, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0 && lane == 0) {
-    // TMA producer
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % STAGES;
-      const uint32_t ph = (kb / STAGES) & 1;
-      if (!mbar_wait(&empty[s], ph ^ 1)) {
-        atomicExch(err, 2);
-        failed = 1;
-        break;
+    // TMA producer: every tile's K blocks through the ring
+    int it = 0;
+    for (int t = blockIdx.x; t < tiles && !failed; t += gridDim.x) {
+      const int m0 = (t / ntn) * BM, nt = t % ntn;
+      const bool seg2 = nt >= a.nt1;
+      const int n0 = (seg2 ? nt - a.nt1 : nt) * a.bn;
+      const CUtensorMap* mw = seg2 ? &map_w2 : &map_w1;
+      for (int kb = 0; kb < nk; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1)) {
+          atomicExch(a.err, 2);
+          failed = 1;
+          break;
+        }
+        uint8_t* st = smem + s * STAGE_BYTES;
+        mbar_expect_tx(&full[s], 2 * A_BYTES + b_bytes);
+        tma_load_2d(st, &map_hi, &full[s], kb * BK, m0);
+        tma_load_2d(st + A_BYTES, &map_lo, &full[s], kb * BK, m0);
+        tma_load_2d(st + 2 * A_BYTES, mw, &full[s], kb * BK, n0);
       }
-      uint8_t* st = smem + s * STAGE_BYTES;
-      mbar_expect_tx(&full[s], STAGE_BYTES);
-      tma_load_2d(st, &map_hi, &full[s], kb * BK, m0);
-      tma_load_2d(st + A_BYTES, &map_lo, &full[s], kb * BK, m0);
-      tma_load_2d(st + 2 * A_BYTES, &map_w, &full[s], kb * BK, n0);
     }
   } else if (warp == 1 && lane == 0) {
-    // MMA issuer
-    bool ok = true;
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % STAGES;
-      const uint32_t ph = (kb / STAGES) & 1;
-      if (!mbar_wait(&full[s], ph)) {
-        atomicExch(err, 2);
+    // MMA issuer: tile i into accumulator i & 1
+    int it = 0, tl = 0;
+    for (int t = blockIdx.x; t < tiles && !failed; t += gridDim.x, ++tl) {
+      const int buf = tl & 1;
+      if (!mbar_wait(&acc_empty[buf], ((tl >> 1) & 1) ^ 1)) {
+        atomicExch(a.err, 2);
         failed = 1;
-        ok = false;
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t a_hi = smem_u32(smem + s * STAGE_BYTES);
-      const uint32_t a_lo = a_hi + A_BYTES;
-      const uint32_t b = a_hi + 2 * A_BYTES;
+      const uint32_t acc_t = tmem + uint32_t(buf * BN);
+      bool ok = true;
+      for (int kb = 0; kb < nk; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait(&full[s], ph)) {
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t a_hi = smem_u32(smem + s * STAGE_BYTES);
+        const uint32_t a_lo = a_hi + A_BYTES;
+        const uint32_t b = a_hi + 2 * A_BYTES;
 #pragma unroll
-      for (int k = 0; k < BK / 16; ++k) {
-        const uint64_t db = umma_desc(b + k * 32);
-        umma(tmem, umma_desc(a_hi + k * 32), db, (kb | k) != 0);
-        umma(tmem, umma_desc(a_lo + k * 32), db, 1);
+        for (int k = 0; k < BK / 16; ++k) {
+          const uint64_t db = umma_desc(b + k * 32);
+          umma(acc_t, umma_desc(a_hi + k * 32), db, idesc, (kb | k) != 0);
+          umma(acc_t, umma_desc(a_lo + k * 32), db, idesc, 1);
+        }
+        umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
       }
-      umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+      if (!ok) {
+        atomicExch(a.err, 2);
+        failed = 1;
+        break;
+      }
+      umma_commit(&acc_full[buf]);
     }
-    if (ok) umma_commit(accum);
   } else if (warp >= 2) {
     // epilogue: warp w reads TMEM lanes 32 * (w % 4) ...
     const int q = warp & 3;
-    const bool ok = mbar_wait(accum, 0);
-    if (!ok) {
-      atomicExch(err, 2);
-    } else {
+    int tl = 0;
+    for (int t = blockIdx.x; t < tiles && !failed; t += gridDim.x, ++tl) {
+      const int buf = tl & 1;
+      if (!mbar_wait(&acc_full[buf], (tl >> 1) & 1)) {
+        atomicExch(a.err, 2);
+        failed = 1;
+        break;
+      }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int m0 = (t / ntn) * BM, nt = t % ntn;
+      const bool seg2 = nt >= a.nt1;
+      const int n0 = (seg2 ? nt - a.nt1 : nt) * a.bn;
+      const int N = seg2 ? a.N2 : a.N1;
+      float* y = seg2 ? a.y2 : a.y1;
+      const int64_t ldy = seg2 ? a.ldy2 : a.ldy1;
       const int row = m0 + q * 32 + lane;
-      for (int c = 0; c < BN; c += 16) {
+      for (int c = 0; c < a.bn; c += 16) {
         float v[16];
-        tmem_ld16(tmem + (uint32_t(q * 32) << 16) + uint32_t(c), v);
-        if (row < T) {
+        tmem_ld16(tmem + (uint32_t(q * 32) << 16) + uint32_t(buf * BN + c), v);
+        if (row < a.T && n0 + c < N) {
           float* yr = y + int64_t(row) * ldy + n0 + c;
           if (n0 + c + 16 <= N && (reinterpret_cast<uintptr_t>(yr) & 15) == 0) {
 #pragma unroll
             for (int i = 0; i < 16; i += 4) {
               float4* p = reinterpret_cast<float4*>(yr + i);
               float4 o = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-              if (accumulate) {
+              if (a.accumulate) {
                 const float4 old = *p;
                 o.x += old.x;
                 o.y += old.y;
@@ -198,10 +259,14 @@ __global__ void __launch_bounds__(kThreadsG, 1)
             }
           } else {
             for (int i = 0; i < 16; ++i)
-              if (n0 + c + i < N) yr[i] = accumulate ? yr[i] + v[i] : v[i];
+              if (n0 + c + i < N) yr[i] = a.accumulate ? yr[i] + v[i] : v[i];
           }
         }
       }
+      // the accumulator goes back to the MMA warp
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -342,20 +407,72 @@ cudaError_t launch_swiglu_split(const float* g, const float* u, int64_t n, uint1
   return cudaGetLastError();
 }
 
+// Tile width for N columns over `rows_tiles` 128-row blocks on num_sms SMs:
+// the widest of 256, 192, 128 (multiples of 16 the MMA takes) whose tiles
+// fill the last round of the persistent grid best.
+int pick_bn(int64_t N, int64_t m_tiles, int num_sms) {
+  int best = 256;
+  double best_eff = -1.0;
+  for (int bn : {256, 192, 128}) {
+    const int64_t tiles = m_tiles * ((N + bn - 1) / bn);
+    const int64_t rounds = (tiles + num_sms - 1) / num_sms;
+    const double eff = double(tiles) / double(rounds * num_sms) * double(N) /
+                       double(((N + bn - 1) / bn) * bn);
+    if (eff > best_eff + 0.02) {
+      best_eff = eff;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+cudaError_t launch_gemm_tc2(const uint16_t* x_hi, const uint16_t* x_lo, const uint16_t* w1,
+                            int64_t N1, float* y1, int64_t ldy1, const uint16_t* w2, int64_t N2,
+                            float* y2, int64_t ldy2, int64_t T, int64_t K, bool accumulate,
+                            int32_t* err, cudaStream_t s) {
+  if (T <= 0 || N1 + N2 <= 0) return cudaSuccess;
+  if (K % 8 != 0 || N1 <= 0 || N2 < 0 || (N2 > 0 && !w2) || T > (int64_t(1) << 30) ||
+      N1 > (int64_t(1) << 30) || N2 > (int64_t(1) << 30) || K > (int64_t(1) << 30) || !err)
+    return cudaErrorInvalidValue;
+  static int num_sms = 0;
+  if (!num_sms) {
+    int dev = 0;
+    TMG_CUDA_TRY(cudaGetDevice(&dev));
+    TMG_CUDA_TRY(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev));
+  }
+  const int64_t mt = (T + BM - 1) / BM;
+  // one width for both segments (gate and up have the same N)
+  const int bn = pick_bn(N1 + N2, mt, num_sms);
+  CUtensorMap mh, ml, mw1, mw2;
+  if (!make_map(&mh, x_hi, T, K, BM) || !make_map(&ml, x_lo, T, K, BM) ||
+      !make_map(&mw1, w1, N1, K, bn) || !make_map(&mw2, N2 > 0 ? w2 : w1, N2 > 0 ? N2 : N1, K, bn))
+    return cudaErrorInvalidValue;
+  GemmTcArgs a;
+  a.y1 = y1;
+  a.ldy1 = ldy1;
+  a.y2 = y2;
+  a.ldy2 = ldy2;
+  a.T = int(T);
+  a.K = int(K);
+  a.N1 = int(N1);
+  a.N2 = int(N2);
+  a.bn = bn;
+  a.nt1 = int((N1 + bn - 1) / bn);
+  a.nt2 = int((N2 + bn - 1) / bn);
+  a.mt = int(mt);
+  a.accumulate = accumulate ? 1 : 0;
+  a.err = err;
+  const int64_t tiles = mt * (a.nt1 + a.nt2);
+  const unsigned grid = unsigned(std::min<int64_t>(tiles, num_sms));
+  gemm_tc_kernel<<<grid, kThreadsG, SMEM_BYTES, s>>>(mh, ml, mw1, mw2, a);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_gemm_tc(const uint16_t* x_hi, const uint16_t* x_lo, const uint16_t* w,
                            int64_t T, int64_t N, int64_t K, float* y, int64_t ldy,
                            bool accumulate, int32_t* err, cudaStream_t s) {
-  if (T <= 0 || N <= 0) return cudaSuccess;
-  if (K % 8 != 0 || T > (int64_t(1) << 30) || N > (int64_t(1) << 30) || K > (int64_t(1) << 30))
-    return cudaErrorInvalidValue;
-  CUtensorMap mh, ml, mw;
-  if (!make_map(&mh, x_hi, T, K, BM) || !make_map(&ml, x_lo, T, K, BM) ||
-      !make_map(&mw, w, N, K, BN))
-    return cudaErrorInvalidValue;
-  dim3 grid(unsigned((N + BN - 1) / BN), unsigned((T + BM - 1) / BM));
-  gemm_tc_kernel<<<grid, kThreadsG, SMEM_BYTES, s>>>(mh, ml, mw, y, ldy, int(T), int(N), int(K),
-                                                     accumulate ? 1 : 0, err);
-  return cudaGetLastError();
+  return launch_gemm_tc2(x_hi, x_lo, w, N, y, ldy, nullptr, 0, nullptr, 0, T, K, accumulate, err,
+                         s);
 }
 
 }  // namespace tmg

@@ -242,6 +242,12 @@ cudaError_t launch_swiglu_split(const float* g, const float* u, int64_t n, uint1
 cudaError_t launch_gemm_tc(const uint16_t* x_hi, const uint16_t* x_lo, const uint16_t* w,
                            int64_t T, int64_t N, int64_t K, float* y, int64_t ldy,
                            bool accumulate, int32_t* err, cudaStream_t s);
+// The same over two weight matrices of one input in one launch: columns
+// [0, N1) of W1 into y1, then [0, N2) of W2 into y2 (N2 = 0: W1 only).
+cudaError_t launch_gemm_tc2(const uint16_t* x_hi, const uint16_t* x_lo, const uint16_t* w1,
+                            int64_t N1, float* y1, int64_t ldy1, const uint16_t* w2, int64_t N2,
+                            float* y2, int64_t ldy2, int64_t T, int64_t K, bool accumulate,
+                            int32_t* err, cudaStream_t s);
 // argmax per row (op level and the first greedy step).
 cudaError_t launch_argmax_rows(const float* logits, int64_t V, int rows, uint32_t* out,
                                cudaStream_t s);
