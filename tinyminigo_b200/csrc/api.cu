@@ -123,6 +123,9 @@ struct tmg_ctx {
   // hi/lo BF16 split of the prefill GEMM's activations
   uint16_t *sp_hi = nullptr, *sp_lo = nullptr;
   size_t sp_cap = 0;
+  // hi/lo parts of the SwiGLU output written by the gate/up GEMM's epilogue
+  uint16_t *sa_hi = nullptr, *sa_lo = nullptr;
+  size_t sa_cap = 0;
   // BF16 parts of q, k and v^T for the tensor-core prefill attention
   void* pfa = nullptr;
   size_t pfa_cap = 0;
@@ -622,6 +625,19 @@ struct NvtxRange {
   NvtxRange& operator=(const NvtxRange&) = delete;
 };
 
+cudaError_t ensure_act_split(tmg_ctx* c, size_t n) {
+  if (c->sa_cap >= n) return cudaSuccess;
+  TMG_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  if (c->sa_hi) cudaFree(c->sa_hi);
+  if (c->sa_lo) cudaFree(c->sa_lo);
+  c->sa_hi = c->sa_lo = nullptr;
+  c->sa_cap = 0;
+  TMG_CUDA_TRY(cudaMalloc(&c->sa_hi, n * 2));
+  TMG_CUDA_TRY(cudaMalloc(&c->sa_lo, n * 2));
+  c->sa_cap = n;
+  return cudaSuccess;
+}
+
 cudaError_t ensure_split(tmg_ctx* c, size_t n) {
   if (c->sp_cap >= n) return cudaSuccess;
   TMG_CUDA_TRY(cudaStreamSynchronize(c->stream));
@@ -1020,10 +1036,24 @@ int forward_seq(tmg_ctx* c, tmg_kv* kv, int stream, const uint32_t* tokens, int6
            "gemm o");
       }
       CK(launch_rmsnorm(c->X, Lw.post_norm, eps, c->h, Tc, 1, c->Xn, c->stream), "rmsnorm");
+      bool swiglu_done = false;  // act already split for the down GEMM
       if (c->i8) {
         CK(gemm_layer(c, c->Xn, Lw.wg, Lw.qg, Lw.sg, Tc, c->I, c->h, c->G, c->I, false),
            "gemm gate");
         CK(gemm_layer(c, c->Xn, nullptr, Lw.qu, Lw.su, Tc, c->I, c->h, c->U, c->I, false), "gemm up");
+      } else if (gemm_tc_supported(c->h, Lw.wg) && gemm_tc_supported(c->h, Lw.wu) &&
+                 gemm_tc_supported(c->I, Lw.wd) &&
+                 ensure_act_split(c, size_t(Tc) * c->I) == cudaSuccess &&
+                 gemm_swiglu_supported(c->I, c->sa_hi, c->sa_lo)) {
+        // gate and up read the same input: one hi/lo split, one launch whose
+        // tiles hold matching gate and up columns, SwiGLU in its epilogue
+        // written as the down GEMM's hi/lo operands
+        CK(ensure_split(c, size_t(Tc) * c->h), "split");
+        CK(launch_split(c->Xn, Tc * c->h, c->sp_hi, c->sp_lo, c->stream), "split");
+        CK(launch_gemm_tc_swiglu(c->sp_hi, c->sp_lo, Lw.wg, Lw.wu, c->I, Tc, c->h, c->sa_hi,
+                                 c->sa_lo, c->d_err, c->stream),
+           "gemm gate/up + swiglu");
+        swiglu_done = true;
       } else if (gemm_tc_supported(c->h, Lw.wg) && gemm_tc_supported(c->h, Lw.wu)) {
         // gate and up read the same input: one hi/lo split, one launch whose
         // tiles cover both outputs
@@ -1037,7 +1067,11 @@ int forward_seq(tmg_ctx* c, tmg_kv* kv, int stream, const uint32_t* tokens, int6
         CK(gemm(c, c->Xn, Lw.wu, Tc, c->I, c->h, c->U, c->I, false), "gemm up");
       }
       float* down_y = tp ? c->Xn : c->X;
-      if (c->i8) {
+      if (swiglu_done) {
+        CK(launch_gemm_tc(c->sa_hi, c->sa_lo, Lw.wd, Tc, c->h, c->I, down_y, c->h, !tp, c->d_err,
+                          c->stream),
+           "gemm down");
+      } else if (c->i8) {
         CK(launch_swiglu(c->G, c->U, Tc * c->I, c->G, c->stream), "swiglu");
         CK(gemm_layer(c, c->G, nullptr, Lw.qd, Lw.sd, Tc, c->h, c->I, down_y, c->h, !tp), "gemm down");
       } else if (gemm_tc_supported(c->I, Lw.wd) && (ensure_split(c, size_t(Tc) * c->I) == cudaSuccess) &&
@@ -1535,6 +1569,7 @@ int tmg_destroy(tmg_ctx* c) {
   free_all(c->allocs);
   for (void* p : {(void*)c->X, (void*)c->Xn, (void*)c->QKV, (void*)c->ATT, (void*)c->G,
                   (void*)c->U, (void*)c->d_tok, c->op_buf, (void*)c->sp_hi, (void*)c->sp_lo, c->pfa,
+                  (void*)c->sa_hi, (void*)c->sa_lo,
                   (void*)c->dq, (void*)c->i8acc})
     if (p) cudaFree(p);
   if (c->pinned) cudaFreeHost(c->pinned);

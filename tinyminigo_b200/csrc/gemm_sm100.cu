@@ -55,6 +55,14 @@ struct GemmTcArgs {
   int nt1, nt2, mt;    // tiles along N1, N2 and T
   int accumulate;
   int32_t* err;
+  // SwiGLU mode: each tile holds bn/2 gate rows (W1) and the same bn/2 up
+  // rows (W2) of the columns [n0, n0 + bn/2), and the epilogue writes
+  // act = g / (1 + exp(-g)) * u straight as BF16 hi/lo parts (the next GEMM's
+  // operands) instead of y1 / y2.
+  int swiglu;
+  uint16_t* act_hi;
+  uint16_t* act_lo;
+  int64_t ld_act;
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
@@ -163,7 +171,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
     for (int t = blockIdx.x; t < tiles && !failed; t += gridDim.x) {
       const int m0 = (t / ntn) * BM, nt = t % ntn;
       const bool seg2 = nt >= a.nt1;
-      const int n0 = (seg2 ? nt - a.nt1 : nt) * a.bn;
+      const int n0 = a.swiglu ? nt * (a.bn / 2) : (seg2 ? nt - a.nt1 : nt) * a.bn;
       const CUtensorMap* mw = seg2 ? &map_w2 : &map_w1;
       for (int kb = 0; kb < nk; ++kb, ++it) {
         const int s = it % STAGES;
@@ -177,7 +185,12 @@ __global__ void __launch_bounds__(kThreadsG, 1)
         mbar_expect_tx(&full[s], 2 * A_BYTES + b_bytes);
         tma_load_2d(st, &map_hi, &full[s], kb * BK, m0);
         tma_load_2d(st + A_BYTES, &map_lo, &full[s], kb * BK, m0);
-        tma_load_2d(st + 2 * A_BYTES, mw, &full[s], kb * BK, n0);
+        if (a.swiglu) {  // gate rows, then the same up rows
+          tma_load_2d(st + 2 * A_BYTES, &map_w1, &full[s], kb * BK, n0);
+          tma_load_2d(st + 2 * A_BYTES + (a.bn / 2) * BK * 2, &map_w2, &full[s], kb * BK, n0);
+        } else {
+          tma_load_2d(st + 2 * A_BYTES, mw, &full[s], kb * BK, n0);
+        }
       }
     }
   } else if (warp == 1 && lane == 0) {
@@ -232,15 +245,59 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const int m0 = (t / ntn) * BM, nt = t % ntn;
+      const int row = m0 + q * 32 + lane;
+      const uint32_t tacc = tmem + (uint32_t(q * 32) << 16) + uint32_t(buf * BN);
+      if (a.swiglu) {
+        // columns [0, bn/2) hold gate, [bn/2, bn) up, for act columns n0 ..
+        const int half = a.bn / 2, n0 = nt * half;
+        for (int c = 0; c < half; c += 16) {
+          float g[16], u[16];
+          tmem_ld16(tacc + uint32_t(c), g);
+          tmem_ld16(tacc + uint32_t(half + c), u);
+          if (row < a.T && n0 + c < a.N1) {
+            uint32_t hw[8], lw[8];
+#pragma unroll
+            for (int i = 0; i < 16; i += 2) {
+              // SwiGLU (src/model.rs:473-475) as swiglu_split4_kernel computes it
+              const float a0 = (g[i] / (1.0f + expf(-g[i]))) * u[i];
+              const float a1 = (g[i + 1] / (1.0f + expf(-g[i + 1]))) * u[i + 1];
+              const __nv_bfloat16 h0 = __float2bfloat16_rn(a0), h1 = __float2bfloat16_rn(a1);
+              const __nv_bfloat16 l0 = __float2bfloat16_rn(a0 - __bfloat162float(h0));
+              const __nv_bfloat16 l1 = __float2bfloat16_rn(a1 - __bfloat162float(h1));
+              hw[i / 2] = uint32_t(__bfloat16_as_ushort(h0)) | (uint32_t(__bfloat16_as_ushort(h1)) << 16);
+              lw[i / 2] = uint32_t(__bfloat16_as_ushort(l0)) | (uint32_t(__bfloat16_as_ushort(l1)) << 16);
+            }
+            const int64_t o = int64_t(row) * a.ld_act + n0 + c;
+            if (n0 + c + 16 <= a.N1) {
+              uint4* ph = reinterpret_cast<uint4*>(a.act_hi + o);
+              uint4* pl = reinterpret_cast<uint4*>(a.act_lo + o);
+              ph[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+              ph[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+              pl[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+              pl[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (n0 + c + i < a.N1) {
+                  a.act_hi[o + i] = uint16_t(hw[i / 2] >> (16 * (i & 1)));
+                  a.act_lo[o + i] = uint16_t(lw[i / 2] >> (16 * (i & 1)));
+                }
+            }
+          }
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        continue;
+      }
       const bool seg2 = nt >= a.nt1;
       const int n0 = (seg2 ? nt - a.nt1 : nt) * a.bn;
       const int N = seg2 ? a.N2 : a.N1;
       float* y = seg2 ? a.y2 : a.y1;
       const int64_t ldy = seg2 ? a.ldy2 : a.ldy1;
-      const int row = m0 + q * 32 + lane;
       for (int c = 0; c < a.bn; c += 16) {
         float v[16];
-        tmem_ld16(tmem + (uint32_t(q * 32) << 16) + uint32_t(buf * BN + c), v);
+        tmem_ld16(tacc + uint32_t(c), v);
         if (row < a.T && n0 + c < N) {
           float* yr = y + int64_t(row) * ldy + n0 + c;
           if (n0 + c + 16 <= N && (reinterpret_cast<uintptr_t>(yr) & 15) == 0) {
@@ -462,9 +519,60 @@ cudaError_t launch_gemm_tc2(const uint16_t* x_hi, const uint16_t* x_lo, const ui
   a.mt = int(mt);
   a.accumulate = accumulate ? 1 : 0;
   a.err = err;
+  a.swiglu = 0;
+  a.act_hi = a.act_lo = nullptr;
+  a.ld_act = 0;
   const int64_t tiles = mt * (a.nt1 + a.nt2);
   const unsigned grid = unsigned(std::min<int64_t>(tiles, num_sms));
   gemm_tc_kernel<<<grid, kThreadsG, SMEM_BYTES, s>>>(mh, ml, mw1, mw2, a);
+  return cudaGetLastError();
+}
+
+bool gemm_swiglu_supported(int64_t I, const void* act_hi, const void* act_lo) {
+  return I % 16 == 0 && (reinterpret_cast<uintptr_t>(act_hi) & 31) == 0 &&
+         (reinterpret_cast<uintptr_t>(act_lo) & 31) == 0;
+}
+
+cudaError_t launch_gemm_tc_swiglu(const uint16_t* x_hi, const uint16_t* x_lo, const uint16_t* wg,
+                                  const uint16_t* wu, int64_t I, int64_t T, int64_t K,
+                                  uint16_t* act_hi, uint16_t* act_lo, int32_t* err,
+                                  cudaStream_t s) {
+  if (T <= 0 || I <= 0) return cudaSuccess;
+  if (K % 8 != 0 || T > (int64_t(1) << 30) || I > (int64_t(1) << 30) || K > (int64_t(1) << 30) ||
+      !err || !gemm_swiglu_supported(I, act_hi, act_lo))
+    return cudaErrorInvalidValue;
+  static int num_sms = 0;
+  if (!num_sms) {
+    int dev = 0;
+    TMG_CUDA_TRY(cudaGetDevice(&dev));
+    TMG_CUDA_TRY(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev));
+  }
+  const int64_t mt = (T + BM - 1) / BM;
+  const int bn = pick_bn(2 * I, mt, num_sms);  // bn / 2 gate + bn / 2 up columns per tile
+  CUtensorMap mh, ml, mg, mu;
+  if (!make_map(&mh, x_hi, T, K, BM) || !make_map(&ml, x_lo, T, K, BM) ||
+      !make_map(&mg, wg, I, K, bn / 2) || !make_map(&mu, wu, I, K, bn / 2))
+    return cudaErrorInvalidValue;
+  GemmTcArgs a;
+  a.y1 = a.y2 = nullptr;
+  a.ldy1 = a.ldy2 = 0;
+  a.T = int(T);
+  a.K = int(K);
+  a.N1 = int(I);
+  a.N2 = 0;
+  a.bn = bn;
+  a.nt1 = int((I + bn / 2 - 1) / (bn / 2));
+  a.nt2 = 0;
+  a.mt = int(mt);
+  a.accumulate = 0;
+  a.err = err;
+  a.swiglu = 1;
+  a.act_hi = act_hi;
+  a.act_lo = act_lo;
+  a.ld_act = I;
+  const int64_t tiles = mt * a.nt1;
+  const unsigned grid = unsigned(std::min<int64_t>(tiles, num_sms));
+  gemm_tc_kernel<<<grid, kThreadsG, SMEM_BYTES, s>>>(mh, ml, mg, mu, a);
   return cudaGetLastError();
 }
 

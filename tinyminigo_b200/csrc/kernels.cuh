@@ -242,6 +242,14 @@ cudaError_t launch_swiglu_split(const float* g, const float* u, int64_t n, uint1
 cudaError_t launch_gemm_tc(const uint16_t* x_hi, const uint16_t* x_lo, const uint16_t* w,
                            int64_t T, int64_t N, int64_t K, float* y, int64_t ldy,
                            bool accumulate, int32_t* err, cudaStream_t s);
+// gate and up of one input in one launch with the SwiGLU in the epilogue:
+// act[T, I] = silu(x . Wg^T) * (x . Wu^T) written as its BF16 hi/lo parts
+// (the down GEMM's operands); I % 16 == 0, act_hi / act_lo 32-byte aligned.
+bool gemm_swiglu_supported(int64_t I, const void* act_hi, const void* act_lo);
+cudaError_t launch_gemm_tc_swiglu(const uint16_t* x_hi, const uint16_t* x_lo, const uint16_t* wg,
+                                  const uint16_t* wu, int64_t I, int64_t T, int64_t K,
+                                  uint16_t* act_hi, uint16_t* act_lo, int32_t* err,
+                                  cudaStream_t s);
 // The same over two weight matrices of one input in one launch: columns
 // [0, N1) of W1 into y1, then [0, N2) of W2 into y2 (N2 = 0: W1 only).
 cudaError_t launch_gemm_tc2(const uint16_t* x_hi, const uint16_t* x_lo, const uint16_t* w1,
