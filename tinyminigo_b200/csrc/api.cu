@@ -654,13 +654,18 @@ cudaError_t ensure_split(tmg_ctx* c, size_t n) {
 // Causal prefill attention of T query rows at pos0.. over cache rows
 // [0, pos0 + T): the tcgen05 kernel for head dim 64 (TMG_PREFILL_ATTN=simt
 // keeps the CUDA-core kernel), else the CUDA-core one.
+// With parts (out_hi, out_lo) the tensor-core kernel writes the output as
+// the O GEMM's hi/lo operands and *wrote_parts is set; the CUDA-core kernel
+// always writes f32 into out.
 cudaError_t prefill_attention(tmg_ctx* c, const float* q, int64_t q_ld, const float* kc,
                               const float* vc, int64_t T, int64_t pos0, float scale, float* out,
-                              int64_t out_ld, int nq, int nkv, int d) {
+                              int64_t out_ld, int nq, int nkv, int d, uint16_t* out_hi = nullptr,
+                              uint16_t* out_lo = nullptr, bool* wrote_parts = nullptr) {
   static const bool simt = [] {
     const char* e = std::getenv("TMG_PREFILL_ATTN");
     return e && std::strcmp(e, "simt") == 0;
   }();
+  if (wrote_parts) *wrote_parts = false;
   if (!simt && attn_prefill_tc_ok(q, q_ld, kc, vc, T, pos0, nq, nkv, d, out, out_ld)) {
     const size_t need = attn_prefill_tc_scratch(nq, nkv, T, pos0 + T);
     if (c->pfa_cap < need) {
@@ -672,8 +677,11 @@ cudaError_t prefill_attention(tmg_ctx* c, const float* q, int64_t q_ld, const fl
       TMG_CUDA_TRY(cudaMalloc(&c->pfa, bytes));
       c->pfa_cap = bytes;
     }
-    return launch_attn_prefill_tc(q, q_ld, kc, vc, T, pos0, nq, nkv, scale, out, out_ld, c->pfa,
-                                  c->pfa_cap, c->d_err, c->stream);
+    const bool parts = out_hi && out_lo;
+    if (wrote_parts) *wrote_parts = parts;
+    return launch_attn_prefill_tc(q, q_ld, kc, vc, T, pos0, nq, nkv, scale, out,
+                                  parts ? out_hi : nullptr, parts ? out_lo : nullptr, out_ld,
+                                  c->pfa, c->pfa_cap, c->d_err, c->stream);
   }
   return launch_attn_prefill(q, q_ld, kc, vc, T, pos0, nq, nkv, d, scale, out, out_ld, c->stream);
 }
@@ -1017,17 +1025,38 @@ int forward_seq(tmg_ctx* c, tmg_kv* kv, int stream, const uint32_t* tokens, int6
       NvtxRange layer_range(rname);
       float* kc = kv->k[l] + size_t(stream) * kv->cap * kvd;
       float* vc = kv->v[l] + size_t(stream) * kv->cap * kvd;
-      CK(launch_rmsnorm(c->X, Lw.in_norm, eps, c->h, Tc, 1, c->Xn, c->stream), "rmsnorm");
-      CK(gemm_layer(c, c->Xn, Lw.wqkv, Lw.qqkv, Lw.sqkv, Tc, c->qkv_rows, c->h, c->QKV, c->qkv_rows,
-                    false),
-         "gemm qkv");
+      if (!c->i8 && gemm_tc_supported(c->h, Lw.wqkv)) {
+        // rmsnorm written straight as the qkv GEMM's hi/lo operands
+        CK(ensure_split(c, size_t(Tc) * c->h), "split");
+        CK(launch_rmsnorm_split(c->X, Lw.in_norm, eps, c->h, Tc, c->sp_hi, c->sp_lo, c->stream),
+           "rmsnorm");
+        CK(launch_gemm_tc(c->sp_hi, c->sp_lo, Lw.wqkv, Tc, c->qkv_rows, c->h, c->QKV, c->qkv_rows,
+                          false, c->d_err, c->stream),
+           "gemm qkv");
+      } else {
+        CK(launch_rmsnorm(c->X, Lw.in_norm, eps, c->h, Tc, 1, c->Xn, c->stream), "rmsnorm");
+        CK(gemm_layer(c, c->Xn, Lw.wqkv, Lw.qqkv, Lw.sqkv, Tc, c->qkv_rows, c->h, c->QKV,
+                      c->qkv_rows, false),
+           "gemm qkv");
+      }
       CK(launch_rope_append(c->QKV, c->qkv_rows, Tc, c->nq, c->nkv, c->d, kv->rope_cos,
                             kv->rope_sin, pos0, kc, vc, c->stream),
          "rope");
-      CK(prefill_attention(c, c->QKV, c->qkv_rows, kc, vc, Tc, pos0, scale, c->ATT,
-                           int64_t(c->nq) * c->d, c->nq, c->nkv, c->d),
+      // the attention output straight as the O GEMM's hi/lo operands when
+      // that GEMM runs on the tensor cores
+      const int64_t qd = int64_t(c->nq) * c->d;
+      const bool o_parts = !tp && !c->i8 && gemm_tc_supported(qd, Lw.wo) &&
+                           ensure_split(c, size_t(Tc) * std::max<int64_t>(qd, c->h)) == cudaSuccess;
+      bool att_parts = false;
+      CK(prefill_attention(c, c->QKV, c->qkv_rows, kc, vc, Tc, pos0, scale, c->ATT, qd, c->nq,
+                           c->nkv, c->d, o_parts ? c->sp_hi : nullptr,
+                           o_parts ? c->sp_lo : nullptr, &att_parts),
          "attention");
-      if (tp) {
+      if (att_parts) {
+        CK(launch_gemm_tc(c->sp_hi, c->sp_lo, Lw.wo, Tc, c->h, qd, c->X, c->h, true, c->d_err,
+                          c->stream),
+           "gemm o");
+      } else if (tp) {
         CK(gemm(c, c->ATT, Lw.wo, Tc, c->h, int64_t(c->nq) * c->d, c->Xn, c->h, false), "gemm o");
         CK(tp_reduce_add(c, c->Xn, c->X, Tc * c->h), "allreduce");
       } else {
@@ -1035,21 +1064,29 @@ int forward_seq(tmg_ctx* c, tmg_kv* kv, int stream, const uint32_t* tokens, int6
                       true),
            "gemm o");
       }
-      CK(launch_rmsnorm(c->X, Lw.post_norm, eps, c->h, Tc, 1, c->Xn, c->stream), "rmsnorm");
+      // the MLP's input: rmsnorm as f32 (int8 weights, tensor parallel, other
+      // shapes) or straight as the gate/up GEMM's hi/lo operands
+      const bool fuse_mlp = !c->i8 && gemm_tc_supported(c->h, Lw.wg) &&
+                            gemm_tc_supported(c->h, Lw.wu) && gemm_tc_supported(c->I, Lw.wd) &&
+                            ensure_act_split(c, size_t(Tc) * c->I) == cudaSuccess &&
+                            gemm_swiglu_supported(c->I, c->sa_hi, c->sa_lo);
+      if (fuse_mlp) {
+        CK(ensure_split(c, size_t(Tc) * c->h), "split");
+        CK(launch_rmsnorm_split(c->X, Lw.post_norm, eps, c->h, Tc, c->sp_hi, c->sp_lo,
+                                c->stream),
+           "rmsnorm");
+      } else {
+        CK(launch_rmsnorm(c->X, Lw.post_norm, eps, c->h, Tc, 1, c->Xn, c->stream), "rmsnorm");
+      }
       bool swiglu_done = false;  // act already split for the down GEMM
       if (c->i8) {
         CK(gemm_layer(c, c->Xn, Lw.wg, Lw.qg, Lw.sg, Tc, c->I, c->h, c->G, c->I, false),
            "gemm gate");
         CK(gemm_layer(c, c->Xn, nullptr, Lw.qu, Lw.su, Tc, c->I, c->h, c->U, c->I, false), "gemm up");
-      } else if (gemm_tc_supported(c->h, Lw.wg) && gemm_tc_supported(c->h, Lw.wu) &&
-                 gemm_tc_supported(c->I, Lw.wd) &&
-                 ensure_act_split(c, size_t(Tc) * c->I) == cudaSuccess &&
-                 gemm_swiglu_supported(c->I, c->sa_hi, c->sa_lo)) {
-        // gate and up read the same input: one hi/lo split, one launch whose
-        // tiles hold matching gate and up columns, SwiGLU in its epilogue
-        // written as the down GEMM's hi/lo operands
-        CK(ensure_split(c, size_t(Tc) * c->h), "split");
-        CK(launch_split(c->Xn, Tc * c->h, c->sp_hi, c->sp_lo, c->stream), "split");
+      } else if (fuse_mlp) {
+        // gate and up read the same input: one launch whose tiles hold
+        // matching gate and up columns, SwiGLU in its epilogue written as the
+        // down GEMM's hi/lo operands
         CK(launch_gemm_tc_swiglu(c->sp_hi, c->sp_lo, Lw.wg, Lw.wu, c->I, Tc, c->h, c->sa_hi,
                                  c->sa_lo, c->d_err, c->stream),
            "gemm gate/up + swiglu");

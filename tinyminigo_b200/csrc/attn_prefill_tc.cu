@@ -157,6 +157,8 @@ __device__ __forceinline__ float ex2f(float x) {
 
 struct PfArgs {
   float* out;        // [T, out_ld]: head h at columns h * 64
+  uint16_t* out_hi;  // or (when set) its BF16 hi/lo parts, same layout
+  uint16_t* out_lo;
   int64_t out_ld;
   int32_t* err;
   int T;             // query rows
@@ -441,12 +443,31 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       failed = 1;
       atomicExch(a.err, 2);
     } else if (q0 + r < a.T) {
-      float* dst = a.out + int64_t(q0 + r) * a.out_ld + int64_t(h) * kPD + hf * 32;
+      const int64_t base = int64_t(q0 + r) * a.out_ld + int64_t(h) * kPD + hf * 32;
       const float inv = lt > 0.f ? 1.f / lt : 0.f;
+      if (a.out_hi) {
+        // the O GEMM's operands: hi = bf16(v), lo = bf16(v - hi)
 #pragma unroll
-      for (int c = 0; c < 32; c += 4)
-        *reinterpret_cast<float4*>(dst + c) =
-            make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
+        for (int c = 0; c < 32; c += 8) {
+          uint32_t hw[4], lw[4];
+#pragma unroll
+          for (int t = 0; t < 8; t += 2) {
+            const float v0 = o[c + t] * inv, v1 = o[c + t + 1] * inv;
+            const uint32_t hb = bf16x2_bits(v0, v1);
+            hw[t / 2] = hb;
+            lw[t / 2] = bf16x2_bits(v0 - __uint_as_float(hb << 16),
+                                    v1 - __uint_as_float(hb & 0xffff0000u));
+          }
+          *reinterpret_cast<uint4*>(a.out_hi + base + c) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          *reinterpret_cast<uint4*>(a.out_lo + base + c) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
+      } else {
+        float* dst = a.out + base;
+#pragma unroll
+        for (int c = 0; c < 32; c += 4)
+          *reinterpret_cast<float4*>(dst + c) =
+              make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
+      }
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -551,12 +572,12 @@ size_t attn_prefill_tc_scratch(int nq, int nkv, int64_t T, int64_t Lk) {
 }
 
 bool attn_prefill_tc_ok(const float* q, int64_t q_ld, const float* kc, const float* vc, int64_t T,
-                        int64_t pos0, int nq, int nkv, int d, const float* out, int64_t out_ld) {
+                        int64_t pos0, int nq, int nkv, int d, const void* out, int64_t out_ld) {
   if (d != kPD || nkv <= 0 || nq % nkv || T <= 0 || pos0 < 0) return false;
   if (pos0 + T > (int64_t(1) << 30) || int64_t(nq) * round_up(T, kQB) > (int64_t(1) << 30) ||
       int64_t(nkv) * round_up(pos0 + T, kKB) > (int64_t(1) << 30))
     return false;
-  if ((reinterpret_cast<uintptr_t>(out) & 15) || out_ld % 4) return false;
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || out_ld % 8) return false;
   (void)q;
   (void)q_ld;
   (void)kc;
@@ -570,9 +591,13 @@ cudaError_t attn_prefill_tc_prepare() {
 
 cudaError_t launch_attn_prefill_tc(const float* q, int64_t q_ld, const float* kc, const float* vc,
                                    int64_t T, int64_t pos0, int nq, int nkv, float scale,
-                                   float* out, int64_t out_ld, void* scratch, size_t scratch_bytes,
-                                   int32_t* err, cudaStream_t s) {
-  if (!attn_prefill_tc_ok(q, q_ld, kc, vc, T, pos0, nq, nkv, kPD, out, out_ld) || !err)
+                                   float* out, uint16_t* out_hi, uint16_t* out_lo, int64_t out_ld,
+                                   void* scratch, size_t scratch_bytes, int32_t* err,
+                                   cudaStream_t s) {
+  const void* dst = out_hi ? static_cast<const void*>(out_hi) : static_cast<const void*>(out);
+  if (!attn_prefill_tc_ok(q, q_ld, kc, vc, T, pos0, nq, nkv, kPD, dst, out_ld) ||
+      !err || (out_hi && ((reinterpret_cast<uintptr_t>(out_lo) & 15) || !out_lo)) ||
+      (!out_hi && !out))
     return cudaErrorInvalidValue;
   const int64_t Lk = pos0 + T;
   const int64_t Tq = round_up(T, kQB), Lkp = round_up(Lk, kKB);
@@ -609,6 +634,8 @@ cudaError_t launch_attn_prefill_tc(const float* q, int64_t q_ld, const float* kc
     return cudaErrorInvalidValue;
   PfArgs a;
   a.out = out;
+  a.out_hi = out_hi;
+  a.out_lo = out_lo;
   a.out_ld = out_ld;
   a.err = err;
   a.T = int(T);

@@ -196,6 +196,10 @@ cudaError_t launch_embed(const uint16_t* embed, const uint32_t* tokens, int64_t 
 // out = rmsnorm rows (mode 0: (v*inv)*w, mode 1: v*(inv*w)).
 cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int64_t n, int64_t rows,
                            int mode, float* out, cudaStream_t s);
+// rms_norm_batch (mode 1) written as the BF16 hi/lo parts of its result
+// (the tcgen05 GEMM's operands) instead of f32.
+cudaError_t launch_rmsnorm_split(const float* x, const float* w, float eps, int64_t n,
+                                 int64_t rows, uint16_t* hi, uint16_t* lo, cudaStream_t s);
 // Rotate q and k of T rows in place (qkv layout) at positions pos0.., and
 // append rotated k and raw v to the cache at pos0...
 cudaError_t launch_rope_append(float* qkv, int64_t qkv_ld, int64_t T, int nq, int nkv, int d,
@@ -214,13 +218,16 @@ cudaError_t launch_attn_prefill(const float* q, int64_t q_ld, const float* kc, c
 // 64: q, k and v^T are split into BF16 parts in `scratch` (at least
 // attn_prefill_tc_scratch bytes) by two kernels before the MMA kernel.
 bool attn_prefill_tc_ok(const float* q, int64_t q_ld, const float* kc, const float* vc, int64_t T,
-                        int64_t pos0, int nq, int nkv, int d, const float* out, int64_t out_ld);
+                        int64_t pos0, int nq, int nkv, int d, const void* out, int64_t out_ld);
 size_t attn_prefill_tc_scratch(int nq, int nkv, int64_t T, int64_t Lk);
 cudaError_t attn_prefill_tc_prepare();
+// out_hi / out_lo (both or neither): the output written as its BF16 hi/lo
+// parts (the O GEMM's operands) instead of f32 into out.
 cudaError_t launch_attn_prefill_tc(const float* q, int64_t q_ld, const float* kc, const float* vc,
                                    int64_t T, int64_t pos0, int nq, int nkv, float scale,
-                                   float* out, int64_t out_ld, void* scratch, size_t scratch_bytes,
-                                   int32_t* err, cudaStream_t s);
+                                   float* out, uint16_t* out_hi, uint16_t* out_lo, int64_t out_ld,
+                                   void* scratch, size_t scratch_bytes, int32_t* err,
+                                   cudaStream_t s);
 // out = gate / (1 + exp(-gate)) * up.
 cudaError_t launch_swiglu(const float* gate, const float* up, int64_t n, float* out,
                           cudaStream_t s);

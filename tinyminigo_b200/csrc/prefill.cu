@@ -5,6 +5,8 @@
 // (src/tensor.rs:1063-1073).
 #include <math.h>
 
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -39,6 +41,30 @@ __global__ void __launch_bounds__(NT) rmsnorm_kernel(const float* __restrict__ x
       const float f = inv * w[k];
       out[r * n + k] = v * f;
     }
+  }
+}
+
+// rmsnorm_kernel's mode 1 (rms_norm_batch) written straight as the next
+// GEMM's BF16 hi/lo operands: the same value v * (inv * w[k]), then hi =
+// bf16(value), lo = bf16(value - hi) as the split kernels compute them.
+template <int NT>
+__global__ void __launch_bounds__(NT) rmsnorm_split_kernel(const float* __restrict__ x,
+                                                           const float* __restrict__ w, float eps,
+                                                           int64_t n, __nv_bfloat16* __restrict__ hi,
+                                                           __nv_bfloat16* __restrict__ lo) {
+  __shared__ float red[NT / 32];
+  const int64_t r = blockIdx.x;
+  const float* xr = x + r * n;
+  float ss = 0.f;
+  for (int64_t k = threadIdx.x; k < n; k += NT) ss = fmaf(xr[k], xr[k], ss);
+  ss = block_sum<NT>(ss, red);
+  const float inv = 1.0f / sqrtf(ss / float(n) + eps);
+  for (int64_t k = threadIdx.x; k < n; k += NT) {
+    const float f = inv * w[k];
+    const float v = xr[k] * f;
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    hi[r * n + k] = h;
+    lo[r * n + k] = __float2bfloat16_rn(v - __bfloat162float(h));
   }
 }
 
@@ -153,6 +179,7 @@ __global__ void step_end_kernel(StreamState st, const float* __restrict__ logits
 cudaError_t prefill_prepare() {
   TMG_CUDA_TRY(set_carveout(embed_kernel));
   TMG_CUDA_TRY(set_carveout(rmsnorm_kernel<256>));
+  TMG_CUDA_TRY(set_carveout(rmsnorm_split_kernel<256>));
   TMG_CUDA_TRY(set_carveout(swiglu_kernel));
   TMG_CUDA_TRY(set_carveout(gemm_simt_kernel));
   TMG_CUDA_TRY(set_carveout(argmax_rows_kernel));
@@ -172,6 +199,14 @@ cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int64_t n,
                            int mode, float* out, cudaStream_t s) {
   if (rows <= 0) return cudaSuccess;
   rmsnorm_kernel<256><<<unsigned(rows), 256, 0, s>>>(x, w, eps, n, mode, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm_split(const float* x, const float* w, float eps, int64_t n,
+                                 int64_t rows, uint16_t* hi, uint16_t* lo, cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  rmsnorm_split_kernel<256><<<unsigned(rows), 256, 0, s>>>(
+      x, w, eps, n, reinterpret_cast<__nv_bfloat16*>(hi), reinterpret_cast<__nv_bfloat16*>(lo));
   return cudaGetLastError();
 }
 
