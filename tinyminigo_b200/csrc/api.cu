@@ -657,15 +657,28 @@ cudaError_t ensure_split(tmg_ctx* c, size_t n) {
 // With parts (out_hi, out_lo) the tensor-core kernel writes the output as
 // the O GEMM's hi/lo operands and *wrote_parts is set; the CUDA-core kernel
 // always writes f32 into out.
-cudaError_t prefill_attention(tmg_ctx* c, const float* q, int64_t q_ld, const float* kc,
-                              const float* vc, int64_t T, int64_t pos0, float scale, float* out,
-                              int64_t out_ld, int nq, int nkv, int d, uint16_t* out_hi = nullptr,
-                              uint16_t* out_lo = nullptr, bool* wrote_parts = nullptr) {
+// TMG_PREFILL_ATTN=simt: the CUDA-core prefill attention instead of the
+// tensor-core one.
+bool prefill_attn_simt() {
   static const bool simt = [] {
     const char* e = std::getenv("TMG_PREFILL_ATTN");
     return e && std::strcmp(e, "simt") == 0;
   }();
+  return simt;
+}
+
+// rope_cos / rope_sin: q holds the chunk's un-rotated projections and the
+// tensor-core path does RoPE and the KV append itself (*roped set); the
+// caller runs launch_rope_append when *roped stays false.
+cudaError_t prefill_attention(tmg_ctx* c, const float* q, int64_t q_ld, const float* kc,
+                              const float* vc, int64_t T, int64_t pos0, float scale, float* out,
+                              int64_t out_ld, int nq, int nkv, int d, uint16_t* out_hi = nullptr,
+                              uint16_t* out_lo = nullptr, bool* wrote_parts = nullptr,
+                              const float* rope_cos = nullptr, const float* rope_sin = nullptr,
+                              bool* roped = nullptr) {
+  const bool simt = prefill_attn_simt();
   if (wrote_parts) *wrote_parts = false;
+  if (roped) *roped = false;
   if (!simt && attn_prefill_tc_ok(q, q_ld, kc, vc, T, pos0, nq, nkv, d, out, out_ld)) {
     const size_t need = attn_prefill_tc_scratch(nq, nkv, T, pos0 + T);
     if (c->pfa_cap < need) {
@@ -679,9 +692,12 @@ cudaError_t prefill_attention(tmg_ctx* c, const float* q, int64_t q_ld, const fl
     }
     const bool parts = out_hi && out_lo;
     if (wrote_parts) *wrote_parts = parts;
+    const bool rope = rope_cos && rope_sin && roped;
+    if (rope) *roped = true;
     return launch_attn_prefill_tc(q, q_ld, kc, vc, T, pos0, nq, nkv, scale, out,
                                   parts ? out_hi : nullptr, parts ? out_lo : nullptr, out_ld,
-                                  c->pfa, c->pfa_cap, c->d_err, c->stream);
+                                  c->pfa, c->pfa_cap, c->d_err, c->stream,
+                                  rope ? rope_cos : nullptr, rope ? rope_sin : nullptr);
   }
   return launch_attn_prefill(q, q_ld, kc, vc, T, pos0, nq, nkv, d, scale, out, out_ld, c->stream);
 }
@@ -1039,19 +1055,27 @@ int forward_seq(tmg_ctx* c, tmg_kv* kv, int stream, const uint32_t* tokens, int6
                       c->qkv_rows, false),
            "gemm qkv");
       }
-      CK(launch_rope_append(c->QKV, c->qkv_rows, Tc, c->nq, c->nkv, c->d, kv->rope_cos,
-                            kv->rope_sin, pos0, kc, vc, c->stream),
-         "rope");
       // the attention output straight as the O GEMM's hi/lo operands when
-      // that GEMM runs on the tensor cores
+      // that GEMM runs on the tensor cores; RoPE and the KV append inside
+      // the tensor-core attention's first pass (else rope_append first)
       const int64_t qd = int64_t(c->nq) * c->d;
       const bool o_parts = !tp && !c->i8 && gemm_tc_supported(qd, Lw.wo) &&
                            ensure_split(c, size_t(Tc) * std::max<int64_t>(qd, c->h)) == cudaSuccess;
-      bool att_parts = false;
+      bool att_parts = false, roped = false;
+      const bool tc_attn = attn_prefill_tc_ok(c->QKV, c->qkv_rows, kc, vc, Tc, pos0, c->nq, c->nkv,
+                                              c->d, c->ATT, qd) &&
+                           !prefill_attn_simt();
+      if (!tc_attn)
+        CK(launch_rope_append(c->QKV, c->qkv_rows, Tc, c->nq, c->nkv, c->d, kv->rope_cos,
+                              kv->rope_sin, pos0, kc, vc, c->stream),
+           "rope");
       CK(prefill_attention(c, c->QKV, c->qkv_rows, kc, vc, Tc, pos0, scale, c->ATT, qd, c->nq,
                            c->nkv, c->d, o_parts ? c->sp_hi : nullptr,
-                           o_parts ? c->sp_lo : nullptr, &att_parts),
+                           o_parts ? c->sp_lo : nullptr, &att_parts,
+                           tc_attn ? kv->rope_cos : nullptr, tc_attn ? kv->rope_sin : nullptr,
+                           &roped),
          "attention");
+      if (tc_attn && !roped) return fail(c, TMG_ERR_CUDA, "prefill attention: RoPE not applied");
       if (att_parts) {
         CK(launch_gemm_tc(c->sp_hi, c->sp_lo, Lw.wo, Tc, c->h, qd, c->X, c->h, true, c->d_err,
                           c->stream),

@@ -507,15 +507,18 @@ __global__ void attn_pf_split_q_kernel(const float* __restrict__ q, int64_t q_ld
 // [n_kv][Lkp][64]; v split in two and transposed into [n_kv][64][Lkp]
 // (keys Lk..Lkp-1 zero).  Grid (Lkp / 64, n_kv), 256 threads: one 64-key
 // block per CTA.
+// Keys at or past `kend` are left alone (attn_pf_prep_kernel writes them).
 __global__ void attn_pf_split_kv_kernel(const float* __restrict__ kc, const float* __restrict__ vc,
-                                        int64_t kvd, int Lk, int Lkp, uint16_t* __restrict__ khi,
-                                        uint16_t* __restrict__ kmid, uint16_t* __restrict__ klo,
-                                        uint16_t* __restrict__ vhi, uint16_t* __restrict__ vlo) {
+                                        int64_t kvd, int Lk, int Lkp, int kend,
+                                        uint16_t* __restrict__ khi, uint16_t* __restrict__ kmid,
+                                        uint16_t* __restrict__ klo, uint16_t* __restrict__ vhi,
+                                        uint16_t* __restrict__ vlo) {
   __shared__ float vs[kKB][kPD + 1];
   const int kvh = blockIdx.y, key0 = blockIdx.x * kKB;
   for (int i = threadIdx.x; i < kKB * kPD; i += blockDim.x) {
     const int kk = i / kPD, c = i % kPD;
     const int key = key0 + kk;
+    if (key >= kend) continue;
     const bool in = key < Lk;
     const float kx = in ? kc[int64_t(key) * kvd + int64_t(kvh) * kPD + c] : 0.f;
     vs[kk][c] = in ? vc[int64_t(key) * kvd + int64_t(kvh) * kPD + c] : 0.f;
@@ -525,11 +528,96 @@ __global__ void attn_pf_split_kv_kernel(const float* __restrict__ kc, const floa
   __syncthreads();
   for (int i = threadIdx.x; i < kKB * kPD; i += blockDim.x) {
     const int c = i / kKB, kk = i % kKB;
+    if (key0 + kk >= kend) continue;
     const float v = vs[kk][c];
     const __nv_bfloat16 hb = __float2bfloat16_rn(v);
     const int64_t o = (int64_t(kvh) * kPD + c) * Lkp + key0 + kk;
     vhi[o] = __bfloat16_as_ushort(hb);
     vlo[o] = __bfloat16_as_ushort(__float2bfloat16_rn(v - __bfloat162float(hb)));
+  }
+}
+
+// RoPE with the reference's rounding (each product rounded, then the sum),
+// as the decode kernels apply it.
+__device__ __forceinline__ void rot_pf(float a, float b, float c, float s, float* o0, float* o1) {
+  const float ac = __fmul_rn(a, c), bs = __fmul_rn(b, s), as = __fmul_rn(a, s), bc = __fmul_rn(b, c);
+  *o0 = __fsub_rn(ac, bs);
+  *o1 = __fadd_rn(as, bc);
+}
+
+// The new rows of a prefill chunk in one pass over the projections
+// (src/model.rs:533-553): RoPE of q and k at pos0 + t, k and v appended to
+// the cache, and the attention's operand parts: q (times qs) three ways
+// into [n_q][Tq][64] (rows T..Tq-1 zero), k three ways into [n_kv][Lkp][64]
+// and v two ways transposed into [n_kv][64][Lkp] for keys pos0 .. Lkp-1
+// (keys past pos0 + T zero).  Grid (row blocks of 64, n_q + n_kv), 256
+// threads: a q head's rows, or a kv head's keys.
+__global__ void attn_pf_prep_kernel(const float* __restrict__ qkv, int64_t ld, int nq, int nkv,
+                                    int T, int64_t pos0, int Tq, int Lkp,
+                                    const float* __restrict__ cs, const float* __restrict__ sn,
+                                    float qs, float* __restrict__ kc, float* __restrict__ vc,
+                                    uint16_t* __restrict__ qh, uint16_t* __restrict__ qm,
+                                    uint16_t* __restrict__ ql, uint16_t* __restrict__ kh,
+                                    uint16_t* __restrict__ km, uint16_t* __restrict__ kl,
+                                    uint16_t* __restrict__ vh, uint16_t* __restrict__ vl) {
+  __shared__ float vs[kKB][kPD + 1];
+  constexpr int half = kPD / 2;
+  const int hs = blockIdx.y, t0 = blockIdx.x * kKB;
+  const int64_t kvd = int64_t(nkv) * kPD;
+  if (hs < nq) {
+    if (t0 >= Tq) return;
+    for (int i = threadIdx.x; i < kKB * half; i += blockDim.x) {
+      const int tt = i / half, j = i % half, t = t0 + tt;
+      float o0 = 0.f, o1 = 0.f;
+      if (t < T) {
+        const float* v = qkv + int64_t(t) * ld + int64_t(hs) * kPD;
+        const int64_t pos = pos0 + t;
+        rot_pf(v[j], v[j + half], cs[pos * half + j], sn[pos * half + j], &o0, &o1);
+      }
+      const int64_t o = (int64_t(hs) * Tq + t) * kPD;
+      split3(o0 * qs, qh + o + j, qm + o + j, ql + o + j);
+      split3(o1 * qs, qh + o + j + half, qm + o + j + half, ql + o + j + half);
+    }
+    return;
+  }
+  const int kvh = hs - nq;
+  const int64_t key0 = pos0 + t0;
+  if (key0 >= Lkp) return;
+  for (int i = threadIdx.x; i < kKB * half; i += blockDim.x) {
+    const int tt = i / half, j = i % half, t = t0 + tt;
+    const int64_t key = key0 + tt;
+    if (key >= Lkp) continue;
+    float o0 = 0.f, o1 = 0.f, v0 = 0.f, v1 = 0.f;
+    if (t < T) {
+      const float* row = qkv + int64_t(t) * ld;
+      const float* kv = row + int64_t(nq + kvh) * kPD;
+      rot_pf(kv[j], kv[j + half], cs[key * half + j], sn[key * half + j], &o0, &o1);
+      const float* vv = row + int64_t(nq + nkv + kvh) * kPD;
+      v0 = vv[j];
+      v1 = vv[j + half];
+      float* kd = kc + key * kvd + int64_t(kvh) * kPD;
+      float* vd = vc + key * kvd + int64_t(kvh) * kPD;
+      kd[j] = o0;
+      kd[j + half] = o1;
+      vd[j] = v0;
+      vd[j + half] = v1;
+    }
+    const int64_t o = (int64_t(kvh) * Lkp + key) * kPD;
+    split3(o0, kh + o + j, km + o + j, kl + o + j);
+    split3(o1, kh + o + j + half, km + o + j + half, kl + o + j + half);
+    vs[tt][j] = v0;
+    vs[tt][j + half] = v1;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < kKB * kPD; i += blockDim.x) {
+    const int c = i / kKB, tt = i % kKB;
+    const int64_t key = key0 + tt;
+    if (key >= Lkp) continue;
+    const float v = vs[tt][c];
+    const __nv_bfloat16 hb = __float2bfloat16_rn(v);
+    const int64_t o = (int64_t(kvh) * kPD + c) * Lkp + key;
+    vh[o] = __bfloat16_as_ushort(hb);
+    vl[o] = __bfloat16_as_ushort(__float2bfloat16_rn(v - __bfloat162float(hb)));
   }
 }
 
@@ -593,7 +681,7 @@ cudaError_t launch_attn_prefill_tc(const float* q, int64_t q_ld, const float* kc
                                    int64_t T, int64_t pos0, int nq, int nkv, float scale,
                                    float* out, uint16_t* out_hi, uint16_t* out_lo, int64_t out_ld,
                                    void* scratch, size_t scratch_bytes, int32_t* err,
-                                   cudaStream_t s) {
+                                   cudaStream_t s, const float* rope_cos, const float* rope_sin) {
   const void* dst = out_hi ? static_cast<const void*>(out_hi) : static_cast<const void*>(out);
   if (!attn_prefill_tc_ok(q, q_ld, kc, vc, T, pos0, nq, nkv, kPD, dst, out_ld) ||
       !err || (out_hi && ((reinterpret_cast<uintptr_t>(out_lo) & 15) || !out_lo)) ||
@@ -616,12 +704,29 @@ cudaError_t launch_attn_prefill_tc(const float* q, int64_t q_ld, const float* kc
   uint16_t *vh = take(nke), *vl = take(nke);
   if (p > reinterpret_cast<uint8_t*>(scratch) + scratch_bytes) return cudaErrorInvalidValue;
   const int64_t kvd = int64_t(nkv) * kPD;
-  attn_pf_split_q_kernel<<<dim3(unsigned(Tq / 4), unsigned(nq)), 256, 0, s>>>(
-      q, q_ld, int(T), int(Tq), scale * kLog2ePf, qh, qm, ql);
-  TMG_CUDA_TRY(cudaGetLastError());
-  attn_pf_split_kv_kernel<<<dim3(unsigned(Lkp / kKB), unsigned(nkv)), 256, 0, s>>>(
-      kc, vc, kvd, int(Lk), int(Lkp), kh, km, kl, vh, vl);
-  TMG_CUDA_TRY(cudaGetLastError());
+  if (rope_cos) {
+    // q, k, v of the chunk's rows un-rotated in q (rows of q_ld: q | k | v):
+    // one pass rotates, appends to the cache and writes their parts; the
+    // older cache rows [0, pos0) are split from the cache
+    if (pos0 > 0) {
+      attn_pf_split_kv_kernel<<<dim3(unsigned((pos0 + kKB - 1) / kKB), unsigned(nkv)), 256, 0, s>>>(
+          kc, vc, kvd, int(Lk), int(Lkp), int(pos0), kh, km, kl, vh, vl);
+      TMG_CUDA_TRY(cudaGetLastError());
+    }
+    const int64_t rows = std::max<int64_t>(Tq, Lkp - pos0);
+    attn_pf_prep_kernel<<<dim3(unsigned((rows + kKB - 1) / kKB), unsigned(nq + nkv)), 256, 0, s>>>(
+        q, q_ld, nq, nkv, int(T), pos0, int(Tq), int(Lkp), rope_cos, rope_sin,
+        scale * kLog2ePf, const_cast<float*>(kc), const_cast<float*>(vc), qh, qm, ql, kh, km, kl,
+        vh, vl);
+    TMG_CUDA_TRY(cudaGetLastError());
+  } else {
+    attn_pf_split_q_kernel<<<dim3(unsigned(Tq / 4), unsigned(nq)), 256, 0, s>>>(
+        q, q_ld, int(T), int(Tq), scale * kLog2ePf, qh, qm, ql);
+    TMG_CUDA_TRY(cudaGetLastError());
+    attn_pf_split_kv_kernel<<<dim3(unsigned(Lkp / kKB), unsigned(nkv)), 256, 0, s>>>(
+        kc, vc, kvd, int(Lk), int(Lkp), int(Lkp), kh, km, kl, vh, vl);
+    TMG_CUDA_TRY(cudaGetLastError());
+  }
   CUtensorMap mqh, mqm, mql, mkh, mkm, mkl, mvh, mvl;
   if (!map_bf16(&mqh, qh, int64_t(nq) * Tq, kPD, kQB) ||
       !map_bf16(&mqm, qm, int64_t(nq) * Tq, kPD, kQB) ||

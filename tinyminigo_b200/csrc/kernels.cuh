@@ -222,12 +222,16 @@ bool attn_prefill_tc_ok(const float* q, int64_t q_ld, const float* kc, const flo
 size_t attn_prefill_tc_scratch(int nq, int nkv, int64_t T, int64_t Lk);
 cudaError_t attn_prefill_tc_prepare();
 // out_hi / out_lo (both or neither): the output written as its BF16 hi/lo
-// parts (the O GEMM's operands) instead of f32 into out.
+// parts (the O GEMM's operands) instead of f32 into out.  With rope_cos /
+// rope_sin, q points at the chunk's un-rotated projections (rows of q_ld:
+// q | k | v): RoPE, the KV append to kc / vc and the operand parts are done
+// in one pass (launch_rope_append is then not needed).
 cudaError_t launch_attn_prefill_tc(const float* q, int64_t q_ld, const float* kc, const float* vc,
                                    int64_t T, int64_t pos0, int nq, int nkv, float scale,
                                    float* out, uint16_t* out_hi, uint16_t* out_lo, int64_t out_ld,
                                    void* scratch, size_t scratch_bytes, int32_t* err,
-                                   cudaStream_t s);
+                                   cudaStream_t s, const float* rope_cos = nullptr,
+                                   const float* rope_sin = nullptr);
 // out = gate / (1 + exp(-gate)) * up.
 cudaError_t launch_swiglu(const float* gate, const float* up, int64_t n, float* out,
                           cudaStream_t s);
