@@ -66,8 +66,7 @@ constexpr int kOffP = kOffV + kVStages * kVStage;      // 152 KB; P[2] x {hi, lo
 constexpr int kOffBar = kOffP + 2 * 2 * kPPart;        // 216 KB
 constexpr int kSmemPf = kOffBar + 256 + 1024;          // + barriers + alignment slack
 constexpr int kPfThreads = 320;  // producer, MMA, 8 softmax warps
-constexpr int kOBufs = 3;              // O_j buffers: O_{j-2} is folded while S_j is read
-constexpr uint32_t kPfTmemCols = 512;  // S[2] at 0, 64; O[3] at 128, 192, 256
+constexpr uint32_t kPfTmemCols = 256;  // S[2] at 0, 64; O[2] at 128, 192
 // kind::f16: BF16 x BF16 -> F32, both K-major, M = 128, N = 64.
 constexpr uint32_t kIdescPf =
     (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(64 >> 3) << 17) | (uint32_t(128 >> 4) << 24);
@@ -108,10 +107,9 @@ __device__ __forceinline__ void commit(uint64_t* bar) {
                : "memory");
 }
 
-// 32 consecutive TMEM columns of this warp's 32 lanes (one row per thread),
-// without the wait (several loads, then one tmem_wait_ld).
-__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, float* v) {
-  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+// 32 consecutive TMEM columns of this warp's 32 lanes (one row per thread).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
 #pragma unroll
   for (int c = 0; c < 32; c += 16)
     asm volatile(
@@ -122,9 +120,9 @@ __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, float* v) {
           "=r"(r[c + 10]), "=r"(r[c + 11]), "=r"(r[c + 12]), "=r"(r[c + 13]), "=r"(r[c + 14]),
           "=r"(r[c + 15])
         : "r"(taddr + uint32_t(c)));
-}
-__device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // Barrier `id` (1..15) among `n` threads (whole warps).
@@ -190,9 +188,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint64_t* qfull = vempty + kVStages;                             // q parts loaded
   uint64_t* s_full = qfull + 1;                                  // [2] S_j in TMEM
   uint64_t* p_full = s_full + 2;                                 // [2] P_j in smem (S_j read)
-  uint64_t* o_full = p_full + 2;                                 // [3] O_j in TMEM
-  uint64_t* o_free = o_full + kOBufs;                            // [3] O_j read
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + kOBufs);
+  uint64_t* o_full = p_full + 2;                                 // [2] O_j in TMEM
+  uint64_t* o_free = o_full + 2;                                 // [2] O_j read
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 2);
   __shared__ volatile int failed;
   __shared__ float red_mx[2][2][kQB];  // [block parity][half][row]: a half's max of the block
   __shared__ float red_l[2][kQB];      // [half][row]: a half's share of the row's sum
@@ -217,8 +215,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&p_full[b], 8);
-    }
-    for (int b = 0; b < kOBufs; ++b) {
       mbar_init(&o_full[b], 1);
       mbar_init(&o_free[b], 8);
     }
@@ -301,12 +297,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           commit(&kempty[s]);  // k stage s is free once these MMAs have read it
         }
         if (j >= 1) {
-          // O_i = P_i V_i for i = j - 1 into O buffer i % 3 (its previous
-          // user, O_{i-3}, folded)
-          const int i = j - 1, b = i & 1, ob = i % kOBufs;
+          // O_i = P_i V_i for i = j - 1 into O buffer i & 1
+          const int i = j - 1, b = i & 1;
           const int s = i % kVStages;
           if (failed || !mbar_wait(&p_full[b], (i >> 1) & 1) ||
-              (i >= kOBufs && !mbar_wait(&o_free[ob], ((i - kOBufs) / kOBufs) & 1)) ||
+              (i >= 2 && !mbar_wait(&o_free[b], ((i - 2) >> 1) & 1)) ||
               !mbar_wait(&vfull[s], (i / kVStages) & 1)) {
             ok = false;
             break;
@@ -316,7 +311,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           const uint32_t vh = vb, vl = vb + kVPart;
           const uint32_t pb = smem_u32(sm + kOffP + b * 2 * kPPart);
           const uint32_t ph = pb, pl = pb + kPPart;
-          const uint32_t to = tmem + 128u + uint32_t(ob * 64);
+          const uint32_t to = tmem + 128u + uint32_t(b * 64);
 #pragma unroll
           for (int k = 0; k < kKB / 16; ++k) {
             const uint32_t o = uint32_t(k * 32);
@@ -324,7 +319,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             mma(to, sdesc(ph + o), sdesc(vl + o), 1);
             mma(to, sdesc(pl + o), sdesc(vh + o), 1);
           }
-          commit(&o_full[ob]);
+          commit(&o_full[b]);
           commit(&vempty[s]);  // v stage s is free once these MMAs have read it
         }
       }
@@ -350,31 +345,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     float o[32];
 #pragma unroll
     for (int c = 0; c < 32; ++c) o[c] = 0.f;
-    // alpha_j rescales the sum through block j-1 to block j's max; O_i is
-    // folded two blocks behind (o = o * alpha_i + O_i), together with S_j's
-    // load, so one TMEM wait covers both
-    float m = -INFINITY, l = 0.f, alpha_m1 = 0.f, alpha_m2 = 0.f;
+    float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
     bool ok = true;
     // A failed wait does not leave the loop on its own: the pair's barrier
     // below ANDs both threads' status, so both leave at the same block and
     // every barrier of the pair is met.
     for (int j = 0; j < nb; ++j) {
       const int b = j & 1;
-      const int fi = j - 2, fb = fi >= 0 ? fi % kOBufs : 0;  // the block folded now
-      bool got = mbar_wait(&s_full[b], (j >> 1) & 1);
-      if (fi >= 0) got = mbar_wait(&o_full[fb], (fi / kOBufs) & 1) && got;
+      const bool got = mbar_wait(&s_full[b], (j >> 1) & 1);
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      float sv[32], ob[32];
-      tmem_ld32_nowait(tmem + lanes + uint32_t(b * 64) + cofs, sv);
-      if (fi >= 0) tmem_ld32_nowait(tmem + lanes + 128u + uint32_t(fb * 64) + cofs, ob);
-      tmem_wait_ld();
-      if (fi >= 0) {
-#pragma unroll
-        for (int c = 0; c < 32; ++c) o[c] = fmaf(o[c], alpha_m2, ob[c]);
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&o_free[fb]);
-      }
+      float sv[32];
+      tmem_ld32(tmem + lanes + uint32_t(b * 64) + cofs, sv);
       const int64_t k0 = int64_t(j) * kKB + hf * 32;
       // only blocks that reach past the first row's position or past the
       // keys need the mask (the same for every row of the CTA)
@@ -397,7 +378,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       // P_j (row r, this half's 32 keys) into P buffer b: BF16 hi and lo,
       // 16-byte chunk e of the 128-byte row at chunk e ^ (r & 7) (the
       // 128-byte swizzle).  The buffer was last read by PV_{j-2}, which
-      // completed before O_{j-2} was folded above.
+      // completed before O_{j-2} was folded.
       uint8_t* prow_h = sm + kOffP + b * 2 * kPPart + r * 128;
       uint8_t* prow_l = prow_h + kPPart;
 #pragma unroll
@@ -427,23 +408,31 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[b]);
-      alpha_m2 = alpha_m1;
-      alpha_m1 = alpha;
-    }
-    // the last two blocks' O (fewer when nb < 2)
-    for (int fi = (nb >= 2 ? nb - 2 : 0); fi < nb && ok; ++fi) {
-      const int fb = fi % kOBufs;
-      if (!mbar_wait(&o_full[fb], (fi / kOBufs) & 1)) {
-        ok = false;
-        break;
-      }
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      float ob[32];
-      tmem_ld32_nowait(tmem + lanes + 128u + uint32_t(fb * 64) + cofs, ob);
-      tmem_wait_ld();
-      const float al = fi == nb - 1 ? alpha_m1 : alpha_m2;
+      if (j >= 1) {
+        const int i = j - 1, bi = i & 1;
+        if (!mbar_wait(&o_full[bi], (i >> 1) & 1)) ok = false;  // leaves at the next barrier
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        float ob[32];
+        tmem_ld32(tmem + lanes + 128u + uint32_t(bi * 64) + cofs, ob);
 #pragma unroll
-      for (int c = 0; c < 32; ++c) o[c] = fmaf(o[c], al, ob[c]);
+        for (int c = 0; c < 32; ++c) o[c] = fmaf(o[c], alpha_prev, ob[c]);
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&o_free[bi]);
+      }
+      alpha_prev = alpha;
+    }
+    if (ok) {
+      const int i = nb - 1, bi = i & 1;
+      if (!mbar_wait(&o_full[bi], (i >> 1) & 1)) {
+        ok = false;
+      } else {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        float ob[32];
+        tmem_ld32(tmem + lanes + 128u + uint32_t(bi * 64) + cofs, ob);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) o[c] = fmaf(o[c], alpha_prev, ob[c]);
+      }
     }
     // the row's sum: this thread's share and its partner's (every thread
     // reaches this barrier, also after a failed wait)
