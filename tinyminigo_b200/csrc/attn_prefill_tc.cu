@@ -364,9 +364,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         for (int c = 0; c < 32; ++c)
           if (k0 + c > tq || k0 + c >= a.Lk) sv[c] = -INFINITY;
       }
-      float lmx = sv[0];
+      // four independent chains (max is exact in any order)
+      float mx4[4] = {sv[0], sv[1], sv[2], sv[3]};
 #pragma unroll
-      for (int c = 1; c < 32; ++c) lmx = fmaxf(lmx, sv[c]);
+      for (int c = 4; c < 32; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
+      const float lmx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       red_mx[b][hf][r] = lmx;
       if (!bar_and(2 + qd, 64, ok && got)) {
         ok = false;
@@ -374,7 +376,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
       const float mx = fmaxf(m, fmaxf(lmx, red_mx[b][hf ^ 1][r]));
       const float alpha = m == -INFINITY ? 0.f : ex2f(m - mx);
-      float sum = 0.f;
+      // mx is finite (key 0 is visible to every row), so a masked score
+      // gives ex2(-inf) = 0 without a test; the sum in four chains
+      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
       // P_j (row r, this half's 32 keys) into P buffer b: BF16 hi and lo,
       // 16-byte chunk e of the 128-byte row at chunk e ^ (r & 7) (the
       // 128-byte swizzle).  The buffer was last read by PV_{j-2}, which
@@ -386,11 +390,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         uint32_t hw[4], lw[4];
 #pragma unroll
         for (int t = 0; t < 8; t += 2) {
-          const float x0 = sv[8 * e + t], x1 = sv[8 * e + t + 1];
-          const float p0 = x0 == -INFINITY ? 0.f : ex2f(x0 - mx);
-          const float p1 = x1 == -INFINITY ? 0.f : ex2f(x1 - mx);
-          sum += p0;
-          sum += p1;
+          const float p0 = ex2f(sv[8 * e + t] - mx);
+          const float p1 = ex2f(sv[8 * e + t + 1] - mx);
+          sum4[t >> 1] += p0;
+          sum4[t >> 1] += p1;
           const uint32_t hb = bf16x2_bits(p0, p1);
           const float r0 = p0 - __uint_as_float(hb << 16);
           const float r1 = p1 - __uint_as_float(hb & 0xffff0000u);
@@ -401,7 +404,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         *reinterpret_cast<uint4*>(prow_h + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
         *reinterpret_cast<uint4*>(prow_l + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
       }
-      l = l * alpha + sum;
+      l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
       m = mx;
       // the P writes (generic proxy) before the MMA (async proxy) reads them
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
