@@ -295,10 +295,8 @@ struct Shared {
   unsigned long long poll_ns;  // limit of one tag poll
   int gid, gn;                 // this CTA in the grid of all ranks, and its size
   int world;                   // GPUs of that grid (1: this one alone)
-  unsigned long long* ll_base;    // this rank's exchange words and partials ...
-  unsigned long long* part_base;
+  unsigned long long* ll_base;    // this rank's exchange words ...
   unsigned long long* ll_peer[kMaxGroupRanks];    // ... and every rank's (by rank)
-  unsigned long long* part_peer[kMaxGroupRanks];
   int gen_ok;
   volatile int abort;      // stop issuing / waiting (error or early end)
   volatile int issued;     // producer: stages issued so far
@@ -521,7 +519,11 @@ __device__ void producer(const FusedArgs& a, const FusedLayer* layers, Shared& S
 // chain of phases that needs every CTA to have finished reading it (every
 // CTA owns groups in every GEMV phase), so a reader never misses its tag.
 // On several GPUs the writer stores each word into every rank's copy (peer
-// stores over NVLink, system scope) and readers poll their own copy.
+// stores over NVLink, system scope) and readers poll their own copy, except
+// for the attention: every rank runs all attention items of a layer itself
+// (it holds all of q/k/v and the whole cache), so the partials and the
+// attention output stay in its own memory and two of a layer's hops never
+// cross GPUs.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void st_tag(unsigned long long* p, unsigned long long w, bool sys) {
   if (sys) asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
@@ -541,20 +543,18 @@ __device__ __forceinline__ void ll_store(const Shared& S, unsigned long long* p,
   const size_t o = size_t(p - S.ll_base);
   for (int r = 0; r < S.world; ++r) st_tag(S.ll_peer[r] + o, w, true);
 }
-// The same for a word of the attention partials.
-__device__ __forceinline__ void part_store(const Shared& S, unsigned long long* p, float v,
-                                           uint32_t tag) {
-  const unsigned long long w = tag_word(v, tag);
-  if (!kGroup) {
-    st_tag(p, w, false);
-    return;
-  }
-  const size_t o = size_t(p - S.part_base);
-  for (int r = 0; r < S.world; ++r) st_tag(S.part_peer[r] + o, w, true);
-}
 __device__ __forceinline__ void ll_store_rep(const Shared& S, unsigned long long* base, int n,
                                              int rep, int r, float v, uint32_t tag) {
   for (int c = 0; c < rep; ++c) ll_store(S, base + size_t(c) * n + r, v, tag);
+}
+// This rank's copy only: the attention partials and outputs (in a group
+// every rank runs all attention items itself, so they never cross GPUs).
+__device__ __forceinline__ void ll_store_local(unsigned long long* p, float v, uint32_t tag) {
+  st_tag(p, tag_word(v, tag), false);
+}
+__device__ __forceinline__ void ll_store_rep_local(unsigned long long* base, int n, int rep, int r,
+                                                   float v, uint32_t tag) {
+  for (int c = 0; c < rep; ++c) ll_store_local(base + size_t(c) * n + r, v, tag);
 }
 __device__ __forceinline__ ulonglong2 ll_load2(const unsigned long long* p, bool sys) {
   ulonglong2 r;
@@ -1229,7 +1229,7 @@ __device__ __forceinline__ bool attn_item(const AttnArgs a, int kvh, int split, 
       const int idx = tid + r * kCThreads;
       if (idx < G * D) {
         const float l = S.l_s[idx / D];
-        ll_store_rep(S, a.att_ll, a.nq * D, a.rep, kvh * G * D + idx, l > 0.f ? o_acc[r] / l : 0.f,
+        ll_store_rep_local(a.att_ll, a.nq * D, a.rep, kvh * G * D + idx, l > 0.f ? o_acc[r] / l : 0.f,
                      tag_att);
       }
     }
@@ -1238,11 +1238,11 @@ __device__ __forceinline__ bool attn_item(const AttnArgs a, int kvh, int split, 
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const int idx = tid + r * kCThreads;
-      if (idx < G * D) part_store(S, part + (idx / D) * (D + 2) + 2 + (idx % D), o_acc[r], tag_att);
+      if (idx < G * D) ll_store_local(part + (idx / D) * (D + 2) + 2 + (idx % D), o_acc[r], tag_att);
     }
     if (tid < G) {
-      part_store(S, part + tid * (D + 2), S.m_s[tid], tag_att);
-      part_store(S, part + tid * (D + 2) + 1, S.l_s[tid], tag_att);
+      ll_store_local(part + tid * (D + 2), S.m_s[tid], tag_att);
+      ll_store_local(part + tid * (D + 2) + 1, S.l_s[tid], tag_att);
     }
   }
   if (tp && tid == 0) tp[8] = global_ns();
@@ -1280,7 +1280,8 @@ __device__ __forceinline__ bool merge_head(const AttnArgs a, int kvh, int n_used
     float acc = 0.f;
     for (int s = 0; s < n_used; ++s) acc = fmaf(P[s * rec + g * (D + 2) + 2 + j], wv[g * n_used + s], acc);
     const float L = Ls[g];
-    ll_store_rep(S, a.att_ll, a.nq * D, a.rep, kvh * G * D + idx, L > 0.f ? acc / L : 0.f, tag_att);
+    ll_store_rep_local(a.att_ll, a.nq * D, a.rep, kvh * G * D + idx, L > 0.f ? acc / L : 0.f,
+                       tag_att);
   }
   csync();
   return true;
@@ -1325,11 +1326,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
     S.gid = a.rank * int(gridDim.x) + int(blockIdx.x);
     S.gn = a.world * int(gridDim.x);
     S.ll_base = a.ll_base;
-    S.part_base = a.part_ll;
-    for (int r = 0; r < kMaxGroupRanks; ++r) {
-      S.ll_peer[r] = a.ll_peer[r];
-      S.part_peer[r] = a.part_peer[r];
-    }
+    for (int r = 0; r < kMaxGroupRanks; ++r) S.ll_peer[r] = a.ll_peer[r];
     mbar_fence_init();
   }
   __syncthreads();
@@ -1397,13 +1394,13 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
         aa.nkv = a.nkv;
         aa.nsplit = a.nsplit;
         aa.scale = a.scale;
-        for (int item = cta_gid(S); item < a.nkv * n_used && ok; item += cta_gn(S))
+        for (int item = int(blockIdx.x); item < a.nkv * n_used && ok; item += int(gridDim.x))
           ok = attn_item<D>(aa, item / n_used, item % n_used, chunk, n_ctx, pos, append, n_used,
-                            tag - 1u, tag, asm_, S, gc, item == cta_gid(S) ? tp : nullptr,
-                            item == cta_gid(S));
+                            tag - 1u, tag, asm_, S, gc, item == int(blockIdx.x) ? tp : nullptr,
+                            item == int(blockIdx.x));
         if (tp && threadIdx.x == 0) tp[5] = global_ns();
         if (n_used > 1)
-          for (int item = cta_gid(S); item < a.nkv * n_used && ok; item += cta_gn(S))
+          for (int item = int(blockIdx.x); item < a.nkv * n_used && ok; item += int(gridDim.x))
             if (item % n_used == 0) ok = merge_head<D>(aa, item / n_used, n_used, tag, asm_, S, gc);
         if (tp && threadIdx.x == 0) tp[6] = global_ns();
         if (!ok) raise_abort(a);
@@ -1496,8 +1493,8 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const FusedA
       // the cache rows of this CTA's first attention item of the layer start
       // loading now (the region is free until the attention phase; no
       // cp.async wait comes before attn_item's)
-      if (ph == PH_QKV && cta_gid(S) < a.nkv * n_used) {
-        const int item = cta_gid(S);
+      if (ph == PH_QKV && int(blockIdx.x) < a.nkv * n_used) {
+        const int item = int(blockIdx.x);
         attn_prefetch<D>(layers_s[l].kc, layers_s[l].vc, a.nkv, a.nq / a.nkv, item / n_used,
                          item % n_used, chunk, n_ctx, append ? pos : n_ctx, asm_);
       }
