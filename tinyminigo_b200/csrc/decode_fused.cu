@@ -38,6 +38,11 @@
 // the rotation and the KV append happen in the QKV epilogue.
 // All arithmetic is f32 with BF16 weights widened exactly, as in the
 // separate kernels.
+// Compiled twice: for one GPU (this file) and for a group of GPUs
+// (decode_fused_group.cu, TMG_FUSED_GROUP = 1), where the CTAs of every rank
+// form one grid for the GEMV phases, exchanged words and KV appends are
+// stored into every rank's memory over NVLink, and each rank runs all
+// attention items itself.
 #include <math.h>
 
 #include "common.cuh"
