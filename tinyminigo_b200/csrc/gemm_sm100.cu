@@ -464,6 +464,7 @@ cudaError_t launch_swiglu_split(const float* g, const float* u, int64_t n, uint1
   return cudaGetLastError();
 }
 
+namespace {
 // Tile width for N columns over `rows_tiles` 128-row blocks on num_sms SMs:
 // the widest of 256, 192, 128 (multiples of 16 the MMA takes) whose tiles
 // fill the last round of the persistent grid best.
@@ -482,6 +483,7 @@ int pick_bn(int64_t N, int64_t m_tiles, int num_sms) {
   }
   return best;
 }
+}  // namespace
 
 cudaError_t launch_gemm_tc2(const uint16_t* x_hi, const uint16_t* x_lo, const uint16_t* w1,
                             int64_t N1, float* y1, int64_t ldy1, const uint16_t* w2, int64_t N2,
