@@ -465,7 +465,7 @@ cudaError_t launch_swiglu_split(const float* g, const float* u, int64_t n, uint1
 }
 
 namespace {
-// Tile width for N columns over `rows_tiles` 128-row blocks on num_sms SMs:
+// Tile width for N columns over m_tiles 128-row blocks on num_sms SMs:
 // the widest of 256, 192, 128 (multiples of 16 the MMA takes) whose tiles
 // fill the last round of the persistent grid best.
 int pick_bn(int64_t N, int64_t m_tiles, int num_sms) {
