@@ -144,3 +144,21 @@ def test_rng_uniforms_match_oracle_restatement(orc):
         assert np.array_equal(rng_uniforms(seed, 100), orc.stdrng_uniforms(seed, 100))
     u = rng_uniforms(7, 10000)
     assert u.min() >= 0 and u.max() < 1 and len(set(u.tolist())) > 9990
+
+
+def test_entry_points_refuse_bad_arguments_before_any_device_call():
+    # argument errors come back as TMG_ERR_INVALID (-1) without touching a
+    # GPU: a null context or cache, a group of one rank or of more than 8,
+    # a rank outside the group
+    import ctypes
+
+    from tinyminigo_b200._lib import lib
+
+    uid = (ctypes.c_uint8 * 128)()
+    L = lib()
+    assert L.tmg_fused_group_init(None, None, uid, 0, 2) == -1
+    assert L.tmg_fused_group_init(None, None, None, 0, 2) == -1
+    assert L.tmg_fused_group_init(None, None, uid, 0, 1) == -1
+    assert L.tmg_fused_group_init(None, None, uid, 2, 2) == -1
+    assert L.tmg_fused_group_init(None, None, uid, 0, 9) == -1
+    assert L.tmg_op_attn_prefill(None, None, None, None, 16, 0, 4, 2, 64, None) == -1
